@@ -1,0 +1,122 @@
+/* kq.h -- C ABI of the B200 (sm_100a) Kindi-Q4 decode / speculative-verify runtime.
+ *
+ * Plain C types only: opaque handles, int status codes (0 = ok, < 0 = error, message from
+ * kq_error()), caller-owned host buffers. This mirrors the conventions of the reference's native
+ * CPU library (scripts/kindi_q4/kindi/kcpu4.c:303-344: int status returns, caller-owned buffers,
+ * an opaque model, sentinel -2 for a backend failure) and the error-string getter of its Metal
+ * bridge (scripts/kindi_q4/kindi/metal4.mm:13).
+ *
+ * Tensor bytes are GGUF block order: row-major [rows][cols/256][block], Q4_K blocks of 144 B and
+ * Q6_K blocks of 210 B (type codes 12 and 14, as in the GGUF file and the Kindi pack index).
+ */
+#ifndef KQ_H
+#define KQ_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KQ_Q4_K 12
+#define KQ_Q6_K 14
+
+/* Status codes. */
+#define KQ_OK            0
+#define KQ_ERR_ARG      -1   /* bad argument (reference: ValueError from cpu4.Engine.feed/step) */
+#define KQ_ERR_BACKEND  -2   /* CUDA failure (reference: kc_step returns -2, kcpu4.c:334) */
+#define KQ_ERR_OVERFLOW -3   /* position past the context (reference: OverflowError, cpu4.py:214-215) */
+#define KQ_ERR_MEMORY   -4   /* device allocation failed (reference: MemoryError admission guards) */
+#define KQ_ERR_TIMEOUT  -5   /* a bounded device wait gave up; the device flagged an error */
+
+/* Dense GQA decoder configuration (BASELINE config-2 by default, see kq_config_default). */
+typedef struct {
+  int dim;            /* hidden width D (multiple of 256) */
+  int n_layers;
+  int n_heads;        /* query heads */
+  int n_kv_heads;
+  int head_dim;       /* 128 */
+  int ffn;            /* SwiGLU width (multiple of 256) */
+  int vocab;          /* multiple of 8 */
+  int ctx;            /* positions in the K/V cache */
+  float rope_theta;
+  float eps;          /* RMS norm epsilon */
+  int t_q, t_k, t_v, t_o, t_gate, t_up, t_down, t_emb, t_out;   /* KQ_Q4_K / KQ_Q6_K per tensor */
+  int max_tokens;     /* widest verify / prefill pass (rows per pass) */
+} kq_config;
+
+/* Tensor kinds for kq_model_set_tensor (layer = -1 for the global tensors). */
+enum {
+  KQ_T_EMB = 0, KQ_T_OUT = 1, KQ_T_OUTNORM = 2,
+  KQ_T_ATTN_NORM = 3, KQ_T_Q = 4, KQ_T_K = 5, KQ_T_V = 6, KQ_T_O = 7,
+  KQ_T_FFN_NORM = 8, KQ_T_GATE = 9, KQ_T_UP = 10, KQ_T_DOWN = 11
+};
+
+typedef struct kq_model kq_model;   /* opaque */
+typedef struct kq_qmat kq_qmat;     /* opaque quantised matrix resident on the device */
+
+/* ------------------------------------------------------------------ library */
+int kq_version(void);
+const char* kq_error(void);                          /* last error of this thread ("" if none) */
+int kq_device_count(void);
+void kq_config_default(kq_config* cfg);              /* BASELINE config-2 */
+
+/* ------------------------------------------------------------------ model lifecycle
+ * Replaces gpu4.Engine.__init__ (scripts/kindi_q4/kindi/gpu4.py:51-90) and make_engine
+ * (scripts/kindi_q4/kindi/engine.py:369-381) for the Q4 pack path. */
+kq_model* kq_model_create(const kq_config* cfg, int device);   /* NULL on failure, see kq_error */
+void kq_model_free(kq_model* m);
+/* Fill every tensor from the seeded synthetic generator, on the device. */
+int kq_model_fill_synthetic(kq_model* m, uint64_t seed);
+/* Upload one tensor: quantised tensors as GGUF block bytes, norms as float32 [dim]. */
+int kq_model_set_tensor(kq_model* m, int layer, int kind, const void* host, size_t bytes);
+/* Engine.reset (cpu4.py:207-209): clears the K/V cache. */
+int kq_model_reset(kq_model* m);
+/* Fill the K/V cache of every layer at positions [0, npos) with seeded fp16 ~ N(0,1). */
+int kq_model_fill_kv(kq_model* m, int npos, uint64_t seed);
+/* Copy one layer's K (which = 0) or V (which = 1) cache rows [0, npos) to the host in the
+ * reference order [pos][kv][head_dim] (kcpu4.c:239-241). */
+int kq_model_get_kv(kq_model* m, int layer, int which, int npos, uint16_t* out);
+
+/* ------------------------------------------------------------------ engine API
+ * Engine.feed / Engine.step / Engine.generate (cpu4.py:211-236; engine.py:308-366), the
+ * equivalents of kc_step(model, tok, pos, head) (kcpu4.c:303). */
+int kq_feed(kq_model* m, int tok, int pos);          /* 0, or an error code */
+int kq_step(kq_model* m, int tok, int pos);          /* greedy next token id, or an error code */
+int kq_feed_batch(kq_model* m, const int32_t* toks, int n, int pos);
+int kq_generate(kq_model* m, const int32_t* ids, int n_ids, int n, int32_t* out);
+/* Engine.ylog (engine.py:323-331): the logits of the last step (row 0) or verify row `row`. */
+int kq_logits(kq_model* m, int row, float* out);
+/* Hidden residual stream after the last step (kcpu4.c:331: h), dim floats. */
+int kq_hidden(kq_model* m, float* out);
+
+/* Device-resident greedy decode: n steps, each feeding the previous step's argmax, starting
+ * from (tok, pos); no host round trip between steps. Writes the n ids to out. */
+int kq_decode_loop(kq_model* m, int tok, int pos, int n, int32_t* out);
+/* Time n device-resident decode steps (CUDA events on the model's stream); returns ms. */
+int kq_time_decode(kq_model* m, int tok, int pos, int n, float* ms_out);
+
+/* ------------------------------------------------------------------ matrix hooks
+ * kc_matvec / kc_dequant equivalents (kcpu4.c:337-341, q4kernels.h:12-36). */
+kq_qmat* kq_qmat_create(int type, int rows, int cols, int device);
+void kq_qmat_free(kq_qmat* a);
+int kq_qmat_upload(kq_qmat* a, const void* gguf_bytes, size_t bytes);
+int kq_qmat_fill_synthetic(kq_qmat* a, uint64_t seed, uint64_t stream);
+/* Bit-exact dequantisation of `nrows` rows starting at `row` into host floats (q4_decode). */
+int kq_qmat_dequant(kq_qmat* a, int row, int nrows, float* out);
+/* y[r] = sum_c W[r][c] x[c] for host x (cols floats) and host y (rows floats). */
+int kq_qmat_matvec(kq_qmat* a, const float* x, float* y);
+/* M-token product Y[m][r] = sum_c W[r][c] X[m][c] (host buffers, M <= 64). */
+int kq_qmat_matmul(kq_qmat* a, const float* x, int M, float* y);
+/* Device-pointer variants on a CUDA stream (0 = legacy default), no synchronisation. */
+int kq_qmat_matvec_dev(kq_qmat* a, const float* x_dev, float* y_dev, void* stream);
+/* Time n launches of the matvec on device buffers, rotating over `ncopies` matrices (so the
+ * weights are re-read from HBM); returns the mean launch ms measured with CUDA events. */
+int kq_time_matvec(kq_qmat* const* mats, int ncopies, int n, float* ms_out);
+/* Bytes the device layout of this matrix occupies (equal to the GGUF bytes). */
+size_t kq_qmat_bytes(const kq_qmat* a);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,258 @@
+"""ctypes bindings for the CPU oracle (TEST INFRASTRUCTURE ONLY).
+
+Loaded by tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference arm to check
+or time the CUDA library against a CPU restatement of the Kindi Q4 path. The product package never
+imports this module.
+
+  liboracle.so       kq_oracle.c: restated block decode, matvec, dense GQA decoder, generator
+  _ref/libkcpu4.so   the reference's own kcpu4.c compiled from its sources (when it was built)
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+Q4K, Q6K = 12, 14
+BLOCK = {Q4K: 144, Q6K: 210}
+
+PF = C.POINTER(C.c_float)
+PU8 = C.POINTER(C.c_uint8)
+PU16 = C.POINTER(C.c_uint16)
+PI32 = C.POINTER(C.c_int32)
+
+# tensor kinds of the synthetic stream numbering (kq_oracle.c)
+T_EMB, T_OUT, T_OUTNORM, T_ATTN_NORM, T_Q, T_K, T_V, T_O, T_FFN_NORM, T_GATE, T_UP, T_DOWN = range(12)
+
+
+def stream(layer, kind):
+    return (layer + 1) * 32 + kind
+
+
+class OCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("D", "NL", "NH", "NKV", "HD", "NFF", "vocab", "ctx")] + \
+               [("rope_theta", C.c_float), ("eps", C.c_float)] + \
+               [(n, C.c_int) for n in ("t_q", "t_k", "t_v", "t_o", "t_gate", "t_up", "t_down", "t_emb", "t_out")]
+
+
+def ptr(a, t=PF):
+    return a.ctypes.data_as(t)
+
+
+def build():
+    """Compile liboracle.so (and oracle/_ref when the reference sources exist)."""
+    import subprocess
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        L = C.CDLL(path)
+        L.or_decode_block.argtypes = [PU8, C.c_int, PF]
+        L.or_matvec_raw.argtypes = [PU8, C.c_int, C.c_int, C.c_int, C.c_int, PF, PF]
+        L.or_dequant_raw.argtypes = [PU8, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, PF]
+        L.or_gen_matrix.argtypes = [PU8, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_uint64]
+        L.or_gen_normal.argtypes = [PF, C.c_int64, C.c_float, C.c_float, C.c_uint64, C.c_uint64]
+        L.or_gen_tokens.argtypes = [PI32, C.c_int64, C.c_int, C.c_uint64, C.c_uint64]
+        L.or_gen_uniform.argtypes = [PF, C.c_int64, C.c_uint64, C.c_uint64]
+        L.or_gen_half_normal.argtypes = [PU16, C.c_int64, C.c_uint64, C.c_uint64]
+        L.or_model_create.argtypes = [C.POINTER(OCfg), C.c_uint64, C.c_int]
+        L.or_model_create.restype = C.c_void_p
+        L.or_model_free.argtypes = [C.c_void_p]
+        L.or_model_reset.argtypes = [C.c_void_p]
+        L.or_model_fill_kv.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
+        L.or_step.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
+        L.or_step.restype = C.c_int
+        L.or_model_logits.argtypes = [C.c_void_p]
+        L.or_model_logits.restype = PF
+        L.or_model_hidden.argtypes = [C.c_void_p]
+        L.or_model_hidden.restype = PF
+        L.or_model_kcache.argtypes = [C.c_void_p, C.c_int]
+        L.or_model_kcache.restype = PU16
+        L.or_model_vcache.argtypes = [C.c_void_p, C.c_int]
+        L.or_model_vcache.restype = PU16
+        L.or_model_tensor.argtypes = [C.c_void_p, C.c_int, C.c_int]
+        L.or_model_tensor.restype = PU8
+        L.or_rmsnorm.argtypes = [PF, PF, C.c_int, PF, PF, C.c_int, C.c_float]
+        L.or_attn_scale.argtypes = [C.c_int]
+        L.or_attn_scale.restype = C.c_float
+        L.or_set_threads.argtypes = [C.c_int]
+        L.or_get_threads.restype = C.c_int
+        assert L.or_sizeof_cfg() == C.sizeof(OCfg)
+        _lib = L
+    return _lib
+
+
+# ----------------------------------------------------------------------------- primitives
+def decode_blocks(raw, ty):
+    """raw [..., BLOCK[ty]] uint8 -> float32 [..., 256] via or_decode_block."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1, BLOCK[ty])
+    out = np.empty((raw.shape[0], 256), np.float32)
+    L = lib()
+    for i in range(raw.shape[0]):
+        L.or_decode_block(ptr(raw[i], PU8), ty, ptr(out[i]))
+    return out
+
+
+def gen_matrix(R, Cc, ty, seed, strm, layout=0):
+    W = np.empty(R * (Cc // 256) * BLOCK[ty], np.uint8)
+    lib().or_gen_matrix(ptr(W, PU8), R, Cc, ty, layout, seed, strm)
+    return W
+
+
+def gen_normal(n, mu, sigma, seed, strm):
+    y = np.empty(n, np.float32)
+    lib().or_gen_normal(ptr(y), n, mu, sigma, seed, strm)
+    return y
+
+
+def gen_tokens(n, V, seed, strm):
+    y = np.empty(n, np.int32)
+    lib().or_gen_tokens(ptr(y, PI32), n, V, seed, strm)
+    return y
+
+
+def gen_uniform(n, seed, strm):
+    y = np.empty(n, np.float32)
+    lib().or_gen_uniform(ptr(y), n, seed, strm)
+    return y
+
+
+def matvec(W, R, Cc, ty, x, layout=0):
+    y = np.empty(R, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    lib().or_matvec_raw(ptr(W, PU8), R, Cc, ty, layout, ptr(x), ptr(y))
+    return y
+
+
+def dequant_row(W, R, Cc, ty, row, layout=0):
+    y = np.empty(Cc, np.float32)
+    lib().or_dequant_raw(ptr(W, PU8), R, Cc, ty, layout, row, ptr(y))
+    return y
+
+
+def to_pack_layout(W, R, Cc, ty):
+    """GGUF row-major [R][G][bs] -> Kindi pack [R/8][G][8][bs] (q4pack.py:151-158)."""
+    bs = BLOCK[ty]
+    return np.ascontiguousarray(W.reshape(R // 8, 8, Cc // 256, bs).transpose(0, 2, 1, 3)).reshape(-1)
+
+
+# ----------------------------------------------------------------------------- dense decoder
+CFG2 = dict(D=4096, NL=32, NH=32, NKV=8, HD=128, NFF=12288, vocab=151936, ctx=4096,
+            rope_theta=1e6, eps=1e-6, t_q=Q4K, t_k=Q4K, t_v=Q6K, t_o=Q4K, t_gate=Q4K, t_up=Q4K,
+            t_down=Q6K, t_emb=Q4K, t_out=Q6K)
+
+
+def make_cfg(**kw):
+    d = dict(CFG2)
+    d.update(kw)
+    return OCfg(**d)
+
+
+class Model(object):
+    """The dense GQA decoder restated on the CPU, weights generated from `seed`."""
+
+    def __init__(self, seed=0, layout=0, **cfg):
+        self.cfg = make_cfg(**cfg)
+        self.L = lib()
+        self.h = self.L.or_model_create(C.byref(self.cfg), seed, layout)
+        if not self.h:
+            raise MemoryError("oracle model allocation failed")
+
+    def close(self):
+        if self.h:
+            self.L.or_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self):
+        self.L.or_model_reset(self.h)
+
+    def fill_kv(self, npos, seed):
+        self.L.or_model_fill_kv(self.h, npos, seed)
+
+    def step(self, tok, pos, head=True):
+        r = self.L.or_step(self.h, int(tok), int(pos), 1 if head else 0)
+        if r == -3:
+            raise ValueError("oracle: bad token or position")
+        return r
+
+    def logits(self):
+        return np.ctypeslib.as_array(self.L.or_model_logits(self.h), shape=(self.cfg.vocab,)).copy()
+
+    def hidden(self):
+        return np.ctypeslib.as_array(self.L.or_model_hidden(self.h), shape=(self.cfg.D,)).copy()
+
+    def kcache(self, layer, npos):
+        n = npos * self.cfg.NKV * self.cfg.HD
+        return np.ctypeslib.as_array(self.L.or_model_kcache(self.h, layer), shape=(n,)).copy()
+
+    def vcache(self, layer, npos):
+        n = npos * self.cfg.NKV * self.cfg.HD
+        return np.ctypeslib.as_array(self.L.or_model_vcache(self.h, layer), shape=(n,)).copy()
+
+    def generate(self, ids, n):
+        """Greedy: kcpu4's Engine.generate order (cpu4.py:227-236)."""
+        self.reset()
+        for i, t in enumerate(ids[:-1]):
+            self.step(t, i, head=False)
+        pos = len(ids)
+        out = [self.step(ids[-1], pos - 1)]
+        while len(out) < n:
+            out.append(self.step(out[-1], pos))
+            pos += 1
+        return out
+
+
+# ----------------------------------------------------------------------------- reference library
+class RefMat(C.Structure):
+    """The reference's Mat (kcpu4.c:26)."""
+    _fields_ = [("W", PU8), ("S", PF), ("R", C.c_int), ("C", C.c_int), ("type", C.c_int),
+                ("offset", C.c_uint64), ("bytes", C.c_uint64)]
+
+
+_ref = None
+
+
+def ref_lib():
+    """The reference's kcpu4.c built from its own sources into oracle/_ref, or None."""
+    global _ref
+    if _ref is None:
+        path = os.path.join(HERE, "_ref", "libkcpu4.so")
+        if not os.path.exists(path):
+            return None
+        L = C.CDLL(path)
+        L.kc_matvec.argtypes = [C.POINTER(RefMat), PF, PF]
+        L.kc_dequant.argtypes = [C.POINTER(RefMat), C.c_int, PF]
+        _ref = L
+    return _ref
+
+
+def ref_matvec(Wpack, R, Cc, ty, x):
+    """kc_matvec on a matrix in the Kindi pack layout."""
+    L = ref_lib()
+    m = RefMat(ptr(Wpack, PU8), None, R, Cc, ty, 0, Wpack.nbytes)
+    y = np.empty(R, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    L.kc_matvec(C.byref(m), ptr(x), ptr(y))
+    return y
+
+
+def ref_dequant(Wpack, R, Cc, ty, row):
+    L = ref_lib()
+    m = RefMat(ptr(Wpack, PU8), None, R, Cc, ty, 0, Wpack.nbytes)
+    y = np.empty(Cc, np.float32)
+    L.kc_dequant(C.byref(m), row, ptr(y))
+    return y

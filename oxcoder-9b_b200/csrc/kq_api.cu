@@ -1,0 +1,938 @@
+// kq_api.cu -- host runtime and C ABI (include/kq.h) of the B200 Kindi-Q4 decode path.
+//
+// Replaces the reference's CuPy engine (scripts/kindi_q4/kindi/gpu4.py:50-110, engine.py:293-366):
+// weights resident in HBM in the kq layout, one decode token = 32 x {QKV GEMV (+norm, rotary,
+// K/V store), attention, o GEMV, gate/up GEMV (+norm, SwiGLU), down GEMV} + head GEMV (+norm,
+// argmax), captured once into a CUDA graph with programmatic-dependent-launch edges and replayed
+// per token. There is no CPU fallback: every entry point fails with KQ_ERR_BACKEND if CUDA does.
+#include "../../include/kq.h"
+#include "kq_common.cuh"
+#include "kq_qformat.cuh"
+#include "kq_gemv.cuh"
+#include "kq_attn.cuh"
+
+#include <cuda_runtime.h>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+using namespace kq;
+
+#define KQ_VERSION 100
+
+// ------------------------------------------------------------------------------ errors
+static thread_local std::string g_err;
+static int set_err(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+#define CU(call)                                                                                 \
+  do {                                                                                           \
+    cudaError_t e_ = (call);                                                                     \
+    if (e_ != cudaSuccess) return set_err(KQ_ERR_BACKEND, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+#define CUP(call)                                                                                \
+  do {                                                                                           \
+    cudaError_t e_ = (call);                                                                     \
+    if (e_ != cudaSuccess) { set_err(KQ_ERR_BACKEND, std::string(#call) + ": " + cudaGetErrorString(e_)); return nullptr; } \
+  } while (0)
+
+// ------------------------------------------------------------------------------ per-device context
+struct DevCtx {
+  bool init = false;
+  int nsm = 0;
+  int* err = nullptr;       // device error word for matrix-hook calls
+  size_t smem_optin = 0;
+};
+static DevCtx g_dev[16];
+static std::mutex g_dev_mu;
+
+static int dev_init(int device) {
+  if (device < 0 || device >= 16) return set_err(KQ_ERR_ARG, "device index out of range");
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DevCtx& d = g_dev[device];
+  if (d.init) return KQ_OK;
+  CU(cudaSetDevice(device));
+  CU(cudaDeviceGetAttribute(&d.nsm, cudaDevAttrMultiProcessorCount, device));
+  int optin = 0;
+  CU(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  d.smem_optin = (size_t)optin;
+  CU(cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+  CU(cudaMalloc(&d.err, sizeof(int)));
+  CU(cudaMemset(d.err, 0, sizeof(int)));
+  d.init = true;
+  return KQ_OK;
+}
+
+// ------------------------------------------------------------------------------ matrices
+struct kq_qmat {
+  int device = 0, type = 0, R = 0, C = 0, G = 0;
+  uint8_t* buf = nullptr;
+  size_t off[4] = {0, 0, 0, 0};
+  size_t bytes = 0;
+  QView view() const {
+    QView v;
+    v.p0 = buf + off[0]; v.p1 = buf + off[1]; v.p2 = buf + off[2]; v.p3 = buf + off[3];
+    v.type = type; v.R = R; v.C = C; v.G = G;
+    return v;
+  }
+  QViewW wview() {
+    QViewW v;
+    v.p0 = buf + off[0]; v.p1 = buf + off[1]; v.p2 = buf + off[2]; v.p3 = buf + off[3];
+    v.type = type; v.R = R; v.C = C; v.G = G;
+    return v;
+  }
+};
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+static int check_shape(int type, int R, int C) {
+  if (type != KQ_Q4_K && type != KQ_Q6_K) return set_err(KQ_ERR_ARG, "tensor type must be 12 (Q4_K) or 14 (Q6_K)");
+  if (R <= 0 || C <= 0 || R % 8 || C % 256)
+    return set_err(KQ_ERR_ARG, "Invalid packed tensor dimensions: rows must be a positive multiple of 8 and cols of 256");
+  const int LPR = 4 * (C / 256);
+  if (!(LPR == 4 || LPR == 8 || LPR == 16 || (LPR % 32 == 0 && LPR <= 384)))
+    return set_err(KQ_ERR_ARG, "unsupported column count (need 256, 512, 1024 or a multiple of 2048 up to 24576)");
+  return KQ_OK;
+}
+
+static kq_qmat* qmat_alloc(int type, int R, int C, int device) {
+  if (check_shape(type, R, C) != KQ_OK) return nullptr;
+  if (dev_init(device) != KQ_OK) return nullptr;
+  CUP(cudaSetDevice(device));
+  kq_qmat* a = new kq_qmat();
+  a->device = device; a->type = type; a->R = R; a->C = C; a->G = C / 256;
+  size_t o = 0;
+  for (int p = 0; p < 4; ++p) {
+    a->off[p] = o;
+    o = align_up(o + (size_t)R * plane_row_bytes(type, p, a->G), 256);
+  }
+  a->bytes = (size_t)R * a->G * block_bytes(type);
+  if (cudaMalloc(&a->buf, o) != cudaSuccess) {
+    delete a;
+    set_err(KQ_ERR_MEMORY, "device allocation of a quantised matrix failed");
+    return nullptr;
+  }
+  return a;
+}
+
+static int qmat_write(kq_qmat* a, int R_src, const uint8_t* src_dev, uint64_t base, int mode, int arg, cudaStream_t s) {
+  const long long n = (long long)R_src * a->G;
+  const int thr = 128;
+  k_qmat_write<<<(unsigned)((n + thr - 1) / thr), thr, 0, s>>>(a->wview(), R_src, src_dev, base, mode, arg);
+  CU(cudaGetLastError());
+  return KQ_OK;
+}
+
+static int qmat_upload_mapped(kq_qmat* a, const void* host, size_t bytes, int R_src, int mode, int arg, cudaStream_t s) {
+  const size_t need = (size_t)R_src * a->G * block_bytes(a->type);
+  if (bytes != need) return set_err(KQ_ERR_ARG, "tensor byte count does not match its shape");
+  uint8_t* tmp = nullptr;
+  CU(cudaMalloc(&tmp, bytes));
+  cudaError_t e = cudaMemcpyAsync(tmp, host, bytes, cudaMemcpyHostToDevice, s);
+  int rc = KQ_OK;
+  if (e != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, std::string("upload: ") + cudaGetErrorString(e));
+  if (rc == KQ_OK) rc = qmat_write(a, R_src, tmp, 0, mode, arg, s);
+  cudaStreamSynchronize(s);
+  cudaFree(tmp);
+  return rc;
+}
+
+// ------------------------------------------------------------------------------ GEMV planning
+struct GemvPlan {
+  int TR, LPR, NRG, RPG, stage_bytes, nslots, threads, grid;
+  size_t smem;
+};
+
+static const size_t KQ_SMEM_BUDGET = 104 * 1024;   // leaves room for the next kernel's CTA (PDL)
+
+static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, bool pairs, int nsm, GemvPlan& pl) {
+  const int G = C / 256, LPR = 4 * G;
+  int rowb = 0;
+  for (int i = 0; i < nseg; ++i) rowb = std::max(rowb, block_bytes(types[i]) * G);
+  int TR = 8;
+  while (TR > 2 && TR * rowb > 28 * 1024) TR /= 2;
+  while (TR < 8 && (TR * G) % 8) TR *= 2;
+  if (pairs && TR < 2) TR = 2;
+  int NRG = 0;
+  for (int n = TR; n >= 1; --n) {
+    if (TR % n) continue;
+    if (LPR * n > 384) continue;
+    if ((LPR * n) % 32) continue;
+    if (pairs && ((TR / n) % 2)) continue;
+    if (n > 14) continue;
+    NRG = n;
+    break;
+  }
+  if (!NRG) return set_err(KQ_ERR_ARG, "no valid GEMV launch shape for this column count");
+  pl.TR = TR; pl.LPR = LPR; pl.NRG = NRG; pl.RPG = TR / NRG;
+  pl.stage_bytes = (int)align_up((size_t)TR * rowb, 128);
+  const int WPR = LPR >= 32 ? LPR / 32 : 1;
+  const size_t extra = 2 * sizeof(uint64_t) * 16 + sizeof(float) * (2 * pl.RPG * NRG * WPR + 2) +
+                       sizeof(double) * NRG * WPR + 8 * NRG + 64;
+  int slots = (int)((KQ_SMEM_BUDGET - extra) / pl.stage_bytes);
+  slots = std::min(12, std::max(2, slots));
+  pl.nslots = slots;
+  pl.smem = (size_t)slots * pl.stage_bytes + sizeof(uint64_t) * 2 * slots + sizeof(float) * (2 * pl.RPG * NRG * WPR + 2) +
+            sizeof(double) * NRG * WPR + sizeof(float) * NRG + sizeof(int) * NRG + 64;
+  pl.threads = LPR * NRG + 32;
+  int nstages = 0;
+  for (int i = 0; i < nseg; ++i) nstages += seg_rows[i] / TR;
+  pl.grid = std::max(1, std::min(nsm, nstages));
+  return KQ_OK;
+}
+
+struct SegSpec {
+  const kq_qmat* m;
+  int epi;
+  float* out_f;
+  __half* out_h;
+};
+
+static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParams& p, GemvPlan& pl) {
+  if (nseg < 1 || nseg > KQ_MAX_SEG) return set_err(KQ_ERR_ARG, "bad segment count");
+  int types[KQ_MAX_SEG], rows[KQ_MAX_SEG];
+  const int C = ss[0].m->C;
+  for (int i = 0; i < nseg; ++i) {
+    if (ss[i].m->C != C) return set_err(KQ_ERR_ARG, "fused GEMV segments must share the column count");
+    types[i] = ss[i].m->type;
+    rows[i] = ss[i].m->R;
+  }
+  int rc = plan_gemv(C, types, nseg, rows, pairs, nsm, pl);
+  if (rc) return rc;
+  std::memset(&p, 0, sizeof(p));
+  p.nseg = nseg;
+  int st = 0;
+  for (int i = 0; i < nseg; ++i) {
+    p.seg[i].w = ss[i].m->view();
+    p.seg[i].stage0 = st;
+    p.seg[i].nstage = ss[i].m->R / pl.TR;
+    p.seg[i].epi = ss[i].epi;
+    p.seg[i].out_f = ss[i].out_f;
+    p.seg[i].out_h = ss[i].out_h;
+    st += p.seg[i].nstage;
+  }
+  p.nstages = st;
+  p.C = C; p.G = C / 256; p.TR = pl.TR; p.LPR = pl.LPR; p.NRG = pl.NRG; p.RPG = pl.RPG;
+  p.stage_bytes = pl.stage_bytes; p.nslots = pl.nslots;
+  return KQ_OK;
+}
+
+static cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& pl, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)pl.grid);
+  cfg.blockDim = dim3((unsigned)pl.threads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_gemv, p);
+}
+
+template <int G>
+static cudaError_t launch_attn_t(const AttnParams& a, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.n_kv, (unsigned)a.nsplit);
+  cfg.blockDim = dim3(ATT_THREADS);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_attn_decode<G>, a);
+}
+static cudaError_t launch_attn(const AttnParams& a, int G, cudaStream_t s, bool pdl) {
+  switch (G) {
+    case 1: return launch_attn_t<1>(a, s, pdl);
+    case 2: return launch_attn_t<2>(a, s, pdl);
+    case 4: return launch_attn_t<4>(a, s, pdl);
+    case 8: return launch_attn_t<8>(a, s, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ------------------------------------------------------------------------------ model
+struct LayerW {
+  kq_qmat *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+  float *attn_norm = nullptr, *ffn_norm = nullptr;
+  __half *kc = nullptr, *vc = nullptr;
+};
+
+struct kq_model {
+  kq_config c{};
+  int device = 0, nsm = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<LayerW> L;
+  kq_qmat *emb = nullptr, *out = nullptr;
+  float* out_norm = nullptr;
+  float *cos_t = nullptr, *sin_t = nullptr;
+  float *h[2] = {nullptr, nullptr}, *y = nullptr, *q = nullptr, *att = nullptr, *mbuf = nullptr, *logits = nullptr;
+  float *apart = nullptr, *apart_ml = nullptr;
+  int* aticket = nullptr;
+  float* hpart_val = nullptr;
+  int* hpart_idx = nullptr;
+  int* hticket = nullptr;
+  DecodeState* st = nullptr;
+  DecodeState* st_host = nullptr;   // pinned
+  int* out_ids = nullptr;           // tokens of the device-resident loop
+  int out_cap = 0;
+  int* err = nullptr;
+  int nsplit = 0;
+  cudaGraphExec_t g_step = nullptr, g_feed = nullptr;
+  std::vector<void*> allocs;
+};
+
+static int model_check(kq_model* m) {
+  if (!m) return set_err(KQ_ERR_ARG, "null model");
+  CU(cudaSetDevice(m->device));
+  return KQ_OK;
+}
+
+extern "C" {
+
+int kq_version(void) { return KQ_VERSION; }
+const char* kq_error(void) { return g_err.c_str(); }
+int kq_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n;
+}
+
+void kq_config_default(kq_config* c) {
+  if (!c) return;
+  c->dim = 4096; c->n_layers = 32; c->n_heads = 32; c->n_kv_heads = 8; c->head_dim = 128; c->ffn = 12288;
+  c->vocab = 151936; c->ctx = 4096; c->rope_theta = 1e6f; c->eps = 1e-6f;
+  c->t_q = KQ_Q4_K; c->t_k = KQ_Q4_K; c->t_v = KQ_Q6_K; c->t_o = KQ_Q4_K; c->t_gate = KQ_Q4_K; c->t_up = KQ_Q4_K;
+  c->t_down = KQ_Q6_K; c->t_emb = KQ_Q4_K; c->t_out = KQ_Q6_K;
+  c->max_tokens = 64;
+}
+
+}  // extern "C"
+
+static void model_release(kq_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  if (m->g_step) cudaGraphExecDestroy(m->g_step);
+  if (m->g_feed) cudaGraphExecDestroy(m->g_feed);
+  for (auto& l : m->L) {
+    kq_qmat* ms[] = {l.q, l.k, l.v, l.o, l.gu, l.down};
+    for (kq_qmat* a : ms)
+      if (a) { cudaFree(a->buf); delete a; }
+  }
+  for (kq_qmat* a : {m->emb, m->out})
+    if (a) { cudaFree(a->buf); delete a; }
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->st_host) cudaFreeHost(m->st_host);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+template <typename T>
+static T* dalloc(kq_model* m, size_t n, bool& ok) {
+  void* p = nullptr;
+  if (cudaMalloc(&p, n * sizeof(T)) != cudaSuccess) { ok = false; return nullptr; }
+  cudaMemset(p, 0, n * sizeof(T));
+  m->allocs.push_back(p);
+  return reinterpret_cast<T*>(p);
+}
+
+static int validate_cfg(const kq_config& c) {
+  if (c.head_dim != 128) return set_err(KQ_ERR_ARG, "head_dim must be 128");
+  if (c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads) return set_err(KQ_ERR_ARG, "n_heads must be a multiple of n_kv_heads");
+  const int G = c.n_heads / c.n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return set_err(KQ_ERR_ARG, "query heads per kv head must be 1, 2, 4 or 8");
+  if (c.dim < 512) return set_err(KQ_ERR_ARG, "dim must be at least 512");
+  if (c.n_heads * c.head_dim < 512) return set_err(KQ_ERR_ARG, "n_heads * head_dim must be at least 512");
+  if (c.ctx < 1 || c.ctx > 1 << 20) return set_err(KQ_ERR_ARG, "ctx out of range");
+  if (c.vocab <= 0 || c.vocab % 8) return set_err(KQ_ERR_ARG, "vocab must be a positive multiple of 8");
+  if (c.t_gate != c.t_up) return set_err(KQ_ERR_ARG, "gate and up must share a quantisation type");
+  if (c.n_layers < 1) return set_err(KQ_ERR_ARG, "n_layers must be positive");
+  const int shapes[][3] = {{c.t_q, c.n_heads * c.head_dim, c.dim}, {c.t_k, c.n_kv_heads * c.head_dim, c.dim},
+                           {c.t_v, c.n_kv_heads * c.head_dim, c.dim}, {c.t_o, c.dim, c.n_heads * c.head_dim},
+                           {c.t_gate, 2 * c.ffn, c.dim}, {c.t_down, c.dim, c.ffn},
+                           {c.t_emb, c.vocab, c.dim}, {c.t_out, c.vocab, c.dim}};
+  for (auto& s : shapes)
+    if (check_shape(s[0], s[1], s[2]) != KQ_OK) return KQ_ERR_ARG;
+  return KQ_OK;
+}
+
+extern "C" kq_model* kq_model_create(const kq_config* cfg, int device) {
+  if (!cfg) { set_err(KQ_ERR_ARG, "null config"); return nullptr; }
+  if (validate_cfg(*cfg) != KQ_OK) return nullptr;
+  if (dev_init(device) != KQ_OK) return nullptr;
+  CUP(cudaSetDevice(device));
+  kq_model* m = new kq_model();
+  m->c = *cfg;
+  m->device = device;
+  m->nsm = g_dev[device].nsm;
+  const kq_config& c = m->c;
+  bool ok = true;
+  if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) ok = false;
+  const int QD = c.n_heads * c.head_dim, KD = c.n_kv_heads * c.head_dim;
+  m->L.resize(c.n_layers);
+  for (int l = 0; ok && l < c.n_layers; ++l) {
+    LayerW& w = m->L[l];
+    w.q = qmat_alloc(c.t_q, QD, c.dim, device);
+    w.k = qmat_alloc(c.t_k, KD, c.dim, device);
+    w.v = qmat_alloc(c.t_v, KD, c.dim, device);
+    w.o = qmat_alloc(c.t_o, c.dim, QD, device);
+    w.gu = qmat_alloc(c.t_gate, 2 * c.ffn, c.dim, device);
+    w.down = qmat_alloc(c.t_down, c.dim, c.ffn, device);
+    if (!w.q || !w.k || !w.v || !w.o || !w.gu || !w.down) { ok = false; break; }
+    w.attn_norm = dalloc<float>(m, c.dim, ok);
+    w.ffn_norm = dalloc<float>(m, c.dim, ok);
+    w.kc = dalloc<__half>(m, (size_t)KD * c.ctx, ok);
+    w.vc = dalloc<__half>(m, (size_t)KD * c.ctx, ok);
+  }
+  if (ok) {
+    m->emb = qmat_alloc(c.t_emb, c.vocab, c.dim, device);
+    m->out = qmat_alloc(c.t_out, c.vocab, c.dim, device);
+    if (!m->emb || !m->out) ok = false;
+  }
+  const int rh = c.head_dim / 2;
+  if (ok) {
+    m->out_norm = dalloc<float>(m, c.dim, ok);
+    m->cos_t = dalloc<float>(m, (size_t)c.ctx * rh, ok);
+    m->sin_t = dalloc<float>(m, (size_t)c.ctx * rh, ok);
+    m->h[0] = dalloc<float>(m, c.dim, ok);
+    m->h[1] = dalloc<float>(m, c.dim, ok);
+    m->y = dalloc<float>(m, c.dim, ok);
+    m->q = dalloc<float>(m, QD, ok);
+    m->att = dalloc<float>(m, QD, ok);
+    m->mbuf = dalloc<float>(m, c.ffn, ok);
+    m->logits = dalloc<float>(m, c.vocab, ok);
+    m->nsplit = (c.ctx + ATT_P - 1) / ATT_P;
+    m->apart = dalloc<float>(m, (size_t)c.n_kv_heads * m->nsplit * (c.n_heads / c.n_kv_heads) * c.head_dim, ok);
+    m->apart_ml = dalloc<float>(m, (size_t)c.n_kv_heads * m->nsplit * (c.n_heads / c.n_kv_heads) * 2, ok);
+    m->aticket = dalloc<int>(m, c.n_kv_heads, ok);
+    m->hpart_val = dalloc<float>(m, 1024, ok);
+    m->hpart_idx = dalloc<int>(m, 1024, ok);
+    m->hticket = dalloc<int>(m, 1, ok);
+    m->st = dalloc<DecodeState>(m, 1, ok);
+    m->out_cap = c.ctx;
+    m->out_ids = dalloc<int>(m, (size_t)m->out_cap, ok);
+    m->err = dalloc<int>(m, 1, ok);
+    if (cudaMallocHost(&m->st_host, sizeof(DecodeState)) != cudaSuccess) ok = false;
+  }
+  if (ok) {
+    // RoPE tables as cpu4.py:175-178: fp64 angles, cast to f32.
+    std::vector<float> ct((size_t)c.ctx * rh), stb((size_t)c.ctx * rh);
+    for (int p = 0; p < c.ctx; ++p)
+      for (int i = 0; i < rh; ++i) {
+        const double inv = std::pow((double)c.rope_theta, -2.0 * (double)i / (double)c.head_dim);
+        const double th = (double)p * inv;
+        ct[(size_t)p * rh + i] = (float)std::cos(th);
+        stb[(size_t)p * rh + i] = (float)std::sin(th);
+      }
+    if (cudaMemcpy(m->cos_t, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(m->sin_t, stb.data(), stb.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      ok = false;
+  }
+  if (!ok || cudaDeviceSynchronize() != cudaSuccess) {
+    if (g_err.empty() || g_err.find("alloc") == std::string::npos) set_err(KQ_ERR_MEMORY, "model allocation failed");
+    model_release(m);
+    return nullptr;
+  }
+  return m;
+}
+
+extern "C" void kq_model_free(kq_model* m) { model_release(m); }
+
+// Synthetic stream numbering (shared specification with the CPU oracle).
+static uint64_t tstream(int layer, int kind) { return (uint64_t)(layer + 1) * 32u + (uint64_t)kind; }
+
+static int gen_normal_dev(float* dst, long long n, float mu, float sigma, uint64_t seed, uint64_t stream, cudaStream_t s) {
+  k_gen_normal<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dst, n, mu, sigma, gen_base(seed, stream));
+  CU(cudaGetLastError());
+  return KQ_OK;
+}
+
+extern "C" int kq_model_fill_synthetic(kq_model* m, uint64_t seed) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  const kq_config& c = m->c;
+  cudaStream_t s = m->stream;
+  for (int l = 0; l < c.n_layers; ++l) {
+    LayerW& w = m->L[l];
+    if ((rc = qmat_write(w.q, w.q->R, nullptr, gen_base(seed, tstream(l, KQ_T_Q)), RM_ROPE_PAIR, c.head_dim, s))) return rc;
+    if ((rc = qmat_write(w.k, w.k->R, nullptr, gen_base(seed, tstream(l, KQ_T_K)), RM_ROPE_PAIR, c.head_dim, s))) return rc;
+    if ((rc = qmat_write(w.v, w.v->R, nullptr, gen_base(seed, tstream(l, KQ_T_V)), RM_IDENT, 0, s))) return rc;
+    if ((rc = qmat_write(w.o, w.o->R, nullptr, gen_base(seed, tstream(l, KQ_T_O)), RM_IDENT, 0, s))) return rc;
+    if ((rc = qmat_write(w.gu, c.ffn, nullptr, gen_base(seed, tstream(l, KQ_T_GATE)), RM_INTERLEAVE, 0, s))) return rc;
+    if ((rc = qmat_write(w.gu, c.ffn, nullptr, gen_base(seed, tstream(l, KQ_T_UP)), RM_INTERLEAVE, 1, s))) return rc;
+    if ((rc = qmat_write(w.down, w.down->R, nullptr, gen_base(seed, tstream(l, KQ_T_DOWN)), RM_IDENT, 0, s))) return rc;
+    if ((rc = gen_normal_dev(w.attn_norm, c.dim, 1.0f, 0.02f, seed, tstream(l, KQ_T_ATTN_NORM), s))) return rc;
+    if ((rc = gen_normal_dev(w.ffn_norm, c.dim, 1.0f, 0.02f, seed, tstream(l, KQ_T_FFN_NORM), s))) return rc;
+  }
+  if ((rc = qmat_write(m->emb, m->emb->R, nullptr, gen_base(seed, tstream(-1, KQ_T_EMB)), RM_IDENT, 0, s))) return rc;
+  if ((rc = qmat_write(m->out, m->out->R, nullptr, gen_base(seed, tstream(-1, KQ_T_OUT)), RM_IDENT, 0, s))) return rc;
+  if ((rc = gen_normal_dev(m->out_norm, c.dim, 1.0f, 0.02f, seed, tstream(-1, KQ_T_OUTNORM), s))) return rc;
+  CU(cudaStreamSynchronize(s));
+  return KQ_OK;
+}
+
+extern "C" int kq_model_set_tensor(kq_model* m, int layer, int kind, const void* host, size_t bytes) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (!host) return set_err(KQ_ERR_ARG, "null tensor data");
+  const kq_config& c = m->c;
+  const bool global = kind == KQ_T_EMB || kind == KQ_T_OUT || kind == KQ_T_OUTNORM;
+  if (global != (layer < 0)) return set_err(KQ_ERR_ARG, "layer must be -1 exactly for the global tensors");
+  if (!global && layer >= c.n_layers) return set_err(KQ_ERR_ARG, "layer out of range");
+  float* fdst = nullptr;
+  switch (kind) {
+    case KQ_T_OUTNORM: fdst = m->out_norm; break;
+    case KQ_T_ATTN_NORM: fdst = m->L[layer].attn_norm; break;
+    case KQ_T_FFN_NORM: fdst = m->L[layer].ffn_norm; break;
+    default: break;
+  }
+  if (fdst) {
+    if (bytes != (size_t)c.dim * 4) return set_err(KQ_ERR_ARG, "norm tensors are dim float32 values");
+    CU(cudaMemcpy(fdst, host, bytes, cudaMemcpyHostToDevice));
+    return KQ_OK;
+  }
+  cudaStream_t s = m->stream;
+  switch (kind) {
+    case KQ_T_EMB: return qmat_upload_mapped(m->emb, host, bytes, m->emb->R, RM_IDENT, 0, s);
+    case KQ_T_OUT: return qmat_upload_mapped(m->out, host, bytes, m->out->R, RM_IDENT, 0, s);
+    case KQ_T_Q: return qmat_upload_mapped(m->L[layer].q, host, bytes, m->L[layer].q->R, RM_ROPE_PAIR, c.head_dim, s);
+    case KQ_T_K: return qmat_upload_mapped(m->L[layer].k, host, bytes, m->L[layer].k->R, RM_ROPE_PAIR, c.head_dim, s);
+    case KQ_T_V: return qmat_upload_mapped(m->L[layer].v, host, bytes, m->L[layer].v->R, RM_IDENT, 0, s);
+    case KQ_T_O: return qmat_upload_mapped(m->L[layer].o, host, bytes, m->L[layer].o->R, RM_IDENT, 0, s);
+    case KQ_T_GATE: return qmat_upload_mapped(m->L[layer].gu, host, bytes, c.ffn, RM_INTERLEAVE, 0, s);
+    case KQ_T_UP: return qmat_upload_mapped(m->L[layer].gu, host, bytes, c.ffn, RM_INTERLEAVE, 1, s);
+    case KQ_T_DOWN: return qmat_upload_mapped(m->L[layer].down, host, bytes, m->L[layer].down->R, RM_IDENT, 0, s);
+    default: return set_err(KQ_ERR_ARG, "unknown tensor kind");
+  }
+}
+
+extern "C" int kq_model_reset(kq_model* m) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  const size_t kvn = (size_t)m->c.n_kv_heads * m->c.head_dim * m->c.ctx;
+  for (auto& l : m->L) {
+    CU(cudaMemsetAsync(l.kc, 0, kvn * 2, m->stream));
+    CU(cudaMemsetAsync(l.vc, 0, kvn * 2, m->stream));
+  }
+  CU(cudaStreamSynchronize(m->stream));
+  return KQ_OK;
+}
+
+// Value of the K/V cache at (kv, pos, d) = generator element (pos * n_kv + kv) * hd + d, which is
+// the element order of the reference layout [pos][kv][hd].
+__global__ void k_fill_kv(__half* dst, int npos, int nkv, int ctx, int hd, uint64_t base) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)npos * nkv * hd) return;
+  const int d = (int)(i % hd);
+  const long long r = i / hd;
+  const int kv = (int)(r % nkv), pos = (int)(r / nkv);
+  dst[((size_t)kv * ctx + pos) * hd + d] = __float2half_rn(gen_nrm(base, (uint64_t)i));
+}
+
+extern "C" int kq_model_fill_kv(kq_model* m, int npos, uint64_t seed) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (npos < 0 || npos > m->c.ctx) return set_err(KQ_ERR_ARG, "npos out of range");
+  const long long n = (long long)npos * m->c.n_kv_heads * m->c.head_dim;
+  if (n == 0) return KQ_OK;
+  for (int l = 0; l < m->c.n_layers; ++l) {
+    k_fill_kv<<<(unsigned)((n + 255) / 256), 256, 0, m->stream>>>(m->L[l].kc, npos, m->c.n_kv_heads, m->c.ctx, m->c.head_dim,
+                                                                   gen_base(seed, tstream(l, 12)));
+    k_fill_kv<<<(unsigned)((n + 255) / 256), 256, 0, m->stream>>>(m->L[l].vc, npos, m->c.n_kv_heads, m->c.ctx, m->c.head_dim,
+                                                                   gen_base(seed, tstream(l, 13)));
+  }
+  CU(cudaGetLastError());
+  CU(cudaStreamSynchronize(m->stream));
+  return KQ_OK;
+}
+
+extern "C" int kq_model_get_kv(kq_model* m, int layer, int which, int npos, uint16_t* out) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (layer < 0 || layer >= m->c.n_layers || npos < 0 || npos > m->c.ctx || !out || (which != 0 && which != 1))
+    return set_err(KQ_ERR_ARG, "bad K/V cache request");
+  const int nkv = m->c.n_kv_heads, hd = m->c.head_dim, ctx = m->c.ctx;
+  std::vector<uint16_t> tmp((size_t)nkv * ctx * hd);
+  CU(cudaMemcpy(tmp.data(), which ? m->L[layer].vc : m->L[layer].kc, tmp.size() * 2, cudaMemcpyDeviceToHost));
+  for (int p = 0; p < npos; ++p)
+    for (int kv = 0; kv < nkv; ++kv)
+      std::memcpy(out + ((size_t)p * nkv + kv) * hd, tmp.data() + ((size_t)kv * ctx + p) * hd, hd * 2);
+  return KQ_OK;
+}
+
+// ------------------------------------------------------------------------------ decode step
+static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
+  const kq_config& c = m->c;
+  const int G = c.n_heads / c.n_kv_heads;
+  GemvParams p;
+  GemvPlan pl;
+  int cur = 0;
+  bool first = true;
+  auto common = [&](GemvParams& pp) {
+    pp.st = m->st;
+    pp.vocab = c.vocab;
+    pp.cos_t = m->cos_t;
+    pp.sin_t = m->sin_t;
+    pp.hd = c.head_dim;
+    pp.ctx = c.ctx;
+    pp.err = m->err;
+    pp.eps = c.eps;
+  };
+  for (int l = 0; l < c.n_layers; ++l) {
+    LayerW& w = m->L[l];
+    // QKV (+ norm or embedding; rotary + K/V store)
+    SegSpec qkv[3] = {{w.q, EPI_ROPE_Q, m->q, nullptr}, {w.k, EPI_ROPE_K, nullptr, w.kc}, {w.v, EPI_V, nullptr, w.vc}};
+    int rc = fill_gemv(qkv, 3, true, m->nsm, p, pl);
+    if (rc) return rc;
+    common(p);
+    if (l == 0) {
+      p.xmode = XS_EMBED;
+      p.emb = m->emb->view();
+      p.h_in = nullptr;
+      p.y_add = nullptr;
+    } else {
+      p.xmode = XS_NORM;
+      p.h_in = m->h[cur];
+      p.y_add = m->y;
+    }
+    p.gamma = w.attn_norm;
+    p.h_out = m->h[cur ^ 1];
+    cur ^= 1;
+    CU(launch_gemv(p, pl, s, !first));
+    first = false;
+    // attention
+    AttnParams a;
+    a.q = m->q; a.kc = w.kc; a.vc = w.vc; a.part = m->apart; a.part_ml = m->apart_ml; a.ticket = m->aticket;
+    a.out = m->att; a.st = m->st; a.n_kv = c.n_kv_heads; a.ctx = c.ctx; a.nsplit = m->nsplit;
+    a.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
+    a.err = m->err;
+    CU(launch_attn(a, G, s, true));
+    // o projection
+    SegSpec so[1] = {{w.o, EPI_F32, m->y, nullptr}};
+    if ((rc = fill_gemv(so, 1, false, m->nsm, p, pl))) return rc;
+    common(p);
+    p.xmode = XS_PLAIN;
+    p.x = m->att;
+    CU(launch_gemv(p, pl, s, true));
+    // gate/up (+ norm, SwiGLU)
+    SegSpec sg[1] = {{w.gu, EPI_SWIGLU, m->mbuf, nullptr}};
+    if ((rc = fill_gemv(sg, 1, true, m->nsm, p, pl))) return rc;
+    common(p);
+    p.xmode = XS_NORM;
+    p.h_in = m->h[cur];
+    p.y_add = m->y;
+    p.gamma = w.ffn_norm;
+    p.h_out = m->h[cur ^ 1];
+    cur ^= 1;
+    CU(launch_gemv(p, pl, s, true));
+    // down
+    SegSpec sd[1] = {{w.down, EPI_F32, m->y, nullptr}};
+    if ((rc = fill_gemv(sd, 1, false, m->nsm, p, pl))) return rc;
+    common(p);
+    p.xmode = XS_PLAIN;
+    p.x = m->mbuf;
+    CU(launch_gemv(p, pl, s, true));
+  }
+  if (head) {
+    SegSpec sh[1] = {{m->out, EPI_ARGMAX, m->logits, nullptr}};
+    int rc = fill_gemv(sh, 1, false, m->nsm, p, pl);
+    if (rc) return rc;
+    if (pl.grid > 1024) return set_err(KQ_ERR_ARG, "head grid too large");
+    common(p);
+    p.xmode = XS_NORM;
+    p.h_in = m->h[cur];
+    p.y_add = m->y;
+    p.gamma = m->out_norm;
+    p.h_out = m->h[cur ^ 1];
+    p.part_val = m->hpart_val;
+    p.part_idx = m->hpart_idx;
+    p.ticket = m->hticket;
+    p.out_ids = m->out_ids;
+    p.out_cap = m->out_cap;
+    CU(launch_gemv(p, pl, s, true));
+  }
+  return KQ_OK;
+}
+
+static int build_graph(kq_model* m, bool head, cudaGraphExec_t* out) {
+  cudaGraph_t g = nullptr;
+  CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_step(m, head, m->stream);
+  cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+  if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+  if (e != cudaSuccess) return set_err(KQ_ERR_BACKEND, std::string("graph capture: ") + cudaGetErrorString(e));
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return set_err(KQ_ERR_BACKEND, std::string("graph instantiate: ") + cudaGetErrorString(e));
+  return KQ_OK;
+}
+
+static int ensure_graphs(kq_model* m) {
+  int rc;
+  if (!m->g_step && (rc = build_graph(m, true, &m->g_step))) return rc;
+  if (!m->g_feed && (rc = build_graph(m, false, &m->g_feed))) return rc;
+  return KQ_OK;
+}
+
+static int check_dev_err(kq_model* m) {
+  int e = 0;
+  CU(cudaMemcpy(&e, m->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (e) {
+    cudaMemset(m->err, 0, sizeof(int));
+    if (e & (KQ_DEV_ERR_BAD_TOKEN | KQ_DEV_ERR_BAD_POS)) return set_err(KQ_ERR_ARG, "device saw an invalid token or position");
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "a bounded device wait gave up (error bits 0x%x)", e);
+    return set_err(KQ_ERR_TIMEOUT, buf);
+  }
+  return KQ_OK;
+}
+
+static int run_one(kq_model* m, int tok, int pos, bool head) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (tok < 0 || tok >= m->c.vocab || pos < 0) return set_err(KQ_ERR_ARG, "Invalid token or position");
+  if (pos >= m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "position is past the context");
+  if ((rc = ensure_graphs(m))) return rc;
+  m->st_host->tok = tok;
+  m->st_host->pos = pos;
+  m->st_host->next_tok = -1;
+  m->st_host->steps = 0;
+  CU(cudaMemcpyAsync(m->st, m->st_host, sizeof(DecodeState), cudaMemcpyHostToDevice, m->stream));
+  CU(cudaGraphLaunch(head ? m->g_step : m->g_feed, m->stream));
+  if (head) CU(cudaMemcpyAsync(m->st_host, m->st, sizeof(DecodeState), cudaMemcpyDeviceToHost, m->stream));
+  CU(cudaStreamSynchronize(m->stream));
+  if ((rc = check_dev_err(m))) return rc;
+  return head ? m->st_host->next_tok : KQ_OK;
+}
+
+extern "C" int kq_feed(kq_model* m, int tok, int pos) { return run_one(m, tok, pos, false); }
+extern "C" int kq_step(kq_model* m, int tok, int pos) { return run_one(m, tok, pos, true); }
+
+extern "C" int kq_feed_batch(kq_model* m, const int32_t* toks, int n, int pos) {
+  if (!toks || n < 0) return set_err(KQ_ERR_ARG, "bad token batch");
+  for (int i = 0; i < n; ++i) {
+    const int rc = kq_feed(m, toks[i], pos + i);
+    if (rc < 0) return rc;
+  }
+  return KQ_OK;
+}
+
+extern "C" int kq_generate(kq_model* m, const int32_t* ids, int n_ids, int n, int32_t* out) {
+  if (!ids || n_ids < 1 || n < 1 || !out) return set_err(KQ_ERR_ARG, "bad generate arguments");
+  int rc = kq_model_reset(m);
+  if (rc) return rc;
+  if ((rc = kq_feed_batch(m, ids, n_ids - 1, 0))) return rc;
+  int pos = n_ids;
+  int t = kq_step(m, ids[n_ids - 1], pos - 1);
+  if (t < 0) return t;
+  out[0] = t;
+  for (int i = 1; i < n; ++i) {
+    t = kq_step(m, out[i - 1], pos);
+    if (t < 0) return t;
+    out[i] = t;
+    ++pos;
+  }
+  return KQ_OK;
+}
+
+extern "C" int kq_logits(kq_model* m, int row, float* out) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (row != 0 || !out) return set_err(KQ_ERR_ARG, "bad logits request");
+  CU(cudaMemcpy(out, m->logits, (size_t)m->c.vocab * 4, cudaMemcpyDeviceToHost));
+  return KQ_OK;
+}
+
+extern "C" int kq_hidden(kq_model* m, float* out) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (!out) return set_err(KQ_ERR_ARG, "null output");
+  // after a step with the head, the residual (h + last block output) is in h[1] (even number of
+  // norm kernels per layer, the head's norm writes the second buffer)
+  CU(cudaMemcpy(out, m->h[1], (size_t)m->c.dim * 4, cudaMemcpyDeviceToHost));
+  return KQ_OK;
+}
+
+extern "C" int kq_decode_loop(kq_model* m, int tok, int pos, int n, int32_t* out) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (n < 1 || !out || tok < 0 || tok >= m->c.vocab || pos < 0) return set_err(KQ_ERR_ARG, "bad decode loop arguments");
+  if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "decode loop runs past the context");
+  if ((rc = ensure_graphs(m))) return rc;
+  if (n > m->out_cap) return set_err(KQ_ERR_ARG, "decode loop longer than the context");
+  m->st_host->tok = tok; m->st_host->pos = pos; m->st_host->next_tok = -1; m->st_host->steps = 0;
+  CU(cudaMemcpyAsync(m->st, m->st_host, sizeof(DecodeState), cudaMemcpyHostToDevice, m->stream));
+  // each replay embeds st->tok at st->pos; the head's last CTA stores the argmax in out_ids and
+  // advances (tok, pos) on the device, so no host round trip separates the steps
+  for (int i = 0; i < n; ++i) CU(cudaGraphLaunch(m->g_step, m->stream));
+  CU(cudaMemcpyAsync(out, m->out_ids, (size_t)n * sizeof(int32_t), cudaMemcpyDeviceToHost, m->stream));
+  CU(cudaStreamSynchronize(m->stream));
+  return check_dev_err(m);
+}
+
+extern "C" int kq_time_decode(kq_model* m, int tok, int pos, int n, float* ms_out) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (n < 1 || !ms_out || tok < 0 || tok >= m->c.vocab || pos < 0) return set_err(KQ_ERR_ARG, "bad timing arguments");
+  if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "timed decode runs past the context");
+  if ((rc = ensure_graphs(m))) return rc;
+  m->st_host->tok = tok; m->st_host->pos = pos; m->st_host->next_tok = -1; m->st_host->steps = 0;
+  CU(cudaMemcpyAsync(m->st, m->st_host, sizeof(DecodeState), cudaMemcpyHostToDevice, m->stream));
+  cudaEvent_t e0, e1;
+  CU(cudaEventCreate(&e0));
+  CU(cudaEventCreate(&e1));
+  CU(cudaStreamSynchronize(m->stream));
+  CU(cudaEventRecord(e0, m->stream));
+  for (int i = 0; i < n; ++i) CU(cudaGraphLaunch(m->g_step, m->stream));
+  CU(cudaEventRecord(e1, m->stream));
+  CU(cudaEventSynchronize(e1));
+  float ms = 0.f;
+  CU(cudaEventElapsedTime(&ms, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *ms_out = ms;
+  return check_dev_err(m);
+}
+
+// ------------------------------------------------------------------------------ matrix hooks
+extern "C" kq_qmat* kq_qmat_create(int type, int rows, int cols, int device) { return qmat_alloc(type, rows, cols, device); }
+extern "C" void kq_qmat_free(kq_qmat* a) {
+  if (!a) return;
+  cudaSetDevice(a->device);
+  cudaFree(a->buf);
+  delete a;
+}
+extern "C" size_t kq_qmat_bytes(const kq_qmat* a) { return a ? a->bytes : 0; }
+
+extern "C" int kq_qmat_upload(kq_qmat* a, const void* bytes_host, size_t bytes) {
+  if (!a || !bytes_host) return set_err(KQ_ERR_ARG, "null argument");
+  CU(cudaSetDevice(a->device));
+  return qmat_upload_mapped(a, bytes_host, bytes, a->R, RM_IDENT, 0, 0);
+}
+
+extern "C" int kq_qmat_fill_synthetic(kq_qmat* a, uint64_t seed, uint64_t stream) {
+  if (!a) return set_err(KQ_ERR_ARG, "null matrix");
+  CU(cudaSetDevice(a->device));
+  int rc = qmat_write(a, a->R, nullptr, gen_base(seed, stream), RM_IDENT, 0, 0);
+  if (rc) return rc;
+  CU(cudaDeviceSynchronize());
+  return KQ_OK;
+}
+
+extern "C" int kq_qmat_dequant(kq_qmat* a, int row, int nrows, float* out) {
+  if (!a || !out || row < 0 || nrows < 1 || row + nrows > a->R) return set_err(KQ_ERR_ARG, "bad dequant request");
+  CU(cudaSetDevice(a->device));
+  float* d = nullptr;
+  const size_t n = (size_t)nrows * a->C;
+  CU(cudaMalloc(&d, n * 4));
+  k_qmat_dequant<<<(unsigned)((n + 255) / 256), 256>>>(a->view(), row, nrows, d);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaMemcpy(out, d, n * 4, cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (e != cudaSuccess) return set_err(KQ_ERR_BACKEND, std::string("dequant: ") + cudaGetErrorString(e));
+  return KQ_OK;
+}
+
+static int qmat_gemv_params(kq_qmat* a, const float* x_dev, float* y_dev, GemvParams& p, GemvPlan& pl) {
+  SegSpec ss[1] = {{a, EPI_F32, y_dev, nullptr}};
+  int rc = fill_gemv(ss, 1, false, g_dev[a->device].nsm, p, pl);
+  if (rc) return rc;
+  p.xmode = XS_PLAIN;
+  p.x = x_dev;
+  p.err = g_dev[a->device].err;
+  return KQ_OK;
+}
+
+extern "C" int kq_qmat_matvec_dev(kq_qmat* a, const float* x_dev, float* y_dev, void* stream) {
+  if (!a || !x_dev || !y_dev) return set_err(KQ_ERR_ARG, "null argument");
+  CU(cudaSetDevice(a->device));
+  GemvParams p;
+  GemvPlan pl;
+  int rc = qmat_gemv_params(a, x_dev, y_dev, p, pl);
+  if (rc) return rc;
+  CU(launch_gemv(p, pl, (cudaStream_t)stream, false));
+  return KQ_OK;
+}
+
+static int dev_err_check(int device) {
+  int e = 0;
+  CU(cudaMemcpy(&e, g_dev[device].err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (e) {
+    cudaMemset(g_dev[device].err, 0, sizeof(int));
+    return set_err(KQ_ERR_TIMEOUT, "a bounded device wait gave up");
+  }
+  return KQ_OK;
+}
+
+extern "C" int kq_qmat_matvec(kq_qmat* a, const float* x, float* y) {
+  if (!a || !x || !y) return set_err(KQ_ERR_ARG, "null argument");
+  CU(cudaSetDevice(a->device));
+  float *xd = nullptr, *yd = nullptr;
+  CU(cudaMalloc(&xd, (size_t)a->C * 4));
+  if (cudaMalloc(&yd, (size_t)a->R * 4) != cudaSuccess) { cudaFree(xd); return set_err(KQ_ERR_MEMORY, "matvec buffers"); }
+  int rc = KQ_OK;
+  if (cudaMemcpy(xd, x, (size_t)a->C * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "matvec upload");
+  if (!rc) rc = kq_qmat_matvec_dev(a, xd, yd, nullptr);
+  if (!rc && cudaMemcpy(y, yd, (size_t)a->R * 4, cudaMemcpyDeviceToHost) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "matvec download");
+  cudaFree(xd);
+  cudaFree(yd);
+  if (!rc) rc = dev_err_check(a->device);
+  return rc;
+}
+
+extern "C" int kq_qmat_matmul(kq_qmat* a, const float* x, int M, float* y) {
+  if (!a || !x || !y || M < 1 || M > 64) return set_err(KQ_ERR_ARG, "bad matmul arguments");
+  for (int mm = 0; mm < M; ++mm) {
+    const int rc = kq_qmat_matvec(a, x + (size_t)mm * a->C, y + (size_t)mm * a->R);
+    if (rc) return rc;
+  }
+  return KQ_OK;
+}
+
+extern "C" int kq_time_matvec(kq_qmat* const* mats, int ncopies, int n, float* ms_out) {
+  if (!mats || ncopies < 1 || n < 1 || !ms_out) return set_err(KQ_ERR_ARG, "bad timing arguments");
+  kq_qmat* a = mats[0];
+  for (int i = 1; i < ncopies; ++i)
+    if (!mats[i] || mats[i]->R != a->R || mats[i]->C != a->C || mats[i]->type != a->type || mats[i]->device != a->device)
+      return set_err(KQ_ERR_ARG, "timing copies must share shape, type and device");
+  CU(cudaSetDevice(a->device));
+  float *xd = nullptr, *yd = nullptr;
+  CU(cudaMalloc(&xd, (size_t)a->C * 4));
+  CU(cudaMalloc(&yd, (size_t)a->R * 4));
+  CU(cudaMemset(xd, 0, (size_t)a->C * 4));
+  cudaStream_t s;
+  CU(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  std::vector<GemvParams> ps(ncopies);
+  GemvPlan pl;
+  int rc = KQ_OK;
+  for (int i = 0; i < ncopies && !rc; ++i) rc = qmat_gemv_params(mats[i], xd, yd, ps[i], pl);
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  for (int i = 0; i < 3 * ncopies && !rc; ++i)
+    if (launch_gemv(ps[i % ncopies], pl, s, false) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "timing launch");
+  cudaEventRecord(e0, s);
+  for (int i = 0; i < n && !rc; ++i)
+    if (launch_gemv(ps[i % ncopies], pl, s, true) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "timing launch");
+  cudaEventRecord(e1, s);
+  cudaEventSynchronize(e1);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  *ms_out = ms / (float)n;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaStreamDestroy(s);
+  cudaFree(xd);
+  cudaFree(yd);
+  if (!rc) rc = dev_err_check(a->device);
+  return rc;
+}

@@ -1,0 +1,93 @@
+// kq_common.cuh -- device helpers shared by the kq kernels (sm_100a).
+//
+// PTX wrappers for mbarriers, non-tensor bulk copies (cp.async.bulk, the TMA engine's 1-D form),
+// L2 cache policies and programmatic dependent launch (griddepcontrol). Every wait on a barrier is
+// bounded: after KQ_WAIT_LIMIT polls it records an error in the model's device error word and the
+// caller unwinds, so a lost copy can never hang the GPU.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+
+namespace kq {
+
+// Device error word bits (read by the host after every synchronised call).
+enum : int {
+  KQ_DEV_ERR_WAIT_FULL = 1,     // a consumer gave up waiting for a weight stage
+  KQ_DEV_ERR_WAIT_EMPTY = 2,    // the producer gave up waiting for a free stage
+  KQ_DEV_ERR_DRAIN = 4,         // copies still in flight at exit after a failure
+  KQ_DEV_ERR_BAD_TOKEN = 8,     // a token id outside [0, vocab) reached a kernel
+  KQ_DEV_ERR_BAD_POS = 16,      // a position outside [0, ctx) reached a kernel
+};
+
+// Polls of mbarrier.try_wait before giving up. Each poll may suspend the thread for a
+// hardware-chosen time; 1 << 26 polls is seconds, orders of magnitude above any real wait.
+constexpr uint32_t KQ_WAIT_LIMIT = 1u << 26;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait; false (and the error bit set) if the phase never completed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int bit) {
+  for (uint32_t it = 0; it < KQ_WAIT_LIMIT; ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  if (err) atomicOr(err, bit);
+  return false;
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing `bytes` on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol) : "memory");
+}
+
+// Programmatic dependent launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(smem_u32(p)));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)));
+  return v;
+}
+
+__device__ __forceinline__ float h2f_bits(uint32_t h16) { return __half2float(__ushort_as_half((unsigned short)h16)); }
+
+// Named barrier over `nthreads` (a multiple of 32) threads.
+__device__ __forceinline__ void named_bar(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+}  // namespace kq

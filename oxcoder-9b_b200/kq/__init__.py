@@ -1,0 +1,318 @@
+"""kq -- Python face of the B200 Kindi-Q4 runtime (libkq.so, C ABI in include/kq.h).
+
+The host runtime is C++/CUDA; this module is a thin ctypes shim with the same engine interface
+as the reference's Q4 engines (scripts/kindi_q4/kindi/cpu4.py:94-236 and gpu4.py:50-110):
+
+    e = Engine(config)          # make_engine(pack, ctx) -> gpu4.Engine
+    e.reset(); e.feed(tok, pos); e.feed_batch(toks, pos)
+    e.step(tok, pos) -> greedy id; e.generate(ids, n) -> list; e.ylog -> logits
+
+Argument errors raise ValueError, positions past the context OverflowError, allocation failures
+MemoryError and CUDA failures RuntimeError, as in the reference engines. There is no CPU
+fallback: importing kq without libkq.so raises ImportError, and every call runs on the GPU.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libkq.so")
+Q4_K, Q6_K = 12, 14
+BLOCK = {Q4_K: 144, Q6_K: 210}
+T_EMB, T_OUT, T_OUTNORM, T_ATTN_NORM, T_Q, T_K, T_V, T_O, T_FFN_NORM, T_GATE, T_UP, T_DOWN = range(12)
+
+OK, ERR_ARG, ERR_BACKEND, ERR_OVERFLOW, ERR_MEMORY, ERR_TIMEOUT = 0, -1, -2, -3, -4, -5
+
+
+class Config(C.Structure):
+    """kq_config (include/kq.h)."""
+    _fields_ = [(n, C.c_int) for n in ("dim", "n_layers", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab", "ctx")] + \
+               [("rope_theta", C.c_float), ("eps", C.c_float)] + \
+               [(n, C.c_int) for n in ("t_q", "t_k", "t_v", "t_o", "t_gate", "t_up", "t_down", "t_emb", "t_out",
+                                       "max_tokens")]
+
+    @classmethod
+    def default(cls, **kw):
+        c = cls()
+        lib().kq_config_default(C.byref(c))
+        for k, v in kw.items():
+            if not hasattr(c, k):
+                raise ValueError("unknown config field %r" % k)
+            setattr(c, k, v)
+        return c
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+PF = C.POINTER(C.c_float)
+PI32 = C.POINTER(C.c_int32)
+PU16 = C.POINTER(C.c_uint16)
+
+# Every symbol include/kq.h declares, with its ctypes signature (restype, argtypes).
+SIGNATURES = {
+    "kq_version": (C.c_int, []),
+    "kq_error": (C.c_char_p, []),
+    "kq_device_count": (C.c_int, []),
+    "kq_config_default": (None, [C.POINTER(Config)]),
+    "kq_model_create": (C.c_void_p, [C.POINTER(Config), C.c_int]),
+    "kq_model_free": (None, [C.c_void_p]),
+    "kq_model_fill_synthetic": (C.c_int, [C.c_void_p, C.c_uint64]),
+    "kq_model_set_tensor": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
+    "kq_model_reset": (C.c_int, [C.c_void_p]),
+    "kq_model_fill_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64]),
+    "kq_model_get_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, PU16]),
+    "kq_feed": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "kq_step": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "kq_feed_batch": (C.c_int, [C.c_void_p, PI32, C.c_int, C.c_int]),
+    "kq_generate": (C.c_int, [C.c_void_p, PI32, C.c_int, C.c_int, PI32]),
+    "kq_logits": (C.c_int, [C.c_void_p, C.c_int, PF]),
+    "kq_hidden": (C.c_int, [C.c_void_p, PF]),
+    "kq_decode_loop": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, PI32]),
+    "kq_time_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, PF]),
+    "kq_qmat_create": (C.c_void_p, [C.c_int, C.c_int, C.c_int, C.c_int]),
+    "kq_qmat_free": (None, [C.c_void_p]),
+    "kq_qmat_upload": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    "kq_qmat_fill_synthetic": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64]),
+    "kq_qmat_dequant": (C.c_int, [C.c_void_p, C.c_int, C.c_int, PF]),
+    "kq_qmat_matvec": (C.c_int, [C.c_void_p, PF, PF]),
+    "kq_qmat_matmul": (C.c_int, [C.c_void_p, PF, C.c_int, PF]),
+    "kq_qmat_matvec_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "kq_time_matvec": (C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.c_int, PF]),
+    "kq_qmat_bytes": (C.c_size_t, [C.c_void_p]),
+}
+
+_lib = None
+
+
+def lib():
+    """The loaded libkq.so. Raises ImportError when it has not been built (no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError("libkq.so is not built (run `make -C oxcoder-9b_b200` or __graft_entry__.build())")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error():
+    return lib().kq_error().decode(errors="replace")
+
+
+def check(rc):
+    """Map a kq status code to the reference engines' exception types."""
+    if rc >= 0:
+        return rc
+    msg = last_error()
+    if rc == ERR_ARG:
+        raise ValueError(msg)
+    if rc == ERR_OVERFLOW:
+        raise OverflowError(msg)
+    if rc == ERR_MEMORY:
+        raise MemoryError(msg)
+    raise RuntimeError(msg or ("kq error %d" % rc))
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _ptr(a, t=PF):
+    return a.ctypes.data_as(t)
+
+
+# ----------------------------------------------------------------------------- matrices
+class QMat(object):
+    """A Q4_K / Q6_K matrix resident on the GPU (kc_matvec / kc_dequant hooks)."""
+
+    def __init__(self, type_, rows, cols, device=0):
+        self.type, self.rows, self.cols = int(type_), int(rows), int(cols)
+        h = lib().kq_qmat_create(self.type, self.rows, self.cols, device)
+        if not h:
+            msg = last_error()
+            raise (MemoryError if "alloc" in msg else ValueError)(msg)
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().kq_qmat_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def nbytes(self):
+        return int(lib().kq_qmat_bytes(self.h))
+
+    def upload(self, gguf_bytes):
+        b = np.ascontiguousarray(gguf_bytes, dtype=np.uint8)
+        check(lib().kq_qmat_upload(self.h, b.ctypes.data, b.nbytes))
+        return self
+
+    def fill_synthetic(self, seed, stream):
+        check(lib().kq_qmat_fill_synthetic(self.h, seed, stream))
+        return self
+
+    def dequant(self, row=0, nrows=None):
+        nrows = self.rows - row if nrows is None else nrows
+        out = np.empty((nrows, self.cols), np.float32)
+        check(lib().kq_qmat_dequant(self.h, row, nrows, _ptr(out)))
+        return out
+
+    def matvec(self, x):
+        x = _f32(x)
+        if x.shape != (self.cols,):
+            raise ValueError("x must have %d elements" % self.cols)
+        y = np.empty(self.rows, np.float32)
+        check(lib().kq_qmat_matvec(self.h, _ptr(x), _ptr(y)))
+        return y
+
+    def matmul(self, X):
+        X = _f32(X)
+        if X.ndim != 2 or X.shape[1] != self.cols:
+            raise ValueError("X must be [M, %d]" % self.cols)
+        Y = np.empty((X.shape[0], self.rows), np.float32)
+        check(lib().kq_qmat_matmul(self.h, _ptr(X), X.shape[0], _ptr(Y)))
+        return Y
+
+
+def time_matvec(mats, n):
+    """Mean ms per launch of the matvec rotating over `mats` (CUDA events)."""
+    arr = (C.c_void_p * len(mats))(*[m.h for m in mats])
+    ms = C.c_float()
+    check(lib().kq_time_matvec(arr, len(mats), n, C.byref(ms)))
+    return ms.value
+
+
+# ----------------------------------------------------------------------------- engine
+class Engine(object):
+    """Dense GQA decoder on one B200 (the gpu4.Engine interface).
+
+    config: a Config (default: the BASELINE config-2 model). seed: fill every tensor from the
+    seeded synthetic generator (None leaves the weights to set_tensor)."""
+
+    def __init__(self, config=None, device=0, seed=0, **overrides):
+        self.config = config if config is not None else Config.default(**overrides)
+        self.ctx = self.config.ctx
+        self.vocab = self.config.vocab
+        h = lib().kq_model_create(C.byref(self.config), device)
+        if not h:
+            msg = last_error()
+            raise (MemoryError if "alloc" in msg else ValueError)(msg)
+        self.h = h
+        self.device = device
+        if seed is not None:
+            check(lib().kq_model_fill_synthetic(self.h, seed))
+        self._ylog = None
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().kq_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    # ---- tensors
+    def set_tensor(self, layer, kind, data):
+        a = np.ascontiguousarray(data)
+        check(lib().kq_model_set_tensor(self.h, layer, kind, a.ctypes.data, a.nbytes))
+
+    def fill_kv(self, npos, seed):
+        check(lib().kq_model_fill_kv(self.h, npos, seed))
+
+    def get_kv(self, layer, which, npos):
+        out = np.empty(npos * self.config.n_kv_heads * self.config.head_dim, np.uint16)
+        check(lib().kq_model_get_kv(self.h, layer, which, npos, _ptr(out, PU16)))
+        return out
+
+    # ---- engine API (cpu4.Engine / gpu4.Engine)
+    def _validate(self, tok, pos):
+        if tok < 0 or tok >= self.vocab or pos < 0:
+            raise ValueError("Invalid token or position")
+        if pos >= self.ctx:
+            raise OverflowError("position %d is past the context (%d)" % (pos, self.ctx))
+
+    def reset(self):
+        check(lib().kq_model_reset(self.h))
+
+    def feed(self, tok, pos):
+        self._validate(tok, pos)
+        check(lib().kq_feed(self.h, int(tok), int(pos)))
+
+    def feed_batch(self, toks, pos):
+        t = np.ascontiguousarray(toks, dtype=np.int32)
+        for i, tok in enumerate(t):
+            self._validate(int(tok), pos + i)
+        check(lib().kq_feed_batch(self.h, _ptr(t, PI32), len(t), int(pos)))
+
+    def step(self, tok, pos):
+        self._validate(tok, pos)
+        self._ylog = None
+        return check(lib().kq_step(self.h, int(tok), int(pos)))
+
+    def generate(self, ids, n):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        for i, tok in enumerate(ids):
+            self._validate(int(tok), i)
+        if len(ids) + n - 1 > self.ctx:
+            raise OverflowError("generation runs past the context")
+        out = np.empty(n, np.int32)
+        check(lib().kq_generate(self.h, _ptr(ids, PI32), len(ids), n, _ptr(out, PI32)))
+        return [int(t) for t in out]
+
+    def decode_loop(self, tok, pos, n):
+        """n greedy steps on the device without host round trips."""
+        self._validate(tok, pos)
+        out = np.empty(n, np.int32)
+        check(lib().kq_decode_loop(self.h, int(tok), int(pos), int(n), _ptr(out, PI32)))
+        return [int(t) for t in out]
+
+    def time_decode(self, tok, pos, n):
+        ms = C.c_float()
+        check(lib().kq_time_decode(self.h, int(tok), int(pos), int(n), C.byref(ms)))
+        return ms.value
+
+    @property
+    def ylog(self):
+        """Logits of the last step (Engine.ylog[:ylog_n])."""
+        out = np.empty(self.vocab, np.float32)
+        check(lib().kq_logits(self.h, 0, _ptr(out)))
+        return out
+
+    @property
+    def ylog_n(self):
+        return self.vocab
+
+    ylog_map = None
+
+    def hidden(self):
+        out = np.empty(self.config.dim, np.float32)
+        check(lib().kq_hidden(self.h, _ptr(out)))
+        return out
+
+
+def make_engine(config=None, ctx=None, device=0, seed=0, **overrides):
+    """engine.make_engine for the Q4 path: one GPU engine (no spec/approximate head flags)."""
+    if ctx is not None:
+        overrides["ctx"] = ctx
+    return Engine(config, device=device, seed=seed, **overrides)

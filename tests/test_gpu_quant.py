@@ -1,0 +1,96 @@
+"""GPU: bit-exact dequantisation and the fused-dequant GEMV against the CPU oracle, through the
+C ABI (kq_qmat_*). The reference's bar: dequantisation bit-exact (q4kernels.h:12-33), matrix
+products within 1e-3 relative L2 of Kindi's CPU path (here also checked at 1e-5)."""
+import numpy as np
+import pytest
+
+from conftest import rel_l2, same_bits_or_both_nan
+
+pytestmark = pytest.mark.gpu
+
+RTOL_L2 = 1e-3        # north-star tolerance for GEMV outputs
+TIGHT_L2 = 2e-5       # what the exact int8 digit-plane arithmetic actually achieves
+
+
+@pytest.fixture(scope="module")
+def kq():
+    import kq as K
+    assert K.lib().kq_device_count() > 0, "no GPU"
+    return K
+
+
+@pytest.mark.parametrize("ty", [12, 14])
+@pytest.mark.parametrize("case", ["refcase", "synth", "edge"])
+def test_dequant_bit_exact_on_golden(kq, golden, ty, case):
+    raw = golden["%s_raw_%d" % (case, ty)]
+    R, Cc = raw.shape[0], raw.shape[1] * 256 if raw.ndim == 3 else 1024
+    if raw.ndim == 1:
+        R = 64
+    m = kq.QMat(ty, R, Cc).upload(raw.reshape(-1))
+    assert same_bits_or_both_nan(m.dequant(), golden["%s_dense_%d" % (case, ty)].reshape(R, Cc))
+
+
+@pytest.mark.parametrize("ty", [12, 14])
+def test_device_generator_matches_oracle(kq, oracle, ty):
+    R, Cc = 24, 2048
+    m = kq.QMat(ty, R, Cc).fill_synthetic(0, 7)
+    W = oracle.gen_matrix(R, Cc, ty, 0, 7)
+    ref = oracle.decode_blocks(W.reshape(-1, oracle.BLOCK[ty]), ty).reshape(R, Cc)
+    assert same_bits_or_both_nan(m.dequant(), ref)
+
+
+SHAPES = [(12, 12288, 4096), (14, 4096, 12288), (14, 1024, 4096), (12, 4096, 4096), (12, 8, 256),
+          (14, 16, 512), (12, 40, 1024), (14, 64, 2048), (12, 128, 6144), (14, 8, 4096)]
+
+
+@pytest.mark.parametrize("ty,R,Cc", SHAPES)
+def test_matvec_parity(kq, oracle, ty, R, Cc):
+    W = oracle.gen_matrix(R, Cc, ty, 0, 100 + R)
+    x = oracle.gen_normal(Cc, 0.0, 1.0, 1, R)
+    m = kq.QMat(ty, R, Cc).upload(W)
+    y = m.matvec(x)
+    ref = oracle.matvec(W, R, Cc, ty, x)
+    e = rel_l2(y, ref)
+    assert e < RTOL_L2
+    assert e < TIGHT_L2, e
+
+
+def test_matvec_golden_reference_case(kq, golden):
+    for ty in (12, 14):
+        raw = golden["refcase_raw_%d" % ty]
+        m = kq.QMat(ty, 16, 512).upload(raw.reshape(-1))
+        assert rel_l2(m.matvec(golden["refcase_x_%d" % ty]), golden["refcase_y_%d" % ty]) < TIGHT_L2
+
+
+def test_matvec_edge_activations(kq, oracle):
+    """Zero, tiny, huge-range and non-finite activations."""
+    R, Cc = 16, 1024
+    W = oracle.gen_matrix(R, Cc, 12, 0, 5)
+    m = kq.QMat(12, R, Cc).upload(W)
+    assert np.array_equal(m.matvec(np.zeros(Cc, np.float32)), oracle.matvec(W, R, Cc, 12, np.zeros(Cc, np.float32)))
+    x = oracle.gen_normal(Cc, 0.0, 1.0, 1, 9)
+    x[:256] *= 1e-30
+    x[256:512] *= 1e20
+    assert rel_l2(m.matvec(x), oracle.matvec(W, R, Cc, 12, x)) < TIGHT_L2
+    x[3] = np.nan
+    assert np.isnan(m.matvec(x)).all()
+
+
+def test_matvec_nan_weights_propagate(kq, golden):
+    raw = golden["edge_raw_12"]
+    m = kq.QMat(12, 8, 256).upload(raw.reshape(-1))
+    y = m.matvec(np.ones(256, np.float32))
+    assert np.isnan(y[1])          # all-0xFF block: d = NaN
+    assert np.isfinite(y[0]) and y[0] == 0.0
+
+
+def test_bad_shapes_rejected(kq):
+    with pytest.raises(ValueError):
+        kq.QMat(12, 7, 256)
+    with pytest.raises(ValueError):
+        kq.QMat(12, 8, 300)
+    with pytest.raises(ValueError):
+        kq.QMat(13, 8, 256)
+    m = kq.QMat(12, 8, 256)
+    with pytest.raises(ValueError):
+        m.upload(np.zeros(100, np.uint8))
