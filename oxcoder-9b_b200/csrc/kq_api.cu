@@ -59,8 +59,10 @@ static int dev_init(int device) {
   CU(cudaDeviceGetAttribute(&d.nsm, cudaDevAttrMultiProcessorCount, device));
   int optin = 0;
   CU(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
-  d.smem_optin = (size_t)optin;
-  CU(cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+  cudaFuncAttributes fa;
+  CU(cudaFuncGetAttributes(&fa, k_gemv));
+  d.smem_optin = (size_t)optin - fa.sharedSizeBytes;
+  CU(cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.smem_optin));
   CU(cudaMalloc(&d.err, sizeof(int)));
   CU(cudaMemset(d.err, 0, sizeof(int)));
   d.init = true;

@@ -36,9 +36,9 @@ struct AttnParams {
 template <int G>
 __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const __grid_constant__ AttnParams P) {
   constexpr int HD = 128;
-  __shared__ float s_sc[G][ATT_P];
+  __shared__ __align__(16) float s_sc[G][ATT_P];
   __shared__ float s_m[G], s_l[G];
-  __shared__ float s_red[ATT_THREADS / 32][G][HD];   // per-warp partial o
+  __shared__ __align__(16) float s_red[ATT_THREADS / 32][G][HD];   // per-warp partial o (float4 stores)
   __shared__ int s_last;
   const int kv = blockIdx.x, sp = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, hl = lane & 15, half = lane >> 4;
