@@ -123,6 +123,25 @@ def run_reference(args, rank, world):
     return 0
 
 
+def run_profile_mode(args):
+    """decode-only: fill the config-2 model (optionally fewer layers), W + K device-resident
+    decode steps at ctx 4K. gemv-only: the config-0 Q4_K GEMV over 16 rotating copies."""
+    import kq
+    if args.mode == "gemv-only":
+        mats = [kq.QMat(12, 12288, 4096).fill_synthetic(0, 1000 + i) for i in range(16)]
+        kq.time_matvec(mats, args.warmup)
+        ms = kq.time_matvec(mats, args.steps)
+        print(json.dumps({"mode": "gemv-only", "ms_per_launch": ms, "gbs": CFG0_BYTES / (ms * 1e-3) / 1e9}))
+        return 0
+    e = kq.Engine(kq.Config.default(ctx=CTX, n_layers=args.layers), seed=0)
+    pos0 = CTX - (args.steps + args.warmup) - 1
+    e.fill_kv(pos0, 2)
+    e.time_decode(1, pos0, args.warmup)
+    ms = e.time_decode(1, pos0 + args.warmup, args.steps)
+    print(json.dumps({"mode": "decode-only", "ms_per_step": ms / args.steps, "tok_s": args.steps / (ms / 1000.0)}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -130,7 +149,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=32, help="decode-only: layers of the model (small ncu captures)")
+    ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only"],
+                    help="decode-only / gemv-only: the small commands the ncu captures in profiles/ run")
     args = ap.parse_args()
+    if args.mode != "full":
+        return run_profile_mode(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -40,6 +41,16 @@ static int set_err(int code, const std::string& msg) {
     if (e_ != cudaSuccess) { set_err(KQ_ERR_BACKEND, std::string(#call) + ": " + cudaGetErrorString(e_)); return nullptr; } \
   } while (0)
 
+// ------------------------------------------------------------------------------ kernel table
+typedef void (*GemvFn)(GemvParams);
+static GemvFn gemv_fn(int tm, int rpg) {
+  static const GemvFn tab[3][3] = {
+      {k_gemv<TM_Q4K, 1>, k_gemv<TM_Q4K, 2>, k_gemv<TM_Q4K, 4>},
+      {k_gemv<TM_Q6K, 1>, k_gemv<TM_Q6K, 2>, k_gemv<TM_Q6K, 4>},
+      {k_gemv<TM_MIXED, 1>, k_gemv<TM_MIXED, 2>, k_gemv<TM_MIXED, 4>}};
+  return tab[tm - 1][rpg == 1 ? 0 : rpg == 2 ? 1 : 2];
+}
+
 // ------------------------------------------------------------------------------ per-device context
 struct DevCtx {
   bool init = false;
@@ -59,10 +70,17 @@ static int dev_init(int device) {
   CU(cudaDeviceGetAttribute(&d.nsm, cudaDevAttrMultiProcessorCount, device));
   int optin = 0;
   CU(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
-  cudaFuncAttributes fa;
-  CU(cudaFuncGetAttributes(&fa, k_gemv));
-  d.smem_optin = (size_t)optin - fa.sharedSizeBytes;
-  CU(cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.smem_optin));
+  size_t static_max = 0;
+  for (int tm = 1; tm <= 3; ++tm)
+    for (int ri = 0; ri < 3; ++ri) {
+      cudaFuncAttributes fa;
+      CU(cudaFuncGetAttributes(&fa, gemv_fn(tm, 1 << ri)));
+      static_max = std::max(static_max, (size_t)fa.sharedSizeBytes);
+    }
+  d.smem_optin = (size_t)optin - static_max;
+  for (int tm = 1; tm <= 3; ++tm)
+    for (int ri = 0; ri < 3; ++ri)
+      CU(cudaFuncSetAttribute(gemv_fn(tm, 1 << ri), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.smem_optin));
   CU(cudaMalloc(&d.err, sizeof(int)));
   CU(cudaMemset(d.err, 0, sizeof(int)));
   d.init = true;
@@ -72,19 +90,16 @@ static int dev_init(int device) {
 // ------------------------------------------------------------------------------ matrices
 struct kq_qmat {
   int device = 0, type = 0, R = 0, C = 0, G = 0;
-  uint8_t* buf = nullptr;
-  size_t off[4] = {0, 0, 0, 0};
+  uint8_t* buf = nullptr;   // R/8 tiles (kq layout)
   size_t bytes = 0;
   QView view() const {
     QView v;
-    v.p0 = buf + off[0]; v.p1 = buf + off[1]; v.p2 = buf + off[2]; v.p3 = buf + off[3];
-    v.type = type; v.R = R; v.C = C; v.G = G;
+    v.base = buf; v.type = type; v.R = R; v.C = C; v.G = G;
     return v;
   }
   QViewW wview() {
     QViewW v;
-    v.p0 = buf + off[0]; v.p1 = buf + off[1]; v.p2 = buf + off[2]; v.p3 = buf + off[3];
-    v.type = type; v.R = R; v.C = C; v.G = G;
+    v.base = buf; v.type = type; v.R = R; v.C = C; v.G = G;
     return v;
   }
 };
@@ -96,8 +111,8 @@ static int check_shape(int type, int R, int C) {
   if (R <= 0 || C <= 0 || R % 8 || C % 256)
     return set_err(KQ_ERR_ARG, "Invalid packed tensor dimensions: rows must be a positive multiple of 8 and cols of 256");
   const int LPR = 4 * (C / 256);
-  if (!(LPR == 4 || LPR == 8 || LPR == 16 || (LPR % 32 == 0 && LPR <= 384)))
-    return set_err(KQ_ERR_ARG, "unsupported column count (need 256, 512, 1024 or a multiple of 2048 up to 24576)");
+  if (!(LPR == 4 || LPR == 8 || LPR == 16 || (LPR % 32 == 0 && LPR <= 256)))
+    return set_err(KQ_ERR_ARG, "unsupported column count (need 256, 512, 1024 or a multiple of 2048 up to 16384)");
   return KQ_OK;
 }
 
@@ -107,13 +122,8 @@ static kq_qmat* qmat_alloc(int type, int R, int C, int device) {
   CUP(cudaSetDevice(device));
   kq_qmat* a = new kq_qmat();
   a->device = device; a->type = type; a->R = R; a->C = C; a->G = C / 256;
-  size_t o = 0;
-  for (int p = 0; p < 4; ++p) {
-    a->off[p] = o;
-    o = align_up(o + (size_t)R * plane_row_bytes(type, p, a->G), 256);
-  }
   a->bytes = (size_t)R * a->G * block_bytes(type);
-  if (cudaMalloc(&a->buf, o) != cudaSuccess) {
+  if (cudaMalloc(&a->buf, a->bytes) != cudaSuccess) {
     delete a;
     set_err(KQ_ERR_MEMORY, "device allocation of a quantised matrix failed");
     return nullptr;
@@ -145,45 +155,64 @@ static int qmat_upload_mapped(kq_qmat* a, const void* host, size_t bytes, int R_
 
 // ------------------------------------------------------------------------------ GEMV planning
 struct GemvPlan {
-  int TR, LPR, NRG, RPG, stage_bytes, nslots, threads, grid;
+  int TR, LPR, NRG, RPG, TM, stage_bytes, nslots, threads, grid;
   size_t smem;
 };
 
-static const size_t KQ_SMEM_BUDGET = 104 * 1024;   // leaves room for the next kernel's CTA (PDL)
+static const size_t KQ_SMEM_BUDGET = 220 * 1024;
 
-static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, bool pairs, int nsm, GemvPlan& pl) {
+// Launch shape of a (fused) GEMV over segments sharing the column count C.
+static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, bool pairs, int nsm, size_t optin,
+                     GemvPlan& pl) {
   const int G = C / 256, LPR = 4 * G;
   int rowb = 0;
-  for (int i = 0; i < nseg; ++i) rowb = std::max(rowb, block_bytes(types[i]) * G);
-  int TR = 8;
-  while (TR > 2 && TR * rowb > 28 * 1024) TR /= 2;
-  while (TR < 8 && (TR * G) % 8) TR *= 2;
-  if (pairs && TR < 2) TR = 2;
-  int NRG = 0;
-  for (int n = TR; n >= 1; --n) {
-    if (TR % n) continue;
-    if (LPR * n > 384) continue;
-    if ((LPR * n) % 32) continue;
-    if (pairs && ((TR / n) % 2)) continue;
-    if (n > 14) continue;
-    NRG = n;
-    break;
+  bool has4 = false, has6 = false;
+  for (int i = 0; i < nseg; ++i) {
+    rowb = std::max(rowb, block_bytes(types[i]) * G);
+    has4 |= types[i] == KQ_Q4_K;
+    has6 |= types[i] == KQ_Q6_K;
   }
-  if (!NRG) return set_err(KQ_ERR_ARG, "no valid GEMV launch shape for this column count");
-  pl.TR = TR; pl.LPR = LPR; pl.NRG = NRG; pl.RPG = TR / NRG;
-  pl.stage_bytes = (int)align_up((size_t)TR * rowb, 128);
-  const int WPR = LPR >= 32 ? LPR / 32 : 1;
-  const size_t extra = 2 * sizeof(uint64_t) * 16 + sizeof(float) * (2 * pl.RPG * NRG * WPR + 2) +
-                       sizeof(double) * NRG * WPR + 8 * NRG + 64;
-  int slots = (int)((KQ_SMEM_BUDGET - extra) / pl.stage_bytes);
-  slots = std::min(12, std::max(2, slots));
-  pl.nslots = slots;
-  pl.smem = (size_t)slots * pl.stage_bytes + sizeof(uint64_t) * 2 * slots + sizeof(float) * (2 * pl.RPG * NRG * WPR + 2) +
-            sizeof(double) * NRG * WPR + sizeof(float) * NRG + sizeof(int) * NRG + 64;
-  pl.threads = LPR * NRG + 32;
-  int nstages = 0;
-  for (int i = 0; i < nseg; ++i) nstages += seg_rows[i] / TR;
-  pl.grid = std::max(1, std::min(nsm, nstages));
+  const size_t budget = std::min(KQ_SMEM_BUDGET, optin);
+  // tuning override for sweeps: KQ_GEMV_RPG (1, 2, 4) and KQ_GEMV_NRG fix the shape if valid
+  const int want_rpg = std::getenv("KQ_GEMV_RPG") ? std::atoi(std::getenv("KQ_GEMV_RPG")) : 0;
+  const int want_nrg = std::getenv("KQ_GEMV_NRG") ? std::atoi(std::getenv("KQ_GEMV_NRG")) : 0;
+  // Candidates are scored: (a) every CTA gets >= 4 stages, so the weight stream is pipelined
+  // from the start (small matrices need short stages); (b) more consumer warps; (c) more rows
+  // per thread (activation reuse).
+  bool found = false;
+  long best = -1;
+  for (int NRG = std::min(KQ_MAX_NRG, KQ_GEMV_MAX_CONSUMERS / LPR); NRG >= 1; --NRG) {
+    if ((LPR * NRG) % 32) continue;
+    if (8 * LPR > KQ_MAX_ITEMS * LPR * NRG) continue;   // prologue items per thread
+    for (int RPG : {4, 2, 1}) {
+      if (pairs && (RPG & 1)) continue;
+      if (want_rpg && RPG != want_rpg) continue;
+      if (want_nrg && NRG != want_nrg) continue;
+      const int TR = NRG * RPG;
+      if (TR % 8) continue;                              // stages are whole 8-row tiles
+      const int stage_bytes = (int)align_up((size_t)TR * rowb, 128);
+      const GemvSmem L0 = gemv_smem_layout(0, stage_bytes, LPR, NRG, RPG, LPR * NRG);
+      const size_t fixed = L0.total + 64;
+      if (fixed + 2 * ((size_t)stage_bytes + 16) > budget) continue;
+      int nstages = 0;
+      for (int i = 0; i < nseg; ++i) nstages += (seg_rows[i] + TR - 1) / TR;
+      const int grid = std::max(1, std::min(nsm, nstages));
+      const long score = (nstages >= 4 * grid ? 1L << 20 : 0) + (long)(LPR * NRG) * 8 + RPG;
+      if (score <= best) continue;
+      best = score;
+      found = true;
+      int slots = (int)((budget - fixed) / (stage_bytes + 16));
+      slots = std::min(8, std::max(2, slots));
+      pl.TR = TR; pl.LPR = LPR; pl.NRG = NRG; pl.RPG = RPG;
+      pl.TM = has4 && has6 ? TM_MIXED : has6 ? TM_Q6K : TM_Q4K;
+      pl.stage_bytes = stage_bytes;
+      pl.nslots = slots;
+      pl.smem = gemv_smem_layout(slots, stage_bytes, LPR, NRG, RPG, LPR * NRG).total;
+      pl.threads = LPR * NRG + 32;
+      pl.grid = grid;
+    }
+  }
+  if (!found) return set_err(KQ_ERR_ARG, "no valid GEMV launch shape for this column count");
   return KQ_OK;
 }
 
@@ -203,7 +232,7 @@ static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParam
     types[i] = ss[i].m->type;
     rows[i] = ss[i].m->R;
   }
-  int rc = plan_gemv(C, types, nseg, rows, pairs, nsm, pl);
+  int rc = plan_gemv(C, types, nseg, rows, pairs, nsm, g_dev[ss[0].m->device].smem_optin, pl);
   if (rc) return rc;
   std::memset(&p, 0, sizeof(p));
   p.nseg = nseg;
@@ -211,14 +240,14 @@ static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParam
   for (int i = 0; i < nseg; ++i) {
     p.seg[i].w = ss[i].m->view();
     p.seg[i].stage0 = st;
-    p.seg[i].nstage = ss[i].m->R / pl.TR;
+    p.seg[i].nstage = (ss[i].m->R + pl.TR - 1) / pl.TR;
     p.seg[i].epi = ss[i].epi;
     p.seg[i].out_f = ss[i].out_f;
     p.seg[i].out_h = ss[i].out_h;
     st += p.seg[i].nstage;
   }
   p.nstages = st;
-  p.C = C; p.G = C / 256; p.TR = pl.TR; p.LPR = pl.LPR; p.NRG = pl.NRG; p.RPG = pl.RPG;
+  p.C = C; p.G = C / 256; p.TR = pl.TR; p.LPR = pl.LPR; p.NRG = pl.NRG;
   p.stage_bytes = pl.stage_bytes; p.nslots = pl.nslots;
   return KQ_OK;
 }
@@ -234,7 +263,7 @@ static cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& pl, cudaStre
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_gemv, p);
+  return cudaLaunchKernelEx(&cfg, gemv_fn(pl.TM, pl.RPG), p);
 }
 
 template <int G>
@@ -354,7 +383,7 @@ static int validate_cfg(const kq_config& c) {
   if (G != 1 && G != 2 && G != 4 && G != 8) return set_err(KQ_ERR_ARG, "query heads per kv head must be 1, 2, 4 or 8");
   if (c.dim < 512) return set_err(KQ_ERR_ARG, "dim must be at least 512");
   if (c.n_heads * c.head_dim < 512) return set_err(KQ_ERR_ARG, "n_heads * head_dim must be at least 512");
-  if (c.ctx < 1 || c.ctx > 1 << 20) return set_err(KQ_ERR_ARG, "ctx out of range");
+  if (c.ctx < 1 || c.ctx > ATT_P * ATT_MAX_SPLITS) return set_err(KQ_ERR_ARG, "ctx out of range (1 .. 65536)");
   if (c.vocab <= 0 || c.vocab % 8) return set_err(KQ_ERR_ARG, "vocab must be a positive multiple of 8");
   if (c.t_gate != c.t_up) return set_err(KQ_ERR_ARG, "gate and up must share a quantisation type");
   if (c.n_layers < 1) return set_err(KQ_ERR_ARG, "n_layers must be positive");
@@ -574,6 +603,7 @@ extern "C" int kq_model_get_kv(kq_model* m, int layer, int which, int npos, uint
 // ------------------------------------------------------------------------------ decode step
 static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
   const kq_config& c = m->c;
+  int trace = 0;   // launch index within the step (phase trace of KQ_TRACE builds)
   const int G = c.n_heads / c.n_kv_heads;
   GemvParams p;
   GemvPlan pl;
@@ -588,6 +618,7 @@ static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
     pp.ctx = c.ctx;
     pp.err = m->err;
     pp.eps = c.eps;
+    pp.trace_id = trace++;
   };
   for (int l = 0; l < c.n_layers; ++l) {
     LayerW& w = m->L[l];
@@ -617,6 +648,7 @@ static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
     a.out = m->att; a.st = m->st; a.n_kv = c.n_kv_heads; a.ctx = c.ctx; a.nsplit = m->nsplit;
     a.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
     a.err = m->err;
+    a.trace_id = trace++;
     CU(launch_attn(a, G, s, true));
     // o projection
     SegSpec so[1] = {{w.o, EPI_F32, m->y, nullptr}};
@@ -804,6 +836,22 @@ extern "C" int kq_time_decode(kq_model* m, int tok, int pos, int n, float* ms_ou
   *ms_out = ms;
   return check_dev_err(m);
 }
+
+#ifdef KQ_TRACE
+// Trace builds only (not part of include/kq.h): copy the phase-trace buffer to the host.
+extern "C" int kq_trace_read(unsigned long long* out, size_t n) {
+  const size_t total = (size_t)KQ_TRACE_LAUNCHES * KQ_TRACE_CTAS * KQ_TRACE_POINTS;
+  if (n > total) n = total;
+  CU(cudaMemcpyFromSymbol(out, g_kq_trace, n * sizeof(unsigned long long)));
+  return KQ_OK;
+}
+extern "C" int kq_trace_clear(void) {
+  static unsigned long long zero[KQ_TRACE_CTAS * KQ_TRACE_POINTS];
+  for (int l = 0; l < KQ_TRACE_LAUNCHES; ++l)
+    CU(cudaMemcpyToSymbol(g_kq_trace, zero, sizeof(zero), (size_t)l * sizeof(zero)));
+  return KQ_OK;
+}
+#endif
 
 // ------------------------------------------------------------------------------ matrix hooks
 extern "C" kq_qmat* kq_qmat_create(int type, int rows, int cols, int device) { return qmat_alloc(type, rows, cols, device); }

@@ -90,4 +90,24 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// ------------------------------------------------------------------------------ tracing
+// Compile-time opt-in (-DKQ_TRACE): per-CTA %globaltimer stamps at phase boundaries of the decode
+// kernels, written to a device buffer the host reads with kq_trace_read (kq_api.cu). Off by
+// default; the product build contains no trace code.
+constexpr int KQ_TRACE_LAUNCHES = 256, KQ_TRACE_CTAS = 1024, KQ_TRACE_POINTS = 8;
+#ifdef KQ_TRACE
+__device__ unsigned long long g_kq_trace[KQ_TRACE_LAUNCHES][KQ_TRACE_CTAS][KQ_TRACE_POINTS];
+__device__ __forceinline__ void kq_trace(int launch, int point) {
+  if (launch < 0 || launch >= KQ_TRACE_LAUNCHES) return;
+  const int cta = blockIdx.x + blockIdx.y * gridDim.x;
+  if (cta >= KQ_TRACE_CTAS) return;
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  g_kq_trace[launch][cta][point] = t;
+}
+#define KQ_TRACE_AT(launch, point) kq_trace((launch), (point))
+#else
+#define KQ_TRACE_AT(launch, point) ((void)0)
+#endif
+
 }  // namespace kq

@@ -4,20 +4,24 @@
 // q4_rms (:39-46) and q4_silu (:36-38), and the rope / K-V store of engine.py:260-267.
 //
 // Design:
-//  * Persistent CTAs, one producer warp per CTA streaming runs of TR rows ("stages") of every
-//    weight plane from HBM into a shared-memory ring with 1-D bulk copies (cp.async.bulk, L2
-//    evict-first), completion tracked by mbarriers. The producer starts before
-//    griddepcontrol.wait, so the weight stream of kernel N+1 overlaps the tail of kernel N.
-//  * Activations stay in registers. Thread u of a row group owns the 64 columns of "unit"
-//    (g, h, jh) (see kq_qformat.cuh) for every row. Its 64 fp32 activations are split exactly
-//    into three int8 digit planes x = s1*x1 + s2*x2 + s3*x3 (s1 a power of two with
-//    max|x| <= 127*s1, s2 = s1/128, s3 = s1/16384; residual <= s1/32768), so the dot products
-//    with 4- and 6-bit weights are exact int32 dp4a sums per 16-element group; the groups are
-//    combined with the block scales in fp32 and the row partials summed with a fixed warp-shuffle
-//    tree, then across the row's warps in a fixed order.
-//  * Fusions: the prologue does the residual add + fp64 RMS norm (q4_rms) or the embedding-row
-//    dequantisation (q4_embed); the epilogue does the NeoX rotary + fp16 K/V store, the V store,
-//    SwiGLU, or the output-head argmax (lowest index on ties, like k_argmax kindi.cu:637-661).
+//  * Persistent CTAs (one per SM). A producer warp streams "stages" of TR rows (whole 8-row tiles
+//    of the kq layout, so ONE contiguous 1-D bulk copy per stage, cp.async.bulk with L2
+//    evict-first) into a shared-memory ring; completion is tracked by mbarriers. The producer
+//    starts before griddepcontrol.wait, so the weight stream of kernel N+1 starts while kernel N
+//    finishes.
+//  * Activations: in the prologue the CTA splits its fp32 activation vector exactly into three
+//    int8 digit planes, x = s1*x1 + s2*x2 + s3*x3 per 64-column "unit" (s1 a power of two with
+//    max|x| <= 127*s1, s2 = s1/128, s3 = s1/16384; residual <= s1/32768), stored in shared
+//    memory as [group k][plane][unit] (conflict-free 16-byte reads).
+//  * Consumers: thread u of a row group owns unit u (64 columns, see kq_qformat.cuh) and RPG rows
+//    of every stage. Dot products of the 4-/6-bit weights with the digit planes are exact int32
+//    dp4a sums per 16-element group, multiplied by the integer block scales in int32; the three
+//    planes are combined once per row in fp32. Row partials are reduced with a fixed warp-shuffle
+//    tree, then across the row's warps in a fixed order (one named barrier per stage), so results
+//    do not depend on timing.
+//  * Fusions: prologue = residual add + fp64 RMS norm (q4_rms) or embedding-row dequantisation
+//    (q4_embed); epilogue = NeoX rotary + fp16 K/V store, V store, SwiGLU, or the output-head
+//    argmax with a last-CTA merge (lowest index on ties, like k_argmax kindi.cu:637-661).
 #pragma once
 #include "kq_common.cuh"
 #include "kq_qformat.cuh"
@@ -27,8 +31,14 @@ namespace kq {
 
 enum { EPI_F32 = 0, EPI_ROPE_Q = 1, EPI_ROPE_K = 2, EPI_V = 3, EPI_SWIGLU = 4, EPI_ARGMAX = 5 };
 enum { XS_PLAIN = 0, XS_NORM = 1, XS_EMBED = 2 };
+enum { TM_Q4K = 1, TM_Q6K = 2, TM_MIXED = 3 };
 constexpr int KQ_MAX_SEG = 4;
-constexpr int KQ_GEMV_MAX_THREADS = 416;   // 384 consumers + 1 producer warp
+constexpr int KQ_GEMV_MAX_CONSUMERS = 384;
+constexpr int KQ_GEMV_MAX_THREADS = KQ_GEMV_MAX_CONSUMERS + 32;   // + one producer warp
+constexpr int KQ_MAX_NRG = 8;              // row groups (named barriers 1..8)
+constexpr int KQ_BAR_PROLOGUE = 14, KQ_BAR_ARGMAX = 15;
+constexpr int KQ_XSCAL = 18;               // per-unit scalars: s3, poison, xsf[4], c[3][4]
+constexpr int KQ_MAX_ITEMS = 4;            // prologue items per thread: the planner keeps >= 2 row groups
 
 struct DecodeState {   // device-resident per-step state
   int tok;        // token processed by this step
@@ -48,7 +58,7 @@ struct Seg {
 struct GemvParams {
   Seg seg[KQ_MAX_SEG];
   int nseg, nstages;
-  int C, G, TR, LPR, NRG, RPG;
+  int C, G, TR, LPR, NRG;
   int stage_bytes, nslots;
   // activation source
   int xmode;
@@ -71,256 +81,126 @@ struct GemvParams {
   int* out_ids;          // ARGMAX: token of step st->steps is written here (device loop)
   int out_cap;
   int* err;
+  int trace_id;          // launch index for the optional phase trace (KQ_TRACE builds)
 };
 
-// ------------------------------------------------------------------------------ activations
-struct XL {
-  uint32_t w[4][3][4];   // [group k][digit plane][word] int8 x 4
-  float s3;
-  float xsf[4];          // sum of the group's digits, 16384*S1 + 128*S2 + S3, as float
-  int c0[4], c1[4];      // 32*S1 and 32*(128*S2 + S3): the "-32" of Q6_K, exact
-  float poison;          // NaN if any activation of the unit was not finite
+// Shared-memory carve-up, identical on host (sizing) and device.
+struct GemvSmem {
+  size_t stages, xplanes, xscal, bars, red, redd, best, total;
 };
+__host__ __device__ inline size_t gs_align(size_t x, size_t a) { return (x + a - 1) / a * a; }
+__host__ __device__ inline GemvSmem gemv_smem_layout(int nslots, int stage_bytes, int LPR, int NRG, int RPG, int nthr_c) {
+  GemvSmem s;
+  const int WPR = LPR >= 32 ? LPR / 32 : 1;
+  size_t o = 0;
+  s.stages = o; o += (size_t)nslots * stage_bytes;
+  s.xplanes = o = gs_align(o, 128); o += (size_t)12 * LPR * 16;
+  s.xscal = o = gs_align(o, 16); o += (size_t)KQ_XSCAL * LPR * 4;
+  s.bars = o = gs_align(o, 8); o += (size_t)2 * nslots * 8;
+  s.red = o = gs_align(o, 8); o += (size_t)2 * RPG * NRG * WPR * 4;
+  s.redd = o = gs_align(o, 8); o += (size_t)((nthr_c + 31) / 32) * 8;
+  s.best = o = gs_align(o, 8); o += (size_t)NRG * RPG * 8;
+  s.total = gs_align(o, 128);
+  return s;
+}
 
 __device__ __forceinline__ float pow2f(int k) { return __int_as_float((k + 127) << 23); }
-
-// v[k][j']: the unit's 64 activations, column 256g + 128h + 32k + 16jh + j'.
-__device__ __forceinline__ void build_xl(const float (&v)[4][16], XL& xl) {
-  float m = 0.f;
-  bool bad = false;
-#pragma unroll
-  for (int k = 0; k < 4; ++k)
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float a = fabsf(v[k][j]);
-      bad |= !(a <= FLT_MAX);
-      m = fmaxf(m, a);
-    }
-  int e = 0;
-  if (!bad && m >= 0x1p-100f) {
-    e = ilogbf(m) - 6;
-    if (m > 127.f * pow2f(e)) ++e;
-  }
-  const float s1 = pow2f(e), s2 = pow2f(e - 7), i1 = pow2f(-e), i2 = pow2f(7 - e), i3 = pow2f(14 - e);
-  xl.s3 = pow2f(e - 14);
-  xl.poison = bad ? __int_as_float(0x7fc00000) : 0.f;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    int S0 = 0, S1 = 0, S2 = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint32_t w0 = 0, w1 = 0, w2 = 0;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const float x = bad ? 0.f : v[k][4 * i + b];
-        const float x1 = rintf(__fmul_rn(x, i1));
-        const float r1 = __fsub_rn(x, __fmul_rn(x1, s1));
-        const float x2 = rintf(__fmul_rn(r1, i2));
-        const float r2 = __fsub_rn(r1, __fmul_rn(x2, s2));
-        const float x3 = rintf(__fmul_rn(r2, i3));
-        const int q1 = (int)x1, q2 = (int)x2, q3 = (int)x3;
-        S0 += q1; S1 += q2; S2 += q3;
-        w0 |= (uint32_t)(q1 & 0xFF) << (8 * b);
-        w1 |= (uint32_t)(q2 & 0xFF) << (8 * b);
-        w2 |= (uint32_t)(q3 & 0xFF) << (8 * b);
-      }
-      xl.w[k][0][i] = w0; xl.w[k][1][i] = w1; xl.w[k][2][i] = w2;
-    }
-    xl.xsf[k] = (float)(S0 * 16384 + S1 * 128 + S2);
-    xl.c0[k] = 32 * S0;
-    xl.c1[k] = 32 * (S1 * 128 + S2);
-  }
-}
 
 __device__ __forceinline__ float byte_to_float_u(uint32_t w, int i) {
   return __fsub_rn(__int_as_float((int)__byte_perm(w, 0x4B000000u, (uint32_t)(i | 0x7440))), 8388608.f);
 }
 
-// Row partial of a Q4_K unit: A, B = nibble chunks of planes 0/1, meta = 16-byte block header.
-__device__ __forceinline__ float row_q4k(const uint4 A, const uint4 B, const uint4 meta, int h, const XL& xl) {
-  const uint32_t a[4] = {A.x, A.y, A.z, A.w}, b[4] = {B.x, B.y, B.z, B.w};
-  float T[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    int acc0 = 0, acc1 = 0, acc2 = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t src = k < 2 ? a[i] : b[i];
-      const int nib = (int)((k & 1) ? ((src >> 4) & 0x0F0F0F0Fu) : (src & 0x0F0F0F0Fu));
-      acc0 = __dp4a(nib, (int)xl.w[k][0][i], acc0);
-      acc1 = __dp4a(nib, (int)xl.w[k][1][i], acc1);
-      acc2 = __dp4a(nib, (int)xl.w[k][2][i], acc2);
-    }
-    T[k] = (float)(acc0 * 16384 + acc1 * 128 + acc2);
-  }
-  // six-bit scales / mins of sub-blocks 4h .. 4h+3 as four bytes (q4kernels.h:17-18)
-  const uint32_t sc_w = h ? ((meta.w & 0x0F0F0F0Fu) | ((meta.y >> 2) & 0x30303030u)) : (meta.y & 0x3F3F3F3Fu);
-  const uint32_t mn_w = h ? (((meta.w >> 4) & 0x0F0F0F0Fu) | ((meta.z >> 2) & 0x30303030u)) : (meta.z & 0x3F3F3F3Fu);
-  float P = __fmul_rn(byte_to_float_u(sc_w, 0), T[0]);
-  float Q = __fmul_rn(byte_to_float_u(mn_w, 0), xl.xsf[0]);
-#pragma unroll
-  for (int k = 1; k < 4; ++k) {
-    P = __fmaf_rn(byte_to_float_u(sc_w, k), T[k], P);
-    Q = __fmaf_rn(byte_to_float_u(mn_w, k), xl.xsf[k], Q);
-  }
-  const float d = h2f_bits(meta.x & 0xFFFFu), dm = h2f_bits(meta.x >> 16);
-  return __fadd_rn(__fmul_rn(xl.s3, __fsub_rn(__fmul_rn(d, P), __fmul_rn(dm, Q))), xl.poison);
+// Per-unit activation scalars held in registers by a consumer thread.
+struct XS {
+  float s3, poison;
+  float xsf[4];     // sum of group k's digits 16384*S1 + 128*S2 + S3, as float (Q4_K dmin term)
+  int c[3][4];      // 32 * (sum of plane L's digits of group k): the "-32" of Q6_K, exact
+};
+
+// ------------------------------------------------------------------------------ row math
+// dp4a with unsigned bytes in a (weights) and signed bytes in b (activation digits).
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int sbyte(uint32_t w, int k) {   // sign-extended byte k
+  return ((int)(w << (24 - 8 * k))) >> 24;
 }
 
-// Row partial of a Q6_K unit: A, B = ql chunks (planes 0/1), H = qh chunk, scw = 4 int8
-// scales (k = 0..3), dbits = fp16 d.
-__device__ __forceinline__ float row_q6k(const uint4 A, const uint4 B, const uint4 H, uint32_t scw, uint32_t dbits,
-                                         const XL& xl) {
-  const uint32_t a[4] = {A.x, A.y, A.z, A.w}, b[4] = {B.x, B.y, B.z, B.w}, q[4] = {H.x, H.y, H.z, H.w};
-  float F[4];
+// Q4_K, group k of a unit, all three digit planes: P[L] += c_k * sum_j q_j * xL_j with
+// c_k = 16 sc_k for the low-nibble groups (k even) and sc_k for the high-nibble groups, whose
+// bytes are used in place (16 q_j = w & 0xF0F0F0F0). So P[L] = 16 * sum_k sc_k * sum_j q_j xL_j,
+// exact in int32 (|P| < 1.3e8).
+__device__ __forceinline__ void q4k_group(const uint32_t (&src)[4], int k, uint32_t sc_w, const uint4 (&xw)[3], int (&P)[3]) {
+  const uint32_t msk = (k & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+  const uint32_t x0[4] = {xw[0].x, xw[0].y, xw[0].z, xw[0].w};
+  const uint32_t x1[4] = {xw[1].x, xw[1].y, xw[1].z, xw[1].w};
+  const uint32_t x2[4] = {xw[2].x, xw[2].y, xw[2].z, xw[2].w};
+  int s0 = 0, s1 = 0, s2 = 0;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    int acc0 = 0, acc1 = 0, acc2 = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t src = (k & 1) ? b[i] : a[i];
-      const uint32_t lo = (k >> 1) ? ((src >> 4) & 0x0F0F0F0Fu) : (src & 0x0F0F0F0Fu);
-      const uint32_t hi = (k == 0) ? ((q[i] << 4) & 0x30303030u)
-                        : (k == 1) ? ((q[i] << 2) & 0x30303030u)
-                        : (k == 2) ? (q[i] & 0x30303030u)
-                                   : ((q[i] >> 2) & 0x30303030u);
-      const int q6 = (int)(lo | hi);
-      acc0 = __dp4a(q6, (int)xl.w[k][0][i], acc0);
-      acc1 = __dp4a(q6, (int)xl.w[k][1][i], acc1);
-      acc2 = __dp4a(q6, (int)xl.w[k][2][i], acc2);
-    }
-    const int th = acc0 - xl.c0[k];
-    const int tl = acc1 * 128 + acc2 - xl.c1[k];
-    F[k] = __fadd_rn(__fmul_rn((float)th, 16384.f), (float)tl);
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t nib = src[i] & msk;
+    s0 = dp4a_us(nib, x0[i], s0);
+    s1 = dp4a_us(nib, x1[i], s1);
+    s2 = dp4a_us(nib, x2[i], s2);
   }
-  float P = __fmul_rn((float)(int)(int8_t)(scw & 0xFF), F[0]);
+  const int ck = (int)((sc_w >> (8 * k)) & 0xFFu) << ((k & 1) ? 0 : 4);
+  P[0] += ck * s0;
+  P[1] += ck * s1;
+  P[2] += ck * s2;
+}
+// Q6_K, group k: P[L] += scale_k * (sum_j q6_j * xL_j - 32 * sum_j xL_j), exact in int32.
+__device__ __forceinline__ void q6k_group(const uint32_t (&a)[4], const uint32_t (&b)[4], const uint32_t (&q)[4], int k,
+                                          uint32_t scw, const uint4 (&xw)[3], const XS& xs, int (&P)[3]) {
+  const uint32_t x0[4] = {xw[0].x, xw[0].y, xw[0].z, xw[0].w};
+  const uint32_t x1[4] = {xw[1].x, xw[1].y, xw[1].z, xw[1].w};
+  const uint32_t x2[4] = {xw[2].x, xw[2].y, xw[2].z, xw[2].w};
+  int s0 = 0, s1 = 0, s2 = 0;
 #pragma unroll
-  for (int k = 1; k < 4; ++k) P = __fmaf_rn((float)(int)(int8_t)((scw >> (8 * k)) & 0xFF), F[k], P);
-  const float d = h2f_bits(dbits);
-  return __fadd_rn(__fmul_rn(xl.s3, __fmul_rn(d, P)), xl.poison);
-}
-
-// ------------------------------------------------------------------------------ the kernel
-__device__ __forceinline__ size_t seg_stage_bytes(const QView& w, int TR) {
-  return (size_t)TR * block_bytes(w.type) * w.G;
-}
-
-// Partial sum of a row across the LPR threads of a row group; the result is in thread u == 0.
-// red: [NRG][WPR] floats for this stage parity.
-__device__ __forceinline__ float row_reduce(float v, int u, int rg, int LPR, float* red) {
-  if (LPR < 32) {
-    for (int off = LPR >> 1; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    return v;
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t srcw = (k & 1) ? b[i] : a[i];
+    const uint32_t lo = (k >> 1) ? ((srcw >> 4) & 0x0F0F0F0Fu) : (srcw & 0x0F0F0F0Fu);
+    const uint32_t hi = (k == 0) ? ((q[i] << 4) & 0x30303030u)
+                      : (k == 1) ? ((q[i] << 2) & 0x30303030u)
+                      : (k == 2) ? (q[i] & 0x30303030u)
+                                 : ((q[i] >> 2) & 0x30303030u);
+    const uint32_t q6 = lo | hi;
+    s0 = dp4a_us(q6, x0[i], s0);
+    s1 = dp4a_us(q6, x1[i], s1);
+    s2 = dp4a_us(q6, x2[i], s2);
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-  const int WPR = LPR >> 5, wr = u >> 5;
-  if ((u & 31) == 0) red[rg * WPR + wr] = v;
-  named_bar(1 + rg, LPR);
-  float s = 0.f;
-  if (u == 0)
-    for (int w = 0; w < WPR; ++w) s += red[rg * WPR + w];
-  return s;
+  const int sk = sbyte(scw, k);
+  P[0] += sk * (s0 - xs.c[0][k]);
+  P[1] += sk * (s1 - xs.c[1][k]);
+  P[2] += sk * (s2 - xs.c[2][k]);
+}
+// The three planes' integer sums combined in fp32: 16384 P0 + 128 P1 + P2 (two roundings).
+__device__ __forceinline__ float planes_combine(const int (&P)[3]) {
+  return __fmaf_rn((float)P[0], 16384.f, __fmaf_rn((float)P[1], 128.f, (float)P[2]));
 }
 
-__device__ __forceinline__ double row_reduce_d(double v, int u, int rg, int LPR, double* redd) {
-  if (LPR < 32) {
-    for (int off = LPR >> 1; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    return v;
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-  const int WPR = LPR >> 5, wr = u >> 5;
-  if ((u & 31) == 0) redd[rg * WPR + wr] = v;
-  named_bar(1 + rg, LPR);
-  double s = 0.0;
-  for (int w = 0; w < WPR; ++w) s += redd[rg * WPR + w];
-  named_bar(1 + rg, LPR);
-  return s;
+// Six-bit scales / mins of sub-blocks 4h .. 4h+3 as four bytes each (q4kernels.h:17-18).
+__device__ __forceinline__ void q4k_scale_words(const uint4 meta, int h, uint32_t& sc_w, uint32_t& mn_w) {
+  sc_w = h ? ((meta.w & 0x0F0F0F0Fu) | ((meta.y >> 2) & 0x30303030u)) : (meta.y & 0x3F3F3F3Fu);
+  mn_w = h ? (((meta.w >> 4) & 0x0F0F0F0Fu) | ((meta.z >> 2) & 0x30303030u)) : (meta.z & 0x3F3F3F3Fu);
 }
 
+// ------------------------------------------------------------------------------ helpers
 __device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
 
-// Loads the unit's 64 activations into v (and the residual-updated h into hv for XS_NORM).
-__device__ __forceinline__ void load_x(const GemvParams& P, int u_thr, int rg, int LPR, double* redd, float (&v)[4][16]) {
-  const int g = u_thr >> 2, uu = u_thr & 3, h = uu >> 1, jh = uu & 1;
-  const int col0 = g * 256 + h * 128 + jh * 16;
-  if (P.xmode == XS_PLAIN) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float4* src = reinterpret_cast<const float4*>(P.x + col0 + 32 * k);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 t = src[i];
-        v[k][4 * i] = t.x; v[k][4 * i + 1] = t.y; v[k][4 * i + 2] = t.z; v[k][4 * i + 3] = t.w;
-      }
-    }
-    return;
-  }
-  // residual stream value for this unit
-  if (P.xmode == XS_EMBED) {
-    int tok = P.st->tok;
-    if (tok < 0 || tok >= P.vocab) {
-      if (u_thr == 0 && rg == 0) atomicOr(P.err, KQ_DEV_ERR_BAD_TOKEN);
-      tok = 0;
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[k][j] = dequant_elem(P.emb, tok, col0 + 32 * k + j);
-  } else {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float4* hs = reinterpret_cast<const float4*>(P.h_in + col0 + 32 * k);
-      const float4* ys = reinterpret_cast<const float4*>(P.y_add + col0 + 32 * k);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 a = hs[i];
-        float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (P.y_add) b = ys[i];
-        v[k][4 * i] = __fadd_rn(a.x, b.x); v[k][4 * i + 1] = __fadd_rn(a.y, b.y);
-        v[k][4 * i + 2] = __fadd_rn(a.z, b.z); v[k][4 * i + 3] = __fadd_rn(a.w, b.w);
-      }
-    }
-  }
-  if (blockIdx.x == 0 && rg == 0 && P.h_out) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float4* ho = reinterpret_cast<float4*>(P.h_out + col0 + 32 * k);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) ho[i] = make_float4(v[k][4 * i], v[k][4 * i + 1], v[k][4 * i + 2], v[k][4 * i + 3]);
-    }
-  }
-  // fp64 sum of squares (q4_rms kindi q4.cu:39-46 / rmsfold kcpu4.c:123-139)
-  double acc = 0.0;
-#pragma unroll
-  for (int k = 0; k < 4; ++k)
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc = __dadd_rn(acc, __dmul_rn((double)v[k][j], (double)v[k][j]));
-  const double tot = row_reduce_d(acc, u_thr, rg, LPR, redd);
-  const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / (double)P.C), P.eps)));
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float4* gs = reinterpret_cast<const float4*>(P.gamma + col0 + 32 * k);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 gm = gs[i];
-      v[k][4 * i] = __fmul_rn(__fmul_rn(v[k][4 * i], s), gm.x);
-      v[k][4 * i + 1] = __fmul_rn(__fmul_rn(v[k][4 * i + 1], s), gm.y);
-      v[k][4 * i + 2] = __fmul_rn(__fmul_rn(v[k][4 * i + 2], s), gm.z);
-      v[k][4 * i + 3] = __fmul_rn(__fmul_rn(v[k][4 * i + 3], s), gm.w);
-    }
-  }
+__device__ __forceinline__ long long seg_stage_bytes(const GemvParams& P, int i) {
+  return (long long)P.TR * block_bytes(P.seg[i].w.type) * P.seg[i].w.G;
 }
 
 // CTA stage range balanced by bytes (segments differ in bytes per stage).
 __device__ __forceinline__ void cta_stage_range(const GemvParams& P, int& s0, int& s1) {
   long long total = 0;
-  for (int i = 0; i < P.nseg; ++i) total += (long long)P.seg[i].nstage * (long long)seg_stage_bytes(P.seg[i].w, P.TR);
+  for (int i = 0; i < P.nseg; ++i) total += (long long)P.seg[i].nstage * seg_stage_bytes(P, i);
   auto stage_at = [&](long long target) -> int {
     long long acc = 0;
     for (int i = 0; i < P.nseg; ++i) {
-      const long long sb = (long long)seg_stage_bytes(P.seg[i].w, P.TR);
+      const long long sb = seg_stage_bytes(P, i);
       const long long segb = (long long)P.seg[i].nstage * sb;
       if (target < acc + segb) return P.seg[i].stage0 + (int)((target - acc + sb - 1) / sb);
       acc += segb;
@@ -331,23 +211,246 @@ __device__ __forceinline__ void cta_stage_range(const GemvParams& P, int& s0, in
   s1 = stage_at(total * (long long)(blockIdx.x + 1) / gridDim.x);
 }
 
+// Prologue item (unit u, part q): the 8 consecutive columns 256g + 128h + 32k + 16jh + 8(q%2) + i,
+// k = q/2. A unit's 8 items sit in 8 consecutive lanes (LPR*8 and the thread count are multiples
+// of 32), so the unit max is a 3-step shuffle.
+__device__ __forceinline__ int item_col0(int item) {
+  const int u = item >> 3, q = item & 7;
+  const int g = u >> 2, uu = u & 3, h = uu >> 1, jh = uu & 1;
+  return g * 256 + h * 128 + (q >> 1) * 32 + jh * 16 + (q & 1) * 8;
+}
+
+// Eight embedding-row values of a Q4_K row (bit-exact q4_decode order), from the device layout.
+__device__ __forceinline__ void embed8_q4k(const QView& m, int row, int col0, float (&v)[8]) {
+  const int G = m.G, g = col0 >> 8, e = col0 & 255;
+  const int h = e >> 7, k6 = (e >> 5) & 3, j0 = e & 31, jh = j0 >> 4, jp0 = j0 & 15, u = 2 * h + jh;
+  const uint4 meta = *reinterpret_cast<const uint4*>(m.base + row_plane_off(Q4K, G, row, 1, (size_t)g * 16));
+  const uint2 nb = *reinterpret_cast<const uint2*>(
+      m.base + row_plane_off(Q4K, G, row, 0, (size_t)(k6 >> 1) * 64 * G + (size_t)g * 64 + u * 16 + jp0));
+  uint32_t scw, mnw;
+  q4k_scale_words(meta, h, scw, mnw);
+  const float d = h2f_bits(meta.x & 0xFFFFu), dm = h2f_bits(meta.x >> 16);
+  const float sc = (float)((scw >> (8 * k6)) & 0xFF), mn = (float)((mnw >> (8 * k6)) & 0xFF);
+  const float ds = __fmul_rn(d, sc), ms = __fmul_rn(dm, mn);
+  const uint32_t w[2] = {nb.x, nb.y};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int q = (w[i >> 2] >> (8 * (i & 3) + (k6 & 1) * 4)) & 15;
+    v[i] = __fsub_rn(__fmul_rn(ds, (float)q), ms);
+  }
+}
+
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = __ldcg(reinterpret_cast<const float4*>(p)), b = __ldcg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Prologue: residual + norm (or plain activations), digit planes and per-unit scalars into shared
+// memory. One pass: every thread issues all of its loads first and keeps the values in registers,
+// then the norm reduction, then the exact digit split (integer rounding done on the FMA pipe).
+__device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem& L, int nthr_c) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint4* xplanes = reinterpret_cast<uint4*>(smem + L.xplanes);
+  float* xscal = reinterpret_cast<float*>(smem + L.xscal);
+  double* redd = reinterpret_cast<double*>(smem + L.redd);
+  const int LPR = P.LPR, nitems = LPR * 8;
+  int tok = 0;
+  if (P.xmode == XS_EMBED) {
+    tok = P.st->tok;
+    if (tok < 0 || tok >= P.vocab) {
+      if (tid == 0) atomicOr(P.err, KQ_DEV_ERR_BAD_TOKEN);
+      tok = 0;
+    }
+  }
+  float v[KQ_MAX_ITEMS][8];
+  // ---- loads (all issued before any use)
+#pragma unroll
+  for (int it = 0; it < KQ_MAX_ITEMS; ++it) {
+    const int item = tid + it * nthr_c;
+    if (item < nitems) {
+      const int col0 = item_col0(item);
+      if (P.xmode == XS_PLAIN) {
+        load8(P.x + col0, v[it]);
+      } else if (P.xmode == XS_EMBED) {
+        if (P.emb.type == Q4K) embed8_q4k(P.emb, tok, col0, v[it]);
+        else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[it][i] = dequant_elem(P.emb, tok, col0 + i);
+        }
+      } else {
+        float hv[8], yv[8];
+        load8(P.h_in + col0, hv);
+        if (P.y_add) load8(P.y_add + col0, yv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[it][i] = P.y_add ? __fadd_rn(hv[i], yv[i]) : hv[i];
+      }
+    }
+  }
+  // ---- residual write-back and the norm scale (q4_rms q4.cu:39-46 / rmsfold kcpu4.c:123-139)
+  if (P.xmode != XS_PLAIN) {
+    double acc = 0.0;
+    const bool wr = blockIdx.x == 0 && P.h_out;
+#pragma unroll
+    for (int it = 0; it < KQ_MAX_ITEMS; ++it) {
+      const int item = tid + it * nthr_c;
+      if (item < nitems) {
+        if (wr) {
+          float4* ho = reinterpret_cast<float4*>(P.h_out + item_col0(item));
+          ho[0] = make_float4(v[it][0], v[it][1], v[it][2], v[it][3]);
+          ho[1] = make_float4(v[it][4], v[it][5], v[it][6], v[it][7]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc = __dadd_rn(acc, __dmul_rn((double)v[it][i], (double)v[it][i]));
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) redd[warp] = acc;
+    named_bar(KQ_BAR_PROLOGUE, nthr_c);
+    double tot = 0.0;
+    for (int w = 0; w < nthr_c / 32; ++w) tot += redd[w];
+    const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / (double)P.C), P.eps)));
+#pragma unroll
+    for (int it = 0; it < KQ_MAX_ITEMS; ++it) {
+      const int item = tid + it * nthr_c;
+      if (item < nitems) {
+        float gm[8];
+        load8(P.gamma + item_col0(item), gm);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[it][i] = __fmul_rn(__fmul_rn(v[it][i], s), gm[i]);
+      }
+    }
+  }
+  // ---- exact digit split per unit
+  const float RND = 12582912.0f;   // 1.5 * 2^23: adding it rounds to an integer (RNE), |y| <= 128
+#pragma unroll
+  for (int it = 0; it < KQ_MAX_ITEMS; ++it) {
+    const int item = tid + it * nthr_c;
+    if (item >= nitems) break;            // uniform across a warp
+    const int u = item >> 3, q = item & 7, k = q >> 1, half = q & 1;
+    float m = 0.f;
+    int bad = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a = fabsf(v[it][i]);
+      bad |= !(a <= FLT_MAX);
+      m = fmaxf(m, a);
+    }
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) {
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+    }
+    int e = 0;
+    if (!bad && m >= 0x1p-100f) {
+      e = ((__float_as_int(m) >> 23) & 0xFF) - 127 - 6;   // m is normal here
+      if (m > 127.f * pow2f(e)) ++e;
+    }
+    const float s1 = pow2f(e), s2 = pow2f(e - 7), i1 = pow2f(-e), i2 = pow2f(7 - e), i3 = pow2f(14 - e);
+    uint32_t w[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+    int S0 = 0, S1 = 0, S2 = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float x = bad ? 0.f : v[it][i];
+      const float t1 = __fadd_rn(__fmul_rn(x, i1), RND);
+      const float x1 = __fsub_rn(t1, RND);
+      const float r1 = __fsub_rn(x, __fmul_rn(x1, s1));
+      const float t2 = __fadd_rn(__fmul_rn(r1, i2), RND);
+      const float x2 = __fsub_rn(t2, RND);
+      const float r2 = __fsub_rn(r1, __fmul_rn(x2, s2));
+      const float t3 = __fadd_rn(__fmul_rn(r2, i3), RND);
+      const int q1 = __float_as_int(t1) - 0x4B400000, q2 = __float_as_int(t2) - 0x4B400000,
+                q3 = __float_as_int(t3) - 0x4B400000;
+      S0 += q1; S1 += q2; S2 += q3;
+      w[0][i >> 2] |= (uint32_t)(q1 & 0xFF) << (8 * (i & 3));
+      w[1][i >> 2] |= (uint32_t)(q2 & 0xFF) << (8 * (i & 3));
+      w[2][i >> 2] |= (uint32_t)(q3 & 0xFF) << (8 * (i & 3));
+    }
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+      *reinterpret_cast<uint2*>(reinterpret_cast<uint32_t*>(&xplanes[(k * 3 + p) * LPR + u]) + half * 2) =
+          make_uint2(w[p][0], w[p][1]);
+    S0 += __shfl_xor_sync(0xffffffffu, S0, 1);
+    S1 += __shfl_xor_sync(0xffffffffu, S1, 1);
+    S2 += __shfl_xor_sync(0xffffffffu, S2, 1);
+    if (half == 0) {
+      xscal[(2 + k) * LPR + u] = (float)(S0 * 16384 + S1 * 128 + S2);
+      reinterpret_cast<int*>(xscal)[(6 + k) * LPR + u] = 32 * S0;
+      reinterpret_cast<int*>(xscal)[(10 + k) * LPR + u] = 32 * S1;
+      reinterpret_cast<int*>(xscal)[(14 + k) * LPR + u] = 32 * S2;
+    }
+    if (q == 0) {
+      xscal[0 * LPR + u] = pow2f(e - 14);
+      xscal[1 * LPR + u] = bad ? __int_as_float(0x7fc00000) : 0.f;
+    }
+  }
+  named_bar(KQ_BAR_PROLOGUE, nthr_c);
+}
+
+// Sum over the LPR threads of a row group of RPG per-thread partials. For LPR >= 32 the warp
+// sums are combined across the row's warps through `red` (this stage's buffer) after a named
+// barrier; for LPR < 32 the row group is a segment of a warp. Returns, in thread u == rr of the
+// row group (rr < RPG), the total of row rr.
+template <int RPG>
+__device__ __forceinline__ float rows_reduce(const float (&p)[RPG], int u, int rg, int LPR, float* red) {
+  const int lane = threadIdx.x & 31;
+  if (LPR < 32) {
+    float mine = 0.f;
+#pragma unroll
+    for (int rr = 0; rr < RPG; ++rr) {
+      float v = p[rr];
+      for (int off = LPR >> 1; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (u == rr) mine = v;
+    }
+    return mine;
+  }
+  // reduce-scatter inside the warp: afterwards the lanes of block rr (32/RPG lanes) hold row rr
+  float v;
+  if (RPG == 1) {
+    v = p[0];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  } else if (RPG == 2) {
+    const bool up = lane & 16;
+    v = (up ? p[RPG - 1] : p[0]) + __shfl_xor_sync(0xffffffffu, up ? p[0] : p[RPG - 1], 16);
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  } else {
+    const bool up = lane & 16, mid = lane & 8;
+    const float a0 = (up ? p[2 % RPG] : p[0]) + __shfl_xor_sync(0xffffffffu, up ? p[0] : p[2 % RPG], 16);
+    const float a1 = (up ? p[3 % RPG] : p[1 % RPG]) + __shfl_xor_sync(0xffffffffu, up ? p[1 % RPG] : p[3 % RPG], 16);
+    v = (mid ? a1 : a0) + __shfl_xor_sync(0xffffffffu, mid ? a0 : a1, 8);
+#pragma unroll
+    for (int off = 4; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  }
+  const int WPR = LPR >> 5, wr = u >> 5, span = 32 / RPG;
+  // row held by this lane: RPG 4 -> lanes 0-7 row 0, 8-15 row 1, 16-23 row 2, 24-31 row 3
+  const int myrow = RPG == 4 ? (((lane >> 4) << 1) | ((lane >> 3) & 1)) : lane / span;
+  if ((lane % span) == 0) red[(rg * RPG + myrow) * WPR + wr] = v;
+  named_bar(1 + rg, LPR);
+  float sum = 0.f;
+  if (u < RPG)
+    for (int w = 0; w < WPR; ++w) sum += red[(rg * RPG + u) * WPR + w];
+  return sum;
+}
+
+// ------------------------------------------------------------------------------ the kernel
+template <int TM, int RPG>
 __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_constant__ GemvParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const int nthr_c = P.LPR * P.NRG;
+  const int LPR = P.LPR, NRG = P.NRG;
+  const int nthr_c = LPR * NRG;
   const int tid = threadIdx.x;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)P.nslots * P.stage_bytes);
+  const GemvSmem L = gemv_smem_layout(P.nslots, P.stage_bytes, LPR, NRG, RPG, nthr_c);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + P.nslots;
-  const int WPR = P.LPR >= 32 ? (P.LPR >> 5) : 1;
-  float* red = reinterpret_cast<float*>(empty + P.nslots);            // [2][RPG][NRG][WPR]
-  double* redd = reinterpret_cast<double*>(red + 2 * P.RPG * P.NRG * WPR + 2);  // [NRG][WPR]
-  float* bestv = reinterpret_cast<float*>(redd + P.NRG * WPR);          // [NRG]
-  int* besti = reinterpret_cast<int*>(bestv + P.NRG);                   // [NRG]
+  float* red = reinterpret_cast<float*>(smem + L.red);
   __shared__ int s_fail, s_issued, s_done;
 
   int s_begin, s_end;
   cta_stage_range(P, s_begin, s_end);
   const int nmine = s_end - s_begin;
-  const int ncw = (nthr_c + 31) >> 5;
+  const int ncw = nthr_c >> 5;
   if (tid == 0) {
     for (int i = 0; i < P.nslots; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], ncw); }
     fence_mbar_init();
@@ -357,6 +460,7 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
   }
   __syncthreads();
   pdl_trigger();
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 0);
 
   if (tid >= nthr_c) {
     // ---------------------------------------------------------------- producer warp
@@ -373,19 +477,15 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
         const int s = s_begin + i;
         while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
         const QView& w = P.seg[segi].w;
-        const size_t row0 = (size_t)(s - P.seg[segi].stage0) * P.TR;
-        uint8_t* buf = smem + (size_t)slot * P.stage_bytes;
-        const uint32_t b0 = (uint32_t)(P.TR * plane_row_bytes(w.type, 0, w.G));
-        const uint32_t b1 = (uint32_t)(P.TR * plane_row_bytes(w.type, 1, w.G));
-        const uint32_t b2 = (uint32_t)(P.TR * plane_row_bytes(w.type, 2, w.G));
-        const uint32_t b3 = (uint32_t)(P.TR * plane_row_bytes(w.type, 3, w.G));
-        mbar_arrive_expect_tx(&full[slot], b0 + b1 + b2 + b3);
-        bulk_g2s(buf, w.p0 + row0 * plane_row_bytes(w.type, 0, w.G), b0, &full[slot], pol);
-        bulk_g2s(buf + b0, w.p1 + row0 * plane_row_bytes(w.type, 1, w.G), b1, &full[slot], pol);
-        if (b2) bulk_g2s(buf + b0 + b1, w.p2 + row0 * plane_row_bytes(w.type, 2, w.G), b2, &full[slot], pol);
-        if (b3) bulk_g2s(buf + b0 + b1 + b2, w.p3 + row0 * plane_row_bytes(w.type, 3, w.G), b3, &full[slot], pol);
+        const int row0 = (s - P.seg[segi].stage0) * P.TR;
+        const int rows = min(P.TR, w.R - row0);          // a multiple of 8 (whole tiles)
+        uint8_t* buf = smem + L.stages + (size_t)slot * P.stage_bytes;
+        const uint32_t bytes = (uint32_t)((size_t)(rows >> 3) * tile_bytes(w.type, w.G));
+        mbar_arrive_expect_tx(&full[slot], bytes);
+        bulk_g2s(buf, w.base + (size_t)(row0 >> 3) * tile_bytes(w.type, w.G), bytes, &full[slot], pol);
         *(volatile int*)&s_issued = i + 1;
       }
+      KQ_TRACE_AT(P.trace_id, 5);
       // failure path only: wait (bounded) for the copies still in flight before the CTA can exit
       if (*(volatile int*)&s_fail) {
         const int issued = *(volatile int*)&s_issued;
@@ -399,113 +499,169 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
 
   // ------------------------------------------------------------------ consumers
   pdl_wait();
-  const int rg = tid / P.LPR, u_thr = tid % P.LPR;
-  const int h = (u_thr & 3) >> 1;
-  const int g = u_thr >> 2;
-  XL xl;
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 1);
+  gemv_prologue(P, smem, L, nthr_c);
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 2);
+  const int rg = tid / LPR, u = tid % LPR;
+  const int h = (u & 3) >> 1, g = u >> 2;
+  const int G = P.G;
+  const uint4* xplanes = reinterpret_cast<const uint4*>(smem + L.xplanes);
+  XS xs;
   {
-    float v[4][16];
-    load_x(P, u_thr, rg, P.LPR, redd, v);
-    build_xl(v, xl);
+    const float* xscal = reinterpret_cast<const float*>(smem + L.xscal);
+    xs.s3 = xscal[u];
+    xs.poison = xscal[LPR + u];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      xs.xsf[k] = xscal[(2 + k) * LPR + u];
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl) xs.c[pl][k] = reinterpret_cast<const int*>(xscal)[(6 + 4 * pl + k) * LPR + u];
+    }
   }
+  const float s3q = xs.s3 * 0.0625f;   // Q4_K sums carry a factor 16 (see q4k_group)
   float bv = -FLT_MAX;
   int bi = 0x7fffffff;
   int segi = 0;
-  const int G = P.G;
+  const int WPR = LPR >= 32 ? LPR >> 5 : 1;
   for (int i = 0; i < nmine; ++i) {
     const int slot = i % P.nslots;
     const uint32_t round = (uint32_t)(i / P.nslots);
     if (!mbar_wait(&full[slot], round & 1, P.err, KQ_DEV_ERR_WAIT_FULL)) { s_fail = 1; break; }
+    if (tid == 0 && i == 0) KQ_TRACE_AT(P.trace_id, 3);
     const int s = s_begin + i;
     while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
     const Seg& sg = P.seg[segi];
-    const uint8_t* buf = smem + (size_t)slot * P.stage_bytes;
-    const int type = sg.w.type;
-    float part[8];
+    const uint8_t* buf = smem + L.stages + (size_t)slot * P.stage_bytes;
+    const bool is_q4 = TM == TM_Q4K || (TM == TM_MIXED && sg.w.type == Q4K);
+    const int row0 = (s - sg.stage0) * P.TR;
+    const int rows = min(P.TR, sg.w.R - row0);
+    const int type = is_q4 ? Q4K : Q6K;
+    const size_t TB = tile_bytes(type, G);
+    const size_t o1 = (size_t)8 * 128 * G;                                  // plane 1 in a tile
+    const size_t o2 = o1 + (size_t)8 * (is_q4 ? 16 : 64) * G, o3 = o2 + (size_t)8 * 16 * G;
+    // ---- load this thread's slice of its RPG rows, then free the stage
+    uint32_t a[RPG][4], b[RPG][4], q[RPG][4];
+    uint32_t m1[RPG];   // Q4_K: d | dmin << 16 ; Q6_K: four int8 scales
+    uint32_t m2[RPG];   // Q4_K: 6-bit scales as 4 bytes ; Q6_K: fp16 d bits
+    uint32_t m3[RPG];   // Q4_K: 6-bit mins as 4 bytes
 #pragma unroll
-    for (int rr = 0; rr < 8; ++rr) {
-      if (rr >= P.RPG) break;
-      const int r = rg * P.RPG + rr;   // row within the stage
-      const uint8_t* p0 = buf + (size_t)r * 128 * G;
-      const uint4 A = lds128(p0 + u_thr * 16);
-      const uint4 B = lds128(p0 + (size_t)64 * G + u_thr * 16);
-      const size_t b0 = (size_t)P.TR * 128 * G;
-      if (type == Q4K) {
-        const uint4 meta = lds128(buf + b0 + ((size_t)r * G + g) * 16);
-        part[rr] = row_q4k(A, B, meta, h, xl);
+    for (int rr = 0; rr < RPG; ++rr) {
+      const int r = min(rg * RPG + rr, rows - 1);   // rows past a short last stage reuse a real one
+      const uint8_t* tb = buf + (size_t)(r >> 3) * TB;
+      const int r8 = r & 7;
+      const uint8_t* p0 = tb + (size_t)r8 * 128 * G;
+      const uint4 A = lds128(p0 + u * 16);
+      const uint4 B = lds128(p0 + (size_t)64 * G + u * 16);
+      a[rr][0] = A.x; a[rr][1] = A.y; a[rr][2] = A.z; a[rr][3] = A.w;
+      b[rr][0] = B.x; b[rr][1] = B.y; b[rr][2] = B.z; b[rr][3] = B.w;
+      if (is_q4) {
+        const uint4 M = lds128(tb + o1 + ((size_t)r8 * G + g) * 16);
+        q4k_scale_words(M, h, m2[rr], m3[rr]);
+        m1[rr] = M.x;
+        q[rr][0] = q[rr][1] = q[rr][2] = q[rr][3] = 0;
       } else {
-        const size_t b1 = (size_t)P.TR * 64 * G, b2 = (size_t)P.TR * 16 * G;
-        const uint4 H = lds128(buf + b0 + (size_t)r * 64 * G + u_thr * 16);
-        const uint32_t scw = lds32(buf + b0 + b1 + (size_t)r * 16 * G + u_thr * 4);
-        const size_t doff = ((size_t)r * G + g) * 2;
-        const uint32_t dw = lds32(buf + b0 + b1 + b2 + (doff & ~(size_t)3));
-        part[rr] = row_q6k(A, B, H, scw, (doff & 2) ? (dw >> 16) : (dw & 0xFFFFu), xl);
+        const uint4 H = lds128(tb + o1 + (size_t)r8 * 64 * G + u * 16);
+        q[rr][0] = H.x; q[rr][1] = H.y; q[rr][2] = H.z; q[rr][3] = H.w;
+        m1[rr] = lds32(tb + o2 + (size_t)r8 * 16 * G + u * 4);
+        const size_t doff = ((size_t)r8 * G + g) * 2;
+        const uint32_t dw = lds32(tb + o3 + (doff & ~(size_t)3));
+        m2[rr] = (doff & 2) ? (dw >> 16) : (dw & 0xFFFFu);
+        m3[rr] = 0;
       }
     }
     __syncwarp();
     if ((tid & 31) == 0) mbar_arrive(&empty[slot]);
     if (tid == 0) *(volatile int*)&s_done = i + 1;
-    // reduce + epilogue
-    float* redb = red + (i & 1) * P.RPG * P.NRG * WPR;
-    float fin[8];
+    // ---- compute: group by group, the digit planes shared by the RPG rows
+    int Pi[RPG][3];
+    float Q_[RPG];
 #pragma unroll
-    for (int rr = 0; rr < 8; ++rr) {
-      if (rr >= P.RPG) break;
-      fin[rr] = row_reduce(part[rr], u_thr, rg, P.LPR, redb + rr * P.NRG * WPR);
-    }
-    if (u_thr == 0) {
-      const int grow0 = (s - sg.stage0) * P.TR + rg * P.RPG;
-      int pos = P.st ? P.st->pos : 0;
-      const bool kv_ok = pos >= 0 && pos < P.ctx;   // the host validates; never store outside the cache
-      if (!kv_ok && (sg.epi == EPI_ROPE_K || sg.epi == EPI_V || sg.epi == EPI_ROPE_Q)) {
-        atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
-        pos = 0;
-      }
-      for (int rr = 0; rr < P.RPG; ++rr) {
-        const int grow = grow0 + rr;
-        const float val = fin[rr];
-        switch (sg.epi) {
-          case EPI_F32: sg.out_f[grow] = val; break;
-          case EPI_ARGMAX:
-            sg.out_f[grow] = val;
-            if (val > bv || (val == bv && grow < bi)) { bv = val; bi = grow; }
-            break;
-          case EPI_V: {
-            const int kv = grow / P.hd, e = grow % P.hd;
-            if (kv_ok) sg.out_h[((size_t)kv * P.ctx + pos) * P.hd + e] = __float2half_rn(val);
-          } break;
-          case EPI_SWIGLU:
-            if ((rr & 1) == 1) sg.out_f[grow >> 1] = __fmul_rn(silu_f(fin[rr - 1]), val);
-            break;
-          case EPI_ROPE_Q:
-          case EPI_ROPE_K:
-            if ((rr & 1) == 1) {
-              const int hh = grow / P.hd, i2 = (grow % P.hd) >> 1, half = P.hd >> 1;
-              const float a = fin[rr - 1], b = val;
-              const float c = P.cos_t[(size_t)pos * half + i2], sn = P.sin_t[(size_t)pos * half + i2];
-              const float o0 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
-              const float o1 = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
-              if (sg.epi == EPI_ROPE_Q) {
-                sg.out_f[hh * P.hd + i2] = o0;
-                sg.out_f[hh * P.hd + i2 + half] = o1;
-              } else if (kv_ok) {
-                __half* dst = sg.out_h + ((size_t)hh * P.ctx + pos) * P.hd;
-                dst[i2] = __float2half_rn(o0);
-                dst[i2 + half] = __float2half_rn(o1);
-              }
-            }
-            break;
+    for (int rr = 0; rr < RPG; ++rr) { Pi[rr][0] = Pi[rr][1] = Pi[rr][2] = 0; Q_[rr] = 0.f; }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint4 xw[3];
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl) xw[pl] = xplanes[(k * 3 + pl) * LPR + u];
+#pragma unroll
+      for (int rr = 0; rr < RPG; ++rr) {
+        if (is_q4) {
+          q4k_group(k < 2 ? a[rr] : b[rr], k, m2[rr], xw, Pi[rr]);
+          Q_[rr] = __fmaf_rn(byte_to_float_u(m3[rr], k), xs.xsf[k], Q_[rr]);
+        } else {
+          q6k_group(a[rr], b[rr], q[rr], k, m1[rr], xw, xs, Pi[rr]);
         }
       }
     }
+    float part[RPG];
+#pragma unroll
+    for (int rr = 0; rr < RPG; ++rr) {
+      const float Pf = planes_combine(Pi[rr]);
+      if (is_q4) {
+        const float d = h2f_bits(m1[rr] & 0xFFFFu), dm = h2f_bits(m1[rr] >> 16);
+        part[rr] = __fadd_rn(__fsub_rn(__fmul_rn(s3q, __fmul_rn(d, Pf)), __fmul_rn(xs.s3, __fmul_rn(dm, Q_[rr]))), xs.poison);
+      } else {
+        part[rr] = __fadd_rn(__fmul_rn(xs.s3, __fmul_rn(h2f_bits(m2[rr]), Pf)), xs.poison);
+      }
+    }
+    // ---- reduce across the row group; thread u == rr holds row rr
+    const float fin = rows_reduce<RPG>(part, u, rg, LPR, red + (i & 1) * RPG * NRG * WPR);
+    // ---- epilogue
+    const int epi = sg.epi;
+    const bool pair_epi = epi == EPI_SWIGLU || epi == EPI_ROPE_Q || epi == EPI_ROPE_K;
+    float fin_odd = 0.f;
+    if (pair_epi) fin_odd = __shfl_down_sync(0xffffffffu, fin, 1);
+    const int rloc = rg * RPG + u;
+    if (u < RPG && rloc < rows) {
+      const int grow = row0 + rloc;
+      int pos = P.st ? P.st->pos : 0;
+      const bool kv_ok = pos >= 0 && pos < P.ctx;   // the host validates; never store outside the cache
+      if (!kv_ok && (epi == EPI_ROPE_K || epi == EPI_V || epi == EPI_ROPE_Q)) {
+        atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
+        pos = 0;
+      }
+      switch (epi) {
+        case EPI_F32: sg.out_f[grow] = fin; break;
+        case EPI_ARGMAX:
+          sg.out_f[grow] = fin;
+          if (fin > bv || (fin == bv && grow < bi)) { bv = fin; bi = grow; }
+          break;
+        case EPI_V: {
+          const int kv = grow / P.hd, e = grow % P.hd;
+          if (kv_ok) sg.out_h[((size_t)kv * P.ctx + pos) * P.hd + e] = __float2half_rn(fin);
+        } break;
+        case EPI_SWIGLU:
+          if ((u & 1) == 0) sg.out_f[grow >> 1] = __fmul_rn(silu_f(fin), fin_odd);
+          break;
+        case EPI_ROPE_Q:
+        case EPI_ROPE_K:
+          if ((u & 1) == 0) {
+            const int hh = grow / P.hd, i2 = (grow % P.hd) >> 1, half = P.hd >> 1;
+            const float c = P.cos_t[(size_t)pos * half + i2], sn = P.sin_t[(size_t)pos * half + i2];
+            const float o0 = __fsub_rn(__fmul_rn(fin, c), __fmul_rn(fin_odd, sn));
+            const float o1v = __fadd_rn(__fmul_rn(fin, sn), __fmul_rn(fin_odd, c));
+            if (epi == EPI_ROPE_Q) {
+              sg.out_f[hh * P.hd + i2] = o0;
+              sg.out_f[hh * P.hd + i2 + half] = o1v;
+            } else if (kv_ok) {
+              __half* dst = sg.out_h + ((size_t)hh * P.ctx + pos) * P.hd;
+              dst[i2] = __float2half_rn(o0);
+              dst[i2 + half] = __float2half_rn(o1v);
+            }
+          }
+          break;
+      }
+    }
   }
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 4);
   // ------------------------------------------------------------------ argmax across CTAs
   if (P.seg[0].epi == EPI_ARGMAX) {
-    if (u_thr == 0) { bestv[rg] = bv; besti[rg] = bi; }
-    named_bar(15, nthr_c);
+    float* bestv = reinterpret_cast<float*>(smem + L.best);
+    int* besti = reinterpret_cast<int*>(bestv + NRG * RPG);
+    if (u < RPG) { bestv[rg * RPG + u] = bv; besti[rg * RPG + u] = bi; }
+    named_bar(KQ_BAR_ARGMAX, nthr_c);
     if (tid == 0) {
       float v0 = -FLT_MAX; int i0 = 0x7fffffff;
-      for (int r = 0; r < P.NRG; ++r)
+      for (int r = 0; r < NRG * RPG; ++r)
         if (bestv[r] > v0 || (bestv[r] == v0 && besti[r] < i0)) { v0 = bestv[r]; i0 = besti[r]; }
       P.part_val[blockIdx.x] = v0;
       P.part_idx[blockIdx.x] = i0;

@@ -1,30 +1,29 @@
 // kq_qformat.cuh -- device layout of Q4_K / Q6_K matrices, the seeded synthetic generator, the
 // GGUF -> device repack and the bit-exact dequantiser.
 //
-// Device layout ("kq layout"). A matrix of R rows and C = 256*G columns is stored as up to four
-// planes, each row-contiguous, so that one bulk copy moves a run of rows of one plane:
-//   p0  [R][2][G][4][16]   nibble bytes (Q4_K qs / Q6_K ql): chunk (c, g, u) holds GGUF block
+// Device layout ("kq layout"). A matrix of R rows (a multiple of 8) and C = 256*G columns is
+// stored as R/8 tiles of 8 rows; a tile holds its rows' planes one after another, so a run of
+// whole tiles is ONE contiguous range (one bulk copy per pipeline stage). Inside a tile:
+//   p0  [8][2][G][4][16]   nibble bytes (Q4_K qs / Q6_K ql): chunk (c, g, u) holds GGUF block
 //                          bytes 64h + 32c + 16jh + (0..15) of the nibble area, u = 2h + jh
-//   p1  Q4_K: [R][G][16]   block header verbatim (d, dmin, 12 packed 6-bit scales/mins)
-//       Q6_K: [R][G][64]   qh bytes verbatim (unit u's 16 bytes at 16u)
-//   p2  Q6_K: [R][G][4][4] int8 scales, unit-major: [u][k] = GGUF scale 8h + 2k + jh
-//   p3  Q6_K: [R][G]       fp16 d
+//   p1  Q4_K: [8][G][16]   block header verbatim (d, dmin, 12 packed 6-bit scales/mins)
+//       Q6_K: [8][G][64]   qh bytes verbatim (unit u's 16 bytes at 16u)
+//   p2  Q6_K: [8][G][4][4] int8 scales, unit-major: [u][k] = GGUF scale 8h + 2k + jh
+//   p3  Q6_K: [8][G]       fp16 d
 // Thread "unit" u of block g covers the 64 columns 256g + 128h + 32k + 16jh + j', k = 0..3,
-// j' = 0..15, for BOTH types, so one set of activation registers serves mixed-type launches.
+// j' = 0..15, for BOTH types, so one set of activation digits serves mixed-type launches.
 // The byte count equals the GGUF byte count (144 or 210 per block); nothing is re-quantised.
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
+#include "kq_common.cuh"
 
 namespace kq {
 
 constexpr int Q4K = 12, Q6K = 14;
 
 struct QView {
-  const uint8_t* p0;
-  const uint8_t* p1;
-  const uint8_t* p2;
-  const uint8_t* p3;
+  const uint8_t* base;   // R/8 tiles
   int type, R, C, G;
 };
 
@@ -34,6 +33,18 @@ __host__ __device__ inline size_t plane_row_bytes(int type, int plane, int G) {
   if (plane == 1) return (size_t)(type == Q4K ? 16 : 64) * G;
   if (plane == 2) return type == Q4K ? 0 : (size_t)16 * G;
   return type == Q4K ? 0 : (size_t)2 * G;
+}
+__host__ __device__ inline size_t tile_bytes(int type, int G) { return (size_t)8 * block_bytes(type) * G; }
+// offset of plane p inside a tile
+__host__ __device__ inline size_t tile_plane_off(int type, int G, int plane) {
+  size_t o = 0;
+  for (int p = 0; p < plane; ++p) o += 8 * plane_row_bytes(type, p, G);
+  return o;
+}
+// byte `off` of plane p of row `row`, relative to a tile-aligned base holding row 0 of a tile
+__host__ __device__ inline size_t row_plane_off(int type, int G, int row, int plane, size_t off) {
+  return (size_t)(row >> 3) * tile_bytes(type, G) + tile_plane_off(type, G, plane) +
+         (size_t)(row & 7) * plane_row_bytes(type, plane, G) + off;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -118,34 +129,34 @@ __host__ __device__ inline int map_row(int s, int mode, int arg) {
 }
 
 struct QViewW {   // writable view
-  uint8_t *p0, *p1, *p2, *p3;
+  uint8_t* base;
   int type, R, C, G;
 };
 
 // Scatter GGUF block b of device row d, block g into the planes.
 __device__ inline void scatter_block(const QViewW& m, int d, int g, const uint8_t* b) {
-  const int G = m.G;
-  if (m.type == Q4K) {
-    uint8_t* meta = m.p1 + ((size_t)d * G + g) * 16;
+  const int G = m.G, t = m.type;
+  if (t == Q4K) {
+    uint8_t* meta = m.base + row_plane_off(t, G, d, 1, (size_t)g * 16);
     for (int i = 0; i < 16; i++) meta[i] = b[i];
-    uint8_t* row = m.p0 + (size_t)d * 128 * G;
+    uint8_t* row = m.base + row_plane_off(t, G, d, 0, 0);
     for (int o = 0; o < 128; o++) {
       const int h = o >> 6, c = (o >> 5) & 1, jh = (o >> 4) & 1, jp = o & 15;
       row[(size_t)c * 64 * G + (size_t)g * 64 + (2 * h + jh) * 16 + jp] = b[16 + o];
     }
   } else {
-    uint8_t* row = m.p0 + (size_t)d * 128 * G;
+    uint8_t* row = m.base + row_plane_off(t, G, d, 0, 0);
     for (int o = 0; o < 128; o++) {
       const int h = o >> 6, c = (o >> 5) & 1, jh = (o >> 4) & 1, jp = o & 15;
       row[(size_t)c * 64 * G + (size_t)g * 64 + (2 * h + jh) * 16 + jp] = b[o];
     }
-    uint8_t* qh = m.p1 + ((size_t)d * G + g) * 64;
+    uint8_t* qh = m.base + row_plane_off(t, G, d, 1, (size_t)g * 64);
     for (int o = 0; o < 64; o++) qh[o] = b[128 + o];
-    uint8_t* sc = m.p2 + ((size_t)d * G + g) * 16;
+    uint8_t* sc = m.base + row_plane_off(t, G, d, 2, (size_t)g * 16);
     for (int h = 0; h < 2; h++)
       for (int jh = 0; jh < 2; jh++)
         for (int k = 0; k < 4; k++) sc[(2 * h + jh) * 4 + k] = b[192 + 8 * h + 2 * k + jh];
-    uint8_t* dd = m.p3 + ((size_t)d * G + g) * 2;
+    uint8_t* dd = m.base + row_plane_off(t, G, d, 3, (size_t)g * 2);
     dd[0] = b[208]; dd[1] = b[209];
   }
 }
@@ -186,25 +197,25 @@ __global__ void k_gen_half_normal(__half* y, long long n, uint64_t base) {
 // operation order (q4kernels.h:12-33): Q4_K w = fl(fl(d*sc)*q) - fl(dmin*mn); Q6_K
 // w = fl(d*scale)*(q-32).
 __device__ inline float dequant_elem(const QView& m, int row, int col) {
-  const int G = m.G, g = col >> 8, e = col & 255;
+  const int G = m.G, t = m.type, g = col >> 8, e = col & 255;
   const int h = e >> 7, k6 = (e >> 5) & 3, j = e & 31, jh = j >> 4, jp = j & 15, u = 2 * h + jh;
-  if (m.type == Q4K) {
-    const uint8_t* meta = m.p1 + ((size_t)row * G + g) * 16;
+  if (t == Q4K) {
+    const uint8_t* meta = m.base + row_plane_off(t, G, row, 1, (size_t)g * 16);
     const float d = h2f_bits(meta[0] | (meta[1] << 8)), dm = h2f_bits(meta[2] | (meta[3] << 8));
     const uint8_t* s = meta + 4;
     const int k = 4 * h + k6;
     const int sc = k < 4 ? (s[k] & 63) : ((s[k + 4] & 15) | ((s[k - 4] >> 6) << 4));
     const int mn = k < 4 ? (s[k + 4] & 63) : ((s[k + 4] >> 4) | ((s[k] >> 6) << 4));
-    const uint8_t byte = m.p0[(size_t)row * 128 * G + (size_t)(k6 >> 1) * 64 * G + (size_t)g * 64 + u * 16 + jp];
+    const uint8_t byte = m.base[row_plane_off(t, G, row, 0, (size_t)(k6 >> 1) * 64 * G + (size_t)g * 64 + u * 16 + jp)];
     const int q = (byte >> ((k6 & 1) * 4)) & 15;
     const float ds = __fmul_rn(d, (float)sc), ms = __fmul_rn(dm, (float)mn);
     return __fsub_rn(__fmul_rn(ds, (float)q), ms);
   }
-  const uint8_t lob = m.p0[(size_t)row * 128 * G + (size_t)(k6 & 1) * 64 * G + (size_t)g * 64 + u * 16 + jp];
+  const uint8_t lob = m.base[row_plane_off(t, G, row, 0, (size_t)(k6 & 1) * 64 * G + (size_t)g * 64 + u * 16 + jp)];
   const int low = (lob >> ((k6 >> 1) * 4)) & 15;
-  const int high = (m.p1[((size_t)row * G + g) * 64 + u * 16 + jp] >> (2 * k6)) & 3;
-  const int scale = (int8_t)m.p2[((size_t)row * G + g) * 16 + u * 4 + k6];
-  const uint8_t* dp = m.p3 + ((size_t)row * G + g) * 2;
+  const int high = (m.base[row_plane_off(t, G, row, 1, (size_t)g * 64 + u * 16 + jp)] >> (2 * k6)) & 3;
+  const int scale = (int8_t)m.base[row_plane_off(t, G, row, 2, (size_t)g * 16 + u * 4 + k6)];
+  const uint8_t* dp = m.base + row_plane_off(t, G, row, 3, (size_t)g * 2);
   const float d = h2f_bits(dp[0] | (dp[1] << 8));
   return __fmul_rn(__fmul_rn(d, (float)scale), (float)((low | (high << 4)) - 32));
 }

@@ -40,7 +40,7 @@ def test_device_generator_matches_oracle(kq, oracle, ty):
 
 
 SHAPES = [(12, 12288, 4096), (14, 4096, 12288), (14, 1024, 4096), (12, 4096, 4096), (12, 8, 256),
-          (14, 16, 512), (12, 40, 1024), (14, 64, 2048), (12, 128, 6144), (14, 8, 4096)]
+          (14, 16, 512), (12, 40, 1024), (14, 64, 2048), (12, 128, 6144), (14, 8, 4096), (12, 16, 16384)]
 
 
 @pytest.mark.parametrize("ty,R,Cc", SHAPES)
