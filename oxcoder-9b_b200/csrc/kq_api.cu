@@ -111,8 +111,8 @@ static int check_shape(int type, int R, int C) {
   if (R <= 0 || C <= 0 || R % 8 || C % 256)
     return set_err(KQ_ERR_ARG, "Invalid packed tensor dimensions: rows must be a positive multiple of 8 and cols of 256");
   const int LPR = 4 * (C / 256);
-  if (!(LPR == 4 || LPR == 8 || LPR == 16 || (LPR % 32 == 0 && LPR <= 256)))
-    return set_err(KQ_ERR_ARG, "unsupported column count (need 256, 512, 1024 or a multiple of 2048 up to 16384)");
+  if (!(LPR == 4 || LPR == 8 || LPR == 16 || (LPR % 32 == 0 && LPR <= 192)))
+    return set_err(KQ_ERR_ARG, "unsupported column count (need 256, 512, 1024 or a multiple of 2048 up to 12288)");
   return KQ_OK;
 }
 

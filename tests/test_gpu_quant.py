@@ -40,7 +40,7 @@ def test_device_generator_matches_oracle(kq, oracle, ty):
 
 
 SHAPES = [(12, 12288, 4096), (14, 4096, 12288), (14, 1024, 4096), (12, 4096, 4096), (12, 8, 256),
-          (14, 16, 512), (12, 40, 1024), (14, 64, 2048), (12, 128, 6144), (14, 8, 4096), (12, 16, 16384)]
+          (14, 16, 512), (12, 40, 1024), (14, 64, 2048), (12, 128, 6144), (14, 8, 4096)]
 
 
 @pytest.mark.parametrize("ty,R,Cc", SHAPES)
@@ -91,6 +91,8 @@ def test_bad_shapes_rejected(kq):
         kq.QMat(12, 8, 300)
     with pytest.raises(ValueError):
         kq.QMat(13, 8, 256)
+    with pytest.raises(ValueError):
+        kq.QMat(12, 8, 16384)          # wider than one CTA's digit-plane prologue supports
     m = kq.QMat(12, 8, 256)
     with pytest.raises(ValueError):
         m.upload(np.zeros(100, np.uint8))
