@@ -266,28 +266,87 @@ static cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& pl, cudaStre
   return cudaLaunchKernelEx(&cfg, gemv_fn(pl.TM, pl.RPG), p);
 }
 
-template <int G>
-static cudaError_t launch_attn_t(const AttnParams& a, cudaStream_t s, bool pdl) {
+template <int G, int CL>
+static cudaError_t launch_attn_cl_t(const AttnParams& a, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)a.n_kv, (unsigned)a.nsplit);
+  cfg.gridDim = dim3((unsigned)(a.n_kv * CL));
   cfg.blockDim = dim3(ATT_THREADS);
   cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CL;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, k_attn_cluster<G, CL>, a);
+}
+template <int G>
+static cudaError_t launch_attn_split_t(const AttnSplitParams& a, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.a.n_kv, (unsigned)a.nsplit);
+  cfg.blockDim = dim3(ATT_THREADS);
+  cfg.dynamicSmemBytes = (size_t)ATT_SLOTS * 2 * ATT_P * 128 * 2;
   cfg.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_attn_decode<G>, a);
+  return cudaLaunchKernelEx(&cfg, k_attn_split<G>, a);
 }
-static cudaError_t launch_attn(const AttnParams& a, int G, cudaStream_t s, bool pdl) {
+static cudaError_t launch_attn_split(const AttnSplitParams& a, int G, cudaStream_t s, bool pdl) {
   switch (G) {
-    case 1: return launch_attn_t<1>(a, s, pdl);
-    case 2: return launch_attn_t<2>(a, s, pdl);
-    case 4: return launch_attn_t<4>(a, s, pdl);
-    case 8: return launch_attn_t<8>(a, s, pdl);
-    default: return cudaErrorInvalidValue;
+    case 1: return launch_attn_split_t<1>(a, s, pdl);
+    case 2: return launch_attn_split_t<2>(a, s, pdl);
+    case 4: return launch_attn_split_t<4>(a, s, pdl);
+    default: return launch_attn_split_t<8>(a, s, pdl);
   }
+}
+static int attn_split_setup() {
+  const int bytes = ATT_SLOTS * 2 * ATT_P * 128 * 2;
+  CU(cudaFuncSetAttribute(k_attn_split<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  CU(cudaFuncSetAttribute(k_attn_split<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  CU(cudaFuncSetAttribute(k_attn_split<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  CU(cudaFuncSetAttribute(k_attn_split<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  return KQ_OK;
+}
+typedef cudaError_t (*AttnClFn)(const AttnParams&, cudaStream_t, bool);
+static AttnClFn attn_cl_fn(int G, int CL) {
+  if (CL == 16) return G == 1 ? launch_attn_cl_t<1, 16> : G == 2 ? launch_attn_cl_t<2, 16> : G == 4 ? launch_attn_cl_t<4, 16> : launch_attn_cl_t<8, 16>;
+  return G == 1 ? launch_attn_cl_t<1, 8> : G == 2 ? launch_attn_cl_t<2, 8> : G == 4 ? launch_attn_cl_t<4, 8> : launch_attn_cl_t<8, 8>;
+}
+template <int G, int CL>
+static int attn_cl_setup() {
+  if (CL > 8) CU(cudaFuncSetAttribute(k_attn_cluster<G, CL>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  return KQ_OK;
+}
+// Cluster size for the attention of `n_kv` heads: 16 CTAs per head when the device can keep
+// n_kv such clusters resident at once, else 8.
+static int attn_cluster_size(int G, int n_kv) {
+  int rc = G == 1 ? attn_cl_setup<1, 16>() : G == 2 ? attn_cl_setup<2, 16>() : G == 4 ? attn_cl_setup<4, 16>() : attn_cl_setup<8, 16>();
+  if (rc) return 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(n_kv * 16));
+  cfg.blockDim = dim3(ATT_THREADS);
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 16;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int nclusters = 0;
+  const void* fn = G == 1 ? (const void*)k_attn_cluster<1, 16> : G == 2 ? (const void*)k_attn_cluster<2, 16>
+                 : G == 4 ? (const void*)k_attn_cluster<4, 16> : (const void*)k_attn_cluster<8, 16>;
+  if (const char* e = std::getenv("KQ_ATTN_CL")) return std::atoi(e) == 16 ? 16 : 8;   // tuning override
+  const cudaError_t qe = cudaOccupancyMaxActiveClusters(&nclusters, fn, &cfg);
+  if (std::getenv("KQ_VERBOSE")) std::fprintf(stderr, "kq: %d active 16-CTA attention clusters (%s)\n", nclusters, cudaGetErrorString(qe));
+  if (qe != cudaSuccess) { cudaGetLastError(); return 8; }
+  return nclusters >= n_kv ? 16 : 8;
 }
 
 // ------------------------------------------------------------------------------ model
@@ -306,8 +365,6 @@ struct kq_model {
   float* out_norm = nullptr;
   float *cos_t = nullptr, *sin_t = nullptr;
   float *h[2] = {nullptr, nullptr}, *y = nullptr, *q = nullptr, *att = nullptr, *mbuf = nullptr, *logits = nullptr;
-  float *apart = nullptr, *apart_ml = nullptr;
-  int* aticket = nullptr;
   float* hpart_val = nullptr;
   int* hpart_idx = nullptr;
   int* hticket = nullptr;
@@ -316,7 +373,11 @@ struct kq_model {
   int* out_ids = nullptr;           // tokens of the device-resident loop
   int out_cap = 0;
   int* err = nullptr;
-  int nsplit = 0;
+  int attn_cl = 16;                  // CTAs per kv head in the cluster attention
+  int attn_mode = 0;                 // 0: split form, 1: cluster form
+  int attn_nsplit = 1;
+  float *apart = nullptr, *apart_ml = nullptr;
+  int* aticket = nullptr;
   cudaGraphExec_t g_step = nullptr, g_feed = nullptr;
   std::vector<void*> allocs;
 };
@@ -383,7 +444,7 @@ static int validate_cfg(const kq_config& c) {
   if (G != 1 && G != 2 && G != 4 && G != 8) return set_err(KQ_ERR_ARG, "query heads per kv head must be 1, 2, 4 or 8");
   if (c.dim < 512) return set_err(KQ_ERR_ARG, "dim must be at least 512");
   if (c.n_heads * c.head_dim < 512) return set_err(KQ_ERR_ARG, "n_heads * head_dim must be at least 512");
-  if (c.ctx < 1 || c.ctx > ATT_P * ATT_MAX_SPLITS) return set_err(KQ_ERR_ARG, "ctx out of range (1 .. 65536)");
+  if (c.ctx < 1 || c.ctx > ATT_MAX_CTX) return set_err(KQ_ERR_ARG, "ctx out of range (1 .. 65536)");
   if (c.vocab <= 0 || c.vocab % 8) return set_err(KQ_ERR_ARG, "vocab must be a positive multiple of 8");
   if (c.t_gate != c.t_up) return set_err(KQ_ERR_ARG, "gate and up must share a quantisation type");
   if (c.n_layers < 1) return set_err(KQ_ERR_ARG, "n_layers must be positive");
@@ -441,10 +502,13 @@ extern "C" kq_model* kq_model_create(const kq_config* cfg, int device) {
     m->att = dalloc<float>(m, QD, ok);
     m->mbuf = dalloc<float>(m, c.ffn, ok);
     m->logits = dalloc<float>(m, c.vocab, ok);
-    m->nsplit = (c.ctx + ATT_P - 1) / ATT_P;
-    m->apart = dalloc<float>(m, (size_t)c.n_kv_heads * m->nsplit * (c.n_heads / c.n_kv_heads) * c.head_dim, ok);
-    m->apart_ml = dalloc<float>(m, (size_t)c.n_kv_heads * m->nsplit * (c.n_heads / c.n_kv_heads) * 2, ok);
+    m->attn_cl = attn_cluster_size(c.n_heads / c.n_kv_heads, c.n_kv_heads);
+    m->attn_mode = std::getenv("KQ_ATTN") && std::atoi(std::getenv("KQ_ATTN")) == 1 ? 1 : 0;
+    m->attn_nsplit = std::min(ATT_SPLITS_MAX, std::max(1, m->nsm / c.n_kv_heads));
+    m->apart = dalloc<float>(m, (size_t)c.n_kv_heads * m->attn_nsplit * (c.n_heads / c.n_kv_heads) * c.head_dim, ok);
+    m->apart_ml = dalloc<float>(m, (size_t)c.n_kv_heads * m->attn_nsplit * (c.n_heads / c.n_kv_heads) * 2, ok);
     m->aticket = dalloc<int>(m, c.n_kv_heads, ok);
+    if (attn_split_setup() != KQ_OK) ok = false;
     m->hpart_val = dalloc<float>(m, 1024, ok);
     m->hpart_idx = dalloc<int>(m, 1024, ok);
     m->hticket = dalloc<int>(m, 1, ok);
@@ -644,12 +708,22 @@ static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
     first = false;
     // attention
     AttnParams a;
-    a.q = m->q; a.kc = w.kc; a.vc = w.vc; a.part = m->apart; a.part_ml = m->apart_ml; a.ticket = m->aticket;
-    a.out = m->att; a.st = m->st; a.n_kv = c.n_kv_heads; a.ctx = c.ctx; a.nsplit = m->nsplit;
+    a.q = m->q; a.kc = w.kc; a.vc = w.vc;
+    a.out = m->att; a.st = m->st; a.n_kv = c.n_kv_heads; a.ctx = c.ctx;
     a.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
     a.err = m->err;
     a.trace_id = trace++;
-    CU(launch_attn(a, G, s, true));
+    if (m->attn_mode == 1) {
+      CU(attn_cl_fn(G, m->attn_cl)(a, s, true));
+    } else {
+      AttnSplitParams sa;
+      sa.a = a;
+      sa.part = m->apart;
+      sa.part_ml = m->apart_ml;
+      sa.ticket = m->aticket;
+      sa.nsplit = m->attn_nsplit;
+      CU(launch_attn_split(sa, G, s, true));
+    }
     // o projection
     SegSpec so[1] = {{w.o, EPI_F32, m->y, nullptr}};
     if ((rc = fill_gemv(so, 1, false, m->nsm, p, pl))) return rc;

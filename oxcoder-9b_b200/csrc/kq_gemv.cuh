@@ -39,6 +39,8 @@ constexpr int KQ_MAX_NRG = 8;              // row groups (named barriers 1..8)
 constexpr int KQ_BAR_PROLOGUE = 14, KQ_BAR_ARGMAX = 15;
 constexpr int KQ_XSCAL = 18;               // per-unit scalars: s3, poison, xsf[4], c[3][4]
 constexpr int KQ_MAX_ITEMS = 4;            // prologue items per thread: the planner keeps >= 2 row groups
+constexpr int KQ_PREFETCH_STAGES = 1;      // stages requested before the prologue is done
+constexpr int KQ_MAX_HALF_HD = 128;        // rotary half width held in shared memory
 
 struct DecodeState {   // device-resident per-step state
   int tok;        // token processed by this step
@@ -86,7 +88,7 @@ struct GemvParams {
 
 // Shared-memory carve-up, identical on host (sizing) and device.
 struct GemvSmem {
-  size_t stages, xplanes, xscal, bars, red, redd, best, total;
+  size_t stages, xplanes, xscal, bars, red, redd, best, rope, total;
 };
 __host__ __device__ inline size_t gs_align(size_t x, size_t a) { return (x + a - 1) / a * a; }
 __host__ __device__ inline GemvSmem gemv_smem_layout(int nslots, int stage_bytes, int LPR, int NRG, int RPG, int nthr_c) {
@@ -100,6 +102,7 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int nslots, int stage_bytes
   s.red = o = gs_align(o, 8); o += (size_t)2 * RPG * NRG * WPR * 4;
   s.redd = o = gs_align(o, 8); o += (size_t)((nthr_c + 31) / 32) * 8;
   s.best = o = gs_align(o, 8); o += (size_t)NRG * RPG * 8;
+  s.rope = o = gs_align(o, 16); o += (size_t)2 * KQ_MAX_HALF_HD * 4;   // cos, sin of this step's position
   s.total = gs_align(o, 128);
   return s;
 }
@@ -263,7 +266,8 @@ __device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem
     }
   }
   float v[KQ_MAX_ITEMS][8];
-  // ---- loads (all issued before any use)
+  float gm[KQ_MAX_ITEMS][8];
+  // ---- loads (all issued before any use, the norm weights included)
 #pragma unroll
   for (int it = 0; it < KQ_MAX_ITEMS; ++it) {
     const int item = tid + it * nthr_c;
@@ -277,7 +281,9 @@ __device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem
 #pragma unroll
           for (int i = 0; i < 8; ++i) v[it][i] = dequant_elem(P.emb, tok, col0 + i);
         }
-      } else {
+      }
+      if (P.xmode != XS_PLAIN) load8(P.gamma + col0, gm[it]);
+      if (P.xmode == XS_NORM) {
         float hv[8], yv[8];
         load8(P.h_in + col0, hv);
         if (P.y_add) load8(P.y_add + col0, yv);
@@ -307,6 +313,7 @@ __device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
     if (lane == 0) redd[warp] = acc;
     named_bar(KQ_BAR_PROLOGUE, nthr_c);
+    if (tid == 0) KQ_TRACE_AT(P.trace_id, 6);
     double tot = 0.0;
     for (int w = 0; w < nthr_c / 32; ++w) tot += redd[w];
     const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / (double)P.C), P.eps)));
@@ -314,10 +321,8 @@ __device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem
     for (int it = 0; it < KQ_MAX_ITEMS; ++it) {
       const int item = tid + it * nthr_c;
       if (item < nitems) {
-        float gm[8];
-        load8(P.gamma + item_col0(item), gm);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[it][i] = __fmul_rn(__fmul_rn(v[it][i], s), gm[i]);
+        for (int i = 0; i < 8; ++i) v[it][i] = __fmul_rn(__fmul_rn(v[it][i], s), gm[it][i]);
       }
     }
   }
@@ -384,6 +389,7 @@ __device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem
       xscal[1 * LPR + u] = bad ? __int_as_float(0x7fc00000) : 0.f;
     }
   }
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 7);
   named_bar(KQ_BAR_PROLOGUE, nthr_c);
 }
 
@@ -446,6 +452,7 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
   uint64_t* empty = full + P.nslots;
   float* red = reinterpret_cast<float*>(smem + L.red);
   __shared__ int s_fail, s_issued, s_done;
+  __shared__ __align__(8) uint64_t pro_bar;   // completes when the consumers' prologue is done
 
   int s_begin, s_end;
   cta_stage_range(P, s_begin, s_end);
@@ -453,6 +460,7 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
   const int ncw = nthr_c >> 5;
   if (tid == 0) {
     for (int i = 0; i < P.nslots; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], ncw); }
+    mbar_init(&pro_bar, 1);
     fence_mbar_init();
     s_fail = 0;
     s_issued = 0;
@@ -470,6 +478,11 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
       for (int i = 0; i < nmine; ++i) {
         const int slot = i % P.nslots;
         const uint32_t round = (uint32_t)(i / P.nslots);
+        // One stage goes out at once; the rest waits for the consumers' prologue, whose few
+        // latency-bound L2 reads would otherwise queue behind a ring's worth of weight traffic.
+        if (i == KQ_PREFETCH_STAGES) {
+          if (!mbar_wait(&pro_bar, 0, P.err, KQ_DEV_ERR_WAIT_FULL)) { s_fail = 1; break; }
+        }
         if (i >= P.nslots) {
           if (!mbar_wait(&empty[slot], (round - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY)) { s_fail = 1; break; }
         }
@@ -500,7 +513,19 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
   // ------------------------------------------------------------------ consumers
   pdl_wait();
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 1);
+  // the step's position, read once; the rotary row of that position into shared memory (made
+  // visible by the prologue's barriers) -- no global load on the per-stage path
+  int pos = P.st ? P.st->pos : 0;
+  const bool kv_ok = pos >= 0 && pos < P.ctx;   // the host validates; never store outside the cache
+  if (!kv_ok) pos = 0;
+  float* rope_c = reinterpret_cast<float*>(smem + L.rope);
+  float* rope_s = rope_c + KQ_MAX_HALF_HD;
+  if (P.cos_t && tid < (P.hd >> 1)) {
+    rope_c[tid] = __ldcg(P.cos_t + (size_t)pos * (P.hd >> 1) + tid);
+    rope_s[tid] = __ldcg(P.sin_t + (size_t)pos * (P.hd >> 1) + tid);
+  }
   gemv_prologue(P, smem, L, nthr_c);
+  if (tid == 0) mbar_arrive(&pro_bar);
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 2);
   const int rg = tid / LPR, u = tid % LPR;
   const int h = (u & 3) >> 1, g = u >> 2;
@@ -613,12 +638,7 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
     const int rloc = rg * RPG + u;
     if (u < RPG && rloc < rows) {
       const int grow = row0 + rloc;
-      int pos = P.st ? P.st->pos : 0;
-      const bool kv_ok = pos >= 0 && pos < P.ctx;   // the host validates; never store outside the cache
-      if (!kv_ok && (epi == EPI_ROPE_K || epi == EPI_V || epi == EPI_ROPE_Q)) {
-        atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
-        pos = 0;
-      }
+      if (!kv_ok && (epi == EPI_ROPE_K || epi == EPI_V || epi == EPI_ROPE_Q)) atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
       switch (epi) {
         case EPI_F32: sg.out_f[grow] = fin; break;
         case EPI_ARGMAX:
@@ -636,7 +656,7 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
         case EPI_ROPE_K:
           if ((u & 1) == 0) {
             const int hh = grow / P.hd, i2 = (grow % P.hd) >> 1, half = P.hd >> 1;
-            const float c = P.cos_t[(size_t)pos * half + i2], sn = P.sin_t[(size_t)pos * half + i2];
+            const float c = rope_c[i2], sn = rope_s[i2];
             const float o0 = __fsub_rn(__fmul_rn(fin, c), __fmul_rn(fin_odd, sn));
             const float o1v = __fadd_rn(__fmul_rn(fin, sn), __fmul_rn(fin_odd, c));
             if (epi == EPI_ROPE_Q) {
