@@ -116,6 +116,28 @@ int kq_time_matvec(kq_qmat* const* mats, int ncopies, int n, float* ms_out);
 /* Bytes the device layout of this matrix occupies (equal to the GGUF bytes). */
 size_t kq_qmat_bytes(const kq_qmat* a);
 
+/* ------------------------------------------------------------------ no-allocation argmax
+ * This entry point has no counterpart in the reference; it is an addition of this library.
+ *
+ * *idx_dev = the lowest row index r with the largest (W x)[r], for device x_dev (cols floats);
+ * the same GEMV and tie rule as the greedy head of kq_step, enqueued on `stream` (0 = legacy
+ * default) without synchronising. It is for callers that may not allocate device memory while
+ * they run: a server that hands all free HBM to its K/V cache at start-up (an allocation would
+ * fail or evict), or a latency-bound sampling loop that cannot take the device-wide
+ * synchronisation cudaMalloc / cudaFree may imply. The call allocates nothing: the kernel's
+ * scratch (the row products, the per-CTA partials and a completion ticket) is a fixed array
+ * inside this library, one per device, KQ_NOALLOC_MAX_ROWS row products at most.
+ *  - Matrices with more than KQ_NOALLOC_MAX_ROWS rows are rejected with KQ_ERR_ARG.
+ *  - The first call on each device looks up that device's scratch address (cudaGetSymbolAddress);
+ *    make it before any stream capture that could include this call.
+ *  - There is one scratch per device: calls on the same device that overlap in time (different
+ *    streams, or different host threads) race and give wrong indices. Calls one after another on
+ *    one stream are safe.
+ *  - A bounded-wait failure on the device is reported, as for kq_qmat_matvec_dev, by the next
+ *    synchronising matrix call (KQ_ERR_TIMEOUT). */
+#define KQ_NOALLOC_MAX_ROWS 262144
+int kq_qmat_argmax_noalloc(kq_qmat* a, const float* x_dev, int32_t* idx_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

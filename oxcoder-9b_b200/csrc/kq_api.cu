@@ -1060,3 +1060,71 @@ extern "C" int kq_time_matvec(kq_qmat* const* mats, int ncopies, int n, float* m
   if (!rc) rc = dev_err_check(a->device);
   return rc;
 }
+
+// ------------------------------------------------------------------------------ no-allocation argmax
+// kq_qmat_argmax_noalloc runs the argmax form of the GEMV (k_gemv with the ARGMAX epilogue, the
+// kernel that closes every decode step) for callers that may not allocate device memory while
+// they run. The kernel's scratch -- the row products, one (value, index) partial per CTA, the
+// CTAs' completion ticket and the step state the epilogue advances -- is the file-scope array
+// below: one fixed-size instance per device, created when the module is loaded, never freed.
+// KQ_NOALLOC_MAX_ROWS (include/kq.h, 262144): row products the scratch holds (1 MiB of floats)
+constexpr int KQ_NOALLOC_MAX_CTAS = 1024;     // CTA partials the scratch holds
+constexpr size_t KQ_NOALLOC_HEADER = 256;     // ticket at 0, DecodeState at 16; zeroed before each launch
+constexpr size_t KQ_NOALLOC_VAL = KQ_NOALLOC_HEADER;
+constexpr size_t KQ_NOALLOC_IDX = KQ_NOALLOC_VAL + (size_t)KQ_NOALLOC_MAX_CTAS * 4;
+constexpr size_t KQ_NOALLOC_PROD = KQ_NOALLOC_IDX + (size_t)KQ_NOALLOC_MAX_CTAS * 4;
+constexpr size_t KQ_NOALLOC_BYTES = KQ_NOALLOC_PROD + (size_t)KQ_NOALLOC_MAX_ROWS * 4;
+static_assert(16 + sizeof(DecodeState) <= KQ_NOALLOC_HEADER, "scratch header too small");
+static_assert(KQ_NOALLOC_PROD % 256 == 0, "row products must stay 256-byte aligned");
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[KQ_NOALLOC_BYTES];
+
+static unsigned char* g_noalloc_addr[16];   // per device, looked up once
+static std::mutex g_noalloc_mu;
+
+// With `device` current: the device address of this device's instance of the scratch array.
+static int noalloc_scratch(int device, unsigned char** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_err(KQ_ERR_BACKEND, std::string("kq_qmat_argmax_noalloc: cudaGetSymbolAddress of the scratch: ") +
+                                         cudaGetErrorString(e));
+    g_noalloc_addr[device] = static_cast<unsigned char*>(p);
+  }
+  *out = g_noalloc_addr[device];
+  return KQ_OK;
+}
+
+extern "C" int kq_qmat_argmax_noalloc(kq_qmat* a, const float* x_dev, int32_t* idx_dev, void* stream) {
+  if (!a || !x_dev || !idx_dev) return set_err(KQ_ERR_ARG, "kq_qmat_argmax_noalloc: null argument");
+  if (a->R > KQ_NOALLOC_MAX_ROWS)
+    return set_err(KQ_ERR_ARG, "kq_qmat_argmax_noalloc: " + std::to_string(a->R) + " rows exceed the static scratch (at most " +
+                                   std::to_string(KQ_NOALLOC_MAX_ROWS) + " rows)");
+  CU(cudaSetDevice(a->device));
+  unsigned char* s = nullptr;
+  int rc = noalloc_scratch(a->device, &s);
+  if (rc) return rc;
+  SegSpec ss[1] = {{a, EPI_ARGMAX, reinterpret_cast<float*>(s + KQ_NOALLOC_PROD), nullptr}};
+  GemvParams p;
+  GemvPlan pl;
+  rc = fill_gemv(ss, 1, false, g_dev[a->device].nsm, p, pl);
+  if (rc) return rc;
+  if (pl.grid > KQ_NOALLOC_MAX_CTAS)
+    return set_err(KQ_ERR_ARG, "kq_qmat_argmax_noalloc: launch needs " + std::to_string(pl.grid) +
+                                   " CTA partials, the static scratch holds " + std::to_string(KQ_NOALLOC_MAX_CTAS));
+  p.xmode = XS_PLAIN;
+  p.x = x_dev;
+  p.err = g_dev[a->device].err;
+  p.ticket = reinterpret_cast<int*>(s);
+  p.st = reinterpret_cast<DecodeState*>(s + 16);
+  p.part_val = reinterpret_cast<float*>(s + KQ_NOALLOC_VAL);
+  p.part_idx = reinterpret_cast<int*>(s + KQ_NOALLOC_IDX);
+  p.out_ids = idx_dev;   // written at st->steps == 0
+  p.out_cap = 1;
+  // the ticket and the step state must start at zero (a call that failed part-way can leave them set)
+  CU(cudaMemsetAsync(s, 0, KQ_NOALLOC_HEADER, (cudaStream_t)stream));
+  CU(launch_gemv(p, pl, (cudaStream_t)stream, false));
+  return KQ_OK;
+}

@@ -81,6 +81,7 @@ SIGNATURES = {
     "kq_qmat_matvec_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "kq_time_matvec": (C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.c_int, PF]),
     "kq_qmat_bytes": (C.c_size_t, [C.c_void_p]),
+    "kq_qmat_argmax_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
 }
 
 _lib = None
