@@ -30,6 +30,9 @@ CTX = 4096
 CFG2_WEIGHT_BYTES = 4434295040
 KV_BYTES_PER_POS = 131072
 CFG0_BYTES = 28311552 + 16384 + 49152        # W + x + y of the 12288 x 4096 Q4_K GEMV
+# DRAM read + write bytes of one config-0 GEMV launch, from the ncu capture summarised in
+# profiles/k_gemv_cfg0_q4k.md (same kernel and shape as the roofline leg below).
+CFG0_TRAFFIC = 28422912
 
 
 def peaks():
@@ -237,7 +240,7 @@ def main():
         line = {
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic (seeded generator, random-init Q4_K/Q6_K weights of the config-2 architecture)",
+            "dtype": "q4_k/q6_k x int8 digit planes (dp4a, int32) + f32", "data": "synthetic (seeded generator, random-init Q4_K/Q6_K weights of the config-2 architecture)",
             "config": {"workload": "config-2 batch-1 greedy decode at ctx 4K (KV pre-filled to %d, %d timed steps)" % (pos0 + W, K),
                        "model": "dense GQA 32L d4096 32q/8kv hd128 ffn12288 vocab151936, Q4_K + Q6_K",
                        "global_batch": world, "seq_len": CTX, "parallelism": "replicas" if world > 1 else "single",
@@ -247,7 +250,7 @@ def main():
             "gpu_launches": (5 * 32 + 1) * K,
             "roofline": {"bound": "hbm", "kernel": "k_gemv (config-0 Q4_K 12288x4096, 16 rotating copies)",
                          "achieved": gemv_gbs, "peak": hbm, "unit": "GB/s", "frac": gemv_gbs / hbm,
-                         "traffic": None, "peak_source": "measured" if pk else "fallback",
+                         "traffic": CFG0_TRAFFIC, "peak_source": "measured" if pk else "fallback",
                          "algorithmic_bytes_per_launch": CFG0_BYTES, "ms_per_launch": gemv_ms},
             "step_roofline": {"bound": "hbm", "achieved": step_gbs, "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm,
                               "bytes_per_token": step_bytes, "roofline_tok_s": hbm * 1e9 / step_bytes},
