@@ -10,6 +10,7 @@
 #include "kq_qformat.cuh"
 #include "kq_gemv.cuh"
 #include "kq_attn.cuh"
+#include "kq_decode.cuh"
 
 #include <cuda_runtime.h>
 #include <cmath>
@@ -204,7 +205,7 @@ static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, boo
       int slots = (int)((budget - fixed) / (stage_bytes + 16));
       slots = std::min(8, std::max(2, slots));
       pl.TR = TR; pl.LPR = LPR; pl.NRG = NRG; pl.RPG = RPG;
-      pl.TM = has4 && has6 ? TM_MIXED : has6 ? TM_Q6K : TM_Q4K;
+      pl.TM = (has4 && has6) || std::getenv("KQ_GEMV_MIXED") ? TM_MIXED : has6 ? TM_Q6K : TM_Q4K;   // env: tuning
       pl.stage_bytes = stage_bytes;
       pl.nslots = slots;
       pl.smem = gemv_smem_layout(slots, stage_bytes, LPR, NRG, RPG, LPR * NRG).total;
@@ -247,8 +248,47 @@ static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParam
     st += p.seg[i].nstage;
   }
   p.nstages = st;
-  p.C = C; p.G = C / 256; p.TR = pl.TR; p.LPR = pl.LPR; p.NRG = pl.NRG;
+  p.C = C; p.G = C / 256; p.TR = pl.TR; p.LPR = pl.LPR; p.NRG = pl.NRG; p.nlanes = 1;
   p.stage_bytes = pl.stage_bytes; p.nslots = pl.nslots;
+  return KQ_OK;
+}
+
+// Launch shape of a GEMV phase of the persistent decode kernel: its 384 threads form lanes of
+// max(32, 2 * LPR) threads (LPR = C/64 threads per row, RPG 4 rows each); a lane consumes whole
+// stages of TR = 4 * (lane threads / LPR) rows (one 8-row tile for C >= 1024) on its own, so
+// stages are small and a CTA's share of a phase splits evenly.
+static int fill_gemv_dec(const SegSpec* ss, int nseg, GemvParams& p, int& stage_bytes) {
+  if (nseg < 1 || nseg > KQ_MAX_SEG) return set_err(KQ_ERR_ARG, "bad segment count");
+  const int C = ss[0].m->C, G = C / 256, LPR = 4 * G;
+  int rowb = 0;
+  for (int i = 0; i < nseg; ++i) {
+    if (ss[i].m->C != C) return set_err(KQ_ERR_ARG, "fused GEMV segments must share the column count");
+    rowb = std::max(rowb, block_bytes(ss[i].m->type) * G);
+  }
+  const int lane_thr = std::max(32, 2 * LPR);
+  if (lane_thr > DEC_CONSUMERS || lane_thr % 32) return set_err(KQ_ERR_ARG, "no persistent-kernel shape for this column count");
+  const int nlanes = DEC_CONSUMERS / lane_thr, NRG = lane_thr / LPR;
+  if (NRG * DEC_RPG % 8) return set_err(KQ_ERR_ARG, "no persistent-kernel shape for this column count");
+  const int TR = NRG * DEC_RPG;
+  const int nthr_c = lane_thr * nlanes;
+  if (8 * LPR > KQ_MAX_ITEMS * nthr_c) return set_err(KQ_ERR_ARG, "persistent kernel: GEMV input too wide");
+  std::memset(&p, 0, sizeof(p));
+  p.nseg = nseg;
+  int st = 0;
+  for (int i = 0; i < nseg; ++i) {
+    p.seg[i].w = ss[i].m->view();
+    p.seg[i].stage0 = st;
+    p.seg[i].nstage = (ss[i].m->R + TR - 1) / TR;
+    p.seg[i].epi = ss[i].epi;
+    p.seg[i].out_f = ss[i].out_f;
+    p.seg[i].out_h = ss[i].out_h;
+    st += p.seg[i].nstage;
+  }
+  p.nstages = st;
+  p.C = C; p.G = G; p.TR = TR; p.LPR = LPR; p.NRG = NRG; p.nlanes = nlanes;
+  stage_bytes = (int)align_up((size_t)TR * rowb, 128);
+  p.stage_bytes = stage_bytes;
+  p.nslots = 0;
   return KQ_OK;
 }
 
@@ -379,6 +419,13 @@ struct kq_model {
   float *apart = nullptr, *apart_ml = nullptr;
   int* aticket = nullptr;
   cudaGraphExec_t g_step = nullptr, g_feed = nullptr;
+  // persistent decode kernel (k_decode): phase table, arrival counters, launch shape
+  bool persist = true;
+  PhaseDesc* d_phases = nullptr;
+  int nph_all = 0;
+  int* dec_bar = nullptr;
+  DecodeParams dec{};
+  size_t dec_smem = 0;
   std::vector<void*> allocs;
 };
 
@@ -504,6 +551,7 @@ extern "C" kq_model* kq_model_create(const kq_config* cfg, int device) {
     m->logits = dalloc<float>(m, c.vocab, ok);
     m->attn_cl = attn_cluster_size(c.n_heads / c.n_kv_heads, c.n_kv_heads);
     m->attn_mode = std::getenv("KQ_ATTN") && std::atoi(std::getenv("KQ_ATTN")) == 1 ? 1 : 0;
+    m->persist = std::getenv("KQ_PERSIST") && std::atoi(std::getenv("KQ_PERSIST")) == 1;   // opt-in for now
     m->attn_nsplit = std::min(ATT_SPLITS_MAX, std::max(1, m->nsm / c.n_kv_heads));
     m->apart = dalloc<float>(m, (size_t)c.n_kv_heads * m->attn_nsplit * (c.n_heads / c.n_kv_heads) * c.head_dim, ok);
     m->apart_ml = dalloc<float>(m, (size_t)c.n_kv_heads * m->attn_nsplit * (c.n_heads / c.n_kv_heads) * 2, ok);
@@ -665,15 +713,28 @@ extern "C" int kq_model_get_kv(kq_model* m, int layer, int which, int npos, uint
 }
 
 // ------------------------------------------------------------------------------ decode step
-static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
+// One token as a list of operations: per layer qkv / attention / o / gate-up / down, then the
+// head. `persist` selects the launch shapes of the persistent kernel instead of the per-kernel
+// planner; the buffers and fusions are the same.
+struct StepOp {
+  int kind;              // PH_GEMV / PH_ATTN
+  GemvParams g;
+  GemvPlan pl;           // per-kernel launches only
+  int stage_bytes;       // persistent kernel only
+  AttnSplitParams a;
+};
+
+static int build_step(kq_model* m, bool head, bool persist, std::vector<StepOp>& ops) {
   const kq_config& c = m->c;
   int trace = 0;   // launch index within the step (phase trace of KQ_TRACE builds)
-  const int G = c.n_heads / c.n_kv_heads;
-  GemvParams p;
-  GemvPlan pl;
+  ops.clear();
   int cur = 0;
-  bool first = true;
-  auto common = [&](GemvParams& pp) {
+  auto gemv = [&](const SegSpec* ss, int nseg, bool pairs, StepOp& op) -> int {
+    op.kind = PH_GEMV;
+    op.stage_bytes = 0;
+    int rc = persist ? fill_gemv_dec(ss, nseg, op.g, op.stage_bytes) : fill_gemv(ss, nseg, pairs, m->nsm, op.g, op.pl);
+    if (rc) return rc;
+    GemvParams& pp = op.g;
     pp.st = m->st;
     pp.vocab = c.vocab;
     pp.cos_t = m->cos_t;
@@ -683,14 +744,16 @@ static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
     pp.err = m->err;
     pp.eps = c.eps;
     pp.trace_id = trace++;
+    return KQ_OK;
   };
   for (int l = 0; l < c.n_layers; ++l) {
     LayerW& w = m->L[l];
+    StepOp op;
     // QKV (+ norm or embedding; rotary + K/V store)
     SegSpec qkv[3] = {{w.q, EPI_ROPE_Q, m->q, nullptr}, {w.k, EPI_ROPE_K, nullptr, w.kc}, {w.v, EPI_V, nullptr, w.vc}};
-    int rc = fill_gemv(qkv, 3, true, m->nsm, p, pl);
+    int rc = gemv(qkv, 3, true, op);
     if (rc) return rc;
-    common(p);
+    GemvParams& p = op.g;
     if (l == 0) {
       p.xmode = XS_EMBED;
       p.emb = m->emb->view();
@@ -704,58 +767,52 @@ static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
     p.gamma = w.attn_norm;
     p.h_out = m->h[cur ^ 1];
     cur ^= 1;
-    CU(launch_gemv(p, pl, s, !first));
-    first = false;
+    ops.push_back(op);
     // attention
-    AttnParams a;
+    StepOp at;
+    std::memset(&at, 0, sizeof(at));
+    at.kind = PH_ATTN;
+    AttnParams& a = at.a.a;
     a.q = m->q; a.kc = w.kc; a.vc = w.vc;
     a.out = m->att; a.st = m->st; a.n_kv = c.n_kv_heads; a.ctx = c.ctx;
     a.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
     a.err = m->err;
     a.trace_id = trace++;
-    if (m->attn_mode == 1) {
-      CU(attn_cl_fn(G, m->attn_cl)(a, s, true));
-    } else {
-      AttnSplitParams sa;
-      sa.a = a;
-      sa.part = m->apart;
-      sa.part_ml = m->apart_ml;
-      sa.ticket = m->aticket;
-      sa.nsplit = m->attn_nsplit;
-      CU(launch_attn_split(sa, G, s, true));
-    }
+    at.a.part = m->apart;
+    at.a.part_ml = m->apart_ml;
+    at.a.ticket = m->aticket;
+    at.a.nsplit = m->attn_nsplit;
+    ops.push_back(at);
     // o projection
     SegSpec so[1] = {{w.o, EPI_F32, m->y, nullptr}};
-    if ((rc = fill_gemv(so, 1, false, m->nsm, p, pl))) return rc;
-    common(p);
-    p.xmode = XS_PLAIN;
-    p.x = m->att;
-    CU(launch_gemv(p, pl, s, true));
+    if ((rc = gemv(so, 1, false, op))) return rc;
+    op.g.xmode = XS_PLAIN;
+    op.g.x = m->att;
+    ops.push_back(op);
     // gate/up (+ norm, SwiGLU)
     SegSpec sg[1] = {{w.gu, EPI_SWIGLU, m->mbuf, nullptr}};
-    if ((rc = fill_gemv(sg, 1, true, m->nsm, p, pl))) return rc;
-    common(p);
-    p.xmode = XS_NORM;
-    p.h_in = m->h[cur];
-    p.y_add = m->y;
-    p.gamma = w.ffn_norm;
-    p.h_out = m->h[cur ^ 1];
+    if ((rc = gemv(sg, 1, true, op))) return rc;
+    op.g.xmode = XS_NORM;
+    op.g.h_in = m->h[cur];
+    op.g.y_add = m->y;
+    op.g.gamma = w.ffn_norm;
+    op.g.h_out = m->h[cur ^ 1];
     cur ^= 1;
-    CU(launch_gemv(p, pl, s, true));
+    ops.push_back(op);
     // down
     SegSpec sd[1] = {{w.down, EPI_F32, m->y, nullptr}};
-    if ((rc = fill_gemv(sd, 1, false, m->nsm, p, pl))) return rc;
-    common(p);
-    p.xmode = XS_PLAIN;
-    p.x = m->mbuf;
-    CU(launch_gemv(p, pl, s, true));
+    if ((rc = gemv(sd, 1, false, op))) return rc;
+    op.g.xmode = XS_PLAIN;
+    op.g.x = m->mbuf;
+    ops.push_back(op);
   }
   if (head) {
+    StepOp op;
     SegSpec sh[1] = {{m->out, EPI_ARGMAX, m->logits, nullptr}};
-    int rc = fill_gemv(sh, 1, false, m->nsm, p, pl);
+    int rc = gemv(sh, 1, false, op);
     if (rc) return rc;
-    if (pl.grid > 1024) return set_err(KQ_ERR_ARG, "head grid too large");
-    common(p);
+    if (!persist && op.pl.grid > 1024) return set_err(KQ_ERR_ARG, "head grid too large");
+    GemvParams& p = op.g;
     p.xmode = XS_NORM;
     p.h_in = m->h[cur];
     p.y_add = m->y;
@@ -766,8 +823,126 @@ static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
     p.ticket = m->hticket;
     p.out_ids = m->out_ids;
     p.out_cap = m->out_cap;
-    CU(launch_gemv(p, pl, s, true));
+    ops.push_back(op);
   }
+  return KQ_OK;
+}
+
+static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
+  std::vector<StepOp> ops;
+  int rc = build_step(m, head, false, ops);
+  if (rc) return rc;
+  const int G = m->c.n_heads / m->c.n_kv_heads;
+  bool first = true;
+  for (const StepOp& op : ops) {
+    if (op.kind == PH_GEMV) {
+      CU(launch_gemv(op.g, op.pl, s, !first));
+    } else if (m->attn_mode == 1) {
+      CU(attn_cl_fn(G, m->attn_cl)(op.a.a, s, true));
+    } else {
+      CU(launch_attn_split(op.a, G, s, true));
+    }
+    first = false;
+  }
+  return KQ_OK;
+}
+
+// ------------------------------------------------------------------------------ persistent kernel
+typedef cudaError_t (*DecFn)(const DecodeParams&, int grid, size_t smem, cudaStream_t s);
+template <int G>
+static cudaError_t launch_decode_t(const DecodeParams& d, int grid, size_t smem, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(DEC_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;   // every CTA resident at once, or the launch fails
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_decode<G>, d);
+}
+static const void* decode_fn_ptr(int G) {
+  return G == 1 ? (const void*)k_decode<1> : G == 2 ? (const void*)k_decode<2> : G == 4 ? (const void*)k_decode<4>
+                                                                                       : (const void*)k_decode<8>;
+}
+static DecFn decode_fn(int G) {
+  return G == 1 ? launch_decode_t<1> : G == 2 ? launch_decode_t<2> : G == 4 ? launch_decode_t<4> : launch_decode_t<8>;
+}
+
+// Builds the phase table and the launch shape of the persistent kernel (once per model).
+static int setup_persistent(kq_model* m) {
+  std::vector<StepOp> ops;
+  int rc = build_step(m, true, true, ops);
+  if (rc) return rc;
+  const int G = m->c.n_heads / m->c.n_kv_heads;
+  size_t slot = (size_t)2 * ATT_P * 128 * 2;   // one K + V chunk
+  size_t work = 0;
+  for (const StepOp& op : ops) {
+    if (op.kind == PH_GEMV) {
+      const int nthr_c = op.g.LPR * op.g.NRG * op.g.nlanes;
+      if (op.g.xmode != XS_PLAIN && 8 * op.g.LPR > 2 * nthr_c)
+        return set_err(KQ_ERR_ARG, "persistent kernel: a normed GEMV input is too wide (more than 2 items per thread)");
+      slot = std::max(slot, (size_t)op.stage_bytes);
+      work = std::max(work, gemv_smem_layout(0, 0, op.g.LPR, op.g.NRG * op.g.nlanes, DEC_RPG, nthr_c).total);
+    }
+  }
+  const size_t att_work = (size_t)(G == 1 ? AttnScratch<1>::total : G == 2 ? AttnScratch<2>::total
+                                   : G == 4 ? AttnScratch<4>::total : AttnScratch<8>::total) * 4;
+  work = align_up(std::max(work, att_work), 128);
+  slot = align_up(slot, 128);
+  const size_t desc = align_up(DEC_NDESC * sizeof(PhaseDesc), 128);
+  cudaFuncAttributes fa;
+  CU(cudaFuncGetAttributes(&fa, decode_fn_ptr(G)));
+  int optin = 0;
+  CU(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device));
+  const size_t budget = (size_t)optin - fa.sharedSizeBytes;
+  const size_t fixed = work + desc + (2 * DEC_NB + DEC_NDESC) * 8;
+  if (budget < fixed + 2 * slot) return set_err(KQ_ERR_ARG, "persistent kernel does not fit in shared memory");
+  const size_t ring = (budget - fixed) / 128 * 128;
+  DecodeParams& d = m->dec;
+  std::memset(&d, 0, sizeof(d));
+  d.ring_bytes = (int)ring;
+  d.work_off = (int)ring;
+  d.desc_off = (int)(d.work_off + work);
+  d.bars_off = (int)(d.desc_off + desc);
+  m->dec_smem = (size_t)d.bars_off + (size_t)(2 * DEC_NB + DEC_NDESC) * 8;
+  CU(cudaFuncSetAttribute(decode_fn_ptr(G), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->dec_smem));
+  // phase table on the device
+  std::vector<PhaseDesc> ph(ops.size());
+  std::memset(ph.data(), 0, ph.size() * sizeof(PhaseDesc));
+  for (size_t i = 0; i < ops.size(); ++i) {
+    ph[i].kind = ops[i].kind;
+    if (ops[i].kind == PH_GEMV) ph[i].g = ops[i].g;
+    else ph[i].a = ops[i].a;
+  }
+  bool ok = true;
+  m->d_phases = dalloc<PhaseDesc>(m, ph.size(), ok);
+  m->nph_all = (int)ph.size();
+  m->dec_bar = dalloc<int>(m, ph.size() + 1, ok);
+  if (!ok) return set_err(KQ_ERR_MEMORY, "persistent kernel tables");
+  CU(cudaMemcpy(m->d_phases, ph.data(), ph.size() * sizeof(PhaseDesc), cudaMemcpyHostToDevice));
+  d.ph = m->d_phases;
+  d.bar = m->dec_bar;
+  d.nbar = m->nph_all + 1;
+  d.st = m->st;
+  d.err = m->err;
+  // the whole grid must be co-resident: one CTA per SM
+  int per_sm = 0;
+  CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fn_ptr(G), DEC_THREADS, m->dec_smem));
+  if (per_sm < 1) return set_err(KQ_ERR_BACKEND, "persistent decode kernel cannot be resident");
+  if (std::getenv("KQ_VERBOSE"))
+    std::fprintf(stderr, "kq: persistent decode: %d phases, ring %zu B (largest stage %zu B), work %zu B, smem %zu B\n",
+                 m->nph_all, ring, slot, work, m->dec_smem);
+  return KQ_OK;
+}
+
+static int launch_persistent(kq_model* m, bool head) {
+  DecodeParams d = m->dec;
+  d.nph = head ? m->nph_all : m->nph_all - 1;
+  const int G = m->c.n_heads / m->c.n_kv_heads;
+  CU(decode_fn(G)(d, m->nsm, m->dec_smem, m->stream));
   return KQ_OK;
 }
 
@@ -786,6 +961,7 @@ static int build_graph(kq_model* m, bool head, cudaGraphExec_t* out) {
 
 static int ensure_graphs(kq_model* m) {
   int rc;
+  if (m->persist) return m->d_phases ? KQ_OK : setup_persistent(m);
   if (!m->g_step && (rc = build_graph(m, true, &m->g_step))) return rc;
   if (!m->g_feed && (rc = build_graph(m, false, &m->g_feed))) return rc;
   return KQ_OK;
@@ -796,6 +972,7 @@ static int check_dev_err(kq_model* m) {
   CU(cudaMemcpy(&e, m->err, sizeof(int), cudaMemcpyDeviceToHost));
   if (e) {
     cudaMemset(m->err, 0, sizeof(int));
+    if (m->dec_bar) cudaMemset(m->dec_bar, 0, (size_t)(m->nph_all + 1) * sizeof(int));   // re-arm the phase counters
     if (e & (KQ_DEV_ERR_BAD_TOKEN | KQ_DEV_ERR_BAD_POS)) return set_err(KQ_ERR_ARG, "device saw an invalid token or position");
     char buf[96];
     std::snprintf(buf, sizeof buf, "a bounded device wait gave up (error bits 0x%x)", e);
@@ -815,7 +992,11 @@ static int run_one(kq_model* m, int tok, int pos, bool head) {
   m->st_host->next_tok = -1;
   m->st_host->steps = 0;
   CU(cudaMemcpyAsync(m->st, m->st_host, sizeof(DecodeState), cudaMemcpyHostToDevice, m->stream));
-  CU(cudaGraphLaunch(head ? m->g_step : m->g_feed, m->stream));
+  if (m->persist) {
+    if ((rc = launch_persistent(m, head))) return rc;
+  } else {
+    CU(cudaGraphLaunch(head ? m->g_step : m->g_feed, m->stream));
+  }
   if (head) CU(cudaMemcpyAsync(m->st_host, m->st, sizeof(DecodeState), cudaMemcpyDeviceToHost, m->stream));
   CU(cudaStreamSynchronize(m->stream));
   if ((rc = check_dev_err(m))) return rc;
@@ -881,7 +1062,13 @@ extern "C" int kq_decode_loop(kq_model* m, int tok, int pos, int n, int32_t* out
   CU(cudaMemcpyAsync(m->st, m->st_host, sizeof(DecodeState), cudaMemcpyHostToDevice, m->stream));
   // each replay embeds st->tok at st->pos; the head's last CTA stores the argmax in out_ids and
   // advances (tok, pos) on the device, so no host round trip separates the steps
-  for (int i = 0; i < n; ++i) CU(cudaGraphLaunch(m->g_step, m->stream));
+  for (int i = 0; i < n; ++i) {
+    if (m->persist) {
+      if ((rc = launch_persistent(m, true))) return rc;
+    } else {
+      CU(cudaGraphLaunch(m->g_step, m->stream));
+    }
+  }
   CU(cudaMemcpyAsync(out, m->out_ids, (size_t)n * sizeof(int32_t), cudaMemcpyDeviceToHost, m->stream));
   CU(cudaStreamSynchronize(m->stream));
   return check_dev_err(m);
@@ -900,7 +1087,13 @@ extern "C" int kq_time_decode(kq_model* m, int tok, int pos, int n, float* ms_ou
   CU(cudaEventCreate(&e1));
   CU(cudaStreamSynchronize(m->stream));
   CU(cudaEventRecord(e0, m->stream));
-  for (int i = 0; i < n; ++i) CU(cudaGraphLaunch(m->g_step, m->stream));
+  for (int i = 0; i < n; ++i) {
+    if (m->persist) {
+      if ((rc = launch_persistent(m, true))) return rc;
+    } else {
+      CU(cudaGraphLaunch(m->g_step, m->stream));
+    }
+  }
   CU(cudaEventRecord(e1, m->stream));
   CU(cudaEventSynchronize(e1));
   float ms = 0.f;

@@ -61,6 +61,8 @@ struct GemvParams {
   Seg seg[KQ_MAX_SEG];
   int nseg, nstages;
   int C, G, TR, LPR, NRG;
+  int nlanes;            // independent thread lanes (the persistent kernel; 1 for k_gemv), each
+                         // LPR * NRG threads consuming its own stages
   int stage_bytes, nslots;
   // activation source
   int xmode;
@@ -251,7 +253,12 @@ __device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
 // Prologue: residual + norm (or plain activations), digit planes and per-unit scalars into shared
 // memory. One pass: every thread issues all of its loads first and keeps the values in registers,
 // then the norm reduction, then the exact digit split (integer rounding done on the FMA pipe).
-__device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem& L, int nthr_c) {
+// MAXI bounds the prologue items per thread (8 columns each) the caller guarantees. A plain
+// (XS_PLAIN) prologue may be split into calls over item blocks it_base, it_base + MAXI, ...;
+// only the call with `last` ends with the barrier that publishes the planes.
+template <int MAXI = KQ_MAX_ITEMS>
+__device__ __forceinline__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem& L, int nthr_c,
+                                              int it_base = 0, bool last = true) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint4* xplanes = reinterpret_cast<uint4*>(smem + L.xplanes);
   float* xscal = reinterpret_cast<float*>(smem + L.xscal);
@@ -265,12 +272,12 @@ __device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem
       tok = 0;
     }
   }
-  float v[KQ_MAX_ITEMS][8];
-  float gm[KQ_MAX_ITEMS][8];
+  float v[MAXI][8];
+  float gm[MAXI][8];
   // ---- loads (all issued before any use, the norm weights included)
 #pragma unroll
-  for (int it = 0; it < KQ_MAX_ITEMS; ++it) {
-    const int item = tid + it * nthr_c;
+  for (int it = 0; it < MAXI; ++it) {
+    const int item = tid + (it_base + it) * nthr_c;
     if (item < nitems) {
       const int col0 = item_col0(item);
       if (P.xmode == XS_PLAIN) {
@@ -297,8 +304,8 @@ __device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem
     double acc = 0.0;
     const bool wr = blockIdx.x == 0 && P.h_out;
 #pragma unroll
-    for (int it = 0; it < KQ_MAX_ITEMS; ++it) {
-      const int item = tid + it * nthr_c;
+    for (int it = 0; it < MAXI; ++it) {
+      const int item = tid + (it_base + it) * nthr_c;
       if (item < nitems) {
         if (wr) {
           float4* ho = reinterpret_cast<float4*>(P.h_out + item_col0(item));
@@ -318,8 +325,8 @@ __device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem
     for (int w = 0; w < nthr_c / 32; ++w) tot += redd[w];
     const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / (double)P.C), P.eps)));
 #pragma unroll
-    for (int it = 0; it < KQ_MAX_ITEMS; ++it) {
-      const int item = tid + it * nthr_c;
+    for (int it = 0; it < MAXI; ++it) {
+      const int item = tid + (it_base + it) * nthr_c;
       if (item < nitems) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[it][i] = __fmul_rn(__fmul_rn(v[it][i], s), gm[it][i]);
@@ -329,8 +336,8 @@ __device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem
   // ---- exact digit split per unit
   const float RND = 12582912.0f;   // 1.5 * 2^23: adding it rounds to an integer (RNE), |y| <= 128
 #pragma unroll
-  for (int it = 0; it < KQ_MAX_ITEMS; ++it) {
-    const int item = tid + it * nthr_c;
+  for (int it = 0; it < MAXI; ++it) {
+    const int item = tid + (it_base + it) * nthr_c;
     if (item >= nitems) break;            // uniform across a warp
     const int u = item >> 3, q = item & 7, k = q >> 1, half = q & 1;
     float m = 0.f;
@@ -390,7 +397,7 @@ __device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem
     }
   }
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 7);
-  named_bar(KQ_BAR_PROLOGUE, nthr_c);
+  if (last) named_bar(KQ_BAR_PROLOGUE, nthr_c);
 }
 
 // Sum over the LPR threads of a row group of RPG per-thread partials. For LPR >= 32 the warp
@@ -398,7 +405,7 @@ __device__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem
 // barrier; for LPR < 32 the row group is a segment of a warp. Returns, in thread u == rr of the
 // row group (rr < RPG), the total of row rr.
 template <int RPG>
-__device__ __forceinline__ float rows_reduce(const float (&p)[RPG], int u, int rg, int LPR, float* red) {
+__device__ __forceinline__ float rows_reduce(const float (&p)[RPG], int u, int rg, int LPR, float* red, int bar0 = 1) {
   const int lane = threadIdx.x & 31;
   if (LPR < 32) {
     float mine = 0.f;
@@ -433,11 +440,268 @@ __device__ __forceinline__ float rows_reduce(const float (&p)[RPG], int u, int r
   // row held by this lane: RPG 4 -> lanes 0-7 row 0, 8-15 row 1, 16-23 row 2, 24-31 row 3
   const int myrow = RPG == 4 ? (((lane >> 4) << 1) | ((lane >> 3) & 1)) : lane / span;
   if ((lane % span) == 0) red[(rg * RPG + myrow) * WPR + wr] = v;
-  named_bar(1 + rg, LPR);
+  if (WPR > 1) named_bar(bar0 + rg, LPR);
+  else __syncwarp();
   float sum = 0.f;
   if (u < RPG)
     for (int w = 0; w < WPR; ++w) sum += red[(rg * RPG + u) * WPR + w];
   return sum;
+}
+
+// ------------------------------------------------------------------------------ consumer pieces
+// Shared by k_gemv (one GEMV per launch) and the persistent decode kernel (one GEMV per phase).
+
+// Per-thread consumer state of one GEMV.
+struct GemvThread {
+  int lane, rg, u, h, g, WPR;
+  int bar0;          // named barrier of row group 0 of this lane
+  int pos;           // the step's position (0 when out of range)
+  bool kv_ok;        // the position lies inside the cache
+  XS xs;
+  float s3q;
+  const float* rope_c;
+  const float* rope_s;
+  const uint4* xplanes;
+  float* red;
+  float bv;          // ARGMAX: best value / index seen by this thread
+  int bi;
+};
+
+__device__ __forceinline__ void gemv_thread_init(const GemvParams& P, uint8_t* smem, const GemvSmem& L, int pos, GemvThread& T) {
+  const int tid = threadIdx.x, LPR = P.LPR, lt = tid % (LPR * P.NRG);
+  T.lane = tid / (LPR * P.NRG);
+  T.rg = lt / LPR;
+  T.u = lt % LPR;
+  T.h = (T.u & 3) >> 1;
+  T.g = T.u >> 2;
+  T.WPR = LPR >= 32 ? LPR >> 5 : 1;
+  T.bar0 = 1 + T.lane * P.NRG;
+  T.kv_ok = pos >= 0 && pos < P.ctx;   // the host validates; never store outside the cache
+  T.pos = T.kv_ok ? pos : 0;
+  T.rope_c = reinterpret_cast<const float*>(smem + L.rope);
+  T.rope_s = T.rope_c + KQ_MAX_HALF_HD;
+  T.xplanes = reinterpret_cast<const uint4*>(smem + L.xplanes);
+  T.red = reinterpret_cast<float*>(smem + L.red) + T.lane * 2 * 4 * P.NRG * T.WPR;   // RPG <= 4
+  T.bv = -FLT_MAX;
+  T.bi = 0x7fffffff;
+}
+
+// The rotary row of the step's position into shared memory; the prologue's barriers publish it.
+__device__ __forceinline__ void gemv_load_rope(const GemvParams& P, uint8_t* smem, const GemvSmem& L, const GemvThread& T) {
+  const int tid = threadIdx.x;
+  float* rc = reinterpret_cast<float*>(smem + L.rope);
+  if (P.cos_t && tid < (P.hd >> 1)) {
+    rc[tid] = __ldcg(P.cos_t + (size_t)T.pos * (P.hd >> 1) + tid);
+    rc[KQ_MAX_HALF_HD + tid] = __ldcg(P.sin_t + (size_t)T.pos * (P.hd >> 1) + tid);
+  }
+}
+
+__device__ __forceinline__ void gemv_load_rope_at(const GemvParams& P, uint8_t* smem, const GemvSmem& L, int pos) {
+  const int tid = threadIdx.x;
+  float* rc = reinterpret_cast<float*>(smem + L.rope);
+  if (P.cos_t && tid < (P.hd >> 1)) {
+    rc[tid] = __ldcg(P.cos_t + (size_t)pos * (P.hd >> 1) + tid);
+    rc[KQ_MAX_HALF_HD + tid] = __ldcg(P.sin_t + (size_t)pos * (P.hd >> 1) + tid);
+  }
+}
+
+// After the prologue: this thread's per-unit activation scalars into registers.
+__device__ __forceinline__ void gemv_load_xs(const GemvParams& P, uint8_t* smem, const GemvSmem& L, GemvThread& T) {
+  const int LPR = P.LPR, u = T.u;
+  const float* xscal = reinterpret_cast<const float*>(smem + L.xscal);
+  T.xs.s3 = xscal[u];
+  T.xs.poison = xscal[LPR + u];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    T.xs.xsf[k] = xscal[(2 + k) * LPR + u];
+#pragma unroll
+    for (int pl = 0; pl < 3; ++pl) T.xs.c[pl][k] = reinterpret_cast<const int*>(xscal)[(6 + 4 * pl + k) * LPR + u];
+  }
+  T.s3q = T.xs.s3 * 0.0625f;   // Q4_K sums carry a factor 16 (see q4k_group)
+}
+
+// Producer: the bytes and source of global stage s (whole 8-row tiles, one contiguous range).
+__device__ __forceinline__ uint32_t gemv_stage_src(const GemvParams& P, int s, int& segi, const uint8_t** src) {
+  while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
+  const QView& w = P.seg[segi].w;
+  const int row0 = (s - P.seg[segi].stage0) * P.TR;
+  const int rows = min(P.TR, w.R - row0);          // a multiple of 8 (whole tiles)
+  *src = w.base + (size_t)(row0 >> 3) * tile_bytes(w.type, w.G);
+  return (uint32_t)((size_t)(rows >> 3) * tile_bytes(w.type, w.G));
+}
+
+// One stage (TR rows of segment segi starting at global stage s) from shared memory `buf`:
+// load this thread's slice, release the slot (one arrive per warp on `empty_bar`; the warp whose
+// arrival frees it calls on_free()), compute, reduce across the row group (reduction buffer
+// `par` = 0/1 alternates between stages), epilogue.
+struct NoHook {
+  __device__ __forceinline__ void operator()() const {}
+};
+template <int TM, int RPG, class OnFree = NoHook>
+__device__ __forceinline__ void gemv_stage(const GemvParams& P, GemvThread& T, int s, int segi, const uint8_t* buf,
+                                           uint64_t* empty_bar, int par, const OnFree& on_free = OnFree()) {
+  const int tid = threadIdx.x, rg = T.rg, u = T.u, h = T.h, g = T.g, G = P.G, NRG = P.NRG, LPR = P.LPR;
+  const Seg& sg = P.seg[segi];
+  const bool is_q4 = TM == TM_Q4K || (TM == TM_MIXED && sg.w.type == Q4K);
+  const int row0 = (s - sg.stage0) * P.TR;
+  const int rows = min(P.TR, sg.w.R - row0);
+  const int type = is_q4 ? Q4K : Q6K;
+  const size_t TB = tile_bytes(type, G);
+  const size_t o1 = (size_t)8 * 128 * G;                                  // plane 1 in a tile
+  const size_t o2 = o1 + (size_t)8 * (is_q4 ? 16 : 64) * G, o3 = o2 + (size_t)8 * 16 * G;
+  // ---- load this thread's slice of its RPG rows, then free the stage
+  uint32_t a[RPG][4], b[RPG][4], q[RPG][4];
+  uint32_t m1[RPG];   // Q4_K: d | dmin << 16 ; Q6_K: four int8 scales
+  uint32_t m2[RPG];   // Q4_K: 6-bit scales as 4 bytes ; Q6_K: fp16 d bits
+  uint32_t m3[RPG];   // Q4_K: 6-bit mins as 4 bytes
+#pragma unroll
+  for (int rr = 0; rr < RPG; ++rr) {
+    const int r = min(rg * RPG + rr, rows - 1);   // rows past a short last stage reuse a real one
+    const uint8_t* tb = buf + (size_t)(r >> 3) * TB;
+    const int r8 = r & 7;
+    const uint8_t* p0 = tb + (size_t)r8 * 128 * G;
+    const uint4 A = lds128(p0 + u * 16);
+    const uint4 B = lds128(p0 + (size_t)64 * G + u * 16);
+    a[rr][0] = A.x; a[rr][1] = A.y; a[rr][2] = A.z; a[rr][3] = A.w;
+    b[rr][0] = B.x; b[rr][1] = B.y; b[rr][2] = B.z; b[rr][3] = B.w;
+    if (is_q4) {
+      const uint4 M = lds128(tb + o1 + ((size_t)r8 * G + g) * 16);
+      q4k_scale_words(M, h, m2[rr], m3[rr]);
+      m1[rr] = M.x;
+      q[rr][0] = q[rr][1] = q[rr][2] = q[rr][3] = 0;
+    } else {
+      const uint4 H = lds128(tb + o1 + (size_t)r8 * 64 * G + u * 16);
+      q[rr][0] = H.x; q[rr][1] = H.y; q[rr][2] = H.z; q[rr][3] = H.w;
+      m1[rr] = lds32(tb + o2 + (size_t)r8 * 16 * G + u * 4);
+      const size_t doff = ((size_t)r8 * G + g) * 2;
+      const uint32_t dw = lds32(tb + o3 + (doff & ~(size_t)3));
+      m2[rr] = (doff & 2) ? (dw >> 16) : (dw & 0xFFFFu);
+      m3[rr] = 0;
+    }
+  }
+  __syncwarp();
+  if ((tid & 31) == 0) {
+    if (mbar_arrive_completes(empty_bar)) on_free();
+  }
+  // ---- compute: group by group, the digit planes shared by the RPG rows
+  int Pi[RPG][3];
+  float Q_[RPG];
+#pragma unroll
+  for (int rr = 0; rr < RPG; ++rr) { Pi[rr][0] = Pi[rr][1] = Pi[rr][2] = 0; Q_[rr] = 0.f; }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint4 xw[3];
+#pragma unroll
+    for (int pl = 0; pl < 3; ++pl) xw[pl] = T.xplanes[(k * 3 + pl) * LPR + u];
+#pragma unroll
+    for (int rr = 0; rr < RPG; ++rr) {
+      if (is_q4) {
+        q4k_group(k < 2 ? a[rr] : b[rr], k, m2[rr], xw, Pi[rr]);
+        Q_[rr] = __fmaf_rn(byte_to_float_u(m3[rr], k), T.xs.xsf[k], Q_[rr]);
+      } else {
+        q6k_group(a[rr], b[rr], q[rr], k, m1[rr], xw, T.xs, Pi[rr]);
+      }
+    }
+  }
+  float part[RPG];
+#pragma unroll
+  for (int rr = 0; rr < RPG; ++rr) {
+    const float Pf = planes_combine(Pi[rr]);
+    if (is_q4) {
+      const float d = h2f_bits(m1[rr] & 0xFFFFu), dm = h2f_bits(m1[rr] >> 16);
+      part[rr] = __fadd_rn(__fsub_rn(__fmul_rn(T.s3q, __fmul_rn(d, Pf)), __fmul_rn(T.xs.s3, __fmul_rn(dm, Q_[rr]))), T.xs.poison);
+    } else {
+      part[rr] = __fadd_rn(__fmul_rn(T.xs.s3, __fmul_rn(h2f_bits(m2[rr]), Pf)), T.xs.poison);
+    }
+  }
+  // ---- reduce across the row group; thread u == rr holds row rr
+  const float fin = rows_reduce<RPG>(part, u, rg, LPR, T.red + par * RPG * NRG * T.WPR, T.bar0);
+  // ---- epilogue
+  const int epi = sg.epi;
+  const bool pair_epi = epi == EPI_SWIGLU || epi == EPI_ROPE_Q || epi == EPI_ROPE_K;
+  float fin_odd = 0.f;
+  if (pair_epi) fin_odd = __shfl_down_sync(0xffffffffu, fin, 1);
+  const int rloc = rg * RPG + u;
+  if (u < RPG && rloc < rows) {
+    const int grow = row0 + rloc;
+    const int pos = T.pos;
+    if (!T.kv_ok && (epi == EPI_ROPE_K || epi == EPI_V || epi == EPI_ROPE_Q)) atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
+    switch (epi) {
+      case EPI_F32: sg.out_f[grow] = fin; break;
+      case EPI_ARGMAX:
+        sg.out_f[grow] = fin;
+        if (fin > T.bv || (fin == T.bv && grow < T.bi)) { T.bv = fin; T.bi = grow; }
+        break;
+      case EPI_V: {
+        const int kv = grow / P.hd, e = grow % P.hd;
+        if (T.kv_ok) sg.out_h[((size_t)kv * P.ctx + pos) * P.hd + e] = __float2half_rn(fin);
+      } break;
+      case EPI_SWIGLU:
+        if ((u & 1) == 0) sg.out_f[grow >> 1] = __fmul_rn(silu_f(fin), fin_odd);
+        break;
+      case EPI_ROPE_Q:
+      case EPI_ROPE_K:
+        if ((u & 1) == 0) {
+          const int hh = grow / P.hd, i2 = (grow % P.hd) >> 1, half = P.hd >> 1;
+          const float c = T.rope_c[i2], sn = T.rope_s[i2];
+          const float o0 = __fsub_rn(__fmul_rn(fin, c), __fmul_rn(fin_odd, sn));
+          const float o1v = __fadd_rn(__fmul_rn(fin, sn), __fmul_rn(fin_odd, c));
+          if (epi == EPI_ROPE_Q) {
+            sg.out_f[hh * P.hd + i2] = o0;
+            sg.out_f[hh * P.hd + i2 + half] = o1v;
+          } else if (T.kv_ok) {
+            __half* dst = sg.out_h + ((size_t)hh * P.ctx + pos) * P.hd;
+            dst[i2] = __float2half_rn(o0);
+            dst[i2 + half] = __float2half_rn(o1v);
+          }
+        }
+        break;
+    }
+  }
+}
+
+// ARGMAX epilogue across CTAs: each CTA's best (value, index) to P.part_val / P.part_idx, and
+// the last CTA (ticket) merges them in CTA order (lowest index on ties), advances the step state
+// and re-arms the ticket. Called by the consumer threads of every CTA.
+template <int RPG>
+__device__ __forceinline__ void gemv_argmax_tail(const GemvParams& P, uint8_t* smem, const GemvSmem& L, const GemvThread& T,
+                                                 int nthr_c) {
+  const int tid = threadIdx.x, NRG = P.NRG * P.nlanes;
+  float* bestv = reinterpret_cast<float*>(smem + L.best);
+  int* besti = reinterpret_cast<int*>(bestv + NRG * RPG);
+  if (T.u < RPG) {
+    const int r = (T.lane * P.NRG + T.rg) * RPG + T.u;
+    bestv[r] = T.bv;
+    besti[r] = T.bi;
+  }
+  named_bar(KQ_BAR_ARGMAX, nthr_c);
+  if (tid == 0) {
+    float v0 = -FLT_MAX; int i0 = 0x7fffffff;
+    for (int r = 0; r < NRG * RPG; ++r)
+      if (bestv[r] > v0 || (bestv[r] == v0 && besti[r] < i0)) { v0 = bestv[r]; i0 = besti[r]; }
+    P.part_val[blockIdx.x] = v0;
+    P.part_idx[blockIdx.x] = i0;
+    __threadfence();
+    const int t = atomicAdd(P.ticket, 1);
+    if (t == (int)gridDim.x - 1) {
+      __threadfence();
+      float v1 = -FLT_MAX; int i1 = 0x7fffffff;
+      for (int c = 0; c < (int)gridDim.x; ++c) {
+        const float pv = *(volatile float*)&P.part_val[c];
+        const int pi = *(volatile int*)&P.part_idx[c];
+        if (pv > v1 || (pv == v1 && pi < i1)) { v1 = pv; i1 = pi; }
+      }
+      if (i1 == 0x7fffffff) i1 = 0;
+      // advance the device-resident step state: the next step embeds this token at pos + 1
+      DecodeState* st = P.st;
+      st->next_tok = i1;
+      if (P.out_ids && st->steps < P.out_cap) P.out_ids[st->steps] = i1;
+      st->steps += 1;
+      st->tok = i1;
+      st->pos += 1;
+      *P.ticket = 0;
+    }
+  }
 }
 
 // ------------------------------------------------------------------------------ the kernel
@@ -450,7 +714,6 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
   const GemvSmem L = gemv_smem_layout(P.nslots, P.stage_bytes, LPR, NRG, RPG, nthr_c);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + P.nslots;
-  float* red = reinterpret_cast<float*>(smem + L.red);
   __shared__ int s_fail, s_issued, s_done;
   __shared__ __align__(8) uint64_t pro_bar;   // completes when the consumers' prologue is done
 
@@ -487,15 +750,11 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
           if (!mbar_wait(&empty[slot], (round - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY)) { s_fail = 1; break; }
         }
         if (*(volatile int*)&s_fail) break;
-        const int s = s_begin + i;
-        while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
-        const QView& w = P.seg[segi].w;
-        const int row0 = (s - P.seg[segi].stage0) * P.TR;
-        const int rows = min(P.TR, w.R - row0);          // a multiple of 8 (whole tiles)
+        const uint8_t* src;
+        const uint32_t bytes = gemv_stage_src(P, s_begin + i, segi, &src);
         uint8_t* buf = smem + L.stages + (size_t)slot * P.stage_bytes;
-        const uint32_t bytes = (uint32_t)((size_t)(rows >> 3) * tile_bytes(w.type, w.G));
         mbar_arrive_expect_tx(&full[slot], bytes);
-        bulk_g2s(buf, w.base + (size_t)(row0 >> 3) * tile_bytes(w.type, w.G), bytes, &full[slot], pol);
+        bulk_g2s(buf, src, bytes, &full[slot], pol);
         *(volatile int*)&s_issued = i + 1;
       }
       KQ_TRACE_AT(P.trace_id, 5);
@@ -513,41 +772,14 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
   // ------------------------------------------------------------------ consumers
   pdl_wait();
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 1);
-  // the step's position, read once; the rotary row of that position into shared memory (made
-  // visible by the prologue's barriers) -- no global load on the per-stage path
-  int pos = P.st ? P.st->pos : 0;
-  const bool kv_ok = pos >= 0 && pos < P.ctx;   // the host validates; never store outside the cache
-  if (!kv_ok) pos = 0;
-  float* rope_c = reinterpret_cast<float*>(smem + L.rope);
-  float* rope_s = rope_c + KQ_MAX_HALF_HD;
-  if (P.cos_t && tid < (P.hd >> 1)) {
-    rope_c[tid] = __ldcg(P.cos_t + (size_t)pos * (P.hd >> 1) + tid);
-    rope_s[tid] = __ldcg(P.sin_t + (size_t)pos * (P.hd >> 1) + tid);
-  }
+  GemvThread T;
+  gemv_thread_init(P, smem, L, P.st ? P.st->pos : 0, T);
+  gemv_load_rope(P, smem, L, T);
   gemv_prologue(P, smem, L, nthr_c);
   if (tid == 0) mbar_arrive(&pro_bar);
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 2);
-  const int rg = tid / LPR, u = tid % LPR;
-  const int h = (u & 3) >> 1, g = u >> 2;
-  const int G = P.G;
-  const uint4* xplanes = reinterpret_cast<const uint4*>(smem + L.xplanes);
-  XS xs;
-  {
-    const float* xscal = reinterpret_cast<const float*>(smem + L.xscal);
-    xs.s3 = xscal[u];
-    xs.poison = xscal[LPR + u];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      xs.xsf[k] = xscal[(2 + k) * LPR + u];
-#pragma unroll
-      for (int pl = 0; pl < 3; ++pl) xs.c[pl][k] = reinterpret_cast<const int*>(xscal)[(6 + 4 * pl + k) * LPR + u];
-    }
-  }
-  const float s3q = xs.s3 * 0.0625f;   // Q4_K sums carry a factor 16 (see q4k_group)
-  float bv = -FLT_MAX;
-  int bi = 0x7fffffff;
+  gemv_load_xs(P, smem, L, T);
   int segi = 0;
-  const int WPR = LPR >= 32 ? LPR >> 5 : 1;
   for (int i = 0; i < nmine; ++i) {
     const int slot = i % P.nslots;
     const uint32_t round = (uint32_t)(i / P.nslots);
@@ -555,158 +787,11 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
     if (tid == 0 && i == 0) KQ_TRACE_AT(P.trace_id, 3);
     const int s = s_begin + i;
     while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
-    const Seg& sg = P.seg[segi];
-    const uint8_t* buf = smem + L.stages + (size_t)slot * P.stage_bytes;
-    const bool is_q4 = TM == TM_Q4K || (TM == TM_MIXED && sg.w.type == Q4K);
-    const int row0 = (s - sg.stage0) * P.TR;
-    const int rows = min(P.TR, sg.w.R - row0);
-    const int type = is_q4 ? Q4K : Q6K;
-    const size_t TB = tile_bytes(type, G);
-    const size_t o1 = (size_t)8 * 128 * G;                                  // plane 1 in a tile
-    const size_t o2 = o1 + (size_t)8 * (is_q4 ? 16 : 64) * G, o3 = o2 + (size_t)8 * 16 * G;
-    // ---- load this thread's slice of its RPG rows, then free the stage
-    uint32_t a[RPG][4], b[RPG][4], q[RPG][4];
-    uint32_t m1[RPG];   // Q4_K: d | dmin << 16 ; Q6_K: four int8 scales
-    uint32_t m2[RPG];   // Q4_K: 6-bit scales as 4 bytes ; Q6_K: fp16 d bits
-    uint32_t m3[RPG];   // Q4_K: 6-bit mins as 4 bytes
-#pragma unroll
-    for (int rr = 0; rr < RPG; ++rr) {
-      const int r = min(rg * RPG + rr, rows - 1);   // rows past a short last stage reuse a real one
-      const uint8_t* tb = buf + (size_t)(r >> 3) * TB;
-      const int r8 = r & 7;
-      const uint8_t* p0 = tb + (size_t)r8 * 128 * G;
-      const uint4 A = lds128(p0 + u * 16);
-      const uint4 B = lds128(p0 + (size_t)64 * G + u * 16);
-      a[rr][0] = A.x; a[rr][1] = A.y; a[rr][2] = A.z; a[rr][3] = A.w;
-      b[rr][0] = B.x; b[rr][1] = B.y; b[rr][2] = B.z; b[rr][3] = B.w;
-      if (is_q4) {
-        const uint4 M = lds128(tb + o1 + ((size_t)r8 * G + g) * 16);
-        q4k_scale_words(M, h, m2[rr], m3[rr]);
-        m1[rr] = M.x;
-        q[rr][0] = q[rr][1] = q[rr][2] = q[rr][3] = 0;
-      } else {
-        const uint4 H = lds128(tb + o1 + (size_t)r8 * 64 * G + u * 16);
-        q[rr][0] = H.x; q[rr][1] = H.y; q[rr][2] = H.z; q[rr][3] = H.w;
-        m1[rr] = lds32(tb + o2 + (size_t)r8 * 16 * G + u * 4);
-        const size_t doff = ((size_t)r8 * G + g) * 2;
-        const uint32_t dw = lds32(tb + o3 + (doff & ~(size_t)3));
-        m2[rr] = (doff & 2) ? (dw >> 16) : (dw & 0xFFFFu);
-        m3[rr] = 0;
-      }
-    }
-    __syncwarp();
-    if ((tid & 31) == 0) mbar_arrive(&empty[slot]);
+    gemv_stage<TM, RPG>(P, T, s, segi, smem + L.stages + (size_t)slot * P.stage_bytes, &empty[slot], i & 1);
     if (tid == 0) *(volatile int*)&s_done = i + 1;
-    // ---- compute: group by group, the digit planes shared by the RPG rows
-    int Pi[RPG][3];
-    float Q_[RPG];
-#pragma unroll
-    for (int rr = 0; rr < RPG; ++rr) { Pi[rr][0] = Pi[rr][1] = Pi[rr][2] = 0; Q_[rr] = 0.f; }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      uint4 xw[3];
-#pragma unroll
-      for (int pl = 0; pl < 3; ++pl) xw[pl] = xplanes[(k * 3 + pl) * LPR + u];
-#pragma unroll
-      for (int rr = 0; rr < RPG; ++rr) {
-        if (is_q4) {
-          q4k_group(k < 2 ? a[rr] : b[rr], k, m2[rr], xw, Pi[rr]);
-          Q_[rr] = __fmaf_rn(byte_to_float_u(m3[rr], k), xs.xsf[k], Q_[rr]);
-        } else {
-          q6k_group(a[rr], b[rr], q[rr], k, m1[rr], xw, xs, Pi[rr]);
-        }
-      }
-    }
-    float part[RPG];
-#pragma unroll
-    for (int rr = 0; rr < RPG; ++rr) {
-      const float Pf = planes_combine(Pi[rr]);
-      if (is_q4) {
-        const float d = h2f_bits(m1[rr] & 0xFFFFu), dm = h2f_bits(m1[rr] >> 16);
-        part[rr] = __fadd_rn(__fsub_rn(__fmul_rn(s3q, __fmul_rn(d, Pf)), __fmul_rn(xs.s3, __fmul_rn(dm, Q_[rr]))), xs.poison);
-      } else {
-        part[rr] = __fadd_rn(__fmul_rn(xs.s3, __fmul_rn(h2f_bits(m2[rr]), Pf)), xs.poison);
-      }
-    }
-    // ---- reduce across the row group; thread u == rr holds row rr
-    const float fin = rows_reduce<RPG>(part, u, rg, LPR, red + (i & 1) * RPG * NRG * WPR);
-    // ---- epilogue
-    const int epi = sg.epi;
-    const bool pair_epi = epi == EPI_SWIGLU || epi == EPI_ROPE_Q || epi == EPI_ROPE_K;
-    float fin_odd = 0.f;
-    if (pair_epi) fin_odd = __shfl_down_sync(0xffffffffu, fin, 1);
-    const int rloc = rg * RPG + u;
-    if (u < RPG && rloc < rows) {
-      const int grow = row0 + rloc;
-      if (!kv_ok && (epi == EPI_ROPE_K || epi == EPI_V || epi == EPI_ROPE_Q)) atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
-      switch (epi) {
-        case EPI_F32: sg.out_f[grow] = fin; break;
-        case EPI_ARGMAX:
-          sg.out_f[grow] = fin;
-          if (fin > bv || (fin == bv && grow < bi)) { bv = fin; bi = grow; }
-          break;
-        case EPI_V: {
-          const int kv = grow / P.hd, e = grow % P.hd;
-          if (kv_ok) sg.out_h[((size_t)kv * P.ctx + pos) * P.hd + e] = __float2half_rn(fin);
-        } break;
-        case EPI_SWIGLU:
-          if ((u & 1) == 0) sg.out_f[grow >> 1] = __fmul_rn(silu_f(fin), fin_odd);
-          break;
-        case EPI_ROPE_Q:
-        case EPI_ROPE_K:
-          if ((u & 1) == 0) {
-            const int hh = grow / P.hd, i2 = (grow % P.hd) >> 1, half = P.hd >> 1;
-            const float c = rope_c[i2], sn = rope_s[i2];
-            const float o0 = __fsub_rn(__fmul_rn(fin, c), __fmul_rn(fin_odd, sn));
-            const float o1v = __fadd_rn(__fmul_rn(fin, sn), __fmul_rn(fin_odd, c));
-            if (epi == EPI_ROPE_Q) {
-              sg.out_f[hh * P.hd + i2] = o0;
-              sg.out_f[hh * P.hd + i2 + half] = o1v;
-            } else if (kv_ok) {
-              __half* dst = sg.out_h + ((size_t)hh * P.ctx + pos) * P.hd;
-              dst[i2] = __float2half_rn(o0);
-              dst[i2 + half] = __float2half_rn(o1v);
-            }
-          }
-          break;
-      }
-    }
   }
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 4);
-  // ------------------------------------------------------------------ argmax across CTAs
-  if (P.seg[0].epi == EPI_ARGMAX) {
-    float* bestv = reinterpret_cast<float*>(smem + L.best);
-    int* besti = reinterpret_cast<int*>(bestv + NRG * RPG);
-    if (u < RPG) { bestv[rg * RPG + u] = bv; besti[rg * RPG + u] = bi; }
-    named_bar(KQ_BAR_ARGMAX, nthr_c);
-    if (tid == 0) {
-      float v0 = -FLT_MAX; int i0 = 0x7fffffff;
-      for (int r = 0; r < NRG * RPG; ++r)
-        if (bestv[r] > v0 || (bestv[r] == v0 && besti[r] < i0)) { v0 = bestv[r]; i0 = besti[r]; }
-      P.part_val[blockIdx.x] = v0;
-      P.part_idx[blockIdx.x] = i0;
-      __threadfence();
-      const int t = atomicAdd(P.ticket, 1);
-      if (t == (int)gridDim.x - 1) {
-        __threadfence();
-        float v1 = -FLT_MAX; int i1 = 0x7fffffff;
-        for (int c = 0; c < (int)gridDim.x; ++c) {
-          const float pv = *(volatile float*)&P.part_val[c];
-          const int pi = *(volatile int*)&P.part_idx[c];
-          if (pv > v1 || (pv == v1 && pi < i1)) { v1 = pv; i1 = pi; }
-        }
-        if (i1 == 0x7fffffff) i1 = 0;
-        // advance the device-resident step state: the next step embeds this token at pos + 1
-        DecodeState* st = P.st;
-        st->next_tok = i1;
-        if (P.out_ids && st->steps < P.out_cap) P.out_ids[st->steps] = i1;
-        st->steps += 1;
-        st->tok = i1;
-        st->pos += 1;
-        *P.ticket = 0;
-      }
-    }
-  }
+  if (P.seg[0].epi == EPI_ARGMAX) gemv_argmax_tail<RPG>(P, smem, L, T, nthr_c);
 }
 
 }  // namespace kq

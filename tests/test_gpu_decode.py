@@ -15,6 +15,15 @@ def kq_cfg(kq, t):
                              ffn=t["NFF"], vocab=t["vocab"], ctx=t["ctx"])
 
 
+@pytest.fixture(params=["persistent", "launches"], autouse=True)
+def decode_path(request, monkeypatch):
+    """Every test runs on both decode paths: the persistent one-kernel-per-token decode
+    (KQ_PERSIST=1) and the per-operation launches in a CUDA graph (the default); the variable is
+    read when a model is created."""
+    monkeypatch.setenv("KQ_PERSIST", "1" if request.param == "persistent" else "0")
+    return request.param
+
+
 @pytest.fixture(scope="module")
 def kq():
     import kq as K
