@@ -248,7 +248,7 @@ static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParam
     st += p.seg[i].nstage;
   }
   p.nstages = st;
-  p.C = C; p.G = C / 256; p.TR = pl.TR; p.LPR = pl.LPR; p.NRG = pl.NRG; p.nlanes = 1;
+  p.C = C; p.G = C / 256; p.TR = pl.TR; p.LPR = pl.LPR; p.NRG = pl.NRG; p.nlanes = 1; p.tps = 1;
   p.stage_bytes = pl.stage_bytes; p.nslots = pl.nslots;
   return KQ_OK;
 }
@@ -286,7 +286,14 @@ static int fill_gemv_dec(const SegSpec* ss, int nseg, GemvParams& p, int& stage_
   }
   p.nstages = st;
   p.C = C; p.G = G; p.TR = TR; p.LPR = LPR; p.NRG = NRG; p.nlanes = nlanes;
-  stage_bytes = (int)align_up((size_t)TR * rowb, 128);
+  // ring entries of up to 3 stages on phases with many stages per CTA (fewer, larger copies);
+  // single stages where a CTA has few (finer balance). An entry stays <= 81 KB.
+  const int per_cta = std::max(1, st / std::max(1, g_dev[ss[0].m->device].nsm));
+  const int tps_env = std::getenv("KQ_DEC_TPS") ? std::atoi(std::getenv("KQ_DEC_TPS")) : 0;   // tuning
+  int tps = tps_env > 0 ? tps_env : std::min(3, std::max(1, per_cta / 8));
+  while (tps > 1 && (size_t)tps * TR * rowb > 82560) --tps;
+  p.tps = tps;
+  stage_bytes = (int)align_up((size_t)tps * TR * rowb, 128);
   p.stage_bytes = stage_bytes;
   p.nslots = 0;
   return KQ_OK;
@@ -737,8 +744,12 @@ static int build_step(kq_model* m, bool head, bool persist, std::vector<StepOp>&
     GemvParams& pp = op.g;
     pp.st = m->st;
     pp.vocab = c.vocab;
-    pp.cos_t = m->cos_t;
-    pp.sin_t = m->sin_t;
+    // the rotary tables only where an epilogue rotates (the q/k/v GEMV); elsewhere the prologue
+    // would wait on loads it does not need
+    bool rope = false;
+    for (int i = 0; i < nseg; ++i) rope |= ss[i].epi == EPI_ROPE_Q || ss[i].epi == EPI_ROPE_K;
+    pp.cos_t = rope ? m->cos_t : nullptr;
+    pp.sin_t = rope ? m->sin_t : nullptr;
     pp.hd = c.head_dim;
     pp.ctx = c.ctx;
     pp.err = m->err;
@@ -900,7 +911,7 @@ static int setup_persistent(kq_model* m) {
   const size_t budget = (size_t)optin - fa.sharedSizeBytes;
   const size_t fixed = work + desc + (2 * DEC_NB + DEC_NDESC) * 8;
   if (budget < fixed + 2 * slot) return set_err(KQ_ERR_ARG, "persistent kernel does not fit in shared memory");
-  const size_t ring = (budget - fixed) / 128 * 128;
+  const size_t ring = (budget - fixed) / 128 * 128;   // >= 2 largest entries (checked above)
   DecodeParams& d = m->dec;
   std::memset(&d, 0, sizeof(d));
   d.ring_bytes = (int)ring;

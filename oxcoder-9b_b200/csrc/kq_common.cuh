@@ -113,7 +113,7 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
 // Compile-time opt-in (-DKQ_TRACE): per-CTA %globaltimer stamps at phase boundaries of the decode
 // kernels, written to a device buffer the host reads with kq_trace_read (kq_api.cu). Off by
 // default; the product build contains no trace code.
-constexpr int KQ_TRACE_LAUNCHES = 256, KQ_TRACE_CTAS = 1024, KQ_TRACE_POINTS = 8;
+constexpr int KQ_TRACE_LAUNCHES = 256, KQ_TRACE_CTAS = 1024, KQ_TRACE_POINTS = 12;
 #ifdef KQ_TRACE
 __device__ unsigned long long g_kq_trace[KQ_TRACE_LAUNCHES][KQ_TRACE_CTAS][KQ_TRACE_POINTS];
 __device__ __forceinline__ void kq_trace(int launch, int point) {

@@ -171,12 +171,18 @@ __device__ __forceinline__ int dec_producer(const DecodeParams& D, RingBook& B, 
       n1 = itm.nch;
     }
     int segi = 0;
-    for (int s = n0; s < n1; ++s) {
+    for (int s = n0; s < n1;) {
       const uint8_t* src;
       const __half* vsrc = nullptr;
       uint32_t bytes;
+      int cnt = 1;
       if (ph.kind == PH_GEMV) {
-        bytes = gemv_stage_src(ph.g, s, segi, &src);
+        bytes = gemv_stage_src(ph.g, s, segi, &src);   // also moves segi to s's segment
+        cnt = gemv_group(ph.g, s, n1, segi);
+        for (int j = 1; j < cnt; ++j) {
+          const uint8_t* s2;
+          bytes += gemv_stage_src(ph.g, s + j, segi, &s2);   // contiguous tiles of one segment
+        }
       } else {
         const int c0 = itm.t_begin + s * ATT_P;
         bytes = (uint32_t)attn_chunk_rows(itm, s, apos) * 128 * 2;
@@ -193,6 +199,7 @@ __device__ __forceinline__ int dec_producer(const DecodeParams& D, RingBook& B, 
         T = B.end[cons % DEC_NB];
         ++cons;
       }
+      if (s == n0) KQ_TRACE_AT(p, 8);
       const int slot = issued % DEC_NB;
       const int off = h % D.ring_bytes;
       B.off[slot] = off;
@@ -204,7 +211,9 @@ __device__ __forceinline__ int dec_producer(const DecodeParams& D, RingBook& B, 
         if (vsrc) bulk_g2s(ring + off + bytes, vsrc, bytes, &full[slot], pol);
       }
       ++issued;
+      s += cnt;
     }
+    KQ_TRACE_AT(p, 9);
   }
   return issued;
 }
@@ -465,7 +474,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant
     }
     if (tid == 0) KQ_TRACE_AT(p, 0);
     // this phase's descriptor (requested DEC_NDESC phases ago)
-    if (!fail && !mbar_wait(&cbar[p % DEC_NDESC], (uint32_t)(p / DEC_NDESC) & 1, D.err, KQ_DEV_ERR_WAIT_FULL)) fail = true;
+    if (!fail && !mbar_wait_abort(&cbar[p % DEC_NDESC], (uint32_t)(p / DEC_NDESC) & 1, D.err, KQ_DEV_ERR_WAIT_FULL))
+      fail = true;
     const PhaseDesc* desc = &cache[p % DEC_NDESC];
     if (desc->kind == PH_GEMV) {
       const GemvParams& P = desc->g;
@@ -489,38 +499,48 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant
         gemv_load_xs(P, work, L, T);
         const int lw = lane_thr >> 5;                       // warps in this lane
         const bool leader = tid % lane_thr == 0;
-        int segi = 0, k = 0;
+        int segi = 0, k = 0, e = 0;
 #ifdef KQ_TRACE
         unsigned long long wait_ns = 0;
 #endif
-        // lane T.lane takes this CTA's stages n0 + lane, n0 + lane + nlanes, ...
-        for (int s = n0 + T.lane; s < n1; s += P.nlanes, ++k) {
-          const int rs = ri + (s - n0), slot = rs % DEC_NB;
-          // after a failure the loop still runs (on whatever the ring holds) so that every thread
-          // keeps taking the same barriers; the phase barrier below then ends the kernel
-          int off = 0;
-#ifdef KQ_TRACE
-          unsigned long long tw0;
-          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tw0));
-#endif
-          if (!fail) {
-            off = wait_stage(D, book, full, rs);
-            if (off < 0) { fail = true; off = 0; }
-          }
-#ifdef KQ_TRACE
-          if (tid == 0) {
-            unsigned long long tw1;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tw1));
-            wait_ns += tw1 - tw0;
-          }
-#endif
-          if (tid == 0 && s == n0) KQ_TRACE_AT(p, 4);
+        // ring entries of this CTA's stages, dealt round-robin to the lanes
+        for (int s = n0; s < n1; ++e) {
           while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
-          if (P.seg[segi].w.type == Q4K)
-            gemv_stage<TM_Q4K, DEC_RPG>(P, T, s, segi, ring + off, &empty[slot], k & 1);
-          else
-            gemv_stage<TM_Q6K, DEC_RPG>(P, T, s, segi, ring + off, &empty[slot], k & 1);
-          if (leader && lw < DEC_CWARPS) mbar_arrive_cnt(&empty[slot], DEC_CWARPS - lw);
+          const int cnt = gemv_group(P, s, n1, segi);
+          if (e % P.nlanes == T.lane) {
+            const int rs = ri + e, slot = rs % DEC_NB;
+            // after a failure the loop still runs (on whatever the ring holds) so that every
+            // thread keeps taking the same barriers; the phase barrier below then ends the kernel
+            int off = 0;
+#ifdef KQ_TRACE
+            unsigned long long tw0;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tw0));
+#endif
+            if (tid == 0 && s == n0) KQ_TRACE_AT(p, 10);
+            if (!fail) {
+              off = wait_stage(D, book, full, rs);
+              if (off < 0) { fail = true; off = 0; }
+            }
+#ifdef KQ_TRACE
+            if (tid == 0) {
+              unsigned long long tw1;
+              asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tw1));
+              wait_ns += tw1 - tw0;
+            }
+#endif
+            if (tid == 0 && s == n0) KQ_TRACE_AT(p, 4);
+            const int type = P.seg[segi].w.type;
+            const size_t sb = (size_t)(P.TR >> 3) * tile_bytes(type, P.G);   // bytes of a full stage
+            for (int j = 0; j < cnt; ++j, ++k) {
+              uint64_t* rel = j == cnt - 1 ? &empty[slot] : nullptr;   // release after the last loads
+              if (type == Q4K)
+                gemv_stage<TM_Q4K, DEC_RPG>(P, T, s + j, segi, ring + off + j * sb, rel, k & 1);
+              else
+                gemv_stage<TM_Q6K, DEC_RPG>(P, T, s + j, segi, ring + off + j * sb, rel, k & 1);
+            }
+            if (leader && lw < DEC_CWARPS) mbar_arrive_cnt(&empty[slot], DEC_CWARPS - lw);
+          }
+          s += cnt;
         }
         if (tid == 0) KQ_TRACE_AT(p, 2);
 #ifdef KQ_TRACE
@@ -528,7 +548,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant
 #endif
         if (!fail && P.seg[0].epi == EPI_ARGMAX) gemv_argmax_tail<DEC_RPG>(P, work, L, T, nthr_c);
       }
-      ri += n1 - n0;   // every thread keeps the ring index in step, idle ones included
+      ri += gemv_group_count(P, n0, n1);   // every thread keeps the ring index in step, idle ones too
     } else {
       const AttnSplitParams& S = desc->a;
       const AttnItem itm = attn_item(S, apos);

@@ -63,6 +63,7 @@ struct GemvParams {
   int C, G, TR, LPR, NRG;
   int nlanes;            // independent thread lanes (the persistent kernel; 1 for k_gemv), each
                          // LPR * NRG threads consuming its own stages
+  int tps;               // persistent kernel: stages (of TR rows) per ring entry
   int stage_bytes, nslots;
   // activation source
   int xmode;
@@ -530,6 +531,21 @@ __device__ __forceinline__ uint32_t gemv_stage_src(const GemvParams& P, int s, i
   return (uint32_t)((size_t)(rows >> 3) * tile_bytes(w.type, w.G));
 }
 
+// Ring entries of the persistent kernel: up to P.tps consecutive stages of one segment.
+// Returns the stage count of the entry starting at stage s (< n1); segi must be s's segment.
+__device__ __forceinline__ int gemv_group(const GemvParams& P, int s, int n1, int segi) {
+  const int seg_end = P.seg[segi].stage0 + P.seg[segi].nstage;
+  return min(P.tps, min(n1, seg_end) - s);
+}
+__device__ __forceinline__ int gemv_group_count(const GemvParams& P, int n0, int n1) {
+  int e = 0, segi = 0;
+  for (int s = n0; s < n1; ++e) {
+    while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
+    s += gemv_group(P, s, n1, segi);
+  }
+  return e;
+}
+
 // One stage (TR rows of segment segi starting at global stage s) from shared memory `buf`:
 // load this thread's slice, release the slot (one arrive per warp on `empty_bar`; the warp whose
 // arrival frees it calls on_free()), compute, reduce across the row group (reduction buffer
@@ -580,7 +596,7 @@ __device__ __forceinline__ void gemv_stage(const GemvParams& P, GemvThread& T, i
     }
   }
   __syncwarp();
-  if ((tid & 31) == 0) {
+  if (empty_bar && (tid & 31) == 0) {   // null: the caller releases the slot after a later stage
     if (mbar_arrive_completes(empty_bar)) on_free();
   }
   // ---- compute: group by group, the digit planes shared by the RPG rows
