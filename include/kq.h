@@ -96,6 +96,34 @@ int kq_decode_loop(kq_model* m, int tok, int pos, int n, int32_t* out);
 /* Time n device-resident decode steps (CUDA events on the model's stream); returns ms. */
 int kq_time_decode(kq_model* m, int tok, int pos, int n, float* ms_out);
 
+/* ------------------------------------------------------------------ speculative verification
+ * Draft-then-verify over a draft TREE (the reference verifies linear chains only: spec.py:790-793
+ * greedy chain, spec.py:769-787 acceptance, spec.py:531-542 commit). A tree of n <= KQ_MAX_TREE
+ * nodes is given by parent pointers: node 0 is the last accepted token (at position pos, not yet
+ * fed), parents[0] = -1 and 0 <= parents[i] < i; a linear chain is parents[i] = i - 1. */
+#define KQ_MAX_TREE 128
+/* Runs every node through the model. Node i's K/V go to cache slot pos + i, its rotary position is
+ * pos + depth(i), and it attends to the positions below pos and to its ancestors and itself.
+ * Optional outputs: logits (n x vocab floats) and best (n argmax ids, lowest id on ties).
+ * The logits stay on the device for kq_accept. */
+int kq_verify(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, int pos, float* logits,
+              int32_t* best);
+/* Accepts a prefix path of the tree verified by the last kq_verify (same tokens / parents), on the
+ * device. temperature 0: greedy (a child is accepted iff its token is the argmax of its parent's
+ * logits; the last node's argmax is emitted). temperature > 0: speculative sampling with target
+ * softmax(logits / T) and draft distributions softmax(draft_logits[v]) (n x vocab, row v: the
+ * distribution v's children were drawn from): child c accepted iff u_acc[c] * q(d_c) < p(d_c),
+ * recursive residuals max(0, p - q) on rejection, final token by inverse CDF at u_fin[v]
+ * (uniforms in [0,1), one per node). Writes the accepted node path (path[0] = 0; *path_len
+ * entries) and the emitted tokens (accepted drafts, then one sampled token). Returns the number
+ * of emitted tokens. The CPU oracle's or_accept computes the identical result. */
+int kq_accept(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, const float* draft_logits,
+              float temperature, const float* u_acc, const float* u_fin, int32_t* path, int32_t* out,
+              int32_t* path_len);
+/* K/V compaction: the K/V rows of path[1..k] (increasing node ids, path[0] = 0) move from slots
+ * pos + path[j] to positions pos + j, so the accepted tokens sit at consecutive positions. */
+int kq_commit(kq_model* m, const int32_t* path, int k, int pos);
+
 /* ------------------------------------------------------------------ matrix hooks
  * kc_matvec / kc_dequant equivalents (kcpu4.c:337-341, q4kernels.h:12-36). */
 kq_qmat* kq_qmat_create(int type, int rows, int cols, int device);

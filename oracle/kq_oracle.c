@@ -414,15 +414,27 @@ static float or_silu(float x){ return x / (1.0f + expf(-x)); }
  * is this value for 256). */
 float or_attn_scale(int HD){ return (float)(1.0 / sqrt((double)HD)); }
 
+/* Tree verification (not in the reference, which verifies linear chains only): the K/V row of
+ * this token goes to cache slot `pos`, its rotary angle is that of position `rpos`, and it attends
+ * to every slot below `tree_base` plus the slots tree_base + j whose bit j is set in `mask`
+ * (its ancestors in the draft tree and itself). A plain decode step is pos == rpos with
+ * tree_base = pos + 1. */
+typedef struct { int rpos, tree_base; uint64_t mask[2]; } OTree;
+static int or_attended(const OTree* tr, int t){
+  if(t < tr->tree_base) return 1;
+  const int j = t - tr->tree_base;
+  return j < 128 && ((tr->mask[j >> 6] >> (j & 63)) & 1);
+}
+
 /* One attention block at position pos (kcpu4.c:218-285 without q/k norm and output gate). */
-static void or_attn(OModel* m, OLayer* L, int pos){
+static void or_attn(OModel* m, OLayer* L, int pos, const OTree* tr){
   const OCfg* c = &m->c;
   const int NH = c->NH, NKV = c->NKV, HD = c->HD, G = NH / NKV, n = pos + 1, rh = HD / 2;
   or_matvec(&L->q, m->xn, m->q);
   or_matvec(&L->k, m->xn, m->k);
   or_matvec(&L->v, m->xn, m->v);
-  const float* cs = m->cos_t + (size_t)pos * rh;
-  const float* sn = m->sin_t + (size_t)pos * rh;
+  const float* cs = m->cos_t + (size_t)tr->rpos * rh;
+  const float* sn = m->sin_t + (size_t)tr->rpos * rh;
   for(int h = 0; h < NH; h++) or_rope(m->q + (size_t)h * HD, cs, sn, m->qr + (size_t)h * HD, HD);
   for(int kv = 0; kv < NKV; kv++){
     or_rope(m->k + (size_t)kv * HD, cs, sn, m->kr + (size_t)kv * HD, HD);
@@ -449,10 +461,10 @@ static void or_attn(OModel* m, OLayer* L, int pos){
   for(int hh = 0; hh < NH; hh++){
     float* s = m->sc + (size_t)hh * c->ctx;
     float mx = -1e30f;
-    for(int t = 0; t < n; t++) mx = fmaxf(mx, s[t]);
+    for(int t = 0; t < n; t++) if(or_attended(tr, t)) mx = fmaxf(mx, s[t]);
     float tot = 0.f;
-    for(int t = 0; t < n; t++) tot += expf(s[t] - mx);
-    for(int t = 0; t < n; t++) s[t] = expf(s[t] - mx) / tot;
+    for(int t = 0; t < n; t++) if(or_attended(tr, t)) tot += expf(s[t] - mx);
+    for(int t = 0; t < n; t++) s[t] = or_attended(tr, t) ? expf(s[t] - mx) / tot : 0.f;
   }
   #pragma omp parallel for schedule(static)
   for(int u = 0; u < NH * (HD / 32); u++){
@@ -480,14 +492,14 @@ static void or_ffn(OModel* m, OLayer* L){
 
 /* One token (kcpu4.c:303-335 structure). head != 0: logits into m->logits and the greedy id
  * (strict > scan, first index wins) is returned; head == 0 returns -1 and leaves h = residual. */
-int or_step(OModel* m, int tok, int pos, int head){
+static int or_step_t(OModel* m, int tok, int pos, int head, const OTree* tr){
   const OCfg* c = &m->c;
-  if(tok < 0 || tok >= c->vocab || pos < 0 || pos >= c->ctx) return -3;
+  if(tok < 0 || tok >= c->vocab || pos < 0 || pos >= c->ctx || tr->rpos < 0 || tr->rpos >= c->ctx) return -3;
   or_dequant_row(&m->emb, tok, m->h);
   for(int l = 0; l < c->NL; l++){
     OLayer* L = m->L + l;
     or_rmsnorm(m->h, m->y, l > 0, L->attn_norm, m->xn, c->D, c->eps);
-    or_attn(m, L, pos);
+    or_attn(m, L, pos, tr);
     or_ffn(m, L);
   }
   if(!head){ for(int e = 0; e < c->D; e++) m->h[e] += m->y[e]; return -1; }
@@ -496,6 +508,63 @@ int or_step(OModel* m, int tok, int pos, int head){
   int bi = 0; float bv = m->logits[0];
   for(int i = 1; i < c->vocab; i++) if(m->logits[i] > bv){ bv = m->logits[i]; bi = i; }
   return bi;
+}
+
+int or_step(OModel* m, int tok, int pos, int head){
+  OTree tr = {pos, pos + 1, {0, 0}};
+  return or_step_t(m, tok, pos, head, &tr);
+}
+
+/* Depths of the nodes of a draft tree given by parent pointers (parents[0] = -1, 0 <= parents[i]
+ * < i); -1 if the tree is malformed. */
+int or_tree_depths(const int* parents, int n, int* depth){
+  if(n < 1 || n > 128 || parents[0] != -1) return -1;
+  depth[0] = 0;
+  for(int i = 1; i < n; i++){
+    if(parents[i] < 0 || parents[i] >= i) return -1;
+    depth[i] = depth[parents[i]] + 1;
+  }
+  return 0;
+}
+
+/* Verification pass over a draft tree of n nodes (node 0 is the last accepted token, at position
+ * pos): node i is run as one decode step with K/V slot pos + i, rotary position pos + depth(i),
+ * attending to the prefix [0, pos) and to its ancestors and itself. Logits of node i go to
+ * logits[i * vocab]; returns 0, or -3 on bad arguments. Node order and arithmetic are those of
+ * or_step, so a linear chain reproduces the greedy steps token for token. */
+int or_verify(OModel* m, const int* tokens, const int* parents, int n, int pos, float* logits, int* best){
+  int depth[128];
+  if(or_tree_depths(parents, n, depth) || pos < 0 || pos + n > m->c.ctx) return -3;
+  uint64_t anc[128][2];
+  for(int i = 0; i < n; i++){
+    anc[i][0] = anc[i][1] = 0;
+    if(i > 0){ anc[i][0] = anc[parents[i]][0]; anc[i][1] = anc[parents[i]][1]; }
+    anc[i][i >> 6] |= 1ull << (i & 63);
+  }
+  for(int i = 0; i < n; i++){
+    OTree tr = {pos + depth[i], pos, {anc[i][0], anc[i][1]}};
+    const int r = or_step_t(m, tokens[i], pos + i, 1, &tr);
+    if(r < 0) return r;
+    if(best) best[i] = r;
+    if(logits) memcpy(logits + (size_t)i * m->c.vocab, m->logits, (size_t)m->c.vocab * sizeof(float));
+  }
+  return 0;
+}
+
+/* KV compaction after acceptance: the accepted path root = path[0] = 0, path[1..k] (node ids)
+ * moves from slots pos + path[j] to positions pos + j, in increasing j (a node's id is at least
+ * its depth, so no source is overwritten before it is read). */
+int or_commit(OModel* m, const int* path, int k, int pos){
+  const OCfg* c = &m->c;
+  if(k < 0 || pos < 0) return -3;
+  for(int j = 1; j <= k; j++) if(path[j] < j || pos + path[j] >= c->ctx) return -3;
+  const size_t row = (size_t)c->NKV * c->HD;
+  for(int l = 0; l < c->NL; l++)
+    for(int j = 1; j <= k; j++){
+      memmove(m->L[l].Kc + (size_t)(pos + j) * row, m->L[l].Kc + (size_t)(pos + path[j]) * row, row * 2);
+      memmove(m->L[l].Vc + (size_t)(pos + j) * row, m->L[l].Vc + (size_t)(pos + path[j]) * row, row * 2);
+    }
+  return 0;
 }
 
 /* Accessors for ctypes callers. */
@@ -526,4 +595,143 @@ int or_get_threads(void){
 #else
   return 1;
 #endif
+}
+
+/* ---------------------------------------------------------------------------------------------
+ * Acceptance of a verified draft tree (speculative sampling), the deterministic rule the GPU
+ * kernel k_accept (csrc/kq_accept.cuh) follows bit for bit.
+ *
+ * The reference accepts a deterministic draft (q one-hot) along a linear chain with numpy's RNG
+ * (scripts/kindi_q4/kindi/spec.py:769-787, sampler spec.py:726-766, sampling.py:57-72); its
+ * rng.choice is not reproducible on a GPU. This restatement generalises to a draft distribution
+ * q per node and to trees, following speculative sampling (Leviathan et al. 2023; Chen et al.
+ * 2023) and its multi-draft form with recursive rejection (SpecInfer, Miao et al. 2024):
+ *   at node v with target p_v = softmax(z_v / T) and draft q_v = softmax(g_v) (the distribution
+ *   v's children were drawn from), children c in increasing id:
+ *     accept c  iff  u_acc[c] * q(d_c) < p(d_c)          (fp32)
+ *     accepted: emit d_c, continue at c with p_c, q_c
+ *     rejected: p <- max(0, p - q) / sum(max(0, p - q))  (back to p_v if that sum is 0)
+ *   no child accepted (or a leaf): emit the inverse-CDF sample of p at u_fin[v], stop.
+ *   T == 0 (greedy): accept c iff d_c is the argmax of z_v (lowest id on ties); emit the argmax
+ *   of the last node.
+ * Arithmetic (fp32, no contraction): e^t by kq_exp below; sums over the vocabulary are blocked:
+ * blocks of 1024 consecutive ids (zero padded), each summed by a balanced pairwise tree, the
+ * block sums added in block order; the inverse CDF walks the block sums in order, then the ids of
+ * the chosen block sequentially from that prefix.
+ * ------------------------------------------------------------------------------------------- */
+
+/* e^t for t <= 0 (0 below -87): Cody-Waite reduction t = k ln2 + r with ln2 split in a high part
+ * exact in fp32 and a low part, |r| <= ln2/2, then e^r by its Taylor series to degree 7 (Horner,
+ * fused multiply-adds), scaled by 2^k. Error about 1 ulp; what matters is that the GPU kernel
+ * computes the identical value. */
+float or_kq_exp(float t){
+  if(!(t >= -87.0f)) return 0.0f;
+  /* fp32 constants: 1/ln2, ln2 = HI + LO (HI has 12 significant bits, so k * HI is exact), 1/n! */
+  const float k = fmaf(t, 0x1.715476p+0f, 12582912.0f) - 12582912.0f;   /* round(t / ln2), 1.5 * 2^23 trick */
+  float r = fmaf(-k, 0x1.62e4p-1f, t);
+  r = fmaf(-k, 0x1.7f7d1cp-20f, r);
+  float p = 0x1.a01a02p-13f;            /* 1/5040 */
+  p = fmaf(p, r, 0x1.6c16c2p-10f);      /* 1/720 */
+  p = fmaf(p, r, 0x1.111112p-7f);       /* 1/120 */
+  p = fmaf(p, r, 0x1.555556p-5f);       /* 1/24 */
+  p = fmaf(p, r, 0x1.555556p-3f);       /* 1/6 */
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  union { float f; int32_t i; } sc;
+  sc.i = ((int32_t)k + 127) << 23;
+  return p * sc.f;
+}
+
+#define OR_ABLK 1024
+static float or_pairwise(const float* a, int n){
+  if(n == 1) return a[0];
+  return or_pairwise(a, n / 2) + or_pairwise(a + n / 2, n / 2);
+}
+/* Block sums into bs[] (ceil(V/1024) of them) and their in-order total. */
+static float or_blocked_sum(const float* w, int V, float* bs){
+  float buf[OR_ABLK];
+  const int nb = (V + OR_ABLK - 1) / OR_ABLK;
+  float tot = 0.0f;
+  for(int b = 0; b < nb; b++){
+    for(int i = 0; i < OR_ABLK; i++){ const int id = b * OR_ABLK + i; buf[i] = id < V ? w[id] : 0.0f; }
+    bs[b] = or_pairwise(buf, OR_ABLK);
+    tot = tot + bs[b];
+  }
+  return tot;
+}
+/* p = softmax(z * tau) with the rule above (tau = 1/T as the caller rounded it). */
+static void or_softmax(const float* z, int V, float tau, float* p, float* bs){
+  float mx = z[0];
+  for(int i = 1; i < V; i++) if(z[i] > mx) mx = z[i];
+  for(int i = 0; i < V; i++) p[i] = or_kq_exp((z[i] - mx) * tau);
+  const float S = or_blocked_sum(p, V, bs);
+  for(int i = 0; i < V; i++) p[i] = p[i] / S;
+}
+static int or_argmax(const float* z, int V){
+  int bi = 0;
+  for(int i = 1; i < V; i++) if(z[i] > z[bi]) bi = i;
+  return bi;
+}
+static int or_inverse_cdf(const float* w, int V, float u, float* bs){
+  const float W = or_blocked_sum(w, V, bs);
+  const float target = u * W;
+  const int nb = (V + OR_ABLK - 1) / OR_ABLK;
+  float prefix = 0.0f;
+  for(int b = 0; b < nb; b++){
+    if(prefix + bs[b] > target){
+      float run = prefix;
+      for(int i = b * OR_ABLK; i < V && i < (b + 1) * OR_ABLK; i++){
+        run = run + w[i];
+        if(run > target) return i;
+      }
+    }
+    prefix = prefix + bs[b];
+  }
+  for(int i = V - 1; i >= 0; i--) if(w[i] > 0.0f) return i;
+  return 0;
+}
+
+/* Tree acceptance. z: target logits [n][V]; g: draft logits [n][V] (row v: the distribution of
+ * v's children; unused for leaves and when tau == 0); tokens[c] the draft token of node c;
+ * u_acc[c], u_fin[v] uniforms in [0,1). tau = 0: greedy. Writes the accepted node path
+ * (path[0] = 0, then the accepted nodes) and the emitted tokens; returns the number of emitted
+ * tokens (accepted drafts + 1), or -3 on bad arguments. */
+int or_accept(const float* z, const float* g, const int* tokens, const int* parents, int n, int V, float tau,
+              const float* u_acc, const float* u_fin, int* path, int* out){
+  int depth[128];
+  if(or_tree_depths(parents, n, depth)) return -3;
+  float* p = (float*)malloc((size_t)V * sizeof(float));
+  float* q = (float*)malloc((size_t)V * sizeof(float));
+  float* bs = (float*)malloc((size_t)((V + OR_ABLK - 1) / OR_ABLK) * sizeof(float));
+  int v = 0, np = 0, no = 0;
+  path[np++] = 0;
+  for(;;){
+    const float* zv = z + (size_t)v * V;
+    int acc = -1;
+    if(tau == 0.0f){
+      const int best = or_argmax(zv, V);
+      for(int c = v + 1; c < n && acc < 0; c++) if(parents[c] == v && tokens[c] == best) acc = c;
+      if(acc < 0){ out[no++] = best; break; }
+    } else {
+      or_softmax(zv, V, tau, p, bs);
+      int first = 1;
+      for(int c = v + 1; c < n && acc < 0; c++){
+        if(parents[c] != v) continue;
+        if(first){ or_softmax(g + (size_t)v * V, V, 1.0f, q, bs); first = 0; }
+        const int d = tokens[c];
+        if(u_acc[c] * q[d] < p[d]){ acc = c; break; }
+        for(int i = 0; i < V; i++){ const float r = p[i] - q[i]; p[i] = r > 0.0f ? r : 0.0f; }
+        const float R = or_blocked_sum(p, V, bs);
+        if(R > 0.0f) for(int i = 0; i < V; i++) p[i] = p[i] / R;
+        else or_softmax(zv, V, tau, p, bs);   /* empty residual (p == q): back to p_v */
+      }
+      if(acc < 0){ out[no++] = or_inverse_cdf(p, V, u_fin[v], bs); break; }
+    }
+    out[no++] = tokens[acc];
+    path[np++] = acc;
+    v = acc;
+  }
+  free(p); free(q); free(bs);
+  return no;
 }

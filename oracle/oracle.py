@@ -83,6 +83,14 @@ def lib():
         L.or_rmsnorm.argtypes = [PF, PF, C.c_int, PF, PF, C.c_int, C.c_float]
         L.or_attn_scale.argtypes = [C.c_int]
         L.or_attn_scale.restype = C.c_float
+        L.or_verify.argtypes = [C.c_void_p, PI32, PI32, C.c_int, C.c_int, PF, PI32]
+        L.or_verify.restype = C.c_int
+        L.or_commit.argtypes = [C.c_void_p, PI32, C.c_int, C.c_int]
+        L.or_commit.restype = C.c_int
+        L.or_accept.argtypes = [PF, PF, PI32, PI32, C.c_int, C.c_int, C.c_float, PF, PF, PI32, PI32]
+        L.or_accept.restype = C.c_int
+        L.or_kq_exp.argtypes = [C.c_float]
+        L.or_kq_exp.restype = C.c_float
         L.or_set_threads.argtypes = [C.c_int]
         L.or_get_threads.restype = C.c_int
         assert L.or_sizeof_cfg() == C.sizeof(OCfg)
@@ -203,6 +211,22 @@ class Model(object):
         n = npos * self.cfg.NKV * self.cfg.HD
         return np.ctypeslib.as_array(self.L.or_model_vcache(self.h, layer), shape=(n,)).copy()
 
+    def verify(self, tokens, parents, pos):
+        """Draft-tree verification (or_verify): (argmax ids [n], logits [n][vocab])."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        par = np.ascontiguousarray(parents, np.int32)
+        n = len(t)
+        logits = np.empty((n, self.cfg.vocab), np.float32)
+        best = np.empty(n, np.int32)
+        if self.L.or_verify(self.h, ptr(t, PI32), ptr(par, PI32), n, int(pos), ptr(logits), ptr(best, PI32)):
+            raise ValueError("oracle: bad verify arguments")
+        return best, logits
+
+    def commit(self, path, pos):
+        p = np.ascontiguousarray(path, np.int32)
+        if self.L.or_commit(self.h, ptr(p, PI32), len(p) - 1, int(pos)):
+            raise ValueError("oracle: bad commit arguments")
+
     def generate(self, ids, n):
         """Greedy: kcpu4's Engine.generate order (cpu4.py:227-236)."""
         self.reset()
@@ -214,6 +238,26 @@ class Model(object):
             out.append(self.step(out[-1], pos))
             pos += 1
         return out
+
+
+def accept(z, g, tokens, parents, temperature, u_acc=None, u_fin=None):
+    """or_accept: (path, emitted tokens) for target logits z [n][V], draft logits g [n][V]
+    (ignored when temperature == 0) and uniforms u_acc / u_fin [n]."""
+    z = np.ascontiguousarray(z, np.float32)
+    n, V = z.shape
+    g = np.ascontiguousarray(g if g is not None else np.zeros_like(z), np.float32)
+    t = np.ascontiguousarray(tokens, np.int32)
+    par = np.ascontiguousarray(parents, np.int32)
+    ua = np.ascontiguousarray(u_acc if u_acc is not None else np.zeros(n), np.float32)
+    uf = np.ascontiguousarray(u_fin if u_fin is not None else np.zeros(n), np.float32)
+    tau = np.float32(1.0) / np.float32(temperature) if temperature > 0 else np.float32(0.0)
+    path = np.empty(n + 1, np.int32)
+    out = np.empty(n + 1, np.int32)
+    no = lib().or_accept(ptr(z), ptr(g), ptr(t, PI32), ptr(par, PI32), n, V, float(tau), ptr(ua), ptr(uf),
+                         ptr(path, PI32), ptr(out, PI32))
+    if no < 0:
+        raise ValueError("oracle: bad accept arguments")
+    return [int(v) for v in path[:no]], [int(v) for v in out[:no]]
 
 
 # ----------------------------------------------------------------------------- reference library

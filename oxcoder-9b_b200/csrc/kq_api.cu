@@ -11,6 +11,7 @@
 #include "kq_gemv.cuh"
 #include "kq_attn.cuh"
 #include "kq_decode.cuh"
+#include "kq_accept.cuh"
 
 #include <cuda_runtime.h>
 #include <cmath>
@@ -433,6 +434,14 @@ struct kq_model {
   int* dec_bar = nullptr;
   DecodeParams dec{};
   size_t dec_smem = 0;
+  // speculative verification (allocated on first use)
+  float* vlogits = nullptr;         // [KQ_MAX_TREE][vocab] logits of the last verify pass
+  int vn = 0;                       // nodes of the last verify pass
+  DecodeState* vstates = nullptr;   // pinned, one per node
+  float *ap = nullptr, *aq = nullptr, *ag = nullptr;   // acceptance scratch, draft logits
+  int *atok = nullptr, *apar = nullptr, *apath = nullptr, *aout = nullptr, *acnt = nullptr;
+  float *auacc = nullptr, *aufin = nullptr;
+  __half** caches = nullptr;        // [2 * n_layers] K/V cache pointers (compaction)
   std::vector<void*> allocs;
 };
 
@@ -478,6 +487,7 @@ static void model_release(kq_model* m) {
     if (a) { cudaFree(a->buf); delete a; }
   for (void* p : m->allocs) cudaFree(p);
   if (m->st_host) cudaFreeHost(m->st_host);
+  if (m->vstates) cudaFreeHost(m->vstates);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
 }
@@ -992,16 +1002,23 @@ static int check_dev_err(kq_model* m) {
   return KQ_OK;
 }
 
+// A plain decode step's state: slot = rotary position = pos, every slot up to pos attended.
+static void plain_state(DecodeState* st, int tok, int pos) {
+  std::memset(st, 0, sizeof(*st));
+  st->tok = tok;
+  st->pos = pos;
+  st->next_tok = -1;
+  st->rpos = pos;
+  st->tree_base = pos + 1;
+}
+
 static int run_one(kq_model* m, int tok, int pos, bool head) {
   int rc = model_check(m);
   if (rc) return rc;
   if (tok < 0 || tok >= m->c.vocab || pos < 0) return set_err(KQ_ERR_ARG, "Invalid token or position");
   if (pos >= m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "position is past the context");
   if ((rc = ensure_graphs(m))) return rc;
-  m->st_host->tok = tok;
-  m->st_host->pos = pos;
-  m->st_host->next_tok = -1;
-  m->st_host->steps = 0;
+  plain_state(m->st_host, tok, pos);
   CU(cudaMemcpyAsync(m->st, m->st_host, sizeof(DecodeState), cudaMemcpyHostToDevice, m->stream));
   if (m->persist) {
     if ((rc = launch_persistent(m, head))) return rc;
@@ -1069,7 +1086,7 @@ extern "C" int kq_decode_loop(kq_model* m, int tok, int pos, int n, int32_t* out
   if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "decode loop runs past the context");
   if ((rc = ensure_graphs(m))) return rc;
   if (n > m->out_cap) return set_err(KQ_ERR_ARG, "decode loop longer than the context");
-  m->st_host->tok = tok; m->st_host->pos = pos; m->st_host->next_tok = -1; m->st_host->steps = 0;
+  plain_state(m->st_host, tok, pos);
   CU(cudaMemcpyAsync(m->st, m->st_host, sizeof(DecodeState), cudaMemcpyHostToDevice, m->stream));
   // each replay embeds st->tok at st->pos; the head's last CTA stores the argmax in out_ids and
   // advances (tok, pos) on the device, so no host round trip separates the steps
@@ -1091,7 +1108,7 @@ extern "C" int kq_time_decode(kq_model* m, int tok, int pos, int n, float* ms_ou
   if (n < 1 || !ms_out || tok < 0 || tok >= m->c.vocab || pos < 0) return set_err(KQ_ERR_ARG, "bad timing arguments");
   if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "timed decode runs past the context");
   if ((rc = ensure_graphs(m))) return rc;
-  m->st_host->tok = tok; m->st_host->pos = pos; m->st_host->next_tok = -1; m->st_host->steps = 0;
+  plain_state(m->st_host, tok, pos);
   CU(cudaMemcpyAsync(m->st, m->st_host, sizeof(DecodeState), cudaMemcpyHostToDevice, m->stream));
   cudaEvent_t e0, e1;
   CU(cudaEventCreate(&e0));
@@ -1113,6 +1130,142 @@ extern "C" int kq_time_decode(kq_model* m, int tok, int pos, int n, float* ms_ou
   cudaEventDestroy(e1);
   *ms_out = ms;
   return check_dev_err(m);
+}
+
+// ------------------------------------------------------------------------------ speculative verification
+// Node depths and ancestor masks of a draft tree (parents[0] = -1, 0 <= parents[i] < i).
+static int tree_check(const int32_t* parents, int n, int* depth, unsigned long long (*anc)[2]) {
+  if (!parents || n < 1 || n > KQ_MAX_TREE || parents[0] != -1) return set_err(KQ_ERR_ARG, "bad draft tree");
+  for (int i = 0; i < n; ++i) {
+    if (i > 0 && (parents[i] < 0 || parents[i] >= i)) return set_err(KQ_ERR_ARG, "bad draft tree: parents[i] must lie in [0, i)");
+    depth[i] = i ? depth[parents[i]] + 1 : 0;
+    anc[i][0] = i ? anc[parents[i]][0] : 0;
+    anc[i][1] = i ? anc[parents[i]][1] : 0;
+    anc[i][i >> 6] |= 1ull << (i & 63);
+  }
+  return KQ_OK;
+}
+
+static int verify_buffers(kq_model* m) {
+  if (m->vlogits) return KQ_OK;
+  bool ok = true;
+  const size_t V = (size_t)m->c.vocab;
+  m->vlogits = dalloc<float>(m, KQ_MAX_TREE * V, ok);
+  m->ap = dalloc<float>(m, V, ok);
+  m->aq = dalloc<float>(m, V, ok);
+  m->ag = dalloc<float>(m, KQ_MAX_TREE * V, ok);
+  m->atok = dalloc<int>(m, KQ_MAX_TREE + 1, ok);
+  m->apar = dalloc<int>(m, KQ_MAX_TREE + 1, ok);
+  m->apath = dalloc<int>(m, KQ_MAX_TREE + 1, ok);
+  m->aout = dalloc<int>(m, KQ_MAX_TREE + 1, ok);
+  m->acnt = dalloc<int>(m, 2, ok);
+  m->auacc = dalloc<float>(m, KQ_MAX_TREE, ok);
+  m->aufin = dalloc<float>(m, KQ_MAX_TREE, ok);
+  m->caches = dalloc<__half*>(m, 2 * (size_t)m->c.n_layers, ok);
+  if (ok && cudaMallocHost(&m->vstates, KQ_MAX_TREE * sizeof(DecodeState)) != cudaSuccess) ok = false;
+  if (!ok) return set_err(KQ_ERR_MEMORY, "verify buffers");
+  std::vector<__half*> cp(2 * (size_t)m->c.n_layers);
+  for (int l = 0; l < m->c.n_layers; ++l) { cp[2 * l] = m->L[l].kc; cp[2 * l + 1] = m->L[l].vc; }
+  CU(cudaMemcpy(m->caches, cp.data(), cp.size() * sizeof(__half*), cudaMemcpyHostToDevice));
+  return KQ_OK;
+}
+
+extern "C" int kq_verify(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, int pos, float* logits,
+                         int32_t* best) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  int depth[KQ_MAX_TREE];
+  unsigned long long anc[KQ_MAX_TREE][2];
+  if ((rc = tree_check(parents, n, depth, anc))) return rc;
+  if (!tokens || pos < 0) return set_err(KQ_ERR_ARG, "bad verify arguments");
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= m->c.vocab) return set_err(KQ_ERR_ARG, "Invalid token in the draft tree");
+  if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "draft tree runs past the context");
+  if ((rc = ensure_graphs(m)) || (rc = verify_buffers(m))) return rc;
+  const size_t V = (size_t)m->c.vocab;
+  for (int i = 0; i < n; ++i) {
+    DecodeState& st = m->vstates[i];
+    std::memset(&st, 0, sizeof(st));
+    st.tok = tokens[i];
+    st.pos = pos + i;            // K/V slot
+    st.next_tok = -1;
+    st.steps = i;                // the head's argmax lands in out_ids[i]
+    st.rpos = pos + depth[i];    // rotary position
+    st.tree_base = pos;
+    st.mask[0] = anc[i][0];
+    st.mask[1] = anc[i][1];
+    CU(cudaMemcpyAsync(m->st, &st, sizeof(DecodeState), cudaMemcpyHostToDevice, m->stream));
+    if (m->persist) {
+      if ((rc = launch_persistent(m, true))) return rc;
+    } else {
+      CU(cudaGraphLaunch(m->g_step, m->stream));
+    }
+    CU(cudaMemcpyAsync(m->vlogits + i * V, m->logits, V * sizeof(float), cudaMemcpyDeviceToDevice, m->stream));
+  }
+  if (best) CU(cudaMemcpyAsync(best, m->out_ids, (size_t)n * sizeof(int32_t), cudaMemcpyDeviceToHost, m->stream));
+  if (logits) CU(cudaMemcpyAsync(logits, m->vlogits, (size_t)n * V * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
+  CU(cudaStreamSynchronize(m->stream));
+  m->vn = n;
+  return check_dev_err(m);
+}
+
+extern "C" int kq_accept(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, const float* draft_logits,
+                         float temperature, const float* u_acc, const float* u_fin, int32_t* path, int32_t* out,
+                         int32_t* path_len) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  int depth[KQ_MAX_TREE];
+  unsigned long long anc[KQ_MAX_TREE][2];
+  if ((rc = tree_check(parents, n, depth, anc))) return rc;
+  if (!tokens || !path || !out || !(temperature >= 0.0f)) return set_err(KQ_ERR_ARG, "bad accept arguments");
+  if (temperature > 0.0f && (!draft_logits || !u_acc || !u_fin)) return set_err(KQ_ERR_ARG, "stochastic acceptance needs draft logits and uniforms");
+  if (!m->vlogits || m->vn != n) return set_err(KQ_ERR_ARG, "kq_accept needs the logits of a kq_verify over the same tree");
+  if (m->c.vocab > ACC_BLK * ACC_MAX_BLOCKS) return set_err(KQ_ERR_ARG, "vocabulary too large for the acceptance kernel");
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= m->c.vocab) return set_err(KQ_ERR_ARG, "Invalid token in the draft tree");
+  const size_t V = (size_t)m->c.vocab;
+  cudaStream_t s = m->stream;
+  CU(cudaMemcpyAsync(m->atok, tokens, n * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->apar, parents, n * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  AcceptParams A;
+  std::memset(&A, 0, sizeof(A));
+  A.tau = temperature > 0.0f ? 1.0f / temperature : 0.0f;
+  if (A.tau > 0.0f) {
+    CU(cudaMemcpyAsync(m->ag, draft_logits, n * V * sizeof(float), cudaMemcpyHostToDevice, s));
+    CU(cudaMemcpyAsync(m->auacc, u_acc, n * sizeof(float), cudaMemcpyHostToDevice, s));
+    CU(cudaMemcpyAsync(m->aufin, u_fin, n * sizeof(float), cudaMemcpyHostToDevice, s));
+  }
+  A.z = m->vlogits; A.g = m->ag; A.tokens = m->atok; A.parents = m->apar; A.u_acc = m->auacc; A.u_fin = m->aufin;
+  A.n = n; A.V = (int)V; A.p = m->ap; A.q = m->aq; A.path = m->apath; A.out = m->aout; A.count = m->acnt;
+  k_accept<<<1, ACC_THREADS, 0, s>>>(A);
+  CU(cudaGetLastError());
+  int cnt[2] = {0, 0};
+  CU(cudaMemcpyAsync(cnt, m->acnt, sizeof(cnt), cudaMemcpyDeviceToHost, s));
+  CU(cudaStreamSynchronize(s));
+  if (cnt[0] < 1 || cnt[0] > n + 1 || cnt[1] < 1 || cnt[1] > n) return set_err(KQ_ERR_BACKEND, "acceptance kernel failed");
+  CU(cudaMemcpy(out, m->aout, cnt[0] * sizeof(int32_t), cudaMemcpyDeviceToHost));
+  CU(cudaMemcpy(path, m->apath, cnt[1] * sizeof(int32_t), cudaMemcpyDeviceToHost));
+  if (path_len) *path_len = cnt[1];
+  return cnt[0];
+}
+
+extern "C" int kq_commit(kq_model* m, const int32_t* path, int k, int pos) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (!path || k < 0 || k >= KQ_MAX_TREE || pos < 0 || path[0] != 0) return set_err(KQ_ERR_ARG, "bad commit arguments");
+  for (int j = 1; j <= k; ++j)
+    if (path[j] <= path[j - 1] || path[j] >= KQ_MAX_TREE) return set_err(KQ_ERR_ARG, "bad commit path (node ids must increase)");
+  if (pos + (k ? path[k] : 0) >= m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "commit path runs past the context");
+  if (k == 0) return KQ_OK;
+  if ((rc = verify_buffers(m))) return rc;
+  CU(cudaMemcpyAsync(m->apath, path, (size_t)(k + 1) * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
+  CommitParams C;
+  C.caches = m->caches; C.path = m->apath; C.k = k; C.pos = pos;
+  C.n_kv = m->c.n_kv_heads; C.ctx = m->c.ctx; C.hd = m->c.head_dim;
+  k_commit<<<2 * m->c.n_layers, 256, 0, m->stream>>>(C);
+  CU(cudaGetLastError());
+  CU(cudaStreamSynchronize(m->stream));
+  return KQ_OK;
 }
 
 #ifdef KQ_TRACE

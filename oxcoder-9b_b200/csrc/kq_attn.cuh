@@ -71,6 +71,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) k_attn_split(const __grid_cons
   int pos = P.st->pos;
   const bool pos_ok = pos >= 0 && pos < P.ctx;
   if (!pos_ok) pos = pos < 0 ? 0 : P.ctx - 1;
+  const int tbase = P.st->tree_base;
+  const unsigned long long tm0 = P.st->mask[0], tm1 = P.st->mask[1];
   const int n = pos + 1;
   const int per = ((n + S.nsplit - 1) / S.nsplit + 15) & ~15;
   const int t_begin = min(n, sp * per), t_end = min(n, t_begin + per);
@@ -137,7 +139,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) k_attn_split(const __grid_cons
         for (int i = 0; i < 8; ++i) a = __fmaf_rn(kf[i], qv[gh][i], a);
 #pragma unroll
         for (int off = 8; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
-        if (tl < cnt && hl == 0) s_sc[gh][tl] = __fmul_rn(a, P.scale);
+        if (tl < cnt && hl == 0)
+          s_sc[gh][tl] = slot_attended(c0 + tl, tbase, tm0, tm1) ? __fmul_rn(a, P.scale) : -INFINITY;
       }
     }
     __syncthreads();
@@ -314,6 +317,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) k_attn_cluster(const __grid_co
   int pos = P.st->pos;
   const bool pos_ok = pos >= 0 && pos < P.ctx;
   if (!pos_ok) pos = pos < 0 ? 0 : P.ctx - 1;
+  const int tbase = P.st->tree_base;
+  const unsigned long long tm0 = P.st->mask[0], tm1 = P.st->mask[1];
   const int n = pos + 1;
   const int per = (n + CL - 1) / CL;
   const int t_begin = min(n, rank * per), t_end = min(n, t_begin + per);
@@ -367,7 +372,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) k_attn_cluster(const __grid_co
         for (int i = 0; i < 8; ++i) a = __fmaf_rn(kf[i], qv[gh][i], a);
 #pragma unroll
         for (int off = 8; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
-        if (tl < cnt && hl == 0) s_sc[gh][tl] = __fmul_rn(a, P.scale);
+        if (tl < cnt && hl == 0)
+          s_sc[gh][tl] = slot_attended(c0 + tl, tbase, tm0, tm1) ? __fmul_rn(a, P.scale) : -INFINITY;
       }
     }
     __syncthreads();

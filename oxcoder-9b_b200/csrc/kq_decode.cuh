@@ -243,6 +243,8 @@ __device__ void dec_attn(const AttnSplitParams& S, float* wk, const DecodeParams
   float* s_f = wk + AS::f;
   const __half* kglob = P.kc + ((size_t)itm.kv * P.ctx) * HD;
   const __half* vglob = P.vc + ((size_t)itm.kv * P.ctx) * HD;
+  const int tbase = P.st->tree_base;
+  const unsigned long long tm0 = P.st->mask[0], tm1 = P.st->mask[1];
   float qv[G][8];
 #pragma unroll
   for (int gh = 0; gh < G; ++gh) {
@@ -285,7 +287,8 @@ __device__ void dec_attn(const AttnSplitParams& S, float* wk, const DecodeParams
         for (int i = 0; i < 8; ++i) a = __fmaf_rn(kf[i], qv[gh][i], a);
 #pragma unroll
         for (int off = 8; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
-        if (tl < cnt && hl == 0) s_sc[gh * ATT_P + tl] = __fmul_rn(a, P.scale);
+        if (tl < cnt && hl == 0)
+          s_sc[gh * ATT_P + tl] = slot_attended(t, tbase, tm0, tm1) ? __fmul_rn(a, P.scale) : -INFINITY;
       }
     }
     named_bar(DEC_BAR_ATTN, ATT_THREADS);
@@ -423,7 +426,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + D.bars_off);
   uint64_t* empty = full + DEC_NB;
   uint64_t* cbar = empty + DEC_NB;
-  __shared__ int s_pos, s_fail;
+  __shared__ int s_pos, s_rpos, s_fail;
   __shared__ RingBook book;
   const int tid = threadIdx.x;
   if (tid == 0) {
@@ -432,6 +435,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant
     fence_mbar_init();
     for (int q = 0; q < DEC_NDESC; ++q) fetch_desc(D, cache, cbar, q);
     s_pos = D.st->pos;
+    s_rpos = D.st->rpos;
     s_fail = 0;
   }
   __syncthreads();
@@ -484,7 +488,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant
       cta_stage_range(P, n0, n1);
       if (tid < nthr_c) {
         const GemvSmem L = gemv_smem_layout(0, 0, P.LPR, P.NRG * P.nlanes, DEC_RPG, nthr_c);
-        gemv_load_rope_at(P, work, L, (pos >= 0 && pos < P.ctx) ? pos : 0);
+        gemv_load_rope_at(P, work, L, (s_rpos >= 0 && s_rpos < P.ctx) ? s_rpos : 0);
         // two items per thread at a time keeps the prologue's registers within the kernel's
         // budget; a norm needs every item at once and is limited to two (the host checks). One
         // call site: two inlined copies of the prologue cost far more registers than one.

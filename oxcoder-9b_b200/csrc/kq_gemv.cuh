@@ -44,10 +44,21 @@ constexpr int KQ_MAX_HALF_HD = 128;        // rotary half width held in shared m
 
 struct DecodeState {   // device-resident per-step state
   int tok;        // token processed by this step
-  int pos;        // its position
+  int pos;        // its K/V slot (its position, for a plain decode step)
   int next_tok;   // argmax written by the output head
   int steps;      // steps completed by the device-resident loop
+  int rpos;       // position of its rotary angle (pos, except for draft-tree nodes)
+  int tree_base;  // slots below tree_base are all attended; slot tree_base + j only if bit j of
+  int pad;        // mask is set (a draft tree's ancestors and the node itself); pos + 1 when
+  unsigned long long mask[2];   // there is no tree
 };
+
+// Attention visibility of cache slot t for the step described by (tree_base, mask).
+__device__ __forceinline__ bool slot_attended(int t, int tree_base, unsigned long long m0, unsigned long long m1) {
+  if (t < tree_base) return true;
+  const int j = t - tree_base;
+  return j < 128 && (((j < 64 ? m0 : m1) >> (j & 63)) & 1ull);
+}
 
 struct Seg {
   QView w;
@@ -487,13 +498,16 @@ __device__ __forceinline__ void gemv_thread_init(const GemvParams& P, uint8_t* s
   T.bi = 0x7fffffff;
 }
 
-// The rotary row of the step's position into shared memory; the prologue's barriers publish it.
+// The rotary row of the step's rotary position into shared memory; the prologue's barriers
+// publish it.
 __device__ __forceinline__ void gemv_load_rope(const GemvParams& P, uint8_t* smem, const GemvSmem& L, const GemvThread& T) {
   const int tid = threadIdx.x;
   float* rc = reinterpret_cast<float*>(smem + L.rope);
   if (P.cos_t && tid < (P.hd >> 1)) {
-    rc[tid] = __ldcg(P.cos_t + (size_t)T.pos * (P.hd >> 1) + tid);
-    rc[KQ_MAX_HALF_HD + tid] = __ldcg(P.sin_t + (size_t)T.pos * (P.hd >> 1) + tid);
+    int rp = P.st ? P.st->rpos : 0;
+    if (rp < 0 || rp >= P.ctx) rp = 0;   // the host validates
+    rc[tid] = __ldcg(P.cos_t + (size_t)rp * (P.hd >> 1) + tid);
+    rc[KQ_MAX_HALF_HD + tid] = __ldcg(P.sin_t + (size_t)rp * (P.hd >> 1) + tid);
   }
 }
 
@@ -715,6 +729,8 @@ __device__ __forceinline__ void gemv_argmax_tail(const GemvParams& P, uint8_t* s
       st->steps += 1;
       st->tok = i1;
       st->pos += 1;
+      st->rpos = st->pos;          // the next step is a plain decode step
+      st->tree_base = st->pos + 1;
       *P.ticket = 0;
     }
   }

@@ -82,6 +82,9 @@ SIGNATURES = {
     "kq_time_matvec": (C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.c_int, PF]),
     "kq_qmat_bytes": (C.c_size_t, [C.c_void_p]),
     "kq_qmat_argmax_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "kq_verify": (C.c_int, [C.c_void_p, PI32, PI32, C.c_int, C.c_int, PF, PI32]),
+    "kq_accept": (C.c_int, [C.c_void_p, PI32, PI32, C.c_int, PF, C.c_float, PF, PF, PI32, PI32, PI32]),
+    "kq_commit": (C.c_int, [C.c_void_p, PI32, C.c_int, C.c_int]),
 }
 
 _lib = None
@@ -287,6 +290,42 @@ class Engine(object):
         out = np.empty(n, np.int32)
         check(lib().kq_decode_loop(self.h, int(tok), int(pos), int(n), _ptr(out, PI32)))
         return [int(t) for t in out]
+
+    # ---- speculative verification (kq_verify / kq_accept / kq_commit)
+    def verify(self, tokens, parents, pos, want_logits=True):
+        """Runs a draft tree (node 0 = last accepted token at `pos`); (argmax ids, logits or None)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        par = np.ascontiguousarray(parents, np.int32)
+        if t.shape != par.shape:
+            raise ValueError("tokens and parents must have the same length")
+        n = len(t)
+        best = np.empty(n, np.int32)
+        logits = np.empty((n, self.vocab), np.float32) if want_logits else None
+        check(lib().kq_verify(self.h, _ptr(t, PI32), _ptr(par, PI32), n, int(pos),
+                              _ptr(logits) if logits is not None else None, _ptr(best, PI32)))
+        return best, logits
+
+    def accept(self, tokens, parents, draft_logits=None, temperature=0.0, u_acc=None, u_fin=None):
+        """On-device acceptance over the last verify pass: (accepted node path, emitted tokens)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        par = np.ascontiguousarray(parents, np.int32)
+        n = len(t)
+        g = _f32(draft_logits) if draft_logits is not None else None
+        ua = _f32(u_acc) if u_acc is not None else None
+        uf = _f32(u_fin) if u_fin is not None else None
+        path = np.empty(n + 1, np.int32)
+        out = np.empty(n + 1, np.int32)
+        plen = C.c_int32()
+        no = check(lib().kq_accept(self.h, _ptr(t, PI32), _ptr(par, PI32), n,
+                                   _ptr(g) if g is not None else None, float(temperature),
+                                   _ptr(ua) if ua is not None else None, _ptr(uf) if uf is not None else None,
+                                   _ptr(path, PI32), _ptr(out, PI32), C.byref(plen)))
+        return [int(v) for v in path[:plen.value]], [int(v) for v in out[:no]]
+
+    def commit(self, path, pos):
+        """K/V compaction of an accepted path (path[0] = 0)."""
+        p = np.ascontiguousarray(path, np.int32)
+        check(lib().kq_commit(self.h, _ptr(p, PI32), len(p) - 1, int(pos)))
 
     def time_decode(self, tok, pos, n):
         ms = C.c_float()

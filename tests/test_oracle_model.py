@@ -109,3 +109,51 @@ def test_bad_token_rejected(oracle):
         m.step(TINY["vocab"], 0)
     with pytest.raises(ValueError):
         m.step(0, TINY["ctx"])
+
+
+def test_oracle_exp_accuracy(oracle):
+    """kq_exp (the acceptance rule's e^t) is within 2 ulp of e^t on [-87, 0] and 0 below."""
+    import ctypes as C
+    L = oracle.lib()
+    ts = np.linspace(-87.0, 0.0, 4001).astype(np.float32)
+    got = np.array([L.or_kq_exp(float(t)) for t in ts], np.float64)
+    ref = np.exp(ts.astype(np.float64))
+    assert np.max(np.abs(got - ref) / ref) < 2 * 2.0 ** -24
+    assert L.or_kq_exp(-87.5) == 0.0 and L.or_kq_exp(-np.inf) == 0.0
+
+
+def test_oracle_accept_rules(oracle):
+    """Greedy and stochastic acceptance on small hand-made trees."""
+    V = 2048
+    rng = np.random.default_rng(3)
+    z = rng.normal(0, 3, (4, V)).astype(np.float32)
+    parents = [-1, 0, 0, 1]
+    best0, best1 = int(np.argmax(z[0])), int(np.argmax(z[1]))
+    # greedy: the second child of the root matches, then node 3 does not
+    toks = [7, (best0 + 1) % V, best0, (int(np.argmax(z[2])) + 1) % V]
+    path, out = oracle.accept(z, None, toks, parents, 0.0)
+    assert path == [0, 2] and out == [best0, int(np.argmax(z[2]))]
+    # greedy chain through node 1 and node 3
+    toks = [7, best0, 5, best1]
+    path, out = oracle.accept(z, None, toks, parents, 0.0)
+    assert path == [0, 1, 3] and out == [best0, best1, int(np.argmax(z[3]))]
+    # stochastic with q == p at temperature 1: u < 1 accepts every draft
+    path, out = oracle.accept(z, z, [7, 11, 13, 17], parents, 1.0, np.full(4, 0.999, np.float32),
+                              np.zeros(4, np.float32))
+    assert path == [0, 1, 3]
+    # stochastic with u = 1: nothing is accepted; the root's sample is a valid token
+    path, out = oracle.accept(z, z, [7, 11, 13, 17], parents, 1.0, np.ones(4, np.float32),
+                              np.full(4, 0.5, np.float32))
+    assert path == [0] and len(out) == 1 and 0 <= out[0] < V
+
+
+def test_oracle_chain_verify_equals_steps(oracle):
+    t = dict(D=512, NL=1, NH=4, NKV=1, HD=128, NFF=1024, vocab=2048, ctx=64)
+    m = oracle.Model(seed=0, **t)
+    m.fill_kv(10, 1)
+    chain = [3]
+    for i in range(4):
+        chain.append(m.step(chain[-1], 10 + i))
+    m.fill_kv(10, 1)
+    best, _ = m.verify(chain, [-1, 0, 1, 2, 3], 10)
+    assert list(best[:-1]) == chain[1:]
