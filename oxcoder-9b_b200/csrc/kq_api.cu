@@ -12,6 +12,7 @@
 #include "kq_attn.cuh"
 #include "kq_decode.cuh"
 #include "kq_accept.cuh"
+#include "kq_batch.cuh"
 
 #include <cuda_runtime.h>
 #include <cmath>
@@ -442,6 +443,13 @@ struct kq_model {
   int *atok = nullptr, *apar = nullptr, *apath = nullptr, *aout = nullptr, *acnt = nullptr;
   float *auacc = nullptr, *aufin = nullptr;
   __half** caches = nullptr;        // [2 * n_layers] K/V cache pointers (compaction)
+  // batched verification pass (up to MM_MAXM tokens at once)
+  float *bh = nullptr, *by = nullptr, *bq = nullptr, *bpart = nullptr;
+  float *bX = nullptr, *batt = nullptr, *bm = nullptr;
+  int *btok = nullptr, *bslot = nullptr, *brpos = nullptr, *bticket = nullptr;
+  unsigned long long* bmask = nullptr;
+  int b_nsplit = 0;
+  bool verify_seq = false;          // node-by-node decode steps instead of the batched pass
   std::vector<void*> allocs;
 };
 
@@ -569,6 +577,7 @@ extern "C" kq_model* kq_model_create(const kq_config* cfg, int device) {
     m->attn_cl = attn_cluster_size(c.n_heads / c.n_kv_heads, c.n_kv_heads);
     m->attn_mode = std::getenv("KQ_ATTN") && std::atoi(std::getenv("KQ_ATTN")) == 1 ? 1 : 0;
     m->persist = std::getenv("KQ_PERSIST") && std::atoi(std::getenv("KQ_PERSIST")) == 1;   // opt-in for now
+    m->verify_seq = std::getenv("KQ_VERIFY_SEQ") && std::atoi(std::getenv("KQ_VERIFY_SEQ")) == 1;
     m->attn_nsplit = std::min(ATT_SPLITS_MAX, std::max(1, m->nsm / c.n_kv_heads));
     m->apart = dalloc<float>(m, (size_t)c.n_kv_heads * m->attn_nsplit * (c.n_heads / c.n_kv_heads) * c.head_dim, ok);
     m->apart_ml = dalloc<float>(m, (size_t)c.n_kv_heads * m->attn_nsplit * (c.n_heads / c.n_kv_heads) * 2, ok);
@@ -1170,6 +1179,148 @@ static int verify_buffers(kq_model* m) {
   return KQ_OK;
 }
 
+static int batch_buffers(kq_model* m) {
+  if (m->bh) return KQ_OK;
+  const kq_config& c = m->c;
+  const size_t MM = MM_MAXM, QD = (size_t)c.n_heads * c.head_dim;
+  bool ok = true;
+  m->bh = dalloc<float>(m, MM * c.dim, ok);
+  m->by = dalloc<float>(m, MM * c.dim, ok);
+  m->bq = dalloc<float>(m, MM * QD, ok);
+  m->bX = dalloc<float>(m, MM * c.dim, ok);
+  m->batt = dalloc<float>(m, MM * QD, ok);
+  m->bm = dalloc<float>(m, MM * c.ffn, ok);
+  m->btok = dalloc<int>(m, MM, ok);
+  m->bslot = dalloc<int>(m, MM, ok);
+  m->brpos = dalloc<int>(m, MM, ok);
+  m->bmask = dalloc<unsigned long long>(m, 2 * MM, ok);
+  const int G = c.n_heads / c.n_kv_heads, tokblocks = (MM_MAXM + BA_TOK - 1) / BA_TOK;
+  m->b_nsplit = std::max(1, std::min(32, 2 * m->nsm / (c.n_kv_heads * tokblocks)));
+  m->bpart = dalloc<float>(m, (size_t)c.n_kv_heads * tokblocks * m->b_nsplit * BA_TOK * G * (128 + 2), ok);
+  m->bticket = dalloc<int>(m, (size_t)c.n_kv_heads * tokblocks, ok);
+  if (!ok) return set_err(KQ_ERR_MEMORY, "batched verify buffers");
+  CU(cudaFuncSetAttribute(k_mm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MM_SMEM));
+  const size_t sm = battn_smem(G);
+  cudaError_t e = G == 1 ? cudaFuncSetAttribute(k_battn<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
+                : G == 2 ? cudaFuncSetAttribute(k_battn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
+                : G == 4 ? cudaFuncSetAttribute(k_battn<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
+                         : cudaFuncSetAttribute(k_battn<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  if (e != cudaSuccess) return set_err(KQ_ERR_BACKEND, std::string("batched attention setup: ") + cudaGetErrorString(e));
+  return KQ_OK;
+}
+
+static bool batch_supported(const kq_model* m) {
+  const kq_config& c = m->c;
+  const int rows[] = {c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim, 2 * c.ffn, c.dim, c.vocab};
+  for (int r : rows)
+    if (r % 16) return false;
+  return true;
+}
+
+static int launch_mm(kq_model* m, const SegSpec* ss, int nseg, const float* X, int out_ld, const BatchParams& B) {
+  MMParams P;
+  std::memset(&P, 0, sizeof(P));
+  int rows = 0;
+  for (int i = 0; i < nseg; ++i) {
+    P.seg[i].w = ss[i].m->view();
+    P.seg[i].epi = ss[i].epi;
+    P.seg[i].out_f = ss[i].out_f;
+    P.seg[i].out_h = ss[i].out_h;
+    rows += ss[i].m->R;
+  }
+  P.nseg = nseg;
+  P.C = ss[0].m->C;
+  P.G = P.C / 256;
+  P.X = X;
+  P.B = B;
+  P.out_ld = out_ld;
+  P.cos_t = m->cos_t;
+  P.sin_t = m->sin_t;
+  P.hd = m->c.head_dim;
+  P.ctx = m->c.ctx;
+  const int per_cta = 16 * MM_WARPS;
+  k_mm<<<(rows + per_cta - 1) / per_cta, MM_WARPS * 32, MM_SMEM, m->stream>>>(P);
+  CU(cudaGetLastError());
+  return KQ_OK;
+}
+
+static int launch_bnorm(kq_model* m, int M, bool embed, const float* gamma, bool add) {
+  BNormParams P;
+  std::memset(&P, 0, sizeof(P));
+  P.M = M; P.D = m->c.dim; P.tok = m->btok;
+  if (embed) P.emb = m->emb->view();
+  P.h = m->bh; P.y = add ? m->by : nullptr; P.gamma = gamma; P.eps = m->c.eps; P.X = m->bX;
+  P.vocab = m->c.vocab; P.err = m->err;
+  k_bnorm<<<M, 256, 0, m->stream>>>(P);
+  CU(cudaGetLastError());
+  return KQ_OK;
+}
+
+static int launch_battn(kq_model* m, int layer, int M, int npos, const BatchParams& B) {
+  const kq_config& c = m->c;
+  const int G = c.n_heads / c.n_kv_heads, tokblocks = (M + BA_TOK - 1) / BA_TOK;
+  BAttnParams P;
+  P.q = m->bq; P.kc = m->L[layer].kc; P.vc = m->L[layer].vc; P.out = m->batt; P.B = B;
+  P.n_kv = c.n_kv_heads; P.G = G; P.ctx = c.ctx; P.npos = npos;
+  P.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
+  P.nsplit = m->b_nsplit; P.part = m->bpart; P.ticket = m->bticket;
+  const dim3 grid((unsigned)c.n_kv_heads, (unsigned)P.nsplit, (unsigned)tokblocks);
+  const size_t sm = battn_smem(G);
+  if (G == 1) k_battn<1><<<grid, BA_THREADS, sm, m->stream>>>(P);
+  else if (G == 2) k_battn<2><<<grid, BA_THREADS, sm, m->stream>>>(P);
+  else if (G == 4) k_battn<4><<<grid, BA_THREADS, sm, m->stream>>>(P);
+  else k_battn<8><<<grid, BA_THREADS, sm, m->stream>>>(P);
+  CU(cudaGetLastError());
+  return KQ_OK;
+}
+
+// One batched pass over nodes [b0, b1) of a verified tree (their ancestors are in this or an
+// earlier pass): logits to vlogits rows b0.., argmax ids to out_ids[b0..].
+static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int pos, const int* depth,
+                       const unsigned long long (*anc)[2]) {
+  const kq_config& c = m->c;
+  const int M = b1 - b0;
+  std::vector<int> tk(M), sl(M), rp(M);
+  std::vector<unsigned long long> mk(2 * M);
+  for (int i = 0; i < M; ++i) {
+    tk[i] = tokens[b0 + i];
+    sl[i] = pos + b0 + i;
+    rp[i] = pos + depth[b0 + i];
+    mk[2 * i] = anc[b0 + i][0];
+    mk[2 * i + 1] = anc[b0 + i][1];
+  }
+  cudaStream_t s = m->stream;
+  CU(cudaMemcpyAsync(m->btok, tk.data(), M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->bslot, sl.data(), M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->brpos, rp.data(), M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->bmask, mk.data(), 2 * M * sizeof(unsigned long long), cudaMemcpyHostToDevice, s));
+  BatchParams B;
+  B.M = M; B.slot = m->bslot; B.rpos = m->brpos; B.mask = m->bmask; B.tree_base = pos;
+  const int QD = c.n_heads * c.head_dim;
+  int rc;
+  for (int l = 0; l < c.n_layers; ++l) {
+    LayerW& w = m->L[l];
+    if ((rc = launch_bnorm(m, M, l == 0, w.attn_norm, l > 0))) return rc;
+    SegSpec qkv[3] = {{w.q, EPI_ROPE_Q, m->bq, nullptr}, {w.k, EPI_ROPE_K, nullptr, w.kc}, {w.v, EPI_V, nullptr, w.vc}};
+    if ((rc = launch_mm(m, qkv, 3, m->bX, QD, B))) return rc;
+    if ((rc = launch_battn(m, l, M, pos + b1, B))) return rc;
+    SegSpec so[1] = {{w.o, EPI_F32, m->by, nullptr}};
+    if ((rc = launch_mm(m, so, 1, m->batt, c.dim, B))) return rc;
+    if ((rc = launch_bnorm(m, M, false, w.ffn_norm, true))) return rc;
+    SegSpec sg[1] = {{w.gu, EPI_SWIGLU, m->bm, nullptr}};
+    if ((rc = launch_mm(m, sg, 1, m->bX, c.ffn, B))) return rc;
+    SegSpec sd[1] = {{w.down, EPI_F32, m->by, nullptr}};
+    if ((rc = launch_mm(m, sd, 1, m->bm, c.dim, B))) return rc;
+  }
+  if ((rc = launch_bnorm(m, M, false, m->out_norm, true))) return rc;
+  const size_t V = (size_t)c.vocab;
+  SegSpec sh[1] = {{m->out, EPI_F32, m->vlogits + (size_t)b0 * V, nullptr}};
+  if ((rc = launch_mm(m, sh, 1, m->bX, c.vocab, B))) return rc;
+  k_argmax_rows<<<M, 256, 0, s>>>(m->vlogits + (size_t)b0 * V, c.vocab, m->out_ids + b0);
+  CU(cudaGetLastError());
+  return KQ_OK;
+}
+
 extern "C" int kq_verify(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, int pos, float* logits,
                          int32_t* best) {
   int rc = model_check(m);
@@ -1183,7 +1334,13 @@ extern "C" int kq_verify(kq_model* m, const int32_t* tokens, const int32_t* pare
   if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "draft tree runs past the context");
   if ((rc = ensure_graphs(m)) || (rc = verify_buffers(m))) return rc;
   const size_t V = (size_t)m->c.vocab;
-  for (int i = 0; i < n; ++i) {
+  const bool batched = !m->verify_seq && batch_supported(m);
+  if (batched) {
+    if ((rc = batch_buffers(m))) return rc;
+    for (int b0 = 0; b0 < n; b0 += MM_MAXM)
+      if ((rc = verify_pass(m, tokens, b0, std::min(n, b0 + MM_MAXM), pos, depth, anc))) return rc;
+  }
+  for (int i = 0; i < n && !batched; ++i) {
     DecodeState& st = m->vstates[i];
     std::memset(&st, 0, sizeof(st));
     st.tok = tokens[i];

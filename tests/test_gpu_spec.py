@@ -73,19 +73,29 @@ def test_tree_verify_matches_oracle(kq, oracle):
     assert rel_l2(Kg, Ko) < 1e-3
 
 
-def test_chain_verify_reproduces_greedy_steps(kq):
+@pytest.mark.parametrize("seq", [1, 0])
+def test_chain_verify_reproduces_greedy_steps(kq, monkeypatch, seq):
+    """A linear chain verified in one call against the same steps decoded one by one: identical
+    ids node by node (KQ_VERIFY_SEQ=1: each node is a decode step), or, for the batched
+    tensor-core pass, logits within 1e-3 and identical ids wherever the top-2 margin is clear."""
+    monkeypatch.setenv("KQ_VERIFY_SEQ", str(seq))
     e = kq.Engine(kq_cfg(kq, TINY), seed=0)
     npos = 40
     e.fill_kv(npos, 4)
-    # greedy continuation, one step at a time
-    chain = [17]
+    chain, step_logits = [17], []
     for i in range(6):
         chain.append(e.step(chain[-1], npos + i))
-    # the same chain in one verify call, from the same cache prefix
+        step_logits.append(e.ylog)
     e.fill_kv(npos, 4)
     parents = [-1] + list(range(len(chain) - 1))
-    best, _ = e.verify(chain, parents, npos, want_logits=False)
-    assert list(best[:-1]) == chain[1:]
+    best, logits = e.verify(chain, parents, npos)
+    if seq:
+        assert list(best[:-1]) == chain[1:]
+    for i, ref in enumerate(step_logits):
+        assert rel_l2(logits[i], ref) < 1e-3
+        top2 = np.sort(ref)[-2:]
+        if top2[1] - top2[0] > 1e-2 * np.abs(ref).max():
+            assert best[i] == chain[i + 1]
 
 
 @pytest.mark.parametrize("temperature", [0.0, 0.7, 1.3])
@@ -135,7 +145,8 @@ def test_accept_full_path_when_draft_equals_target(kq, oracle):
     assert path == list(range(len(toks)))
 
 
-def test_greedy_accept_of_greedy_chain_takes_all(kq):
+def test_greedy_accept_of_greedy_chain_takes_all(kq, monkeypatch):
+    monkeypatch.setenv("KQ_VERIFY_SEQ", "1")   # node-by-node verification reproduces decode exactly
     e = kq.Engine(kq_cfg(kq, TINY), seed=0)
     npos = 25
     e.fill_kv(npos, 7)
