@@ -126,10 +126,75 @@ def run_reference(args, rank, world):
     return 0
 
 
+# Config-3 (speculative verification on the config-2 model): a 2048-position prefix, a draft tree
+# of branching [4, 2, 2, 1] (1 + 4 + 8 + 16 + 16 = 45 nodes; BASELINE's "64 nodes" does not
+# match that branching, the branching is kept), draft tokens ~U{0..vocab-1}, draft distributions
+# softmax of N(0, 2) logits, temperature 0.7, seeded uniforms; and a greedy linear chain of K = 8.
+SPEC_PREFIX = 2048
+SPEC_TREE = [4, 2, 2, 1]
+SPEC_T = 0.7
+SPEC_CHAIN = 8
+
+
+def tree_parents(branching):
+    parents, level = [-1], [0]
+    for b in branching:
+        nxt = []
+        for v in level:
+            for _ in range(b):
+                parents.append(v)
+                nxt.append(len(parents) - 1)
+        level = nxt
+    return parents
+
+
+def spec_bench(e, vocab, steps, warmup):
+    """Draft-then-verify steps through the public API (kq_verify + kq_accept + kq_commit, each
+    synchronising; host-timed, inputs generated before the timed region): verified tokens/s, the
+    verify time, and the accepted-length histogram, for the tree (stochastic) and the chain
+    (greedy)."""
+    import numpy as np
+    out = {}
+    for name, parents, T in (("tree", tree_parents(SPEC_TREE), SPEC_T), ("chain", [-1] + list(range(SPEC_CHAIN)), 0.0)):
+        n = len(parents)
+        rng_d, rng_u = np.random.default_rng(1), np.random.default_rng(2)   # drafts / uniforms (seeds 1, 2)
+        total = steps + warmup
+        drafts = rng_d.integers(0, vocab, (total, n)).astype(np.int32)
+        g = rng_d.normal(0.0, 2.0, (n, vocab)).astype(np.float32) if T > 0 else None
+        ua = rng_u.random((total, n)).astype(np.float32)
+        uf = rng_u.random((total, n)).astype(np.float32)
+        e.fill_kv(SPEC_PREFIX, 2)
+        pos, root, emitted, hist, t_all, t_ver = SPEC_PREFIX, 1, 0, {}, 0.0, 0.0
+        for i in range(total):
+            toks = drafts[i].copy()
+            toks[0] = root
+            t0 = time.perf_counter()
+            e.verify(toks, parents, pos, want_logits=False)
+            t1 = time.perf_counter()
+            path, toks_out = e.accept(toks, parents, g, T, ua[i], uf[i])
+            e.commit(path, pos)
+            t2 = time.perf_counter()
+            if i >= warmup:
+                t_all += t2 - t0
+                t_ver += t1 - t0
+                emitted += len(toks_out)
+                k = len(path) - 1
+                hist[k] = hist.get(k, 0) + 1
+            pos += len(path)
+            root = toks_out[-1]
+        out[name] = {"nodes": n, "temperature": T, "verified_tok_s": emitted / t_all, "verify_ms": 1e3 * t_ver / steps,
+                     "step_ms": 1e3 * t_all / steps, "accepted_hist": {str(k): v for k, v in sorted(hist.items())}}
+    return out
+
+
 def run_profile_mode(args):
     """decode-only: fill the config-2 model (optionally fewer layers), W + K device-resident
     decode steps at ctx 4K. gemv-only: the config-0 Q4_K GEMV over 16 rotating copies."""
     import kq
+    if args.mode == "spec":
+        e = kq.Engine(kq.Config.default(ctx=CTX, n_layers=args.layers), seed=0)
+        print(json.dumps({"mode": "spec", **spec_bench(e, e.vocab, args.steps, args.warmup)}))
+        return 0
     if args.mode == "gemv-only":
         mats = [kq.QMat(12, 12288, 4096).fill_synthetic(0, 1000 + i) for i in range(16)]
         kq.time_matvec(mats, args.warmup)
@@ -153,7 +218,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=32, help="decode-only: layers of the model (small ncu captures)")
-    ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only"],
+    ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only", "spec"],
                     help="decode-only / gemv-only: the small commands the ncu captures in profiles/ run")
     args = ap.parse_args()
     if args.mode != "full":
@@ -215,6 +280,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     e2e_tok_s = world * K / e2e_s
+    spec = spec_bench(e, e.vocab, 8, 3)
     e.close()
 
     # ---- the dominant kernel: config-0 Q4_K GEMV over 16 rotating weight copies (453 MB > L2)
@@ -255,7 +321,8 @@ def main():
             "step_roofline": {"bound": "hbm", "achieved": step_gbs, "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm,
                               "bytes_per_token": step_bytes, "roofline_tok_s": hbm * 1e9 / step_bytes},
             "clocks": clk.summary(),
-            "spec_verify_tok_s": None,
+            "spec_verify_tok_s": spec["tree"]["verified_tok_s"] * world,
+            "spec": spec,
             "cpu_baseline": cb,
         }
         print(json.dumps(line), flush=True)
