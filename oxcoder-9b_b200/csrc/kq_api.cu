@@ -84,6 +84,11 @@ static int dev_init(int device) {
   for (int tm = 1; tm <= 3; ++tm)
     for (int ri = 0; ri < 3; ++ri)
       CU(cudaFuncSetAttribute(gemv_fn(tm, 1 << ri), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.smem_optin));
+  CU(cudaFuncSetAttribute(k_tmm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tmm_smem(TM_MAXN)));
+  CU(cudaFuncSetAttribute(k_battn<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BA_SMEM));
+  CU(cudaFuncSetAttribute(k_battn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BA_SMEM));
+  CU(cudaFuncSetAttribute(k_battn<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BA_SMEM));
+  CU(cudaFuncSetAttribute(k_battn<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BA_SMEM));
   CU(cudaMalloc(&d.err, sizeof(int)));
   CU(cudaMemset(d.err, 0, sizeof(int)));
   d.init = true;
@@ -445,10 +450,14 @@ struct kq_model {
   __half** caches = nullptr;        // [2 * n_layers] K/V cache pointers (compaction)
   // batched verification pass (up to MM_MAXM tokens at once)
   float *bh = nullptr, *by = nullptr, *bq = nullptr, *bpart = nullptr;
-  float *bX = nullptr, *batt = nullptr, *bm = nullptr;
+  __half *bxd = nullptr, *bxa = nullptr, *bxf = nullptr;   // packed GEMM inputs: C = dim, NH*HD, ffn
   int *btok = nullptr, *bslot = nullptr, *brpos = nullptr, *bticket = nullptr;
   unsigned long long* bmask = nullptr;
-  int b_nsplit = 0;
+  int b_nsplit = 0;                 // attention key splits the scratch holds
+  float* tpart = nullptr;           // split-K partials of the tensor-core GEMM
+  int* tticket = nullptr;
+  size_t tpart_floats = 0;
+  int tticket_n = 0;
   bool verify_seq = false;          // node-by-node decode steps instead of the batched pass
   std::vector<void*> allocs;
 };
@@ -1179,6 +1188,75 @@ static int verify_buffers(kq_model* m) {
   return KQ_OK;
 }
 
+// ------------------------------------------------------------------------------ tensor-core GEMM
+// Split-K factor: the fewest waves x super-blocks per CTA (plus a fixed per-CTA cost of about two
+// super-blocks: set-up, pipeline fill, epilogue), over splits of 1..16.
+static int tmm_split(int ntiles, int G, int nsm) {
+  int best = 1;
+  long long best_cost = -1;
+  for (int s = 1; s <= std::min(G, 16); ++s) {
+    const long long ctas = (long long)ntiles * s, waves = (ctas + nsm - 1) / nsm;
+    const long long cost = waves * ((G + s - 1) / s + 2);
+    if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = s; }
+  }
+  return best;
+}
+static int tmm_tiles(const SegSpec* ss, int nseg) {
+  int t = 0;
+  for (int i = 0; i < nseg; ++i) t += (ss[i].m->R + TM_ROWS - 1) / TM_ROWS;
+  return t;
+}
+// Segments, tiles and split of one GEMM over M tokens (outputs and scratch filled by the caller).
+static void tmm_fill(const SegSpec* ss, int nseg, int M, int nsm, TmmParams& P) {
+  std::memset(&P, 0, sizeof(P));
+  int tiles = 0;
+  for (int i = 0; i < nseg; ++i) {
+    P.seg[i].w = ss[i].m->view();
+    P.seg[i].epi = ss[i].epi;
+    P.seg[i].tile0 = tiles;
+    P.seg[i].out_f = ss[i].out_f;
+    P.seg[i].out_h = ss[i].out_h;
+    tiles += (ss[i].m->R + TM_ROWS - 1) / TM_ROWS;
+  }
+  P.nseg = nseg;
+  P.ntiles = tiles;
+  P.C = ss[0].m->C;
+  P.G = P.C / 256;
+  P.M = M;
+  P.Npad = (M + 15) & ~15;
+  P.nsplit = tmm_split(tiles, P.G, nsm);
+}
+static size_t tmm_part_floats(int ntiles, int nsplit, int Npad) {
+  return nsplit > 1 ? (size_t)nsplit * Npad * ntiles * TM_ROWS : 0;
+}
+static cudaError_t tmm_launch(const TmmParams& P, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)P.ntiles, (unsigned)P.nsplit);
+  cfg.blockDim = dim3(TM_THREADS);
+  cfg.dynamicSmemBytes = tmm_smem(P.Npad);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_tmm, P);
+}
+template <class K, class PT>
+static cudaError_t launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const PT& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
 static int batch_buffers(kq_model* m) {
   if (m->bh) return KQ_OK;
   const kq_config& c = m->c;
@@ -1187,60 +1265,61 @@ static int batch_buffers(kq_model* m) {
   m->bh = dalloc<float>(m, MM * c.dim, ok);
   m->by = dalloc<float>(m, MM * c.dim, ok);
   m->bq = dalloc<float>(m, MM * QD, ok);
-  m->bX = dalloc<float>(m, MM * c.dim, ok);
-  m->batt = dalloc<float>(m, MM * QD, ok);
-  m->bm = dalloc<float>(m, MM * c.ffn, ok);
+  m->bxd = dalloc<__half>(m, xp_halves(MM_MAXM, c.dim), ok);
+  m->bxa = dalloc<__half>(m, xp_halves(MM_MAXM, (int)QD), ok);
+  m->bxf = dalloc<__half>(m, xp_halves(MM_MAXM, c.ffn), ok);
   m->btok = dalloc<int>(m, MM, ok);
   m->bslot = dalloc<int>(m, MM, ok);
   m->brpos = dalloc<int>(m, MM, ok);
   m->bmask = dalloc<unsigned long long>(m, 2 * MM, ok);
-  const int G = c.n_heads / c.n_kv_heads, tokblocks = (MM_MAXM + BA_TOK - 1) / BA_TOK;
-  m->b_nsplit = std::max(1, std::min(32, 2 * m->nsm / (c.n_kv_heads * tokblocks)));
-  m->bpart = dalloc<float>(m, (size_t)c.n_kv_heads * tokblocks * m->b_nsplit * BA_TOK * G * (128 + 2), ok);
-  m->bticket = dalloc<int>(m, (size_t)c.n_kv_heads * tokblocks, ok);
+  // attention: key splits of up to 32, row groups of BA_ROWS query rows
+  const int G = c.n_heads / c.n_kv_heads, rowgroups = (MM_MAXM * G + BA_ROWS - 1) / BA_ROWS;
+  m->b_nsplit = 32;
+  m->bpart = dalloc<float>(m, (size_t)c.n_kv_heads * rowgroups * m->b_nsplit * BA_ROWS * (128 + 2), ok);
+  m->bticket = dalloc<int>(m, (size_t)c.n_kv_heads * rowgroups, ok);
+  // GEMM split-K scratch: the largest of the pass's GEMMs
+  const LayerW& w = m->L[0];
+  const SegSpec qkv[3] = {{w.q, 0, nullptr, nullptr}, {w.k, 0, nullptr, nullptr}, {w.v, 0, nullptr, nullptr}};
+  const SegSpec one[4] = {{w.o, 0, nullptr, nullptr}, {w.gu, 0, nullptr, nullptr}, {w.down, 0, nullptr, nullptr},
+                          {m->out, 0, nullptr, nullptr}};
+  size_t pf = 0;
+  int tk = 0;
+  for (int i = -1; i < 4; ++i) {
+    const SegSpec* ss = i < 0 ? qkv : &one[i];
+    const int nseg = i < 0 ? 3 : 1, tiles = tmm_tiles(ss, nseg);
+    pf = std::max(pf, tmm_part_floats(tiles, tmm_split(tiles, ss[0].m->C / 256, m->nsm), MM_MAXM));
+    tk = std::max(tk, tiles);
+  }
+  m->tpart_floats = pf;
+  m->tticket_n = tk;
+  m->tpart = dalloc<float>(m, std::max<size_t>(pf, 1), ok);
+  m->tticket = dalloc<int>(m, (size_t)tk, ok);
   if (!ok) return set_err(KQ_ERR_MEMORY, "batched verify buffers");
-  CU(cudaFuncSetAttribute(k_mm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MM_SMEM));
-  const size_t sm = battn_smem(G);
-  cudaError_t e = G == 1 ? cudaFuncSetAttribute(k_battn<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
-                : G == 2 ? cudaFuncSetAttribute(k_battn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
-                : G == 4 ? cudaFuncSetAttribute(k_battn<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
-                         : cudaFuncSetAttribute(k_battn<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  if (e != cudaSuccess) return set_err(KQ_ERR_BACKEND, std::string("batched attention setup: ") + cudaGetErrorString(e));
   return KQ_OK;
 }
 
 static bool batch_supported(const kq_model* m) {
-  const kq_config& c = m->c;
-  const int rows[] = {c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim, 2 * c.ffn, c.dim, c.vocab};
-  for (int r : rows)
-    if (r % 16) return false;
-  return true;
+  return m->c.ffn % 64 == 0 && (m->c.n_heads * m->c.head_dim) % 64 == 0;
 }
 
-static int launch_mm(kq_model* m, const SegSpec* ss, int nseg, const float* X, int out_ld, const BatchParams& B) {
-  MMParams P;
-  std::memset(&P, 0, sizeof(P));
-  int rows = 0;
-  for (int i = 0; i < nseg; ++i) {
-    P.seg[i].w = ss[i].m->view();
-    P.seg[i].epi = ss[i].epi;
-    P.seg[i].out_f = ss[i].out_f;
-    P.seg[i].out_h = ss[i].out_h;
-    rows += ss[i].m->R;
-  }
-  P.nseg = nseg;
-  P.C = ss[0].m->C;
-  P.G = P.C / 256;
-  P.X = X;
+static int launch_tmm(kq_model* m, const SegSpec* ss, int nseg, const __half* xp, __half* xp_out, int out_ld,
+                      const BatchParams& B) {
+  TmmParams P;
+  tmm_fill(ss, nseg, B.M, m->nsm, P);
+  P.xp = xp;
+  P.xp_out = xp_out;
   P.B = B;
   P.out_ld = out_ld;
   P.cos_t = m->cos_t;
   P.sin_t = m->sin_t;
   P.hd = m->c.head_dim;
   P.ctx = m->c.ctx;
-  const int per_cta = 16 * MM_WARPS;
-  k_mm<<<(rows + per_cta - 1) / per_cta, MM_WARPS * 32, MM_SMEM, m->stream>>>(P);
-  CU(cudaGetLastError());
+  P.part = m->tpart;
+  P.ticket = m->tticket;
+  P.err = m->err;
+  if (tmm_part_floats(P.ntiles, P.nsplit, P.Npad) > m->tpart_floats || P.ntiles > m->tticket_n)
+    return set_err(KQ_ERR_BACKEND, "GEMM scratch too small");
+  CU(tmm_launch(P, m->stream, true));
   return KQ_OK;
 }
 
@@ -1249,28 +1328,34 @@ static int launch_bnorm(kq_model* m, int M, bool embed, const float* gamma, bool
   std::memset(&P, 0, sizeof(P));
   P.M = M; P.D = m->c.dim; P.tok = m->btok;
   if (embed) P.emb = m->emb->view();
-  P.h = m->bh; P.y = add ? m->by : nullptr; P.gamma = gamma; P.eps = m->c.eps; P.X = m->bX;
+  P.h = m->bh; P.y = add ? m->by : nullptr; P.gamma = gamma; P.eps = m->c.eps;
+  P.xp = m->bxd; P.Npad = (M + 15) & ~15;
   P.vocab = m->c.vocab; P.err = m->err;
-  k_bnorm<<<M, 256, 0, m->stream>>>(P);
-  CU(cudaGetLastError());
+  CU(launch_pdl(k_bnorm, dim3((unsigned)M), dim3(256), 0, m->stream, P));
   return KQ_OK;
 }
 
-static int launch_battn(kq_model* m, int layer, int M, int npos, const BatchParams& B) {
+static int launch_battn(kq_model* m, int layer, int npos, const BatchParams& B) {
   const kq_config& c = m->c;
-  const int G = c.n_heads / c.n_kv_heads, tokblocks = (M + BA_TOK - 1) / BA_TOK;
+  const int G = c.n_heads / c.n_kv_heads, M = B.M;
+  const int rowgroups = (M * G + BA_ROWS - 1) / BA_ROWS, nblocks = (npos + BA_KB - 1) / BA_KB;
+  const int base = c.n_kv_heads * rowgroups;
+  int want = std::max(1, (2 * m->nsm + base - 1) / base);
+  want = std::min(want, std::min(nblocks, m->b_nsplit));
   BAttnParams P;
-  P.q = m->bq; P.kc = m->L[layer].kc; P.vc = m->L[layer].vc; P.out = m->batt; P.B = B;
-  P.n_kv = c.n_kv_heads; P.G = G; P.ctx = c.ctx; P.npos = npos;
+  P.q = m->bq; P.kc = m->L[layer].kc; P.vc = m->L[layer].vc; P.out_xp = m->bxa; P.Npad = (M + 15) & ~15; P.B = B;
+  P.n_kv = c.n_kv_heads; P.ctx = c.ctx; P.npos = npos;
   P.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
-  P.nsplit = m->b_nsplit; P.part = m->bpart; P.ticket = m->bticket;
-  const dim3 grid((unsigned)c.n_kv_heads, (unsigned)P.nsplit, (unsigned)tokblocks);
-  const size_t sm = battn_smem(G);
-  if (G == 1) k_battn<1><<<grid, BA_THREADS, sm, m->stream>>>(P);
-  else if (G == 2) k_battn<2><<<grid, BA_THREADS, sm, m->stream>>>(P);
-  else if (G == 4) k_battn<4><<<grid, BA_THREADS, sm, m->stream>>>(P);
-  else k_battn<8><<<grid, BA_THREADS, sm, m->stream>>>(P);
-  CU(cudaGetLastError());
+  P.nblk = (nblocks + want - 1) / want;
+  P.nsplit = (nblocks + P.nblk - 1) / P.nblk;
+  P.part = m->bpart; P.ticket = m->bticket;
+  const dim3 grid((unsigned)c.n_kv_heads, (unsigned)rowgroups, (unsigned)P.nsplit), blk(BA_WARPS * 32);
+  cudaError_t e;
+  if (G == 1) e = launch_pdl(k_battn<1>, grid, blk, BA_SMEM, m->stream, P);
+  else if (G == 2) e = launch_pdl(k_battn<2>, grid, blk, BA_SMEM, m->stream, P);
+  else if (G == 4) e = launch_pdl(k_battn<4>, grid, blk, BA_SMEM, m->stream, P);
+  else e = launch_pdl(k_battn<8>, grid, blk, BA_SMEM, m->stream, P);
+  CU(e);
   return KQ_OK;
 }
 
@@ -1302,20 +1387,20 @@ static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int p
     LayerW& w = m->L[l];
     if ((rc = launch_bnorm(m, M, l == 0, w.attn_norm, l > 0))) return rc;
     SegSpec qkv[3] = {{w.q, EPI_ROPE_Q, m->bq, nullptr}, {w.k, EPI_ROPE_K, nullptr, w.kc}, {w.v, EPI_V, nullptr, w.vc}};
-    if ((rc = launch_mm(m, qkv, 3, m->bX, QD, B))) return rc;
-    if ((rc = launch_battn(m, l, M, pos + b1, B))) return rc;
+    if ((rc = launch_tmm(m, qkv, 3, m->bxd, nullptr, QD, B))) return rc;
+    if ((rc = launch_battn(m, l, pos + b1, B))) return rc;
     SegSpec so[1] = {{w.o, EPI_F32, m->by, nullptr}};
-    if ((rc = launch_mm(m, so, 1, m->batt, c.dim, B))) return rc;
+    if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, c.dim, B))) return rc;
     if ((rc = launch_bnorm(m, M, false, w.ffn_norm, true))) return rc;
-    SegSpec sg[1] = {{w.gu, EPI_SWIGLU, m->bm, nullptr}};
-    if ((rc = launch_mm(m, sg, 1, m->bX, c.ffn, B))) return rc;
+    SegSpec sg[1] = {{w.gu, EPI_SWIGLU, nullptr, nullptr}};
+    if ((rc = launch_tmm(m, sg, 1, m->bxd, m->bxf, 0, B))) return rc;
     SegSpec sd[1] = {{w.down, EPI_F32, m->by, nullptr}};
-    if ((rc = launch_mm(m, sd, 1, m->bm, c.dim, B))) return rc;
+    if ((rc = launch_tmm(m, sd, 1, m->bxf, nullptr, c.dim, B))) return rc;
   }
   if ((rc = launch_bnorm(m, M, false, m->out_norm, true))) return rc;
   const size_t V = (size_t)c.vocab;
   SegSpec sh[1] = {{m->out, EPI_F32, m->vlogits + (size_t)b0 * V, nullptr}};
-  if ((rc = launch_mm(m, sh, 1, m->bX, c.vocab, B))) return rc;
+  if ((rc = launch_tmm(m, sh, 1, m->bxd, nullptr, c.vocab, B))) return rc;
   k_argmax_rows<<<M, 256, 0, s>>>(m->vlogits + (size_t)b0 * V, c.vocab, m->out_ids + b0);
   CU(cudaGetLastError());
   return KQ_OK;
@@ -1527,13 +1612,51 @@ extern "C" int kq_qmat_matvec(kq_qmat* a, const float* x, float* y) {
   return rc;
 }
 
+// M = 1: the decode GEMV; M >= 2: the tensor-core GEMM of the batched passes (split-precision
+// fp16 operands, fp32 accumulation).
 extern "C" int kq_qmat_matmul(kq_qmat* a, const float* x, int M, float* y) {
   if (!a || !x || !y || M < 1 || M > 64) return set_err(KQ_ERR_ARG, "bad matmul arguments");
-  for (int mm = 0; mm < M; ++mm) {
-    const int rc = kq_qmat_matvec(a, x + (size_t)mm * a->C, y + (size_t)mm * a->R);
-    if (rc) return rc;
+  if (M == 1) return kq_qmat_matvec(a, x, y);
+  int rc = dev_init(a->device);
+  if (rc) return rc;
+  CU(cudaSetDevice(a->device));
+  const SegSpec ss[1] = {{a, EPI_F32, nullptr, nullptr}};
+  TmmParams P;
+  tmm_fill(ss, 1, M, g_dev[a->device].nsm, P);
+  const size_t pf = tmm_part_floats(P.ntiles, P.nsplit, P.Npad);
+  float *xd = nullptr, *yd = nullptr, *part = nullptr;
+  __half* xp = nullptr;
+  int* ticket = nullptr;
+  bool ok = cudaMalloc(&xd, (size_t)M * a->C * 4) == cudaSuccess;
+  ok = ok && cudaMalloc(&yd, (size_t)M * a->R * 4) == cudaSuccess;
+  ok = ok && cudaMalloc(&xp, xp_halves(P.Npad, a->C) * 2) == cudaSuccess;
+  ok = ok && cudaMalloc(&part, std::max<size_t>(pf, 1) * 4) == cudaSuccess;
+  ok = ok && cudaMalloc(&ticket, (size_t)P.ntiles * 4) == cudaSuccess;
+  if (!ok) rc = set_err(KQ_ERR_MEMORY, "matmul buffers");
+  if (!rc && (cudaMemset(ticket, 0, (size_t)P.ntiles * 4) != cudaSuccess ||
+              cudaMemcpy(xd, x, (size_t)M * a->C * 4, cudaMemcpyHostToDevice) != cudaSuccess))
+    rc = set_err(KQ_ERR_BACKEND, "matmul upload");
+  if (!rc) {
+    const long long n = (long long)P.Npad * a->C;
+    k_xpack<<<(unsigned)((n + 255) / 256), 256>>>(xd, M, P.Npad, a->C, xp);
+    P.xp = xp;
+    P.seg[0].out_f = yd;
+    P.out_ld = a->R;
+    P.part = part;
+    P.ticket = ticket;
+    P.err = g_dev[a->device].err;
+    if (cudaGetLastError() != cudaSuccess || tmm_launch(P, 0, false) != cudaSuccess)
+      rc = set_err(KQ_ERR_BACKEND, "matmul launch");
   }
-  return KQ_OK;
+  if (!rc && cudaMemcpy(y, yd, (size_t)M * a->R * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+    rc = set_err(KQ_ERR_BACKEND, "matmul download");
+  cudaFree(xd);
+  cudaFree(yd);
+  cudaFree(xp);
+  cudaFree(part);
+  cudaFree(ticket);
+  if (!rc) rc = dev_err_check(a->device);
+  return rc;
 }
 
 extern "C" int kq_time_matvec(kq_qmat* const* mats, int ncopies, int n, float* ms_out) {

@@ -1,0 +1,568 @@
+// kq_tmm.cuh -- fused-dequant GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulators)
+// for the multi-token passes: Y[M][R] = X[M][C] W^T with W in the kq Q4_K / Q6_K device layout and
+// M <= 128 tokens (the verification pass over a draft tree, the M-row matrix product).
+//
+// Precision. The Kindi CPU path dequantises every weight in fp32 (w = (d*sc)*q - dmin*mn, or
+// (d*scale)*(q6 - 32); q4kernels.h:19-30) and accumulates in fp32. Here each weight w and each
+// activation x is carried as two fp16 numbers, hi = fp16(v) and lo = fp16(v - hi) (about 22
+// significant bits), and every 16-column K step issues three MMAs into two fp32 TMEM
+// accumulators: hi(w)*hi(x) into one, the corrections lo(w)*hi(x) + hi(w)*lo(x) into a second (so
+// they are not rounded against the large partial sums), added in the epilogue. The dropped lo*lo
+// term is below 2^-22 of the product, so the result is within a few fp32 roundings of the fp32
+// dot product.
+//
+// CTA = 128 weight rows (16 tiles of the kq layout) x all tokens x a contiguous range of super-
+// blocks (split-K over CTAs; the last CTA of a row tile sums the fp32 partials in split order, so
+// the result does not depend on which CTA finishes last). Warp roles (352 threads):
+//   warps 0-7  dequantise: raw super-block bytes (shared memory) -> hi/lo fp16 A tiles of 64
+//              columns in the SWIZZLE_128B K-major layout the MMA reads; then the epilogue
+//   warp 8     raw loader: cp.async of each super-block's bytes for the 128 rows into a padded ring
+//              (row strides 144 B / 208 B = an odd number of 16-byte units: conflict-free reads)
+//   warp 9     TMEM allocation; lane 0 issues tcgen05.mma (3 x 4 per 64-column sub-stage) and
+//              commits each sub-stage's completion to the barrier that frees its A and X buffers
+//   warp 10    activation loader: one cp.async.bulk per 64-column sub-stage of the packed X
+// Every wait is bounded; on a timeout the CTA records the error, stops issuing work, drains what
+// it issued and frees its tensor memory before it exits.
+#pragma once
+#include "kq_common.cuh"
+#include "kq_qformat.cuh"
+#include "kq_gemv.cuh"
+
+namespace kq {
+
+// ------------------------------------------------------------------------------ packed activations
+// The B operand of the GEMM: for every 64-column group, an hi plane then a lo plane, each Npad
+// token rows of 128 bytes (64 fp16) in the SWIZZLE_128B K-major layout: the 16-byte chunk j of
+// token t's row sits at chunk position j ^ (t & 7). Npad is a multiple of 16 (the MMA's N).
+__host__ __device__ inline size_t xp_group_halves(int Npad) { return (size_t)2 * 64 * Npad; }
+__host__ __device__ inline size_t xp_halves(int Npad, int C) { return (size_t)(C / 64) * xp_group_halves(Npad); }
+__device__ __forceinline__ size_t xp_off(int Npad, int tok, int col) {
+  const int q = col >> 6, j8 = (col >> 3) & 7;
+  return (size_t)q * xp_group_halves(Npad) + (size_t)tok * 64 + (size_t)(((j8 ^ (tok & 7)) << 3) | (col & 7));
+}
+__device__ __forceinline__ void xp_store(__half* xp, int Npad, int tok, int col, float v) {
+  const __half hi = __float2half_rn(v);
+  const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+  const size_t o = xp_off(Npad, tok, col);
+  xp[o] = hi;
+  xp[o + (size_t)64 * Npad] = lo;
+}
+
+// fp32 [M][C] -> packed activations (tokens M..Npad-1 zero).
+__global__ void __launch_bounds__(256) k_xpack(const float* __restrict__ x, int M, int Npad, int C, __half* xp) {
+  const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+  if (i >= (long long)Npad * C) return;
+  const int t = (int)(i / C), col = (int)(i % C);
+  xp_store(xp, Npad, t, col, t < M ? x[(size_t)t * C + col] : 0.f);
+}
+
+// ------------------------------------------------------------------------------ tcgen05 wrappers
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (both operands fp16), fp32 accumulate.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// Arrive once on `bar` when every MMA this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// 8 consecutive fp32 columns of this thread's TMEM lane (the warp's 32-lane quarter), waited.
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r0, r1, r2, r3, r4, r5, r6, r7;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3), "=r"(r4), "=r"(r5), "=r"(r6), "=r"(r7)
+      : "r"(taddr)
+      : "memory");
+  v[0] = __uint_as_float(r0); v[1] = __uint_as_float(r1); v[2] = __uint_as_float(r2); v[3] = __uint_as_float(r3);
+  v[4] = __uint_as_float(r4); v[5] = __uint_as_float(r5); v[6] = __uint_as_float(r6); v[7] = __uint_as_float(r7);
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row atoms of 1024 bytes stacked along
+// M/N (stride 1024), start address 16-byte granular (fields: start >> 4 at bit 0, leading offset
+// at bit 16 (unused by swizzled K-major layouts), stride >> 4 at bit 32, descriptor version 1 at
+// bit 46, layout type 2 = 128-byte swizzle at bit 61).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: fp32 D (bit 4), fp16 A and B (formats 0), both K-major,
+// N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t tc_idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// cp.async of 16 (or 4) bytes, zero-filled when src_bytes = 0; L2 evict-first for streamed weights.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(src_bytes), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+// Arrive on `bar` (counted in its initial count) when this thread's earlier cp.asyncs complete.
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// Named barrier that also ANDs a predicate over the participating threads (uniform result).
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, %2, %3, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(r) : "r"((uint32_t)v), "r"(id), "r"(nthreads) : "memory");
+  return r != 0;
+}
+
+// ------------------------------------------------------------------------------ the GEMM
+struct BatchParams {                   // per-token data of a pass
+  int M;
+  const int* slot;                     // [M] K/V slot
+  const int* rpos;                     // [M] rotary position
+  const unsigned long long* mask;      // [M][2] ancestor masks relative to tree_base
+  int tree_base;
+};
+
+constexpr int TM_ROWS = 128;                       // weight rows per CTA (the MMA's M)
+constexpr int TM_DQ_WARPS = 8;                     // dequantising / epilogue warps
+constexpr int TM_THREADS = (TM_DQ_WARPS + 3) * 32; // + raw loader, MMA, activation loader
+constexpr int TM_RS = 3;                           // raw super-block stages in flight
+constexpr int TM_AS = 2;                           // A / X sub-stage buffers (64 columns each)
+constexpr int TM_RAW_Q4 = 144, TM_RAW_Q6 = 208;    // raw row strides (odd multiples of 16 B)
+constexpr int TM_RAW_BYTES = TM_ROWS * TM_RAW_Q6;  // one raw stage
+constexpr int TM_A_BYTES = 2 * TM_ROWS * 128;      // hi + lo planes of one A sub-stage
+constexpr int TM_MAXN = 128;                       // tokens per GEMM (Npad)
+
+struct TmmSeg {
+  QView w;
+  int epi;
+  int tile0;           // first row tile (of TM_ROWS rows) of this segment in the grid
+  float* out_f;        // F32 / ROPE_Q output
+  __half* out_h;       // ROPE_K / V: this layer's cache [n_kv][ctx][hd]
+};
+struct TmmParams {
+  TmmSeg seg[KQ_MAX_SEG];
+  int nseg, ntiles;    // row tiles over all segments
+  int C, G, nsplit;    // K = C columns, G super-blocks, split over nsplit CTAs
+  int M, Npad;         // tokens, MMA N (multiple of 16)
+  const __half* xp;    // packed activations (xp_off layout)
+  __half* xp_out;      // SWIGLU: packed input of the next GEMM (same Npad)
+  BatchParams B;
+  int out_ld;          // row length of the fp32 outputs
+  const float* cos_t;
+  const float* sin_t;
+  int hd, ctx;
+  float* part;         // split-K partials [nsplit][Npad][ntiles * TM_ROWS]
+  int* ticket;         // [ntiles], zero between launches
+  int* err;
+};
+
+__host__ __device__ inline size_t tmm_smem(int Npad) {
+  return 1024 + (size_t)TM_AS * TM_A_BYTES + (size_t)TM_AS * 256 * Npad + (size_t)TM_RS * TM_RAW_BYTES +
+         (size_t)TM_RS * TM_ROWS * 4;
+}
+
+__device__ __forceinline__ uint64_t tm_clock_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: gives up after TM_WAIT_NS of wall time (or KQ_WAIT_LIMIT polls), or at once when
+// another role of the CTA has flagged a failure. Every wait of the pipeline normally ends in
+// microseconds.
+constexpr uint64_t TM_WAIT_NS = 2000000000ull;
+__device__ __forceinline__ bool tm_wait(uint64_t* bar, uint32_t parity, int* err, int bit, volatile int* abort_f) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0; it < KQ_WAIT_LIMIT; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255) == 255) {
+      if (*abort_f) return false;
+      const uint64_t now = tm_clock_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > TM_WAIT_NS) break;
+    }
+  }
+  atomicOr(err, bit);
+  *abort_f = 1;
+  return false;
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+// Byte e of x (a value < 2^8) as the float 2^23 + value (exact).
+__device__ __forceinline__ float tm_magic(uint32_t x, int e) {
+  return __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540u | (uint32_t)e));
+}
+__device__ __forceinline__ void tm_split(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 hf = __half22float2(h);
+  hi = h2u(h);
+  lo = h2u(__floats2half2_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y)));
+}
+// A tile store: row r (0..127), 16-byte chunk j8 of the 64-column sub-stage, hi and lo planes.
+__device__ __forceinline__ void tm_put(uint8_t* A, int r, int j8, const uint4& hi, const uint4& lo) {
+  const int off = r * 128 + ((j8 ^ (r & 7)) << 4);
+  *reinterpret_cast<uint4*>(A + off) = hi;
+  *reinterpret_cast<uint4*>(A + TM_A_BYTES / 2 + off) = lo;
+}
+// Eight Q4_K weights (nibble values in the bytes of x0, x1): w = ds*q - dm.
+__device__ __forceinline__ void tm_q4_chunk(uint32_t x0, uint32_t x1, float ds, float dm, uint4& hi, uint4& lo) {
+  float w[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    w[e] = fmaf(ds, __fsub_rn(tm_magic(x0, e), 8388608.f), -dm);
+    w[4 + e] = fmaf(ds, __fsub_rn(tm_magic(x1, e), 8388608.f), -dm);
+  }
+  tm_split(w[0], w[1], hi.x, lo.x);
+  tm_split(w[2], w[3], hi.y, lo.y);
+  tm_split(w[4], w[5], hi.z, lo.z);
+  tm_split(w[6], w[7], hi.w, lo.w);
+}
+// Eight Q6_K weights (6-bit values in the bytes of x0, x1): w = dsc * (q - 32).
+__device__ __forceinline__ void tm_q6_chunk(uint32_t x0, uint32_t x1, float dsc, uint4& hi, uint4& lo) {
+  float w[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    w[e] = __fmul_rn(dsc, __fsub_rn(tm_magic(x0, e), 8388640.f));
+    w[4 + e] = __fmul_rn(dsc, __fsub_rn(tm_magic(x1, e), 8388640.f));
+  }
+  tm_split(w[0], w[1], hi.x, lo.x);
+  tm_split(w[2], w[3], hi.y, lo.y);
+  tm_split(w[4], w[5], hi.z, lo.z);
+  tm_split(w[6], w[7], hi.w, lo.w);
+}
+
+// Epilogue of one (row, token) value. lrow: row within the segment; vo: the value of row lrow ^ 1.
+__device__ __forceinline__ void tm_epilogue(const TmmParams& P, const TmmSeg& S, int lrow, int tk, float v, float vo) {
+  switch (S.epi) {
+    case EPI_F32:
+      S.out_f[(size_t)tk * P.out_ld + lrow] = v;
+      break;
+    case EPI_V: {
+      const int kv = lrow / P.hd, d = lrow % P.hd;
+      S.out_h[((size_t)kv * P.ctx + P.B.slot[tk]) * P.hd + d] = __float2half_rn(v);
+    } break;
+    case EPI_SWIGLU:   // rows (2i, 2i + 1) = (gate i, up i)
+      if ((lrow & 1) == 0) xp_store(P.xp_out, P.Npad, tk, lrow >> 1, __fmul_rn(silu_f(v), vo));
+      break;
+    case EPI_ROPE_Q:
+    case EPI_ROPE_K:   // rows (2i, 2i + 1) of a head = NeoX pair (i, i + hd/2)
+      if ((lrow & 1) == 0) {
+        const int hh = lrow / P.hd, i2 = (lrow % P.hd) >> 1, half = P.hd >> 1;
+        const int rp = P.B.rpos[tk];
+        const float cs = __ldg(P.cos_t + (size_t)rp * half + i2), sn = __ldg(P.sin_t + (size_t)rp * half + i2);
+        const float o0 = __fsub_rn(__fmul_rn(v, cs), __fmul_rn(vo, sn));
+        const float o1 = __fadd_rn(__fmul_rn(v, sn), __fmul_rn(vo, cs));
+        if (S.epi == EPI_ROPE_Q) {
+          float* q = S.out_f + (size_t)tk * P.out_ld + (size_t)hh * P.hd;
+          q[i2] = o0;
+          q[i2 + half] = o1;
+        } else {
+          __half* dst = S.out_h + ((size_t)hh * P.ctx + P.B.slot[tk]) * P.hd;
+          dst[i2] = __float2half_rn(o0);
+          dst[i2 + half] = __float2half_rn(o1);
+        }
+      }
+      break;
+  }
+}
+
+__global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ TmmParams P) {
+  extern __shared__ uint8_t tm_dyn[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tm_dyn) + 1023) & ~(uintptr_t)1023);
+  const int Npad = P.Npad;
+  const uint32_t xbytes = 256u * (uint32_t)Npad;
+  uint8_t* a_ring = sm;
+  uint8_t* x_ring = a_ring + TM_AS * TM_A_BYTES;
+  uint8_t* raw_ring = x_ring + TM_AS * xbytes;
+  uint32_t* d_ring = reinterpret_cast<uint32_t*>(raw_ring + TM_RS * TM_RAW_BYTES);
+  __shared__ __align__(8) uint64_t raw_full[TM_RS], raw_empty[TM_RS], a_full[TM_AS], x_full[TM_AS], sfree[TM_AS];
+  __shared__ __align__(8) uint64_t acc_full;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort, s_last;
+  volatile int* abort_f = &s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, sp = blockIdx.y;
+  int si = 0;
+  while (si + 1 < P.nseg && tile >= P.seg[si + 1].tile0) ++si;
+  const TmmSeg& S = P.seg[si];
+  const QView w = S.w;
+  const int row0 = (tile - S.tile0) * TM_ROWS;
+  const int G = P.G;
+  const int g0 = (int)((long long)sp * G / P.nsplit), g1 = (int)((long long)(sp + 1) * G / P.nsplit);
+  const int nsb = g1 - g0, nsub = 4 * nsb;
+  const bool q4 = w.type == Q4K;
+  const int rstride = q4 ? TM_RAW_Q4 : TM_RAW_Q6;
+  // two fp32 accumulators of Npad columns: hi*hi products, and the two correction products
+  const uint32_t ncols = Npad <= 16 ? 32u : Npad <= 32 ? 64u : Npad <= 64 ? 128u : 256u;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < TM_RS; ++i) { mbar_init(&raw_full[i], 32); mbar_init(&raw_empty[i], TM_DQ_WARPS); }
+    for (int i = 0; i < TM_AS; ++i) { mbar_init(&a_full[i], TM_DQ_WARPS); mbar_init(&x_full[i], 1); mbar_init(&sfree[i], 1); }
+    mbar_init(&acc_full, 1);
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(&s_tmem, ncols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  pdl_trigger();
+
+  if (warp == 8) {
+    // ---------------- raw loader: weights do not depend on the previous kernel (no PDL wait)
+    const uint64_t pol = l2_evict_first_policy();
+    for (int k = 0; k < nsb; ++k) {
+      const int slot = k % TM_RS;
+      if (k >= TM_RS && !tm_wait(&raw_empty[slot], (uint32_t)((k / TM_RS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
+        break;
+      const int g = g0 + k;
+      uint8_t* dst = raw_ring + slot * TM_RAW_BYTES;
+      // nibbles / ql (and Q6_K qh): 8 rows per instruction, 4 lanes per 64-byte run
+#pragma unroll 4
+      for (int rb = 0; rb < TM_ROWS / 8; ++rb) {
+        const int r = 8 * rb + (lane >> 2), pc = lane & 3, row = row0 + r;
+        const bool ok = row < w.R;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint8_t* src = ok ? w.base + row_plane_off(w.type, G, row, 0, (size_t)c * 64 * G + (size_t)g * 64 + pc * 16) : w.base;
+          cp_async16(dst + r * rstride + c * 64 + pc * 16, src, ok ? 16u : 0u, pol);
+        }
+        if (!q4) {
+          const uint8_t* src = ok ? w.base + row_plane_off(Q6K, G, row, 1, (size_t)g * 64 + pc * 16) : w.base;
+          cp_async16(dst + r * rstride + 128 + pc * 16, src, ok ? 16u : 0u, pol);
+        }
+      }
+      // Q4_K header / Q6_K scales (16 B per row); Q6_K d: the aligned 4-byte word that holds it
+#pragma unroll
+      for (int rb = 0; rb < TM_ROWS / 32; ++rb) {
+        const int r = 32 * rb + lane, row = row0 + r;
+        const bool ok = row < w.R;
+        const uint8_t* src = ok ? w.base + row_plane_off(w.type, G, row, q4 ? 1 : 2, (size_t)g * 16) : w.base;
+        cp_async16(dst + r * rstride + (q4 ? 128 : 192), src, ok ? 16u : 0u, pol);
+        if (!q4) {
+          const uintptr_t a = ok ? reinterpret_cast<uintptr_t>(w.base + row_plane_off(Q6K, G, row, 3, (size_t)g * 2))
+                                 : reinterpret_cast<uintptr_t>(w.base);
+          cp_async4(d_ring + slot * TM_ROWS + r, reinterpret_cast<const void*>(a & ~(uintptr_t)3), ok ? 4u : 0u);
+        }
+      }
+      cp_async_arrive(&raw_full[slot]);
+    }
+    cp_async_wait_all();
+  } else if (warp == 10) {
+    // ---------------- activation loader
+    if (lane == 0) {
+      pdl_wait();
+      const uint64_t pol = l2_evict_last_policy();
+      int i = 0;
+      for (; i < nsub; ++i) {
+        const int slot = i % TM_AS;
+        if (i >= TM_AS && !tm_wait(&sfree[slot], (uint32_t)((i / TM_AS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
+          break;
+        mbar_arrive_expect_tx(&x_full[slot], xbytes);
+        bulk_g2s(x_ring + slot * xbytes, P.xp + (size_t)(4 * g0 + i) * xp_group_halves(Npad), xbytes, &x_full[slot], pol);
+      }
+      // drain: the last copy into each buffer has completed before the CTA exits
+      for (int j = i - TM_AS < 0 ? 0 : i - TM_AS; j < i; ++j)
+        tm_wait(&x_full[j % TM_AS], (uint32_t)(j / TM_AS) & 1, P.err, KQ_DEV_ERR_DRAIN, abort_f);
+    }
+  } else if (warp == 9) {
+    // ---------------- MMA issue (one thread)
+    if (lane == 0) {
+      const uint32_t idesc = tc_idesc_f16(TM_ROWS, Npad);
+      for (int i = 0; i < nsub; ++i) {
+        const int slot = i % TM_AS;
+        const uint32_t par = (uint32_t)(i / TM_AS) & 1;
+        if (!tm_wait(&a_full[slot], par, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
+        if (!tm_wait(&x_full[slot], par, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(a_ring + slot * TM_A_BYTES), x0 = smem_u32(x_ring + slot * xbytes);
+        const uint32_t a1 = a0 + TM_A_BYTES / 2, x1 = x0 + 128u * (uint32_t)Npad;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t ah = sw128_desc(a0 + 32 * kk), al = sw128_desc(a1 + 32 * kk);
+          const uint64_t bh = sw128_desc(x0 + 32 * kk), bl = sw128_desc(x1 + 32 * kk);
+          tc_mma_f16(tmem + (uint32_t)Npad, al, bh, idesc, (i | kk) ? 1u : 0u);
+          tc_mma_f16(tmem + (uint32_t)Npad, ah, bl, idesc, 1u);
+          tc_mma_f16(tmem, ah, bh, idesc, (i | kk) ? 1u : 0u);
+        }
+        tc_commit(&sfree[slot]);
+      }
+      tc_commit(&acc_full);   // also after a failure: arrives once the issued MMAs are done
+    }
+    __syncwarp();
+  } else {
+    // ---------------- dequantise (warps 0-7): lane = (jh, row) ; 16 rows per warp
+    const int rr = lane & 15, jh = lane >> 4, r = 16 * warp + rr;
+    bool ok = true;
+    for (int k = 0; k < nsb && ok; ++k) {
+      const int slot = k % TM_RS;
+      ok = __all_sync(0xffffffffu, tm_wait(&raw_full[slot], (uint32_t)(k / TM_RS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f));
+      if (!ok) break;
+      const uint8_t* rw = raw_ring + slot * TM_RAW_BYTES + r * rstride;
+      float ds[8], dm[8];
+      if (q4) {
+        const uint4 H = lds128(rw + 128);
+        const float d = h2f_bits(H.x & 0xFFFFu), dmin = h2f_bits(H.x >> 16);
+        const uint32_t sc_lo = H.y & 0x3F3F3F3Fu, mn_lo = H.z & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (H.w & 0x0F0F0F0Fu) | ((H.y >> 2) & 0x30303030u);
+        const uint32_t mn_hi = ((H.w >> 4) & 0x0F0F0F0Fu) | ((H.z >> 2) & 0x30303030u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          ds[e] = __fmul_rn(d, (float)((sc_lo >> (8 * e)) & 0xFFu));
+          dm[e] = __fmul_rn(dmin, (float)((mn_lo >> (8 * e)) & 0xFFu));
+          ds[4 + e] = __fmul_rn(d, (float)((sc_hi >> (8 * e)) & 0xFFu));
+          dm[4 + e] = __fmul_rn(dmin, (float)((mn_hi >> (8 * e)) & 0xFFu));
+        }
+      } else {
+        const uint4 Sc = lds128(rw + 192);   // [u = 2h + jh][k]
+        const uint32_t dw = d_ring[slot * TM_ROWS + r];
+        const float d = h2f_bits(((r & 7) * G + g0 + k) & 1 ? dw >> 16 : dw & 0xFFFFu);
+        const uint32_t s0 = jh ? Sc.y : Sc.x, s1 = jh ? Sc.w : Sc.z;   // h = 0 / h = 1
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          ds[e] = __fmul_rn(d, (float)(int8_t)((s0 >> (8 * e)) & 0xFFu));
+          ds[4 + e] = __fmul_rn(d, (float)(int8_t)((s1 >> (8 * e)) & 0xFFu));
+          dm[e] = dm[4 + e] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const int i = 4 * k + s, as = i % TM_AS;
+        if (i >= TM_AS) {
+          ok = __all_sync(0xffffffffu, tm_wait(&sfree[as], (uint32_t)((i / TM_AS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f));
+          if (!ok) break;
+        }
+        uint8_t* A = a_ring + as * TM_A_BYTES;
+        const int h = s >> 1;
+        uint4 hi, lo;
+        if (q4) {
+          // sub-blocks 2s (low nibbles, columns 0-31) and 2s + 1 (high nibbles, columns 32-63)
+          const uint4 W = lds128(rw + (s & 1) * 64 + h * 32 + jh * 16);
+          const float dsA = ds[2 * s], dmA = dm[2 * s], dsB = ds[2 * s + 1], dmB = dm[2 * s + 1];
+          tm_q4_chunk(W.x & 0x0F0F0F0Fu, W.y & 0x0F0F0F0Fu, dsA, dmA, hi, lo);
+          tm_put(A, r, 2 * jh, hi, lo);
+          tm_q4_chunk(W.z & 0x0F0F0F0Fu, W.w & 0x0F0F0F0Fu, dsA, dmA, hi, lo);
+          tm_put(A, r, 2 * jh + 1, hi, lo);
+          tm_q4_chunk((W.x >> 4) & 0x0F0F0F0Fu, (W.y >> 4) & 0x0F0F0F0Fu, dsB, dmB, hi, lo);
+          tm_put(A, r, 4 + 2 * jh, hi, lo);
+          tm_q4_chunk((W.z >> 4) & 0x0F0F0F0Fu, (W.w >> 4) & 0x0F0F0F0Fu, dsB, dmB, hi, lo);
+          tm_put(A, r, 5 + 2 * jh, hi, lo);
+        } else {
+          // columns 32kk + j of the sub-stage: sub-block k = 2(s & 1) + kk of half h
+          const int n = s & 1;
+          const uint4 QH = lds128(rw + 128 + h * 32 + jh * 16);
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            const int kq = 2 * n + kk;
+            const uint4 QL = lds128(rw + kk * 64 + h * 32 + jh * 16);
+            const int ls = 4 * n, hs = 2 * kq;
+            const float dsc = ds[4 * h + kq];
+            const uint32_t q0 = ((QL.x >> ls) & 0x0F0F0F0Fu) | (((QH.x >> hs) & 0x03030303u) << 4);
+            const uint32_t q1 = ((QL.y >> ls) & 0x0F0F0F0Fu) | (((QH.y >> hs) & 0x03030303u) << 4);
+            const uint32_t q2 = ((QL.z >> ls) & 0x0F0F0F0Fu) | (((QH.z >> hs) & 0x03030303u) << 4);
+            const uint32_t q3 = ((QL.w >> ls) & 0x0F0F0F0Fu) | (((QH.w >> hs) & 0x03030303u) << 4);
+            tm_q6_chunk(q0, q1, dsc, hi, lo);
+            tm_put(A, r, 4 * kk + 2 * jh, hi, lo);
+            tm_q6_chunk(q2, q3, dsc, hi, lo);
+            tm_put(A, r, 4 * kk + 2 * jh + 1, hi, lo);
+          }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[as]);
+      }
+      __syncwarp();
+      if (lane == 0 && ok) mbar_arrive(&raw_empty[slot]);
+    }
+    // ---------------- epilogue (warps 0-7): TMEM lane quarter warp & 3, token half warp >> 2
+    if (ok) ok = tm_wait(&acc_full, 0, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f);
+    const bool good = named_bar_and(1, TM_DQ_WARPS * 32, ok && !*abort_f);
+    if (good) {
+      pdl_wait();
+      tc_fence_after();
+      const int q = warp & 3, rw_ = 32 * q + lane, lrow = row0 + rw_;
+      const bool row_ok = lrow < w.R;
+      const int nc = Npad / 2, c0 = (warp >> 2) * nc;
+      const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
+      const size_t Rtot = (size_t)P.ntiles * TM_ROWS, grow = (size_t)tile * TM_ROWS + rw_;
+      if (P.nsplit > 1) {
+        float* pp = P.part + (size_t)sp * Npad * Rtot + grow;
+        for (int cc = 0; cc < nc; cc += 8) {
+          float v[8], u[8];
+          tc_ld8(tq + (uint32_t)(c0 + cc), v);
+          tc_ld8(tq + (uint32_t)(Npad + c0 + cc), u);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (c0 + cc + e < P.M) __stcg(pp + (size_t)(c0 + cc + e) * Rtot, __fadd_rn(v[e], u[e]));
+        }
+        __threadfence();
+        named_bar(1, TM_DQ_WARPS * 32);
+        if (threadIdx.x == 0) s_last = atomicAdd(&P.ticket[tile], 1) == P.nsplit - 1;
+        named_bar(1, TM_DQ_WARPS * 32);
+        if (s_last) {
+          __threadfence();
+          for (int cc = 0; cc < nc; ++cc) {
+            const int tk = c0 + cc;
+            if (tk >= P.M) break;   // uniform over the warp
+            float v = 0.f;
+            for (int s2 = 0; s2 < P.nsplit; ++s2) v = __fadd_rn(v, __ldcg(P.part + ((size_t)s2 * Npad + tk) * Rtot + grow));
+            const float vo = __shfl_xor_sync(0xffffffffu, v, 1);
+            if (row_ok) tm_epilogue(P, S, lrow, tk, v, vo);
+          }
+          if (threadIdx.x == 0) P.ticket[tile] = 0;
+        }
+      } else {
+        for (int cc = 0; cc < nc; cc += 8) {
+          float v[8], u[8];
+          tc_ld8(tq + (uint32_t)(c0 + cc), v);
+          tc_ld8(tq + (uint32_t)(Npad + c0 + cc), u);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            v[e] = __fadd_rn(v[e], u[e]);
+            const float vo = __shfl_xor_sync(0xffffffffu, v[e], 1);
+            if (c0 + cc + e < P.M && row_ok) tm_epilogue(P, S, lrow, c0 + cc + e, v[e], vo);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, ncols);
+  }
+}
+
+}  // namespace kq

@@ -96,3 +96,41 @@ def test_bad_shapes_rejected(kq):
     m = kq.QMat(12, 8, 256)
     with pytest.raises(ValueError):
         m.upload(np.zeros(100, np.uint8))
+
+
+# The tensor-core GEMM of the batched passes (kq_qmat_matmul, M >= 2): split-precision fp16
+# operands with fp32 accumulation, checked row by row against the oracle's fp32 matvec. Shapes
+# cover one and many row tiles of 128, partial tiles, single and split-K launches, both types.
+MM_SHAPES = [(12, 128, 256), (14, 128, 512), (12, 256, 4096), (14, 1024, 4096), (12, 6144, 4096),
+             (14, 4096, 12288), (12, 200, 1024), (14, 24, 2048), (12, 12288, 4096)]
+
+
+@pytest.mark.parametrize("M", [2, 5, 16, 45, 64])
+@pytest.mark.parametrize("ty,R,Cc", MM_SHAPES)
+def test_matmul_parity(kq, oracle, ty, R, Cc, M):
+    if R * Cc > 4096 * 4096 and M not in (16, 45):
+        pytest.skip("large shapes at two token counts")
+    W = oracle.gen_matrix(R, Cc, ty, 0, 300 + R)
+    X = np.stack([oracle.gen_normal(Cc, 0.0, 1.0, 1, 1000 * M + i) for i in range(M)])
+    m = kq.QMat(ty, R, Cc).upload(W)
+    Y = m.matmul(X)
+    assert Y.shape == (M, R)
+    for i in range(M):
+        ref = oracle.matvec(W, R, Cc, ty, X[i])
+        e = rel_l2(Y[i], ref)
+        assert e < RTOL_L2, (i, e)
+        assert e < TIGHT_L2, (i, e)
+
+
+def test_matmul_rows_independent_of_batch(kq, oracle):
+    """Each token's row depends only on its own activations: the same x gives the same products
+    whatever the other tokens of the batch are (the MMA N dimension only carries tokens)."""
+    R, Cc = 512, 2048
+    W = oracle.gen_matrix(R, Cc, 12, 0, 9)
+    m = kq.QMat(12, R, Cc).upload(W)
+    X = np.stack([oracle.gen_normal(Cc, 0.0, 1.0, 1, 50 + i) for i in range(8)])
+    Y8 = m.matmul(X)
+    X2 = X.copy()
+    X2[1:] = np.stack([oracle.gen_normal(Cc, 0.0, 3.0, 1, 90 + i) for i in range(7)])
+    Y2 = m.matmul(X2)
+    assert np.array_equal(Y8[0], Y2[0])
