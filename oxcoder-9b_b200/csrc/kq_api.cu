@@ -60,6 +60,7 @@ struct DevCtx {
   int nsm = 0;
   int* err = nullptr;       // device error word for matrix-hook calls
   size_t smem_optin = 0;
+  size_t tmm_budget = 0;    // dynamic shared memory of the tensor-core GEMM
 };
 static DevCtx g_dev[16];
 static std::mutex g_dev_mu;
@@ -84,7 +85,12 @@ static int dev_init(int device) {
   for (int tm = 1; tm <= 3; ++tm)
     for (int ri = 0; ri < 3; ++ri)
       CU(cudaFuncSetAttribute(gemv_fn(tm, 1 << ri), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.smem_optin));
-  CU(cudaFuncSetAttribute(k_tmm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tmm_smem(TM_MAXN)));
+  {
+    cudaFuncAttributes fa;
+    CU(cudaFuncGetAttributes(&fa, k_tmm));
+    d.tmm_budget = (size_t)optin - fa.sharedSizeBytes;
+    CU(cudaFuncSetAttribute(k_tmm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.tmm_budget));
+  }
   CU(cudaFuncSetAttribute(k_battn<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BA_SMEM));
   CU(cudaFuncSetAttribute(k_battn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BA_SMEM));
   CU(cudaFuncSetAttribute(k_battn<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BA_SMEM));
@@ -1207,7 +1213,8 @@ static int tmm_tiles(const SegSpec* ss, int nseg) {
   return t;
 }
 // Segments, tiles and split of one GEMM over M tokens (outputs and scratch filled by the caller).
-static void tmm_fill(const SegSpec* ss, int nseg, int M, int nsm, TmmParams& P) {
+static void tmm_fill(const SegSpec* ss, int nseg, int M, int device, TmmParams& P) {
+  const int nsm = g_dev[device].nsm;
   std::memset(&P, 0, sizeof(P));
   int tiles = 0;
   for (int i = 0; i < nseg; ++i) {
@@ -1225,15 +1232,17 @@ static void tmm_fill(const SegSpec* ss, int nseg, int M, int nsm, TmmParams& P) 
   P.M = M;
   P.Npad = (M + 15) & ~15;
   P.nsplit = tmm_split(tiles, P.G, nsm);
+  P.xs = tmm_xs(P.Npad, g_dev[device].tmm_budget);
 }
 static size_t tmm_part_floats(int ntiles, int nsplit, int Npad) {
   return nsplit > 1 ? (size_t)nsplit * Npad * ntiles * TM_ROWS : 0;
 }
 static cudaError_t tmm_launch(const TmmParams& P, cudaStream_t s, bool pdl) {
+  if (P.xs < 1 || P.Npad > TM_MAXN) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)P.ntiles, (unsigned)P.nsplit);
   cfg.blockDim = dim3(TM_THREADS);
-  cfg.dynamicSmemBytes = tmm_smem(P.Npad);
+  cfg.dynamicSmemBytes = tmm_smem(P.Npad, P.xs);
   cfg.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1274,8 +1283,8 @@ static int batch_buffers(kq_model* m) {
   m->bmask = dalloc<unsigned long long>(m, 2 * MM, ok);
   // attention: key splits of up to 32, row groups of BA_ROWS query rows
   const int G = c.n_heads / c.n_kv_heads, rowgroups = (MM_MAXM * G + BA_ROWS - 1) / BA_ROWS;
-  m->b_nsplit = 32;
-  m->bpart = dalloc<float>(m, (size_t)c.n_kv_heads * rowgroups * m->b_nsplit * BA_ROWS * (128 + 2), ok);
+  m->b_nsplit = BA_MAX_SPLIT;
+  m->bpart = dalloc<float>(m, (size_t)c.n_kv_heads * rowgroups * m->b_nsplit * BA_ROWS * BA_PLD, ok);
   m->bticket = dalloc<int>(m, (size_t)c.n_kv_heads * rowgroups, ok);
   // GEMM split-K scratch: the largest of the pass's GEMMs
   const LayerW& w = m->L[0];
@@ -1305,7 +1314,7 @@ static bool batch_supported(const kq_model* m) {
 static int launch_tmm(kq_model* m, const SegSpec* ss, int nseg, const __half* xp, __half* xp_out, int out_ld,
                       const BatchParams& B) {
   TmmParams P;
-  tmm_fill(ss, nseg, B.M, m->nsm, P);
+  tmm_fill(ss, nseg, B.M, m->device, P);
   P.xp = xp;
   P.xp_out = xp_out;
   P.B = B;
@@ -1622,7 +1631,7 @@ extern "C" int kq_qmat_matmul(kq_qmat* a, const float* x, int M, float* y) {
   CU(cudaSetDevice(a->device));
   const SegSpec ss[1] = {{a, EPI_F32, nullptr, nullptr}};
   TmmParams P;
-  tmm_fill(ss, 1, M, g_dev[a->device].nsm, P);
+  tmm_fill(ss, 1, M, a->device, P);
   const size_t pf = tmm_part_floats(P.ntiles, P.nsplit, P.Npad);
   float *xd = nullptr, *yd = nullptr, *part = nullptr;
   __half* xp = nullptr;

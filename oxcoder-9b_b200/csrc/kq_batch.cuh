@@ -77,6 +77,8 @@ constexpr int BA_WARPS = 4;                 // warps per CTA, 16 query rows each
 constexpr int BA_ROWS = 16 * BA_WARPS;      // query rows (token x head) per CTA
 constexpr int BA_LD = 128 + 8;              // padded shared-memory row (halves): conflict-free
 constexpr size_t BA_SMEM = (size_t)2 * 2 * BA_KB * BA_LD * 2;   // K and V blocks, two stages
+constexpr int BA_PLD = 128 + 4;             // partial row: o[128], m, l, padding (16-byte rows)
+constexpr int BA_MAX_SPLIT = 32;
 
 struct BAttnParams {
   const float* q;                    // [M][NH * HD] rotated queries
@@ -88,7 +90,7 @@ struct BAttnParams {
   int n_kv, ctx, npos;               // keys [0, npos) may be attended
   float scale;
   int nsplit, nblk;                  // key blocks per split
-  float* part;                       // [n_kv][rowgroups][nsplit][BA_ROWS][HD + 2]
+  float* part;                       // [n_kv][rowgroups][nsplit][BA_ROWS][BA_PLD]
   int* ticket;                       // [n_kv][rowgroups]
 };
 
@@ -263,16 +265,14 @@ __global__ void __launch_bounds__(BA_WARPS * 32) k_battn(const __grid_constant__
     }
     __syncthreads();   // the stage is refilled by the next iteration's prefetch
   }
-  // ---- partial (o, m, l) of this split: [kv][rg][sp][BA_ROWS][HD + 2]
-  const size_t pbase = (((size_t)kv * rowgroups + rg) * P.nsplit + sp) * BA_ROWS * (HD + 2);
-  float* pa = P.part + pbase + (size_t)(warp * 16 + grp) * (HD + 2);
-  float* pb = pa + 8 * (HD + 2);
+  // ---- partial (o, m, l) of this split: [kv][rg][sp][BA_ROWS][BA_PLD]
+  const size_t pbase = (((size_t)kv * rowgroups + rg) * P.nsplit + sp) * BA_ROWS * BA_PLD;
+  float* pa = P.part + pbase + (size_t)(warp * 16 + grp) * BA_PLD;
+  float* pb = pa + 8 * BA_PLD;
 #pragma unroll
   for (int n = 0; n < 16; ++n) {
-    __stcg(pa + 8 * n + 2 * t4, o[n][0]);
-    __stcg(pa + 8 * n + 2 * t4 + 1, o[n][1]);
-    __stcg(pb + 8 * n + 2 * t4, o[n][2]);
-    __stcg(pb + 8 * n + 2 * t4 + 1, o[n][3]);
+    __stcg(reinterpret_cast<float2*>(pa + 8 * n + 2 * t4), make_float2(o[n][0], o[n][1]));
+    __stcg(reinterpret_cast<float2*>(pb + 8 * n + 2 * t4), make_float2(o[n][2], o[n][3]));
   }
   if (t4 == 0) {
     __stcg(pa + HD, mA); __stcg(pa + HD + 1, lA);
@@ -284,22 +284,41 @@ __global__ void __launch_bounds__(BA_WARPS * 32) k_battn(const __grid_constant__
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // ---- merge the splits in order; packed fp16 hi / lo output for the o GEMM
-  const size_t mb = ((size_t)kv * rowgroups + rg) * P.nsplit * BA_ROWS * (HD + 2);
-  for (int e = tid; e < BA_ROWS * HD; e += BA_WARPS * 32) {
-    const int lr = e / HD, d = e % HD, qr = rg * BA_ROWS + lr;
-    if (qr >= nrows) break;
+  // ---- merge the splits in order: per-row weights exp(m_s - max) and the sum L first, then
+  // float4 columns (the K/V stages are free: their copies all completed in the loop)
+  float* fac = reinterpret_cast<float*>(ba_sm);   // [nsplit][BA_ROWS]
+  float* lsum = fac + P.nsplit * BA_ROWS;         // [BA_ROWS]
+  const float* mbp = P.part + ((size_t)kv * rowgroups + rg) * P.nsplit * BA_ROWS * BA_PLD;
+  if (tid < BA_ROWS) {
     float Mx = -INFINITY;
-    for (int s2 = 0; s2 < P.nsplit; ++s2) Mx = fmaxf(Mx, __ldcg(P.part + mb + ((size_t)s2 * BA_ROWS + lr) * (HD + 2) + HD));
-    float L = 0.f, O = 0.f;
+    for (int s2 = 0; s2 < P.nsplit; ++s2) Mx = fmaxf(Mx, __ldcg(mbp + ((size_t)s2 * BA_ROWS + tid) * BA_PLD + HD));
+    float L = 0.f;
     for (int s2 = 0; s2 < P.nsplit; ++s2) {
-      const float* pr = P.part + mb + ((size_t)s2 * BA_ROWS + lr) * (HD + 2);
+      const float* pr = mbp + ((size_t)s2 * BA_ROWS + tid) * BA_PLD;
       const float ms = __ldcg(pr + HD);
       const float wgt = ms == -INFINITY ? 0.f : expf(__fsub_rn(ms, Mx));
+      fac[s2 * BA_ROWS + tid] = wgt;
       L = fmaf(wgt, __ldcg(pr + HD + 1), L);
-      O = fmaf(wgt, __ldcg(pr + d), O);
     }
-    xp_store(P.out_xp, P.Npad, qr / G, (kv * G + qr % G) * HD + d, __fdiv_rn(O, L));
+    lsum[tid] = L;
+  }
+  __syncthreads();
+  for (int e = tid; e < BA_ROWS * (HD / 4); e += BA_WARPS * 32) {
+    const int lr = e / (HD / 4), d4 = e % (HD / 4), qr = rg * BA_ROWS + lr;
+    if (qr >= nrows) break;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int s2 = 0; s2 < P.nsplit; ++s2) {
+      const float wgt = fac[s2 * BA_ROWS + lr];
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(mbp + ((size_t)s2 * BA_ROWS + lr) * BA_PLD) + d4);
+      O.x = fmaf(wgt, v.x, O.x); O.y = fmaf(wgt, v.y, O.y); O.z = fmaf(wgt, v.z, O.z); O.w = fmaf(wgt, v.w, O.w);
+    }
+    const float L = lsum[lr];
+    const int col = (kv * G + qr % G) * HD + 4 * d4, tk = qr / G;
+    xp_store(P.out_xp, P.Npad, tk, col, __fdiv_rn(O.x, L));
+    xp_store(P.out_xp, P.Npad, tk, col + 1, __fdiv_rn(O.y, L));
+    xp_store(P.out_xp, P.Npad, tk, col + 2, __fdiv_rn(O.z, L));
+    xp_store(P.out_xp, P.Npad, tk, col + 3, __fdiv_rn(O.w, L));
   }
   if (tid == 0) P.ticket[kv * rowgroups + rg] = 0;
 }

@@ -20,7 +20,8 @@
 //              (row strides 144 B / 208 B = an odd number of 16-byte units: conflict-free reads)
 //   warp 9     TMEM allocation; lane 0 issues tcgen05.mma (3 x 4 per 64-column sub-stage) and
 //              commits each sub-stage's completion to the barrier that frees its A and X buffers
-//   warp 10    activation loader: one cp.async.bulk per 64-column sub-stage of the packed X
+//   warp 10    activation loader: one cp.async.bulk per 64-column sub-stage of the packed X, into
+//              its own ring (as deep as shared memory allows), freed by its own MMA commits
 // Every wait is bounded; on a timeout the CTA records the error, stops issuing work, drains what
 // it issued and frees its tensor memory before it exits.
 #pragma once
@@ -152,12 +153,14 @@ struct BatchParams {                   // per-token data of a pass
 constexpr int TM_ROWS = 128;                       // weight rows per CTA (the MMA's M)
 constexpr int TM_DQ_WARPS = 8;                     // dequantising / epilogue warps
 constexpr int TM_THREADS = (TM_DQ_WARPS + 3) * 32; // + raw loader, MMA, activation loader
-constexpr int TM_RS = 3;                           // raw super-block stages in flight
-constexpr int TM_AS = 2;                           // A / X sub-stage buffers (64 columns each)
+constexpr int TM_RS = 2;                           // raw super-block stages in flight
+constexpr int TM_AS = 3;                           // A sub-stage buffers (64 columns each)
+constexpr int TM_XS_MAX = 8;                       // activation sub-stage buffers (fill the rest)
 constexpr int TM_RAW_Q4 = 144, TM_RAW_Q6 = 208;    // raw row strides (odd multiples of 16 B)
 constexpr int TM_RAW_BYTES = TM_ROWS * TM_RAW_Q6;  // one raw stage
 constexpr int TM_A_BYTES = 2 * TM_ROWS * 128;      // hi + lo planes of one A sub-stage
 constexpr int TM_MAXN = 128;                       // tokens per GEMM (Npad)
+static_assert(TM_A_BYTES % 1024 == 0 && TM_RAW_BYTES % 1024 == 0, "rings must keep 1024-byte alignment");
 
 struct TmmSeg {
   QView w;
@@ -171,6 +174,7 @@ struct TmmParams {
   int nseg, ntiles;    // row tiles over all segments
   int C, G, nsplit;    // K = C columns, G super-blocks, split over nsplit CTAs
   int M, Npad;         // tokens, MMA N (multiple of 16)
+  int xs;              // activation ring stages (1..TM_XS_MAX), see tmm_smem
   const __half* xp;    // packed activations (xp_off layout)
   __half* xp_out;      // SWIGLU: packed input of the next GEMM (same Npad)
   BatchParams B;
@@ -183,9 +187,17 @@ struct TmmParams {
   int* err;
 };
 
-__host__ __device__ inline size_t tmm_smem(int Npad) {
-  return 1024 + (size_t)TM_AS * TM_A_BYTES + (size_t)TM_AS * 256 * Npad + (size_t)TM_RS * TM_RAW_BYTES +
-         (size_t)TM_RS * TM_ROWS * 4;
+// Dynamic shared memory: 1024-byte alignment slack, A ring, raw ring, `xs` activation stages of
+// 256 * Npad bytes, Q6_K d words (the rings start on 1024-byte boundaries).
+__host__ __device__ inline size_t tmm_smem_fixed() {
+  return 1024 + (size_t)TM_AS * TM_A_BYTES + (size_t)TM_RS * TM_RAW_BYTES + (size_t)TM_RS * TM_ROWS * 4;
+}
+__host__ __device__ inline size_t tmm_smem(int Npad, int xs) { return tmm_smem_fixed() + (size_t)xs * 256 * Npad; }
+// The deepest activation ring that fits `budget` bytes of dynamic shared memory.
+__host__ __device__ inline int tmm_xs(int Npad, size_t budget) {
+  const size_t room = budget > tmm_smem_fixed() ? budget - tmm_smem_fixed() : 0;
+  const int xs = (int)(room / ((size_t)256 * Npad));
+  return xs < 1 ? 0 : xs > TM_XS_MAX ? TM_XS_MAX : xs;
 }
 
 __device__ __forceinline__ uint64_t tm_clock_ns() {
@@ -199,6 +211,10 @@ __device__ __forceinline__ uint64_t tm_clock_ns() {
 constexpr uint64_t TM_WAIT_NS = 2000000000ull;
 __device__ __forceinline__ bool tm_wait(uint64_t* bar, uint32_t parity, int* err, int bit, volatile int* abort_f) {
   uint64_t t0 = 0;
+  // non-suspending probes first: the pipeline's hand-offs are short, and a suspended thread
+  // is woken late
+  for (int it = 0; it < 4096; ++it)
+    if (mbar_test_wait(bar, parity)) return true;
   for (uint32_t it = 0; it < KQ_WAIT_LIMIT; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255) == 255) {
@@ -297,11 +313,13 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tm_dyn) + 1023) & ~(uintptr_t)1023);
   const int Npad = P.Npad;
   const uint32_t xbytes = 256u * (uint32_t)Npad;
+  const int XS = P.xs;
   uint8_t* a_ring = sm;
-  uint8_t* x_ring = a_ring + TM_AS * TM_A_BYTES;
-  uint8_t* raw_ring = x_ring + TM_AS * xbytes;
-  uint32_t* d_ring = reinterpret_cast<uint32_t*>(raw_ring + TM_RS * TM_RAW_BYTES);
-  __shared__ __align__(8) uint64_t raw_full[TM_RS], raw_empty[TM_RS], a_full[TM_AS], x_full[TM_AS], sfree[TM_AS];
+  uint8_t* raw_ring = a_ring + TM_AS * TM_A_BYTES;
+  uint8_t* x_ring = raw_ring + TM_RS * TM_RAW_BYTES;   // 1024-aligned (SWIZZLE_128B atoms)
+  uint32_t* d_ring = reinterpret_cast<uint32_t*>(x_ring + (size_t)XS * xbytes);
+  __shared__ __align__(8) uint64_t raw_full[TM_RS], raw_empty[TM_RS], a_full[TM_AS], sfree[TM_AS];
+  __shared__ __align__(8) uint64_t x_full[TM_XS_MAX], x_free[TM_XS_MAX];
   __shared__ __align__(8) uint64_t acc_full;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_last;
@@ -324,7 +342,8 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < TM_RS; ++i) { mbar_init(&raw_full[i], 32); mbar_init(&raw_empty[i], TM_DQ_WARPS); }
-    for (int i = 0; i < TM_AS; ++i) { mbar_init(&a_full[i], TM_DQ_WARPS); mbar_init(&x_full[i], 1); mbar_init(&sfree[i], 1); }
+    for (int i = 0; i < TM_AS; ++i) { mbar_init(&a_full[i], TM_DQ_WARPS); mbar_init(&sfree[i], 1); }
+    for (int i = 0; i < XS; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_free[i], 1); }
     mbar_init(&acc_full, 1);
     s_abort = 0;
     fence_mbar_init();
@@ -386,37 +405,40 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
       const uint64_t pol = l2_evict_last_policy();
       int i = 0;
       for (; i < nsub; ++i) {
-        const int slot = i % TM_AS;
-        if (i >= TM_AS && !tm_wait(&sfree[slot], (uint32_t)((i / TM_AS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
+        const int slot = i % XS;
+        if (i >= XS && !tm_wait(&x_free[slot], (uint32_t)((i / XS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
           break;
         mbar_arrive_expect_tx(&x_full[slot], xbytes);
         bulk_g2s(x_ring + slot * xbytes, P.xp + (size_t)(4 * g0 + i) * xp_group_halves(Npad), xbytes, &x_full[slot], pol);
       }
       // drain: the last copy into each buffer has completed before the CTA exits
-      for (int j = i - TM_AS < 0 ? 0 : i - TM_AS; j < i; ++j)
-        tm_wait(&x_full[j % TM_AS], (uint32_t)(j / TM_AS) & 1, P.err, KQ_DEV_ERR_DRAIN, abort_f);
+      for (int j = i - XS < 0 ? 0 : i - XS; j < i; ++j)
+        tm_wait(&x_full[j % XS], (uint32_t)(j / XS) & 1, P.err, KQ_DEV_ERR_DRAIN, abort_f);
     }
   } else if (warp == 9) {
     // ---------------- MMA issue (one thread)
     if (lane == 0) {
       const uint32_t idesc = tc_idesc_f16(TM_ROWS, Npad);
+      // descriptors of the ring bases; a sub-stage / K step only moves the start address field
+      // (16-byte units, addresses < 256 KiB so the 14-bit field never carries)
+      const uint64_t dA = sw128_desc(smem_u32(a_ring)), dX = sw128_desc(smem_u32(x_ring));
+      const uint64_t a_lo_off = (TM_A_BYTES / 2) >> 4, x_lo_off = (128u * (uint32_t)Npad) >> 4;
       for (int i = 0; i < nsub; ++i) {
-        const int slot = i % TM_AS;
-        const uint32_t par = (uint32_t)(i / TM_AS) & 1;
-        if (!tm_wait(&a_full[slot], par, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
-        if (!tm_wait(&x_full[slot], par, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
+        const int slot = i % TM_AS, xsl = i % XS;
+        if (!tm_wait(&a_full[slot], (uint32_t)(i / TM_AS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
+        if (!tm_wait(&x_full[xsl], (uint32_t)(i / XS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(a_ring + slot * TM_A_BYTES), x0 = smem_u32(x_ring + slot * xbytes);
-        const uint32_t a1 = a0 + TM_A_BYTES / 2, x1 = x0 + 128u * (uint32_t)Npad;
+        const uint64_t a0 = dA + (uint64_t)((slot * TM_A_BYTES) >> 4), x0 = dX + (uint64_t)((xsl * xbytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ah = sw128_desc(a0 + 32 * kk), al = sw128_desc(a1 + 32 * kk);
-          const uint64_t bh = sw128_desc(x0 + 32 * kk), bl = sw128_desc(x1 + 32 * kk);
+          const uint64_t ah = a0 + 2 * kk, al = ah + a_lo_off;   // + 32 bytes per K step
+          const uint64_t bh = x0 + 2 * kk, bl = bh + x_lo_off;
           tc_mma_f16(tmem + (uint32_t)Npad, al, bh, idesc, (i | kk) ? 1u : 0u);
           tc_mma_f16(tmem + (uint32_t)Npad, ah, bl, idesc, 1u);
           tc_mma_f16(tmem, ah, bh, idesc, (i | kk) ? 1u : 0u);
         }
         tc_commit(&sfree[slot]);
+        tc_commit(&x_free[xsl]);
       }
       tc_commit(&acc_full);   // also after a failure: arrives once the issued MMAs are done
     }
