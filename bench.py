@@ -187,6 +187,24 @@ def spec_bench(e, vocab, steps, warmup):
     return out
 
 
+def prefill_bench(e, vocab, n, reps=3):
+    """Prefill of an n-token prompt of uniform random ids (seed 1) through kq_feed_batch (batched
+    tensor-core passes of up to 128 tokens), host-timed around the synchronising call: the median
+    of `reps` runs after one warm-up, as prompt tokens per second."""
+    import numpy as np
+    ids = np.random.default_rng(1).integers(0, vocab, n).astype(np.int32)
+    e.reset()
+    e.feed_batch(ids, 0)
+    ts = []
+    for _ in range(reps):
+        e.reset()
+        t0 = time.perf_counter()
+        e.feed_batch(ids, 0)
+        ts.append(time.perf_counter() - t0)
+    ms = 1e3 * sorted(ts)[len(ts) // 2]
+    return {"prompt": n, "ms": ms, "tok_s": n / (ms / 1e3)}
+
+
 def run_profile_mode(args):
     """decode-only: fill the config-2 model (optionally fewer layers), W + K device-resident
     decode steps at ctx 4K. gemv-only: the config-0 Q4_K GEMV over 16 rotating copies."""
@@ -194,6 +212,11 @@ def run_profile_mode(args):
     if args.mode == "spec":
         e = kq.Engine(kq.Config.default(ctx=CTX, n_layers=args.layers), seed=0)
         print(json.dumps({"mode": "spec", **spec_bench(e, e.vocab, args.steps, args.warmup)}))
+        return 0
+    if args.mode == "prefill":
+        e = kq.Engine(kq.Config.default(ctx=CTX, n_layers=args.layers), seed=0)
+        print(json.dumps({"mode": "prefill", "p512": prefill_bench(e, e.vocab, 512, args.steps),
+                          "p2048": prefill_bench(e, e.vocab, 2048, 1)}))
         return 0
     if args.mode == "gemv-only":
         mats = [kq.QMat(12, 12288, 4096).fill_synthetic(0, 1000 + i) for i in range(16)]
@@ -218,7 +241,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=32, help="decode-only: layers of the model (small ncu captures)")
-    ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only", "spec"],
+    ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only", "spec", "prefill"],
                     help="decode-only / gemv-only: the small commands the ncu captures in profiles/ run")
     args = ap.parse_args()
     if args.mode != "full":
@@ -281,6 +304,7 @@ def main():
         e2e_s = float(t.item())
     e2e_tok_s = world * K / e2e_s
     spec = spec_bench(e, e.vocab, 8, 3)
+    prefill = prefill_bench(e, e.vocab, 512)
     e.close()
 
     # ---- the dominant kernel: config-0 Q4_K GEMV over 16 rotating weight copies (453 MB > L2)
@@ -323,6 +347,8 @@ def main():
             "clocks": clk.summary(),
             "spec_verify_tok_s": spec["tree"]["verified_tok_s"] * world,
             "spec": spec,
+            "prefill_tok_s": prefill["tok_s"] * world,
+            "prefill": prefill,
             "cpu_baseline": cb,
         }
         print(json.dumps(line), flush=True)

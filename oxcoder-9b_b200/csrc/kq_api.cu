@@ -1058,13 +1058,48 @@ static int run_one(kq_model* m, int tok, int pos, bool head) {
 extern "C" int kq_feed(kq_model* m, int tok, int pos) { return run_one(m, tok, pos, false); }
 extern "C" int kq_step(kq_model* m, int tok, int pos) { return run_one(m, tok, pos, true); }
 
-extern "C" int kq_feed_batch(kq_model* m, const int32_t* toks, int n, int pos) {
-  if (!toks || n < 0) return set_err(KQ_ERR_ARG, "bad token batch");
-  for (int i = 0; i < n; ++i) {
-    const int rc = kq_feed(m, toks[i], pos + i);
-    if (rc < 0) return rc;
+static int verify_buffers(kq_model* m);
+static int batch_buffers(kq_model* m);
+static bool batch_supported(const kq_model* m);
+static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int pos, const int* depth,
+                       const unsigned long long (*anc)[2], bool head = true);
+
+// Ancestor masks of a linear chain of MM_MAXM tokens: token j attends to tokens 0..j.
+struct ChainMasks {
+  int depth[MM_MAXM];
+  unsigned long long anc[MM_MAXM][2];
+  ChainMasks() {
+    for (int j = 0; j < MM_MAXM; ++j) {
+      depth[j] = j;
+      anc[j][0] = j >= 63 ? ~0ull : ((1ull << (j + 1)) - 1);
+      anc[j][1] = j < 64 ? 0ull : j == 127 ? ~0ull : ((1ull << (j - 63)) - 1);
+    }
   }
-  return KQ_OK;
+};
+
+// Prefill (Engine.feed_batch, gpu4.py:109-110 feeds token by token): chunks of up to MM_MAXM
+// tokens run as batched passes on the tensor cores, each chunk a linear chain whose token j
+// attends to the positions below the chunk and to chunk tokens 0..j; K/V only, no head. A single
+// token, and configurations the batched pass does not cover, take the decode step.
+extern "C" int kq_feed_batch(kq_model* m, const int32_t* toks, int n, int pos) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (!toks || n < 0 || pos < 0) return set_err(KQ_ERR_ARG, "bad token batch");
+  for (int i = 0; i < n; ++i)
+    if (toks[i] < 0 || toks[i] >= m->c.vocab) return set_err(KQ_ERR_ARG, "Invalid token");
+  if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "prompt runs past the context");
+  if (n < 2 || m->verify_seq || !batch_supported(m)) {
+    for (int i = 0; i < n; ++i)
+      if ((rc = kq_feed(m, toks[i], pos + i)) < 0) return rc;
+    return KQ_OK;
+  }
+  if ((rc = ensure_graphs(m)) || (rc = verify_buffers(m)) || (rc = batch_buffers(m))) return rc;
+  static const ChainMasks chain;
+  for (int c0 = 0; c0 < n; c0 += MM_MAXM)
+    if ((rc = verify_pass(m, toks + c0, 0, std::min(MM_MAXM, n - c0), pos + c0, chain.depth, chain.anc, false)))
+      return rc;
+  CU(cudaStreamSynchronize(m->stream));
+  return check_dev_err(m);
 }
 
 extern "C" int kq_generate(kq_model* m, const int32_t* ids, int n_ids, int n, int32_t* out) {
@@ -1369,9 +1404,11 @@ static int launch_battn(kq_model* m, int layer, int npos, const BatchParams& B) 
 }
 
 // One batched pass over nodes [b0, b1) of a verified tree (their ancestors are in this or an
-// earlier pass): logits to vlogits rows b0.., argmax ids to out_ids[b0..].
+// earlier pass): node i's K/V to slot pos + i, rotary position pos + depth[i], attention to the
+// slots below pos and its ancestors (anc, bits relative to pos). With `head`: logits to vlogits
+// rows b0.., argmax ids to out_ids[b0..]; without (prefill): the K/V cache only.
 static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int pos, const int* depth,
-                       const unsigned long long (*anc)[2]) {
+                       const unsigned long long (*anc)[2], bool head) {
   const kq_config& c = m->c;
   const int M = b1 - b0;
   std::vector<int> tk(M), sl(M), rp(M);
@@ -1406,6 +1443,7 @@ static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int p
     SegSpec sd[1] = {{w.down, EPI_F32, m->by, nullptr}};
     if ((rc = launch_tmm(m, sd, 1, m->bxf, nullptr, c.dim, B))) return rc;
   }
+  if (!head) return KQ_OK;
   if ((rc = launch_bnorm(m, M, false, m->out_norm, true))) return rc;
   const size_t V = (size_t)c.vocab;
   SegSpec sh[1] = {{m->out, EPI_F32, m->vlogits + (size_t)b0 * V, nullptr}};

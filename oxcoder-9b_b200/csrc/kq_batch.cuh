@@ -1,5 +1,5 @@
-// kq_batch.cuh -- the non-GEMM kernels of a forward pass over M <= 64 tokens at once (the
-// verification pass over a draft tree); the GEMMs are k_tmm (kq_tmm.cuh).
+// kq_batch.cuh -- the non-GEMM kernels of a forward pass over M <= 128 tokens at once (the
+// verification pass over a draft tree, a prefill chunk); the GEMMs are k_tmm (kq_tmm.cuh).
 //
 //  * k_bnorm: per token, the residual add and fp64-sum RMS norm (or the embedding row), writing
 //    h and the packed hi/lo fp16 input of the next GEMM.
@@ -20,7 +20,7 @@
 
 namespace kq {
 
-constexpr int MM_MAXM = 64;            // tokens per verification pass
+constexpr int MM_MAXM = 128;           // tokens per batched pass (verification, prefill)
 
 // ------------------------------------------------------------------------------ norm / embedding
 struct BNormParams {
