@@ -1375,7 +1375,7 @@ static int launch_bnorm(kq_model* m, int M, bool embed, const float* gamma, bool
   P.h = m->bh; P.y = add ? m->by : nullptr; P.gamma = gamma; P.eps = m->c.eps;
   P.xp = m->bxd; P.Npad = (M + 15) & ~15;
   P.vocab = m->c.vocab; P.err = m->err;
-  CU(launch_pdl(k_bnorm, dim3((unsigned)M), dim3(256), 0, m->stream, P));
+  CU(launch_pdl(k_bnorm, dim3((unsigned)M), dim3(BN_THREADS), 0, m->stream, P));
   return KQ_OK;
 }
 

@@ -36,39 +36,68 @@ struct BNormParams {
   int vocab;
   int* err;
 };
-__global__ void __launch_bounds__(256) k_bnorm(const __grid_constant__ BNormParams P) {
+constexpr int BN_THREADS = 512;
+// One CTA per token; thread t owns the 8-column chunks t, t + 512, ... (float4 loads, and one
+// 16-byte hi and one 16-byte lo store of the packed layout per chunk).
+__global__ void __launch_bounds__(BN_THREADS) k_bnorm(const __grid_constant__ BNormParams P) {
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  __shared__ double red[8];
+  __shared__ double red[BN_THREADS / 32];
   pdl_wait();
   pdl_trigger();
   float* h = P.h + (size_t)t * P.D;
-  double acc = 0.0;
+  int tok = 0;
   if (P.emb.base) {
-    int tok = P.tok[t];
+    tok = P.tok[t];
     if (tok < 0 || tok >= P.vocab) {
       if (tid == 0) atomicOr(P.err, KQ_DEV_ERR_BAD_TOKEN);
       tok = 0;
     }
-    for (int i = tid; i < P.D; i += 256) {
-      const float v = dequant_elem(P.emb, tok, i);
-      h[i] = v;
-      acc = __dadd_rn(acc, __dmul_rn((double)v, (double)v));
+  }
+  double acc = 0.0;
+  const int nch = P.D / 8;
+  for (int c = tid; c < nch; c += BN_THREADS) {
+    float v[8];
+    if (P.emb.base) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = dequant_elem(P.emb, tok, 8 * c + e);
+    } else {
+      const float4 a0 = reinterpret_cast<const float4*>(h)[2 * c], a1 = reinterpret_cast<const float4*>(h)[2 * c + 1];
+      v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w; v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+      if (P.y) {
+        const float4* y4 = reinterpret_cast<const float4*>(P.y + (size_t)t * P.D);
+        const float4 b0 = y4[2 * c], b1 = y4[2 * c + 1];
+        v[0] = __fadd_rn(v[0], b0.x); v[1] = __fadd_rn(v[1], b0.y); v[2] = __fadd_rn(v[2], b0.z); v[3] = __fadd_rn(v[3], b0.w);
+        v[4] = __fadd_rn(v[4], b1.x); v[5] = __fadd_rn(v[5], b1.y); v[6] = __fadd_rn(v[6], b1.z); v[7] = __fadd_rn(v[7], b1.w);
+      }
     }
-  } else {
-    for (int i = tid; i < P.D; i += 256) {
-      const float v = P.y ? __fadd_rn(h[i], P.y[(size_t)t * P.D + i]) : h[i];
-      h[i] = v;
-      acc = __dadd_rn(acc, __dmul_rn((double)v, (double)v));
-    }
+    reinterpret_cast<float4*>(h)[2 * c] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(h)[2 * c + 1] = make_float4(v[4], v[5], v[6], v[7]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc = __dadd_rn(acc, __dmul_rn((double)v[e], (double)v[e]));
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (lane == 0) red[warp] = acc;
   __syncthreads();
   double tot = 0.0;
-  for (int w = 0; w < 8; ++w) tot += red[w];
+  for (int w = 0; w < BN_THREADS / 32; ++w) tot += red[w];
   const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / (double)P.D), P.eps)));
-  for (int i = tid; i < P.D; i += 256) xp_store(P.xp, P.Npad, t, i, __fmul_rn(__fmul_rn(h[i], s), P.gamma[i]));
+  for (int c = tid; c < nch; c += BN_THREADS) {
+    const float4 a0 = reinterpret_cast<const float4*>(h)[2 * c], a1 = reinterpret_cast<const float4*>(h)[2 * c + 1];
+    const float4 g0 = reinterpret_cast<const float4*>(P.gamma)[2 * c], g1 = reinterpret_cast<const float4*>(P.gamma)[2 * c + 1];
+    const float x[8] = {__fmul_rn(__fmul_rn(a0.x, s), g0.x), __fmul_rn(__fmul_rn(a0.y, s), g0.y),
+                        __fmul_rn(__fmul_rn(a0.z, s), g0.z), __fmul_rn(__fmul_rn(a0.w, s), g0.w),
+                        __fmul_rn(__fmul_rn(a1.x, s), g1.x), __fmul_rn(__fmul_rn(a1.y, s), g1.y),
+                        __fmul_rn(__fmul_rn(a1.z, s), g1.z), __fmul_rn(__fmul_rn(a1.w, s), g1.w)};
+    uint4 hi, lo;
+    tm_split(x[0], x[1], hi.x, lo.x);
+    tm_split(x[2], x[3], hi.y, lo.y);
+    tm_split(x[4], x[5], hi.z, lo.z);
+    tm_split(x[6], x[7], hi.w, lo.w);
+    const size_t o = xp_off(P.Npad, t, 8 * c);   // 8 consecutive halves
+    *reinterpret_cast<uint4*>(P.xp + o) = hi;
+    *reinterpret_cast<uint4*>(P.xp + o + (size_t)64 * P.Npad) = lo;
+  }
 }
 
 // ------------------------------------------------------------------------------ tree attention

@@ -5,20 +5,23 @@
 // Precision. The Kindi CPU path dequantises every weight in fp32 (w = (d*sc)*q - dmin*mn, or
 // (d*scale)*(q6 - 32); q4kernels.h:19-30) and accumulates in fp32. Here each weight w and each
 // activation x is carried as two fp16 numbers, hi = fp16(v) and lo = fp16(v - hi) (about 22
-// significant bits), and every 16-column K step issues three MMAs into two fp32 TMEM
-// accumulators: hi(w)*hi(x) into one, the corrections lo(w)*hi(x) + hi(w)*lo(x) into a second (so
-// they are not rounded against the large partial sums), added in the epilogue. The dropped lo*lo
-// term is below 2^-22 of the product, so the result is within a few fp32 roundings of the fp32
-// dot product.
+// significant bits), and every 16-column K step issues two MMAs: hi(w) * [hi(x); lo(x)] (the
+// activation stage stacks the hi and the lo token rows, so one MMA of N = 2 Npad forms both
+// products) and lo(w) * hi(x), each product in its own fp32 TMEM accumulator (the small
+// corrections are not rounded against the large partial sums) and summed in the epilogue. The
+// dropped lo*lo term is below 2^-22 of the product, so the result is within a few fp32 roundings
+// of the fp32 dot product. The weights' hi/lo pairs live in tensor memory (the MMA's A operand),
+// written by the dequantising warps with tcgen05.st; only the raw bytes and the activations pass
+// through shared memory.
 //
 // CTA = 128 weight rows (16 tiles of the kq layout) x all tokens x a contiguous range of super-
 // blocks (split-K over CTAs; the last CTA of a row tile sums the fp32 partials in split order, so
 // the result does not depend on which CTA finishes last). Warp roles (352 threads):
-//   warps 0-7  dequantise: raw super-block bytes (shared memory) -> hi/lo fp16 A tiles of 64
-//              columns in the SWIZZLE_128B K-major layout the MMA reads; then the epilogue
+//   warps 0-7  dequantise: raw super-block bytes (shared memory) -> hi/lo fp16 A sub-stages of
+//              64 columns in tensor memory (thread = weight row); then the epilogue
 //   warp 8     raw loader: cp.async of each super-block's bytes for the 128 rows into a padded ring
 //              (row strides 144 B / 208 B = an odd number of 16-byte units: conflict-free reads)
-//   warp 9     TMEM allocation; lane 0 issues tcgen05.mma (3 x 4 per 64-column sub-stage) and
+//   warp 9     TMEM allocation; lane 0 issues tcgen05.mma (2 x 4 per 64-column sub-stage) and
 //              commits each sub-stage's completion to the barrier that frees its A and X buffers
 //   warp 10    activation loader: one cp.async.bulk per 64-column sub-stage of the packed X, into
 //              its own ring (as deep as shared memory allows), freed by its own MMA commits
@@ -153,14 +156,23 @@ struct BatchParams {                   // per-token data of a pass
 constexpr int TM_ROWS = 128;                       // weight rows per CTA (the MMA's M)
 constexpr int TM_DQ_WARPS = 8;                     // dequantising / epilogue warps
 constexpr int TM_THREADS = (TM_DQ_WARPS + 3) * 32; // + raw loader, MMA, activation loader
-constexpr int TM_RS = 2;                           // raw super-block stages in flight
-constexpr int TM_AS = 3;                           // A sub-stage buffers (64 columns each)
+constexpr int TM_RS = 4;                           // raw super-block stages in flight
+constexpr int TM_AS = 3;                           // A sub-stages (128 columns each) in tensor memory, at most
 constexpr int TM_XS_MAX = 8;                       // activation sub-stage buffers (fill the rest)
 constexpr int TM_RAW_Q4 = 144, TM_RAW_Q6 = 208;    // raw row strides (odd multiples of 16 B)
 constexpr int TM_RAW_BYTES = TM_ROWS * TM_RAW_Q6;  // one raw stage
-constexpr int TM_A_BYTES = 2 * TM_ROWS * 128;      // hi + lo planes of one A sub-stage
 constexpr int TM_MAXN = 128;                       // tokens per GEMM (Npad)
-static_assert(TM_A_BYTES % 1024 == 0 && TM_RAW_BYTES % 1024 == 0, "rings must keep 1024-byte alignment");
+// A sub-stage is 128 K columns (half a super-block). Tensor memory (512 columns of 128 lanes x
+// 32 bits): accumulators first, hi(w) * hi(x) in columns [0, Npad) and the corrections
+// hi(w) * lo(x) + lo(w) * hi(x) in [Npad, 2 Npad) (the first MMA of a K step has N = 2 Npad: the
+// activation stage holds the hi token rows then the lo rows); then A sub-stages of 128 columns
+// from tmm_acol(Npad): 64 columns of hi fp16 pairs, 64 of lo, lane = weight row, column c = K
+// elements 2c, 2c + 1. Npad <= 64: 3 A stages; Npad <= 128: 2.
+constexpr uint32_t TM_TMEM_COLS = 512, TM_ASTAGE_COLS = 128;
+__host__ __device__ constexpr uint32_t tmm_acol(int Npad) { return Npad <= 64 ? 128u : 256u; }
+__host__ __device__ constexpr int tmm_as(int Npad) { return Npad <= 64 ? 3 : 2; }
+static_assert(128 + 3 * TM_ASTAGE_COLS <= TM_TMEM_COLS && 256 + 2 * TM_ASTAGE_COLS <= TM_TMEM_COLS, "tensor memory plan");
+static_assert(TM_RAW_BYTES % 1024 == 0, "rings must keep 1024-byte alignment");
 
 struct TmmSeg {
   QView w;
@@ -187,16 +199,16 @@ struct TmmParams {
   int* err;
 };
 
-// Dynamic shared memory: 1024-byte alignment slack, A ring, raw ring, `xs` activation stages of
-// 256 * Npad bytes, Q6_K d words (the rings start on 1024-byte boundaries).
+// Dynamic shared memory: 1024-byte alignment slack, raw ring, `xs` activation stages of
+// 512 * Npad bytes (two 64-column groups; 1024-byte aligned: SWIZZLE_128B atoms), Q6_K d words.
 __host__ __device__ inline size_t tmm_smem_fixed() {
-  return 1024 + (size_t)TM_AS * TM_A_BYTES + (size_t)TM_RS * TM_RAW_BYTES + (size_t)TM_RS * TM_ROWS * 4;
+  return 1024 + (size_t)TM_RS * TM_RAW_BYTES + (size_t)TM_RS * TM_ROWS * 4;
 }
-__host__ __device__ inline size_t tmm_smem(int Npad, int xs) { return tmm_smem_fixed() + (size_t)xs * 256 * Npad; }
+__host__ __device__ inline size_t tmm_smem(int Npad, int xs) { return tmm_smem_fixed() + (size_t)xs * 512 * Npad; }
 // The deepest activation ring that fits `budget` bytes of dynamic shared memory.
 __host__ __device__ inline int tmm_xs(int Npad, size_t budget) {
   const size_t room = budget > tmm_smem_fixed() ? budget - tmm_smem_fixed() : 0;
-  const int xs = (int)(room / ((size_t)256 * Npad));
+  const int xs = (int)(room / ((size_t)512 * Npad));
   return xs < 1 ? 0 : xs > TM_XS_MAX ? TM_XS_MAX : xs;
 }
 
@@ -211,10 +223,6 @@ __device__ __forceinline__ uint64_t tm_clock_ns() {
 constexpr uint64_t TM_WAIT_NS = 2000000000ull;
 __device__ __forceinline__ bool tm_wait(uint64_t* bar, uint32_t parity, int* err, int bit, volatile int* abort_f) {
   uint64_t t0 = 0;
-  // non-suspending probes first: the pipeline's hand-offs are short, and a suspended thread
-  // is woken late
-  for (int it = 0; it < 4096; ++it)
-    if (mbar_test_wait(bar, parity)) return true;
   for (uint32_t it = 0; it < KQ_WAIT_LIMIT; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255) == 255) {
@@ -229,6 +237,24 @@ __device__ __forceinline__ bool tm_wait(uint64_t* bar, uint32_t parity, int* err
   return false;
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16, fp32 accumulate (A read from tensor memory).
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// 16 consecutive 32-bit columns of this thread's TMEM lane (the warp's 32-lane quarter).
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 // Byte e of x (a value < 2^8) as the float 2^23 + value (exact).
 __device__ __forceinline__ float tm_magic(uint32_t x, int e) {
@@ -240,37 +266,38 @@ __device__ __forceinline__ void tm_split(float a, float b, uint32_t& hi, uint32_
   hi = h2u(h);
   lo = h2u(__floats2half2_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y)));
 }
-// A tile store: row r (0..127), 16-byte chunk j8 of the 64-column sub-stage, hi and lo planes.
-__device__ __forceinline__ void tm_put(uint8_t* A, int r, int j8, const uint4& hi, const uint4& lo) {
-  const int off = r * 128 + ((j8 ^ (r & 7)) << 4);
-  *reinterpret_cast<uint4*>(A + off) = hi;
-  *reinterpret_cast<uint4*>(A + TM_A_BYTES / 2 + off) = lo;
-}
-// Eight Q4_K weights (nibble values in the bytes of x0, x1): w = ds*q - dm.
-__device__ __forceinline__ void tm_q4_chunk(uint32_t x0, uint32_t x1, float ds, float dm, uint4& hi, uint4& lo) {
-  float w[8];
+// 32 Q4_K weights of one row, columns j = 0..31 of a sub-block: the nibble at `sh` (0 or 4) of the
+// 32 bytes W0, W1; w = ds*q - dm, as 16 hi and 16 lo words (column pairs 2m, 2m + 1).
+__device__ __forceinline__ void tm_q4_row32(const uint4& W0, const uint4& W1, int sh, float ds, float dm,
+                                            uint32_t (&h)[16], uint32_t (&l)[16]) {
+  const uint32_t wd[8] = {W0.x, W0.y, W0.z, W0.w, W1.x, W1.y, W1.z, W1.w};
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    w[e] = fmaf(ds, __fsub_rn(tm_magic(x0, e), 8388608.f), -dm);
-    w[4 + e] = fmaf(ds, __fsub_rn(tm_magic(x1, e), 8388608.f), -dm);
-  }
-  tm_split(w[0], w[1], hi.x, lo.x);
-  tm_split(w[2], w[3], hi.y, lo.y);
-  tm_split(w[4], w[5], hi.z, lo.z);
-  tm_split(w[6], w[7], hi.w, lo.w);
-}
-// Eight Q6_K weights (6-bit values in the bytes of x0, x1): w = dsc * (q - 32).
-__device__ __forceinline__ void tm_q6_chunk(uint32_t x0, uint32_t x1, float dsc, uint4& hi, uint4& lo) {
-  float w[8];
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t x = (wd[i] >> sh) & 0x0F0F0F0Fu;
+    float w[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    w[e] = __fmul_rn(dsc, __fsub_rn(tm_magic(x0, e), 8388640.f));
-    w[4 + e] = __fmul_rn(dsc, __fsub_rn(tm_magic(x1, e), 8388640.f));
+    for (int e = 0; e < 4; ++e) w[e] = fmaf(ds, __fsub_rn(tm_magic(x, e), 8388608.f), -dm);
+    tm_split(w[0], w[1], h[2 * i], l[2 * i]);
+    tm_split(w[2], w[3], h[2 * i + 1], l[2 * i + 1]);
   }
-  tm_split(w[0], w[1], hi.x, lo.x);
-  tm_split(w[2], w[3], hi.y, lo.y);
-  tm_split(w[4], w[5], hi.z, lo.z);
-  tm_split(w[6], w[7], hi.w, lo.w);
+}
+// 32 Q6_K weights of one row (columns j = 0..31 of a sub-block k of half h): low 4 bits from the
+// ql bytes L0, L1 at shift ls, high 2 bits from the qh bytes H0, H1 at shift hs; scale ds0 for
+// j < 16, ds1 for j >= 16; w = ds * (q - 32).
+__device__ __forceinline__ void tm_q6_row32(const uint4& L0, const uint4& L1, const uint4& H0, const uint4& H1, int ls,
+                                            int hs, float ds0, float ds1, uint32_t (&h)[16], uint32_t (&l)[16]) {
+  const uint32_t lw[8] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w};
+  const uint32_t hw[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t x = ((lw[i] >> ls) & 0x0F0F0F0Fu) | (((hw[i] >> hs) & 0x03030303u) << 4);
+    const float ds = i < 4 ? ds0 : ds1;
+    float w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) w[e] = __fmul_rn(ds, __fsub_rn(tm_magic(x, e), 8388640.f));
+    tm_split(w[0], w[1], h[2 * i], l[2 * i]);
+    tm_split(w[2], w[3], h[2 * i + 1], l[2 * i + 1]);
+  }
 }
 
 // Epilogue of one (row, token) value. lrow: row within the segment; vo: the value of row lrow ^ 1.
@@ -312,10 +339,9 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
   extern __shared__ uint8_t tm_dyn[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tm_dyn) + 1023) & ~(uintptr_t)1023);
   const int Npad = P.Npad;
-  const uint32_t xbytes = 256u * (uint32_t)Npad;
+  const uint32_t xbytes = 512u * (uint32_t)Npad;
   const int XS = P.xs;
-  uint8_t* a_ring = sm;
-  uint8_t* raw_ring = a_ring + TM_AS * TM_A_BYTES;
+  uint8_t* raw_ring = sm;
   uint8_t* x_ring = raw_ring + TM_RS * TM_RAW_BYTES;   // 1024-aligned (SWIZZLE_128B atoms)
   uint32_t* d_ring = reinterpret_cast<uint32_t*>(x_ring + (size_t)XS * xbytes);
   __shared__ __align__(8) uint64_t raw_full[TM_RS], raw_empty[TM_RS], a_full[TM_AS], sfree[TM_AS];
@@ -334,22 +360,22 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
   const int row0 = (tile - S.tile0) * TM_ROWS;
   const int G = P.G;
   const int g0 = (int)((long long)sp * G / P.nsplit), g1 = (int)((long long)(sp + 1) * G / P.nsplit);
-  const int nsb = g1 - g0, nsub = 4 * nsb;
+  const int nsb = g1 - g0, nsub = 2 * nsb;
   const bool q4 = w.type == Q4K;
   const int rstride = q4 ? TM_RAW_Q4 : TM_RAW_Q6;
-  // two fp32 accumulators of Npad columns: hi*hi products, and the two correction products
-  const uint32_t ncols = Npad <= 16 ? 32u : Npad <= 32 ? 64u : Npad <= 64 ? 128u : 256u;
+  const int AS = tmm_as(Npad);
+  const uint32_t acol = tmm_acol(Npad);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < TM_RS; ++i) { mbar_init(&raw_full[i], 32); mbar_init(&raw_empty[i], TM_DQ_WARPS); }
-    for (int i = 0; i < TM_AS; ++i) { mbar_init(&a_full[i], TM_DQ_WARPS); mbar_init(&sfree[i], 1); }
+    for (int i = 0; i < AS; ++i) { mbar_init(&a_full[i], TM_DQ_WARPS); mbar_init(&sfree[i], 1); }
     for (int i = 0; i < XS; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_free[i], 1); }
     mbar_init(&acc_full, 1);
     s_abort = 0;
     fence_mbar_init();
   }
   if (warp == 9) {
-    tmem_alloc(&s_tmem, ncols);
+    tmem_alloc(&s_tmem, TM_TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -409,33 +435,30 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
         if (i >= XS && !tm_wait(&x_free[slot], (uint32_t)((i / XS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
           break;
         mbar_arrive_expect_tx(&x_full[slot], xbytes);
-        bulk_g2s(x_ring + slot * xbytes, P.xp + (size_t)(4 * g0 + i) * xp_group_halves(Npad), xbytes, &x_full[slot], pol);
+        bulk_g2s(x_ring + slot * xbytes, P.xp + (size_t)(4 * g0 + 2 * i) * xp_group_halves(Npad), xbytes, &x_full[slot], pol);
       }
       // drain: the last copy into each buffer has completed before the CTA exits
       for (int j = i - XS < 0 ? 0 : i - XS; j < i; ++j)
         tm_wait(&x_full[j % XS], (uint32_t)(j / XS) & 1, P.err, KQ_DEV_ERR_DRAIN, abort_f);
     }
   } else if (warp == 9) {
-    // ---------------- MMA issue (one thread)
+    // ---------------- MMA issue (one thread): A from tensor memory, activations from shared memory
     if (lane == 0) {
-      const uint32_t idesc = tc_idesc_f16(TM_ROWS, Npad);
-      // descriptors of the ring bases; a sub-stage / K step only moves the start address field
-      // (16-byte units, addresses < 256 KiB so the 14-bit field never carries)
-      const uint64_t dA = sw128_desc(smem_u32(a_ring)), dX = sw128_desc(smem_u32(x_ring));
-      const uint64_t a_lo_off = (TM_A_BYTES / 2) >> 4, x_lo_off = (128u * (uint32_t)Npad) >> 4;
+      const uint32_t idesc1 = tc_idesc_f16(TM_ROWS, 2 * Npad), idesc2 = tc_idesc_f16(TM_ROWS, Npad);
+      const uint64_t dX = sw128_desc(smem_u32(x_ring));
       for (int i = 0; i < nsub; ++i) {
-        const int slot = i % TM_AS, xsl = i % XS;
-        if (!tm_wait(&a_full[slot], (uint32_t)(i / TM_AS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
+        const int slot = i % AS, xsl = i % XS;
+        if (!tm_wait(&a_full[slot], (uint32_t)(i / AS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
         if (!tm_wait(&x_full[xsl], (uint32_t)(i / XS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
         tc_fence_after();
-        const uint64_t a0 = dA + (uint64_t)((slot * TM_A_BYTES) >> 4), x0 = dX + (uint64_t)((xsl * xbytes) >> 4);
+        const uint32_t ta = tmem + acol + (uint32_t)slot * TM_ASTAGE_COLS;
+        const uint64_t x0 = dX + (uint64_t)((xsl * xbytes) >> 4), gstep = (256u * (uint32_t)Npad) >> 4;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ah = a0 + 2 * kk, al = ah + a_lo_off;   // + 32 bytes per K step
-          const uint64_t bh = x0 + 2 * kk, bl = bh + x_lo_off;
-          tc_mma_f16(tmem + (uint32_t)Npad, al, bh, idesc, (i | kk) ? 1u : 0u);
-          tc_mma_f16(tmem + (uint32_t)Npad, ah, bl, idesc, 1u);
-          tc_mma_f16(tmem, ah, bh, idesc, (i | kk) ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t ah = ta + 8 * kk, al = ah + 64;                     // 16 K elements = 8 columns
+          const uint64_t bx = x0 + (kk >> 2) * gstep + 2 * (kk & 3);         // group, + 32 bytes per K step
+          tc_mma_f16_ts(tmem, ah, bx, idesc1, (i | kk) ? 1u : 0u);          // hi(w) [hi(x); lo(x)]
+          tc_mma_f16_ts(tmem + (uint32_t)Npad, al, bx, idesc2, 1u);          // + lo(w) hi(x)
         }
         tc_commit(&sfree[slot]);
         tc_commit(&x_free[xsl]);
@@ -444,15 +467,19 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
     }
     __syncwarp();
   } else {
-    // ---------------- dequantise (warps 0-7): lane = (jh, row) ; 16 rows per warp
-    const int rr = lane & 15, jh = lane >> 4, r = 16 * warp + rr;
+    // ---------------- dequantise (warps 0-7): lane = weight row 32 * (warp & 3) + lane (the warp's
+    // TMEM lane quarter); warp >> 2 = which 64 of the sub-stage's 128 columns
+    const int qd = warp & 3, hf = warp >> 2, r = 32 * qd + lane;
+    const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
     bool ok = true;
     for (int k = 0; k < nsb && ok; ++k) {
       const int slot = k % TM_RS;
       ok = __all_sync(0xffffffffu, tm_wait(&raw_full[slot], (uint32_t)(k / TM_RS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f));
       if (!ok) break;
       const uint8_t* rw = raw_ring + slot * TM_RAW_BYTES + r * rstride;
-      float ds[8], dm[8];
+      // scales of this row for sub-stage h (columns 128h + 64hf + 32m + j):
+      // Q4_K sub-block 4h + 2hf + m: (d*sc, dmin*mn); Q6_K sub-block k = 2hf + m: d*scale for j < 16, j >= 16
+      float ds[2][2][2], dm[2][2];
       if (q4) {
         const uint4 H = lds128(rw + 128);
         const float d = h2f_bits(H.x & 0xFFFFu), dmin = h2f_bits(H.x >> 16);
@@ -460,67 +487,59 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
         const uint32_t sc_hi = (H.w & 0x0F0F0F0Fu) | ((H.y >> 2) & 0x30303030u);
         const uint32_t mn_hi = ((H.w >> 4) & 0x0F0F0F0Fu) | ((H.z >> 2) & 0x30303030u);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          ds[e] = __fmul_rn(d, (float)((sc_lo >> (8 * e)) & 0xFFu));
-          dm[e] = __fmul_rn(dmin, (float)((mn_lo >> (8 * e)) & 0xFFu));
-          ds[4 + e] = __fmul_rn(d, (float)((sc_hi >> (8 * e)) & 0xFFu));
-          dm[4 + e] = __fmul_rn(dmin, (float)((mn_hi >> (8 * e)) & 0xFFu));
-        }
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const int sh = 8 * (2 * hf + m);   // sub-block 4h + 2hf + m: byte 2hf + m of word h
+            ds[h][m][0] = ds[h][m][1] = __fmul_rn(d, (float)(((h ? sc_hi : sc_lo) >> sh) & 0xFFu));
+            dm[h][m] = __fmul_rn(dmin, (float)(((h ? mn_hi : mn_lo) >> sh) & 0xFFu));
+          }
       } else {
         const uint4 Sc = lds128(rw + 192);   // [u = 2h + jh][k]
         const uint32_t dw = d_ring[slot * TM_ROWS + r];
         const float d = h2f_bits(((r & 7) * G + g0 + k) & 1 ? dw >> 16 : dw & 0xFFFFu);
-        const uint32_t s0 = jh ? Sc.y : Sc.x, s1 = jh ? Sc.w : Sc.z;   // h = 0 / h = 1
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          ds[e] = __fmul_rn(d, (float)(int8_t)((s0 >> (8 * e)) & 0xFFu));
-          ds[4 + e] = __fmul_rn(d, (float)(int8_t)((s1 >> (8 * e)) & 0xFFu));
-          dm[e] = dm[4 + e] = 0.f;
-        }
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const int sh = 8 * (2 * hf + m);
+            ds[h][m][0] = __fmul_rn(d, (float)(int8_t)(((h ? Sc.z : Sc.x) >> sh) & 0xFFu));
+            ds[h][m][1] = __fmul_rn(d, (float)(int8_t)(((h ? Sc.w : Sc.y) >> sh) & 0xFFu));
+            dm[h][m] = 0.f;
+          }
       }
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const int i = 4 * k + s, as = i % TM_AS;
-        if (i >= TM_AS) {
-          ok = __all_sync(0xffffffffu, tm_wait(&sfree[as], (uint32_t)((i / TM_AS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f));
+      for (int h = 0; h < 2; ++h) {
+        const int i = 2 * k + h, as = i % AS;
+        if (i >= AS) {
+          ok = __all_sync(0xffffffffu, tm_wait(&sfree[as], (uint32_t)((i / AS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f));
           if (!ok) break;
+          tc_fence_after();   // the MMAs that read this stage have completed
         }
-        uint8_t* A = a_ring + as * TM_A_BYTES;
-        const int h = s >> 1;
-        uint4 hi, lo;
+        uint32_t hv[2][16], lv[2][16];
         if (q4) {
-          // sub-blocks 2s (low nibbles, columns 0-31) and 2s + 1 (high nibbles, columns 32-63)
-          const uint4 W = lds128(rw + (s & 1) * 64 + h * 32 + jh * 16);
-          const float dsA = ds[2 * s], dmA = dm[2 * s], dsB = ds[2 * s + 1], dmB = dm[2 * s + 1];
-          tm_q4_chunk(W.x & 0x0F0F0F0Fu, W.y & 0x0F0F0F0Fu, dsA, dmA, hi, lo);
-          tm_put(A, r, 2 * jh, hi, lo);
-          tm_q4_chunk(W.z & 0x0F0F0F0Fu, W.w & 0x0F0F0F0Fu, dsA, dmA, hi, lo);
-          tm_put(A, r, 2 * jh + 1, hi, lo);
-          tm_q4_chunk((W.x >> 4) & 0x0F0F0F0Fu, (W.y >> 4) & 0x0F0F0F0Fu, dsB, dmB, hi, lo);
-          tm_put(A, r, 4 + 2 * jh, hi, lo);
-          tm_q4_chunk((W.z >> 4) & 0x0F0F0F0Fu, (W.w >> 4) & 0x0F0F0F0Fu, dsB, dmB, hi, lo);
-          tm_put(A, r, 5 + 2 * jh, hi, lo);
+          // the 32 bytes of (h, c = hf): low nibbles = sub-block 4h + 2hf, high = 4h + 2hf + 1
+          const uint8_t* b = rw + hf * 64 + h * 32;
+          const uint4 W0 = lds128(b), W1 = lds128(b + 16);
+          tm_q4_row32(W0, W1, 0, ds[h][0][0], dm[h][0], hv[0], lv[0]);
+          tm_q4_row32(W0, W1, 4, ds[h][1][0], dm[h][1], hv[1], lv[1]);
         } else {
-          // columns 32kk + j of the sub-stage: sub-block k = 2(s & 1) + kk of half h
-          const int n = s & 1;
-          const uint4 QH = lds128(rw + 128 + h * 32 + jh * 16);
+          // sub-block k = 2hf + m of half h: ql chunk c = m, nibble hf, qh shift 2k
+          const uint8_t* hq = rw + 128 + h * 32;
+          const uint4 H0 = lds128(hq), H1 = lds128(hq + 16);
 #pragma unroll
-          for (int kk = 0; kk < 2; ++kk) {
-            const int kq = 2 * n + kk;
-            const uint4 QL = lds128(rw + kk * 64 + h * 32 + jh * 16);
-            const int ls = 4 * n, hs = 2 * kq;
-            const float dsc = ds[4 * h + kq];
-            const uint32_t q0 = ((QL.x >> ls) & 0x0F0F0F0Fu) | (((QH.x >> hs) & 0x03030303u) << 4);
-            const uint32_t q1 = ((QL.y >> ls) & 0x0F0F0F0Fu) | (((QH.y >> hs) & 0x03030303u) << 4);
-            const uint32_t q2 = ((QL.z >> ls) & 0x0F0F0F0Fu) | (((QH.z >> hs) & 0x03030303u) << 4);
-            const uint32_t q3 = ((QL.w >> ls) & 0x0F0F0F0Fu) | (((QH.w >> hs) & 0x03030303u) << 4);
-            tm_q6_chunk(q0, q1, dsc, hi, lo);
-            tm_put(A, r, 4 * kk + 2 * jh, hi, lo);
-            tm_q6_chunk(q2, q3, dsc, hi, lo);
-            tm_put(A, r, 4 * kk + 2 * jh + 1, hi, lo);
+          for (int m = 0; m < 2; ++m) {
+            const uint8_t* lq = rw + m * 64 + h * 32;
+            tm_q6_row32(lds128(lq), lds128(lq + 16), H0, H1, 4 * hf, 2 * (2 * hf + m), ds[h][m][0], ds[h][m][1], hv[m], lv[m]);
           }
         }
-        fence_proxy_async();
+        const uint32_t ta = trow + acol + (uint32_t)as * TM_ASTAGE_COLS + 32u * (uint32_t)hf;
+        tc_st16(ta, hv[0]);
+        tc_st16(ta + 16, hv[1]);
+        tc_st16(ta + 64, lv[0]);
+        tc_st16(ta + 80, lv[1]);
+        tc_wait_st();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[as]);
       }
@@ -583,7 +602,7 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
   __syncthreads();
   if (warp == 9) {
     tc_fence_after();
-    tmem_dealloc(tmem, ncols);
+    tmem_dealloc(tmem, TM_TMEM_COLS);
   }
 }
 
