@@ -218,6 +218,15 @@ def run_profile_mode(args):
         print(json.dumps({"mode": "prefill", "p512": prefill_bench(e, e.vocab, 512, args.steps),
                           "p2048": prefill_bench(e, e.vocab, 2048, 1)}))
         return 0
+    if args.mode == "gemm":
+        # the batched-pass GEMM alone: gate/up shape (Q4_K 24576 x 4096), 45 tokens, through kq_qmat_matmul
+        import numpy as np
+        m = kq.QMat(12, 24576, 4096).fill_synthetic(0, 3)
+        X = np.random.default_rng(1).standard_normal((45, 4096)).astype(np.float32)
+        for _ in range(max(1, args.steps)):
+            Y = m.matmul(X)
+        print(json.dumps({"mode": "gemm", "rows": 24576, "cols": 4096, "tokens": 45, "checksum": float(np.abs(Y).sum())}))
+        return 0
     if args.mode == "gemv-only":
         mats = [kq.QMat(12, 12288, 4096).fill_synthetic(0, 1000 + i) for i in range(16)]
         kq.time_matvec(mats, args.warmup)
@@ -241,7 +250,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=32, help="decode-only: layers of the model (small ncu captures)")
-    ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only", "spec", "prefill"],
+    ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only", "spec", "prefill", "gemm"],
                     help="decode-only / gemv-only: the small commands the ncu captures in profiles/ run")
     args = ap.parse_args()
     if args.mode != "full":
