@@ -66,6 +66,19 @@ void kq_config_default(kq_config* cfg);              /* BASELINE config-2 */
  * (scripts/kindi_q4/kindi/engine.py:369-381) for the Q4 pack path. */
 kq_model* kq_model_create(const kq_config* cfg, int device);   /* NULL on failure, see kq_error */
 void kq_model_free(kq_model* m);
+
+/* ------------------------------------------------------------------ tensor parallelism
+ * One process per GPU. A shard holds KV heads [r*nkv/W, (r+1)*nkv/W) with their query heads
+ * (q/k/v rows, o input columns, K/V cache), the FFN slice r (gate/up rows, down input columns) and
+ * the vocabulary slice r of the output head; embedding and norms are whole on every rank. The
+ * batched pass (kq_feed_batch, kq_verify, kq_step) sums the o and down partials with one NCCL
+ * all-reduce each per layer and all-gathers the head's per-rank argmax. Generated shards are
+ * bit-identical slices of the whole model kq_model_fill_synthetic generates. Needs n_kv_heads and
+ * vocab divisible by W and 256-column slices of ffn and n_heads*head_dim. Not available on a
+ * shard: kq_logits, kq_hidden, kq_decode_loop, kq_time_decode, kq_accept, kq_model_set_tensor. */
+int kq_tp_unique_id(uint8_t* out128);                 /* ncclGetUniqueId, 128 bytes */
+kq_model* kq_model_create_tp(const kq_config* cfg, int device, int rank, int world, const uint8_t* id128);
+int kq_model_tp(const kq_model* m, int* rank, int* world);
 /* Fill every tensor from the seeded synthetic generator, on the device. */
 int kq_model_fill_synthetic(kq_model* m, uint64_t seed);
 /* Upload one tensor: quantised tensors as GGUF block bytes, norms as float32 [dim]. */

@@ -13,6 +13,7 @@
 #include "kq_decode.cuh"
 #include "kq_accept.cuh"
 #include "kq_batch.cuh"
+#include "kq_nccl.h"
 
 #include <cuda_runtime.h>
 #include <cmath>
@@ -145,10 +146,12 @@ static kq_qmat* qmat_alloc(int type, int R, int C, int device) {
   return a;
 }
 
-static int qmat_write(kq_qmat* a, int R_src, const uint8_t* src_dev, uint64_t base, int mode, int arg, cudaStream_t s) {
+static int qmat_write(kq_qmat* a, int R_src, const uint8_t* src_dev, uint64_t base, int mode, int arg, cudaStream_t s,
+                      ShardMap sh = ShardMap{0, 0, 0}) {
   const long long n = (long long)R_src * a->G;
   const int thr = 128;
-  k_qmat_write<<<(unsigned)((n + thr - 1) / thr), thr, 0, s>>>(a->wview(), R_src, src_dev, base, mode, arg);
+  if (sh.G_src == 0) sh.G_src = a->G;
+  k_qmat_write<<<(unsigned)((n + thr - 1) / thr), thr, 0, s>>>(a->wview(), R_src, src_dev, base, mode, arg, sh);
   CU(cudaGetLastError());
   return KQ_OK;
 }
@@ -419,6 +422,16 @@ struct LayerW {
 struct kq_model {
   kq_config c{};
   int device = 0, nsm = 0;
+  // tensor parallelism (world 1: the whole model). Rank r holds KV heads [r nkv_l, (r+1) nkv_l)
+  // and their query heads (q/k/v rows, o input columns, K/V cache), the FFN slice
+  // [r ffn_l, (r+1) ffn_l) (gate/up rows, down input columns) and the vocabulary slice
+  // [r vocab_l, ...) of the head; embedding and norms are whole on every rank. One NCCL
+  // all-reduce of the o and the down outputs per layer, an all-gather of the head's argmax.
+  int tp_rank = 0, tp_world = 1;
+  int nh_l = 0, nkv_l = 0, ffn_l = 0, vocab_l = 0;
+  ncclComm_t comm = nullptr;
+  float* tp_val = nullptr;          // [world][MM_MAXM] head argmax values of every rank
+  int* tp_idx = nullptr;            // [world][MM_MAXM] their (global) ids
   cudaStream_t stream = nullptr;
   std::vector<LayerW> L;
   kq_qmat *emb = nullptr, *out = nullptr;
@@ -499,6 +512,7 @@ static void model_release(kq_model* m) {
   if (!m) return;
   cudaSetDevice(m->device);
   if (m->stream) cudaStreamSynchronize(m->stream);
+  if (m->comm && nccl().ok) nccl().CommDestroy(m->comm);
   if (m->g_step) cudaGraphExecDestroy(m->g_step);
   if (m->g_feed) cudaGraphExecDestroy(m->g_feed);
   for (auto& l : m->L) {
@@ -544,19 +558,31 @@ static int validate_cfg(const kq_config& c) {
   return KQ_OK;
 }
 
-extern "C" kq_model* kq_model_create(const kq_config* cfg, int device) {
+static kq_model* model_create(const kq_config* cfg, int device, int rank, int world) {
   if (!cfg) { set_err(KQ_ERR_ARG, "null config"); return nullptr; }
   if (validate_cfg(*cfg) != KQ_OK) return nullptr;
+  if (world < 1 || rank < 0 || rank >= world) { set_err(KQ_ERR_ARG, "bad tensor-parallel rank / world"); return nullptr; }
+  if (world > 1 && (cfg->n_kv_heads % world || (cfg->ffn / world) % 256 || cfg->vocab % world ||
+                    ((cfg->n_heads / world) * cfg->head_dim) % 256)) {
+    set_err(KQ_ERR_ARG, "tensor-parallel split needs n_kv_heads, vocab divisible by world and 256-column slices");
+    return nullptr;
+  }
   if (dev_init(device) != KQ_OK) return nullptr;
   CUP(cudaSetDevice(device));
   kq_model* m = new kq_model();
   m->c = *cfg;
   m->device = device;
   m->nsm = g_dev[device].nsm;
+  m->tp_rank = rank;
+  m->tp_world = world;
   const kq_config& c = m->c;
+  m->nh_l = c.n_heads / world;
+  m->nkv_l = c.n_kv_heads / world;
+  m->ffn_l = c.ffn / world;
+  m->vocab_l = c.vocab / world;
   bool ok = true;
   if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) ok = false;
-  const int QD = c.n_heads * c.head_dim, KD = c.n_kv_heads * c.head_dim;
+  const int QD = m->nh_l * c.head_dim, KD = m->nkv_l * c.head_dim;
   m->L.resize(c.n_layers);
   for (int l = 0; ok && l < c.n_layers; ++l) {
     LayerW& w = m->L[l];
@@ -564,8 +590,8 @@ extern "C" kq_model* kq_model_create(const kq_config* cfg, int device) {
     w.k = qmat_alloc(c.t_k, KD, c.dim, device);
     w.v = qmat_alloc(c.t_v, KD, c.dim, device);
     w.o = qmat_alloc(c.t_o, c.dim, QD, device);
-    w.gu = qmat_alloc(c.t_gate, 2 * c.ffn, c.dim, device);
-    w.down = qmat_alloc(c.t_down, c.dim, c.ffn, device);
+    w.gu = qmat_alloc(c.t_gate, 2 * m->ffn_l, c.dim, device);
+    w.down = qmat_alloc(c.t_down, c.dim, m->ffn_l, device);
     if (!w.q || !w.k || !w.v || !w.o || !w.gu || !w.down) { ok = false; break; }
     w.attn_norm = dalloc<float>(m, c.dim, ok);
     w.ffn_norm = dalloc<float>(m, c.dim, ok);
@@ -574,8 +600,12 @@ extern "C" kq_model* kq_model_create(const kq_config* cfg, int device) {
   }
   if (ok) {
     m->emb = qmat_alloc(c.t_emb, c.vocab, c.dim, device);
-    m->out = qmat_alloc(c.t_out, c.vocab, c.dim, device);
+    m->out = qmat_alloc(c.t_out, m->vocab_l, c.dim, device);
     if (!m->emb || !m->out) ok = false;
+  }
+  if (ok && world > 1) {
+    m->tp_val = dalloc<float>(m, (size_t)(world + 1) * MM_MAXM, ok);   // gathered rows + this rank's
+    m->tp_idx = dalloc<int>(m, (size_t)(world + 1) * MM_MAXM, ok);
   }
   const int rh = c.head_dim / 2;
   if (ok) {
@@ -629,6 +659,45 @@ extern "C" kq_model* kq_model_create(const kq_config* cfg, int device) {
   return m;
 }
 
+extern "C" kq_model* kq_model_create(const kq_config* cfg, int device) { return model_create(cfg, device, 0, 1); }
+
+extern "C" int kq_tp_unique_id(uint8_t* out128) {
+  if (!out128) return set_err(KQ_ERR_ARG, "null id buffer");
+  if (!nccl().ok) return set_err(KQ_ERR_BACKEND, "NCCL could not be loaded");
+  ncclUniqueId id;
+  const ncclResult_t r = nccl().GetUniqueId(&id);
+  if (r != ncclSuccess) return set_err(KQ_ERR_BACKEND, std::string("ncclGetUniqueId: ") + nccl().GetErrorString(r));
+  static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id size");
+  std::memcpy(out128, &id, 128);
+  return KQ_OK;
+}
+
+// Every rank calls this with the same id (from kq_tp_unique_id on one rank); it returns once all
+// `world` ranks have joined the communicator.
+extern "C" kq_model* kq_model_create_tp(const kq_config* cfg, int device, int rank, int world, const uint8_t* id128) {
+  if (!id128 && world > 1) { set_err(KQ_ERR_ARG, "null NCCL id"); return nullptr; }
+  kq_model* m = model_create(cfg, device, rank, world);
+  if (!m || world == 1) return m;
+  if (!nccl().ok) { set_err(KQ_ERR_BACKEND, "NCCL could not be loaded"); model_release(m); return nullptr; }
+  ncclUniqueId id;
+  std::memcpy(&id, id128, 128);
+  const ncclResult_t r = nccl().CommInitRank(&m->comm, world, id, rank);
+  if (r != ncclSuccess) {
+    set_err(KQ_ERR_BACKEND, std::string("ncclCommInitRank: ") + nccl().GetErrorString(r));
+    m->comm = nullptr;
+    model_release(m);
+    return nullptr;
+  }
+  return m;
+}
+
+extern "C" int kq_model_tp(const kq_model* m, int* rank, int* world) {
+  if (!m) return set_err(KQ_ERR_ARG, "null model");
+  if (rank) *rank = m->tp_rank;
+  if (world) *world = m->tp_world;
+  return KQ_OK;
+}
+
 extern "C" void kq_model_free(kq_model* m) { model_release(m); }
 
 // Synthetic stream numbering (shared specification with the CPU oracle).
@@ -645,20 +714,25 @@ extern "C" int kq_model_fill_synthetic(kq_model* m, uint64_t seed) {
   if (rc) return rc;
   const kq_config& c = m->c;
   cudaStream_t s = m->stream;
+  // tensor-parallel shards draw the blocks of the full matrices they slice (ShardMap)
+  const int r = m->tp_rank, G = c.dim / 256, QDf = c.n_heads * c.head_dim;
+  const ShardMap sq{r * m->nh_l * c.head_dim, 0, G}, skv{r * m->nkv_l * c.head_dim, 0, G};
+  const ShardMap so{0, r * m->nh_l * c.head_dim / 256, QDf / 256}, sgu{r * m->ffn_l, 0, G};
+  const ShardMap sdn{0, r * m->ffn_l / 256, c.ffn / 256}, sout{r * m->vocab_l, 0, G};
   for (int l = 0; l < c.n_layers; ++l) {
     LayerW& w = m->L[l];
-    if ((rc = qmat_write(w.q, w.q->R, nullptr, gen_base(seed, tstream(l, KQ_T_Q)), RM_ROPE_PAIR, c.head_dim, s))) return rc;
-    if ((rc = qmat_write(w.k, w.k->R, nullptr, gen_base(seed, tstream(l, KQ_T_K)), RM_ROPE_PAIR, c.head_dim, s))) return rc;
-    if ((rc = qmat_write(w.v, w.v->R, nullptr, gen_base(seed, tstream(l, KQ_T_V)), RM_IDENT, 0, s))) return rc;
-    if ((rc = qmat_write(w.o, w.o->R, nullptr, gen_base(seed, tstream(l, KQ_T_O)), RM_IDENT, 0, s))) return rc;
-    if ((rc = qmat_write(w.gu, c.ffn, nullptr, gen_base(seed, tstream(l, KQ_T_GATE)), RM_INTERLEAVE, 0, s))) return rc;
-    if ((rc = qmat_write(w.gu, c.ffn, nullptr, gen_base(seed, tstream(l, KQ_T_UP)), RM_INTERLEAVE, 1, s))) return rc;
-    if ((rc = qmat_write(w.down, w.down->R, nullptr, gen_base(seed, tstream(l, KQ_T_DOWN)), RM_IDENT, 0, s))) return rc;
+    if ((rc = qmat_write(w.q, w.q->R, nullptr, gen_base(seed, tstream(l, KQ_T_Q)), RM_ROPE_PAIR, c.head_dim, s, sq))) return rc;
+    if ((rc = qmat_write(w.k, w.k->R, nullptr, gen_base(seed, tstream(l, KQ_T_K)), RM_ROPE_PAIR, c.head_dim, s, skv))) return rc;
+    if ((rc = qmat_write(w.v, w.v->R, nullptr, gen_base(seed, tstream(l, KQ_T_V)), RM_IDENT, 0, s, skv))) return rc;
+    if ((rc = qmat_write(w.o, w.o->R, nullptr, gen_base(seed, tstream(l, KQ_T_O)), RM_IDENT, 0, s, so))) return rc;
+    if ((rc = qmat_write(w.gu, m->ffn_l, nullptr, gen_base(seed, tstream(l, KQ_T_GATE)), RM_INTERLEAVE, 0, s, sgu))) return rc;
+    if ((rc = qmat_write(w.gu, m->ffn_l, nullptr, gen_base(seed, tstream(l, KQ_T_UP)), RM_INTERLEAVE, 1, s, sgu))) return rc;
+    if ((rc = qmat_write(w.down, w.down->R, nullptr, gen_base(seed, tstream(l, KQ_T_DOWN)), RM_IDENT, 0, s, sdn))) return rc;
     if ((rc = gen_normal_dev(w.attn_norm, c.dim, 1.0f, 0.02f, seed, tstream(l, KQ_T_ATTN_NORM), s))) return rc;
     if ((rc = gen_normal_dev(w.ffn_norm, c.dim, 1.0f, 0.02f, seed, tstream(l, KQ_T_FFN_NORM), s))) return rc;
   }
   if ((rc = qmat_write(m->emb, m->emb->R, nullptr, gen_base(seed, tstream(-1, KQ_T_EMB)), RM_IDENT, 0, s))) return rc;
-  if ((rc = qmat_write(m->out, m->out->R, nullptr, gen_base(seed, tstream(-1, KQ_T_OUT)), RM_IDENT, 0, s))) return rc;
+  if ((rc = qmat_write(m->out, m->out->R, nullptr, gen_base(seed, tstream(-1, KQ_T_OUT)), RM_IDENT, 0, s, sout))) return rc;
   if ((rc = gen_normal_dev(m->out_norm, c.dim, 1.0f, 0.02f, seed, tstream(-1, KQ_T_OUTNORM), s))) return rc;
   CU(cudaStreamSynchronize(s));
   return KQ_OK;
@@ -667,6 +741,7 @@ extern "C" int kq_model_fill_synthetic(kq_model* m, uint64_t seed) {
 extern "C" int kq_model_set_tensor(kq_model* m, int layer, int kind, const void* host, size_t bytes) {
   int rc = model_check(m);
   if (rc) return rc;
+  if (m->tp_world > 1) return set_err(KQ_ERR_ARG, "tensor uploads go to a whole model (tensor-parallel models are generated)");
   if (!host) return set_err(KQ_ERR_ARG, "null tensor data");
   const kq_config& c = m->c;
   const bool global = kind == KQ_T_EMB || kind == KQ_T_OUT || kind == KQ_T_OUTNORM;
@@ -702,7 +777,7 @@ extern "C" int kq_model_set_tensor(kq_model* m, int layer, int kind, const void*
 extern "C" int kq_model_reset(kq_model* m) {
   int rc = model_check(m);
   if (rc) return rc;
-  const size_t kvn = (size_t)m->c.n_kv_heads * m->c.head_dim * m->c.ctx;
+  const size_t kvn = (size_t)m->nkv_l * m->c.head_dim * m->c.ctx;
   for (auto& l : m->L) {
     CU(cudaMemsetAsync(l.kc, 0, kvn * 2, m->stream));
     CU(cudaMemsetAsync(l.vc, 0, kvn * 2, m->stream));
@@ -713,26 +788,29 @@ extern "C" int kq_model_reset(kq_model* m) {
 
 // Value of the K/V cache at (kv, pos, d) = generator element (pos * n_kv + kv) * hd + d, which is
 // the element order of the reference layout [pos][kv][hd].
-__global__ void k_fill_kv(__half* dst, int npos, int nkv, int ctx, int hd, uint64_t base) {
+// A tensor-parallel rank holds heads [kv_off, kv_off + nkv) of nkv_all.
+__global__ void k_fill_kv(__half* dst, int npos, int nkv, int ctx, int hd, uint64_t base, int nkv_all, int kv_off) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)npos * nkv * hd) return;
   const int d = (int)(i % hd);
   const long long r = i / hd;
   const int kv = (int)(r % nkv), pos = (int)(r / nkv);
-  dst[((size_t)kv * ctx + pos) * hd + d] = __float2half_rn(gen_nrm(base, (uint64_t)i));
+  const uint64_t gi = ((uint64_t)pos * nkv_all + kv_off + kv) * hd + d;
+  dst[((size_t)kv * ctx + pos) * hd + d] = __float2half_rn(gen_nrm(base, gi));
 }
 
 extern "C" int kq_model_fill_kv(kq_model* m, int npos, uint64_t seed) {
   int rc = model_check(m);
   if (rc) return rc;
   if (npos < 0 || npos > m->c.ctx) return set_err(KQ_ERR_ARG, "npos out of range");
-  const long long n = (long long)npos * m->c.n_kv_heads * m->c.head_dim;
+  const long long n = (long long)npos * m->nkv_l * m->c.head_dim;
   if (n == 0) return KQ_OK;
+  const int kv_off = m->tp_rank * m->nkv_l;
   for (int l = 0; l < m->c.n_layers; ++l) {
-    k_fill_kv<<<(unsigned)((n + 255) / 256), 256, 0, m->stream>>>(m->L[l].kc, npos, m->c.n_kv_heads, m->c.ctx, m->c.head_dim,
-                                                                   gen_base(seed, tstream(l, 12)));
-    k_fill_kv<<<(unsigned)((n + 255) / 256), 256, 0, m->stream>>>(m->L[l].vc, npos, m->c.n_kv_heads, m->c.ctx, m->c.head_dim,
-                                                                   gen_base(seed, tstream(l, 13)));
+    k_fill_kv<<<(unsigned)((n + 255) / 256), 256, 0, m->stream>>>(m->L[l].kc, npos, m->nkv_l, m->c.ctx, m->c.head_dim,
+                                                                   gen_base(seed, tstream(l, 12)), m->c.n_kv_heads, kv_off);
+    k_fill_kv<<<(unsigned)((n + 255) / 256), 256, 0, m->stream>>>(m->L[l].vc, npos, m->nkv_l, m->c.ctx, m->c.head_dim,
+                                                                   gen_base(seed, tstream(l, 13)), m->c.n_kv_heads, kv_off);
   }
   CU(cudaGetLastError());
   CU(cudaStreamSynchronize(m->stream));
@@ -744,7 +822,7 @@ extern "C" int kq_model_get_kv(kq_model* m, int layer, int which, int npos, uint
   if (rc) return rc;
   if (layer < 0 || layer >= m->c.n_layers || npos < 0 || npos > m->c.ctx || !out || (which != 0 && which != 1))
     return set_err(KQ_ERR_ARG, "bad K/V cache request");
-  const int nkv = m->c.n_kv_heads, hd = m->c.head_dim, ctx = m->c.ctx;
+  const int nkv = m->nkv_l, hd = m->c.head_dim, ctx = m->c.ctx;   // this rank's heads
   std::vector<uint16_t> tmp((size_t)nkv * ctx * hd);
   CU(cudaMemcpy(tmp.data(), which ? m->L[layer].vc : m->L[layer].kc, tmp.size() * 2, cudaMemcpyDeviceToHost));
   for (int p = 0; p < npos; ++p)
@@ -1055,8 +1133,29 @@ static int run_one(kq_model* m, int tok, int pos, bool head) {
   return head ? m->st_host->next_tok : KQ_OK;
 }
 
-extern "C" int kq_feed(kq_model* m, int tok, int pos) { return run_one(m, tok, pos, false); }
-extern "C" int kq_step(kq_model* m, int tok, int pos) { return run_one(m, tok, pos, true); }
+extern "C" int kq_verify(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, int pos, float* logits,
+                         int32_t* best);
+extern "C" int kq_feed_batch(kq_model* m, const int32_t* toks, int n, int pos);
+
+// A tensor-parallel model runs every token through the batched pass (a one-node pass for a
+// decode step); the whole model uses the decode graph.
+extern "C" int kq_feed(kq_model* m, int tok, int pos) {
+  if (m && m->tp_world > 1) return kq_feed_batch(m, &tok, 1, pos);
+  return run_one(m, tok, pos, false);
+}
+extern "C" int kq_step(kq_model* m, int tok, int pos) {
+  if (m && m->tp_world > 1) {
+    const int32_t par = -1;
+    int32_t best = -1;
+    const int rc = kq_verify(m, &tok, &par, 1, pos, nullptr, &best);
+    return rc < 0 ? rc : best;
+  }
+  return run_one(m, tok, pos, true);
+}
+static int not_tp(kq_model* m, const char* what) {
+  if (m && m->tp_world > 1) return set_err(KQ_ERR_ARG, std::string(what) + " runs on a whole model, not a tensor-parallel shard");
+  return KQ_OK;
+}
 
 static int verify_buffers(kq_model* m);
 static int batch_buffers(kq_model* m);
@@ -1088,12 +1187,12 @@ extern "C" int kq_feed_batch(kq_model* m, const int32_t* toks, int n, int pos) {
   for (int i = 0; i < n; ++i)
     if (toks[i] < 0 || toks[i] >= m->c.vocab) return set_err(KQ_ERR_ARG, "Invalid token");
   if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "prompt runs past the context");
-  if (n < 2 || m->verify_seq || !batch_supported(m)) {
+  if (m->tp_world == 1 && (n < 2 || m->verify_seq || !batch_supported(m))) {
     for (int i = 0; i < n; ++i)
       if ((rc = kq_feed(m, toks[i], pos + i)) < 0) return rc;
     return KQ_OK;
   }
-  if ((rc = ensure_graphs(m)) || (rc = verify_buffers(m)) || (rc = batch_buffers(m))) return rc;
+  if ((m->tp_world == 1 && (rc = ensure_graphs(m))) || (rc = verify_buffers(m)) || (rc = batch_buffers(m))) return rc;
   static const ChainMasks chain;
   for (int c0 = 0; c0 < n; c0 += MM_MAXM)
     if ((rc = verify_pass(m, toks + c0, 0, std::min(MM_MAXM, n - c0), pos + c0, chain.depth, chain.anc, false)))
@@ -1122,7 +1221,7 @@ extern "C" int kq_generate(kq_model* m, const int32_t* ids, int n_ids, int n, in
 
 extern "C" int kq_logits(kq_model* m, int row, float* out) {
   int rc = model_check(m);
-  if (rc) return rc;
+  if (rc || (rc = not_tp(m, "kq_logits"))) return rc;
   if (row != 0 || !out) return set_err(KQ_ERR_ARG, "bad logits request");
   CU(cudaMemcpy(out, m->logits, (size_t)m->c.vocab * 4, cudaMemcpyDeviceToHost));
   return KQ_OK;
@@ -1130,7 +1229,7 @@ extern "C" int kq_logits(kq_model* m, int row, float* out) {
 
 extern "C" int kq_hidden(kq_model* m, float* out) {
   int rc = model_check(m);
-  if (rc) return rc;
+  if (rc || (rc = not_tp(m, "kq_hidden"))) return rc;
   if (!out) return set_err(KQ_ERR_ARG, "null output");
   // after a step with the head, the residual (h + last block output) is in h[1] (even number of
   // norm kernels per layer, the head's norm writes the second buffer)
@@ -1140,7 +1239,7 @@ extern "C" int kq_hidden(kq_model* m, float* out) {
 
 extern "C" int kq_decode_loop(kq_model* m, int tok, int pos, int n, int32_t* out) {
   int rc = model_check(m);
-  if (rc) return rc;
+  if (rc || (rc = not_tp(m, "kq_decode_loop"))) return rc;
   if (n < 1 || !out || tok < 0 || tok >= m->c.vocab || pos < 0) return set_err(KQ_ERR_ARG, "bad decode loop arguments");
   if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "decode loop runs past the context");
   if ((rc = ensure_graphs(m))) return rc;
@@ -1163,7 +1262,7 @@ extern "C" int kq_decode_loop(kq_model* m, int tok, int pos, int n, int32_t* out
 
 extern "C" int kq_time_decode(kq_model* m, int tok, int pos, int n, float* ms_out) {
   int rc = model_check(m);
-  if (rc) return rc;
+  if (rc || (rc = not_tp(m, "kq_time_decode"))) return rc;
   if (n < 1 || !ms_out || tok < 0 || tok >= m->c.vocab || pos < 0) return set_err(KQ_ERR_ARG, "bad timing arguments");
   if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "timed decode runs past the context");
   if ((rc = ensure_graphs(m))) return rc;
@@ -1301,17 +1400,26 @@ static cudaError_t launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, cudaSt
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
+// Sum of the row-split GEMM partials over the tensor-parallel ranks (fp32, in place, on the
+// model's stream). World 1: nothing.
+static int tp_allreduce(kq_model* m, float* buf, size_t n) {
+  if (m->tp_world == 1) return KQ_OK;
+  const ncclResult_t r = nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum, m->comm, m->stream);
+  if (r != ncclSuccess) return set_err(KQ_ERR_BACKEND, std::string("ncclAllReduce: ") + nccl().GetErrorString(r));
+  return KQ_OK;
+}
+
 static int batch_buffers(kq_model* m) {
   if (m->bh) return KQ_OK;
   const kq_config& c = m->c;
-  const size_t MM = MM_MAXM, QD = (size_t)c.n_heads * c.head_dim;
+  const size_t MM = MM_MAXM, QD = (size_t)m->nh_l * c.head_dim;   // this rank's heads
   bool ok = true;
   m->bh = dalloc<float>(m, MM * c.dim, ok);
   m->by = dalloc<float>(m, MM * c.dim, ok);
   m->bq = dalloc<float>(m, MM * QD, ok);
   m->bxd = dalloc<__half>(m, xp_halves(MM_MAXM, c.dim), ok);
   m->bxa = dalloc<__half>(m, xp_halves(MM_MAXM, (int)QD), ok);
-  m->bxf = dalloc<__half>(m, xp_halves(MM_MAXM, c.ffn), ok);
+  m->bxf = dalloc<__half>(m, xp_halves(MM_MAXM, m->ffn_l), ok);
   m->btok = dalloc<int>(m, MM, ok);
   m->bslot = dalloc<int>(m, MM, ok);
   m->brpos = dalloc<int>(m, MM, ok);
@@ -1319,8 +1427,8 @@ static int batch_buffers(kq_model* m) {
   // attention: key splits of up to 32, row groups of BA_ROWS query rows
   const int G = c.n_heads / c.n_kv_heads, rowgroups = (MM_MAXM * G + BA_ROWS - 1) / BA_ROWS;
   m->b_nsplit = BA_MAX_SPLIT;
-  m->bpart = dalloc<float>(m, (size_t)c.n_kv_heads * rowgroups * m->b_nsplit * BA_ROWS * BA_PLD, ok);
-  m->bticket = dalloc<int>(m, (size_t)c.n_kv_heads * rowgroups, ok);
+  m->bpart = dalloc<float>(m, (size_t)m->nkv_l * rowgroups * m->b_nsplit * BA_ROWS * BA_PLD, ok);
+  m->bticket = dalloc<int>(m, (size_t)m->nkv_l * rowgroups, ok);
   // GEMM split-K scratch: the largest of the pass's GEMMs
   const LayerW& w = m->L[0];
   const SegSpec qkv[3] = {{w.q, 0, nullptr, nullptr}, {w.k, 0, nullptr, nullptr}, {w.v, 0, nullptr, nullptr}};
@@ -1343,7 +1451,7 @@ static int batch_buffers(kq_model* m) {
 }
 
 static bool batch_supported(const kq_model* m) {
-  return m->c.ffn % 64 == 0 && (m->c.n_heads * m->c.head_dim) % 64 == 0;
+  return m->ffn_l % 64 == 0 && (m->nh_l * m->c.head_dim) % 64 == 0;
 }
 
 static int launch_tmm(kq_model* m, const SegSpec* ss, int nseg, const __half* xp, __half* xp_out, int out_ld,
@@ -1383,17 +1491,17 @@ static int launch_battn(kq_model* m, int layer, int npos, const BatchParams& B) 
   const kq_config& c = m->c;
   const int G = c.n_heads / c.n_kv_heads, M = B.M;
   const int rowgroups = (M * G + BA_ROWS - 1) / BA_ROWS, nblocks = (npos + BA_KB - 1) / BA_KB;
-  const int base = c.n_kv_heads * rowgroups;
+  const int base = m->nkv_l * rowgroups;
   int want = std::max(1, (2 * m->nsm + base - 1) / base);
   want = std::min(want, std::min(nblocks, m->b_nsplit));
   BAttnParams P;
   P.q = m->bq; P.kc = m->L[layer].kc; P.vc = m->L[layer].vc; P.out_xp = m->bxa; P.Npad = (M + 15) & ~15; P.B = B;
-  P.n_kv = c.n_kv_heads; P.ctx = c.ctx; P.npos = npos;
+  P.n_kv = m->nkv_l; P.ctx = c.ctx; P.npos = npos;
   P.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
   P.nblk = (nblocks + want - 1) / want;
   P.nsplit = (nblocks + P.nblk - 1) / P.nblk;
   P.part = m->bpart; P.ticket = m->bticket;
-  const dim3 grid((unsigned)c.n_kv_heads, (unsigned)rowgroups, (unsigned)P.nsplit), blk(BA_WARPS * 32);
+  const dim3 grid((unsigned)m->nkv_l, (unsigned)rowgroups, (unsigned)P.nsplit), blk(BA_WARPS * 32);
   cudaError_t e;
   if (G == 1) e = launch_pdl(k_battn<1>, grid, blk, BA_SMEM, m->stream, P);
   else if (G == 2) e = launch_pdl(k_battn<2>, grid, blk, BA_SMEM, m->stream, P);
@@ -1427,7 +1535,7 @@ static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int p
   CU(cudaMemcpyAsync(m->bmask, mk.data(), 2 * M * sizeof(unsigned long long), cudaMemcpyHostToDevice, s));
   BatchParams B;
   B.M = M; B.slot = m->bslot; B.rpos = m->brpos; B.mask = m->bmask; B.tree_base = pos;
-  const int QD = c.n_heads * c.head_dim;
+  const int QD = m->nh_l * c.head_dim;
   int rc;
   for (int l = 0; l < c.n_layers; ++l) {
     LayerW& w = m->L[l];
@@ -1437,18 +1545,35 @@ static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int p
     if ((rc = launch_battn(m, l, pos + b1, B))) return rc;
     SegSpec so[1] = {{w.o, EPI_F32, m->by, nullptr}};
     if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, c.dim, B))) return rc;
+    if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;   // row-split o: sum the partials
     if ((rc = launch_bnorm(m, M, false, w.ffn_norm, true))) return rc;
     SegSpec sg[1] = {{w.gu, EPI_SWIGLU, nullptr, nullptr}};
     if ((rc = launch_tmm(m, sg, 1, m->bxd, m->bxf, 0, B))) return rc;
     SegSpec sd[1] = {{w.down, EPI_F32, m->by, nullptr}};
     if ((rc = launch_tmm(m, sd, 1, m->bxf, nullptr, c.dim, B))) return rc;
+    if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;   // row-split down
   }
   if (!head) return KQ_OK;
   if ((rc = launch_bnorm(m, M, false, m->out_norm, true))) return rc;
-  const size_t V = (size_t)c.vocab;
+  const size_t V = (size_t)m->vocab_l;   // this rank's vocabulary slice
   SegSpec sh[1] = {{m->out, EPI_F32, m->vlogits + (size_t)b0 * V, nullptr}};
-  if ((rc = launch_tmm(m, sh, 1, m->bxd, nullptr, c.vocab, B))) return rc;
-  k_argmax_rows<<<M, 256, 0, s>>>(m->vlogits + (size_t)b0 * V, c.vocab, m->out_ids + b0);
+  if ((rc = launch_tmm(m, sh, 1, m->bxd, nullptr, (int)V, B))) return rc;
+  if (m->tp_world == 1) {
+    k_argmax_rows<<<M, 256, 0, s>>>(m->vlogits + (size_t)b0 * V, (int)V, m->out_ids + b0);
+    CU(cudaGetLastError());
+    return KQ_OK;
+  }
+  // vocabulary-split head: each rank's (best value, global id) per token, gathered, then the
+  // best over ranks (rank order = id order, so ties keep the lowest id)
+  const int W = m->tp_world;
+  float* sv = m->tp_val + (size_t)W * MM_MAXM;
+  int* si = m->tp_idx + (size_t)W * MM_MAXM;
+  k_argmax_rows_vi<<<M, 256, 0, s>>>(m->vlogits + (size_t)b0 * V, (int)V, m->tp_rank * (int)V, sv, si);
+  CU(cudaGetLastError());
+  if (nccl().AllGather(sv, m->tp_val, (size_t)MM_MAXM, ncclFloat32, m->comm, s) != ncclSuccess ||
+      nccl().AllGather(si, m->tp_idx, (size_t)MM_MAXM, ncclInt32, m->comm, s) != ncclSuccess)
+    return set_err(KQ_ERR_BACKEND, "NCCL all-gather of the head's argmax failed");
+  k_pick_rows<<<(M + 127) / 128, 128, 0, s>>>(m->tp_val, m->tp_idx, W, MM_MAXM, M, m->out_ids + b0);
   CU(cudaGetLastError());
   return KQ_OK;
 }
@@ -1464,9 +1589,10 @@ extern "C" int kq_verify(kq_model* m, const int32_t* tokens, const int32_t* pare
   for (int i = 0; i < n; ++i)
     if (tokens[i] < 0 || tokens[i] >= m->c.vocab) return set_err(KQ_ERR_ARG, "Invalid token in the draft tree");
   if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "draft tree runs past the context");
-  if ((rc = ensure_graphs(m)) || (rc = verify_buffers(m))) return rc;
-  const size_t V = (size_t)m->c.vocab;
-  const bool batched = !m->verify_seq && batch_supported(m);
+  if (m->tp_world > 1 && logits) return set_err(KQ_ERR_ARG, "a tensor-parallel shard holds a vocabulary slice: request best ids only");
+  if ((m->tp_world == 1 && (rc = ensure_graphs(m))) || (rc = verify_buffers(m))) return rc;
+  const size_t V = (size_t)m->vocab_l;
+  const bool batched = m->tp_world > 1 || (!m->verify_seq && batch_supported(m));
   if (batched) {
     if ((rc = batch_buffers(m))) return rc;
     for (int b0 = 0; b0 < n; b0 += MM_MAXM)
@@ -1502,7 +1628,7 @@ extern "C" int kq_accept(kq_model* m, const int32_t* tokens, const int32_t* pare
                          float temperature, const float* u_acc, const float* u_fin, int32_t* path, int32_t* out,
                          int32_t* path_len) {
   int rc = model_check(m);
-  if (rc) return rc;
+  if (rc || (rc = not_tp(m, "kq_accept"))) return rc;
   int depth[KQ_MAX_TREE];
   unsigned long long anc[KQ_MAX_TREE][2];
   if ((rc = tree_check(parents, n, depth, anc))) return rc;
@@ -1550,7 +1676,7 @@ extern "C" int kq_commit(kq_model* m, const int32_t* path, int k, int pos) {
   CU(cudaMemcpyAsync(m->apath, path, (size_t)(k + 1) * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
   CommitParams C;
   C.caches = m->caches; C.path = m->apath; C.k = k; C.pos = pos;
-  C.n_kv = m->c.n_kv_heads; C.ctx = m->c.ctx; C.hd = m->c.head_dim;
+  C.n_kv = m->nkv_l; C.ctx = m->c.ctx; C.hd = m->c.head_dim;
   k_commit<<<2 * m->c.n_layers, 256, 0, m->stream>>>(C);
   CU(cudaGetLastError());
   CU(cudaStreamSynchronize(m->stream));

@@ -380,4 +380,44 @@ __global__ void __launch_bounds__(256) k_argmax_rows(const float* logits, int V,
   }
 }
 
+// Tensor-parallel head: per-token (best value, global id) of this rank's vocabulary slice, whose
+// first id is idx_off (lowest id on ties).
+__global__ void __launch_bounds__(256) k_argmax_rows_vi(const float* logits, int V, int idx_off, float* out_v, int* out_i) {
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float bv[8];
+  __shared__ int bi[8];
+  float v = -INFINITY;
+  int vi = 0x7fffffff;
+  const float* z = logits + (size_t)t * V;
+  for (int i = tid; i < V; i += 256) {
+    const float x = z[i];
+    if (x > v || (x == v && i < vi)) { v = x; vi = i; }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, vi, off);
+    if (ov > v || (ov == v && oi < vi)) { v = ov; vi = oi; }
+  }
+  if (lane == 0) { bv[warp] = v; bi[warp] = vi; }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < 8; ++w)
+      if (bv[w] > v || (bv[w] == v && bi[w] < vi)) { v = bv[w]; vi = bi[w]; }
+    out_v[t] = v;
+    out_i[t] = (vi == 0x7fffffff ? 0 : vi) + idx_off;
+  }
+}
+// The best over the ranks' gathered rows [W][ld] for each of M tokens: rank order is id order,
+// so a strict > keeps the lowest id on ties.
+__global__ void k_pick_rows(const float* val, const int* idx, int W, int ld, int M, int* out) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= M) return;
+  float v = val[t];
+  int vi = idx[t];
+  for (int r = 1; r < W; ++r)
+    if (val[(size_t)r * ld + t] > v) { v = val[(size_t)r * ld + t]; vi = idx[(size_t)r * ld + t]; }
+  out[t] = vi;
+}
+
 }  // namespace kq

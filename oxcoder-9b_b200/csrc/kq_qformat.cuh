@@ -163,8 +163,13 @@ __device__ inline void scatter_block(const QViewW& m, int d, int g, const uint8_
 
 // One thread per (source row, block): block from `src` (GGUF row-major bytes of R_src rows) or,
 // if src == nullptr, from the generator (stream, seed); written to device row map_row(s).
+// A tensor-parallel shard draws the blocks of the full matrix it is a slice of: generator block
+// index (s + sh.row_off) * sh.G_src + (g + sh.g_off), with G_src the full matrix's super-blocks.
+struct ShardMap {
+  int row_off, g_off, G_src;   // {0, 0, G}: the whole matrix
+};
 __global__ void k_qmat_write(QViewW m, int R_src, const uint8_t* __restrict__ src, uint64_t base,
-                             int mode, int arg) {
+                             int mode, int arg, ShardMap sh) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)R_src * m.G) return;
   const int s = (int)(idx / m.G), g = (int)(idx % m.G);
@@ -174,9 +179,9 @@ __global__ void k_qmat_write(QViewW m, int R_src, const uint8_t* __restrict__ sr
     const uint8_t* p = src + ((size_t)s * m.G + g) * bs;
     for (int i = 0; i < bs; i++) b[i] = p[i];
   } else if (m.type == Q4K) {
-    gen_q4k_block(base, (uint64_t)s * m.G + g, b);
+    gen_q4k_block(base, (uint64_t)(s + sh.row_off) * sh.G_src + (uint64_t)(g + sh.g_off), b);
   } else {
-    gen_q6k_block(base, (uint64_t)s * m.G + g, b);
+    gen_q6k_block(base, (uint64_t)(s + sh.row_off) * sh.G_src + (uint64_t)(g + sh.g_off), b);
   }
   scatter_block(m, map_row(s, mode, arg), g, b);
 }

@@ -58,6 +58,9 @@ SIGNATURES = {
     "kq_config_default": (None, [C.POINTER(Config)]),
     "kq_model_create": (C.c_void_p, [C.POINTER(Config), C.c_int]),
     "kq_model_free": (None, [C.c_void_p]),
+    "kq_tp_unique_id": (C.c_int, [C.c_char_p]),
+    "kq_model_create_tp": (C.c_void_p, [C.POINTER(Config), C.c_int, C.c_int, C.c_int, C.c_char_p]),
+    "kq_model_tp": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "kq_model_fill_synthetic": (C.c_int, [C.c_void_p, C.c_uint64]),
     "kq_model_set_tensor": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
     "kq_model_reset": (C.c_int, [C.c_void_p]),
@@ -199,17 +202,34 @@ def time_matvec(mats, n):
 
 
 # ----------------------------------------------------------------------------- engine
+def tp_unique_id():
+    """A fresh NCCL unique id (128 bytes) for kq.Engine(tp=(rank, world, id)); one rank makes it
+    and every rank passes the same bytes."""
+    buf = C.create_string_buffer(128)
+    check(lib().kq_tp_unique_id(buf))
+    return buf.raw
+
+
 class Engine(object):
     """Dense GQA decoder on one B200 (the gpu4.Engine interface).
 
     config: a Config (default: the BASELINE config-2 model). seed: fill every tensor from the
-    seeded synthetic generator (None leaves the weights to set_tensor)."""
+    seeded synthetic generator (None leaves the weights to set_tensor). tp=(rank, world, id):
+    this process's shard of a tensor-parallel model over `world` GPUs (one process per GPU, the
+    same 128-byte NCCL id from tp_unique_id() on every rank); it returns when all ranks joined."""
 
-    def __init__(self, config=None, device=0, seed=0, **overrides):
+    def __init__(self, config=None, device=0, seed=0, tp=None, **overrides):
         self.config = config if config is not None else Config.default(**overrides)
         self.ctx = self.config.ctx
         self.vocab = self.config.vocab
-        h = lib().kq_model_create(C.byref(self.config), device)
+        self.tp = tp
+        if tp is not None:
+            rank, world, uid = tp
+            if len(uid) != 128:
+                raise ValueError("the NCCL id is 128 bytes")
+            h = lib().kq_model_create_tp(C.byref(self.config), device, int(rank), int(world), bytes(uid))
+        else:
+            h = lib().kq_model_create(C.byref(self.config), device)
         if not h:
             msg = last_error()
             raise (MemoryError if "alloc" in msg else ValueError)(msg)
@@ -245,7 +265,10 @@ class Engine(object):
         check(lib().kq_model_fill_kv(self.h, npos, seed))
 
     def get_kv(self, layer, which, npos):
-        out = np.empty(npos * self.config.n_kv_heads * self.config.head_dim, np.uint16)
+        """K (which 0) or V (1) cache rows [0, npos) as fp16 bits in the order [pos][kv][hd]; a
+        tensor-parallel shard returns its own KV heads."""
+        nkv = self.config.n_kv_heads // (self.tp[1] if self.tp is not None else 1)
+        out = np.empty(npos * nkv * self.config.head_dim, np.uint16)
         check(lib().kq_model_get_kv(self.h, layer, which, npos, _ptr(out, PU16)))
         return out
 

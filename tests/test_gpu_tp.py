@@ -1,0 +1,85 @@
+"""GPU, 2+ devices: the tensor-parallel model (kq_model_create_tp) against the whole model.
+
+Each rank is a process on its own GPU holding its shard (KV heads, FFN slice, vocabulary slice)
+joined by NCCL; the batched pass all-reduces the o and down partials and all-gathers the head's
+argmax. Bars: every rank's K/V cache heads after a prefill within 1e-3 rel-L2 of the same heads
+of the whole model on one GPU, and the greedy steps that follow identical. Skips with fewer
+than two GPUs (the round-end suite runs on one); run under `gpurun --gpus 2`."""
+import multiprocessing as mp
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(D=1024, NL=2, NH=8, NKV=2, HD=128, NFF=2048, vocab=4096, ctx=512)
+HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(os.path.dirname(HERE), "oxcoder-9b_b200")
+
+
+def _cfg(kq, t):
+    return kq.Config.default(dim=t["D"], n_layers=t["NL"], n_heads=t["NH"], n_kv_heads=t["NKV"], head_dim=t["HD"],
+                             ffn=t["NFF"], vocab=t["vocab"], ctx=t["ctx"])
+
+
+def _run(kq, e, prompt, npos, nsteps):
+    e.fill_kv(npos, 4)
+    e.feed_batch(prompt, npos)
+    end = npos + len(prompt)
+    toks, t = [], prompt[-1]
+    for i in range(nsteps):
+        t = e.step(t, end + i)
+        toks.append(t)
+    kv = [[e.get_kv(l, w, end) for w in (0, 1)] for l in range(CFG["NL"])]
+    return toks, kv
+
+
+def _rank_main(rank, world, uid, prompt, npos, nsteps, q):
+    try:
+        sys.path.insert(0, PKG)
+        import kq
+        e = kq.Engine(_cfg(kq, CFG), device=rank, seed=0, tp=(rank, world, uid))
+        q.put((rank, _run(kq, e, prompt, npos, nsteps)))
+        e.close()
+    except Exception as ex:   # reported to the parent
+        q.put((rank, repr(ex)))
+
+
+@pytest.fixture(scope="module")
+def kq():
+    import kq as K
+    return K
+
+
+@pytest.mark.parametrize("world", [2])
+def test_tp_prefill_and_steps_match_whole_model(kq, world):
+    if kq.lib().kq_device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    rng = np.random.default_rng(3)
+    prompt = [int(v) for v in rng.integers(0, CFG["vocab"], 70)]
+    npos, nsteps = 30, 6
+    uid = kq.tp_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, uid, prompt, npos, nsteps, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert not isinstance(res[r], str), res[r]
+    whole = kq.Engine(_cfg(kq, CFG), device=0, seed=0)
+    toks, kv = _run(kq, whole, prompt, npos, nsteps)
+    nkv_l, hd, end = CFG["NKV"] // world, CFG["HD"], npos + len(prompt)
+    for r in range(world):
+        assert res[r][0] == toks, (r, res[r][0], toks)
+        for l in range(CFG["NL"]):
+            for w in (0, 1):
+                got = res[r][1][l][w].view(np.float16).astype(np.float32).reshape(end, nkv_l, hd)
+                ref = kv[l][w].view(np.float16).astype(np.float32).reshape(end, CFG["NKV"], hd)[:, r * nkv_l:(r + 1) * nkv_l]
+                assert rel_l2(got, ref) < 1e-3, (r, l, w)
