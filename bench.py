@@ -205,6 +205,39 @@ def prefill_bench(e, vocab, n, reps=3):
     return {"prompt": n, "ms": ms, "tok_s": n / (ms / 1e3)}
 
 
+TP_PROMPT = 8192
+# config-4 prefill work per 8192-token sequence: 2 x 6.17e9 weights x tokens (linear, no head) +
+# causal attention 4 x 32 heads x 128 x T^2 / 2 x 32 layers = 101.2 + 17.6 TFLOP
+TP_PREFILL_FLOP = 2.0 * 6.1740e9 * TP_PROMPT + 4.0 * 32 * 128 * (TP_PROMPT ** 2) / 2.0 * 32
+
+
+def tp_prefill_bench(kq, dist, rank, world, local, peak_tflops):
+    """Config-4 prefill: one 8192-token prompt through the tensor-parallel model over all ranks
+    (KV heads / FFN / vocabulary split, NCCL all-reduce after o and down), host-timed around the
+    synchronising kq_feed_batch on every rank, max over ranks."""
+    import numpy as np
+    import torch
+    obj = [kq.tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    e = kq.Engine(kq.Config.default(ctx=TP_PROMPT + 256), device=local, seed=0, tp=(rank, world, obj[0]))
+    ids = np.random.default_rng(1).integers(0, e.vocab, TP_PROMPT).astype(np.int32)
+    e.feed_batch(ids[:512], 0)   # warm-up
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    e.feed_batch(ids, 0)
+    dt = time.perf_counter() - t0
+    t = torch.tensor([dt], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    e.close()
+    achieved = TP_PREFILL_FLOP / dt / 1e12
+    return {"world": world, "prompt": TP_PROMPT, "ms": 1e3 * dt, "tok_s": TP_PROMPT / dt,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tflops * world, "unit": "TFLOP/s",
+                         "frac": achieved / (peak_tflops * world), "flop": TP_PREFILL_FLOP,
+                         "note": "algorithmic flops; the split-precision GEMM issues 2 MMAs per 16 columns"}}
+
+
 def run_profile_mode(args):
     """decode-only: fill the config-2 model (optionally fewer layers), W + K device-resident
     decode steps at ctx 4K. gemv-only: the config-0 Q4_K GEMV over 16 rotating copies."""
@@ -315,6 +348,10 @@ def main():
     spec = spec_bench(e, e.vocab, 8, 3)
     prefill = prefill_bench(e, e.vocab, 512)
     e.close()
+    tp = None
+    if dist is not None:
+        pk0 = peaks()
+        tp = tp_prefill_bench(kq, dist, rank, world, local, pk0["bf16_tflops"] if pk0 else 1590.0)
 
     # ---- the dominant kernel: config-0 Q4_K GEMV over 16 rotating weight copies (453 MB > L2)
     mats = [kq.QMat(12, 12288, 4096, device=local).fill_synthetic(0, 1000 + i) for i in range(16)]
@@ -358,6 +395,7 @@ def main():
             "spec": spec,
             "prefill_tok_s": prefill["tok_s"] * world,
             "prefill": prefill,
+            "tp_prefill": tp,
             "cpu_baseline": cb,
         }
         print(json.dumps(line), flush=True)
