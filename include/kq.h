@@ -133,6 +133,14 @@ int kq_verify(kq_model* m, const int32_t* tokens, const int32_t* parents, int n,
 int kq_accept(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, const float* draft_logits,
               float temperature, const float* u_acc, const float* u_fin, int32_t* path, int32_t* out,
               int32_t* path_len);
+/* Draft distributions resident on the device (a drafter on the GPU writes its logits there):
+ * kq_draft_logits gives the model's buffer (KQ_MAX_TREE rows of `ld` = vocab floats, row v = the
+ * distribution v's children were drawn from), kq_draft_upload fills rows [0, n) from the host,
+ * and kq_accept_resident is kq_accept reading the draft logits from that buffer. */
+int kq_draft_logits(kq_model* m, float** dev, int* ld);
+int kq_draft_upload(kq_model* m, const float* host, int n);
+int kq_accept_resident(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, float temperature,
+                       const float* u_acc, const float* u_fin, int32_t* path, int32_t* out, int32_t* path_len);
 /* K/V compaction: the K/V rows of path[1..k] (increasing node ids, path[0] = 0) move from slots
  * pos + path[j] to positions pos + j, so the accepted tokens sit at consecutive positions. */
 int kq_commit(kq_model* m, const int32_t* path, int k, int pos);

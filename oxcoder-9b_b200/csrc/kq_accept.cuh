@@ -199,14 +199,27 @@ __global__ void __launch_bounds__(ACC_THREADS, 1) k_accept(const AcceptParams A)
             }
             prefix = __fadd_rn(prefix, sh.bs[b]);
           }
-          if (pick < 0) {
-            pick = 0;
-            for (int i = V - 1; i >= 0; --i)
-              if (A.p[i] > 0.0f) { pick = i; break; }
-          }
           sh.pick = pick;
-          A.out[no] = pick;
         }
+        __syncthreads();
+        if (sh.pick < 0) {
+          // rounding left the target above every running sum: the largest id with p > 0 (0 if
+          // none), as a block-wide max instead of one thread scanning down the vocabulary
+          int hi = -1;
+          for (int i = tid; i < V; i += ACC_THREADS)
+            if (A.p[i] > 0.0f) hi = i;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, off));
+          if ((tid & 31) == 0) sh.fidx[tid >> 5] = hi;
+          __syncthreads();
+          if (tid == 0) {
+            int b = -1;
+            for (int w = 0; w < ACC_THREADS / 32; ++w) b = max(b, sh.fidx[w]);
+            sh.pick = b < 0 ? 0 : b;
+          }
+          __syncthreads();
+        }
+        if (tid == 0) A.out[no] = sh.pick;
         __syncthreads();
         ++no;
         break;

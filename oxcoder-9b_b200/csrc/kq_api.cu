@@ -1624,11 +1624,15 @@ extern "C" int kq_verify(kq_model* m, const int32_t* tokens, const int32_t* pare
   return check_dev_err(m);
 }
 
-extern "C" int kq_accept(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, const float* draft_logits,
-                         float temperature, const float* u_acc, const float* u_fin, int32_t* path, int32_t* out,
-                         int32_t* path_len) {
+// draft_logits: host rows copied in (kq_accept), or null with `resident`: the rows are already in
+// the model's device buffer (kq_accept_resident; a drafter on the GPU writes there, see
+// kq_draft_logits).
+static int accept_impl(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, const float* draft_logits,
+                       bool resident, float temperature, const float* u_acc, const float* u_fin, int32_t* path,
+                       int32_t* out, int32_t* path_len) {
   int rc = model_check(m);
   if (rc || (rc = not_tp(m, "kq_accept"))) return rc;
+  if (resident) draft_logits = m->ag;
   int depth[KQ_MAX_TREE];
   unsigned long long anc[KQ_MAX_TREE][2];
   if ((rc = tree_check(parents, n, depth, anc))) return rc;
@@ -1646,7 +1650,7 @@ extern "C" int kq_accept(kq_model* m, const int32_t* tokens, const int32_t* pare
   std::memset(&A, 0, sizeof(A));
   A.tau = temperature > 0.0f ? 1.0f / temperature : 0.0f;
   if (A.tau > 0.0f) {
-    CU(cudaMemcpyAsync(m->ag, draft_logits, n * V * sizeof(float), cudaMemcpyHostToDevice, s));
+    if (!resident) CU(cudaMemcpyAsync(m->ag, draft_logits, n * V * sizeof(float), cudaMemcpyHostToDevice, s));
     CU(cudaMemcpyAsync(m->auacc, u_acc, n * sizeof(float), cudaMemcpyHostToDevice, s));
     CU(cudaMemcpyAsync(m->aufin, u_fin, n * sizeof(float), cudaMemcpyHostToDevice, s));
   }
@@ -1662,6 +1666,30 @@ extern "C" int kq_accept(kq_model* m, const int32_t* tokens, const int32_t* pare
   CU(cudaMemcpy(path, m->apath, cnt[1] * sizeof(int32_t), cudaMemcpyDeviceToHost));
   if (path_len) *path_len = cnt[1];
   return cnt[0];
+}
+
+extern "C" int kq_accept(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, const float* draft_logits,
+                         float temperature, const float* u_acc, const float* u_fin, int32_t* path, int32_t* out,
+                         int32_t* path_len) {
+  return accept_impl(m, tokens, parents, n, draft_logits, false, temperature, u_acc, u_fin, path, out, path_len);
+}
+extern "C" int kq_accept_resident(kq_model* m, const int32_t* tokens, const int32_t* parents, int n, float temperature,
+                                  const float* u_acc, const float* u_fin, int32_t* path, int32_t* out, int32_t* path_len) {
+  return accept_impl(m, tokens, parents, n, nullptr, true, temperature, u_acc, u_fin, path, out, path_len);
+}
+extern "C" int kq_draft_logits(kq_model* m, float** dev, int* ld) {
+  int rc = model_check(m);
+  if (rc || (rc = not_tp(m, "kq_draft_logits")) || (rc = verify_buffers(m))) return rc;
+  if (dev) *dev = m->ag;
+  if (ld) *ld = m->c.vocab;
+  return KQ_OK;
+}
+extern "C" int kq_draft_upload(kq_model* m, const float* host, int n) {
+  int rc = model_check(m);
+  if (rc || (rc = not_tp(m, "kq_draft_upload")) || (rc = verify_buffers(m))) return rc;
+  if (!host || n < 1 || n > KQ_MAX_TREE) return set_err(KQ_ERR_ARG, "bad draft logits");
+  CU(cudaMemcpy(m->ag, host, (size_t)n * m->c.vocab * sizeof(float), cudaMemcpyHostToDevice));
+  return KQ_OK;
 }
 
 extern "C" int kq_commit(kq_model* m, const int32_t* path, int k, int pos) {

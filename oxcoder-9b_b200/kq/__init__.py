@@ -87,6 +87,9 @@ SIGNATURES = {
     "kq_qmat_argmax_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "kq_verify": (C.c_int, [C.c_void_p, PI32, PI32, C.c_int, C.c_int, PF, PI32]),
     "kq_accept": (C.c_int, [C.c_void_p, PI32, PI32, C.c_int, PF, C.c_float, PF, PF, PI32, PI32, PI32]),
+    "kq_accept_resident": (C.c_int, [C.c_void_p, PI32, PI32, C.c_int, C.c_float, PF, PF, PI32, PI32, PI32]),
+    "kq_draft_logits": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_int)]),
+    "kq_draft_upload": (C.c_int, [C.c_void_p, PF, C.c_int]),
     "kq_commit": (C.c_int, [C.c_void_p, PI32, C.c_int, C.c_int]),
 }
 
@@ -328,22 +331,39 @@ class Engine(object):
                               _ptr(logits) if logits is not None else None, _ptr(best, PI32)))
         return best, logits
 
-    def accept(self, tokens, parents, draft_logits=None, temperature=0.0, u_acc=None, u_fin=None):
-        """On-device acceptance over the last verify pass: (accepted node path, emitted tokens)."""
+    def accept(self, tokens, parents, draft_logits=None, temperature=0.0, u_acc=None, u_fin=None, resident=False):
+        """On-device acceptance over the last verify pass: (accepted node path, emitted tokens).
+        resident=True: the draft logits are the rows already on the device (upload_draft, or a
+        drafter writing draft_logits_device()), not copied from the host."""
         t = np.ascontiguousarray(tokens, np.int32)
         par = np.ascontiguousarray(parents, np.int32)
         n = len(t)
-        g = _f32(draft_logits) if draft_logits is not None else None
+        g = _f32(draft_logits) if draft_logits is not None and not resident else None
         ua = _f32(u_acc) if u_acc is not None else None
         uf = _f32(u_fin) if u_fin is not None else None
         path = np.empty(n + 1, np.int32)
         out = np.empty(n + 1, np.int32)
         plen = C.c_int32()
-        no = check(lib().kq_accept(self.h, _ptr(t, PI32), _ptr(par, PI32), n,
-                                   _ptr(g) if g is not None else None, float(temperature),
-                                   _ptr(ua) if ua is not None else None, _ptr(uf) if uf is not None else None,
-                                   _ptr(path, PI32), _ptr(out, PI32), C.byref(plen)))
+        pua = _ptr(ua) if ua is not None else None
+        puf = _ptr(uf) if uf is not None else None
+        if resident:
+            no = check(lib().kq_accept_resident(self.h, _ptr(t, PI32), _ptr(par, PI32), n, float(temperature), pua, puf,
+                                                _ptr(path, PI32), _ptr(out, PI32), C.byref(plen)))
+        else:
+            no = check(lib().kq_accept(self.h, _ptr(t, PI32), _ptr(par, PI32), n, _ptr(g) if g is not None else None,
+                                       float(temperature), pua, puf, _ptr(path, PI32), _ptr(out, PI32), C.byref(plen)))
         return [int(v) for v in path[:plen.value]], [int(v) for v in out[:no]]
+
+    def upload_draft(self, draft_logits):
+        """Copy draft logits (n x vocab) into the device buffer accept(resident=True) reads."""
+        g = _f32(draft_logits)
+        check(lib().kq_draft_upload(self.h, _ptr(g), g.shape[0]))
+
+    def draft_logits_device(self):
+        """(device pointer, row length) of the resident draft-logit buffer, for a GPU drafter."""
+        p, ld = C.c_void_p(), C.c_int()
+        check(lib().kq_draft_logits(self.h, C.byref(p), C.byref(ld)))
+        return p.value, ld.value
 
     def commit(self, path, pos):
         """K/V compaction of an accepted path (path[0] = 0)."""

@@ -126,6 +126,26 @@ def test_accept_bit_exact_with_oracle(kq, oracle, temperature, branching, seed):
         assert out[j - 1] == toks[path[j]]
 
 
+def test_accept_resident_draft_equals_host_draft(kq):
+    """Draft logits already on the device (kq_draft_upload + kq_accept_resident) give the same
+    decision as the host copy."""
+    e = kq.Engine(kq_cfg(kq, TINY), seed=0)
+    rng = np.random.default_rng(21)
+    e.fill_kv(50, 5)
+    parents = tree_from_branching([3, 2])
+    n = len(parents)
+    toks = [int(v) for v in rng.integers(0, TINY["vocab"], n)]
+    g = rng.normal(0.0, 2.0, (n, TINY["vocab"])).astype(np.float32)
+    ua, uf = rng.random(n).astype(np.float32), rng.random(n).astype(np.float32)
+    e.verify(toks, parents, 50, want_logits=False)
+    a = e.accept(toks, parents, g, 0.9, ua, uf)
+    e.upload_draft(g)
+    b = e.accept(toks, parents, None, 0.9, ua, uf, resident=True)
+    assert a == b
+    ptr, ld = e.draft_logits_device()
+    assert ptr and ld == TINY["vocab"]
+
+
 def test_accept_full_path_when_draft_equals_target(kq, oracle):
     """q = p: every draft is accepted (u * q(d) < p(d) for u < 1)."""
     e = kq.Engine(kq_cfg(kq, TINY), seed=0)
