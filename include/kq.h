@@ -145,6 +145,18 @@ int kq_accept_resident(kq_model* m, const int32_t* tokens, const int32_t* parent
  * pos + path[j] to positions pos + j, so the accepted tokens sit at consecutive positions. */
 int kq_commit(kq_model* m, const int32_t* path, int k, int pos);
 
+/* ------------------------------------------------------------------ batched decode of many sequences
+ * Config-4 decode (no counterpart in the reference's Q4 path, which decodes one sequence): every
+ * sequence has its own K/V cache ([n_kv][ctx][hd] per layer and tensor, on a tensor-parallel
+ * shard its own KV heads), and a step takes one token per sequence through the batched pass, so
+ * the weights stream once for all of them. kq_batch_caches allocates the caches (zeroed) for
+ * n_seq sequences; kq_batch_feed prefills sequence `seq` from `pos`; kq_batch_step runs one token
+ * of each of n <= 128 distinct sequences (token toks[i] at position pos[i] of sequence seqs[i],
+ * attending to [0, pos[i]]) and writes their greedy ids to out. */
+int kq_batch_caches(kq_model* m, int n_seq);
+int kq_batch_feed(kq_model* m, int seq, const int32_t* toks, int n, int pos);
+int kq_batch_step(kq_model* m, const int32_t* seqs, const int32_t* toks, const int32_t* pos, int n, int32_t* out);
+
 /* ------------------------------------------------------------------ matrix hooks
  * kc_matvec / kc_dequant equivalents (kcpu4.c:337-341, q4kernels.h:12-36). */
 kq_qmat* kq_qmat_create(int type, int rows, int cols, int device);

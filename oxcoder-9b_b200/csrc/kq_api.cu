@@ -417,6 +417,7 @@ struct LayerW {
   kq_qmat *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
   float *attn_norm = nullptr, *ffn_norm = nullptr;
   __half *kc = nullptr, *vc = nullptr;
+  __half *bkc = nullptr, *bvc = nullptr;   // batched decode: [n_seq][n_kv][ctx][hd] per tensor
 };
 
 struct kq_model {
@@ -430,6 +431,9 @@ struct kq_model {
   int tp_rank = 0, tp_world = 1;
   int nh_l = 0, nkv_l = 0, ffn_l = 0, vocab_l = 0;
   ncclComm_t comm = nullptr;
+  int n_seq = 0;                    // sequences of the batched-decode caches (kq_batch_caches)
+  int *bseq = nullptr, *bposv = nullptr;   // [MM_MAXM] per-token sequence / position of a batched step
+  float* dpart = nullptr;           // batched decode attention partials
   float* tp_val = nullptr;          // [world][MM_MAXM] head argmax values of every rank
   int* tp_idx = nullptr;            // [world][MM_MAXM] their (global) ids
   cudaStream_t stream = nullptr;
@@ -1161,7 +1165,8 @@ static int verify_buffers(kq_model* m);
 static int batch_buffers(kq_model* m);
 static bool batch_supported(const kq_model* m);
 static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int pos, const int* depth,
-                       const unsigned long long (*anc)[2], bool head = true);
+                       const unsigned long long (*anc)[2], bool head = true, int seq = -1);
+static int head_argmax(kq_model* m, int M, const BatchParams& B, int* out_ids, size_t row0 = 0);
 
 // Ancestor masks of a linear chain of MM_MAXM tokens: token j attends to tokens 0..j.
 struct ChainMasks {
@@ -1466,6 +1471,7 @@ static int launch_tmm(kq_model* m, const SegSpec* ss, int nseg, const __half* xp
   P.sin_t = m->sin_t;
   P.hd = m->c.head_dim;
   P.ctx = m->c.ctx;
+  P.nkv = m->nkv_l;
   P.part = m->tpart;
   P.ticket = m->tticket;
   P.err = m->err;
@@ -1487,7 +1493,7 @@ static int launch_bnorm(kq_model* m, int M, bool embed, const float* gamma, bool
   return KQ_OK;
 }
 
-static int launch_battn(kq_model* m, int layer, int npos, const BatchParams& B) {
+static int launch_battn(kq_model* m, const __half* kc, const __half* vc, int npos, const BatchParams& B) {
   const kq_config& c = m->c;
   const int G = c.n_heads / c.n_kv_heads, M = B.M;
   const int rowgroups = (M * G + BA_ROWS - 1) / BA_ROWS, nblocks = (npos + BA_KB - 1) / BA_KB;
@@ -1495,7 +1501,7 @@ static int launch_battn(kq_model* m, int layer, int npos, const BatchParams& B) 
   int want = std::max(1, (2 * m->nsm + base - 1) / base);
   want = std::min(want, std::min(nblocks, m->b_nsplit));
   BAttnParams P;
-  P.q = m->bq; P.kc = m->L[layer].kc; P.vc = m->L[layer].vc; P.out_xp = m->bxa; P.Npad = (M + 15) & ~15; P.B = B;
+  P.q = m->bq; P.kc = kc; P.vc = vc; P.out_xp = m->bxa; P.Npad = (M + 15) & ~15; P.B = B;
   P.n_kv = m->nkv_l; P.ctx = c.ctx; P.npos = npos;
   P.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
   P.nblk = (nblocks + want - 1) / want;
@@ -1516,7 +1522,7 @@ static int launch_battn(kq_model* m, int layer, int npos, const BatchParams& B) 
 // slots below pos and its ancestors (anc, bits relative to pos). With `head`: logits to vlogits
 // rows b0.., argmax ids to out_ids[b0..]; without (prefill): the K/V cache only.
 static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int pos, const int* depth,
-                       const unsigned long long (*anc)[2], bool head) {
+                       const unsigned long long (*anc)[2], bool head, int seq) {
   const kq_config& c = m->c;
   const int M = b1 - b0;
   std::vector<int> tk(M), sl(M), rp(M);
@@ -1534,15 +1540,18 @@ static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int p
   CU(cudaMemcpyAsync(m->brpos, rp.data(), M * sizeof(int), cudaMemcpyHostToDevice, s));
   CU(cudaMemcpyAsync(m->bmask, mk.data(), 2 * M * sizeof(unsigned long long), cudaMemcpyHostToDevice, s));
   BatchParams B;
-  B.M = M; B.slot = m->bslot; B.rpos = m->brpos; B.mask = m->bmask; B.tree_base = pos;
+  B.M = M; B.slot = m->bslot; B.rpos = m->brpos; B.mask = m->bmask; B.tree_base = pos; B.seq = nullptr;
+  const size_t sstride = (size_t)m->nkv_l * c.ctx * c.head_dim;   // one sequence of the batched-decode caches
   const int QD = m->nh_l * c.head_dim;
   int rc;
   for (int l = 0; l < c.n_layers; ++l) {
     LayerW& w = m->L[l];
     if ((rc = launch_bnorm(m, M, l == 0, w.attn_norm, l > 0))) return rc;
-    SegSpec qkv[3] = {{w.q, EPI_ROPE_Q, m->bq, nullptr}, {w.k, EPI_ROPE_K, nullptr, w.kc}, {w.v, EPI_V, nullptr, w.vc}};
+    __half* kc = seq < 0 ? w.kc : w.bkc + (size_t)seq * sstride;
+    __half* vc = seq < 0 ? w.vc : w.bvc + (size_t)seq * sstride;
+    SegSpec qkv[3] = {{w.q, EPI_ROPE_Q, m->bq, nullptr}, {w.k, EPI_ROPE_K, nullptr, kc}, {w.v, EPI_V, nullptr, vc}};
     if ((rc = launch_tmm(m, qkv, 3, m->bxd, nullptr, QD, B))) return rc;
-    if ((rc = launch_battn(m, l, pos + b1, B))) return rc;
+    if ((rc = launch_battn(m, kc, vc, pos + b1, B))) return rc;
     SegSpec so[1] = {{w.o, EPI_F32, m->by, nullptr}};
     if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, c.dim, B))) return rc;
     if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;   // row-split o: sum the partials
@@ -1554,12 +1563,20 @@ static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int p
     if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;   // row-split down
   }
   if (!head) return KQ_OK;
+  return head_argmax(m, M, B, m->out_ids + b0, (size_t)b0);
+}
+
+// Final norm, output head and per-token greedy id of a batched pass's M tokens (logits to vlogits
+// rows row0.., ids to out_ids); a tensor-parallel rank gathers the ranks' (value, id) pairs.
+static int head_argmax(kq_model* m, int M, const BatchParams& B, int* out_ids, size_t row0) {
+  int rc;
+  cudaStream_t s = m->stream;
   if ((rc = launch_bnorm(m, M, false, m->out_norm, true))) return rc;
   const size_t V = (size_t)m->vocab_l;   // this rank's vocabulary slice
-  SegSpec sh[1] = {{m->out, EPI_F32, m->vlogits + (size_t)b0 * V, nullptr}};
+  SegSpec sh[1] = {{m->out, EPI_F32, m->vlogits + row0 * V, nullptr}};
   if ((rc = launch_tmm(m, sh, 1, m->bxd, nullptr, (int)V, B))) return rc;
   if (m->tp_world == 1) {
-    k_argmax_rows<<<M, 256, 0, s>>>(m->vlogits + (size_t)b0 * V, (int)V, m->out_ids + b0);
+    k_argmax_rows<<<M, 256, 0, s>>>(m->vlogits + row0 * V, (int)V, out_ids);
     CU(cudaGetLastError());
     return KQ_OK;
   }
@@ -1568,12 +1585,12 @@ static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int p
   const int W = m->tp_world;
   float* sv = m->tp_val + (size_t)W * MM_MAXM;
   int* si = m->tp_idx + (size_t)W * MM_MAXM;
-  k_argmax_rows_vi<<<M, 256, 0, s>>>(m->vlogits + (size_t)b0 * V, (int)V, m->tp_rank * (int)V, sv, si);
+  k_argmax_rows_vi<<<M, 256, 0, s>>>(m->vlogits + row0 * V, (int)V, m->tp_rank * (int)V, sv, si);
   CU(cudaGetLastError());
   if (nccl().AllGather(sv, m->tp_val, (size_t)MM_MAXM, ncclFloat32, m->comm, s) != ncclSuccess ||
       nccl().AllGather(si, m->tp_idx, (size_t)MM_MAXM, ncclInt32, m->comm, s) != ncclSuccess)
     return set_err(KQ_ERR_BACKEND, "NCCL all-gather of the head's argmax failed");
-  k_pick_rows<<<(M + 127) / 128, 128, 0, s>>>(m->tp_val, m->tp_idx, W, MM_MAXM, M, m->out_ids + b0);
+  k_pick_rows<<<(M + 127) / 128, 128, 0, s>>>(m->tp_val, m->tp_idx, W, MM_MAXM, M, out_ids);
   CU(cudaGetLastError());
   return KQ_OK;
 }
@@ -1690,6 +1707,122 @@ extern "C" int kq_draft_upload(kq_model* m, const float* host, int n) {
   if (!host || n < 1 || n > KQ_MAX_TREE) return set_err(KQ_ERR_ARG, "bad draft logits");
   CU(cudaMemcpy(m->ag, host, (size_t)n * m->c.vocab * sizeof(float), cudaMemcpyHostToDevice));
   return KQ_OK;
+}
+
+// ------------------------------------------------------------------------------ batched decode
+// Many sequences at once (config-4 decode): each has its own K/V cache [n_kv][ctx][hd] per layer;
+// a step takes one token per sequence through the batched pass (the weights stream once for all
+// of them) with attention over each token's own cache. Whole and tensor-parallel models alike.
+extern "C" int kq_batch_caches(kq_model* m, int n_seq) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (n_seq < 1) return set_err(KQ_ERR_ARG, "n_seq must be positive");
+  if (m->n_seq) return m->n_seq == n_seq ? KQ_OK : set_err(KQ_ERR_ARG, "the batched-decode caches are already allocated");
+  const kq_config& c = m->c;
+  const size_t per = (size_t)n_seq * m->nkv_l * c.ctx * c.head_dim;
+  bool ok = true;
+  for (auto& w : m->L) {
+    w.bkc = dalloc<__half>(m, per, ok);
+    w.bvc = dalloc<__half>(m, per, ok);
+    if (!ok) break;
+  }
+  const int G = c.n_heads / c.n_kv_heads;
+  if (ok) {
+    m->bseq = dalloc<int>(m, MM_MAXM, ok);
+    m->bposv = dalloc<int>(m, MM_MAXM, ok);
+    m->dpart = dalloc<float>(m, (size_t)MM_MAXM * m->nkv_l * DA_MAX_SPLIT * G * (c.head_dim + 4), ok);
+  }
+  if (!ok) return set_err(KQ_ERR_MEMORY, "batched-decode caches");
+  m->n_seq = n_seq;
+  return KQ_OK;
+}
+
+// Prefill of sequence `seq`'s cache (chunks of up to MM_MAXM tokens, as kq_feed_batch).
+extern "C" int kq_batch_feed(kq_model* m, int seq, const int32_t* toks, int n, int pos) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (seq < 0 || seq >= m->n_seq) return set_err(KQ_ERR_ARG, "sequence out of range (kq_batch_caches first)");
+  if (!toks || n < 1 || pos < 0) return set_err(KQ_ERR_ARG, "bad token batch");
+  for (int i = 0; i < n; ++i)
+    if (toks[i] < 0 || toks[i] >= m->c.vocab) return set_err(KQ_ERR_ARG, "Invalid token");
+  if (pos + n > m->c.ctx) return set_err(KQ_ERR_OVERFLOW, "prompt runs past the context");
+  if (!batch_supported(m)) return set_err(KQ_ERR_ARG, "configuration not covered by the batched pass");
+  if ((rc = verify_buffers(m)) || (rc = batch_buffers(m))) return rc;
+  static const ChainMasks chain;
+  for (int c0 = 0; c0 < n; c0 += MM_MAXM)
+    if ((rc = verify_pass(m, toks + c0, 0, std::min(MM_MAXM, n - c0), pos + c0, chain.depth, chain.anc, false, seq)))
+      return rc;
+  CU(cudaStreamSynchronize(m->stream));
+  return check_dev_err(m);
+}
+
+template <int G>
+static cudaError_t launch_dattn_t(const DAttnParams& P, int M, int nkv, cudaStream_t s) {
+  cudaError_t e = launch_pdl(k_dattn<G>, dim3((unsigned)M, (unsigned)nkv, (unsigned)P.nsplit), dim3(DA_WARPS * 32), 0, s, P);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(k_dattn_merge<G>, dim3((unsigned)M, (unsigned)nkv), dim3(128), 0, s, P);
+}
+
+// One decode step for n sequences: token toks[i] at position pos[i] of sequence seqs[i] (distinct
+// sequences). Writes the greedy ids to out[i] and the K/V rows to the sequences' caches.
+extern "C" int kq_batch_step(kq_model* m, const int32_t* seqs, const int32_t* toks, const int32_t* pos, int n,
+                             int32_t* out) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (!seqs || !toks || !pos || !out || n < 1 || n > MM_MAXM) return set_err(KQ_ERR_ARG, "bad batched step arguments");
+  const kq_config& c = m->c;
+  int maxpos = 0;
+  for (int i = 0; i < n; ++i) {
+    if (seqs[i] < 0 || seqs[i] >= m->n_seq) return set_err(KQ_ERR_ARG, "sequence out of range (kq_batch_caches first)");
+    if (toks[i] < 0 || toks[i] >= c.vocab || pos[i] < 0) return set_err(KQ_ERR_ARG, "Invalid token or position");
+    if (pos[i] >= c.ctx) return set_err(KQ_ERR_OVERFLOW, "position past the context");
+    for (int j = 0; j < i; ++j)
+      if (seqs[j] == seqs[i]) return set_err(KQ_ERR_ARG, "one token per sequence in a batched step");
+    maxpos = std::max(maxpos, pos[i]);
+  }
+  if (!batch_supported(m)) return set_err(KQ_ERR_ARG, "configuration not covered by the batched pass");
+  if ((rc = verify_buffers(m)) || (rc = batch_buffers(m))) return rc;
+  cudaStream_t s = m->stream;
+  const int M = n;
+  CU(cudaMemcpyAsync(m->btok, toks, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->bslot, pos, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->brpos, pos, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->bseq, seqs, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  BatchParams B;
+  std::memset(&B, 0, sizeof(B));
+  B.M = M; B.slot = m->bslot; B.rpos = m->brpos; B.seq = m->bseq;
+  const int G = c.n_heads / c.n_kv_heads, QD = m->nh_l * c.head_dim;
+  DAttnParams D;
+  std::memset(&D, 0, sizeof(D));
+  D.q = m->bq; D.seq = m->bseq; D.pos = m->bslot; D.n_kv = m->nkv_l; D.ctx = c.ctx;
+  D.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
+  D.part = m->dpart; D.out_xp = m->bxa; D.Npad = (M + 15) & ~15;
+  // splits: about four CTAs per SM, at least 64 positions each
+  D.nsplit = std::max(1, std::min(DA_MAX_SPLIT, std::min((4 * m->nsm + M * m->nkv_l - 1) / (M * m->nkv_l), (maxpos + 64) / 64)));
+  for (int l = 0; l < c.n_layers; ++l) {
+    LayerW& w = m->L[l];
+    if ((rc = launch_bnorm(m, M, l == 0, w.attn_norm, l > 0))) return rc;
+    SegSpec qkv[3] = {{w.q, EPI_ROPE_Q, m->bq, nullptr}, {w.k, EPI_ROPE_K, nullptr, w.bkc}, {w.v, EPI_V, nullptr, w.bvc}};
+    if ((rc = launch_tmm(m, qkv, 3, m->bxd, nullptr, QD, B))) return rc;
+    D.kc = w.bkc;
+    D.vc = w.bvc;
+    cudaError_t e = G == 1 ? launch_dattn_t<1>(D, M, m->nkv_l, s) : G == 2 ? launch_dattn_t<2>(D, M, m->nkv_l, s)
+                  : G == 4 ? launch_dattn_t<4>(D, M, m->nkv_l, s) : launch_dattn_t<8>(D, M, m->nkv_l, s);
+    CU(e);
+    SegSpec so[1] = {{w.o, EPI_F32, m->by, nullptr}};
+    if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, c.dim, B))) return rc;
+    if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;
+    if ((rc = launch_bnorm(m, M, false, w.ffn_norm, true))) return rc;
+    SegSpec sg[1] = {{w.gu, EPI_SWIGLU, nullptr, nullptr}};
+    if ((rc = launch_tmm(m, sg, 1, m->bxd, m->bxf, 0, B))) return rc;
+    SegSpec sd[1] = {{w.down, EPI_F32, m->by, nullptr}};
+    if ((rc = launch_tmm(m, sd, 1, m->bxf, nullptr, c.dim, B))) return rc;
+    if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;
+  }
+  if ((rc = head_argmax(m, M, B, m->out_ids))) return rc;
+  CU(cudaMemcpyAsync(out, m->out_ids, M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  CU(cudaStreamSynchronize(s));
+  return check_dev_err(m);
 }
 
 extern "C" int kq_commit(kq_model* m, const int32_t* path, int k, int pos) {

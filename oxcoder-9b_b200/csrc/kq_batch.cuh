@@ -380,6 +380,122 @@ __global__ void __launch_bounds__(256) k_argmax_rows(const float* logits, int V,
   }
 }
 
+// ------------------------------------------------------------------------------ batched decode attention
+// One token per sequence, each over its own sequence's cache (batched decode of many sequences):
+// CTA = (token, KV head, split of positions [0, pos + 1)); 4 warps take positions in turn, a lane
+// owns 4 of the 128 dims, the G query heads' scores are warp sums (xor tree), online softmax per
+// warp, the warps' (m, l, o) combined in fixed order into the split's partial. fp32 throughout,
+// fp16 K/V as stored. k_dattn_merge merges the splits in order into the packed o-GEMM input.
+constexpr int DA_WARPS = 4;
+constexpr int DA_MAX_SPLIT = 64;
+struct DAttnParams {
+  const float* q;            // [M][NH_l * HD] rotated queries
+  const __half* kc;          // [nseq][n_kv][ctx][HD]
+  const __half* vc;
+  const int* seq;            // [M] sequence of each token
+  const int* pos;            // [M] its position (attends to [0, pos])
+  int n_kv, ctx, nsplit;
+  float scale;
+  float* part;               // [M][n_kv][nsplit][G][HD + 4] (o, m, l, pad)
+  __half* out_xp;            // packed o-GEMM input (merge)
+  int Npad;
+};
+template <int G>
+__global__ void __launch_bounds__(DA_WARPS * 32) k_dattn(const __grid_constant__ DAttnParams P) {
+  constexpr int HD = 128, PLD = HD + 4;
+  const int t = blockIdx.x, kv = blockIdx.y, sp = blockIdx.z, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float s_m[DA_WARPS][G], s_l[DA_WARPS][G];
+  __shared__ __align__(16) float s_o[DA_WARPS][G][HD];
+  pdl_wait();
+  pdl_trigger();
+  const int n = P.pos[t] + 1, per = (n + P.nsplit - 1) / P.nsplit;
+  const int p0 = min(n, sp * per), p1 = min(n, p0 + per);
+  const size_t cbase = ((size_t)P.seq[t] * P.n_kv + kv) * P.ctx * HD;
+  const __half* kb = P.kc + cbase;
+  const __half* vb = P.vc + cbase;
+  const int NHHD = P.n_kv * G * HD;
+  float q[G][4], o[G][4], m[G], l[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float4 qq = *reinterpret_cast<const float4*>(P.q + (size_t)t * NHHD + (size_t)(kv * G + g) * HD + 4 * lane);
+    q[g][0] = qq.x; q[g][1] = qq.y; q[g][2] = qq.z; q[g][3] = qq.w;
+    o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+  }
+  for (int p = p0 + warp; p < p1; p += DA_WARPS) {
+    const uint2 kr = __ldcs(reinterpret_cast<const uint2*>(kb + (size_t)p * HD) + lane);
+    const uint2 vr = __ldcs(reinterpret_cast<const uint2*>(vb + (size_t)p * HD) + lane);
+    const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kr.x));
+    const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&kr.y));
+    const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vr.x));
+    const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vr.y));
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float d = __fmul_rn(q[g][0], k01.x);
+      d = __fmaf_rn(q[g][1], k01.y, d);
+      d = __fmaf_rn(q[g][2], k23.x, d);
+      d = __fmaf_rn(q[g][3], k23.y, d);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, off));
+      const float sc = __fmul_rn(d, P.scale);
+      const float mn = fmaxf(m[g], sc);
+      const float f = expf(__fsub_rn(m[g], mn)), e = expf(__fsub_rn(sc, mn));
+      m[g] = mn;
+      l[g] = __fmaf_rn(l[g], f, e);
+      o[g][0] = __fmaf_rn(o[g][0], f, __fmul_rn(e, v01.x));
+      o[g][1] = __fmaf_rn(o[g][1], f, __fmul_rn(e, v01.y));
+      o[g][2] = __fmaf_rn(o[g][2], f, __fmul_rn(e, v23.x));
+      o[g][3] = __fmaf_rn(o[g][3], f, __fmul_rn(e, v23.y));
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (lane == 0) { s_m[warp][g] = m[g]; s_l[warp][g] = l[g]; }
+    *reinterpret_cast<float4*>(&s_o[warp][g][4 * lane]) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+  }
+  __syncthreads();
+  // the warps' partials combined in warp order: thread = (head g, 4 dims)
+  float* part = P.part + (((size_t)t * P.n_kv + kv) * P.nsplit + sp) * G * PLD;
+  for (int e = threadIdx.x; e < G * (HD / 4); e += DA_WARPS * 32) {
+    const int g = e / (HD / 4), d4 = e % (HD / 4);
+    float M = -INFINITY;
+    for (int w = 0; w < DA_WARPS; ++w) M = fmaxf(M, s_m[w][g]);
+    float L = 0.f, O0 = 0.f, O1 = 0.f, O2 = 0.f, O3 = 0.f;
+    for (int w = 0; w < DA_WARPS; ++w) {
+      const float wt = s_m[w][g] == -INFINITY ? 0.f : expf(__fsub_rn(s_m[w][g], M));
+      const float4 ow = *reinterpret_cast<const float4*>(&s_o[w][g][4 * d4]);
+      L = __fmaf_rn(wt, s_l[w][g], L);
+      O0 = __fmaf_rn(wt, ow.x, O0); O1 = __fmaf_rn(wt, ow.y, O1); O2 = __fmaf_rn(wt, ow.z, O2); O3 = __fmaf_rn(wt, ow.w, O3);
+    }
+    __stcg(reinterpret_cast<float4*>(part + (size_t)g * PLD) + d4, make_float4(O0, O1, O2, O3));
+    if (d4 == 0) { __stcg(part + (size_t)g * PLD + HD, M); __stcg(part + (size_t)g * PLD + HD + 1, L); }
+  }
+}
+// grid (token, KV head): the splits merged in order, the result packed for the o GEMM.
+template <int G>
+__global__ void __launch_bounds__(128) k_dattn_merge(const __grid_constant__ DAttnParams P) {
+  constexpr int HD = 128, PLD = HD + 4;
+  const int t = blockIdx.x, kv = blockIdx.y;
+  pdl_wait();
+  pdl_trigger();
+  const float* pb = P.part + ((size_t)t * P.n_kv + kv) * P.nsplit * G * PLD;
+  for (int e = threadIdx.x; e < G * HD; e += 128) {
+    const int g = e / HD, d = e % HD;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < P.nsplit; ++s2) M = fmaxf(M, __ldcg(pb + ((size_t)s2 * G + g) * PLD + HD));
+    float L = 0.f, O = 0.f;
+    for (int s2 = 0; s2 < P.nsplit; ++s2) {
+      const float* pr = pb + ((size_t)s2 * G + g) * PLD;
+      const float ms = __ldcg(pr + HD);
+      const float wt = ms == -INFINITY ? 0.f : expf(__fsub_rn(ms, M));
+      L = __fmaf_rn(wt, __ldcg(pr + HD + 1), L);
+      O = __fmaf_rn(wt, __ldcg(pr + d), O);
+    }
+    xp_store(P.out_xp, P.Npad, t, (kv * G + g) * HD + d, __fdiv_rn(O, L));
+  }
+}
+
 // Tensor-parallel head: per-token (best value, global id) of this rank's vocabulary slice, whose
 // first id is idx_off (lowest id on ties).
 __global__ void __launch_bounds__(256) k_argmax_rows_vi(const float* logits, int V, int idx_off, float* out_v, int* out_i) {

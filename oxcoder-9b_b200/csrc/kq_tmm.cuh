@@ -151,6 +151,7 @@ struct BatchParams {                   // per-token data of a pass
   const int* rpos;                     // [M] rotary position
   const unsigned long long* mask;      // [M][2] ancestor masks relative to tree_base
   int tree_base;
+  const int* seq;                      // [M] sequence of each token (batched decode), or null: 0
 };
 
 constexpr int TM_ROWS = 128;                       // weight rows per CTA (the MMA's M)
@@ -194,6 +195,7 @@ struct TmmParams {
   const float* cos_t;
   const float* sin_t;
   int hd, ctx;
+  int nkv;             // KV heads per sequence in the cache ([seq][nkv][ctx][hd]; one sequence: any)
   float* part;         // split-K partials [nsplit][Npad][ntiles * TM_ROWS]
   int* ticket;         // [ntiles], zero between launches
   int* err;
@@ -308,7 +310,8 @@ __device__ __forceinline__ void tm_epilogue(const TmmParams& P, const TmmSeg& S,
       break;
     case EPI_V: {
       const int kv = lrow / P.hd, d = lrow % P.hd;
-      S.out_h[((size_t)kv * P.ctx + P.B.slot[tk]) * P.hd + d] = __float2half_rn(v);
+      const int sq = P.B.seq ? P.B.seq[tk] : 0;
+      S.out_h[((size_t)(sq * P.nkv + kv) * P.ctx + P.B.slot[tk]) * P.hd + d] = __float2half_rn(v);
     } break;
     case EPI_SWIGLU:   // rows (2i, 2i + 1) = (gate i, up i)
       if ((lrow & 1) == 0) xp_store(P.xp_out, P.Npad, tk, lrow >> 1, __fmul_rn(silu_f(v), vo));
@@ -326,7 +329,8 @@ __device__ __forceinline__ void tm_epilogue(const TmmParams& P, const TmmSeg& S,
           q[i2] = o0;
           q[i2 + half] = o1;
         } else {
-          __half* dst = S.out_h + ((size_t)hh * P.ctx + P.B.slot[tk]) * P.hd;
+          const int sq = P.B.seq ? P.B.seq[tk] : 0;
+          __half* dst = S.out_h + ((size_t)(sq * P.nkv + hh) * P.ctx + P.B.slot[tk]) * P.hd;
           dst[i2] = __float2half_rn(o0);
           dst[i2 + half] = __float2half_rn(o1);
         }

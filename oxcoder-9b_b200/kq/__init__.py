@@ -59,6 +59,9 @@ SIGNATURES = {
     "kq_model_create": (C.c_void_p, [C.POINTER(Config), C.c_int]),
     "kq_model_free": (None, [C.c_void_p]),
     "kq_tp_unique_id": (C.c_int, [C.c_char_p]),
+    "kq_batch_caches": (C.c_int, [C.c_void_p, C.c_int]),
+    "kq_batch_feed": (C.c_int, [C.c_void_p, C.c_int, PI32, C.c_int, C.c_int]),
+    "kq_batch_step": (C.c_int, [C.c_void_p, PI32, PI32, PI32, C.c_int, PI32]),
     "kq_model_create_tp": (C.c_void_p, [C.POINTER(Config), C.c_int, C.c_int, C.c_int, C.c_char_p]),
     "kq_model_tp": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "kq_model_fill_synthetic": (C.c_int, [C.c_void_p, C.c_uint64]),
@@ -364,6 +367,26 @@ class Engine(object):
         p, ld = C.c_void_p(), C.c_int()
         check(lib().kq_draft_logits(self.h, C.byref(p), C.byref(ld)))
         return p.value, ld.value
+
+    # ---- batched decode of many sequences
+    def batch_caches(self, n_seq):
+        """Allocate (zeroed) K/V caches for n_seq sequences."""
+        check(lib().kq_batch_caches(self.h, int(n_seq)))
+
+    def batch_feed(self, seq, toks, pos):
+        """Prefill sequence `seq` with toks from position pos."""
+        t = np.ascontiguousarray(toks, np.int32)
+        check(lib().kq_batch_feed(self.h, int(seq), _ptr(t, PI32), len(t), int(pos)))
+
+    def batch_step(self, seqs, toks, pos):
+        """One token for each of the distinct sequences seqs (token toks[i] at position pos[i]):
+        their greedy ids."""
+        sq = np.ascontiguousarray(seqs, np.int32)
+        t = np.ascontiguousarray(toks, np.int32)
+        p = np.ascontiguousarray(pos, np.int32)
+        out = np.empty(len(t), np.int32)
+        check(lib().kq_batch_step(self.h, _ptr(sq, PI32), _ptr(t, PI32), _ptr(p, PI32), len(t), _ptr(out, PI32)))
+        return [int(v) for v in out]
 
     def commit(self, path, pos):
         """K/V compaction of an accepted path (path[0] = 0)."""
