@@ -241,6 +241,44 @@ def tp_prefill_bench(kq, dist, rank, world, local, peak_tflops):
                          "note": "algorithmic flops; the split-precision GEMM issues 2 MMAs per 16 columns"}}
 
 
+TP_DEC_SEQ, TP_DEC_CTX = 64, 32768
+
+
+def tp_decode_bench(kq, dist, rank, world, local, hbm_gbs, steps=5, warmup=2):
+    """Config-4 decode: 64 sequences at context 32 768, one token each per step, through the
+    tensor-parallel model (each rank: its KV heads of all 64 caches, 274.9 GB / world of K/V).
+    The caches are zero-filled (uniform attention; the bytes read are the same). Host-timed around
+    the synchronising kq_batch_step on every rank, max over ranks."""
+    import numpy as np
+    import torch
+    obj = [kq.tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    e = kq.Engine(kq.Config.default(ctx=TP_DEC_CTX), device=local, seed=0, tp=(rank, world, obj[0]))
+    e.batch_caches(TP_DEC_SEQ)
+    seqs = list(range(TP_DEC_SEQ))
+    pos0 = TP_DEC_CTX - (steps + warmup) - 1
+    cur = [int(v) for v in (np.arange(TP_DEC_SEQ) * 7919) % e.vocab]
+    for i in range(warmup):
+        cur = e.batch_step(seqs, cur, [pos0 + i] * TP_DEC_SEQ)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(steps):
+        cur = e.batch_step(seqs, cur, [pos0 + warmup + i] * TP_DEC_SEQ)
+    dt = time.perf_counter() - t0
+    t = torch.tensor([dt], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    e.close()
+    avg_ctx = pos0 + warmup + steps / 2.0 + 1
+    bytes_step = CFG2_WEIGHT_BYTES + TP_DEC_SEQ * KV_BYTES_PER_POS * avg_ctx   # all ranks together
+    achieved = bytes_step * steps / dt / 1e9
+    return {"world": world, "sequences": TP_DEC_SEQ, "ctx": TP_DEC_CTX, "steps": steps, "ms_per_step": 1e3 * dt / steps,
+            "tok_s": TP_DEC_SEQ * steps / dt,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs * world, "unit": "GB/s",
+                         "frac": achieved / (hbm_gbs * world), "bytes_per_step": bytes_step}}
+
+
 def run_profile_mode(args):
     """decode-only: fill the config-2 model (optionally fewer layers), W + K device-resident
     decode steps at ctx 4K. gemv-only: the config-0 Q4_K GEMV over 16 rotating copies."""
@@ -253,6 +291,25 @@ def run_profile_mode(args):
         e = kq.Engine(kq.Config.default(ctx=CTX, n_layers=args.layers), seed=0)
         print(json.dumps({"mode": "prefill", "p512": prefill_bench(e, e.vocab, 512, args.steps),
                           "p2048": prefill_bench(e, e.vocab, 2048, 1)}))
+        return 0
+    if args.mode == "batch-decode":
+        # batched decode on one GPU: 64 sequences at context 8192 (69 GB of K/V), zero caches
+        import numpy as np
+        ctx, nseq = 8192, 64
+        e = kq.Engine(kq.Config.default(ctx=ctx), seed=0)
+        e.batch_caches(nseq)
+        seqs = list(range(nseq))
+        cur = [int(v) for v in (np.arange(nseq) * 7919) % e.vocab]
+        pos0 = ctx - (args.steps + args.warmup) - 1
+        for i in range(args.warmup):
+            cur = e.batch_step(seqs, cur, [pos0 + i] * nseq)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            cur = e.batch_step(seqs, cur, [pos0 + args.warmup + i] * nseq)
+        dt = time.perf_counter() - t0
+        kv = nseq * KV_BYTES_PER_POS * (pos0 + args.warmup + args.steps / 2.0)
+        print(json.dumps({"mode": "batch-decode", "sequences": nseq, "ctx": ctx, "ms_per_step": 1e3 * dt / args.steps,
+                          "tok_s": nseq * args.steps / dt, "gbs": (CFG2_WEIGHT_BYTES + kv) * args.steps / dt / 1e9}))
         return 0
     if args.mode == "gemm":
         # the batched-pass GEMM alone: gate/up shape (Q4_K 24576 x 4096), 45 tokens, through kq_qmat_matmul
@@ -286,7 +343,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=32, help="decode-only: layers of the model (small ncu captures)")
-    ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only", "spec", "prefill", "gemm"],
+    ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only", "spec", "prefill", "gemm", "batch-decode"],
                     help="decode-only / gemv-only: the small commands the ncu captures in profiles/ run")
     args = ap.parse_args()
     if args.mode != "full":
@@ -351,10 +408,11 @@ def main():
     spec = spec_bench(e, e.vocab, 8, 3)
     prefill = prefill_bench(e, e.vocab, 512)
     e.close()
-    tp = None
+    tp = tpd = None
     if dist is not None:
         pk0 = peaks()
         tp = tp_prefill_bench(kq, dist, rank, world, local, pk0["bf16_tflops"] if pk0 else 1590.0)
+        tpd = tp_decode_bench(kq, dist, rank, world, local, pk0["hbm_gbs"] if pk0 else 6650.0)
 
     # ---- the dominant kernel: config-0 Q4_K GEMV over 16 rotating weight copies (453 MB > L2)
     mats = [kq.QMat(12, 12288, 4096, device=local).fill_synthetic(0, 1000 + i) for i in range(16)]
@@ -399,6 +457,7 @@ def main():
             "prefill_tok_s": prefill["tok_s"] * world,
             "prefill": prefill,
             "tp_prefill": tp,
+            "tp_decode": tpd,
             "cpu_baseline": cb,
         }
         print(json.dumps(line), flush=True)

@@ -3,7 +3,8 @@
 Each rank is a process on its own GPU holding its shard (KV heads, FFN slice, vocabulary slice)
 joined by NCCL; the batched pass all-reduces the o and down partials and all-gathers the head's
 argmax. Bars: every rank's K/V cache heads after a prefill within 1e-3 rel-L2 of the same heads
-of the whole model on one GPU, and the greedy steps that follow identical. Skips with fewer
+of the whole model on one GPU, the greedy steps that follow identical, and batched decode of three
+sequences (kq_batch_*) giving the whole model's ids. Skips with fewer
 than two GPUs (the round-end suite runs on one); run under `gpurun --gpus 2`."""
 import multiprocessing as mp
 import os
@@ -35,7 +36,17 @@ def _run(kq, e, prompt, npos, nsteps):
         t = e.step(t, end + i)
         toks.append(t)
     kv = [[e.get_kv(l, w, end) for w in (0, 1)] for l in range(CFG["NL"])]
-    return toks, kv
+    # batched decode of three sequences (prompt prefixes of different lengths)
+    e.batch_caches(3)
+    lens = [len(prompt), 41, 17]
+    for sq, n in enumerate(lens):
+        e.batch_feed(sq, prompt[:n - 1], 0)
+    cur, pos, bt = [prompt[n - 1] for n in lens], [n - 1 for n in lens], []
+    for i in range(4):
+        cur = e.batch_step([0, 1, 2], cur, pos)
+        bt.append(list(cur))
+        pos = [p + 1 for p in pos]
+    return toks, kv, bt
 
 
 def _rank_main(rank, world, uid, prompt, npos, nsteps, q):
@@ -74,10 +85,11 @@ def test_tp_prefill_and_steps_match_whole_model(kq, world):
     for r in range(world):
         assert not isinstance(res[r], str), res[r]
     whole = kq.Engine(_cfg(kq, CFG), device=0, seed=0)
-    toks, kv = _run(kq, whole, prompt, npos, nsteps)
+    toks, kv, bt = _run(kq, whole, prompt, npos, nsteps)
     nkv_l, hd, end = CFG["NKV"] // world, CFG["HD"], npos + len(prompt)
     for r in range(world):
         assert res[r][0] == toks, (r, res[r][0], toks)
+        assert res[r][2] == bt, (r, res[r][2], bt)
         for l in range(CFG["NL"]):
             for w in (0, 1):
                 got = res[r][1][l][w].view(np.float16).astype(np.float32).reshape(end, nkv_l, hd)
