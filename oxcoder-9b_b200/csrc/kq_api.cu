@@ -451,7 +451,8 @@ struct kq_model {
   int out_cap = 0;
   int* err = nullptr;
   int attn_cl = 16;                  // CTAs per kv head in the cluster attention
-  int attn_mode = 0;                 // 0: split form, 1: cluster form
+  int attn_mode = 0;                 // 0: split form, 1: cluster form, 2: tensor-core split form
+  float* dpart1 = nullptr;          // decode-step partials of the tensor-core split form
   int attn_nsplit = 1;
   float *apart = nullptr, *apart_ml = nullptr;
   int* aticket = nullptr;
@@ -624,7 +625,9 @@ static kq_model* model_create(const kq_config* cfg, int device, int rank, int wo
     m->mbuf = dalloc<float>(m, c.ffn, ok);
     m->logits = dalloc<float>(m, c.vocab, ok);
     m->attn_cl = attn_cluster_size(c.n_heads / c.n_kv_heads, c.n_kv_heads);
-    m->attn_mode = std::getenv("KQ_ATTN") && std::atoi(std::getenv("KQ_ATTN")) == 1 ? 1 : 0;
+    m->attn_mode = std::getenv("KQ_ATTN") ? std::atoi(std::getenv("KQ_ATTN")) : 2;   // tuning override
+    if (m->attn_mode < 0 || m->attn_mode > 2) m->attn_mode = 2;
+    m->dpart1 = dalloc<float>(m, (size_t)c.n_kv_heads * DA_MAX_SPLIT * (c.n_heads / c.n_kv_heads) * (c.head_dim + 4), ok);
     m->persist = std::getenv("KQ_PERSIST") && std::atoi(std::getenv("KQ_PERSIST")) == 1;   // opt-in for now
     m->verify_seq = std::getenv("KQ_VERIFY_SEQ") && std::atoi(std::getenv("KQ_VERIFY_SEQ")) == 1;
     m->attn_nsplit = std::min(ATT_SPLITS_MAX, std::max(1, m->nsm / c.n_kv_heads));
@@ -955,6 +958,29 @@ static int build_step(kq_model* m, bool head, bool persist, std::vector<StepOp>&
   return KQ_OK;
 }
 
+// A launch that may start while the previous kernel on the stream finishes (it waits in-kernel).
+template <class K, class PT>
+static cudaError_t launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const PT& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+// Decode attention on the tensor cores: grid (token, KV head, split), merge per (token, KV head).
+template <int G>
+static cudaError_t launch_dattn_t(const DAttnParams& P, int M, int nkv, cudaStream_t s) {
+  cudaError_t e = launch_pdl(k_dattn_mma<G>, dim3((unsigned)M, (unsigned)nkv, (unsigned)P.nsplit), dim3(32), DM_SMEM, s, P);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(k_dattn_merge<G>, dim3((unsigned)M, (unsigned)nkv, (unsigned)G), dim3(DM_MERGE_THREADS), 0, s, P);
+}
+
 static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
   std::vector<StepOp> ops;
   int rc = build_step(m, head, false, ops);
@@ -966,6 +992,14 @@ static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
       CU(launch_gemv(op.g, op.pl, s, !first));
     } else if (m->attn_mode == 1) {
       CU(attn_cl_fn(G, m->attn_cl)(op.a.a, s, true));
+    } else if (m->attn_mode == 2) {
+      DAttnParams D;
+      std::memset(&D, 0, sizeof(D));
+      D.q = op.a.a.q; D.kc = op.a.a.kc; D.vc = op.a.a.vc; D.st = op.a.a.st; D.err = op.a.a.err;
+      D.n_kv = op.a.a.n_kv; D.ctx = op.a.a.ctx; D.scale = op.a.a.scale;
+      D.nsplit = DA_MAX_SPLIT; D.part = m->dpart1; D.out_f = op.a.a.out;
+      CU(G == 1 ? launch_dattn_t<1>(D, 1, D.n_kv, s) : G == 2 ? launch_dattn_t<2>(D, 1, D.n_kv, s)
+         : G == 4 ? launch_dattn_t<4>(D, 1, D.n_kv, s) : launch_dattn_t<8>(D, 1, D.n_kv, s));
     } else {
       CU(launch_attn_split(op.a, G, s, true));
     }
@@ -1390,20 +1424,6 @@ static cudaError_t tmm_launch(const TmmParams& P, cudaStream_t s, bool pdl) {
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k_tmm, P);
 }
-template <class K, class PT>
-static cudaError_t launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const PT& p) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, p);
-}
 
 // Sum of the row-split GEMM partials over the tensor-parallel ranks (fp32, in place, on the
 // model's stream). World 1: nothing.
@@ -1756,13 +1776,6 @@ extern "C" int kq_batch_feed(kq_model* m, int seq, const int32_t* toks, int n, i
   return check_dev_err(m);
 }
 
-template <int G>
-static cudaError_t launch_dattn_t(const DAttnParams& P, int M, int nkv, cudaStream_t s) {
-  cudaError_t e = launch_pdl(k_dattn<G>, dim3((unsigned)M, (unsigned)nkv, (unsigned)P.nsplit), dim3(DA_WARPS * 32), 0, s, P);
-  if (e != cudaSuccess) return e;
-  return launch_pdl(k_dattn_merge<G>, dim3((unsigned)M, (unsigned)nkv), dim3(128), 0, s, P);
-}
-
 // One decode step for n sequences: token toks[i] at position pos[i] of sequence seqs[i] (distinct
 // sequences). Writes the greedy ids to out[i] and the K/V rows to the sequences' caches.
 extern "C" int kq_batch_step(kq_model* m, const int32_t* seqs, const int32_t* toks, const int32_t* pos, int n,
@@ -1797,8 +1810,8 @@ extern "C" int kq_batch_step(kq_model* m, const int32_t* seqs, const int32_t* to
   D.q = m->bq; D.seq = m->bseq; D.pos = m->bslot; D.n_kv = m->nkv_l; D.ctx = c.ctx;
   D.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
   D.part = m->dpart; D.out_xp = m->bxa; D.Npad = (M + 15) & ~15;
-  // splits: about four CTAs per SM, at least 64 positions each
-  D.nsplit = std::max(1, std::min(DA_MAX_SPLIT, std::min((4 * m->nsm + M * m->nkv_l - 1) / (M * m->nkv_l), (maxpos + 64) / 64)));
+  // splits: about six one-warp CTAs per SM, at least two 32-key blocks each
+  D.nsplit = std::max(1, std::min(DA_MAX_SPLIT, std::min((6 * m->nsm + M * m->nkv_l - 1) / (M * m->nkv_l), (maxpos + 64) / 64)));
   for (int l = 0; l < c.n_layers; ++l) {
     LayerW& w = m->L[l];
     if ((rc = launch_bnorm(m, M, l == 0, w.attn_norm, l > 0))) return rc;

@@ -397,8 +397,12 @@ struct DAttnParams {
   int n_kv, ctx, nsplit;
   float scale;
   float* part;               // [M][n_kv][nsplit][G][HD + 4] (o, m, l, pad)
-  __half* out_xp;            // packed o-GEMM input (merge)
+  __half* out_xp;            // packed o-GEMM input (merge), or
+  float* out_f;              // fp32 [M][n_kv * G * HD] (the decode step's GEMV input)
   int Npad;
+  const DecodeState* st;     // decode step (M = 1): position, tree base and ancestor mask from the
+                             // device-resident step state instead of pos / seq
+  int* err;
 };
 template <int G>
 __global__ void __launch_bounds__(DA_WARPS * 32) k_dattn(const __grid_constant__ DAttnParams P) {
@@ -472,27 +476,219 @@ __global__ void __launch_bounds__(DA_WARPS * 32) k_dattn(const __grid_constant__
     if (d4 == 0) { __stcg(part + (size_t)g * PLD + HD, M); __stcg(part + (size_t)g * PLD + HD + 1, L); }
   }
 }
-// grid (token, KV head): the splits merged in order, the result packed for the o GEMM.
+// Tensor-core form: one warp per (token, KV head, split); 32-key blocks of K/V through shared
+// memory (cp.async, two stages, padded rows); the G query heads are rows 0..G-1 of an m16 tile
+// (Q as hi + lo fp16), S = Q K^T and O += P V on mma.sync with fp32 accumulation and the online
+// softmax in registers, as the tree attention. Same partial layout as k_dattn (k_dattn_merge).
+constexpr int DM_KB = 32;                                            // keys per block
+constexpr size_t DM_SMEM = (size_t)2 * 2 * DM_KB * BA_LD * 2;          // K and V, two stages
 template <int G>
-__global__ void __launch_bounds__(128) k_dattn_merge(const __grid_constant__ DAttnParams P) {
+__global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnParams P) {
   constexpr int HD = 128, PLD = HD + 4;
-  const int t = blockIdx.x, kv = blockIdx.y;
+  extern __shared__ __align__(16) uint8_t dm_sm[];
+  __half* ksm = reinterpret_cast<__half*>(dm_sm);   // [2][DM_KB][BA_LD]
+  __half* vsm = ksm + 2 * DM_KB * BA_LD;
+  const int t = blockIdx.x, kv = blockIdx.y, sp = blockIdx.z, lane = threadIdx.x, grp = lane >> 2, t4 = lane & 3;
   pdl_wait();
   pdl_trigger();
-  const float* pb = P.part + ((size_t)t * P.n_kv + kv) * P.nsplit * G * PLD;
-  for (int e = threadIdx.x; e < G * HD; e += 128) {
-    const int g = e / HD, d = e % HD;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < P.nsplit; ++s2) M = fmaxf(M, __ldcg(pb + ((size_t)s2 * G + g) * PLD + HD));
-    float L = 0.f, O = 0.f;
-    for (int s2 = 0; s2 < P.nsplit; ++s2) {
-      const float* pr = pb + ((size_t)s2 * G + g) * PLD;
-      const float ms = __ldcg(pr + HD);
-      const float wt = ms == -INFINITY ? 0.f : expf(__fsub_rn(ms, M));
-      L = __fmaf_rn(wt, __ldcg(pr + HD + 1), L);
-      O = __fmaf_rn(wt, __ldcg(pr + d), O);
+  int n = (P.st ? P.st->pos : P.pos[t]) + 1;
+  if (n > P.ctx || n < 1) {
+    if (lane == 0 && sp == 0 && kv == 0 && P.err) atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
+    n = n < 1 ? 1 : P.ctx;
+  }
+  const int tbase = P.st ? P.st->tree_base : n;
+  const unsigned long long tm0 = P.st ? P.st->mask[0] : 0ull, tm1 = P.st ? P.st->mask[1] : 0ull;
+  const int per = (n + P.nsplit - 1) / P.nsplit;
+  const int p0 = min(n, sp * per), p1 = min(n, p0 + per);
+  const size_t cbase = ((size_t)(P.seq ? P.seq[t] : 0) * P.n_kv + kv) * P.ctx * HD;
+  const __half* kg = P.kc + cbase;
+  const __half* vg = P.vc + cbase;
+  auto load_block = [&](int b0, int stage) {
+    __half* kd = ksm + stage * DM_KB * BA_LD;
+    __half* vd = vsm + stage * DM_KB * BA_LD;
+#pragma unroll 4
+    for (int i = lane; i < DM_KB * 16; i += 32) {   // 16 chunks of 16 B per key row
+      const int r = i >> 4, c = i & 15, tk = b0 + r;
+      const bool ok = tk < p1;
+      const size_t off = (size_t)(ok ? tk : p0) * HD + c * 8;
+      cp_async16_plain(kd + r * BA_LD + c * 8, kg + off, ok ? 16u : 0u);
+      cp_async16_plain(vd + r * BA_LD + c * 8, vg + off, ok ? 16u : 0u);
     }
-    xp_store(P.out_xp, P.Npad, t, (kv * G + g) * HD + d, __fdiv_rn(O, L));
+  };
+  if (p0 < p1) load_block(p0, 0);
+  cp_async_commit();
+  // Q fragments: rows grp (a0, a2) and grp + 8 (a1, a3); rows >= G are zero
+  const int NHHD = P.n_kv * G * HD;
+  const bool va = grp < G, vb = grp + 8 < G;
+  const float* qa = P.q + (size_t)t * NHHD + (size_t)(kv * G + (va ? grp : 0)) * HD;
+  const float* qb = P.q + (size_t)t * NHHD + (size_t)(kv * G + (vb ? grp + 8 : 0)) * HD;
+  uint32_t qh[8][4], ql[8][4];
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const int d = 16 * ks + 2 * t4;
+    const float2 z = make_float2(0.f, 0.f);
+    const float2 x0 = va ? *reinterpret_cast<const float2*>(qa + d) : z;
+    const float2 x1 = vb ? *reinterpret_cast<const float2*>(qb + d) : z;
+    const float2 x2 = va ? *reinterpret_cast<const float2*>(qa + d + 8) : z;
+    const float2 x3 = vb ? *reinterpret_cast<const float2*>(qb + d + 8) : z;
+    tm_split(x0.x, x0.y, qh[ks][0], ql[ks][0]);
+    tm_split(x1.x, x1.y, qh[ks][1], ql[ks][1]);
+    tm_split(x2.x, x2.y, qh[ks][2], ql[ks][2]);
+    tm_split(x3.x, x3.y, qh[ks][3], ql[ks][3]);
+  }
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+  const int mi = lane >> 3;
+  int st = 0;
+  for (int b0 = p0; b0 < p1; b0 += DM_KB, st ^= 1) {
+    if (b0 + DM_KB < p1) load_block(b0 + DM_KB, st ^ 1);
+    cp_async_commit();
+    cp_async_wait1();
+    __syncwarp();
+    const __half* kd = ksm + st * DM_KB * BA_LD;
+    const __half* vd = vsm + st * DM_KB * BA_LD;
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(kd + (16 * np + ((mi >> 1) << 3) + (lane & 7)) * BA_LD + 16 * ks + ((mi & 1) << 3), r0, r1, r2, r3);
+        mma16816(s[2 * np], ql[ks], r0, r1);
+        mma16816(s[2 * np], qh[ks], r0, r1);
+        mma16816(s[2 * np + 1], ql[ks], r2, r3);
+        mma16816(s[2 * np + 1], qh[ks], r2, r3);
+      }
+    }
+    float bmA = -INFINITY, bmB = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tk = b0 + 8 * i + 2 * t4 + (e & 1);
+        const float a = tk < p1 && slot_attended(tk, tbase, tm0, tm1) ? __fmul_rn(s[i][e], P.scale) : -INFINITY;
+        s[i][e] = a;
+        if (e < 2) bmA = fmaxf(bmA, a); else bmB = fmaxf(bmB, a);
+      }
+    }
+    bmA = fmaxf(bmA, __shfl_xor_sync(0xffffffffu, bmA, 1));
+    bmA = fmaxf(bmA, __shfl_xor_sync(0xffffffffu, bmA, 2));
+    bmB = fmaxf(bmB, __shfl_xor_sync(0xffffffffu, bmB, 1));
+    bmB = fmaxf(bmB, __shfl_xor_sync(0xffffffffu, bmB, 2));
+    const float nmA = fmaxf(mA, bmA), nmB = fmaxf(mB, bmB);
+    const float uA = nmA == -INFINITY ? 0.f : nmA, uB = nmB == -INFINITY ? 0.f : nmB;
+    const float fA = expf(__fsub_rn(mA, uA)), fB = expf(__fsub_rn(mB, uB));
+    mA = nmA;
+    mB = nmB;
+    float sA = 0.f, sB = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float pe = expf(__fsub_rn(s[i][e], e < 2 ? uA : uB));
+        s[i][e] = pe;
+        if (e < 2) sA = __fadd_rn(sA, pe); else sB = __fadd_rn(sB, pe);
+      }
+    }
+    sA = __fadd_rn(sA, __shfl_xor_sync(0xffffffffu, sA, 1));
+    sA = __fadd_rn(sA, __shfl_xor_sync(0xffffffffu, sA, 2));
+    sB = __fadd_rn(sB, __shfl_xor_sync(0xffffffffu, sB, 1));
+    sB = __fadd_rn(sB, __shfl_xor_sync(0xffffffffu, sB, 2));
+    lA = fmaf(lA, fA, sA);
+    lB = fmaf(lB, fB, sB);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) { o[i][0] *= fA; o[i][1] *= fA; o[i][2] *= fB; o[i][3] *= fB; }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint32_t ah[4], al[4];
+      tm_split(s[2 * j][0], s[2 * j][1], ah[0], al[0]);
+      tm_split(s[2 * j][2], s[2 * j][3], ah[1], al[1]);
+      tm_split(s[2 * j + 1][0], s[2 * j + 1][1], ah[2], al[2]);
+      tm_split(s[2 * j + 1][2], s[2 * j + 1][3], ah[3], al[3]);
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_t(vd + (16 * j + ((mi & 1) << 3) + (lane & 7)) * BA_LD + 16 * dp + ((mi >> 1) << 3), r0, r1, r2, r3);
+        mma16816(o[2 * dp], al, r0, r1);
+        mma16816(o[2 * dp], ah, r0, r1);
+        mma16816(o[2 * dp + 1], al, r2, r3);
+        mma16816(o[2 * dp + 1], ah, r2, r3);
+      }
+    }
+    __syncwarp();   // the stage is refilled by the next iteration's prefetch
+  }
+  // partial of rows 0..G-1 (row grp in elements 0-1, row grp + 8 in elements 2-3)
+  float* part = P.part + (((size_t)t * P.n_kv + kv) * P.nsplit + sp) * G * PLD;
+  if (va) {
+    float* pr = part + (size_t)grp * PLD;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) __stcg(reinterpret_cast<float2*>(pr + 8 * i + 2 * t4), make_float2(o[i][0], o[i][1]));
+    if (t4 == 0) { __stcg(pr + HD, mA); __stcg(pr + HD + 1, lA); }
+  }
+  if (vb) {
+    float* pr = part + (size_t)(grp + 8) * PLD;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) __stcg(reinterpret_cast<float2*>(pr + 8 * i + 2 * t4), make_float2(o[i][2], o[i][3]));
+    if (t4 == 0) { __stcg(pr + HD, mB); __stcg(pr + HD + 1, lB); }
+  }
+}
+
+// grid (token, KV head, query head), DM_MERGE_THREADS threads: the split weights exp(m_s - M) and
+// the denominator once per block in shared memory, then four groups of 128 threads (one per
+// output column) each sum a quarter of the splits' rows and the groups' sums are added in group
+// order. The result goes to the packed o-GEMM input or, for the decode step, to fp32.
+constexpr int DM_MERGE_THREADS = 512;
+static_assert(DA_MAX_SPLIT <= 64, "the merge weighs at most two splits per lane");
+template <int G>
+__global__ void __launch_bounds__(DM_MERGE_THREADS) k_dattn_merge(const __grid_constant__ DAttnParams P) {
+  constexpr int HD = 128, PLD = HD + 4, NQ = DM_MERGE_THREADS / HD;
+  __shared__ float s_w[DA_MAX_SPLIT];
+  __shared__ float s_o[NQ][HD];
+  __shared__ float s_L;
+  const int t = blockIdx.x, kv = blockIdx.y, g = blockIdx.z, tid = threadIdx.x, lane = tid & 31;
+  pdl_wait();
+  pdl_trigger();
+  const int ns = P.nsplit;
+  const float* pb = P.part + ((size_t)t * P.n_kv + kv) * ns * G * PLD + (size_t)g * PLD;
+  if (tid < 32) {
+    const float m0 = lane < ns ? __ldcg(pb + (size_t)lane * G * PLD + HD) : -INFINITY;
+    const float m1 = lane + 32 < ns ? __ldcg(pb + (size_t)(lane + 32) * G * PLD + HD) : -INFINITY;
+    float M = fmaxf(m0, m1);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float w0 = m0 == -INFINITY ? 0.f : expf(__fsub_rn(m0, M));
+    const float w1 = m1 == -INFINITY ? 0.f : expf(__fsub_rn(m1, M));
+    float L = 0.f;
+    if (w0 != 0.f) L = __fmul_rn(w0, __ldcg(pb + (size_t)lane * G * PLD + HD + 1));
+    if (w1 != 0.f) L = __fmaf_rn(w1, __ldcg(pb + (size_t)(lane + 32) * G * PLD + HD + 1), L);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L = __fadd_rn(L, __shfl_xor_sync(0xffffffffu, L, off));
+    if (lane < ns) s_w[lane] = w0;
+    if (lane + 32 < ns) s_w[lane + 32] = w1;
+    if (lane == 0) s_L = L;
+  }
+  __syncthreads();
+  const int q = tid / HD, d = tid % HD, per = (ns + NQ - 1) / NQ, s0 = q * per, s1 = min(ns, s0 + per);
+  float O = 0.f;
+#pragma unroll 8
+  for (int s2 = s0; s2 < s1; ++s2) {
+    const float wt = s_w[s2];
+    if (wt != 0.f) O = __fmaf_rn(wt, __ldcg(pb + (size_t)s2 * G * PLD + d), O);
+  }
+  s_o[q][d] = O;
+  __syncthreads();
+  if (q == 0) {
+    float v = s_o[0][d];
+#pragma unroll
+    for (int k = 1; k < NQ; ++k) v = __fadd_rn(v, s_o[k][d]);
+    v = __fdiv_rn(v, s_L);
+    const int col = (kv * G + g) * HD + d;
+    if (P.out_f) P.out_f[(size_t)t * P.n_kv * G * HD + col] = v;
+    else xp_store(P.out_xp, P.Npad, t, col, v);
   }
 }
 
