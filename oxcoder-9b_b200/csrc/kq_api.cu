@@ -13,6 +13,7 @@
 #include "kq_decode.cuh"
 #include "kq_accept.cuh"
 #include "kq_batch.cuh"
+#include "kq_tmv.cuh"
 #include "kq_nccl.h"
 
 #include <cuda_runtime.h>
@@ -62,6 +63,7 @@ struct DevCtx {
   int* err = nullptr;       // device error word for matrix-hook calls
   size_t smem_optin = 0;
   size_t tmm_budget = 0;    // dynamic shared memory of the tensor-core GEMM
+  size_t tmv_smem = 0;      // dynamic shared memory available to k_tmv (0: the tensor-core GEMV is off)
 };
 static DevCtx g_dev[16];
 static std::mutex g_dev_mu;
@@ -96,6 +98,14 @@ static int dev_init(int device) {
   CU(cudaFuncSetAttribute(k_battn<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BA_SMEM));
   CU(cudaFuncSetAttribute(k_battn<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BA_SMEM));
   CU(cudaFuncSetAttribute(k_battn<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BA_SMEM));
+  {
+    cudaFuncAttributes fa;
+    CU(cudaFuncGetAttributes(&fa, k_tmv));
+    const size_t budget = (size_t)optin - fa.sharedSizeBytes;
+    CU(cudaFuncSetAttribute(k_tmv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)budget));
+    const char* ev = std::getenv("KQ_TMV");   // opt-in while it is validated: 1 = the tensor-core GEMV
+    d.tmv_smem = (ev && std::atoi(ev) == 1) ? budget : 0;
+  }
   CU(cudaMalloc(&d.err, sizeof(int)));
   CU(cudaMemset(d.err, 0, sizeof(int)));
   d.init = true;
@@ -107,6 +117,8 @@ struct kq_qmat {
   int device = 0, type = 0, R = 0, C = 0, G = 0;
   uint8_t* buf = nullptr;   // R/8 tiles (kq layout)
   size_t bytes = 0;
+  float* tv_part = nullptr; // split-K scratch of the tensor-core GEMV (matvec calls), lazily
+  int* tv_ticket = nullptr;
   QView view() const {
     QView v;
     v.base = buf; v.type = type; v.R = R; v.C = C; v.G = G;
@@ -453,6 +465,8 @@ struct kq_model {
   int attn_cl = 16;                  // CTAs per kv head in the cluster attention
   int attn_mode = 0;                 // 0: split form, 1: cluster form, 2: tensor-core split form
   float* dpart1 = nullptr;          // decode-step partials of the tensor-core split form
+  float* tv_part = nullptr;         // split-K scratch of the tensor-core GEMV (decode graph)
+  int* tv_ticket = nullptr;
   int attn_nsplit = 1;
   float *apart = nullptr, *apart_ml = nullptr;
   int* aticket = nullptr;
@@ -634,6 +648,8 @@ static kq_model* model_create(const kq_config* cfg, int device, int rank, int wo
     m->apart = dalloc<float>(m, (size_t)c.n_kv_heads * m->attn_nsplit * (c.n_heads / c.n_kv_heads) * c.head_dim, ok);
     m->apart_ml = dalloc<float>(m, (size_t)c.n_kv_heads * m->attn_nsplit * (c.n_heads / c.n_kv_heads) * 2, ok);
     m->aticket = dalloc<int>(m, c.n_kv_heads, ok);
+    m->tv_part = dalloc<float>(m, (size_t)m->nsm * 2 * TV_ROWS, ok);
+    m->tv_ticket = dalloc<int>(m, (size_t)TV_MAX_TILES, ok);
     if (attn_split_setup() != KQ_OK) ok = false;
     m->hpart_val = dalloc<float>(m, 1024, ok);
     m->hpart_idx = dalloc<int>(m, 1024, ok);
@@ -848,7 +864,59 @@ struct StepOp {
   GemvPlan pl;           // per-kernel launches only
   int stage_bytes;       // persistent kernel only
   AttnSplitParams a;
+  bool tmv;              // per-kernel launches: this GEMV runs as k_tmv (t, tgrid)
+  TmvParams t;
+  dim3 tgrid;
 };
+
+// The tensor-core GEMV form of a decode GEMV: the same segments, activation source and
+// epilogues; one CTA per SM over the (128-row tile, super-block) units. `part` holds nsm * 2 * 128
+// floats and `ticket` TV_MAX_TILES ints (zero). False when the launch is not covered (embedding
+// prologue, argmax epilogue, more than TV_MAX_G super-blocks per row, shared memory) or the
+// tensor-core GEMV is off: k_gemv runs it.
+static bool tmv_plan(const GemvParams& g, int nsm, size_t smem_max, float* part, int* ticket, TmvParams& T, dim3& grid) {
+  if (smem_max == 0 || g.nseg < 1 || g.nseg > TV_MAX_SEG || g.G > TV_MAX_G) return false;
+  if (g.xmode != XS_PLAIN && g.xmode != XS_NORM) return false;
+  std::memset(&T, 0, sizeof(T));
+  int ntiles = 0;
+  for (int i = 0; i < g.nseg; ++i) {
+    const Seg& sg = g.seg[i];
+    if (sg.epi == EPI_ARGMAX || sg.w.G != g.G) return false;
+    T.seg[i].w = sg.w;
+    T.seg[i].tile0 = ntiles;
+    T.seg[i].epi = sg.epi;
+    T.seg[i].out_f = sg.out_f;
+    T.seg[i].out_h = sg.out_h;
+    ntiles += (sg.w.R + TV_ROWS - 1) / TV_ROWS;
+    if (sg.w.type == Q4K) T.has_q4 = 1;
+    else T.has_q6 = 1;
+  }
+  if (ntiles > TV_MAX_TILES) return false;
+  const size_t smem = tv_smem(g.G, T.has_q4 != 0, T.has_q6 != 0).total;
+  if (smem > smem_max) return false;
+  T.nseg = g.nseg;
+  T.ntiles = ntiles;
+  T.G = g.G;
+  T.smem = (int)smem;
+  T.xmode = g.xmode;
+  T.x = g.x;
+  T.h_in = g.h_in;
+  T.y_add = g.y_add;
+  T.gamma = g.gamma;
+  T.h_out = g.h_out;
+  T.eps = g.eps;
+  T.st = g.st;
+  T.cos_t = g.cos_t;
+  T.sin_t = g.sin_t;
+  T.hd = g.hd;
+  T.ctx = g.ctx;
+  T.part = part;
+  T.ticket = ticket;
+  T.err = g.err;
+  const long long U = (long long)ntiles * g.G;
+  grid = dim3((unsigned)std::min<long long>(nsm, U));
+  return true;
+}
 
 static int build_step(kq_model* m, bool head, bool persist, std::vector<StepOp>& ops) {
   const kq_config& c = m->c;
@@ -857,6 +925,7 @@ static int build_step(kq_model* m, bool head, bool persist, std::vector<StepOp>&
   int cur = 0;
   auto gemv = [&](const SegSpec* ss, int nseg, bool pairs, StepOp& op) -> int {
     op.kind = PH_GEMV;
+    op.tmv = false;
     op.stage_bytes = 0;
     int rc = persist ? fill_gemv_dec(ss, nseg, op.g, op.stage_bytes) : fill_gemv(ss, nseg, pairs, m->nsm, op.g, op.pl);
     if (rc) return rc;
@@ -899,8 +968,7 @@ static int build_step(kq_model* m, bool head, bool persist, std::vector<StepOp>&
     cur ^= 1;
     ops.push_back(op);
     // attention
-    StepOp at;
-    std::memset(&at, 0, sizeof(at));
+    StepOp at{};
     at.kind = PH_ATTN;
     AttnParams& a = at.a.a;
     a.q = m->q; a.kc = w.kc; a.vc = w.vc;
@@ -955,6 +1023,10 @@ static int build_step(kq_model* m, bool head, bool persist, std::vector<StepOp>&
     p.out_cap = m->out_cap;
     ops.push_back(op);
   }
+  if (!persist)
+    for (StepOp& op : ops)
+      if (op.kind == PH_GEMV)
+        op.tmv = tmv_plan(op.g, m->nsm, g_dev[m->device].tmv_smem, m->tv_part, m->tv_ticket, op.t, op.tgrid);
   return KQ_OK;
 }
 
@@ -989,7 +1061,8 @@ static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
   bool first = true;
   for (const StepOp& op : ops) {
     if (op.kind == PH_GEMV) {
-      CU(launch_gemv(op.g, op.pl, s, !first));
+      if (op.tmv) CU(launch_pdl(k_tmv, op.tgrid, dim3(TV_THREADS), (size_t)op.t.smem, s, op.t));
+      else CU(launch_gemv(op.g, op.pl, s, !first));
     } else if (m->attn_mode == 1) {
       CU(attn_cl_fn(G, m->attn_cl)(op.a.a, s, true));
     } else if (m->attn_mode == 2) {
@@ -1879,6 +1952,8 @@ extern "C" void kq_qmat_free(kq_qmat* a) {
   if (!a) return;
   cudaSetDevice(a->device);
   cudaFree(a->buf);
+  cudaFree(a->tv_part);
+  cudaFree(a->tv_ticket);
   delete a;
 }
 extern "C" size_t kq_qmat_bytes(const kq_qmat* a) { return a ? a->bytes : 0; }
@@ -1912,24 +1987,45 @@ extern "C" int kq_qmat_dequant(kq_qmat* a, int row, int nrows, float* out) {
   return KQ_OK;
 }
 
-static int qmat_gemv_params(kq_qmat* a, const float* x_dev, float* y_dev, GemvParams& p, GemvPlan& pl) {
-  SegSpec ss[1] = {{a, EPI_F32, y_dev, nullptr}};
-  int rc = fill_gemv(ss, 1, false, g_dev[a->device].nsm, p, pl);
+// One matrix-vector product y = W x: the tensor-core GEMV where it covers the shape, else k_gemv.
+struct MatvecLaunch {
+  GemvParams p;
+  GemvPlan pl;
+  bool tmv = false;
+  TmvParams t;
+  dim3 grid;
+};
+
+static int qmat_gemv_params(kq_qmat* a, const float* x_dev, float* y_dev, MatvecLaunch& L) {
+  int rc = dev_init(a->device);
   if (rc) return rc;
-  p.xmode = XS_PLAIN;
-  p.x = x_dev;
-  p.err = g_dev[a->device].err;
+  SegSpec ss[1] = {{a, EPI_F32, y_dev, nullptr}};
+  if ((rc = fill_gemv(ss, 1, false, g_dev[a->device].nsm, L.p, L.pl))) return rc;
+  L.p.xmode = XS_PLAIN;
+  L.p.x = x_dev;
+  L.p.err = g_dev[a->device].err;
+  const DevCtx& D = g_dev[a->device];
+  if (D.tmv_smem > 0 && !a->tv_part) {
+    if (cudaMalloc(&a->tv_part, (size_t)D.nsm * 2 * TV_ROWS * 4) != cudaSuccess ||
+        cudaMalloc(&a->tv_ticket, (size_t)TV_MAX_TILES * 4) != cudaSuccess ||
+        cudaMemset(a->tv_ticket, 0, (size_t)TV_MAX_TILES * 4) != cudaSuccess)
+      return set_err(KQ_ERR_MEMORY, "matvec scratch");
+  }
+  L.tmv = tmv_plan(L.p, D.nsm, D.tmv_smem, a->tv_part, a->tv_ticket, L.t, L.grid);
   return KQ_OK;
+}
+static cudaError_t matvec_launch(const MatvecLaunch& L, cudaStream_t s, bool pdl) {
+  if (L.tmv) return launch_pdl(k_tmv, L.grid, dim3(TV_THREADS), (size_t)L.t.smem, s, L.t);
+  return launch_gemv(L.p, L.pl, s, pdl);
 }
 
 extern "C" int kq_qmat_matvec_dev(kq_qmat* a, const float* x_dev, float* y_dev, void* stream) {
   if (!a || !x_dev || !y_dev) return set_err(KQ_ERR_ARG, "null argument");
   CU(cudaSetDevice(a->device));
-  GemvParams p;
-  GemvPlan pl;
-  int rc = qmat_gemv_params(a, x_dev, y_dev, p, pl);
+  MatvecLaunch L;
+  int rc = qmat_gemv_params(a, x_dev, y_dev, L);
   if (rc) return rc;
-  CU(launch_gemv(p, pl, (cudaStream_t)stream, false));
+  CU(matvec_launch(L, (cudaStream_t)stream, false));
   return KQ_OK;
 }
 
@@ -2019,18 +2115,17 @@ extern "C" int kq_time_matvec(kq_qmat* const* mats, int ncopies, int n, float* m
   CU(cudaMemset(xd, 0, (size_t)a->C * 4));
   cudaStream_t s;
   CU(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
-  std::vector<GemvParams> ps(ncopies);
-  GemvPlan pl;
+  std::vector<MatvecLaunch> ps(ncopies);
   int rc = KQ_OK;
-  for (int i = 0; i < ncopies && !rc; ++i) rc = qmat_gemv_params(mats[i], xd, yd, ps[i], pl);
+  for (int i = 0; i < ncopies && !rc; ++i) rc = qmat_gemv_params(mats[i], xd, yd, ps[i]);
   cudaEvent_t e0, e1;
   cudaEventCreate(&e0);
   cudaEventCreate(&e1);
   for (int i = 0; i < 3 * ncopies && !rc; ++i)
-    if (launch_gemv(ps[i % ncopies], pl, s, false) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "timing launch");
+    if (matvec_launch(ps[i % ncopies], s, false) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "timing launch");
   cudaEventRecord(e0, s);
   for (int i = 0; i < n && !rc; ++i)
-    if (launch_gemv(ps[i % ncopies], pl, s, true) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "timing launch");
+    if (matvec_launch(ps[i % ncopies], s, true) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "timing launch");
   cudaEventRecord(e1, s);
   cudaEventSynchronize(e1);
   float ms = 0.f;

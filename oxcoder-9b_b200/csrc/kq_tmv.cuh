@@ -1,0 +1,668 @@
+// kq_tmv.cuh -- single-token Q4_K / Q6_K GEMV on the 5th-generation tensor cores (tcgen05.mma
+// kind::i8, A in tensor memory), for the decode step's per-layer projections.
+//
+// Replaces, for the q/k/v, o, gate/up and down projections of one token, the reference's
+// q4_gemv (scripts/kindi_q4/kindi/q4.cu:18-27) with the same fusions as the CUDA-core k_gemv:
+// residual + RMS norm prologue (q4_rms q4.cu:39-46), rotary + fp16 K/V store, V store, SwiGLU
+// (q4_silu q4.cu:36-38) or a plain fp32 output.
+//
+// Arithmetic. The activation vector of each 256-column super-block is split exactly into three
+// int8 digit planes, x = s3 * (16384 x1 + 128 x2 + x3) (s3 a power of two per super-block). The
+// weights enter the MMA as their raw unsigned digits: Q4_K low nibbles as bytes q (w & 0x0F0F0F0F),
+// high nibbles in place as 16 q (w & 0xF0F0F0F0), Q6_K as the 6-bit q. One MMA per 32-column
+// group (K = 32, M = 128 rows, N = 16, the smallest N of an M = 128 MMA): its B operand is the
+// group's three planes (rows 0-2 of the 16-row B tile; the other rows are don't-care, read from
+// whatever follows in shared memory), so D columns 0-2 are the exact int32 dot products of the
+// group's weight digits with each plane (for Q6_K, whose scale blocks are 16 columns, the B tile
+// holds the first 16 columns' planes in rows 0-2 and the last 16's in rows 3-5, zero elsewhere).
+// The thread owning the row then applies the integer sub-block scales in int32 (exact: |sum| <
+// 2.5e8), combines the planes in fp32 and adds the d / dmin terms as k_gemv does.
+//
+// Work split ("stream-K"): the units (128-row tile t, super-block g), ordered t-major, are cut into
+// one contiguous run per CTA (one CTA per SM, all resident). A CTA streams its run without a break
+// at tile boundaries; a tile it covers whole gets its epilogue at once, the (at most two) tiles it
+// shares with neighbours leave an fp32 partial and the last contributor (ticket) sums the partials
+// in CTA order and runs the epilogue, so the result does not depend on timing. Warp roles:
+//   warps 0-7   thread (row r = 32 (warp & 3) + lane, half hh = warp >> 2 of the super-block):
+//               prologue (activation digits -> B tiles), then per unit its A digits to tensor
+//               memory and the read-back of the previous unit's D; tile flushes and epilogues
+//   warps 8-11  raw loaders: cp.async of each unit's bytes for 32 rows each (row strides 144 /
+//               208 B: conflict-free 16-byte reads)
+//   warp 12     TMEM allocation (512 columns: A digits of two units in [0, 128), two D regions of
+//               8 groups x 16 columns in [128, 384)); lane 0 issues the 8 MMAs of each unit
+// Every wait is bounded; on a timeout the CTA records the error, skips the remaining work (every
+// thread still takes the same barriers) and drains before it exits.
+#pragma once
+#include "kq_common.cuh"
+#include "kq_qformat.cuh"
+#include "kq_gemv.cuh"
+#include "kq_tmm.cuh"
+
+namespace kq {
+
+constexpr int TV_ROWS = 128;
+constexpr int TV_DQ_WARPS = 8;
+constexpr int TV_LD_WARPS = 4;
+constexpr int TV_MMA_WARP = TV_DQ_WARPS + TV_LD_WARPS;
+constexpr int TV_THREADS = (TV_MMA_WARP + 1) * 32;
+constexpr int TV_RS = 5;                                          // raw unit stages
+constexpr int TV_MAX_G = 48;                                      // super-blocks per row, at most
+constexpr int TV_MAX_SEG = 3;
+constexpr int TV_MAX_TILES = 4096;                                // row tiles per launch, at most
+constexpr uint32_t TV_TMEM_COLS = 512;
+constexpr int TV_MMA_N = 16;                                      // D columns per group
+constexpr int TV_B_Q4 = 96, TV_B_Q6 = 144;                        // B bytes per 32-column group
+constexpr int TV_B_PAD = 320;                                     // the 16-row B tile's don't-care rows
+constexpr int TV_RAW_Q4 = TM_RAW_Q4, TV_RAW_Q6 = TM_RAW_Q6;       // 144 / 208
+constexpr size_t TV_RAW_BYTES = (size_t)TV_ROWS * TV_RAW_Q6;      // one raw stage (either type)
+
+// Dynamic shared memory, identical on host (sizing) and device: raw ring, Q6_K d words, s3[G],
+// X32[G][8], C16[G][16] (int4), red[128], the Q4_K-layout B tiles (if any Q4_K segment), the
+// Q6_K-layout B tiles (if any Q6_K segment).
+struct TvSmem {
+  size_t d, s3, x32, c16, red, bq4, bq6, total;
+};
+__host__ __device__ inline TvSmem tv_smem(int G, bool has_q4, bool has_q6) {
+  TvSmem L;
+  size_t o = (size_t)TV_RS * TV_RAW_BYTES;
+  L.d = o; o += (size_t)TV_RS * TV_ROWS * 4;
+  L.s3 = o; o += (size_t)G * 4;
+  o = (o + 15) & ~(size_t)15;
+  L.x32 = o; o += (size_t)G * 8 * 4;
+  o = (o + 15) & ~(size_t)15;
+  L.c16 = o; o += (size_t)G * 16 * 16;
+  L.red = o; o += (size_t)TV_ROWS * 4;
+  L.bq4 = o; if (has_q4) o += (size_t)G * 8 * TV_B_Q4 + TV_B_PAD;
+  o = (o + 15) & ~(size_t)15;
+  L.bq6 = o; if (has_q6) o += (size_t)G * 8 * TV_B_Q6 + TV_B_PAD;
+  L.total = (o + 127) & ~(size_t)127;
+  return L;
+}
+
+struct TvSeg {
+  QView w;
+  int tile0;            // first row tile of this segment
+  int epi;
+  float* out_f;
+  __half* out_h;
+};
+
+struct TmvParams {
+  TvSeg seg[TV_MAX_SEG];
+  int nseg, ntiles, G;
+  int has_q4, has_q6;
+  int smem;             // dynamic shared memory bytes (tv_smem(G, has_q4, has_q6).total)
+  int xmode;            // XS_PLAIN or XS_NORM
+  const float* x;
+  const float* h_in;
+  const float* y_add;
+  const float* gamma;
+  float* h_out;
+  float eps;
+  DecodeState* st;
+  const float* cos_t;
+  const float* sin_t;
+  int hd, ctx;
+  float* part;          // partials of shared tiles [gridDim.x][2][128]
+  int* ticket;          // [ntiles], zero between launches
+  int* err;
+};
+
+// Instruction descriptor, kind::i8: s32 D (2 at bit 4), A unsigned (0 at bit 7), B signed (1 at
+// bit 10), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t tc_idesc_i8(int M, int N) {
+  return (2u << 4) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// Shared-memory descriptor of a 16-row B tile, K-major without swizzle: 8-row groups of 16-byte
+// rows per K half (rows contiguous), the second K half `lbo` bytes after the first, the second
+// 8-row group (don't-care rows here) 128 bytes after the first. Version 1 at bit 46, layout 0.
+__device__ __forceinline__ uint64_t tv_bdesc(uint32_t saddr, uint32_t lbo) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(128 >> 4) << 32) |
+         ((uint64_t)1 << 46);
+}
+// D[tmem] = A[tmem] * B[smem desc]^T, kind::i8 (u8 x s8 -> s32), no accumulation.
+__device__ __forceinline__ void tc_mma_i8_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, 0, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+// 4 / 8 consecutive 32-bit columns of this thread's TMEM lane; not waited (tc_wait_ld).
+__device__ __forceinline__ void tc_ld4_nw(uint32_t taddr, int (&v)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(taddr)
+               : "memory");
+}
+__device__ __forceinline__ void tc_ld8_nw(uint32_t taddr, int (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Unsigned byte k of w (the signed one is sbyte in kq_gemv.cuh).
+__device__ __forceinline__ int tv_ubyte(uint32_t w, int k) { return (int)__byte_perm(w, 0, 0x4440u | (uint32_t)k); }
+
+// Unit range of CTA c of n over U units, and the CTA that holds unit u.
+__host__ __device__ inline long long tv_unit0(int c, int n, long long U) { return (long long)c * U / n; }
+__host__ __device__ inline int tv_cta_of(long long u, int n, long long U) { return (int)(((u + 1) * n - 1) / U); }
+
+// Prologue (warps 0-7): the activations of all G super-blocks as int8 digit planes in the MMA's B
+// tiles (the Q4_K and / or the Q6_K layout, as the launch's segments need), and the per-super-block
+// / per-group scalars: s3 (the digit unit), X32 (the digit sum of each 32-column group as a float,
+// for the Q4_K min term) and C16 (32 x the digit sums of each 16 columns, for the Q6_K "-32").
+// XS_NORM: residual add and RMS norm over all C columns first (q4_rms q4.cu:39-46; fp64 sum of
+// squares), CTA 0 writing the residual sum to h_out. The digit split is k_gemv's, per super-block:
+// s1 = 2^e with max |x| <= 127 s1, s2 = s1 / 128, s3 = s1 / 16384.
+__device__ __forceinline__ void tv_prologue(const TmvParams& P, uint8_t* sm, const TvSmem& L, double* redd) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NT = TV_DQ_WARPS * 32;
+  const int C = 256 * P.G;
+  float ns = 1.f;
+  if (P.xmode == XS_NORM) {
+    double acc = 0.0;
+    const bool wr = blockIdx.x == 0 && P.h_out;
+    for (int c0 = 8 * tid; c0 < C; c0 += 8 * NT) {
+      float hv[8], yv[8];
+      load8(P.h_in + c0, hv);
+      if (P.y_add) {
+        load8(P.y_add + c0, yv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) hv[i] = __fadd_rn(hv[i], yv[i]);
+      }
+      if (wr) {
+        float4* ho = reinterpret_cast<float4*>(P.h_out + c0);
+        ho[0] = make_float4(hv[0], hv[1], hv[2], hv[3]);
+        ho[1] = make_float4(hv[4], hv[5], hv[6], hv[7]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = __dadd_rn(acc, __dmul_rn((double)hv[i], (double)hv[i]));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) redd[warp] = acc;
+    named_bar(2, NT);
+    double tot = 0.0;
+    for (int w = 0; w < TV_DQ_WARPS; ++w) tot += redd[w];
+    ns = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / (double)C), P.eps)));
+  }
+  uint8_t* bq4 = sm + L.bq4;
+  uint8_t* bq6 = sm + L.bq6;
+  float* s3a = reinterpret_cast<float*>(sm + L.s3);
+  float* x32 = reinterpret_cast<float*>(sm + L.x32);
+  int4* c16 = reinterpret_cast<int4*>(sm + L.c16);
+  const float RND = 12582912.0f;   // 1.5 * 2^23: adding it rounds to an integer (RNE), |y| <= 128
+  // chunk q = 8 columns; a warp holds one super-block (q >> 5 is warp-uniform)
+  for (int q = tid; q < 32 * P.G; q += NT) {
+    const int kb = q >> 5, j = q & 31, c0 = 256 * kb + 8 * j;
+    float v[8];
+    if (P.xmode == XS_NORM) {
+      float hv[8], yv[8], gm[8];
+      load8(P.h_in + c0, hv);
+      load8(P.gamma + c0, gm);
+      if (P.y_add) load8(P.y_add + c0, yv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(P.y_add ? __fadd_rn(hv[i], yv[i]) : hv[i], ns), gm[i]);
+    } else {
+      load8(P.x + c0, v);
+    }
+    float mx = 0.f;
+    int bad = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a = fabsf(v[i]);
+      bad |= !(a <= FLT_MAX);
+      mx = fmaxf(mx, a);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+    }
+    int e = 0;
+    if (!bad && mx >= 0x1p-100f) {
+      e = ((__float_as_int(mx) >> 23) & 0xFF) - 127 - 6;   // mx is normal here
+      if (mx > 127.f * pow2f(e)) ++e;
+    }
+    const float s1 = pow2f(e), s2 = pow2f(e - 7), i1 = pow2f(-e), i2 = pow2f(7 - e), i3 = pow2f(14 - e);
+    uint32_t wv[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+    int S0 = 0, S1 = 0, S2 = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float x = bad ? 0.f : v[i];
+      const float t1 = __fadd_rn(__fmul_rn(x, i1), RND);
+      const float x1 = __fsub_rn(t1, RND);
+      const float r1 = __fsub_rn(x, __fmul_rn(x1, s1));
+      const float t2 = __fadd_rn(__fmul_rn(r1, i2), RND);
+      const float x2 = __fsub_rn(t2, RND);
+      const float r2 = __fsub_rn(r1, __fmul_rn(x2, s2));
+      const float t3 = __fadd_rn(__fmul_rn(r2, i3), RND);
+      const int q1 = __float_as_int(t1) - 0x4B400000, q2 = __float_as_int(t2) - 0x4B400000,
+                q3 = __float_as_int(t3) - 0x4B400000;
+      S0 += q1; S1 += q2; S2 += q3;
+      wv[0][i >> 2] |= (uint32_t)(q1 & 0xFF) << (8 * (i & 3));
+      wv[1][i >> 2] |= (uint32_t)(q2 & 0xFF) << (8 * (i & 3));
+      wv[2][i >> 2] |= (uint32_t)(q3 & 0xFF) << (8 * (i & 3));
+    }
+    // B tile of group gi = j >> 2 (32 columns); this chunk is its 8 columns 8p .. 8p + 7
+    const int gi = j >> 2, p = j & 3;
+    if (P.has_q4) {
+      // [K half][plane][16 B]: rows 0-2 of the tile are the planes, the K halves 48 B apart
+      uint8_t* b = bq4 + (size_t)(kb * 8 + gi) * TV_B_Q4 + 48 * (p >> 1) + 8 * (p & 1);
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl) *reinterpret_cast<uint2*>(b + 16 * pl) = make_uint2(wv[pl][0], wv[pl][1]);
+    }
+    if (P.has_q6) {
+      // [first 16 columns' planes][48 zero bytes][last 16 columns' planes]: the tile at +0 has rows
+      // (a0 a1 a2 0 0 0 ..) in K half 0 and the one at +48 (0 0 0 b0 b1 b2 ..) in K half 1
+      uint8_t* gb = bq6 + (size_t)(kb * 8 + gi) * TV_B_Q6;
+      uint8_t* b = gb + ((p >> 1) ? 96 : 0) + 8 * (p & 1);
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl) *reinterpret_cast<uint2*>(b + 16 * pl) = make_uint2(wv[pl][0], wv[pl][1]);
+      if (p == 0) {
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(gb + 48) = z;
+        *reinterpret_cast<uint4*>(gb + 64) = z;
+        *reinterpret_cast<uint4*>(gb + 80) = z;
+      }
+    }
+    S0 += __shfl_xor_sync(0xffffffffu, S0, 1);
+    S1 += __shfl_xor_sync(0xffffffffu, S1, 1);
+    S2 += __shfl_xor_sync(0xffffffffu, S2, 1);
+    if (P.has_q6 && (j & 1) == 0) c16[kb * 16 + (j >> 1)] = make_int4(32 * S0, 32 * S1, 32 * S2, 0);
+    S0 += __shfl_xor_sync(0xffffffffu, S0, 2);
+    S1 += __shfl_xor_sync(0xffffffffu, S1, 2);
+    S2 += __shfl_xor_sync(0xffffffffu, S2, 2);
+    if (P.has_q4 && (j & 3) == 0) x32[kb * 8 + gi] = (float)(S0 * 16384 + S1 * 128 + S2);
+    if (j == 0) s3a[kb] = bad ? __int_as_float(0x7fc00000) : pow2f(e - 14);
+  }
+}
+
+// Epilogue of row lrow of segment S (value v; vo = the value of row lrow ^ 1), as k_gemv's.
+__device__ __forceinline__ void tv_epilogue(const TmvParams& P, const TvSeg& S, int lrow, float v, float vo) {
+  const int epi = S.epi;
+  if (epi == EPI_F32) {
+    S.out_f[lrow] = v;
+    return;
+  }
+  int pos = P.st ? P.st->pos : 0;
+  const bool kv_ok = pos >= 0 && pos < P.ctx;   // the host validates; never store outside the cache
+  if (!kv_ok) {
+    pos = 0;
+    if (epi == EPI_ROPE_K || epi == EPI_V || epi == EPI_ROPE_Q) atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
+  }
+  switch (epi) {
+    case EPI_V: {
+      const int kv = lrow / P.hd, e = lrow % P.hd;
+      if (kv_ok) S.out_h[((size_t)kv * P.ctx + pos) * P.hd + e] = __float2half_rn(v);
+    } break;
+    case EPI_SWIGLU:
+      if ((lrow & 1) == 0) S.out_f[lrow >> 1] = __fmul_rn(silu_f(v), vo);
+      break;
+    case EPI_ROPE_Q:
+    case EPI_ROPE_K:
+      if ((lrow & 1) == 0) {
+        int rp = P.st ? P.st->rpos : 0;
+        if (rp < 0 || rp >= P.ctx) rp = 0;   // the host validates
+        const int hh = lrow / P.hd, i2 = (lrow % P.hd) >> 1, half = P.hd >> 1;
+        const float c = __ldg(P.cos_t + (size_t)rp * half + i2), sn = __ldg(P.sin_t + (size_t)rp * half + i2);
+        const float o0 = __fsub_rn(__fmul_rn(v, c), __fmul_rn(vo, sn));
+        const float o1 = __fadd_rn(__fmul_rn(v, sn), __fmul_rn(vo, c));
+        if (epi == EPI_ROPE_Q) {
+          S.out_f[hh * P.hd + i2] = o0;
+          S.out_f[hh * P.hd + i2 + half] = o1;
+        } else if (kv_ok) {
+          __half* dst = S.out_h + ((size_t)hh * P.ctx + pos) * P.hd;
+          dst[i2] = __float2half_rn(o0);
+          dst[i2 + half] = __float2half_rn(o1);
+        }
+      }
+      break;
+  }
+}
+
+// Bounded wait that ignores the abort flag: the final drain of the CTA's own MMAs, which finish
+// on their own.
+__device__ __forceinline__ void tv_drain_wait(uint64_t* bar, uint32_t parity, int* err) {
+  const uint64_t t0 = tm_clock_ns();
+  for (uint32_t it = 0; it < KQ_WAIT_LIMIT; ++it) {
+    if (mbar_try_wait(bar, parity)) return;
+    if ((it & 255) == 255 && tm_clock_ns() - t0 > TM_WAIT_NS) break;
+  }
+  atomicOr(err, KQ_DEV_ERR_DRAIN);
+}
+
+__global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ TmvParams P) {
+  extern __shared__ __align__(128) uint8_t tv_sm[];
+  uint8_t* sm = tv_sm;
+  const TvSmem L = tv_smem(P.G, P.has_q4 != 0, P.has_q6 != 0);
+  uint8_t* raw_ring = sm;
+  uint32_t* d_ring = reinterpret_cast<uint32_t*>(sm + L.d);
+  __shared__ __align__(8) uint64_t raw_full[TV_RS], raw_empty[TV_RS], a_full[2], d_full[2], d_free[2], b_ready, mma_done;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort, s_last;
+  __shared__ double s_redd[TV_DQ_WARPS];
+  volatile int* abort_f = &s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = P.G, nct = (int)gridDim.x, cta = (int)blockIdx.x;
+  const long long U = (long long)P.ntiles * G;
+  const long long u0 = tv_unit0(cta, nct, U);
+  const int n = (int)(tv_unit0(cta + 1, nct, U) - u0);
+  auto seg_of = [&](int t) -> int {
+    int si = 0;
+    while (si + 1 < P.nseg && t >= P.seg[si + 1].tile0) ++si;
+    return si;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < TV_RS; ++i) { mbar_init(&raw_full[i], TV_LD_WARPS * 32); mbar_init(&raw_empty[i], TV_DQ_WARPS); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&a_full[i], TV_DQ_WARPS);
+      mbar_init(&d_full[i], 1);
+      mbar_init(&d_free[i], TV_DQ_WARPS);
+    }
+    mbar_init(&b_ready, 1);
+    mbar_init(&mma_done, 1);
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == TV_MMA_WARP) {
+    tmem_alloc(&s_tmem, TV_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  pdl_trigger();
+  if (threadIdx.x == 0) KQ_TRACE_AT(0, 10);
+
+  if (warp >= TV_DQ_WARPS && warp < TV_MMA_WARP) {
+    // ---------------- raw loaders: rows [32 lw, 32 lw + 32) of every unit; the weights do not
+    // depend on the previous kernel (no PDL wait)
+    const int lw = warp - TV_DQ_WARPS;
+    const uint64_t pol = l2_evict_first_policy();
+    for (int k = 0; k < n; ++k) {
+      const int slot = k % TV_RS;
+      if (k >= TV_RS && !tm_wait(&raw_empty[slot], (uint32_t)((k / TV_RS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
+        break;
+      const long long u = u0 + k;
+      const int t = (int)(u / G), g = (int)(u % G);
+      const TvSeg& S = P.seg[seg_of(t)];
+      const QView& w = S.w;
+      const int row0 = (t - S.tile0) * TV_ROWS;
+      const bool q4 = w.type == Q4K;
+      const int rstride = q4 ? TV_RAW_Q4 : TV_RAW_Q6;
+      uint8_t* dst = raw_ring + (size_t)slot * TV_RAW_BYTES;
+      // nibbles / ql (and Q6_K qh): 8 rows per instruction, 4 lanes per 64-byte run
+#pragma unroll
+      for (int rb = 0; rb < 4; ++rb) {
+        const int r = 32 * lw + 8 * rb + (lane >> 2), pc = lane & 3, row = row0 + r;
+        const bool ok = row < w.R;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint8_t* src = ok ? w.base + row_plane_off(w.type, G, row, 0, (size_t)c * 64 * G + (size_t)g * 64 + pc * 16) : w.base;
+          cp_async16(dst + r * rstride + c * 64 + pc * 16, src, ok ? 16u : 0u, pol);
+        }
+        if (!q4) {
+          const uint8_t* src = ok ? w.base + row_plane_off(Q6K, G, row, 1, (size_t)g * 64 + pc * 16) : w.base;
+          cp_async16(dst + r * rstride + 128 + pc * 16, src, ok ? 16u : 0u, pol);
+        }
+      }
+      // Q4_K header / Q6_K scales (16 B per row); Q6_K d: the aligned 4-byte word that holds it
+      {
+        const int r = 32 * lw + lane, row = row0 + r;
+        const bool ok = row < w.R;
+        const uint8_t* src = ok ? w.base + row_plane_off(w.type, G, row, q4 ? 1 : 2, (size_t)g * 16) : w.base;
+        cp_async16(dst + r * rstride + (q4 ? 128 : 192), src, ok ? 16u : 0u, pol);
+        if (!q4) {
+          const uintptr_t a = ok ? reinterpret_cast<uintptr_t>(w.base + row_plane_off(Q6K, G, row, 3, (size_t)g * 2))
+                                 : reinterpret_cast<uintptr_t>(w.base);
+          cp_async4(d_ring + slot * TV_ROWS + r, reinterpret_cast<const void*>(a & ~(uintptr_t)3), ok ? 4u : 0u);
+        }
+      }
+      cp_async_arrive(&raw_full[slot]);
+    }
+    cp_async_wait_all();
+  } else if (warp == TV_MMA_WARP) {
+    // ---------------- MMA issue (one thread): unit k uses A columns [64 (k & 1), +64) and D columns
+    // [128 + 128 (k & 1), +128) (group gi at 16 gi)
+    if (lane == 0) {
+      const uint32_t idesc = tc_idesc_i8(TV_ROWS, TV_MMA_N);
+      const uint32_t bq4 = smem_u32(sm + L.bq4), bq6 = smem_u32(sm + L.bq6);
+      if (tm_wait(&b_ready, 0, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) {
+        for (int k = 0; k < n; ++k) {
+          const int slot = k & 1;
+          if (!tm_wait(&a_full[slot], (uint32_t)(k >> 1) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
+          if (k >= 2 && !tm_wait(&d_free[slot], (uint32_t)((k - 2) >> 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f)) break;
+          KQ_TRACE_AT(k, 4);
+          tc_fence_after();
+          const long long u = u0 + k;
+          const int t = (int)(u / G), g = (int)(u % G);
+          const bool q4 = P.seg[seg_of(t)].w.type == Q4K;
+          const uint32_t bb = (q4 ? bq4 : bq6) + (uint32_t)g * 8u * (q4 ? TV_B_Q4 : TV_B_Q6), bst = q4 ? TV_B_Q4 : TV_B_Q6;
+          const uint32_t ta = tmem + 64u * (uint32_t)slot, td = tmem + 128u + 128u * (uint32_t)slot;
+#pragma unroll
+          for (int gi = 0; gi < 8; ++gi)
+            tc_mma_i8_ts(td + (uint32_t)TV_MMA_N * gi, ta + 8u * gi, tv_bdesc(bb + (uint32_t)gi * bst, 48u), idesc);
+          tc_commit(&d_full[slot]);
+          KQ_TRACE_AT(k, 5);
+        }
+      }
+      tc_commit(&mma_done);
+      tv_drain_wait(&mma_done, 0, P.err);   // every MMA issued here has completed
+    }
+    __syncwarp();
+  } else {
+    // ---------------- warps 0-7: thread (row r of the warp's TMEM lane quarter, half hh)
+    const int qd = warp & 3, hh = warp >> 2, r = 32 * qd + lane;
+    pdl_wait();
+    tv_prologue(P, sm, L, s_redd);
+    fence_proxy_async();   // the B tiles are read by the tensor cores
+    named_bar(1, TV_DQ_WARPS * 32);
+    if (threadIdx.x == 0) {
+      mbar_arrive(&b_ready);
+      KQ_TRACE_AT(255, 0);
+    }
+    const uint32_t tl = tmem + ((uint32_t)(32 * qd) << 16);
+    const float* s3a = reinterpret_cast<const float*>(sm + L.s3);
+    const float* x32 = reinterpret_cast<const float*>(sm + L.x32);
+    const int4* c16 = reinterpret_cast<const int4*>(sm + L.c16);
+    float* red = reinterpret_cast<float*>(sm + L.red);
+    const int tf0 = (int)(u0 / G);   // this CTA's first tile
+    float acc = 0.f;
+    bool ok = true;
+    // read-back of unit k (super-block g, type q4), groups 4 hh + j: the row's int32 dot products
+    // with the scales applied (Q4_K: cw = the 6-bit scales of sub-blocks 4hh .. 4hh + 3 as bytes,
+    // mw the mins, d0 = d, d1 = dmin; Q6_K: cw, mw = scale words 2hh (first 16 columns of each
+    // group) and 2hh + 1 (last 16), d0 = d)
+    auto readout = [&](int k, int g, bool q4, uint32_t cw, uint32_t mw, float d0, float d1) -> bool {
+      const int slot = k & 1;
+      if (!__all_sync(0xffffffffu, tm_wait(&d_full[slot], (uint32_t)(k >> 1) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)))
+        return false;
+      tc_fence_after();
+      if (threadIdx.x == 0) KQ_TRACE_AT(k, 2);
+      const uint32_t td = tl + 128u + 128u * (uint32_t)slot + (uint32_t)(4 * TV_MMA_N) * (uint32_t)hh;
+      const float s3 = s3a[g];
+      int P3[3] = {0, 0, 0};
+      if (q4) {
+        int D[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tc_ld4_nw(td + (uint32_t)TV_MMA_N * j, D[j]);
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&d_free[slot]);
+        float Qm = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {   // sub-block 4hh + j: c = j >> 1, high nibble if j odd
+          const int c = tv_ubyte(cw, j) << ((j & 1) ? 0 : 4);   // high nibbles enter as 16 q
+          P3[0] += c * D[j][0];
+          P3[1] += c * D[j][1];
+          P3[2] += c * D[j][2];
+          Qm = __fmaf_rn((float)tv_ubyte(mw, j), x32[g * 8 + 4 * hh + j], Qm);
+        }
+        const float Pf = planes_combine(P3);
+        acc = __fadd_rn(acc, __fsub_rn(__fmul_rn(__fmul_rn(s3, 0.0625f), __fmul_rn(d0, Pf)), __fmul_rn(s3, __fmul_rn(d1, Qm))));
+      } else {
+        int D[4][8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tc_ld8_nw(td + (uint32_t)TV_MMA_N * j, D[j]);
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&d_free[slot]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {   // group k = j of half hh: scale bytes j of the two words
+          const int gi = 4 * hh + j;
+          const int sa = sbyte(cw, j), sb = sbyte(mw, j);
+          const int4 ca = c16[g * 16 + 2 * gi], cb = c16[g * 16 + 2 * gi + 1];
+          P3[0] += sa * (D[j][0] - ca.x) + sb * (D[j][3] - cb.x);
+          P3[1] += sa * (D[j][1] - ca.y) + sb * (D[j][4] - cb.y);
+          P3[2] += sa * (D[j][2] - ca.z) + sb * (D[j][5] - cb.z);
+        }
+        acc = __fadd_rn(acc, __fmul_rn(s3, __fmul_rn(d0, planes_combine(P3))));
+      }
+      if (threadIdx.x == 0) KQ_TRACE_AT(k, 3);
+      return true;
+    };
+    // end of tile t's units in this CTA: the row sums of both halves; the epilogue if the CTA
+    // covered the whole tile, else the partial and, for the last contributor, the merge in CTA
+    // order. Every warp of 0-7 takes the same barriers, also after a failure.
+    auto flush = [&](int t, bool whole) {
+      if (hh == 1) red[r] = acc;
+      const bool good = named_bar_and(1, TV_DQ_WARPS * 32, ok && !*abort_f);
+      if (hh == 0) {
+        const TvSeg& S = P.seg[seg_of(t)];
+        const int row = (t - S.tile0) * TV_ROWS + r;
+        float v = __fadd_rn(acc, red[r]);
+        bool fin = good && whole;
+        if (good && !whole) {
+          __stcg(P.part + ((size_t)cta * 2 + (t == tf0 ? 0 : 1)) * TV_ROWS + r, v);
+          __threadfence();
+          named_bar(3, 4 * 32);
+          const int cf = tv_cta_of((long long)t * G, nct, U), cl = tv_cta_of((long long)t * G + G - 1, nct, U);
+          if (threadIdx.x == 0) s_last = atomicAdd(&P.ticket[t], 1) == cl - cf;
+          named_bar(3, 4 * 32);
+          fin = s_last;
+          if (fin) {
+            __threadfence();
+            v = 0.f;
+            for (int c = cf; c <= cl; ++c) {
+              const int tfc = (int)(tv_unit0(c, nct, U) / G);
+              v = __fadd_rn(v, __ldcg(P.part + ((size_t)c * 2 + (t == tfc ? 0 : 1)) * TV_ROWS + r));
+            }
+            if (threadIdx.x == 0) P.ticket[t] = 0;
+          }
+        }
+        if (fin) {
+          const float vo = __shfl_xor_sync(0xffffffffu, v, 1);
+          if (row < S.w.R) tv_epilogue(P, S, row, v, vo);
+        }
+      }
+      named_bar(1, TV_DQ_WARPS * 32);   // red[] and s_last are reused by the next flush
+      acc = 0.f;
+    };
+    // the read-back of unit k, then the flush if it ends its tile's run in this CTA
+    auto finish = [&](int k, int g, bool q4, uint32_t cw, uint32_t mw, float d0, float d1) {
+      if (ok) ok = readout(k, g, q4, cw, mw, d0, d1);
+      const long long u = u0 + k;
+      const int t = (int)(u / G);
+      if (k == n - 1 || (int)((u + 1) / G) != t) flush(t, u0 <= (long long)t * G && (int)(u % G) == G - 1);
+    };
+    uint32_t pcw = 0, pmw = 0;   // the previous unit's header
+    float pd0 = 0.f, pd1 = 0.f;
+    int pg = 0;
+    bool pq4 = true;
+    for (int k = 0; k < n; ++k) {
+      const int slot = k % TV_RS;
+      const long long u = u0 + k;
+      const int t = (int)(u / G), g = (int)(u % G);
+      const TvSeg& S = P.seg[seg_of(t)];
+      const bool q4 = S.w.type == Q4K;
+      if (ok) ok = __all_sync(0xffffffffu, tm_wait(&raw_full[slot], (uint32_t)(k / TV_RS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f));
+      if (threadIdx.x == 0) KQ_TRACE_AT(k, 0);
+      uint32_t cw = 0, mw = 0;
+      float d0 = 0.f, d1 = 0.f;
+      if (ok) {
+        const int rstride = q4 ? TV_RAW_Q4 : TV_RAW_Q6;
+        const uint8_t* rw = raw_ring + (size_t)slot * TV_RAW_BYTES + (size_t)r * rstride;
+        const uint32_t ta = tl + 64u * (uint32_t)(k & 1) + 32u * (uint32_t)hh;
+        if (q4) {
+          const uint4 H = lds128(rw + 128);
+          d0 = h2f_bits(H.x & 0xFFFFu);
+          d1 = h2f_bits(H.x >> 16);
+          cw = hh ? ((H.w & 0x0F0F0F0Fu) | ((H.y >> 2) & 0x30303030u)) : (H.y & 0x3F3F3F3Fu);          // scales
+          mw = hh ? (((H.w >> 4) & 0x0F0F0F0Fu) | ((H.z >> 2) & 0x30303030u)) : (H.z & 0x3F3F3F3Fu);   // mins
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            // the 32 bytes of (hh, c): low nibbles = sub-block 4hh + 2c, high = 4hh + 2c + 1
+            const uint8_t* b = rw + c * 64 + hh * 32;
+            const uint4 W0 = lds128(b), W1 = lds128(b + 16);
+            const uint32_t wd[8] = {W0.x, W0.y, W0.z, W0.w, W1.x, W1.y, W1.z, W1.w};
+            uint32_t lo[8], hi[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { lo[i] = wd[i] & 0x0F0F0F0Fu; hi[i] = wd[i] & 0xF0F0F0F0u; }
+            tc_st8(ta + 16u * c, lo);
+            tc_st8(ta + 16u * c + 8u, hi);
+          }
+        } else {
+          const uint2 Sc = *reinterpret_cast<const uint2*>(rw + 192 + 8 * hh);   // scale words 2hh, 2hh + 1
+          cw = Sc.x;
+          mw = Sc.y;
+          const uint32_t dw = d_ring[slot * TV_ROWS + r];
+          d0 = h2f_bits(((r & 7) * G + g) & 1 ? dw >> 16 : dw & 0xFFFFu);
+          const uint8_t* hq = rw + 128 + hh * 32;
+          const uint4 H0 = lds128(hq), H1 = lds128(hq + 16);
+          const uint32_t qh[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const uint8_t* lq = rw + m * 64 + hh * 32;
+            const uint4 L0 = lds128(lq), L1 = lds128(lq + 16);
+            const uint32_t ql[8] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w};
+#pragma unroll
+            for (int nib = 0; nib < 2; ++nib) {
+              // group k = 2 nib + m: ql chunk m, nibble nib, qh bits 2k
+              const int kk = 2 * nib + m;
+              uint32_t q6[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                q6[i] = ((ql[i] >> (4 * nib)) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * kk)) & 0x03030303u) << 4);
+              tc_st8(ta + 8u * kk, q6);
+            }
+          }
+        }
+        tc_wait_st();
+        tc_fence_before();
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&a_full[k & 1]);
+        mbar_arrive(&raw_empty[slot]);
+      }
+      if (threadIdx.x == 0) KQ_TRACE_AT(k, 1);
+      if (k > 0) finish(k - 1, pg, pq4, pcw, pmw, pd0, pd1);
+      pcw = cw; pmw = mw; pd0 = d0; pd1 = d1; pg = g; pq4 = q4;
+    }
+    if (n > 0) finish(n - 1, pg, pq4, pcw, pmw, pd0, pd1);
+    if (threadIdx.x == 0) KQ_TRACE_AT(255, 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) KQ_TRACE_AT(0, 11);
+  if (warp == TV_MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TV_TMEM_COLS);
+  }
+}
+
+}  // namespace kq
