@@ -17,6 +17,7 @@
 #include "kq_nccl.h"
 
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -874,6 +875,47 @@ struct StepOp {
 // floats and `ticket` TV_MAX_TILES ints (zero). False when the launch is not covered (embedding
 // prologue, argmax epilogue, more than TV_MAX_G super-blocks per row, shared memory) or the
 // tensor-core GEMV is off: k_gemv runs it.
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+// 3-D byte map over one plane of the kq tile layout: [R/8 tiles (stride tile_bytes)][8 rows
+// (stride `inner`)][inner bytes], box `box0` x 8 x 16 (128 rows), zero fill past the last tile.
+static bool tv_encode(CUtensorMap* m, const uint8_t* base, uint64_t inner, uint64_t tiles, uint64_t tb, uint32_t box0,
+                      bool sw64) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = tmap_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {inner, 8, tiles};
+  const cuuint64_t strides[2] = {inner, tb};
+  const cuuint32_t box[3] = {box0, 8, 16};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// The maps of one segment (kq_tmv.cuh TvSeg).
+static bool tv_seg_maps(TvSeg& S) {
+  const QView& w = S.w;
+  const uint64_t G = (uint64_t)w.G, tiles = (uint64_t)w.R / 8, tb = tile_bytes(w.type, w.G);
+  if (!tv_encode(&S.m0, w.base, 128 * G, tiles, tb, 64, true)) return false;
+  if (w.type == Q4K) {
+    if (!tv_encode(&S.m1, w.base + tile_plane_off(Q4K, w.G, 1), 16 * G, tiles, tb, 16, false)) return false;
+    S.m2 = S.m1;
+    return true;
+  }
+  return tv_encode(&S.m1, w.base + tile_plane_off(Q6K, w.G, 1), 64 * G, tiles, tb, 64, true) &&
+         tv_encode(&S.m2, w.base + tile_plane_off(Q6K, w.G, 2), 16 * G, tiles, tb, 16, false);
+}
+
 static bool tmv_plan(const GemvParams& g, int nsm, size_t smem_max, float* part, int* ticket, TmvParams& T, dim3& grid) {
   if (smem_max == 0 || g.nseg < 1 || g.nseg > TV_MAX_SEG || g.G > TV_MAX_G) return false;
   if (g.xmode != XS_PLAIN && g.xmode != XS_NORM) return false;
@@ -887,6 +929,7 @@ static bool tmv_plan(const GemvParams& g, int nsm, size_t smem_max, float* part,
     T.seg[i].epi = sg.epi;
     T.seg[i].out_f = sg.out_f;
     T.seg[i].out_h = sg.out_h;
+    if (!tv_seg_maps(T.seg[i])) return false;
     ntiles += (sg.w.R + TV_ROWS - 1) / TV_ROWS;
     if (sg.w.type == Q4K) T.has_q4 = 1;
     else T.has_q6 = 1;

@@ -26,13 +26,16 @@
 //   warps 0-7   thread (row r = 32 (warp & 3) + lane, half hh = warp >> 2 of the super-block):
 //               prologue (activation digits -> B tiles), then per unit its A digits to tensor
 //               memory and the read-back of the previous unit's D; tile flushes and epilogues
-//   warps 8-11  raw loaders: cp.async of each unit's bytes for 32 rows each (row strides 144 /
-//               208 B: conflict-free 16-byte reads)
-//   warp 12     TMEM allocation (512 columns: A digits of two units in [0, 128), two D regions of
+//   warp 8      raw loader: lane 0 issues the unit's TMA tensor copies (3-D maps over the planes of
+//               the kq tile layout: 64-byte rows of the nibble / qh planes with the 64-byte swizzle,
+//               conflict-free for 8 consecutive rows; 16-byte rows of the header / scale planes),
+//               all lanes the Q6_K d words (cp.async)
+//   warp 9      TMEM allocation (512 columns: A digits of two units in [0, 128), two D regions of
 //               8 groups x 16 columns in [128, 384)); lane 0 issues the 8 MMAs of each unit
 // Every wait is bounded; on a timeout the CTA records the error, skips the remaining work (every
 // thread still takes the same barriers) and drains before it exits.
 #pragma once
+#include <cuda.h>
 #include "kq_common.cuh"
 #include "kq_qformat.cuh"
 #include "kq_gemv.cuh"
@@ -42,7 +45,7 @@ namespace kq {
 
 constexpr int TV_ROWS = 128;
 constexpr int TV_DQ_WARPS = 8;
-constexpr int TV_LD_WARPS = 4;
+constexpr int TV_LD_WARPS = 1;
 constexpr int TV_MMA_WARP = TV_DQ_WARPS + TV_LD_WARPS;
 constexpr int TV_THREADS = (TV_MMA_WARP + 1) * 32;
 constexpr int TV_RS = 5;                                          // raw unit stages
@@ -53,8 +56,12 @@ constexpr uint32_t TV_TMEM_COLS = 512;
 constexpr int TV_MMA_N = 16;                                      // D columns per group
 constexpr int TV_B_Q4 = 96, TV_B_Q6 = 144;                        // B bytes per 32-column group
 constexpr int TV_B_PAD = 320;                                     // the 16-row B tile's don't-care rows
-constexpr int TV_RAW_Q4 = TM_RAW_Q4, TV_RAW_Q6 = TM_RAW_Q6;       // 144 / 208
-constexpr size_t TV_RAW_BYTES = (size_t)TV_ROWS * TV_RAW_Q6;      // one raw stage (either type)
+// One raw stage (1024-byte aligned): [0, 8192) nibbles / ql of plane chunk c = 0 (128 rows x 64 B,
+// 64-byte swizzle), [8192, 16384) c = 1, then Q4_K: [16384, 18432) headers (128 x 16 B); Q6_K:
+// [16384, 24576) qh (128 x 64 B, swizzled), [24576, 26624) scales (128 x 16 B).
+constexpr int TV_ST_C1 = 8192, TV_ST_HDR = 16384, TV_ST_QH = 16384, TV_ST_SC = 24576;
+constexpr uint32_t TV_TX_Q4 = 18432, TV_TX_Q6 = 26624;
+constexpr size_t TV_RAW_BYTES = 26624;
 
 // Dynamic shared memory, identical on host (sizing) and device: raw ring, Q6_K d words, s3[G],
 // X32[G][8], C16[G][16] (int4), red[128], the Q4_K-layout B tiles (if any Q4_K segment), the
@@ -62,6 +69,7 @@ constexpr size_t TV_RAW_BYTES = (size_t)TV_ROWS * TV_RAW_Q6;      // one raw sta
 struct TvSmem {
   size_t d, s3, x32, c16, red, bq4, bq6, total;
 };
+// (offsets from the 1024-byte aligned start; the launch adds 1024 bytes of alignment slack)
 __host__ __device__ inline TvSmem tv_smem(int G, bool has_q4, bool has_q6) {
   TvSmem L;
   size_t o = (size_t)TV_RS * TV_RAW_BYTES;
@@ -75,11 +83,14 @@ __host__ __device__ inline TvSmem tv_smem(int G, bool has_q4, bool has_q6) {
   L.bq4 = o; if (has_q4) o += (size_t)G * 8 * TV_B_Q4 + TV_B_PAD;
   o = (o + 15) & ~(size_t)15;
   L.bq6 = o; if (has_q6) o += (size_t)G * 8 * TV_B_Q6 + TV_B_PAD;
-  L.total = (o + 127) & ~(size_t)127;
+  L.total = ((o + 127) & ~(size_t)127) + 1024;
   return L;
 }
 
 struct TvSeg {
+  CUtensorMap m0;       // nibbles / ql: [R/8 tiles][8 rows][128 G bytes], box 64 x 8 x 16, 64 B swizzle
+  CUtensorMap m1;       // Q4_K headers [..][16 G] box 16 x 8 x 16; Q6_K qh [..][64 G] box 64 x 8 x 16 swizzled
+  CUtensorMap m2;       // Q6_K scales [..][16 G], box 16 x 8 x 16
   QView w;
   int tile0;            // first row tile of this segment
   int epi;
@@ -147,6 +158,20 @@ __device__ __forceinline__ void tc_ld8_nw(uint32_t taddr, int (&v)[8]) {
                : "memory");
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// TMA tensor copy of box (x, y, z) of a 3-D map into this CTA's shared memory, completing its bytes
+// on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+// Byte address of 16-byte chunk j (0..3) of row r in a box of 64-byte rows written with the 64-byte
+// swizzle (chunk bits [4, 6) XOR address bits [7, 9); the box starts 512-byte aligned).
+__device__ __forceinline__ const uint8_t* tv_sw64(const uint8_t* box, int r, int j) {
+  return box + r * 64 + 16 * (j ^ ((r >> 1) & 3));
+}
 
 // Unsigned byte k of w (the signed one is sbyte in kq_gemv.cuh).
 __device__ __forceinline__ int tv_ubyte(uint32_t w, int k) { return (int)__byte_perm(w, 0, 0x4440u | (uint32_t)k); }
@@ -342,7 +367,7 @@ __device__ __forceinline__ void tv_drain_wait(uint64_t* bar, uint32_t parity, in
 
 __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ TmvParams P) {
   extern __shared__ __align__(128) uint8_t tv_sm[];
-  uint8_t* sm = tv_sm;
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tv_sm) + 1023) & ~(uintptr_t)1023);
   const TvSmem L = tv_smem(P.G, P.has_q4 != 0, P.has_q6 != 0);
   uint8_t* raw_ring = sm;
   uint32_t* d_ring = reinterpret_cast<uint32_t*>(sm + L.d);
@@ -364,7 +389,7 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
   };
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < TV_RS; ++i) { mbar_init(&raw_full[i], TV_LD_WARPS * 32); mbar_init(&raw_empty[i], TV_DQ_WARPS); }
+    for (int i = 0; i < TV_RS; ++i) { mbar_init(&raw_full[i], 1 + 32); mbar_init(&raw_empty[i], TV_DQ_WARPS); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&a_full[i], TV_DQ_WARPS);
       mbar_init(&d_full[i], 1);
@@ -387,10 +412,9 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
   if (threadIdx.x == 0) KQ_TRACE_AT(0, 10);
 
   if (warp >= TV_DQ_WARPS && warp < TV_MMA_WARP) {
-    // ---------------- raw loaders: rows [32 lw, 32 lw + 32) of every unit; the weights do not
-    // depend on the previous kernel (no PDL wait)
-    const int lw = warp - TV_DQ_WARPS;
-    const uint64_t pol = l2_evict_first_policy();
+    // ---------------- raw loader: the weights do not depend on the previous kernel (no PDL wait).
+    // Lane 0: the unit's tensor copies (one expect_tx arrival); every lane: the Q6_K d words of 4
+    // rows by cp.async and one arrival when they land (none pending for Q4_K).
     for (int k = 0; k < n; ++k) {
       const int slot = k % TV_RS;
       if (k >= TV_RS && !tm_wait(&raw_empty[slot], (uint32_t)((k / TV_RS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
@@ -399,32 +423,25 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
       const int t = (int)(u / G), g = (int)(u % G);
       const TvSeg& S = P.seg[seg_of(t)];
       const QView& w = S.w;
-      const int row0 = (t - S.tile0) * TV_ROWS;
+      const int row0 = (t - S.tile0) * TV_ROWS, z = row0 >> 3;
       const bool q4 = w.type == Q4K;
-      const int rstride = q4 ? TV_RAW_Q4 : TV_RAW_Q6;
       uint8_t* dst = raw_ring + (size_t)slot * TV_RAW_BYTES;
-      // nibbles / ql (and Q6_K qh): 8 rows per instruction, 4 lanes per 64-byte run
-#pragma unroll
-      for (int rb = 0; rb < 4; ++rb) {
-        const int r = 32 * lw + 8 * rb + (lane >> 2), pc = lane & 3, row = row0 + r;
-        const bool ok = row < w.R;
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint8_t* src = ok ? w.base + row_plane_off(w.type, G, row, 0, (size_t)c * 64 * G + (size_t)g * 64 + pc * 16) : w.base;
-          cp_async16(dst + r * rstride + c * 64 + pc * 16, src, ok ? 16u : 0u, pol);
-        }
-        if (!q4) {
-          const uint8_t* src = ok ? w.base + row_plane_off(Q6K, G, row, 1, (size_t)g * 64 + pc * 16) : w.base;
-          cp_async16(dst + r * rstride + 128 + pc * 16, src, ok ? 16u : 0u, pol);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&raw_full[slot], q4 ? TV_TX_Q4 : TV_TX_Q6);
+        tma_load_3d(dst, &S.m0, 64 * g, 0, z, &raw_full[slot]);
+        tma_load_3d(dst + TV_ST_C1, &S.m0, 64 * G + 64 * g, 0, z, &raw_full[slot]);
+        if (q4) {
+          tma_load_3d(dst + TV_ST_HDR, &S.m1, 16 * g, 0, z, &raw_full[slot]);
+        } else {
+          tma_load_3d(dst + TV_ST_QH, &S.m1, 64 * g, 0, z, &raw_full[slot]);
+          tma_load_3d(dst + TV_ST_SC, &S.m2, 16 * g, 0, z, &raw_full[slot]);
         }
       }
-      // Q4_K header / Q6_K scales (16 B per row); Q6_K d: the aligned 4-byte word that holds it
-      {
-        const int r = 32 * lw + lane, row = row0 + r;
-        const bool ok = row < w.R;
-        const uint8_t* src = ok ? w.base + row_plane_off(w.type, G, row, q4 ? 1 : 2, (size_t)g * 16) : w.base;
-        cp_async16(dst + r * rstride + (q4 ? 128 : 192), src, ok ? 16u : 0u, pol);
-        if (!q4) {
+      if (!q4) {
+#pragma unroll
+        for (int i = 0; i < TV_ROWS / 32; ++i) {
+          const int r = 32 * i + lane, row = row0 + r;
+          const bool ok = row < w.R;
           const uintptr_t a = ok ? reinterpret_cast<uintptr_t>(w.base + row_plane_off(Q6K, G, row, 3, (size_t)g * 2))
                                  : reinterpret_cast<uintptr_t>(w.base);
           cp_async4(d_ring + slot * TV_ROWS + r, reinterpret_cast<const void*>(a & ~(uintptr_t)3), ok ? 4u : 0u);
@@ -433,6 +450,12 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
       cp_async_arrive(&raw_full[slot]);
     }
     cp_async_wait_all();
+    if (lane == 0) {
+      // drain: the tensor copies into the last stages have landed before the CTA exits
+      for (int k = n - TV_RS < 0 ? 0 : n - TV_RS; k < n; ++k)
+        tm_wait(&raw_full[k % TV_RS], (uint32_t)(k / TV_RS) & 1, P.err, KQ_DEV_ERR_DRAIN, abort_f);
+    }
+    __syncwarp();
   } else if (warp == TV_MMA_WARP) {
     // ---------------- MMA issue (one thread): unit k uses A columns [64 (k & 1), +64) and D columns
     // [128 + 128 (k & 1), +128) (group gi at 16 gi)
@@ -594,11 +617,10 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
       uint32_t cw = 0, mw = 0;
       float d0 = 0.f, d1 = 0.f;
       if (ok) {
-        const int rstride = q4 ? TV_RAW_Q4 : TV_RAW_Q6;
-        const uint8_t* rw = raw_ring + (size_t)slot * TV_RAW_BYTES + (size_t)r * rstride;
+        const uint8_t* st = raw_ring + (size_t)slot * TV_RAW_BYTES;
         const uint32_t ta = tl + 64u * (uint32_t)(k & 1) + 32u * (uint32_t)hh;
         if (q4) {
-          const uint4 H = lds128(rw + 128);
+          const uint4 H = lds128(st + TV_ST_HDR + 16 * r);
           d0 = h2f_bits(H.x & 0xFFFFu);
           d1 = h2f_bits(H.x >> 16);
           cw = hh ? ((H.w & 0x0F0F0F0Fu) | ((H.y >> 2) & 0x30303030u)) : (H.y & 0x3F3F3F3Fu);          // scales
@@ -606,8 +628,8 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             // the 32 bytes of (hh, c): low nibbles = sub-block 4hh + 2c, high = 4hh + 2c + 1
-            const uint8_t* b = rw + c * 64 + hh * 32;
-            const uint4 W0 = lds128(b), W1 = lds128(b + 16);
+            const uint8_t* b = st + c * TV_ST_C1;
+            const uint4 W0 = lds128(tv_sw64(b, r, 2 * hh)), W1 = lds128(tv_sw64(b, r, 2 * hh + 1));
             const uint32_t wd[8] = {W0.x, W0.y, W0.z, W0.w, W1.x, W1.y, W1.z, W1.w};
             uint32_t lo[8], hi[8];
 #pragma unroll
@@ -616,18 +638,17 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
             tc_st8(ta + 16u * c + 8u, hi);
           }
         } else {
-          const uint2 Sc = *reinterpret_cast<const uint2*>(rw + 192 + 8 * hh);   // scale words 2hh, 2hh + 1
+          const uint2 Sc = *reinterpret_cast<const uint2*>(st + TV_ST_SC + 16 * r + 8 * hh);   // scale words 2hh, 2hh + 1
           cw = Sc.x;
           mw = Sc.y;
           const uint32_t dw = d_ring[slot * TV_ROWS + r];
           d0 = h2f_bits(((r & 7) * G + g) & 1 ? dw >> 16 : dw & 0xFFFFu);
-          const uint8_t* hq = rw + 128 + hh * 32;
-          const uint4 H0 = lds128(hq), H1 = lds128(hq + 16);
+          const uint4 H0 = lds128(tv_sw64(st + TV_ST_QH, r, 2 * hh)), H1 = lds128(tv_sw64(st + TV_ST_QH, r, 2 * hh + 1));
           const uint32_t qh[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
 #pragma unroll
           for (int m = 0; m < 2; ++m) {
-            const uint8_t* lq = rw + m * 64 + hh * 32;
-            const uint4 L0 = lds128(lq), L1 = lds128(lq + 16);
+            const uint8_t* lq = st + m * TV_ST_C1;
+            const uint4 L0 = lds128(tv_sw64(lq, r, 2 * hh)), L1 = lds128(tv_sw64(lq, r, 2 * hh + 1));
             const uint32_t ql[8] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w};
 #pragma unroll
             for (int nib = 0; nib < 2; ++nib) {
