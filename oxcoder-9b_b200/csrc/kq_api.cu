@@ -17,7 +17,6 @@
 #include "kq_nccl.h"
 
 #include <cuda_runtime.h>
-#include <cudaTypedefs.h>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -120,9 +119,11 @@ struct kq_qmat {
   size_t bytes = 0;
   float* tv_part = nullptr; // split-K scratch of the tensor-core GEMV (matvec calls), lazily
   int* tv_ticket = nullptr;
+  bool tvon = false;        // keep the unit-major copy of the tensor-core GEMV
+  uint8_t* tvbuf = nullptr; // that copy (kq_tmv.cuh), rebuilt by every write
   QView view() const {
     QView v;
-    v.base = buf; v.type = type; v.R = R; v.C = C; v.G = G;
+    v.base = buf; v.type = type; v.R = R; v.C = C; v.G = G; v.tv = tvbuf;
     return v;
   }
   QViewW wview() {
@@ -156,7 +157,25 @@ static kq_qmat* qmat_alloc(int type, int R, int C, int device) {
     set_err(KQ_ERR_MEMORY, "device allocation of a quantised matrix failed");
     return nullptr;
   }
+  a->tvon = g_dev[device].tmv_smem > 0 && a->G <= TV_MAX_G;
   return a;
+}
+
+// The unit-major copy of the tensor-core GEMV, (re)built from the tile layout on stream s.
+static int qmat_tv_build(kq_qmat* a, cudaStream_t s) {
+  if (!a->tvon) return KQ_OK;
+  const long long ntiles = (a->R + TV_ROWS - 1) / TV_ROWS, nthr = ntiles * a->G * TV_ROWS;
+  if (!a->tvbuf) {
+    const size_t ub = a->type == Q4K ? TV_UNIT_Q4 : TV_UNIT_Q6;
+    if (cudaMalloc(&a->tvbuf, (size_t)ntiles * a->G * ub) != cudaSuccess) {
+      a->tvon = false;   // the tile layout alone still serves every kernel
+      cudaGetLastError();
+      return KQ_OK;
+    }
+  }
+  k_tv_repack<<<(unsigned)((nthr + 255) / 256), 256, 0, s>>>(a->view(), a->tvbuf);
+  CU(cudaGetLastError());
+  return KQ_OK;
 }
 
 static int qmat_write(kq_qmat* a, int R_src, const uint8_t* src_dev, uint64_t base, int mode, int arg, cudaStream_t s,
@@ -166,7 +185,7 @@ static int qmat_write(kq_qmat* a, int R_src, const uint8_t* src_dev, uint64_t ba
   if (sh.G_src == 0) sh.G_src = a->G;
   k_qmat_write<<<(unsigned)((n + thr - 1) / thr), thr, 0, s>>>(a->wview(), R_src, src_dev, base, mode, arg, sh);
   CU(cudaGetLastError());
-  return KQ_OK;
+  return qmat_tv_build(a, s);
 }
 
 static int qmat_upload_mapped(kq_qmat* a, const void* host, size_t bytes, int R_src, int mode, int arg, cudaStream_t s) {
@@ -538,10 +557,10 @@ static void model_release(kq_model* m) {
   for (auto& l : m->L) {
     kq_qmat* ms[] = {l.q, l.k, l.v, l.o, l.gu, l.down};
     for (kq_qmat* a : ms)
-      if (a) { cudaFree(a->buf); delete a; }
+      if (a) { cudaFree(a->buf); cudaFree(a->tvbuf); delete a; }
   }
   for (kq_qmat* a : {m->emb, m->out})
-    if (a) { cudaFree(a->buf); delete a; }
+    if (a) { cudaFree(a->buf); cudaFree(a->tvbuf); delete a; }
   for (void* p : m->allocs) cudaFree(p);
   if (m->st_host) cudaFreeHost(m->st_host);
   if (m->vstates) cudaFreeHost(m->vstates);
@@ -622,6 +641,7 @@ static kq_model* model_create(const kq_config* cfg, int device, int rank, int wo
     m->emb = qmat_alloc(c.t_emb, c.vocab, c.dim, device);
     m->out = qmat_alloc(c.t_out, m->vocab_l, c.dim, device);
     if (!m->emb || !m->out) ok = false;
+    else m->emb->tvon = m->out->tvon = false;   // the embedding and the head run on k_gemv
   }
   if (ok && world > 1) {
     m->tp_val = dalloc<float>(m, (size_t)(world + 1) * MM_MAXM, ok);   // gathered rows + this rank's
@@ -875,47 +895,6 @@ struct StepOp {
 // floats and `ticket` TV_MAX_TILES ints (zero). False when the launch is not covered (embedding
 // prologue, argmax epilogue, more than TV_MAX_G super-blocks per row, shared memory) or the
 // tensor-core GEMV is off: k_gemv runs it.
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
-static PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-// 3-D byte map over one plane of the kq tile layout: [R/8 tiles (stride tile_bytes)][8 rows
-// (stride `inner`)][inner bytes], box `box0` x 8 x 16 (128 rows), zero fill past the last tile.
-static bool tv_encode(CUtensorMap* m, const uint8_t* base, uint64_t inner, uint64_t tiles, uint64_t tb, uint32_t box0,
-                      bool sw64) {
-  PFN_cuTensorMapEncodeTiled_v12000 fn = tmap_encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[3] = {inner, 8, tiles};
-  const cuuint64_t strides[2] = {inner, tb};
-  const cuuint32_t box[3] = {box0, 8, 16};
-  const cuuint32_t es[3] = {1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, sw64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
-            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-// The maps of one segment (kq_tmv.cuh TvSeg).
-static bool tv_seg_maps(TvSeg& S) {
-  const QView& w = S.w;
-  const uint64_t G = (uint64_t)w.G, tiles = (uint64_t)w.R / 8, tb = tile_bytes(w.type, w.G);
-  if (!tv_encode(&S.m0, w.base, 128 * G, tiles, tb, 64, true)) return false;
-  if (w.type == Q4K) {
-    if (!tv_encode(&S.m1, w.base + tile_plane_off(Q4K, w.G, 1), 16 * G, tiles, tb, 16, false)) return false;
-    S.m2 = S.m1;
-    return true;
-  }
-  return tv_encode(&S.m1, w.base + tile_plane_off(Q6K, w.G, 1), 64 * G, tiles, tb, 64, true) &&
-         tv_encode(&S.m2, w.base + tile_plane_off(Q6K, w.G, 2), 16 * G, tiles, tb, 16, false);
-}
-
 static bool tmv_plan(const GemvParams& g, int nsm, size_t smem_max, float* part, int* ticket, TmvParams& T, dim3& grid) {
   if (smem_max == 0 || g.nseg < 1 || g.nseg > TV_MAX_SEG || g.G > TV_MAX_G) return false;
   if (g.xmode != XS_PLAIN && g.xmode != XS_NORM) return false;
@@ -923,13 +902,12 @@ static bool tmv_plan(const GemvParams& g, int nsm, size_t smem_max, float* part,
   int ntiles = 0;
   for (int i = 0; i < g.nseg; ++i) {
     const Seg& sg = g.seg[i];
-    if (sg.epi == EPI_ARGMAX || sg.w.G != g.G) return false;
+    if (sg.epi == EPI_ARGMAX || sg.w.G != g.G || !sg.w.tv) return false;
     T.seg[i].w = sg.w;
     T.seg[i].tile0 = ntiles;
     T.seg[i].epi = sg.epi;
     T.seg[i].out_f = sg.out_f;
     T.seg[i].out_h = sg.out_h;
-    if (!tv_seg_maps(T.seg[i])) return false;
     ntiles += (sg.w.R + TV_ROWS - 1) / TV_ROWS;
     if (sg.w.type == Q4K) T.has_q4 = 1;
     else T.has_q6 = 1;
@@ -1995,6 +1973,7 @@ extern "C" void kq_qmat_free(kq_qmat* a) {
   if (!a) return;
   cudaSetDevice(a->device);
   cudaFree(a->buf);
+  cudaFree(a->tvbuf);
   cudaFree(a->tv_part);
   cudaFree(a->tv_ticket);
   delete a;

@@ -25,6 +25,7 @@ constexpr int Q4K = 12, Q6K = 14;
 struct QView {
   const uint8_t* base;   // R/8 tiles
   int type, R, C, G;
+  const uint8_t* tv;     // the unit-major copy of the tensor-core GEMV (kq_tmv.cuh), or null
 };
 
 __host__ __device__ inline int block_bytes(int type) { return type == Q4K ? 144 : 210; }

@@ -10,9 +10,9 @@
 // int8 digit planes, x = s3 * (16384 x1 + 128 x2 + x3) (s3 a power of two per super-block). The
 // weights enter the MMA as their raw unsigned digits: Q4_K low nibbles as bytes q (w & 0x0F0F0F0F),
 // high nibbles in place as 16 q (w & 0xF0F0F0F0), Q6_K as the 6-bit q. One MMA per 32-column
-// group (K = 32, M = 128 rows, N = 16, the smallest N of an M = 128 MMA): its B operand is the
-// group's three planes (rows 0-2 of the 16-row B tile; the other rows are don't-care, read from
-// whatever follows in shared memory), so D columns 0-2 are the exact int32 dot products of the
+// group (K = 32, M = 128 rows, N = 8): its B operand is the group's three planes (rows 0-2 of the
+// 8-row B tile; the other rows are don't-care, read from whatever follows in shared memory), so
+// D columns 0-2 are the exact int32 dot products of the
 // group's weight digits with each plane (for Q6_K, whose scale blocks are 16 columns, the B tile
 // holds the first 16 columns' planes in rows 0-2 and the last 16's in rows 3-5, zero elsewhere).
 // The thread owning the row then applies the integer sub-block scales in int32 (exact: |sum| <
@@ -26,16 +26,25 @@
 //   warps 0-7   thread (row r = 32 (warp & 3) + lane, half hh = warp >> 2 of the super-block):
 //               prologue (activation digits -> B tiles), then per unit its A digits to tensor
 //               memory and the read-back of the previous unit's D; tile flushes and epilogues
-//   warp 8      raw loader: lane 0 issues the unit's TMA tensor copies (3-D maps over the planes of
-//               the kq tile layout: 64-byte rows of the nibble / qh planes with the 64-byte swizzle,
-//               conflict-free for 8 consecutive rows; 16-byte rows of the header / scale planes),
-//               all lanes the Q6_K d words (cp.async)
+//   warp 8      raw loader: lane 0 issues one bulk copy per unit from the matrix's unit-major copy
+//               (see below)
 //   warp 9      TMEM allocation (512 columns: A digits of two units in [0, 128), two D regions of
-//               8 groups x 16 columns in [128, 384)); lane 0 issues the 8 MMAs of each unit
+//               8 groups x 8 columns at 128 and 256); lane 0 issues the 8 MMAs of each unit
 // Every wait is bounded; on a timeout the CTA records the error, skips the remaining work (every
 // thread still takes the same barriers) and drains before it exits.
+//
+// Unit-major weight copy. In the kq tile layout a unit's bytes are 512 pieces of 16-64 B (each
+// row's chunks of the super-block, rows 2 KB apart), which the copy engines move at ~16 GB/s per
+// SM. Each matrix the decode step multiplies therefore also keeps a second copy (HBM holds both
+// easily: the decode weights are ~4 GB of 180) in which every unit is stored exactly as its
+// shared-memory stage image, so one 18-27 KB bulk copy moves it:
+//   Q4_K (18432 B): [0, 8192) nibble chunk c = 0 as 128 rows x 64 B, [8192, 16384) c = 1, the 16-byte
+//                   chunks of row r at position j ^ ((r >> 1) & 3) (conflict-free 16-byte reads by 8
+//                   consecutive rows); [16384, 18432) block headers, 16 B per row
+//   Q6_K (26880 B): [0, 16384) ql as above, [16384, 24576) qh (64 B per row, same chunk order),
+//                   [24576, 26624) scales (16 B per row), [26624, 26880) d (2 B per row)
+// Rows past the matrix are zero. k_tv_repack builds it from the tile layout.
 #pragma once
-#include <cuda.h>
 #include "kq_common.cuh"
 #include "kq_qformat.cuh"
 #include "kq_gemv.cuh"
@@ -53,27 +62,24 @@ constexpr int TV_MAX_G = 48;                                      // super-block
 constexpr int TV_MAX_SEG = 3;
 constexpr int TV_MAX_TILES = 4096;                                // row tiles per launch, at most
 constexpr uint32_t TV_TMEM_COLS = 512;
-constexpr int TV_MMA_N = 16;                                      // D columns per group
+constexpr int TV_MMA_N = 8;                                       // D columns per group (the MMA's N)
 constexpr int TV_B_Q4 = 96, TV_B_Q6 = 144;                        // B bytes per 32-column group
 constexpr int TV_B_PAD = 320;                                     // the 16-row B tile's don't-care rows
-// One raw stage (1024-byte aligned): [0, 8192) nibbles / ql of plane chunk c = 0 (128 rows x 64 B,
-// 64-byte swizzle), [8192, 16384) c = 1, then Q4_K: [16384, 18432) headers (128 x 16 B); Q6_K:
-// [16384, 24576) qh (128 x 64 B, swizzled), [24576, 26624) scales (128 x 16 B).
-constexpr int TV_ST_C1 = 8192, TV_ST_HDR = 16384, TV_ST_QH = 16384, TV_ST_SC = 24576;
-constexpr uint32_t TV_TX_Q4 = 18432, TV_TX_Q6 = 26624;
-constexpr size_t TV_RAW_BYTES = 26624;
+// Offsets inside a unit's stage image (see the unit-major copy above).
+constexpr int TV_ST_C1 = 8192, TV_ST_HDR = 16384, TV_ST_QH = 16384, TV_ST_SC = 24576, TV_ST_D = 26624;
+constexpr uint32_t TV_UNIT_Q4 = 18432, TV_UNIT_Q6 = 26880;
+constexpr size_t TV_RAW_BYTES = TV_UNIT_Q6;                        // one ring stage (a multiple of 128 B)
 
 // Dynamic shared memory, identical on host (sizing) and device: raw ring, Q6_K d words, s3[G],
 // X32[G][8], C16[G][16] (int4), red[128], the Q4_K-layout B tiles (if any Q4_K segment), the
 // Q6_K-layout B tiles (if any Q6_K segment).
 struct TvSmem {
-  size_t d, s3, x32, c16, red, bq4, bq6, total;
+  size_t s3, x32, c16, red, bq4, bq6, total;
 };
 // (offsets from the 1024-byte aligned start; the launch adds 1024 bytes of alignment slack)
 __host__ __device__ inline TvSmem tv_smem(int G, bool has_q4, bool has_q6) {
   TvSmem L;
   size_t o = (size_t)TV_RS * TV_RAW_BYTES;
-  L.d = o; o += (size_t)TV_RS * TV_ROWS * 4;
   L.s3 = o; o += (size_t)G * 4;
   o = (o + 15) & ~(size_t)15;
   L.x32 = o; o += (size_t)G * 8 * 4;
@@ -88,10 +94,7 @@ __host__ __device__ inline TvSmem tv_smem(int G, bool has_q4, bool has_q6) {
 }
 
 struct TvSeg {
-  CUtensorMap m0;       // nibbles / ql: [R/8 tiles][8 rows][128 G bytes], box 64 x 8 x 16, 64 B swizzle
-  CUtensorMap m1;       // Q4_K headers [..][16 G] box 16 x 8 x 16; Q6_K qh [..][64 G] box 64 x 8 x 16 swizzled
-  CUtensorMap m2;       // Q6_K scales [..][16 G], box 16 x 8 x 16
-  QView w;
+  QView w;              // w.tv: the unit-major copy
   int tile0;            // first row tile of this segment
   int epi;
   float* out_f;
@@ -124,9 +127,9 @@ struct TmvParams {
 __host__ __device__ constexpr uint32_t tc_idesc_i8(int M, int N) {
   return (2u << 4) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-// Shared-memory descriptor of a 16-row B tile, K-major without swizzle: 8-row groups of 16-byte
-// rows per K half (rows contiguous), the second K half `lbo` bytes after the first, the second
-// 8-row group (don't-care rows here) 128 bytes after the first. Version 1 at bit 46, layout 0.
+// Shared-memory descriptor of an 8-row B tile, K-major without swizzle: 16-byte rows per K half
+// (rows contiguous), the second K half `lbo` bytes after the first; the stride between 8-row
+// groups (unused at N = 8) set to 128. Version 1 at bit 46, layout 0.
 __device__ __forceinline__ uint64_t tv_bdesc(uint32_t saddr, uint32_t lbo) {
   return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(128 >> 4) << 32) |
          ((uint64_t)1 << 46);
@@ -159,18 +162,37 @@ __device__ __forceinline__ void tc_ld8_nw(uint32_t taddr, int (&v)[8]) {
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// TMA tensor copy of box (x, y, z) of a 3-D map into this CTA's shared memory, completing its bytes
-// on `bar` (no multicast).
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-      : "memory");
-}
-// Byte address of 16-byte chunk j (0..3) of row r in a box of 64-byte rows written with the 64-byte
-// swizzle (chunk bits [4, 6) XOR address bits [7, 9); the box starts 512-byte aligned).
-__device__ __forceinline__ const uint8_t* tv_sw64(const uint8_t* box, int r, int j) {
-  return box + r * 64 + 16 * (j ^ ((r >> 1) & 3));
+// Byte offset of 16-byte chunk j (0..3) of row r in a part of 64-byte rows of a stage image.
+__host__ __device__ __forceinline__ int tv_sw64(int r, int j) { return r * 64 + 16 * (j ^ ((r >> 1) & 3)); }
+
+// kq tile layout -> unit-major copy: one thread per (unit, row).
+__global__ void __launch_bounds__(256) k_tv_repack(const QView w, uint8_t* tv) {
+  const int G = w.G, ntiles = (w.R + TV_ROWS - 1) / TV_ROWS;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)ntiles * G * TV_ROWS) return;
+  const int r = (int)(i % TV_ROWS);
+  const long long unit = i / TV_ROWS;
+  const int g = (int)(unit % G), t = (int)(unit / G), row = t * TV_ROWS + r;
+  const bool ok = row < w.R, q4 = w.type == Q4K;
+  uint8_t* dst = tv + (size_t)unit * (q4 ? TV_UNIT_Q4 : TV_UNIT_Q6);
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  auto ld16 = [&](int plane, size_t off) -> uint4 {
+    return ok ? *reinterpret_cast<const uint4*>(w.base + row_plane_off(w.type, G, row, plane, off)) : z;
+  };
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4*>(dst + c * TV_ST_C1 + tv_sw64(r, j)) = ld16(0, (size_t)c * 64 * G + (size_t)g * 64 + 16 * j);
+  if (q4) {
+    *reinterpret_cast<uint4*>(dst + TV_ST_HDR + 16 * r) = ld16(1, (size_t)g * 16);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(dst + TV_ST_QH + tv_sw64(r, j)) = ld16(1, (size_t)g * 64 + 16 * j);
+    *reinterpret_cast<uint4*>(dst + TV_ST_SC + 16 * r) = ld16(2, (size_t)g * 16);
+    *reinterpret_cast<uint16_t*>(dst + TV_ST_D + 2 * r) =
+        ok ? *reinterpret_cast<const uint16_t*>(w.base + row_plane_off(Q6K, G, row, 3, (size_t)g * 2)) : (uint16_t)0;
+  }
 }
 
 // Unsigned byte k of w (the signed one is sbyte in kq_gemv.cuh).
@@ -370,7 +392,6 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tv_sm) + 1023) & ~(uintptr_t)1023);
   const TvSmem L = tv_smem(P.G, P.has_q4 != 0, P.has_q6 != 0);
   uint8_t* raw_ring = sm;
-  uint32_t* d_ring = reinterpret_cast<uint32_t*>(sm + L.d);
   __shared__ __align__(8) uint64_t raw_full[TV_RS], raw_empty[TV_RS], a_full[2], d_full[2], d_free[2], b_ready, mma_done;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_last;
@@ -389,7 +410,7 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
   };
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < TV_RS; ++i) { mbar_init(&raw_full[i], 1 + 32); mbar_init(&raw_empty[i], TV_DQ_WARPS); }
+    for (int i = 0; i < TV_RS; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], TV_DQ_WARPS); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&a_full[i], TV_DQ_WARPS);
       mbar_init(&d_full[i], 1);
@@ -412,48 +433,25 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
   if (threadIdx.x == 0) KQ_TRACE_AT(0, 10);
 
   if (warp >= TV_DQ_WARPS && warp < TV_MMA_WARP) {
-    // ---------------- raw loader: the weights do not depend on the previous kernel (no PDL wait).
-    // Lane 0: the unit's tensor copies (one expect_tx arrival); every lane: the Q6_K d words of 4
-    // rows by cp.async and one arrival when they land (none pending for Q4_K).
-    for (int k = 0; k < n; ++k) {
-      const int slot = k % TV_RS;
-      if (k >= TV_RS && !tm_wait(&raw_empty[slot], (uint32_t)((k / TV_RS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
-        break;
-      const long long u = u0 + k;
-      const int t = (int)(u / G), g = (int)(u % G);
-      const TvSeg& S = P.seg[seg_of(t)];
-      const QView& w = S.w;
-      const int row0 = (t - S.tile0) * TV_ROWS, z = row0 >> 3;
-      const bool q4 = w.type == Q4K;
-      uint8_t* dst = raw_ring + (size_t)slot * TV_RAW_BYTES;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&raw_full[slot], q4 ? TV_TX_Q4 : TV_TX_Q6);
-        tma_load_3d(dst, &S.m0, 64 * g, 0, z, &raw_full[slot]);
-        tma_load_3d(dst + TV_ST_C1, &S.m0, 64 * G + 64 * g, 0, z, &raw_full[slot]);
-        if (q4) {
-          tma_load_3d(dst + TV_ST_HDR, &S.m1, 16 * g, 0, z, &raw_full[slot]);
-        } else {
-          tma_load_3d(dst + TV_ST_QH, &S.m1, 64 * g, 0, z, &raw_full[slot]);
-          tma_load_3d(dst + TV_ST_SC, &S.m2, 16 * g, 0, z, &raw_full[slot]);
-        }
-      }
-      if (!q4) {
-#pragma unroll
-        for (int i = 0; i < TV_ROWS / 32; ++i) {
-          const int r = 32 * i + lane, row = row0 + r;
-          const bool ok = row < w.R;
-          const uintptr_t a = ok ? reinterpret_cast<uintptr_t>(w.base + row_plane_off(Q6K, G, row, 3, (size_t)g * 2))
-                                 : reinterpret_cast<uintptr_t>(w.base);
-          cp_async4(d_ring + slot * TV_ROWS + r, reinterpret_cast<const void*>(a & ~(uintptr_t)3), ok ? 4u : 0u);
-        }
-      }
-      cp_async_arrive(&raw_full[slot]);
-    }
-    cp_async_wait_all();
+    // ---------------- raw loader (lane 0): one bulk copy per unit from the unit-major copy; the
+    // weights do not depend on the previous kernel (no PDL wait)
     if (lane == 0) {
-      // drain: the tensor copies into the last stages have landed before the CTA exits
-      for (int k = n - TV_RS < 0 ? 0 : n - TV_RS; k < n; ++k)
-        tm_wait(&raw_full[k % TV_RS], (uint32_t)(k / TV_RS) & 1, P.err, KQ_DEV_ERR_DRAIN, abort_f);
+      const uint64_t pol = l2_evict_first_policy();
+      int k = 0;
+      for (; k < n; ++k) {
+        const int slot = k % TV_RS;
+        if (k >= TV_RS && !tm_wait(&raw_empty[slot], (uint32_t)((k / TV_RS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
+          break;
+        const long long u = u0 + k;
+        const int t = (int)(u / G), g = (int)(u % G);
+        const TvSeg& S = P.seg[seg_of(t)];
+        const uint32_t ub = S.w.type == Q4K ? TV_UNIT_Q4 : TV_UNIT_Q6;
+        mbar_arrive_expect_tx(&raw_full[slot], ub);
+        bulk_g2s(raw_ring + (size_t)slot * TV_RAW_BYTES, S.w.tv + ((size_t)(t - S.tile0) * G + g) * ub, ub, &raw_full[slot], pol);
+      }
+      // drain: the copies into the last stages have landed before the CTA exits
+      for (int j = k - TV_RS < 0 ? 0 : k - TV_RS; j < k; ++j)
+        tm_wait(&raw_full[j % TV_RS], (uint32_t)(j / TV_RS) & 1, P.err, KQ_DEV_ERR_DRAIN, abort_f);
     }
     __syncwarp();
   } else if (warp == TV_MMA_WARP) {
@@ -629,7 +627,7 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
           for (int c = 0; c < 2; ++c) {
             // the 32 bytes of (hh, c): low nibbles = sub-block 4hh + 2c, high = 4hh + 2c + 1
             const uint8_t* b = st + c * TV_ST_C1;
-            const uint4 W0 = lds128(tv_sw64(b, r, 2 * hh)), W1 = lds128(tv_sw64(b, r, 2 * hh + 1));
+            const uint4 W0 = lds128(b + tv_sw64(r, 2 * hh)), W1 = lds128(b + tv_sw64(r, 2 * hh + 1));
             const uint32_t wd[8] = {W0.x, W0.y, W0.z, W0.w, W1.x, W1.y, W1.z, W1.w};
             uint32_t lo[8], hi[8];
 #pragma unroll
@@ -641,14 +639,13 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
           const uint2 Sc = *reinterpret_cast<const uint2*>(st + TV_ST_SC + 16 * r + 8 * hh);   // scale words 2hh, 2hh + 1
           cw = Sc.x;
           mw = Sc.y;
-          const uint32_t dw = d_ring[slot * TV_ROWS + r];
-          d0 = h2f_bits(((r & 7) * G + g) & 1 ? dw >> 16 : dw & 0xFFFFu);
-          const uint4 H0 = lds128(tv_sw64(st + TV_ST_QH, r, 2 * hh)), H1 = lds128(tv_sw64(st + TV_ST_QH, r, 2 * hh + 1));
+          d0 = h2f_bits(*reinterpret_cast<const uint16_t*>(st + TV_ST_D + 2 * r));
+          const uint4 H0 = lds128(st + TV_ST_QH + tv_sw64(r, 2 * hh)), H1 = lds128(st + TV_ST_QH + tv_sw64(r, 2 * hh + 1));
           const uint32_t qh[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
 #pragma unroll
           for (int m = 0; m < 2; ++m) {
             const uint8_t* lq = st + m * TV_ST_C1;
-            const uint4 L0 = lds128(tv_sw64(lq, r, 2 * hh)), L1 = lds128(tv_sw64(lq, r, 2 * hh + 1));
+            const uint4 L0 = lds128(lq + tv_sw64(r, 2 * hh)), L1 = lds128(lq + tv_sw64(r, 2 * hh + 1));
             const uint32_t ql[8] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w};
 #pragma unroll
             for (int nib = 0; nib < 2; ++nib) {
