@@ -53,10 +53,14 @@
 namespace kq {
 
 constexpr int TV_ROWS = 128;
-constexpr int TV_DQ_WARPS = 8;
-constexpr int TV_LD_WARPS = 1;
-constexpr int TV_MMA_WARP = TV_DQ_WARPS + TV_LD_WARPS;
+constexpr int TV_DQ_WARPS = 8;                                    // A-digit writers
+constexpr int TV_RO_WARPS = 4;                                    // D read-back, prologue, epilogues
+constexpr int TV_LD_WARP = TV_DQ_WARPS + TV_RO_WARPS;             // raw loader
+constexpr int TV_MMA_WARP = TV_LD_WARP + 1;                       // TMEM allocation, MMA issue
 constexpr int TV_THREADS = (TV_MMA_WARP + 1) * 32;
+constexpr int TV_AS = 4;                                          // A slots (64 columns each)
+constexpr int TV_DS = 4;                                          // D slots (64 columns each)
+constexpr int TV_HS = TV_AS + TV_DS;                              // header slots
 constexpr int TV_RS = 5;                                          // raw unit stages
 constexpr int TV_MAX_G = 48;                                      // super-blocks per row, at most
 constexpr int TV_MAX_SEG = 3;
@@ -70,11 +74,12 @@ constexpr int TV_ST_C1 = 8192, TV_ST_HDR = 16384, TV_ST_QH = 16384, TV_ST_SC = 2
 constexpr uint32_t TV_UNIT_Q4 = 18432, TV_UNIT_Q6 = 26880;
 constexpr size_t TV_RAW_BYTES = TV_UNIT_Q6;                        // one ring stage (a multiple of 128 B)
 
-// Dynamic shared memory, identical on host (sizing) and device: raw ring, Q6_K d words, s3[G],
-// X32[G][8], C16[G][16] (int4), red[128], the Q4_K-layout B tiles (if any Q4_K segment), the
+// Dynamic shared memory, identical on host (sizing) and device: raw ring, s3[G], X32[G][8],
+// C16[G][16] (int4), red[128], per-unit row headers hdr[TV_HS][128] (Q4_K block header / Q6_K
+// scale words) and hdrd[TV_HS][128] (Q6_K d), the Q4_K-layout B tiles (if any Q4_K segment), the
 // Q6_K-layout B tiles (if any Q6_K segment).
 struct TvSmem {
-  size_t s3, x32, c16, red, bq4, bq6, total;
+  size_t s3, x32, c16, red, hdr, hdrd, bq4, bq6, total;
 };
 // (offsets from the 1024-byte aligned start; the launch adds 1024 bytes of alignment slack)
 __host__ __device__ inline TvSmem tv_smem(int G, bool has_q4, bool has_q6) {
@@ -86,6 +91,9 @@ __host__ __device__ inline TvSmem tv_smem(int G, bool has_q4, bool has_q6) {
   o = (o + 15) & ~(size_t)15;
   L.c16 = o; o += (size_t)G * 16 * 16;
   L.red = o; o += (size_t)TV_ROWS * 4;
+  o = (o + 15) & ~(size_t)15;
+  L.hdr = o; o += (size_t)TV_HS * TV_ROWS * 16;
+  L.hdrd = o; o += (size_t)TV_HS * TV_ROWS * 4;
   L.bq4 = o; if (has_q4) o += (size_t)G * 8 * TV_B_Q4 + TV_B_PAD;
   o = (o + 15) & ~(size_t)15;
   L.bq6 = o; if (has_q6) o += (size_t)G * 8 * TV_B_Q6 + TV_B_PAD;
@@ -161,6 +169,18 @@ __device__ __forceinline__ void tc_ld8_nw(uint32_t taddr, int (&v)[8]) {
                : "memory");
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 32 consecutive 32-bit columns of this thread's TMEM lane; not waited (tc_wait_ld).
+__device__ __forceinline__ void tc_ld32_nw(uint32_t taddr, int (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,"
+      "%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
 
 // Byte offset of 16-byte chunk j (0..3) of row r in a part of 64-byte rows of a stage image.
 __host__ __device__ __forceinline__ int tv_sw64(int r, int j) { return r * 64 + 16 * (j ^ ((r >> 1) & 3)); }
@@ -209,9 +229,10 @@ __host__ __device__ inline int tv_cta_of(long long u, int n, long long U) { retu
 // XS_NORM: residual add and RMS norm over all C columns first (q4_rms q4.cu:39-46; fp64 sum of
 // squares), CTA 0 writing the residual sum to h_out. The digit split is k_gemv's, per super-block:
 // s1 = 2^e with max |x| <= 127 s1, s2 = s1 / 128, s3 = s1 / 16384.
-__device__ __forceinline__ void tv_prologue(const TmvParams& P, uint8_t* sm, const TvSmem& L, double* redd) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int NT = TV_DQ_WARPS * 32;
+// Run by the NT threads tid = 0 .. NT - 1 of warps whose first is warp w0 (named barrier 2).
+template <int NT>
+__device__ __forceinline__ void tv_prologue(const TmvParams& P, uint8_t* sm, const TvSmem& L, double* redd, int tid) {
+  const int lane = tid & 31, warp = tid >> 5;
   const int C = 256 * P.G;
   float ns = 1.f;
   if (P.xmode == XS_NORM) {
@@ -238,7 +259,7 @@ __device__ __forceinline__ void tv_prologue(const TmvParams& P, uint8_t* sm, con
     if (lane == 0) redd[warp] = acc;
     named_bar(2, NT);
     double tot = 0.0;
-    for (int w = 0; w < TV_DQ_WARPS; ++w) tot += redd[w];
+    for (int w = 0; w < NT / 32; ++w) tot += redd[w];
     ns = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / (double)C), P.eps)));
   }
   uint8_t* bq4 = sm + L.bq4;
@@ -376,6 +397,27 @@ __device__ __forceinline__ void tv_epilogue(const TmvParams& P, const TvSeg& S, 
   }
 }
 
+// Bounded wait of the roles off the MMA thread's critical path: between probes the thread sleeps
+// `ns`, so waiting warps leave the issue slots of their SM sub-partition to the MMA thread (which
+// shares one with them). Gives up after TM_WAIT_NS, or at once when another role flagged a failure.
+__device__ __forceinline__ bool tv_wait(uint64_t* bar, uint32_t parity, int* err, int bit, volatile int* abort_f, unsigned ns) {
+  if (mbar_test_wait(bar, parity)) return true;
+  uint64_t t0 = 0;
+  for (uint32_t it = 0; it < KQ_WAIT_LIMIT; ++it) {
+    __nanosleep(ns);
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((it & 63) == 63) {
+      if (*abort_f) return false;
+      const uint64_t now = tm_clock_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > TM_WAIT_NS) break;
+    }
+  }
+  atomicOr(err, bit);
+  *abort_f = 1;
+  return false;
+}
+
 // Bounded wait that ignores the abort flag: the final drain of the CTA's own MMAs, which finish
 // on their own.
 __device__ __forceinline__ void tv_drain_wait(uint64_t* bar, uint32_t parity, int* err) {
@@ -392,10 +434,13 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tv_sm) + 1023) & ~(uintptr_t)1023);
   const TvSmem L = tv_smem(P.G, P.has_q4 != 0, P.has_q6 != 0);
   uint8_t* raw_ring = sm;
-  __shared__ __align__(8) uint64_t raw_full[TV_RS], raw_empty[TV_RS], a_full[2], d_full[2], d_free[2], b_ready, mma_done;
+  uint4* hdr = reinterpret_cast<uint4*>(sm + L.hdr);         // [TV_HS][128]
+  uint32_t* hdrd = reinterpret_cast<uint32_t*>(sm + L.hdrd);  // [TV_HS][128]
+  __shared__ __align__(8) uint64_t raw_full[TV_RS], raw_empty[TV_RS], a_full[TV_AS], a_free[TV_AS], d_full[TV_DS],
+      d_free[TV_DS], h_full[TV_HS], b_ready, mma_done;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_last;
-  __shared__ double s_redd[TV_DQ_WARPS];
+  __shared__ double s_redd[TV_DQ_WARPS + TV_RO_WARPS];
   volatile int* abort_f = &s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -411,11 +456,9 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < TV_RS; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], TV_DQ_WARPS); }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&a_full[i], TV_DQ_WARPS);
-      mbar_init(&d_full[i], 1);
-      mbar_init(&d_free[i], TV_DQ_WARPS);
-    }
+    for (int i = 0; i < TV_AS; ++i) { mbar_init(&a_full[i], TV_DQ_WARPS); mbar_init(&a_free[i], 1); }
+    for (int i = 0; i < TV_DS; ++i) { mbar_init(&d_full[i], 1); mbar_init(&d_free[i], TV_RO_WARPS); }
+    for (int i = 0; i < TV_HS; ++i) mbar_init(&h_full[i], 1);
     mbar_init(&b_ready, 1);
     mbar_init(&mma_done, 1);
     s_abort = 0;
@@ -432,7 +475,7 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
   pdl_trigger();
   if (threadIdx.x == 0) KQ_TRACE_AT(0, 10);
 
-  if (warp >= TV_DQ_WARPS && warp < TV_MMA_WARP) {
+  if (warp == TV_LD_WARP) {
     // ---------------- raw loader (lane 0): one bulk copy per unit from the unit-major copy; the
     // weights do not depend on the previous kernel (no PDL wait)
     if (lane == 0) {
@@ -440,7 +483,7 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
       int k = 0;
       for (; k < n; ++k) {
         const int slot = k % TV_RS;
-        if (k >= TV_RS && !tm_wait(&raw_empty[slot], (uint32_t)((k / TV_RS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
+        if (k >= TV_RS && !tv_wait(&raw_empty[slot], (uint32_t)((k / TV_RS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f, 64))
           break;
         const long long u = u0 + k;
         const int t = (int)(u / G), g = (int)(u % G);
@@ -455,27 +498,33 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
     }
     __syncwarp();
   } else if (warp == TV_MMA_WARP) {
-    // ---------------- MMA issue (one thread): unit k uses A columns [64 (k & 1), +64) and D columns
-    // [128 + 128 (k & 1), +128) (group gi at 16 gi)
+    // ---------------- MMA issue (one thread): unit k reads A slot k % TV_AS (columns 64 (k % TV_AS))
+    // and writes D slot k % TV_DS (columns 256 + 64 (k % TV_DS), group gi at 8 gi)
     if (lane == 0) {
       const uint32_t idesc = tc_idesc_i8(TV_ROWS, TV_MMA_N);
       const uint32_t bq4 = smem_u32(sm + L.bq4), bq6 = smem_u32(sm + L.bq6);
       if (tm_wait(&b_ready, 0, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) {
         for (int k = 0; k < n; ++k) {
-          const int slot = k & 1;
-          if (!tm_wait(&a_full[slot], (uint32_t)(k >> 1) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
-          if (k >= 2 && !tm_wait(&d_free[slot], (uint32_t)((k - 2) >> 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f)) break;
+          const int as = k % TV_AS, ds = k % TV_DS;
+          if (!tm_wait(&a_full[as], (uint32_t)(k / TV_AS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
+          if (k >= TV_DS && !tm_wait(&d_free[ds], (uint32_t)((k / TV_DS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f)) break;
           KQ_TRACE_AT(k, 4);
-          tc_fence_after();
+          // hands the header slot of unit k (written before the writers' a_full arrivals, acquired
+          // above) on to the read-back warps
+          mbar_arrive(&h_full[k % TV_HS]);
+          // (no tcgen05 fence here: the writers' tcgen05.wait::st before their arrival orders their
+          // tensor-memory stores before these MMAs, as CUTLASS's transform-to-MMA pipeline does; a
+          // fence::after_thread_sync per unit serialised each unit's MMAs behind the previous ones)
           const long long u = u0 + k;
           const int t = (int)(u / G), g = (int)(u % G);
           const bool q4 = P.seg[seg_of(t)].w.type == Q4K;
-          const uint32_t bb = (q4 ? bq4 : bq6) + (uint32_t)g * 8u * (q4 ? TV_B_Q4 : TV_B_Q6), bst = q4 ? TV_B_Q4 : TV_B_Q6;
-          const uint32_t ta = tmem + 64u * (uint32_t)slot, td = tmem + 128u + 128u * (uint32_t)slot;
+          const uint32_t bst = q4 ? TV_B_Q4 : TV_B_Q6, bb = (q4 ? bq4 : bq6) + (uint32_t)g * 8u * bst;
+          const uint32_t ta = tmem + 64u * (uint32_t)as, td = tmem + 256u + 64u * (uint32_t)ds;
 #pragma unroll
           for (int gi = 0; gi < 8; ++gi)
             tc_mma_i8_ts(td + (uint32_t)TV_MMA_N * gi, ta + 8u * gi, tv_bdesc(bb + (uint32_t)gi * bst, 48u), idesc);
-          tc_commit(&d_full[slot]);
+          tc_commit(&a_free[as]);
+          tc_commit(&d_full[ds]);
           KQ_TRACE_AT(k, 5);
         }
       }
@@ -484,195 +533,198 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
     }
     __syncwarp();
   } else {
-    // ---------------- warps 0-7: thread (row r of the warp's TMEM lane quarter, half hh)
-    const int qd = warp & 3, hh = warp >> 2, r = 32 * qd + lane;
+    // ---------------- warps 0-11: the prologue (activation digits -> B tiles), then their roles
+    constexpr int NP = (TV_DQ_WARPS + TV_RO_WARPS) * 32;
     pdl_wait();
-    tv_prologue(P, sm, L, s_redd);
+    tv_prologue<NP>(P, sm, L, s_redd, threadIdx.x);
     fence_proxy_async();   // the B tiles are read by the tensor cores
-    named_bar(1, TV_DQ_WARPS * 32);
+    named_bar(1, NP);
     if (threadIdx.x == 0) {
       mbar_arrive(&b_ready);
       KQ_TRACE_AT(255, 0);
     }
+  if (warp < TV_DQ_WARPS) {
+    // ---------------- A-digit writers: thread (row r of the warp's TMEM lane quarter, half hh of
+    // the super-block); the thread of half 0 also copies its row's header for the read-back
+    const int qd = warp & 3, hh = warp >> 2, r = 32 * qd + lane;
+    const uint32_t tl = tmem + ((uint32_t)(32 * qd) << 16);
+    for (int k = 0; k < n; ++k) {
+      const int slot = k % TV_RS, as = k % TV_AS, hs = k % TV_HS;
+      if (!__all_sync(0xffffffffu, tv_wait(&raw_full[slot], (uint32_t)(k / TV_RS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f, 64)))
+        break;
+      // A slot and header slot free: the MMAs of unit k - TV_AS have completed, and they were issued
+      // after the read-back of unit k - TV_AS - TV_DS (= k - TV_HS) released its D slot
+      if (k >= TV_AS &&
+          !__all_sync(0xffffffffu, tv_wait(&a_free[as], (uint32_t)((k / TV_AS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f, 64)))
+        break;
+      tc_fence_after();
+      if (threadIdx.x == 0) KQ_TRACE_AT(k, 0);
+      const long long u = u0 + k;
+      const bool q4 = P.seg[seg_of((int)(u / G))].w.type == Q4K;
+      const uint8_t* st = raw_ring + (size_t)slot * TV_RAW_BYTES;
+      const uint32_t ta = tl + 64u * (uint32_t)as + 32u * (uint32_t)hh;
+      if (q4) {
+        if (hh == 0) hdr[hs * TV_ROWS + r] = lds128(st + TV_ST_HDR + 16 * r);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          // the 32 bytes of (hh, c): low nibbles = sub-block 4hh + 2c, high = 4hh + 2c + 1
+          const uint8_t* b = st + c * TV_ST_C1;
+          const uint4 W0 = lds128(b + tv_sw64(r, 2 * hh)), W1 = lds128(b + tv_sw64(r, 2 * hh + 1));
+          const uint32_t wd[8] = {W0.x, W0.y, W0.z, W0.w, W1.x, W1.y, W1.z, W1.w};
+          uint32_t lo[8], hi[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) { lo[i] = wd[i] & 0x0F0F0F0Fu; hi[i] = wd[i] & 0xF0F0F0F0u; }
+          tc_st8(ta + 16u * c, lo);
+          tc_st8(ta + 16u * c + 8u, hi);
+        }
+      } else {
+        if (hh == 0) {
+          hdr[hs * TV_ROWS + r] = lds128(st + TV_ST_SC + 16 * r);
+          hdrd[hs * TV_ROWS + r] = *reinterpret_cast<const uint16_t*>(st + TV_ST_D + 2 * r);
+        }
+        const uint4 H0 = lds128(st + TV_ST_QH + tv_sw64(r, 2 * hh)), H1 = lds128(st + TV_ST_QH + tv_sw64(r, 2 * hh + 1));
+        const uint32_t qh[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+          const uint8_t* lq = st + m * TV_ST_C1;
+          const uint4 L0 = lds128(lq + tv_sw64(r, 2 * hh)), L1 = lds128(lq + tv_sw64(r, 2 * hh + 1));
+          const uint32_t ql[8] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w};
+#pragma unroll
+          for (int nib = 0; nib < 2; ++nib) {
+            // group k = 2 nib + m: ql chunk m, nibble nib, qh bits 2k
+            const int kk = 2 * nib + m;
+            uint32_t q6[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              q6[i] = ((ql[i] >> (4 * nib)) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * kk)) & 0x03030303u) << 4);
+            tc_st8(ta + 8u * kk, q6);
+          }
+        }
+      }
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&a_full[as]);
+        mbar_arrive(&raw_empty[slot]);
+        if (k < 50) KQ_TRACE_AT(100 + k, warp);
+      }
+      if (threadIdx.x == 0) KQ_TRACE_AT(k, 1);
+    }
+  } else {
+    // ---------------- read-back warps (thread = row r of the warp's TMEM lane quarter): prologue,
+    // then per unit the row's int32 dot products with the scales applied, tile flushes, epilogues
+    const int tid = threadIdx.x - TV_DQ_WARPS * 32, qd = warp & 3, r = 32 * qd + lane;
+    constexpr int NT = TV_RO_WARPS * 32;
     const uint32_t tl = tmem + ((uint32_t)(32 * qd) << 16);
     const float* s3a = reinterpret_cast<const float*>(sm + L.s3);
     const float* x32 = reinterpret_cast<const float*>(sm + L.x32);
     const int4* c16 = reinterpret_cast<const int4*>(sm + L.c16);
-    float* red = reinterpret_cast<float*>(sm + L.red);
     const int tf0 = (int)(u0 / G);   // this CTA's first tile
     float acc = 0.f;
     bool ok = true;
-    // read-back of unit k (super-block g, type q4), groups 4 hh + j: the row's int32 dot products
-    // with the scales applied (Q4_K: cw = the 6-bit scales of sub-blocks 4hh .. 4hh + 3 as bytes,
-    // mw the mins, d0 = d, d1 = dmin; Q6_K: cw, mw = scale words 2hh (first 16 columns of each
-    // group) and 2hh + 1 (last 16), d0 = d)
-    auto readout = [&](int k, int g, bool q4, uint32_t cw, uint32_t mw, float d0, float d1) -> bool {
-      const int slot = k & 1;
-      if (!__all_sync(0xffffffffu, tm_wait(&d_full[slot], (uint32_t)(k >> 1) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)))
+    // Header slot k % TV_HS is rewritten (unit k + TV_HS) only after the A slot of unit k + TV_DS
+    // is free, i.e. after the MMAs of unit k + TV_DS, which wait for this read-back's D release:
+    // the header is read before that release.
+    auto readout = [&](int k) -> bool {
+      const int ds = k % TV_DS, hs = k % TV_HS;
+      if (!__all_sync(0xffffffffu, tv_wait(&h_full[hs], (uint32_t)(k / TV_HS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f, 32)))
+        return false;
+      const uint4 H = hdr[hs * TV_ROWS + r];
+      const uint32_t Hd = hdrd[hs * TV_ROWS + r];
+      if (!__all_sync(0xffffffffu, tv_wait(&d_full[ds], (uint32_t)(k / TV_DS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f, 32)))
         return false;
       tc_fence_after();
-      if (threadIdx.x == 0) KQ_TRACE_AT(k, 2);
-      const uint32_t td = tl + 128u + 128u * (uint32_t)slot + (uint32_t)(4 * TV_MMA_N) * (uint32_t)hh;
+      if (tid == 0) KQ_TRACE_AT(k, 2);
+      const long long u = u0 + k;
+      const int g = (int)(u % G);
+      const bool q4 = P.seg[seg_of((int)(u / G))].w.type == Q4K;
+      const uint32_t td = tl + 256u + 64u * (uint32_t)ds;
+      int D0[32], D1[32];   // groups 0-3 and 4-7, 8 columns each
+      tc_ld32_nw(td, D0);
+      tc_ld32_nw(td + 32u, D1);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&d_free[ds]);
       const float s3 = s3a[g];
       int P3[3] = {0, 0, 0};
       if (q4) {
-        int D[4][4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tc_ld4_nw(td + (uint32_t)TV_MMA_N * j, D[j]);
-        tc_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&d_free[slot]);
+        const float d = h2f_bits(H.x & 0xFFFFu), dmin = h2f_bits(H.x >> 16);
+        const uint32_t sc0 = H.y & 0x3F3F3F3Fu, sc1 = (H.w & 0x0F0F0F0Fu) | ((H.y >> 2) & 0x30303030u);
+        const uint32_t mn0 = H.z & 0x3F3F3F3Fu, mn1 = ((H.w >> 4) & 0x0F0F0F0Fu) | ((H.z >> 2) & 0x30303030u);
         float Qm = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {   // sub-block 4hh + j: c = j >> 1, high nibble if j odd
-          const int c = tv_ubyte(cw, j) << ((j & 1) ? 0 : 4);   // high nibbles enter as 16 q
-          P3[0] += c * D[j][0];
-          P3[1] += c * D[j][1];
-          P3[2] += c * D[j][2];
-          Qm = __fmaf_rn((float)tv_ubyte(mw, j), x32[g * 8 + 4 * hh + j], Qm);
+        for (int j = 0; j < 8; ++j) {   // sub-block j: high nibble if j odd (entered as 16 q)
+          const int* Dj = j < 4 ? &D0[8 * j] : &D1[8 * (j - 4)];
+          const int c = tv_ubyte(j < 4 ? sc0 : sc1, j & 3) << ((j & 1) ? 0 : 4);
+          P3[0] += c * Dj[0];
+          P3[1] += c * Dj[1];
+          P3[2] += c * Dj[2];
+          Qm = __fmaf_rn((float)tv_ubyte(j < 4 ? mn0 : mn1, j & 3), x32[g * 8 + j], Qm);
         }
         const float Pf = planes_combine(P3);
-        acc = __fadd_rn(acc, __fsub_rn(__fmul_rn(__fmul_rn(s3, 0.0625f), __fmul_rn(d0, Pf)), __fmul_rn(s3, __fmul_rn(d1, Qm))));
+        acc = __fadd_rn(acc, __fsub_rn(__fmul_rn(__fmul_rn(s3, 0.0625f), __fmul_rn(d, Pf)), __fmul_rn(s3, __fmul_rn(dmin, Qm))));
       } else {
-        int D[4][8];
+        const float d = h2f_bits(Hd);
+        const uint32_t sw[4] = {H.x, H.y, H.z, H.w};   // scale words [u = 2h + jh][k]
 #pragma unroll
-        for (int j = 0; j < 4; ++j) tc_ld8_nw(td + (uint32_t)TV_MMA_N * j, D[j]);
-        tc_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&d_free[slot]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {   // group k = j of half hh: scale bytes j of the two words
-          const int gi = 4 * hh + j;
-          const int sa = sbyte(cw, j), sb = sbyte(mw, j);
+        for (int gi = 0; gi < 8; ++gi) {   // group (h, k) = (gi >> 2, gi & 3)
+          const int* Dj = gi < 4 ? &D0[8 * gi] : &D1[8 * (gi - 4)];
+          const int h = gi >> 2, kk = gi & 3;
+          const int sa = sbyte(sw[2 * h], kk), sb = sbyte(sw[2 * h + 1], kk);
           const int4 ca = c16[g * 16 + 2 * gi], cb = c16[g * 16 + 2 * gi + 1];
-          P3[0] += sa * (D[j][0] - ca.x) + sb * (D[j][3] - cb.x);
-          P3[1] += sa * (D[j][1] - ca.y) + sb * (D[j][4] - cb.y);
-          P3[2] += sa * (D[j][2] - ca.z) + sb * (D[j][5] - cb.z);
+          P3[0] += sa * (Dj[0] - ca.x) + sb * (Dj[3] - cb.x);
+          P3[1] += sa * (Dj[1] - ca.y) + sb * (Dj[4] - cb.y);
+          P3[2] += sa * (Dj[2] - ca.z) + sb * (Dj[5] - cb.z);
         }
-        acc = __fadd_rn(acc, __fmul_rn(s3, __fmul_rn(d0, planes_combine(P3))));
+        acc = __fadd_rn(acc, __fmul_rn(s3, __fmul_rn(d, planes_combine(P3))));
       }
-      if (threadIdx.x == 0) KQ_TRACE_AT(k, 3);
+      if (tid == 0) KQ_TRACE_AT(k, 3);
       return true;
     };
-    // end of tile t's units in this CTA: the row sums of both halves; the epilogue if the CTA
-    // covered the whole tile, else the partial and, for the last contributor, the merge in CTA
-    // order. Every warp of 0-7 takes the same barriers, also after a failure.
+    // end of tile t's units in this CTA: the epilogue if the CTA covered the whole tile, else the
+    // partial and, for the last contributor, the merge in CTA order. Every read-back thread takes
+    // the same barriers, also after a failure.
     auto flush = [&](int t, bool whole) {
-      if (hh == 1) red[r] = acc;
-      const bool good = named_bar_and(1, TV_DQ_WARPS * 32, ok && !*abort_f);
-      if (hh == 0) {
-        const TvSeg& S = P.seg[seg_of(t)];
-        const int row = (t - S.tile0) * TV_ROWS + r;
-        float v = __fadd_rn(acc, red[r]);
-        bool fin = good && whole;
-        if (good && !whole) {
-          __stcg(P.part + ((size_t)cta * 2 + (t == tf0 ? 0 : 1)) * TV_ROWS + r, v);
-          __threadfence();
-          named_bar(3, 4 * 32);
-          const int cf = tv_cta_of((long long)t * G, nct, U), cl = tv_cta_of((long long)t * G + G - 1, nct, U);
-          if (threadIdx.x == 0) s_last = atomicAdd(&P.ticket[t], 1) == cl - cf;
-          named_bar(3, 4 * 32);
-          fin = s_last;
-          if (fin) {
-            __threadfence();
-            v = 0.f;
-            for (int c = cf; c <= cl; ++c) {
-              const int tfc = (int)(tv_unit0(c, nct, U) / G);
-              v = __fadd_rn(v, __ldcg(P.part + ((size_t)c * 2 + (t == tfc ? 0 : 1)) * TV_ROWS + r));
-            }
-            if (threadIdx.x == 0) P.ticket[t] = 0;
-          }
-        }
+      const bool good = named_bar_and(4, NT, ok && !*abort_f);
+      const TvSeg& S = P.seg[seg_of(t)];
+      const int row = (t - S.tile0) * TV_ROWS + r;
+      float v = acc;
+      bool fin = good && whole;
+      if (good && !whole) {
+        __stcg(P.part + ((size_t)cta * 2 + (t == tf0 ? 0 : 1)) * TV_ROWS + r, v);
+        __threadfence();
+        named_bar(3, NT);
+        const int cf = tv_cta_of((long long)t * G, nct, U), cl = tv_cta_of((long long)t * G + G - 1, nct, U);
+        if (tid == 0) s_last = atomicAdd(&P.ticket[t], 1) == cl - cf;
+        named_bar(3, NT);
+        fin = s_last;
         if (fin) {
-          const float vo = __shfl_xor_sync(0xffffffffu, v, 1);
-          if (row < S.w.R) tv_epilogue(P, S, row, v, vo);
+          __threadfence();
+          v = 0.f;
+          for (int c = cf; c <= cl; ++c) {
+            const int tfc = (int)(tv_unit0(c, nct, U) / G);
+            v = __fadd_rn(v, __ldcg(P.part + ((size_t)c * 2 + (t == tfc ? 0 : 1)) * TV_ROWS + r));
+          }
+          if (tid == 0) P.ticket[t] = 0;
         }
       }
-      named_bar(1, TV_DQ_WARPS * 32);   // red[] and s_last are reused by the next flush
+      if (fin) {
+        const float vo = __shfl_xor_sync(0xffffffffu, v, 1);
+        if (row < S.w.R) tv_epilogue(P, S, row, v, vo);
+      }
+      named_bar(4, NT);   // s_last is reused by the next flush
       acc = 0.f;
     };
-    // the read-back of unit k, then the flush if it ends its tile's run in this CTA
-    auto finish = [&](int k, int g, bool q4, uint32_t cw, uint32_t mw, float d0, float d1) {
-      if (ok) ok = readout(k, g, q4, cw, mw, d0, d1);
+    for (int k = 0; k < n; ++k) {
+      if (ok) ok = readout(k);
       const long long u = u0 + k;
       const int t = (int)(u / G);
       if (k == n - 1 || (int)((u + 1) / G) != t) flush(t, u0 <= (long long)t * G && (int)(u % G) == G - 1);
-    };
-    uint32_t pcw = 0, pmw = 0;   // the previous unit's header
-    float pd0 = 0.f, pd1 = 0.f;
-    int pg = 0;
-    bool pq4 = true;
-    for (int k = 0; k < n; ++k) {
-      const int slot = k % TV_RS;
-      const long long u = u0 + k;
-      const int t = (int)(u / G), g = (int)(u % G);
-      const TvSeg& S = P.seg[seg_of(t)];
-      const bool q4 = S.w.type == Q4K;
-      if (ok) ok = __all_sync(0xffffffffu, tm_wait(&raw_full[slot], (uint32_t)(k / TV_RS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f));
-      if (threadIdx.x == 0) KQ_TRACE_AT(k, 0);
-      uint32_t cw = 0, mw = 0;
-      float d0 = 0.f, d1 = 0.f;
-      if (ok) {
-        const uint8_t* st = raw_ring + (size_t)slot * TV_RAW_BYTES;
-        const uint32_t ta = tl + 64u * (uint32_t)(k & 1) + 32u * (uint32_t)hh;
-        if (q4) {
-          const uint4 H = lds128(st + TV_ST_HDR + 16 * r);
-          d0 = h2f_bits(H.x & 0xFFFFu);
-          d1 = h2f_bits(H.x >> 16);
-          cw = hh ? ((H.w & 0x0F0F0F0Fu) | ((H.y >> 2) & 0x30303030u)) : (H.y & 0x3F3F3F3Fu);          // scales
-          mw = hh ? (((H.w >> 4) & 0x0F0F0F0Fu) | ((H.z >> 2) & 0x30303030u)) : (H.z & 0x3F3F3F3Fu);   // mins
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            // the 32 bytes of (hh, c): low nibbles = sub-block 4hh + 2c, high = 4hh + 2c + 1
-            const uint8_t* b = st + c * TV_ST_C1;
-            const uint4 W0 = lds128(b + tv_sw64(r, 2 * hh)), W1 = lds128(b + tv_sw64(r, 2 * hh + 1));
-            const uint32_t wd[8] = {W0.x, W0.y, W0.z, W0.w, W1.x, W1.y, W1.z, W1.w};
-            uint32_t lo[8], hi[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) { lo[i] = wd[i] & 0x0F0F0F0Fu; hi[i] = wd[i] & 0xF0F0F0F0u; }
-            tc_st8(ta + 16u * c, lo);
-            tc_st8(ta + 16u * c + 8u, hi);
-          }
-        } else {
-          const uint2 Sc = *reinterpret_cast<const uint2*>(st + TV_ST_SC + 16 * r + 8 * hh);   // scale words 2hh, 2hh + 1
-          cw = Sc.x;
-          mw = Sc.y;
-          d0 = h2f_bits(*reinterpret_cast<const uint16_t*>(st + TV_ST_D + 2 * r));
-          const uint4 H0 = lds128(st + TV_ST_QH + tv_sw64(r, 2 * hh)), H1 = lds128(st + TV_ST_QH + tv_sw64(r, 2 * hh + 1));
-          const uint32_t qh[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            const uint8_t* lq = st + m * TV_ST_C1;
-            const uint4 L0 = lds128(lq + tv_sw64(r, 2 * hh)), L1 = lds128(lq + tv_sw64(r, 2 * hh + 1));
-            const uint32_t ql[8] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w};
-#pragma unroll
-            for (int nib = 0; nib < 2; ++nib) {
-              // group k = 2 nib + m: ql chunk m, nibble nib, qh bits 2k
-              const int kk = 2 * nib + m;
-              uint32_t q6[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                q6[i] = ((ql[i] >> (4 * nib)) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * kk)) & 0x03030303u) << 4);
-              tc_st8(ta + 8u * kk, q6);
-            }
-          }
-        }
-        tc_wait_st();
-        tc_fence_before();
-      }
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[k & 1]);
-        mbar_arrive(&raw_empty[slot]);
-      }
-      if (threadIdx.x == 0) KQ_TRACE_AT(k, 1);
-      if (k > 0) finish(k - 1, pg, pq4, pcw, pmw, pd0, pd1);
-      pcw = cw; pmw = mw; pd0 = d0; pd1 = d1; pg = g; pq4 = q4;
     }
-    if (n > 0) finish(n - 1, pg, pq4, pcw, pmw, pd0, pd1);
-    if (threadIdx.x == 0) KQ_TRACE_AT(255, 1);
+    if (tid == 0) KQ_TRACE_AT(255, 1);
+  }
   }
   tc_fence_before();
   __syncthreads();
