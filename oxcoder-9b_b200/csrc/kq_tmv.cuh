@@ -436,8 +436,11 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
   uint8_t* raw_ring = sm;
   uint4* hdr = reinterpret_cast<uint4*>(sm + L.hdr);         // [TV_HS][128]
   uint32_t* hdrd = reinterpret_cast<uint32_t*>(sm + L.hdrd);  // [TV_HS][128]
-  __shared__ __align__(8) uint64_t raw_full[TV_RS], raw_empty[TV_RS], a_full[TV_AS], a_free[TV_AS], d_full[TV_DS],
-      d_free[TV_DS], h_full[TV_HS], b_ready, mma_done;
+  // mdone[k % TV_AS]: the MMAs of unit k have completed (A slot free for unit k + TV_AS, D slot
+  // ready for the read-back); d_free[k % TV_DS]: the read-back of unit k has its D and header
+  static_assert(TV_AS == TV_DS, "one completion barrier per unit serves the A and the D slot");
+  __shared__ __align__(8) uint64_t raw_full[TV_RS], raw_empty[TV_RS], a_full[TV_AS], mdone[TV_AS], d_free[TV_DS],
+      h_full[TV_HS], b_ready, mma_done;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_last;
   __shared__ double s_redd[TV_DQ_WARPS + TV_RO_WARPS];
@@ -456,8 +459,8 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < TV_RS; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], TV_DQ_WARPS); }
-    for (int i = 0; i < TV_AS; ++i) { mbar_init(&a_full[i], TV_DQ_WARPS); mbar_init(&a_free[i], 1); }
-    for (int i = 0; i < TV_DS; ++i) { mbar_init(&d_full[i], 1); mbar_init(&d_free[i], TV_RO_WARPS); }
+    for (int i = 0; i < TV_AS; ++i) { mbar_init(&a_full[i], TV_DQ_WARPS); mbar_init(&mdone[i], 1); }
+    for (int i = 0; i < TV_DS; ++i) mbar_init(&d_free[i], TV_RO_WARPS);
     for (int i = 0; i < TV_HS; ++i) mbar_init(&h_full[i], 1);
     mbar_init(&b_ready, 1);
     mbar_init(&mma_done, 1);
@@ -505,9 +508,10 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
       const uint32_t bq4 = smem_u32(sm + L.bq4), bq6 = smem_u32(sm + L.bq6);
       if (tm_wait(&b_ready, 0, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) {
         for (int k = 0; k < n; ++k) {
+          // a_full implies both slots are free: its writers waited for the MMAs and the read-back
+          // of unit k - TV_AS (one wait here; each mbarrier wait costs this thread ~200 cycles)
           const int as = k % TV_AS, ds = k % TV_DS;
           if (!tm_wait(&a_full[as], (uint32_t)(k / TV_AS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
-          if (k >= TV_DS && !tm_wait(&d_free[ds], (uint32_t)((k / TV_DS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f)) break;
           KQ_TRACE_AT(k, 4);
           // hands the header slot of unit k (written before the writers' a_full arrivals, acquired
           // above) on to the read-back warps
@@ -523,8 +527,7 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
 #pragma unroll
           for (int gi = 0; gi < 8; ++gi)
             tc_mma_i8_ts(td + (uint32_t)TV_MMA_N * gi, ta + 8u * gi, tv_bdesc(bb + (uint32_t)gi * bst, 48u), idesc);
-          tc_commit(&a_free[as]);
-          tc_commit(&d_full[ds]);
+          tc_commit(&mdone[as]);
           KQ_TRACE_AT(k, 5);
         }
       }
@@ -552,10 +555,12 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
       const int slot = k % TV_RS, as = k % TV_AS, hs = k % TV_HS;
       if (!__all_sync(0xffffffffu, tv_wait(&raw_full[slot], (uint32_t)(k / TV_RS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f, 64)))
         break;
-      // A slot and header slot free: the MMAs of unit k - TV_AS have completed, and they were issued
-      // after the read-back of unit k - TV_AS - TV_DS (= k - TV_HS) released its D slot
+      // A slot free (the MMAs of unit k - TV_AS have completed) and D slot free (the read-back of
+      // unit k - TV_AS has its D and header; it reads the header slot (k - TV_AS) % TV_HS, and the
+      // header slot k % TV_HS was last read by the read-back of unit k - TV_HS, earlier still)
       if (k >= TV_AS &&
-          !__all_sync(0xffffffffu, tv_wait(&a_free[as], (uint32_t)((k / TV_AS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f, 64)))
+          !(__all_sync(0xffffffffu, tv_wait(&mdone[as], (uint32_t)((k / TV_AS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f, 64)) &&
+            __all_sync(0xffffffffu, tv_wait(&d_free[as], (uint32_t)((k / TV_AS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f, 64))))
         break;
       tc_fence_after();
       if (threadIdx.x == 0) KQ_TRACE_AT(k, 0);
@@ -623,16 +628,16 @@ __global__ void __launch_bounds__(TV_THREADS, 1) k_tmv(const __grid_constant__ T
     const int tf0 = (int)(u0 / G);   // this CTA's first tile
     float acc = 0.f;
     bool ok = true;
-    // Header slot k % TV_HS is rewritten (unit k + TV_HS) only after the A slot of unit k + TV_DS
-    // is free, i.e. after the MMAs of unit k + TV_DS, which wait for this read-back's D release:
-    // the header is read before that release.
+    // Header slot k % TV_HS is rewritten (unit k + TV_HS) only after the writers of unit k + TV_HS
+    // saw the D release of unit k + TV_HS - TV_DS, which follows this read-back's release: the
+    // header is read before that release.
     auto readout = [&](int k) -> bool {
       const int ds = k % TV_DS, hs = k % TV_HS;
       if (!__all_sync(0xffffffffu, tv_wait(&h_full[hs], (uint32_t)(k / TV_HS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f, 32)))
         return false;
       const uint4 H = hdr[hs * TV_ROWS + r];
       const uint32_t Hd = hdrd[hs * TV_ROWS + r];
-      if (!__all_sync(0xffffffffu, tv_wait(&d_full[ds], (uint32_t)(k / TV_DS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f, 32)))
+      if (!__all_sync(0xffffffffu, tv_wait(&mdone[ds], (uint32_t)(k / TV_DS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f, 32)))
         return false;
       tc_fence_after();
       if (tid == 0) KQ_TRACE_AT(k, 2);
