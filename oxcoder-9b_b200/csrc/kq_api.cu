@@ -225,9 +225,11 @@ static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, boo
   // tuning override for sweeps: KQ_GEMV_RPG (1, 2, 4) and KQ_GEMV_NRG fix the shape if valid
   const int want_rpg = std::getenv("KQ_GEMV_RPG") ? std::atoi(std::getenv("KQ_GEMV_RPG")) : 0;
   const int want_nrg = std::getenv("KQ_GEMV_NRG") ? std::atoi(std::getenv("KQ_GEMV_NRG")) : 0;
-  // Candidates are scored: (a) every CTA gets >= 4 stages, so the weight stream is pipelined
-  // from the start (small matrices need short stages); (b) more consumer warps; (c) more rows
-  // per thread (activation reuse).
+  // Candidates are scored: (a) when every CTA's share fits the ring (the producer issues all of
+  // it before the consumers' prologue ends), fewer stages per CTA: a stage of 24 rows costs
+  // ~2.1 us of consumer time against ~1.5 us for 8 rows; (b) otherwise every CTA gets >= 4
+  // stages, so the weight stream is pipelined from the start; then (c) more consumer warps and
+  // (d) more rows per thread (activation reuse).
   bool found = false;
   long best = -1;
   for (int NRG = std::min(KQ_MAX_NRG, KQ_GEMV_MAX_CONSUMERS / LPR); NRG >= 1; --NRG) {
@@ -246,12 +248,14 @@ static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, boo
       int nstages = 0;
       for (int i = 0; i < nseg; ++i) nstages += (seg_rows[i] + TR - 1) / TR;
       const int grid = std::max(1, std::min(nsm, nstages));
-      const long score = (nstages >= 4 * grid ? 1L << 20 : 0) + (long)(LPR * NRG) * 8 + RPG;
+      int slots = (int)((budget - fixed) / (stage_bytes + 16));
+      slots = std::min(8, std::max(2, slots));
+      const int per_cta = (nstages + grid - 1) / grid;
+      const long score = (per_cta <= slots ? (1L << 21) - 1024L * per_cta : nstages >= 4 * grid ? 1L << 20 : 0) +
+                         (long)(LPR * NRG) * 8 + RPG;
       if (score <= best) continue;
       best = score;
       found = true;
-      int slots = (int)((budget - fixed) / (stage_bytes + 16));
-      slots = std::min(8, std::max(2, slots));
       pl.TR = TR; pl.LPR = LPR; pl.NRG = NRG; pl.RPG = RPG;
       pl.TM = (has4 && has6) || std::getenv("KQ_GEMV_MIXED") ? TM_MIXED : has6 ? TM_Q6K : TM_Q4K;   // env: tuning
       pl.stage_bytes = stage_bytes;
@@ -298,6 +302,8 @@ static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParam
   p.nstages = st;
   p.C = C; p.G = C / 256; p.TR = pl.TR; p.LPR = pl.LPR; p.NRG = pl.NRG; p.nlanes = 1; p.tps = 1;
   p.stage_bytes = pl.stage_bytes; p.nslots = pl.nslots;
+  // tuning override for sweeps: KQ_GEMV_PREFETCH stages go out before the prologue is done
+  p.prefetch = std::getenv("KQ_GEMV_PREFETCH") ? std::max(0, std::atoi(std::getenv("KQ_GEMV_PREFETCH"))) : pl.nslots;
   return KQ_OK;
 }
 

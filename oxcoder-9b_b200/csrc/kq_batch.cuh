@@ -640,12 +640,14 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
 // grid (token, KV head, query head), DM_MERGE_THREADS threads: the split weights exp(m_s - M) and
 // the denominator once per block in shared memory, then four groups of 128 threads (one per
 // output column) each sum a quarter of the splits' rows and the groups' sums are added in group
-// order. The result goes to the packed o-GEMM input or, for the decode step, to fp32.
+// order. Every thread issues its quarter's row loads before the weights are known, so the block
+// waits for one L2 round trip, not two. The result goes to the packed o-GEMM input or, for the
+// decode step, to fp32.
 constexpr int DM_MERGE_THREADS = 512;
 static_assert(DA_MAX_SPLIT <= 64, "the merge weighs at most two splits per lane");
 template <int G>
 __global__ void __launch_bounds__(DM_MERGE_THREADS) k_dattn_merge(const __grid_constant__ DAttnParams P) {
-  constexpr int HD = 128, PLD = HD + 4, NQ = DM_MERGE_THREADS / HD;
+  constexpr int HD = 128, PLD = HD + 4, NQ = DM_MERGE_THREADS / HD, PER_MAX = (DA_MAX_SPLIT + NQ - 1) / NQ;
   __shared__ float s_w[DA_MAX_SPLIT];
   __shared__ float s_o[NQ][HD];
   __shared__ float s_L;
@@ -654,6 +656,10 @@ __global__ void __launch_bounds__(DM_MERGE_THREADS) k_dattn_merge(const __grid_c
   pdl_trigger();
   const int ns = P.nsplit;
   const float* pb = P.part + ((size_t)t * P.n_kv + kv) * ns * G * PLD + (size_t)g * PLD;
+  const int q = tid / HD, d = tid % HD, per = (ns + NQ - 1) / NQ, s0 = q * per, s1 = min(ns, s0 + per);
+  float ov[PER_MAX];
+#pragma unroll
+  for (int j = 0; j < PER_MAX; ++j) ov[j] = s0 + j < s1 ? __ldcg(pb + (size_t)(s0 + j) * G * PLD + d) : 0.f;
   if (tid < 32) {
     const float m0 = lane < ns ? __ldcg(pb + (size_t)lane * G * PLD + HD) : -INFINITY;
     const float m1 = lane + 32 < ns ? __ldcg(pb + (size_t)(lane + 32) * G * PLD + HD) : -INFINITY;
@@ -672,12 +678,13 @@ __global__ void __launch_bounds__(DM_MERGE_THREADS) k_dattn_merge(const __grid_c
     if (lane == 0) s_L = L;
   }
   __syncthreads();
-  const int q = tid / HD, d = tid % HD, per = (ns + NQ - 1) / NQ, s0 = q * per, s1 = min(ns, s0 + per);
   float O = 0.f;
-#pragma unroll 8
-  for (int s2 = s0; s2 < s1; ++s2) {
-    const float wt = s_w[s2];
-    if (wt != 0.f) O = __fmaf_rn(wt, __ldcg(pb + (size_t)s2 * G * PLD + d), O);
+#pragma unroll
+  for (int j = 0; j < PER_MAX; ++j) {
+    if (s0 + j < s1) {
+      const float wt = s_w[s0 + j];
+      if (wt != 0.f) O = __fmaf_rn(wt, ov[j], O);
+    }
   }
   s_o[q][d] = O;
   __syncthreads();

@@ -39,7 +39,6 @@ constexpr int KQ_MAX_NRG = 8;              // row groups (named barriers 1..8)
 constexpr int KQ_BAR_PROLOGUE = 14, KQ_BAR_ARGMAX = 15;
 constexpr int KQ_XSCAL = 18;               // per-unit scalars: s3, poison, xsf[4], c[3][4]
 constexpr int KQ_MAX_ITEMS = 4;            // prologue items per thread: the planner keeps >= 2 row groups
-constexpr int KQ_PREFETCH_STAGES = 1;      // stages requested before the prologue is done
 constexpr int KQ_MAX_HALF_HD = 128;        // rotary half width held in shared memory
 
 struct DecodeState {   // device-resident per-step state
@@ -98,6 +97,7 @@ struct GemvParams {
   int out_cap;
   int* err;
   int trace_id;          // launch index for the optional phase trace (KQ_TRACE builds)
+  int prefetch;          // k_gemv: stages the producer issues before the consumers' prologue is done
 };
 
 // Shared-memory carve-up, identical on host (sizing) and device.
@@ -773,9 +773,10 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
       for (int i = 0; i < nmine; ++i) {
         const int slot = i % P.nslots;
         const uint32_t round = (uint32_t)(i / P.nslots);
-        // One stage goes out at once; the rest waits for the consumers' prologue, whose few
-        // latency-bound L2 reads would otherwise queue behind a ring's worth of weight traffic.
-        if (i == KQ_PREFETCH_STAGES) {
+        // P.prefetch stages (by default the whole ring) go out at once; the rest waits for the
+        // consumers' prologue. A full ring before the prologue measured faster than one stage
+        // (the prologue's L2 reads did not slow down behind the weight traffic).
+        if (i == P.prefetch) {
           if (!mbar_wait(&pro_bar, 0, P.err, KQ_DEV_ERR_WAIT_FULL)) { s_fail = 1; break; }
         }
         if (i >= P.nslots) {
