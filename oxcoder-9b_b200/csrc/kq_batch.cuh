@@ -480,6 +480,10 @@ __global__ void __launch_bounds__(DA_WARPS * 32) k_dattn(const __grid_constant__
 // memory (cp.async, two stages, padded rows); the G query heads are rows 0..G-1 of an m16 tile
 // (Q as hi + lo fp16), S = Q K^T and O += P V on mma.sync with fp32 accumulation and the online
 // softmax in registers, as the tree attention. Same partial layout as k_dattn (k_dattn_merge).
+// Decode step (P.st): the preceding q/k/v GEMV writes only cache slot pos; every older slot was
+// written by an earlier step (hundreds of launches back), so the first two blocks are requested
+// before the dependency wait when none of their keys is pos, and the K/V stream overlaps the
+// GEMV's tail. The step state (pos, tree) was written by the previous step's output head.
 constexpr int DM_KB = 32;                                            // keys per block
 constexpr size_t DM_SMEM = (size_t)2 * 2 * DM_KB * BA_LD * 2;          // K and V, two stages
 template <int G>
@@ -489,8 +493,7 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
   __half* ksm = reinterpret_cast<__half*>(dm_sm);   // [2][DM_KB][BA_LD]
   __half* vsm = ksm + 2 * DM_KB * BA_LD;
   const int t = blockIdx.x, kv = blockIdx.y, sp = blockIdx.z, lane = threadIdx.x, grp = lane >> 2, t4 = lane & 3;
-  pdl_wait();
-  pdl_trigger();
+  if (!P.st) pdl_wait();
   int n = (P.st ? P.st->pos : P.pos[t]) + 1;
   if (n > P.ctx || n < 1) {
     if (lane == 0 && sp == 0 && kv == 0 && P.err) atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
@@ -515,7 +518,20 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
       cp_async16_plain(vd + r * BA_LD + c * 8, vg + off, ok ? 16u : 0u);
     }
   };
-  if (p0 < p1) load_block(p0, 0);
+  // blocks 0 and 1 before the wait (decode step, keys all below pos); cp.async groups are
+  // committed in the same places either way, and wait_group 1 below only ever waits for more
+  bool pre0 = false, pre1 = false;
+  if (P.st) {
+    pre0 = p0 < p1 && min(p0 + DM_KB, p1) <= n - 1;
+    pre1 = p0 + DM_KB < p1 && min(p0 + 2 * DM_KB, p1) <= n - 1;
+    if (pre0) load_block(p0, 0);
+    cp_async_commit();
+    if (pre1) load_block(p0 + DM_KB, 1);
+    cp_async_commit();
+    pdl_wait();
+  }
+  pdl_trigger();
+  if (p0 < p1 && !pre0) load_block(p0, 0);
   cp_async_commit();
   // Q fragments: rows grp (a0, a2) and grp + 8 (a1, a3); rows >= G are zero
   const int NHHD = P.n_kv * G * HD;
@@ -543,7 +559,7 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
   const int mi = lane >> 3;
   int st = 0;
   for (int b0 = p0; b0 < p1; b0 += DM_KB, st ^= 1) {
-    if (b0 + DM_KB < p1) load_block(b0 + DM_KB, st ^ 1);
+    if (b0 + DM_KB < p1 && !(b0 == p0 && pre1)) load_block(b0 + DM_KB, st ^ 1);
     cp_async_commit();
     cp_async_wait1();
     __syncwarp();
