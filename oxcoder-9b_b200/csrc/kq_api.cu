@@ -225,8 +225,8 @@ static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, boo
   // tuning override for sweeps: KQ_GEMV_RPG (1, 2, 4) and KQ_GEMV_NRG fix the shape if valid
   const int want_rpg = std::getenv("KQ_GEMV_RPG") ? std::atoi(std::getenv("KQ_GEMV_RPG")) : 0;
   const int want_nrg = std::getenv("KQ_GEMV_NRG") ? std::atoi(std::getenv("KQ_GEMV_NRG")) : 0;
-  // Candidates are scored: (a) when every CTA's share fits the ring (the producer issues all of
-  // it before the consumers' prologue ends), fewer stages per CTA: a stage of 24 rows costs
+  // Candidates are scored: (a) when every CTA's share fits the ring (no stage waits for a slot
+  // to be released), fewer stages per CTA: a stage of 24 rows costs
   // ~2.1 us of consumer time against ~1.5 us for 8 rows; (b) otherwise every CTA gets >= 4
   // stages, so the weight stream is pipelined from the start; then (c) more consumer warps and
   // (d) more rows per thread (activation reuse).
@@ -303,7 +303,7 @@ static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParam
   p.C = C; p.G = C / 256; p.TR = pl.TR; p.LPR = pl.LPR; p.NRG = pl.NRG; p.nlanes = 1; p.tps = 1;
   p.stage_bytes = pl.stage_bytes; p.nslots = pl.nslots;
   // tuning override for sweeps: KQ_GEMV_PREFETCH stages go out before the prologue is done
-  p.prefetch = std::getenv("KQ_GEMV_PREFETCH") ? std::max(0, std::atoi(std::getenv("KQ_GEMV_PREFETCH"))) : pl.nslots;
+  p.prefetch = std::getenv("KQ_GEMV_PREFETCH") ? std::max(0, std::atoi(std::getenv("KQ_GEMV_PREFETCH"))) : KQ_PREFETCH_STAGES;
   return KQ_OK;
 }
 
@@ -490,6 +490,7 @@ struct kq_model {
   int* err = nullptr;
   int attn_cl = 16;                  // CTAs per kv head in the cluster attention
   int attn_mode = 0;                 // 0: split form, 1: cluster form, 2: tensor-core split form
+  int dsplit = 0;                    // key splits of the tensor-core decode attention
   float* dpart1 = nullptr;          // decode-step partials of the tensor-core split form
   float* tv_part = nullptr;         // split-K scratch of the tensor-core GEMV (decode graph)
   int* tv_ticket = nullptr;
@@ -668,6 +669,8 @@ static kq_model* model_create(const kq_config* cfg, int device, int rank, int wo
     m->attn_cl = attn_cluster_size(c.n_heads / c.n_kv_heads, c.n_kv_heads);
     m->attn_mode = std::getenv("KQ_ATTN") ? std::atoi(std::getenv("KQ_ATTN")) : 2;   // tuning override
     if (m->attn_mode < 0 || m->attn_mode > 2) m->attn_mode = 2;
+    m->dsplit = std::getenv("KQ_DSPLIT") ? std::atoi(std::getenv("KQ_DSPLIT")) : DA_MAX_SPLIT;   // tuning override
+    if (m->dsplit < 1 || m->dsplit > DA_MAX_SPLIT) m->dsplit = DA_MAX_SPLIT;
     m->dpart1 = dalloc<float>(m, (size_t)c.n_kv_heads * DA_MAX_SPLIT * (c.n_heads / c.n_kv_heads) * (c.head_dim + 4), ok);
     m->persist = std::getenv("KQ_PERSIST") && std::atoi(std::getenv("KQ_PERSIST")) == 1;   // opt-in for now
     m->verify_seq = std::getenv("KQ_VERIFY_SEQ") && std::atoi(std::getenv("KQ_VERIFY_SEQ")) == 1;
@@ -1097,7 +1100,7 @@ static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
       std::memset(&D, 0, sizeof(D));
       D.q = op.a.a.q; D.kc = op.a.a.kc; D.vc = op.a.a.vc; D.st = op.a.a.st; D.err = op.a.a.err;
       D.n_kv = op.a.a.n_kv; D.ctx = op.a.a.ctx; D.scale = op.a.a.scale;
-      D.nsplit = DA_MAX_SPLIT; D.part = m->dpart1; D.out_f = op.a.a.out;
+      D.nsplit = m->dsplit; D.part = m->dpart1; D.out_f = op.a.a.out;
       CU(G == 1 ? launch_dattn_t<1>(D, 1, D.n_kv, s) : G == 2 ? launch_dattn_t<2>(D, 1, D.n_kv, s)
          : G == 4 ? launch_dattn_t<4>(D, 1, D.n_kv, s) : launch_dattn_t<8>(D, 1, D.n_kv, s));
     } else {

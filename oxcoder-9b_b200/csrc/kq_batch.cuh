@@ -387,7 +387,8 @@ __global__ void __launch_bounds__(256) k_argmax_rows(const float* logits, int V,
 // warp, the warps' (m, l, o) combined in fixed order into the split's partial. fp32 throughout,
 // fp16 K/V as stored. k_dattn_merge merges the splits in order into the packed o-GEMM input.
 constexpr int DA_WARPS = 4;
-constexpr int DA_MAX_SPLIT = 64;
+constexpr int DA_MAX_SPLIT = 64;   // key splits (64 keys each for the single-token step at ctx 4K;
+                                   // measured against 16 / 32 / 48 / 96 / 128: 64 is fastest)
 struct DAttnParams {
   const float* q;            // [M][NH_l * HD] rotated queries
   const __half* kc;          // [nseq][n_kv][ctx][HD]
@@ -660,7 +661,7 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
 // waits for one L2 round trip, not two. The result goes to the packed o-GEMM input or, for the
 // decode step, to fp32.
 constexpr int DM_MERGE_THREADS = 512;
-static_assert(DA_MAX_SPLIT <= 64, "the merge weighs at most two splits per lane");
+constexpr int DM_PER_LANE = (DA_MAX_SPLIT + 31) / 32;   // splits weighed per lane of the first warp
 template <int G>
 __global__ void __launch_bounds__(DM_MERGE_THREADS) k_dattn_merge(const __grid_constant__ DAttnParams P) {
   constexpr int HD = 128, PLD = HD + 4, NQ = DM_MERGE_THREADS / HD, PER_MAX = (DA_MAX_SPLIT + NQ - 1) / NQ;
@@ -677,20 +678,26 @@ __global__ void __launch_bounds__(DM_MERGE_THREADS) k_dattn_merge(const __grid_c
 #pragma unroll
   for (int j = 0; j < PER_MAX; ++j) ov[j] = s0 + j < s1 ? __ldcg(pb + (size_t)(s0 + j) * G * PLD + d) : 0.f;
   if (tid < 32) {
-    const float m0 = lane < ns ? __ldcg(pb + (size_t)lane * G * PLD + HD) : -INFINITY;
-    const float m1 = lane + 32 < ns ? __ldcg(pb + (size_t)(lane + 32) * G * PLD + HD) : -INFINITY;
-    float M = fmaxf(m0, m1);
+    // (m, l) of splits lane, lane + 32, ...: one 8-byte load each
+    float2 ml[DM_PER_LANE];
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < DM_PER_LANE; ++j) {
+      const int sp = lane + 32 * j;
+      ml[j] = sp < ns ? __ldcg(reinterpret_cast<const float2*>(pb + (size_t)sp * G * PLD + HD)) : make_float2(-INFINITY, 0.f);
+      M = fmaxf(M, ml[j].x);
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    const float w0 = m0 == -INFINITY ? 0.f : expf(__fsub_rn(m0, M));
-    const float w1 = m1 == -INFINITY ? 0.f : expf(__fsub_rn(m1, M));
     float L = 0.f;
-    if (w0 != 0.f) L = __fmul_rn(w0, __ldcg(pb + (size_t)lane * G * PLD + HD + 1));
-    if (w1 != 0.f) L = __fmaf_rn(w1, __ldcg(pb + (size_t)(lane + 32) * G * PLD + HD + 1), L);
+#pragma unroll
+    for (int j = 0; j < DM_PER_LANE; ++j) {
+      const float w = ml[j].x == -INFINITY ? 0.f : expf(__fsub_rn(ml[j].x, M));
+      if (w != 0.f) L = __fmaf_rn(w, ml[j].y, L);
+      if (lane + 32 * j < ns) s_w[lane + 32 * j] = w;
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) L = __fadd_rn(L, __shfl_xor_sync(0xffffffffu, L, off));
-    if (lane < ns) s_w[lane] = w0;
-    if (lane + 32 < ns) s_w[lane + 32] = w1;
     if (lane == 0) s_L = L;
   }
   __syncthreads();

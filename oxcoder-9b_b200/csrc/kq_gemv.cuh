@@ -40,6 +40,10 @@ constexpr int KQ_BAR_PROLOGUE = 14, KQ_BAR_ARGMAX = 15;
 constexpr int KQ_XSCAL = 18;               // per-unit scalars: s3, poison, xsf[4], c[3][4]
 constexpr int KQ_MAX_ITEMS = 4;            // prologue items per thread: the planner keeps >= 2 row groups
 constexpr int KQ_MAX_HALF_HD = 128;        // rotary half width held in shared memory
+// Stages the producer issues before the consumers' prologue is done (the ring holds >= 2).
+// Measured on the config-0 GEMV / config-2 decode step: 1 stage 12.1 us / 2.62 ms, 2 stages
+// 12.05 us / 2.57 ms, the whole ring (3 slots) 13.0 us / 2.58 ms.
+constexpr int KQ_PREFETCH_STAGES = 2;
 
 struct DecodeState {   // device-resident per-step state
   int tok;        // token processed by this step
@@ -773,9 +777,7 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
       for (int i = 0; i < nmine; ++i) {
         const int slot = i % P.nslots;
         const uint32_t round = (uint32_t)(i / P.nslots);
-        // P.prefetch stages (by default the whole ring) go out at once; the rest waits for the
-        // consumers' prologue. A full ring before the prologue measured faster than one stage
-        // (the prologue's L2 reads did not slow down behind the weight traffic).
+        // P.prefetch stages go out at once; the rest waits for the consumers' prologue.
         if (i == P.prefetch) {
           if (!mbar_wait(&pro_bar, 0, P.err, KQ_DEV_ERR_WAIT_FULL)) { s_fail = 1; break; }
         }
