@@ -227,9 +227,9 @@ static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, boo
   const int want_nrg = std::getenv("KQ_GEMV_NRG") ? std::atoi(std::getenv("KQ_GEMV_NRG")) : 0;
   // Candidates are scored: (a) when every CTA's share fits the ring (no stage waits for a slot
   // to be released), fewer stages per CTA: a stage of 24 rows costs
-  // ~2.1 us of consumer time against ~1.5 us for 8 rows; (b) otherwise every CTA gets >= 4
-  // stages, so the weight stream is pipelined from the start; then (c) more consumer warps and
-  // (d) more rows per thread (activation reuse).
+  // ~2.1 us of consumer time against ~1.5 us for 8 rows; then (b) more consumer warps and
+  // (c) more rows per thread (activation reuse). Short stages for a deeper pipeline lost: the
+  // config-0 GEMV takes 12.1 us with 8-row stages (>= 4 per CTA), 11.2 us with 24-row stages.
   bool found = false;
   long best = -1;
   for (int NRG = std::min(KQ_MAX_NRG, KQ_GEMV_MAX_CONSUMERS / LPR); NRG >= 1; --NRG) {
@@ -251,8 +251,7 @@ static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, boo
       int slots = (int)((budget - fixed) / (stage_bytes + 16));
       slots = std::min(8, std::max(2, slots));
       const int per_cta = (nstages + grid - 1) / grid;
-      const long score = (per_cta <= slots ? (1L << 21) - 1024L * per_cta : nstages >= 4 * grid ? 1L << 20 : 0) +
-                         (long)(LPR * NRG) * 8 + RPG;
+      const long score = (per_cta <= slots ? (1L << 21) - 1024L * per_cta : 0) + (long)(LPR * NRG) * 8 + RPG;
       if (score <= best) continue;
       best = score;
       found = true;
