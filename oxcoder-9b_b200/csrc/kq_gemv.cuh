@@ -271,10 +271,12 @@ __device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
 // then the norm reduction, then the exact digit split (integer rounding done on the FMA pipe).
 // MAXI bounds the prologue items per thread (8 columns each) the caller guarantees. A plain
 // (XS_PLAIN) prologue may be split into calls over item blocks it_base, it_base + MAXI, ...;
-// only the call with `last` ends with the barrier that publishes the planes.
-template <int MAXI = KQ_MAX_ITEMS>
-__device__ __forceinline__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem& L, int nthr_c,
-                                              int it_base = 0, bool last = true) {
+// only the call with `last` ends with the barrier that publishes the planes. With GPRE the norm
+// weights gm were loaded by the caller (gemv_load_gamma, before the dependency wait: they are
+// constants of the model, not outputs of the preceding kernel).
+template <int MAXI, bool GPRE>
+__device__ __forceinline__ void gemv_prologue_core(const GemvParams& P, uint8_t* smem, const GemvSmem& L, int nthr_c,
+                                                   int it_base, bool last, float (&gm)[MAXI][8]) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint4* xplanes = reinterpret_cast<uint4*>(smem + L.xplanes);
   float* xscal = reinterpret_cast<float*>(smem + L.xscal);
@@ -289,7 +291,6 @@ __device__ __forceinline__ void gemv_prologue(const GemvParams& P, uint8_t* smem
     }
   }
   float v[MAXI][8];
-  float gm[MAXI][8];
   // ---- loads (all issued before any use, the norm weights included)
 #pragma unroll
   for (int it = 0; it < MAXI; ++it) {
@@ -305,7 +306,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvParams& P, uint8_t* smem
           for (int i = 0; i < 8; ++i) v[it][i] = dequant_elem(P.emb, tok, col0 + i);
         }
       }
-      if (P.xmode != XS_PLAIN) load8(P.gamma + col0, gm[it]);
+      if (P.xmode != XS_PLAIN && !GPRE) load8(P.gamma + col0, gm[it]);
       if (P.xmode == XS_NORM) {
         float hv[8], yv[8];
         load8(P.h_in + col0, hv);
@@ -414,6 +415,26 @@ __device__ __forceinline__ void gemv_prologue(const GemvParams& P, uint8_t* smem
   }
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 7);
   if (last) named_bar(KQ_BAR_PROLOGUE, nthr_c);
+}
+
+template <int MAXI = KQ_MAX_ITEMS>
+__device__ __forceinline__ void gemv_prologue(const GemvParams& P, uint8_t* smem, const GemvSmem& L, int nthr_c,
+                                              int it_base = 0, bool last = true) {
+  float gm[MAXI][8];
+  gemv_prologue_core<MAXI, false>(P, smem, L, nthr_c, it_base, last, gm);
+}
+
+// The norm weights of this thread's prologue items (item blocks from 0), for gemv_prologue_core
+// with GPRE; nothing for a plain prologue.
+template <int MAXI = KQ_MAX_ITEMS>
+__device__ __forceinline__ void gemv_load_gamma(const GemvParams& P, int nthr_c, float (&gm)[MAXI][8]) {
+  if (P.xmode == XS_PLAIN) return;
+  const int nitems = P.LPR * 8;
+#pragma unroll
+  for (int it = 0; it < MAXI; ++it) {
+    const int item = threadIdx.x + it * nthr_c;
+    if (item < nitems) load8(P.gamma + item_col0(item), gm[it]);
+  }
 }
 
 // Sum over the LPR threads of a row group of RPG per-thread partials. For LPR >= 32 the warp
@@ -805,12 +826,14 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
   }
 
   // ------------------------------------------------------------------ consumers
+  float gm[KQ_MAX_ITEMS][8];
+  gemv_load_gamma(P, nthr_c, gm);   // constants: requested before the dependency wait
   pdl_wait();
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 1);
   GemvThread T;
   gemv_thread_init(P, smem, L, P.st ? P.st->pos : 0, T);
   gemv_load_rope(P, smem, L, T);
-  gemv_prologue(P, smem, L, nthr_c);
+  gemv_prologue_core<KQ_MAX_ITEMS, true>(P, smem, L, nthr_c, 0, true, gm);
   if (tid == 0) mbar_arrive(&pro_bar);
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 2);
   gemv_load_xs(P, smem, L, T);
