@@ -376,25 +376,33 @@ __device__ __forceinline__ void gemv_prologue_core(const GemvParams& P, uint8_t*
       if (m > 127.f * pow2f(e)) ++e;
     }
     const float s1 = pow2f(e), s2 = pow2f(e - 7), i1 = pow2f(-e), i2 = pow2f(7 - e), i3 = pow2f(14 - e);
-    uint32_t w[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+    // Every product below is by a power of two and exact (x1 s1 and x2 s2: small integers times
+    // normal powers of two), or so small that the integer rounding gives RND either way, so the
+    // fused forms equal the separate multiply and add.
+    int dq[3][8];
     int S0 = 0, S1 = 0, S2 = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float x = bad ? 0.f : v[it][i];
-      const float t1 = __fadd_rn(__fmul_rn(x, i1), RND);
+      const float t1 = __fmaf_rn(x, i1, RND);
       const float x1 = __fsub_rn(t1, RND);
-      const float r1 = __fsub_rn(x, __fmul_rn(x1, s1));
-      const float t2 = __fadd_rn(__fmul_rn(r1, i2), RND);
+      const float r1 = __fmaf_rn(-x1, s1, x);
+      const float t2 = __fmaf_rn(r1, i2, RND);
       const float x2 = __fsub_rn(t2, RND);
-      const float r2 = __fsub_rn(r1, __fmul_rn(x2, s2));
-      const float t3 = __fadd_rn(__fmul_rn(r2, i3), RND);
-      const int q1 = __float_as_int(t1) - 0x4B400000, q2 = __float_as_int(t2) - 0x4B400000,
-                q3 = __float_as_int(t3) - 0x4B400000;
-      S0 += q1; S1 += q2; S2 += q3;
-      w[0][i >> 2] |= (uint32_t)(q1 & 0xFF) << (8 * (i & 3));
-      w[1][i >> 2] |= (uint32_t)(q2 & 0xFF) << (8 * (i & 3));
-      w[2][i >> 2] |= (uint32_t)(q3 & 0xFF) << (8 * (i & 3));
+      const float r2 = __fmaf_rn(-x2, s2, r1);
+      const float t3 = __fmaf_rn(r2, i3, RND);
+      dq[0][i] = __float_as_int(t1) - 0x4B400000;
+      dq[1][i] = __float_as_int(t2) - 0x4B400000;
+      dq[2][i] = __float_as_int(t3) - 0x4B400000;
+      S0 += dq[0][i]; S1 += dq[1][i]; S2 += dq[2][i];
     }
+    uint32_t w[3][2];   // the low bytes (two's complement digits), four per word
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        w[p][j] = __byte_perm(__byte_perm((uint32_t)dq[p][4 * j], (uint32_t)dq[p][4 * j + 1], 0x0040),
+                              __byte_perm((uint32_t)dq[p][4 * j + 2], (uint32_t)dq[p][4 * j + 3], 0x0040), 0x5410);
 #pragma unroll
     for (int p = 0; p < 3; ++p)
       *reinterpret_cast<uint2*>(reinterpret_cast<uint32_t*>(&xplanes[(k * 3 + p) * LPR + u]) + half * 2) =
