@@ -669,8 +669,10 @@ __global__ void __launch_bounds__(DM_MERGE_THREADS) k_dattn_merge(const __grid_c
   __shared__ float s_o[NQ][HD];
   __shared__ float s_L;
   const int t = blockIdx.x, kv = blockIdx.y, g = blockIdx.z, tid = threadIdx.x, lane = tid & 31;
-  pdl_wait();
+  // the next kernel (the o GEMV) may become resident now and request its weights while the
+  // partials finish; it reads this kernel's output only after its own dependency wait
   pdl_trigger();
+  pdl_wait();
   const int ns = P.nsplit;
   const float* pb = P.part + ((size_t)t * P.n_kv + kv) * ns * G * PLD + (size_t)g * PLD;
   const int q = tid / HD, d = tid % HD, per = (ns + NQ - 1) / NQ, s0 = q * per, s1 = min(ns, s0 + per);
