@@ -494,6 +494,7 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
   __half* ksm = reinterpret_cast<__half*>(dm_sm);   // [2][DM_KB][BA_LD]
   __half* vsm = ksm + 2 * DM_KB * BA_LD;
   const int t = blockIdx.x, kv = blockIdx.y, sp = blockIdx.z, lane = threadIdx.x, grp = lane >> 2, t4 = lane & 3;
+  pdl_trigger();   // the merge may launch now; it reads the partials after its own dependency wait
   if (!P.st) pdl_wait();
   int n = (P.st ? P.st->pos : P.pos[t]) + 1;
   if (n > P.ctx || n < 1) {
@@ -531,7 +532,6 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
     cp_async_commit();
     pdl_wait();
   }
-  pdl_trigger();
   if (p0 < p1 && !pre0) load_block(p0, 0);
   cp_async_commit();
   // Q fragments: rows grp (a0, a2) and grp + 8 (a1, a3); rows >= G are zero
