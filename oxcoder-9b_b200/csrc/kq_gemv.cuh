@@ -836,11 +836,16 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
   // ------------------------------------------------------------------ consumers
   float gm[KQ_MAX_ITEMS][8];
   gemv_load_gamma(P, nthr_c, gm);   // constants: requested before the dependency wait
-  pdl_wait();
-  if (tid == 0) KQ_TRACE_AT(P.trace_id, 1);
+  // The step state (position, rotary position) and the rotary row are read before the
+  // dependency wait too: the state is written before a step starts (by the host, or by the
+  // previous step's output head), and a step's first kernel is launched with a full dependency
+  // on that writer. (After the wait, the in-order warps stalled on the position's round trip
+  // before issuing the prologue's loads.)
   GemvThread T;
   gemv_thread_init(P, smem, L, P.st ? P.st->pos : 0, T);
   gemv_load_rope(P, smem, L, T);
+  pdl_wait();
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 1);
   gemv_prologue_core<KQ_MAX_ITEMS, true>(P, smem, L, nthr_c, 0, true, gm);
   if (tid == 0) mbar_arrive(&pro_bar);
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 2);
