@@ -26,13 +26,21 @@ for p in (ROOT, PKG):
 
 METRIC = "batch-1 decode tok/s (ctx 4K) + spec-verify tok/s; Q4_K GEMV HBM GB/s vs peak"
 CTX = 4096
-# Algorithmic bytes: weights per token + one embedding row + norms; KV per position.
+# Algorithmic bytes of config-2: weights per token (32 layers + head + one embedding row + norms)
+# and K/V bytes per cached position (32 layers x 8 KV heads x 128 x fp16 x K and V).
 CFG2_WEIGHT_BYTES = 4434295040
 KV_BYTES_PER_POS = 131072
 CFG0_BYTES = 28311552 + 16384 + 49152        # W + x + y of the 12288 x 4096 Q4_K GEMV
-# DRAM read + write bytes of one config-0 GEMV launch, from the ncu capture summarised in
-# profiles/k_gemv_cfg0_q4k.md (same kernel and shape as the roofline leg below).
+# DRAM read + write bytes of one config-0 GEMV launch (same kernel and shape as the roofline leg
+# below), from an ncu capture of `bench.py --mode gemv-only`; this run does not measure it.
 CFG0_TRAFFIC = 28422912
+# Config-1 (one layer's MLP block): gate/up Q4_K 2 x 12288 x 4096 + down Q6_K 4096 x 12288 weight
+# bytes per block pass, activation bytes per row (x, the 12288-wide SwiGLU output written and
+# read, y), and flops per row (2 x 3 x 4096 x 12288 multiply-adds plus the element-wise work).
+CFG1_WEIGHT_BYTES = 97910784
+CFG1_ACT_BYTES_PER_ROW = 196608
+CFG1_FLOP_PER_ROW = 3.02e8
+CFG1_WIDTHS = (1, 4, 8, 16)
 
 
 def peaks():
@@ -87,41 +95,114 @@ class Clocks(object):
                 "reasons": reasons, "samples": len(rows)}
 
 
-def cpu_baseline(steps=1):
-    """The oracle (C restatement of the reference CPU path) on all host cores: one decode step of
-    config-2 at context 4K, after one warm-up step."""
+def host_cores():
+    """Physical cores of this host (the CPU legs use all of them, whatever OMP_NUM_THREADS a
+    launcher such as torchrun set), and the CPU model name."""
+    n = None
+    try:
+        import psutil
+        n = psutil.cpu_count(logical=False)
+    except Exception:
+        pass
+    n = n or os.cpu_count() or 1
+    try:
+        n = min(n, len(os.sched_getaffinity(0)))
+    except Exception:
+        pass
+    model = "unknown CPU"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except Exception:
+        pass
+    return n, model
+
+
+def cpu_decode_steps(steps, warmup):
+    """The oracle (C restatement of the reference CPU path) on all host cores: `warmup` untimed,
+    then `steps` timed greedy decode steps of config-2 at context 4K (K/V pre-filled). Returns
+    (per-step seconds, threads, model generation seconds)."""
     from oracle import oracle as O
     L = O.lib()
+    cores, _ = host_cores()
+    L.or_set_threads(cores)
     threads = L.or_get_threads()
     t0 = time.time()
     m = O.Model(seed=0, ctx=CTX)
     gen_s = time.time() - t0
-    pos = CTX - steps - 1
+    pos = CTX - steps - warmup - 1
     m.fill_kv(pos, 2)
-    m.step(1, pos)                       # warm-up (page-in)
-    t0 = time.perf_counter()
-    tok = 2
+    tok = 1
+    for i in range(warmup):
+        tok = m.step(tok, pos + i)
+    dts = []
     for i in range(steps):
-        tok = m.step(tok, pos + 1 + i)
-    dt = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        tok = m.step(tok, pos + warmup + i)
+        dts.append(time.perf_counter() - t0)
     m.close()
-    import platform
-    return {"value": steps / dt, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": "%d greedy decode step(s) of config-2 at ctx %d (KV pre-filled), OpenMP %d threads, %s; "
-                      "model generation %.1fs excluded" % (steps, CTX, threads, platform.processor() or platform.machine(), gen_s)}
+    return dts, threads, gen_s
+
+
+def ref_matvec_timing(reps=7):
+    """The reference's own kc_matvec (its kcpu4.c built unmodified into oracle/_ref) on the
+    config-0 Q4_K matrix, 12288 x 4096 in the Kindi pack layout: median of `reps` runs after one
+    warm-up, on all host cores and on one thread. None when the library is absent."""
+    from oracle import oracle as O
+    if O.ref_lib() is None:
+        return None
+    R, Cc = 12288, 4096
+    W = O.to_pack_layout(O.gen_matrix(R, Cc, 12, 0, 1000), R, Cc, 12)
+    x = O.gen_normal(Cc, 0.0, 1.0, 1, 1)
+    cores, model = host_cores()
+    out = {"kernel": "kc_matvec (reference kcpu4.c)", "shape": "Q4_K 12288 x 4096", "bytes": CFG0_BYTES, "cpu": model}
+    for th in (cores, 1):
+        O.lib().or_set_threads(th)
+        O.ref_matvec(W, R, Cc, 12, x)
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            O.ref_matvec(W, R, Cc, 12, x)
+            ts.append(time.perf_counter() - t0)
+        med = statistics.median(ts)
+        out["threads_%d" % th] = {"ms": 1e3 * med, "gbs": CFG0_BYTES / med / 1e9}
+    O.lib().or_set_threads(cores)
+    return out
+
+
+def cpu_baseline(steps=5):
+    """The CPU leg of the GPU line: the median of `steps` config-2 decode steps of the oracle port
+    after one warm-up, on all host cores, plus the reference's own kc_matvec on config-0."""
+    dts, threads, gen_s = cpu_decode_steps(steps, 1)
+    med = statistics.median(dts)
+    _, model = host_cores()
+    return {"value": 1.0 / med, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": "median of %d greedy decode steps of config-2 at ctx %d (KV pre-filled) after 1 warm-up, "
+                      "OpenMP %d threads on %s; model generation %.1fs excluded" % (steps, CTX, threads, model, gen_s),
+            "ref_kc_matvec_cfg0": ref_matvec_timing()}
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the reference's CPU path (the oracle port; kc_step cannot run the dense
+    config-2 model) timed on all host cores, `warmup` + `steps` decode steps, on rank 0 only."""
     if rank != 0:
         return 0
-    cb = cpu_baseline(steps=max(1, min(args.steps, 3)))
-    line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
+    dts, threads, gen_s = cpu_decode_steps(args.steps, args.warmup)
+    tot = sum(dts)
+    value = args.steps / tot
+    _, model = host_cores()
+    cb = {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+          "sample": "%d timed greedy decode steps of config-2 at ctx %d after %d warm-up, OpenMP %d threads on %s"
+                    % (args.steps, CTX, args.warmup, threads, model)}
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator, random-init weights)",
-            "config": {"workload": "config-2 batch-1 greedy decode, ctx 4K (KV pre-filled)", "global_batch": 1,
+            "config": {"workload": "config-2 batch-1 greedy decode at ctx 4K (KV pre-filled)", "global_batch": 1,
                        "seq_len": CTX, "parallelism": "cpu"},
             "impl": "reference", "cpu_baseline": cb,
-            "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -217,22 +298,27 @@ TP_PREFILL_FLOP = 2.0 * 6.1740e9 * TP_PROMPT + 4.0 * 32 * 128 * (TP_PROMPT ** 2)
 def tp_prefill_bench(kq, dist, rank, world, local, peak_tflops):
     """Config-4 prefill: one 8192-token prompt through the tensor-parallel model over all ranks
     (KV heads / FFN / vocabulary split, NCCL all-reduce after o and down), host-timed around the
-    synchronising kq_feed_batch on every rank, max over ranks."""
+    synchronising kq_feed_batch on every rank, max over ranks. World 1: the whole model on one GPU
+    (the same batched passes without collectives)."""
     import numpy as np
-    import torch
-    obj = [kq.tp_unique_id() if rank == 0 else None]
-    dist.broadcast_object_list(obj, src=0)
-    e = kq.Engine(kq.Config.default(ctx=TP_PROMPT + 256), device=local, seed=0, tp=(rank, world, obj[0]))
+    if world > 1:
+        import torch
+        obj = [kq.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        e = kq.Engine(kq.Config.default(ctx=TP_PROMPT + 256), device=local, seed=0, tp=(rank, world, obj[0]))
+    else:
+        e = kq.Engine(kq.Config.default(ctx=TP_PROMPT + 256), device=local, seed=0)
     ids = np.random.default_rng(1).integers(0, e.vocab, TP_PROMPT).astype(np.int32)
-    e.feed_batch(ids[:512], 0)   # warm-up
-    torch.cuda.synchronize()
-    dist.barrier()
+    e.feed_batch(ids[:512], 0)   # warm-up (the call synchronises)
+    if dist is not None:
+        dist.barrier()
     t0 = time.perf_counter()
     e.feed_batch(ids, 0)
     dt = time.perf_counter() - t0
-    t = torch.tensor([dt], device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dt = float(t.item())
+    if dist is not None:
+        t = torch.tensor([dt], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
     e.close()
     achieved = TP_PREFILL_FLOP / dt / 1e12
     return {"world": world, "prompt": TP_PROMPT, "ms": 1e3 * dt, "tok_s": TP_PROMPT / dt,
@@ -277,6 +363,23 @@ def tp_decode_bench(kq, dist, rank, world, local, hbm_gbs, steps=5, warmup=2):
             "tok_s": TP_DEC_SEQ * steps / dt,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs * world, "unit": "GB/s",
                          "frac": achieved / (hbm_gbs * world), "bytes_per_step": bytes_step}}
+
+
+def cfg1_bench(e, hbm_gbs, peak_tflops, n=96):
+    """Config-1: the MLP block (rmsnorm, gate/up Q4_K + SwiGLU, down Q6_K) of the config-2 model at
+    M = 1, 4, 8, 16 rows, device-resident, successive blocks on successive layers (3.1 GB of MLP
+    weights over the 32 layers, larger than L2); CUDA events, mean per block."""
+    out = {}
+    for M in CFG1_WIDTHS:
+        e.time_ffn_block(M, 32)
+        ms = e.time_ffn_block(M, n)
+        sec = ms * 1e-3
+        gbs = (CFG1_WEIGHT_BYTES + M * CFG1_ACT_BYTES_PER_ROW) / sec / 1e9
+        tfs = CFG1_FLOP_PER_ROW * M / sec / 1e12
+        out[str(M)] = {"us_per_block": 1e3 * ms, "rows_per_s": M / sec, "gbs": gbs, "hbm_frac": gbs / hbm_gbs,
+                       "tflops": tfs, "tensor_frac": tfs / peak_tflops,
+                       "path": "decode GEMVs (k_gemv)" if M == 1 else "batched tensor-core pass (k_bnorm + k_tmm)"}
+    return out
 
 
 def run_profile_mode(args):
@@ -354,6 +457,21 @@ def main():
     if args.impl == "reference":
         return run_reference(args, rank, world)
     args.warmup = max(3, args.warmup)
+    try:
+        return run_ours(args, rank, world, local)
+    except BaseException as ex:   # every rank says what failed, torchrun only prints a summary
+        import traceback
+        try:
+            import kq
+            kerr = kq.last_error()
+        except Exception:
+            kerr = ""
+        print(json.dumps({"rank": rank, "error": repr(ex), "kq_error": kerr,
+                          "traceback": traceback.format_exc()[-3000:]}), flush=True)
+        return 1
+
+
+def run_ours(args, rank, world, local):
     dist = None
     if world > 1:
         import torch
@@ -362,10 +480,12 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120))
 
-    import numpy as np
     import kq
 
     K, W = args.steps, args.warmup
+    pk = peaks()
+    hbm = pk["hbm_gbs"] if pk else 6650.0
+    tflops = pk["bf16_tflops"] if pk else 1590.0
     e = kq.Engine(kq.Config.default(ctx=CTX), device=local, seed=0)
     pos0 = CTX - (K + W) - 1
     e.fill_kv(pos0, 2)
@@ -388,6 +508,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     tok_s = world * K / (ms / 1000.0)
+    step_kernels = e.step_kernels()
 
     # ---- end to end through the public API (host token in / host token out per step)
     e.fill_kv(pos0, 2)
@@ -407,12 +528,13 @@ def main():
     e2e_tok_s = world * K / e2e_s
     spec = spec_bench(e, e.vocab, 8, 3)
     prefill = prefill_bench(e, e.vocab, 512)
+    cfg1 = cfg1_bench(e, hbm, tflops)
     e.close()
-    tp = tpd = None
+    tp = tp_prefill_bench(kq, dist, rank, world, local, tflops)
     if dist is not None:
-        pk0 = peaks()
-        tp = tp_prefill_bench(kq, dist, rank, world, local, pk0["bf16_tflops"] if pk0 else 1590.0)
-        tpd = tp_decode_bench(kq, dist, rank, world, local, pk0["hbm_gbs"] if pk0 else 6650.0)
+        tpd = tp_decode_bench(kq, dist, rank, world, local, hbm)
+    else:
+        tpd = {"world": 1, "infeasible": "64 sequences x 32768 positions of K/V are 274.9 GB, more than one GPU's HBM"}
 
     # ---- the dominant kernel: config-0 Q4_K GEMV over 16 rotating weight copies (453 MB > L2)
     mats = [kq.QMat(12, 12288, 4096, device=local).fill_synthetic(0, 1000 + i) for i in range(16)]
@@ -420,18 +542,16 @@ def main():
     gemv_ms = kq.time_matvec(mats, 512)
     for m in mats:
         m.close()
-    pk = peaks()
-    hbm = pk["hbm_gbs"] if pk else 6650.0
     gemv_gbs = CFG0_BYTES / (gemv_ms * 1e-3) / 1e9
     avg_ctx = pos0 + W + K / 2.0
     step_bytes = CFG2_WEIGHT_BYTES + KV_BYTES_PER_POS * avg_ctx
-    step_gbs = step_bytes * (K / (ms / 1000.0)) / 1e9 / 1.0
+    step_gbs = step_bytes * (K / (ms / 1000.0)) / 1e9
 
     if rank == 0:
         cb = None
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             try:
-                cb = cpu_baseline(steps=1)
+                cb = cpu_baseline(steps=5)
             except Exception as ex:  # the baseline must not hide the GPU line
                 cb = {"value": None, "unit": "tok/s", "cores": None, "kind": "port", "sample": "failed: %s" % ex}
         line = {
@@ -444,10 +564,12 @@ def main():
                        "l2": "inputs larger than L2 (%.2f GB of weights + KV per token)" % (step_bytes / 1e9)},
             "e2e": {"value": e2e_tok_s, "unit": "tok/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 16,
                     "api": "kq_step via ctypes, host-timed"},
-            "gpu_launches": (5 * 32 + 1) * K,
+            "gpu_launches": step_kernels * K,
+            "gpu_launches_per_step": step_kernels,
             "roofline": {"bound": "hbm", "kernel": "k_gemv (config-0 Q4_K 12288x4096, 16 rotating copies)",
                          "achieved": gemv_gbs, "peak": hbm, "unit": "GB/s", "frac": gemv_gbs / hbm,
-                         "traffic": CFG0_TRAFFIC, "peak_source": "measured" if pk else "fallback",
+                         "traffic": CFG0_TRAFFIC, "traffic_source": "ncu capture of the same kernel and shape, not measured by this run",
+                         "peak_source": "measured" if pk else "fallback",
                          "algorithmic_bytes_per_launch": CFG0_BYTES, "ms_per_launch": gemv_ms},
             "step_roofline": {"bound": "hbm", "achieved": step_gbs, "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm,
                               "bytes_per_token": step_bytes, "roofline_tok_s": hbm * 1e9 / step_bytes},
@@ -456,6 +578,7 @@ def main():
             "spec": spec,
             "prefill_tok_s": prefill["tok_s"] * world,
             "prefill": prefill,
+            "config1_mlp_block": cfg1,
             "tp_prefill": tp,
             "tp_decode": tpd,
             "cpu_baseline": cb,

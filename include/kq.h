@@ -108,6 +108,10 @@ int kq_hidden(kq_model* m, float* out);
 int kq_decode_loop(kq_model* m, int tok, int pos, int n, int32_t* out);
 /* Time n device-resident decode steps (CUDA events on the model's stream); returns ms. */
 int kq_time_decode(kq_model* m, int tok, int pos, int n, float* ms_out);
+/* Kernels one decode step launches (the kernel nodes of the step's CUDA graph; 1 for the
+ * persistent form), or < 0 on error. A measurement hook with no reference counterpart: the
+ * reference's CuPy engine launches its kernels one by one from Python (gpu4.py:50-110). */
+int kq_step_kernels(kq_model* m);
 
 /* ------------------------------------------------------------------ speculative verification
  * Draft-then-verify over a draft TREE (the reference verifies linear chains only: spec.py:790-793
@@ -174,6 +178,17 @@ int kq_qmat_matvec_dev(kq_qmat* a, const float* x_dev, float* y_dev, void* strea
 /* Time n launches of the matvec on device buffers, rotating over `ncopies` matrices (so the
  * weights are re-read from HBM); returns the mean launch ms measured with CUDA events. */
 int kq_time_matvec(kq_qmat* const* mats, int ncopies, int n, float* ms_out);
+
+/* ------------------------------------------------------------------ the MLP block (config-1)
+ * The feed-forward block of layer `layer` on M rows (1 <= M <= 128), the reference's ffn()
+ * (kcpu4.c:287-295) without its residual add: xn = rmsnorm(x) * ffn_norm (fp64 sum of squares,
+ * kcpu4.c:123-139), m = silu(gate xn) * (up xn) (kcpu4.c:292), y = down m. The reference runs it
+ * as M separate token steps (kc_matvec per matrix); here M = 1 is the decode GEMV pair and M >= 2
+ * one batched tensor-core pass. x and y are host [M][dim] floats. Whole models only. */
+int kq_ffn_block(kq_model* m, int layer, const float* x, int M, float* y);
+/* Time n blocks of M rows on device buffers, block i on layer i % n_layers (the weights stream
+ * from HBM); mean ms per block from CUDA events. */
+int kq_time_ffn_block(kq_model* m, int M, int n, float* ms_out);
 /* Bytes the device layout of this matrix occupies (equal to the GGUF bytes). */
 size_t kq_qmat_bytes(const kq_qmat* a);
 

@@ -490,6 +490,25 @@ static void or_ffn(OModel* m, OLayer* L){
   or_matvec(&L->down, m->m, m->y);
 }
 
+/* The MLP block of layer `layer` on M rows of x (row-major [M][D]) into y [M][D]: the steps of
+ * ffn() (kcpu4.c:287-295) without the residual add -- xn = rmsnorm(x) * ffn_norm, gate and up
+ * matvecs, silu(g) * u, the down matvec -- one row after another as the reference runs tokens.
+ * Uses the model's scratch (h, xn, g, u, m); returns 0, or -3 on bad arguments. */
+int or_ffn_block(OModel* m, int layer, const float* x, int M, float* y){
+  if(layer < 0 || layer >= m->c.NL || M < 1) return -3;
+  OLayer* L = m->L + layer;
+  const int D = m->c.D;
+  for(int r = 0; r < M; r++){
+    memcpy(m->h, x + (size_t)r * D, (size_t)D * sizeof(float));
+    or_rmsnorm(m->h, NULL, 0, L->ffn_norm, m->xn, D, m->c.eps);
+    or_matvec(&L->gate, m->xn, m->g);
+    or_matvec(&L->up, m->xn, m->u);
+    for(int e = 0; e < m->c.NFF; e++) m->m[e] = or_silu(m->g[e]) * m->u[e];
+    or_matvec(&L->down, m->m, y + (size_t)r * D);
+  }
+  return 0;
+}
+
 /* One token (kcpu4.c:303-335 structure). head != 0: logits into m->logits and the greedy id
  * (strict > scan, first index wins) is returned; head == 0 returns -1 and leaves h = residual. */
 static int or_step_t(OModel* m, int tok, int pos, int head, const OTree* tr){

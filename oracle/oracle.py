@@ -85,6 +85,8 @@ def lib():
         L.or_attn_scale.restype = C.c_float
         L.or_verify.argtypes = [C.c_void_p, PI32, PI32, C.c_int, C.c_int, PF, PI32]
         L.or_verify.restype = C.c_int
+        L.or_ffn_block.argtypes = [C.c_void_p, C.c_int, PF, C.c_int, PF]
+        L.or_ffn_block.restype = C.c_int
         L.or_commit.argtypes = [C.c_void_p, PI32, C.c_int, C.c_int]
         L.or_commit.restype = C.c_int
         L.or_accept.argtypes = [PF, PF, PI32, PI32, C.c_int, C.c_int, C.c_float, PF, PF, PI32, PI32]
@@ -221,6 +223,14 @@ class Model(object):
         if self.L.or_verify(self.h, ptr(t, PI32), ptr(par, PI32), n, int(pos), ptr(logits), ptr(best, PI32)):
             raise ValueError("oracle: bad verify arguments")
         return best, logits
+
+    def ffn_block(self, layer, X):
+        """or_ffn_block: the MLP block of `layer` on the rows of X [M, D]."""
+        X = np.ascontiguousarray(X, np.float32)
+        Y = np.empty_like(X)
+        if self.L.or_ffn_block(self.h, int(layer), ptr(X), X.shape[0], ptr(Y)):
+            raise ValueError("oracle: bad MLP block arguments")
+        return Y
 
     def commit(self, path, pos):
         p = np.ascontiguousarray(path, np.int32)

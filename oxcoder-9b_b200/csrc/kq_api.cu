@@ -135,13 +135,26 @@ struct kq_qmat {
 
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Shape rule of every quantised matrix: whole 8-row tiles, whole super-blocks, and at most 12288
+// columns (the widest activation vector the digit-plane prologue and the packed batched-pass
+// input hold). The tensor-core GEMM of the batched passes takes any such shape.
 static int check_shape(int type, int R, int C) {
   if (type != KQ_Q4_K && type != KQ_Q6_K) return set_err(KQ_ERR_ARG, "tensor type must be 12 (Q4_K) or 14 (Q6_K)");
   if (R <= 0 || C <= 0 || R % 8 || C % 256)
     return set_err(KQ_ERR_ARG, "Invalid packed tensor dimensions: rows must be a positive multiple of 8 and cols of 256");
+  if (C > 12288) return set_err(KQ_ERR_ARG, "unsupported column count (at most 12288)");
+  return KQ_OK;
+}
+
+// Extra rule of the single-token GEMV (k_gemv, k_tmv, the persistent kernel): a row's C/64
+// threads reduce by warp shuffles within a power-of-two segment of a warp (4, 8, 16 threads) or
+// over whole warps (a multiple of 32), so C is 256, 512, 1024 or a multiple of 2048. A
+// tensor-parallel shard whose slice breaks it (1536 or 3072 FFN columns) only runs the batched
+// pass.
+static int check_gemv_cols(int C) {
   const int LPR = 4 * (C / 256);
   if (!(LPR == 4 || LPR == 8 || LPR == 16 || (LPR % 32 == 0 && LPR <= 192)))
-    return set_err(KQ_ERR_ARG, "unsupported column count (need 256, 512, 1024 or a multiple of 2048 up to 12288)");
+    return set_err(KQ_ERR_ARG, "the single-token GEMV needs 256, 512, 1024 or a multiple of 2048 columns up to 12288");
   return KQ_OK;
 }
 
@@ -279,6 +292,7 @@ static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParam
   if (nseg < 1 || nseg > KQ_MAX_SEG) return set_err(KQ_ERR_ARG, "bad segment count");
   int types[KQ_MAX_SEG], rows[KQ_MAX_SEG];
   const int C = ss[0].m->C;
+  if (check_gemv_cols(C) != KQ_OK) return KQ_ERR_ARG;
   for (int i = 0; i < nseg; ++i) {
     if (ss[i].m->C != C) return set_err(KQ_ERR_ARG, "fused GEMV segments must share the column count");
     types[i] = ss[i].m->type;
@@ -313,6 +327,7 @@ static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParam
 static int fill_gemv_dec(const SegSpec* ss, int nseg, GemvParams& p, int& stage_bytes) {
   if (nseg < 1 || nseg > KQ_MAX_SEG) return set_err(KQ_ERR_ARG, "bad segment count");
   const int C = ss[0].m->C, G = C / 256, LPR = 4 * G;
+  if (check_gemv_cols(C) != KQ_OK) return KQ_ERR_ARG;
   int rowb = 0;
   for (int i = 0; i < nseg; ++i) {
     if (ss[i].m->C != C) return set_err(KQ_ERR_ARG, "fused GEMV segments must share the column count");
@@ -497,6 +512,7 @@ struct kq_model {
   float *apart = nullptr, *apart_ml = nullptr;
   int* aticket = nullptr;
   cudaGraphExec_t g_step = nullptr, g_feed = nullptr;
+  int step_kernels = 0;             // kernel nodes of the decode-step graph
   // persistent decode kernel (k_decode): phase table, arrival counters, launch shape
   bool persist = true;
   PhaseDesc* d_phases = nullptr;
@@ -598,8 +614,10 @@ static int validate_cfg(const kq_config& c) {
                            {c.t_v, c.n_kv_heads * c.head_dim, c.dim}, {c.t_o, c.dim, c.n_heads * c.head_dim},
                            {c.t_gate, 2 * c.ffn, c.dim}, {c.t_down, c.dim, c.ffn},
                            {c.t_emb, c.vocab, c.dim}, {c.t_out, c.vocab, c.dim}};
+  // the whole model runs the single-token GEMV in its decode graph (tensor-parallel shards are
+  // checked by qmat_alloc with the generic rule only)
   for (auto& s : shapes)
-    if (check_shape(s[0], s[1], s[2]) != KQ_OK) return KQ_ERR_ARG;
+    if (check_shape(s[0], s[1], s[2]) != KQ_OK || check_gemv_cols(s[2]) != KQ_OK) return KQ_ERR_ARG;
   return KQ_OK;
 }
 
@@ -1059,9 +1077,10 @@ static int build_step(kq_model* m, bool head, bool persist, std::vector<StepOp>&
   return KQ_OK;
 }
 
-// A launch that may start while the previous kernel on the stream finishes (it waits in-kernel).
+// A launch that may start while the previous kernel on the stream finishes (it waits in-kernel);
+// pdl = false: an ordinary launch that starts after the previous work on the stream.
 template <class K, class PT>
-static cudaError_t launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const PT& p) {
+static cudaError_t launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const PT& p, bool pdl = true) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -1071,7 +1090,7 @@ static cudaError_t launch_pdl(K kern, dim3 grid, dim3 block, size_t smem, cudaSt
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 // Decode attention on the tensor cores: grid (token, KV head, split), merge per (token, KV head).
@@ -1082,6 +1101,10 @@ static cudaError_t launch_dattn_t(const DAttnParams& P, int M, int nkv, cudaStre
   return launch_pdl(k_dattn_merge<G>, dim3((unsigned)M, (unsigned)nkv, (unsigned)G), dim3(DM_MERGE_THREADS), 0, s, P);
 }
 
+// The step's first kernel (the q/k/v GEMV that embeds the token) is launched without the PDL
+// attribute: the GEMV prologues read the step state (token, position) before their dependency
+// wait, which is only safe when the host's state upload has completed before the kernel starts.
+// Every later kernel reads state that an earlier kernel of the same step does not write.
 static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
   std::vector<StepOp> ops;
   int rc = build_step(m, head, false, ops);
@@ -1090,7 +1113,7 @@ static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
   bool first = true;
   for (const StepOp& op : ops) {
     if (op.kind == PH_GEMV) {
-      if (op.tmv) CU(launch_pdl(k_tmv, op.tgrid, dim3(TV_THREADS), (size_t)op.t.smem, s, op.t));
+      if (op.tmv) CU(launch_pdl(k_tmv, op.tgrid, dim3(TV_THREADS), (size_t)op.t.smem, s, op.t, !first));
       else CU(launch_gemv(op.g, op.pl, s, !first));
     } else if (m->attn_mode == 1) {
       CU(attn_cl_fn(G, m->attn_cl)(op.a.a, s, true));
@@ -1216,6 +1239,17 @@ static int build_graph(kq_model* m, bool head, cudaGraphExec_t* out) {
   cudaError_t e = cudaStreamEndCapture(m->stream, &g);
   if (rc) { if (g) cudaGraphDestroy(g); return rc; }
   if (e != cudaSuccess) return set_err(KQ_ERR_BACKEND, std::string("graph capture: ") + cudaGetErrorString(e));
+  size_t nn = 0;
+  if (head && cudaGraphGetNodes(g, nullptr, &nn) == cudaSuccess) {   // kernels of one decode step
+    std::vector<cudaGraphNode_t> nodes(nn);
+    int kernels = 0;
+    if (nn && cudaGraphGetNodes(g, nodes.data(), &nn) == cudaSuccess)
+      for (cudaGraphNode_t n : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(n, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+      }
+    m->step_kernels = kernels;
+  }
   e = cudaGraphInstantiate(out, g, 0);
   cudaGraphDestroy(g);
   if (e != cudaSuccess) return set_err(KQ_ERR_BACKEND, std::string("graph instantiate: ") + cudaGetErrorString(e));
@@ -1399,6 +1433,13 @@ extern "C" int kq_decode_loop(kq_model* m, int tok, int pos, int n, int32_t* out
   CU(cudaMemcpyAsync(out, m->out_ids, (size_t)n * sizeof(int32_t), cudaMemcpyDeviceToHost, m->stream));
   CU(cudaStreamSynchronize(m->stream));
   return check_dev_err(m);
+}
+
+extern "C" int kq_step_kernels(kq_model* m) {
+  int rc = model_check(m);
+  if (rc || (rc = not_tp(m, "kq_step_kernels"))) return rc;
+  if ((rc = ensure_graphs(m))) return rc;
+  return m->persist ? 1 : m->step_kernels;
 }
 
 extern "C" int kq_time_decode(kq_model* m, int tok, int pos, int n, float* ms_out) {
@@ -2167,6 +2208,109 @@ extern "C" int kq_time_matvec(kq_qmat* const* mats, int ncopies, int n, float* m
   cudaFree(xd);
   cudaFree(yd);
   if (!rc) rc = dev_err_check(a->device);
+  return rc;
+}
+
+// ------------------------------------------------------------------------------ the MLP block
+// Config-1's block on M rows of a layer's weights (the reference's ffn(), kcpu4.c:287-295, without
+// its residual add): xn = rmsnorm(x) * ffn_norm, m = silu(gate xn) * (up xn), y = down m.
+// M = 1: the decode graph's two GEMVs (norm in the gate/up prologue, SwiGLU in its epilogue);
+// M >= 2: the batched pass (k_bnorm, then the tensor-core GEMM of gate/up with the SwiGLU
+// epilogue writing the packed input of the down GEMM). x_dev is read and rewritten unchanged by
+// the batched norm; y_dev receives M x dim floats.
+static int ffn_block_enqueue(kq_model* m, int layer, float* x_dev, int M, float* y_dev, bool pdl) {
+  const kq_config& c = m->c;
+  LayerW& w = m->L[layer];
+  cudaStream_t s = m->stream;
+  if (M == 1) {
+    StepOp g1, g2;
+    const SegSpec sg[1] = {{w.gu, EPI_SWIGLU, m->mbuf, nullptr}};
+    const SegSpec sd[1] = {{w.down, EPI_F32, y_dev, nullptr}};
+    int rc = fill_gemv(sg, 1, true, m->nsm, g1.g, g1.pl);
+    if (rc || (rc = fill_gemv(sd, 1, false, m->nsm, g2.g, g2.pl))) return rc;
+    for (GemvParams* p : {&g1.g, &g2.g}) {
+      p->st = m->st; p->vocab = c.vocab; p->hd = c.head_dim; p->ctx = c.ctx; p->err = m->err; p->eps = c.eps;
+    }
+    g1.g.xmode = XS_NORM; g1.g.h_in = x_dev; g1.g.gamma = w.ffn_norm;
+    g2.g.xmode = XS_PLAIN; g2.g.x = m->mbuf;
+    CU(launch_gemv(g1.g, g1.pl, s, pdl));
+    CU(launch_gemv(g2.g, g2.pl, s, true));
+    return KQ_OK;
+  }
+  BNormParams P;
+  std::memset(&P, 0, sizeof(P));
+  P.M = M; P.D = c.dim; P.h = x_dev; P.gamma = w.ffn_norm; P.eps = c.eps;
+  P.xp = m->bxd; P.Npad = (M + 15) & ~15; P.vocab = c.vocab; P.err = m->err;
+  CU(launch_pdl(k_bnorm, dim3((unsigned)M), dim3(BN_THREADS), 0, s, P, pdl));
+  BatchParams B;
+  B.M = M; B.slot = m->bslot; B.rpos = m->brpos; B.mask = m->bmask; B.tree_base = 0; B.seq = nullptr;
+  const SegSpec sg[1] = {{w.gu, EPI_SWIGLU, nullptr, nullptr}};
+  const SegSpec sd[1] = {{w.down, EPI_F32, y_dev, nullptr}};
+  int rc = launch_tmm(m, sg, 1, m->bxd, m->bxf, 0, B);
+  if (rc || (rc = launch_tmm(m, sd, 1, m->bxf, nullptr, c.dim, B))) return rc;
+  return KQ_OK;
+}
+
+static int ffn_block_check(kq_model* m, int layer, int M) {
+  int rc = model_check(m);
+  if (rc || (rc = not_tp(m, "the MLP block"))) return rc;
+  if (layer < 0 || layer >= m->c.n_layers) return set_err(KQ_ERR_ARG, "layer out of range");
+  if (M < 1 || M > MM_MAXM) return set_err(KQ_ERR_ARG, "rows must be in 1 .. 128");
+  if (M > 1 && !batch_supported(m)) return set_err(KQ_ERR_ARG, "the batched pass does not cover this configuration");
+  if (M > 1 && (rc = batch_buffers(m))) return rc;
+  return KQ_OK;
+}
+
+extern "C" int kq_ffn_block(kq_model* m, int layer, const float* x, int M, float* y) {
+  int rc = ffn_block_check(m, layer, M);
+  if (rc) return rc;
+  if (!x || !y) return set_err(KQ_ERR_ARG, "null argument");
+  const size_t n = (size_t)M * m->c.dim;
+  float *xd = nullptr, *yd = nullptr;
+  if (cudaMalloc(&xd, n * 4) != cudaSuccess || cudaMalloc(&yd, n * 4) != cudaSuccess) {
+    cudaFree(xd);
+    return set_err(KQ_ERR_MEMORY, "MLP block buffers");
+  }
+  if (cudaMemcpyAsync(xd, x, n * 4, cudaMemcpyHostToDevice, m->stream) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "MLP block upload");
+  if (!rc) rc = ffn_block_enqueue(m, layer, xd, M, yd, false);
+  if (!rc && cudaMemcpyAsync(y, yd, n * 4, cudaMemcpyDeviceToHost, m->stream) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "MLP block download");
+  if (cudaStreamSynchronize(m->stream) != cudaSuccess && !rc) rc = set_err(KQ_ERR_BACKEND, "MLP block");
+  cudaFree(xd);
+  cudaFree(yd);
+  if (!rc) rc = check_dev_err(m);
+  return rc;
+}
+
+extern "C" int kq_time_ffn_block(kq_model* m, int M, int n, float* ms_out) {
+  int rc = ffn_block_check(m, 0, M);
+  if (rc) return rc;
+  if (n < 1 || !ms_out) return set_err(KQ_ERR_ARG, "bad timing arguments");
+  const size_t nx = (size_t)M * m->c.dim;
+  float *xd = nullptr, *yd = nullptr;
+  if (cudaMalloc(&xd, nx * 4) != cudaSuccess || cudaMalloc(&yd, nx * 4) != cudaSuccess) {
+    cudaFree(xd);
+    return set_err(KQ_ERR_MEMORY, "MLP block buffers");
+  }
+  gen_normal_dev(xd, (long long)nx, 0.f, 1.f, 1, 77, m->stream);
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  // successive blocks use successive layers' weights, so a run longer than the layer count
+  // streams the whole model's MLP weights (3.1 GB for config-2) instead of an L2-resident layer
+  const int L = m->c.n_layers;
+  for (int i = 0; i < std::min(n, 2 * L) && !rc; ++i) rc = ffn_block_enqueue(m, i % L, xd, M, yd, i > 0);
+  if (!rc && cudaEventRecord(e0, m->stream) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "event");
+  for (int i = 0; i < n && !rc; ++i) rc = ffn_block_enqueue(m, i % L, xd, M, yd, true);
+  if (!rc && cudaEventRecord(e1, m->stream) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "event");
+  if (!rc && cudaEventSynchronize(e1) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "MLP block timing");
+  float ms = 0.f;
+  if (!rc) cudaEventElapsedTime(&ms, e0, e1);
+  *ms_out = ms / (float)n;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFree(xd);
+  cudaFree(yd);
+  if (!rc) rc = check_dev_err(m);
   return rc;
 }
 

@@ -77,6 +77,9 @@ SIGNATURES = {
     "kq_hidden": (C.c_int, [C.c_void_p, PF]),
     "kq_decode_loop": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, PI32]),
     "kq_time_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, PF]),
+    "kq_step_kernels": (C.c_int, [C.c_void_p]),
+    "kq_ffn_block": (C.c_int, [C.c_void_p, C.c_int, PF, C.c_int, PF]),
+    "kq_time_ffn_block": (C.c_int, [C.c_void_p, C.c_int, C.c_int, PF]),
     "kq_qmat_create": (C.c_void_p, [C.c_int, C.c_int, C.c_int, C.c_int]),
     "kq_qmat_free": (None, [C.c_void_p]),
     "kq_qmat_upload": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
@@ -392,6 +395,25 @@ class Engine(object):
         """K/V compaction of an accepted path (path[0] = 0)."""
         p = np.ascontiguousarray(path, np.int32)
         check(lib().kq_commit(self.h, _ptr(p, PI32), len(p) - 1, int(pos)))
+
+    def ffn_block(self, layer, X):
+        """The MLP block of `layer` (rmsnorm, gate/up + SwiGLU, down) on the rows of X [M, dim]."""
+        X = _f32(X)
+        if X.ndim != 2 or X.shape[1] != self.config.dim:
+            raise ValueError("X must be [M, %d]" % self.config.dim)
+        Y = np.empty_like(X)
+        check(lib().kq_ffn_block(self.h, int(layer), _ptr(X), X.shape[0], _ptr(Y)))
+        return Y
+
+    def time_ffn_block(self, M, n):
+        """Mean ms per MLP block of M rows over n blocks (successive layers' weights)."""
+        ms = C.c_float()
+        check(lib().kq_time_ffn_block(self.h, int(M), int(n), C.byref(ms)))
+        return ms.value
+
+    def step_kernels(self):
+        """Kernels one decode step launches (kernel nodes of the step graph)."""
+        return check(lib().kq_step_kernels(self.h))
 
     def time_decode(self, tok, pos, n):
         ms = C.c_float()

@@ -1,7 +1,7 @@
 """Generates tests/golden/quant_golden.npz from the REFERENCE implementation.
 
-Run once in a container that has the reference tree (read-only) and oracle/_ref built:
-    python tests/golden/make_golden.py [/path/to/reference]
+Run once on a host that has the reference tree (read-only) and oracle/_ref built:
+    python tests/golden/make_golden.py /path/to/reference      (or set KQ_REFERENCE)
 
 Sources of truth:
   - the reference's numpy block decoder, scripts/kindi_q4/kindi/q4pack.py:52-76 (decode_blocks)
@@ -27,7 +27,7 @@ sys.path.insert(0, ROOT)
 from oracle import oracle as O  # noqa: E402
 
 
-def main(ref_root="/root/reference"):
+def main(ref_root):
     sys.path.insert(0, os.path.join(ref_root, "scripts", "kindi_q4"))
     from kindi.q4pack import decode_blocks, BLOCK  # the reference's numpy decoder
     assert O.ref_lib() is not None, "build oracle/_ref first (make -C oracle)"
@@ -87,4 +87,7 @@ def main(ref_root="/root/reference"):
 
 
 if __name__ == "__main__":
-    main(*sys.argv[1:])
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KQ_REFERENCE")
+    if not root:
+        sys.exit("usage: make_golden.py /path/to/reference   (or set KQ_REFERENCE)")
+    main(root)

@@ -102,14 +102,18 @@ def test_bad_shapes_rejected(kq):
 # operands with fp32 accumulation, checked row by row against the oracle's fp32 matvec. Shapes
 # cover one and many row tiles of 128, partial tiles, single and split-K launches, both types.
 MM_SHAPES = [(12, 128, 256), (14, 128, 512), (12, 256, 4096), (14, 1024, 4096), (12, 6144, 4096),
-             (14, 4096, 12288), (12, 200, 1024), (14, 24, 2048), (12, 12288, 4096)]
+             (14, 4096, 12288), (12, 200, 1024), (14, 24, 2048), (12, 12288, 4096),
+             (14, 4096, 3072), (14, 4096, 1536)]   # the down shards of 4- and 8-way tensor parallelism
 
 
-@pytest.mark.parametrize("M", [2, 5, 16, 45, 64])
+# Token counts: config-1's speculative-verify widths 4, 8, 16 (and M = 1, the GEMV, above), the
+# 45 nodes of config-3's draft tree, and others for partial MMA tiles. The three large shapes
+# (config-1's 12288 x 4096 Q4_K and 4096 x 12288 Q6_K, and 6144 x 4096) run the config widths and 45.
+@pytest.mark.parametrize("M", [2, 4, 5, 8, 16, 45, 64])
 @pytest.mark.parametrize("ty,R,Cc", MM_SHAPES)
 def test_matmul_parity(kq, oracle, ty, R, Cc, M):
-    if R * Cc > 4096 * 4096 and M not in (16, 45):
-        pytest.skip("large shapes at two token counts")
+    if R * Cc > 4096 * 4096 and M not in (4, 8, 16, 45):
+        pytest.skip("large shapes at the config widths")
     W = oracle.gen_matrix(R, Cc, ty, 0, 300 + R)
     X = np.stack([oracle.gen_normal(Cc, 0.0, 1.0, 1, 1000 * M + i) for i in range(M)])
     m = kq.QMat(ty, R, Cc).upload(W)
@@ -134,3 +138,18 @@ def test_matmul_rows_independent_of_batch(kq, oracle):
     X2[1:] = np.stack([oracle.gen_normal(Cc, 0.0, 3.0, 1, 90 + i) for i in range(7)])
     Y2 = m.matmul(X2)
     assert np.array_equal(Y8[0], Y2[0])
+
+
+def test_gemv_rule_only_binds_the_single_token_gemv(kq, oracle):
+    """1536 and 3072 columns (the down-projection shards of 8- and 4-way tensor parallelism) are
+    valid matrices for the batched GEMM but not for the single-token GEMV, whose rows reduce over
+    power-of-two warp segments or whole warps: matvec refuses them with ValueError."""
+    for Cc in (1536, 3072):
+        W = oracle.gen_matrix(16, Cc, 14, 0, 7)
+        m = kq.QMat(14, 16, Cc).upload(W)
+        with pytest.raises(ValueError):
+            m.matvec(np.ones(Cc, np.float32))
+        X = np.stack([oracle.gen_normal(Cc, 0.0, 1.0, 1, 3 + i) for i in range(2)])
+        Y = m.matmul(X)
+        for i in range(2):
+            assert rel_l2(Y[i], oracle.matvec(W, 16, Cc, 14, X[i])) < TIGHT_L2

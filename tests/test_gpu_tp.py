@@ -4,8 +4,9 @@ Each rank is a process on its own GPU holding its shard (KV heads, FFN slice, vo
 joined by NCCL; the batched pass all-reduces the o and down partials and all-gathers the head's
 argmax. Bars: every rank's K/V cache heads after a prefill within 1e-3 rel-L2 of the same heads
 of the whole model on one GPU, the greedy steps that follow identical, and batched decode of three
-sequences (kq_batch_*) giving the whole model's ids. Skips with fewer
-than two GPUs (the round-end suite runs on one); run under `gpurun --gpus 2`."""
+sequences (kq_batch_*) giving the whole model's ids. Worlds 2, 4 and 8 each skip when the
+host has fewer GPUs. The FFN of 12288 gives the per-rank down-projection widths of config-4:
+6144, 3072 and 1536 input columns."""
 import multiprocessing as mp
 import os
 import sys
@@ -17,7 +18,7 @@ from conftest import rel_l2
 
 pytestmark = pytest.mark.gpu
 
-CFG = dict(D=1024, NL=2, NH=8, NKV=2, HD=128, NFF=2048, vocab=4096, ctx=512)
+CFG = dict(D=1024, NL=2, NH=32, NKV=8, HD=128, NFF=12288, vocab=4096, ctx=512)
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(os.path.dirname(HERE), "oxcoder-9b_b200")
 
@@ -66,7 +67,7 @@ def kq():
     return K
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_prefill_and_steps_match_whole_model(kq, world):
     if kq.lib().kq_device_count() < world:
         pytest.skip("needs %d GPUs" % world)

@@ -157,3 +157,26 @@ def test_oracle_chain_verify_equals_steps(oracle):
     m.fill_kv(10, 1)
     best, _ = m.verify(chain, [-1, 0, 1, 2, 3], 10)
     assert list(best[:-1]) == chain[1:]
+
+
+def test_ffn_block_matches_numpy(oracle):
+    """or_ffn_block (config-1's block: kcpu4.c:287-295 without the residual add) against a numpy
+    fp64 restatement from the same tensors: rmsnorm, gate/up, silu(g) * u, down."""
+    t = dict(TINY, NL=1)
+    m = oracle.Model(seed=0, **t)
+    D, F = t["D"], t["NFF"]
+    X = np.stack([oracle.gen_normal(D, 0.0, 1.0, 1, 40 + i) for i in range(3)])
+    Y = m.ffn_block(0, X)
+
+    def mat(kind, R, Cc, ty):
+        W = np.ctypeslib.as_array(oracle.lib().or_model_tensor(m.h, 0, kind), shape=(R * (Cc // 256) * oracle.BLOCK[ty],))
+        return oracle.decode_blocks(W.reshape(-1, oracle.BLOCK[ty]), ty).reshape(R, Cc).astype(np.float64)
+    Wg, Wu, Wd = mat(oracle.T_GATE, F, D, 12), mat(oracle.T_UP, F, D, 12), mat(oracle.T_DOWN, D, F, 14)
+    gamma = oracle.gen_normal(D, 1.0, 0.02, 0, oracle.stream(0, oracle.T_FFN_NORM)).astype(np.float64)
+    for i in range(3):
+        x = X[i].astype(np.float64)
+        xn = x / np.sqrt(np.mean(x * x) + 1e-6) * gamma
+        g, u = Wg @ xn, Wu @ xn
+        ref = Wd @ (g / (1.0 + np.exp(-g)) * u)
+        assert rel_l2(Y[i], ref) < 1e-5, i
+    m.close()
