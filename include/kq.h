@@ -67,6 +67,19 @@ void kq_config_default(kq_config* cfg);              /* BASELINE config-2 */
 kq_model* kq_model_create(const kq_config* cfg, int device);   /* NULL on failure, see kq_error */
 void kq_model_free(kq_model* m);
 
+/* Kindi Q4 packs (a repacked GGUF directory: kindi_pack.json, index.json, weights.bin in the 8-row
+ * interleave, f32.bin; scripts/kindi_q4/kindi/q4pack.py:110-180). The manifest, file sizes,
+ * SHA-256 digests (skipped when KINDI_Q4_VERIFY=size), tensor set, shapes, types and spans are
+ * checked before anything is allocated, as verify_pack does (q4pack.py:86-108). The manifest's
+ * `dimensions` describe the dense GQA decoder (layers, width, ffn, heads, kv_heads, head_dim,
+ * rope_dim = head_dim, rope_base, optional norm_eps, full_attention_interval 1); the reference's
+ * hybrid GDN profile is rejected with KQ_ERR_ARG.
+ * kq_pack_read_config: validate only (no GPU) and return the model configuration for context ctx.
+ * kq_model_load_pack: validate, create the model on `device` and upload every tensor (make_engine,
+ * engine.py:369-381, with gpu4.Engine's weight upload, gpu4.py:51-90). NULL on failure. */
+int kq_pack_read_config(const char* dir, int ctx, kq_config* out);
+kq_model* kq_model_load_pack(const char* dir, int ctx, int device);
+
 /* ------------------------------------------------------------------ tensor parallelism
  * One process per GPU. A shard holds KV heads [r*nkv/W, (r+1)*nkv/W) with their query heads
  * (q/k/v rows, o input columns, K/V cache), the FFN slice r (gate/up rows, down input columns) and

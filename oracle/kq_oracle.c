@@ -589,6 +589,7 @@ int or_commit(OModel* m, const int* path, int k, int pos){
 /* Accessors for ctypes callers. */
 float* or_model_logits(OModel* m){ return m->logits; }
 float* or_model_hidden(OModel* m){ return m->h; }
+float* or_model_swiglu(OModel* m){ return m->m; }   /* SwiGLU output of the last layer run */
 uint16_t* or_model_kcache(OModel* m, int layer){ return m->L[layer].Kc; }
 uint16_t* or_model_vcache(OModel* m, int layer){ return m->L[layer].Vc; }
 const uint8_t* or_model_tensor(OModel* m, int layer, int kind){

@@ -74,6 +74,8 @@ def lib():
         L.or_model_logits.restype = PF
         L.or_model_hidden.argtypes = [C.c_void_p]
         L.or_model_hidden.restype = PF
+        L.or_model_swiglu.argtypes = [C.c_void_p]
+        L.or_model_swiglu.restype = PF
         L.or_model_kcache.argtypes = [C.c_void_p, C.c_int]
         L.or_model_kcache.restype = PU16
         L.or_model_vcache.argtypes = [C.c_void_p, C.c_int]
@@ -204,6 +206,10 @@ class Model(object):
 
     def hidden(self):
         return np.ctypeslib.as_array(self.L.or_model_hidden(self.h), shape=(self.cfg.D,)).copy()
+
+    def swiglu(self):
+        """The SwiGLU output (silu(gate) * up, NFF floats) of the last layer of the last step."""
+        return np.ctypeslib.as_array(self.L.or_model_swiglu(self.h), shape=(self.cfg.NFF,)).copy()
 
     def kcache(self, layer, npos):
         n = npos * self.cfg.NKV * self.cfg.HD

@@ -15,8 +15,12 @@
 #include "kq_batch.cuh"
 #include "kq_tmv.cuh"
 #include "kq_nccl.h"
+#include "kq_pack.h"
 
 #include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <unistd.h>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -201,7 +205,9 @@ static int qmat_write(kq_qmat* a, int R_src, const uint8_t* src_dev, uint64_t ba
   return qmat_tv_build(a, s);
 }
 
-static int qmat_upload_mapped(kq_qmat* a, const void* host, size_t bytes, int R_src, int mode, int arg, cudaStream_t s) {
+// `pack`: the host bytes are in the Kindi pack's 8-row interleave instead of GGUF row-major order.
+static int qmat_upload_mapped(kq_qmat* a, const void* host, size_t bytes, int R_src, int mode, int arg, cudaStream_t s,
+                              bool pack = false) {
   const size_t need = (size_t)R_src * a->G * block_bytes(a->type);
   if (bytes != need) return set_err(KQ_ERR_ARG, "tensor byte count does not match its shape");
   uint8_t* tmp = nullptr;
@@ -209,7 +215,7 @@ static int qmat_upload_mapped(kq_qmat* a, const void* host, size_t bytes, int R_
   cudaError_t e = cudaMemcpyAsync(tmp, host, bytes, cudaMemcpyHostToDevice, s);
   int rc = KQ_OK;
   if (e != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, std::string("upload: ") + cudaGetErrorString(e));
-  if (rc == KQ_OK) rc = qmat_write(a, R_src, tmp, 0, mode, arg, s);
+  if (rc == KQ_OK) rc = qmat_write(a, R_src, tmp, 0, mode, arg, s, ShardMap{0, 0, 0, pack ? 1 : 0});
   cudaStreamSynchronize(s);
   cudaFree(tmp);
   return rc;
@@ -531,6 +537,8 @@ struct kq_model {
   // batched verification pass (up to MM_MAXM tokens at once)
   float *bh = nullptr, *by = nullptr, *bq = nullptr, *bpart = nullptr;
   __half *bxd = nullptr, *bxa = nullptr, *bxf = nullptr;   // packed GEMM inputs: C = dim, NH*HD, ffn
+  float *bxs_n = nullptr, *bxs_f = nullptr;   // per-token range scales of bxd (norm) and bxf (SwiGLU)
+  float* bmf = nullptr;                       // [MM_MAXM][ffn_l] SwiGLU output before packing
   int *btok = nullptr, *bslot = nullptr, *brpos = nullptr, *bticket = nullptr;
   unsigned long long* bmask = nullptr;
   int b_nsplit = 0;                 // attention key splits the scratch holds
@@ -808,7 +816,11 @@ extern "C" int kq_model_fill_synthetic(kq_model* m, uint64_t seed) {
   return KQ_OK;
 }
 
+static int set_tensor_impl(kq_model* m, int layer, int kind, const void* host, size_t bytes, bool pack);
 extern "C" int kq_model_set_tensor(kq_model* m, int layer, int kind, const void* host, size_t bytes) {
+  return set_tensor_impl(m, layer, kind, host, bytes, false);
+}
+static int set_tensor_impl(kq_model* m, int layer, int kind, const void* host, size_t bytes, bool pack) {
   int rc = model_check(m);
   if (rc) return rc;
   if (m->tp_world > 1) return set_err(KQ_ERR_ARG, "tensor uploads go to a whole model (tensor-parallel models are generated)");
@@ -831,17 +843,87 @@ extern "C" int kq_model_set_tensor(kq_model* m, int layer, int kind, const void*
   }
   cudaStream_t s = m->stream;
   switch (kind) {
-    case KQ_T_EMB: return qmat_upload_mapped(m->emb, host, bytes, m->emb->R, RM_IDENT, 0, s);
-    case KQ_T_OUT: return qmat_upload_mapped(m->out, host, bytes, m->out->R, RM_IDENT, 0, s);
-    case KQ_T_Q: return qmat_upload_mapped(m->L[layer].q, host, bytes, m->L[layer].q->R, RM_ROPE_PAIR, c.head_dim, s);
-    case KQ_T_K: return qmat_upload_mapped(m->L[layer].k, host, bytes, m->L[layer].k->R, RM_ROPE_PAIR, c.head_dim, s);
-    case KQ_T_V: return qmat_upload_mapped(m->L[layer].v, host, bytes, m->L[layer].v->R, RM_IDENT, 0, s);
-    case KQ_T_O: return qmat_upload_mapped(m->L[layer].o, host, bytes, m->L[layer].o->R, RM_IDENT, 0, s);
-    case KQ_T_GATE: return qmat_upload_mapped(m->L[layer].gu, host, bytes, c.ffn, RM_INTERLEAVE, 0, s);
-    case KQ_T_UP: return qmat_upload_mapped(m->L[layer].gu, host, bytes, c.ffn, RM_INTERLEAVE, 1, s);
-    case KQ_T_DOWN: return qmat_upload_mapped(m->L[layer].down, host, bytes, m->L[layer].down->R, RM_IDENT, 0, s);
+    case KQ_T_EMB: return qmat_upload_mapped(m->emb, host, bytes, m->emb->R, RM_IDENT, 0, s, pack);
+    case KQ_T_OUT: return qmat_upload_mapped(m->out, host, bytes, m->out->R, RM_IDENT, 0, s, pack);
+    case KQ_T_Q: return qmat_upload_mapped(m->L[layer].q, host, bytes, m->L[layer].q->R, RM_ROPE_PAIR, c.head_dim, s, pack);
+    case KQ_T_K: return qmat_upload_mapped(m->L[layer].k, host, bytes, m->L[layer].k->R, RM_ROPE_PAIR, c.head_dim, s, pack);
+    case KQ_T_V: return qmat_upload_mapped(m->L[layer].v, host, bytes, m->L[layer].v->R, RM_IDENT, 0, s, pack);
+    case KQ_T_O: return qmat_upload_mapped(m->L[layer].o, host, bytes, m->L[layer].o->R, RM_IDENT, 0, s, pack);
+    case KQ_T_GATE: return qmat_upload_mapped(m->L[layer].gu, host, bytes, c.ffn, RM_INTERLEAVE, 0, s, pack);
+    case KQ_T_UP: return qmat_upload_mapped(m->L[layer].gu, host, bytes, c.ffn, RM_INTERLEAVE, 1, s, pack);
+    case KQ_T_DOWN: return qmat_upload_mapped(m->L[layer].down, host, bytes, m->L[layer].down->R, RM_IDENT, 0, s, pack);
     default: return set_err(KQ_ERR_ARG, "unknown tensor kind");
   }
+}
+
+// ------------------------------------------------------------------------------ Kindi packs
+// make_engine(pack, ctx) (engine.py:369-381): validate the pack on the host (kq_pack.h, the
+// checks of verify_pack, q4pack.py:86-108), then create the model and move every tensor from the
+// memory-mapped weights.bin / f32.bin to the device, the 8-row interleave regrouped on the device.
+extern "C" int kq_pack_read_config(const char* dir, int ctx, kq_config* out) {
+  kqpack::Pack P;
+  std::string err;
+  if (kqpack::read_pack(dir, ctx, P, err)) return set_err(KQ_ERR_ARG, err);
+  if (validate_cfg(P.cfg) != KQ_OK) return KQ_ERR_ARG;
+  if (out) *out = P.cfg;
+  return KQ_OK;
+}
+
+namespace {
+struct MappedFile {
+  void* p = MAP_FAILED;
+  size_t n = 0;
+  bool open(const std::string& path, size_t size) {
+    n = size;
+    if (!size) return true;
+    const int fd = ::open(path.c_str(), O_RDONLY);
+    if (fd < 0) return false;
+    p = ::mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+    ::close(fd);
+    return p != MAP_FAILED;
+  }
+  const uint8_t* at(uint64_t off) const { return static_cast<const uint8_t*>(p) + off; }
+  ~MappedFile() { if (p != MAP_FAILED && n) ::munmap(p, n); }
+};
+}  // namespace
+
+extern "C" kq_model* kq_model_load_pack(const char* dir, int ctx, int device) {
+  kqpack::Pack P;
+  std::string err;
+  if (kqpack::read_pack(dir, ctx, P, err)) { set_err(KQ_ERR_ARG, err); return nullptr; }
+  MappedFile wf, ff;
+  if (!wf.open(P.dir + "/weights.bin", P.weights_size) || !ff.open(P.dir + "/f32.bin", P.f32_size)) {
+    set_err(KQ_ERR_BACKEND, "cannot map the pack's weights.bin / f32.bin");
+    return nullptr;
+  }
+  kq_model* m = model_create(&P.cfg, device, 0, 1);
+  if (!m) return nullptr;
+  struct Kind { const char* suffix; int kind; };
+  const Kind kinds[] = {{"attn_norm.weight", KQ_T_ATTN_NORM}, {"attn_q.weight", KQ_T_Q}, {"attn_k.weight", KQ_T_K},
+                        {"attn_v.weight", KQ_T_V}, {"attn_output.weight", KQ_T_O}, {"ffn_gate.weight", KQ_T_GATE},
+                        {"ffn_up.weight", KQ_T_UP}, {"ffn_down.weight", KQ_T_DOWN}};
+  auto put = [&](const std::string& name, int layer, int kind) -> int {
+    const kqpack::Tensor& T = P.t.at(name);
+    if (T.type == 0) return set_tensor_impl(m, layer, kind, ff.at(T.f32_off), (size_t)T.rows * T.cols * 4, false);
+    return set_tensor_impl(m, layer, kind, wf.at(T.offset), (size_t)T.bytes, true);
+  };
+  int rc = put("token_embd.weight", -1, KQ_T_EMB);
+  if (!rc) rc = put("output.weight", -1, KQ_T_OUT);
+  if (!rc) rc = put("output_norm.weight", -1, KQ_T_OUTNORM);
+  for (int l = 0; !rc && l < P.cfg.n_layers; ++l) {
+    const std::string p = "blk." + std::to_string(l) + ".";
+    for (const Kind& k : kinds)
+      if (!rc) rc = put(p + k.suffix, l, k.kind);
+    if (!rc) rc = put(p + P.ffn_norm_name, l, KQ_T_FFN_NORM);
+  }
+  if (!rc && cudaStreamSynchronize(m->stream) != cudaSuccess) rc = set_err(KQ_ERR_BACKEND, "pack upload");
+  if (rc) {
+    const std::string keep = g_err;
+    model_release(m);
+    set_err(rc, keep);
+    return nullptr;
+  }
+  return m;
 }
 
 extern "C" int kq_model_reset(kq_model* m) {
@@ -1588,6 +1670,9 @@ static int batch_buffers(kq_model* m) {
   m->bxd = dalloc<__half>(m, xp_halves(MM_MAXM, c.dim), ok);
   m->bxa = dalloc<__half>(m, xp_halves(MM_MAXM, (int)QD), ok);
   m->bxf = dalloc<__half>(m, xp_halves(MM_MAXM, m->ffn_l), ok);
+  m->bxs_n = dalloc<float>(m, MM, ok);
+  m->bxs_f = dalloc<float>(m, MM, ok);
+  m->bmf = dalloc<float>(m, MM * m->ffn_l, ok);
   m->btok = dalloc<int>(m, MM, ok);
   m->bslot = dalloc<int>(m, MM, ok);
   m->brpos = dalloc<int>(m, MM, ok);
@@ -1622,12 +1707,13 @@ static bool batch_supported(const kq_model* m) {
   return m->ffn_l % 64 == 0 && (m->nh_l * m->c.head_dim) % 64 == 0;
 }
 
-static int launch_tmm(kq_model* m, const SegSpec* ss, int nseg, const __half* xp, __half* xp_out, int out_ld,
+// xscale: the per-token scales of the packed input xp (k_bnorm / k_xpack_tok), or null.
+static int launch_tmm(kq_model* m, const SegSpec* ss, int nseg, const __half* xp, const float* xscale, int out_ld,
                       const BatchParams& B) {
   TmmParams P;
   tmm_fill(ss, nseg, B.M, m->device, P);
   P.xp = xp;
-  P.xp_out = xp_out;
+  P.xscale = xscale;
   P.B = B;
   P.out_ld = out_ld;
   P.cos_t = m->cos_t;
@@ -1650,10 +1736,24 @@ static int launch_bnorm(kq_model* m, int M, bool embed, const float* gamma, bool
   P.M = M; P.D = m->c.dim; P.tok = m->btok;
   if (embed) P.emb = m->emb->view();
   P.h = m->bh; P.y = add ? m->by : nullptr; P.gamma = gamma; P.eps = m->c.eps;
-  P.xp = m->bxd; P.Npad = (M + 15) & ~15;
+  P.xp = m->bxd; P.xscale = m->bxs_n; P.Npad = (M + 15) & ~15;
   P.vocab = m->c.vocab; P.err = m->err;
   CU(launch_pdl(k_bnorm, dim3((unsigned)M), dim3(BN_THREADS), 0, m->stream, P));
   return KQ_OK;
+}
+
+// The MLP of a batched pass after its norm (bxd): gate/up GEMM with the SwiGLU epilogue (fp32
+// rows in bmf), the per-token range-scaled packing of those rows (k_xpack_tok), the down GEMM
+// into y (M x dim).
+static int launch_mlp(kq_model* m, LayerW& w, float* y, const BatchParams& B) {
+  const int M = B.M, Npad = (M + 15) & ~15;
+  SegSpec sg[1] = {{w.gu, EPI_SWIGLU, m->bmf, nullptr}};
+  int rc = launch_tmm(m, sg, 1, m->bxd, m->bxs_n, m->ffn_l, B);
+  if (rc) return rc;
+  const XPackParams X = {m->bmf, m->ffn_l, m->ffn_l, Npad, m->bxf, m->bxs_f};
+  CU(launch_pdl(k_xpack_tok, dim3((unsigned)M), dim3(XP_THREADS), 0, m->stream, X));
+  SegSpec sd[1] = {{w.down, EPI_F32, y, nullptr}};
+  return launch_tmm(m, sd, 1, m->bxf, m->bxs_f, m->c.dim, B);
 }
 
 static int launch_battn(kq_model* m, const __half* kc, const __half* vc, int npos, const BatchParams& B) {
@@ -1713,16 +1813,13 @@ static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int p
     __half* kc = seq < 0 ? w.kc : w.bkc + (size_t)seq * sstride;
     __half* vc = seq < 0 ? w.vc : w.bvc + (size_t)seq * sstride;
     SegSpec qkv[3] = {{w.q, EPI_ROPE_Q, m->bq, nullptr}, {w.k, EPI_ROPE_K, nullptr, kc}, {w.v, EPI_V, nullptr, vc}};
-    if ((rc = launch_tmm(m, qkv, 3, m->bxd, nullptr, QD, B))) return rc;
+    if ((rc = launch_tmm(m, qkv, 3, m->bxd, m->bxs_n, QD, B))) return rc;
     if ((rc = launch_battn(m, kc, vc, pos + b1, B))) return rc;
     SegSpec so[1] = {{w.o, EPI_F32, m->by, nullptr}};
-    if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, c.dim, B))) return rc;
+    if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, c.dim, B))) return rc;   // attention output: |x| <= max|V|
     if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;   // row-split o: sum the partials
     if ((rc = launch_bnorm(m, M, false, w.ffn_norm, true))) return rc;
-    SegSpec sg[1] = {{w.gu, EPI_SWIGLU, nullptr, nullptr}};
-    if ((rc = launch_tmm(m, sg, 1, m->bxd, m->bxf, 0, B))) return rc;
-    SegSpec sd[1] = {{w.down, EPI_F32, m->by, nullptr}};
-    if ((rc = launch_tmm(m, sd, 1, m->bxf, nullptr, c.dim, B))) return rc;
+    if ((rc = launch_mlp(m, w, m->by, B))) return rc;
     if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;   // row-split down
   }
   if (!head) return KQ_OK;
@@ -1737,7 +1834,7 @@ static int head_argmax(kq_model* m, int M, const BatchParams& B, int* out_ids, s
   if ((rc = launch_bnorm(m, M, false, m->out_norm, true))) return rc;
   const size_t V = (size_t)m->vocab_l;   // this rank's vocabulary slice
   SegSpec sh[1] = {{m->out, EPI_F32, m->vlogits + row0 * V, nullptr}};
-  if ((rc = launch_tmm(m, sh, 1, m->bxd, nullptr, (int)V, B))) return rc;
+  if ((rc = launch_tmm(m, sh, 1, m->bxd, m->bxs_n, (int)V, B))) return rc;
   if (m->tp_world == 1) {
     k_argmax_rows<<<M, 256, 0, s>>>(m->vlogits + row0 * V, (int)V, out_ids);
     CU(cudaGetLastError());
@@ -1959,20 +2056,17 @@ extern "C" int kq_batch_step(kq_model* m, const int32_t* seqs, const int32_t* to
     LayerW& w = m->L[l];
     if ((rc = launch_bnorm(m, M, l == 0, w.attn_norm, l > 0))) return rc;
     SegSpec qkv[3] = {{w.q, EPI_ROPE_Q, m->bq, nullptr}, {w.k, EPI_ROPE_K, nullptr, w.bkc}, {w.v, EPI_V, nullptr, w.bvc}};
-    if ((rc = launch_tmm(m, qkv, 3, m->bxd, nullptr, QD, B))) return rc;
+    if ((rc = launch_tmm(m, qkv, 3, m->bxd, m->bxs_n, QD, B))) return rc;
     D.kc = w.bkc;
     D.vc = w.bvc;
     cudaError_t e = G == 1 ? launch_dattn_t<1>(D, M, m->nkv_l, s) : G == 2 ? launch_dattn_t<2>(D, M, m->nkv_l, s)
                   : G == 4 ? launch_dattn_t<4>(D, M, m->nkv_l, s) : launch_dattn_t<8>(D, M, m->nkv_l, s);
     CU(e);
     SegSpec so[1] = {{w.o, EPI_F32, m->by, nullptr}};
-    if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, c.dim, B))) return rc;
+    if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, c.dim, B))) return rc;   // attention output: |x| <= max|V|
     if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;
     if ((rc = launch_bnorm(m, M, false, w.ffn_norm, true))) return rc;
-    SegSpec sg[1] = {{w.gu, EPI_SWIGLU, nullptr, nullptr}};
-    if ((rc = launch_tmm(m, sg, 1, m->bxd, m->bxf, 0, B))) return rc;
-    SegSpec sd[1] = {{w.down, EPI_F32, m->by, nullptr}};
-    if ((rc = launch_tmm(m, sd, 1, m->bxf, nullptr, c.dim, B))) return rc;
+    if ((rc = launch_mlp(m, w, m->by, B))) return rc;
     if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;
   }
   if ((rc = head_argmax(m, M, B, m->out_ids))) return rc;
@@ -2138,22 +2232,25 @@ extern "C" int kq_qmat_matmul(kq_qmat* a, const float* x, int M, float* y) {
   TmmParams P;
   tmm_fill(ss, 1, M, a->device, P);
   const size_t pf = tmm_part_floats(P.ntiles, P.nsplit, P.Npad);
-  float *xd = nullptr, *yd = nullptr, *part = nullptr;
+  float *xd = nullptr, *yd = nullptr, *part = nullptr, *xs = nullptr;
   __half* xp = nullptr;
   int* ticket = nullptr;
   bool ok = cudaMalloc(&xd, (size_t)M * a->C * 4) == cudaSuccess;
+  ok = ok && cudaMalloc(&xs, (size_t)M * 4) == cudaSuccess;
   ok = ok && cudaMalloc(&yd, (size_t)M * a->R * 4) == cudaSuccess;
   ok = ok && cudaMalloc(&xp, xp_halves(P.Npad, a->C) * 2) == cudaSuccess;
   ok = ok && cudaMalloc(&part, std::max<size_t>(pf, 1) * 4) == cudaSuccess;
   ok = ok && cudaMalloc(&ticket, (size_t)P.ntiles * 4) == cudaSuccess;
   if (!ok) rc = set_err(KQ_ERR_MEMORY, "matmul buffers");
   if (!rc && (cudaMemset(ticket, 0, (size_t)P.ntiles * 4) != cudaSuccess ||
+              cudaMemset(xp, 0, xp_halves(P.Npad, a->C) * 2) != cudaSuccess ||
               cudaMemcpy(xd, x, (size_t)M * a->C * 4, cudaMemcpyHostToDevice) != cudaSuccess))
     rc = set_err(KQ_ERR_BACKEND, "matmul upload");
   if (!rc) {
-    const long long n = (long long)P.Npad * a->C;
-    k_xpack<<<(unsigned)((n + 255) / 256), 256>>>(xd, M, P.Npad, a->C, xp);
+    const XPackParams X = {xd, a->C, a->C, P.Npad, xp, xs};
+    k_xpack_tok<<<(unsigned)M, XP_THREADS>>>(X);
     P.xp = xp;
+    P.xscale = xs;
     P.seg[0].out_f = yd;
     P.out_ld = a->R;
     P.part = part;
@@ -2167,6 +2264,7 @@ extern "C" int kq_qmat_matmul(kq_qmat* a, const float* x, int M, float* y) {
   cudaFree(xd);
   cudaFree(yd);
   cudaFree(xp);
+  cudaFree(xs);
   cudaFree(part);
   cudaFree(ticket);
   if (!rc) rc = dev_err_check(a->device);
@@ -2240,15 +2338,11 @@ static int ffn_block_enqueue(kq_model* m, int layer, float* x_dev, int M, float*
   BNormParams P;
   std::memset(&P, 0, sizeof(P));
   P.M = M; P.D = c.dim; P.h = x_dev; P.gamma = w.ffn_norm; P.eps = c.eps;
-  P.xp = m->bxd; P.Npad = (M + 15) & ~15; P.vocab = c.vocab; P.err = m->err;
+  P.xp = m->bxd; P.xscale = m->bxs_n; P.Npad = (M + 15) & ~15; P.vocab = c.vocab; P.err = m->err;
   CU(launch_pdl(k_bnorm, dim3((unsigned)M), dim3(BN_THREADS), 0, s, P, pdl));
   BatchParams B;
   B.M = M; B.slot = m->bslot; B.rpos = m->brpos; B.mask = m->bmask; B.tree_base = 0; B.seq = nullptr;
-  const SegSpec sg[1] = {{w.gu, EPI_SWIGLU, nullptr, nullptr}};
-  const SegSpec sd[1] = {{w.down, EPI_F32, y_dev, nullptr}};
-  int rc = launch_tmm(m, sg, 1, m->bxd, m->bxf, 0, B);
-  if (rc || (rc = launch_tmm(m, sd, 1, m->bxf, nullptr, c.dim, B))) return rc;
-  return KQ_OK;
+  return launch_mlp(m, w, y_dev, B);
 }
 
 static int ffn_block_check(kq_model* m, int layer, int M) {

@@ -32,6 +32,7 @@ struct BNormParams {
   const float* gamma;      // [D]
   float eps;
   __half* xp;              // packed input of the next GEMM (C = D)
+  float* xscale;           // [M] the power of two each packed row was divided by (xp_scale_exp)
   int Npad;
   int vocab;
   int* err;
@@ -54,6 +55,7 @@ __global__ void __launch_bounds__(BN_THREADS) k_bnorm(const __grid_constant__ BN
     }
   }
   double acc = 0.0;
+  float hmax = 0.f, gmax = 0.f;   // bound of the output row: max|h| * s * max|gamma|
   const int nch = P.D / 8;
   for (int c = tid; c < nch; c += BN_THREADS) {
     float v[8];
@@ -72,23 +74,46 @@ __global__ void __launch_bounds__(BN_THREADS) k_bnorm(const __grid_constant__ BN
     }
     reinterpret_cast<float4*>(h)[2 * c] = make_float4(v[0], v[1], v[2], v[3]);
     reinterpret_cast<float4*>(h)[2 * c + 1] = make_float4(v[4], v[5], v[6], v[7]);
+    const float4 g0 = reinterpret_cast<const float4*>(P.gamma)[2 * c], g1 = reinterpret_cast<const float4*>(P.gamma)[2 * c + 1];
+    gmax = fmaxf(gmax, fmaxf(fmaxf(fmaxf(fabsf(g0.x), fabsf(g0.y)), fmaxf(fabsf(g0.z), fabsf(g0.w))),
+                             fmaxf(fmaxf(fabsf(g1.x), fabsf(g1.y)), fmaxf(fabsf(g1.z), fabsf(g1.w)))));
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc = __dadd_rn(acc, __dmul_rn((double)v[e], (double)v[e]));
+    for (int e = 0; e < 8; ++e) {
+      acc = __dadd_rn(acc, __dmul_rn((double)v[e], (double)v[e]));
+      hmax = fmaxf(hmax, fabsf(v[e]));
+    }
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) red[warp] = acc;
+  for (int off = 16; off > 0; off >>= 1) {
+    acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    hmax = fmaxf(hmax, __shfl_xor_sync(0xffffffffu, hmax, off));
+    gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, off));
+  }
+  __shared__ float redm[2][BN_THREADS / 32];
+  if (lane == 0) { red[warp] = acc; redm[0][warp] = hmax; redm[1][warp] = gmax; }
   __syncthreads();
   double tot = 0.0;
-  for (int w = 0; w < BN_THREADS / 32; ++w) tot += red[w];
+  for (int w = 0; w < BN_THREADS / 32; ++w) {
+    tot += red[w];
+    hmax = fmaxf(hmax, redm[0][w]);
+    gmax = fmaxf(gmax, redm[1][w]);
+  }
   const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / (double)P.D), P.eps)));
+  // every output |fl(fl(h s) gamma)| <= hmax * s * gmax (1 + 2^-22); the slack covers the roundings
+  const int e_t = xp_scale_exp(__fmul_rn(__fmul_rn(__fmul_rn(hmax, s), gmax), 1.0000005f));
+  const float inv = xp_pow2(-e_t);
+  if (tid == 0) P.xscale[t] = xp_pow2(e_t);
   for (int c = tid; c < nch; c += BN_THREADS) {
     const float4 a0 = reinterpret_cast<const float4*>(h)[2 * c], a1 = reinterpret_cast<const float4*>(h)[2 * c + 1];
     const float4 g0 = reinterpret_cast<const float4*>(P.gamma)[2 * c], g1 = reinterpret_cast<const float4*>(P.gamma)[2 * c + 1];
-    const float x[8] = {__fmul_rn(__fmul_rn(a0.x, s), g0.x), __fmul_rn(__fmul_rn(a0.y, s), g0.y),
-                        __fmul_rn(__fmul_rn(a0.z, s), g0.z), __fmul_rn(__fmul_rn(a0.w, s), g0.w),
-                        __fmul_rn(__fmul_rn(a1.x, s), g1.x), __fmul_rn(__fmul_rn(a1.y, s), g1.y),
-                        __fmul_rn(__fmul_rn(a1.z, s), g1.z), __fmul_rn(__fmul_rn(a1.w, s), g1.w)};
+    float x[8] = {__fmul_rn(__fmul_rn(a0.x, s), g0.x), __fmul_rn(__fmul_rn(a0.y, s), g0.y),
+                  __fmul_rn(__fmul_rn(a0.z, s), g0.z), __fmul_rn(__fmul_rn(a0.w, s), g0.w),
+                  __fmul_rn(__fmul_rn(a1.x, s), g1.x), __fmul_rn(__fmul_rn(a1.y, s), g1.y),
+                  __fmul_rn(__fmul_rn(a1.z, s), g1.z), __fmul_rn(__fmul_rn(a1.w, s), g1.w)};
+    if (e_t) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = __fmul_rn(x[e], inv);
+    }
     uint4 hi, lo;
     tm_split(x[0], x[1], hi.x, lo.x);
     tm_split(x[2], x[3], hi.y, lo.y);

@@ -168,6 +168,8 @@ __device__ inline void scatter_block(const QViewW& m, int d, int g, const uint8_
 // index (s + sh.row_off) * sh.G_src + (g + sh.g_off), with G_src the full matrix's super-blocks.
 struct ShardMap {
   int row_off, g_off, G_src;   // {0, 0, G}: the whole matrix
+  int pack;                    // 1: `src` is in the Kindi pack's 8-row interleave (q4kernels.h:8-10),
+                               // block (row, g) at ((row / 8) * G + g) * 8 + row % 8
 };
 __global__ void k_qmat_write(QViewW m, int R_src, const uint8_t* __restrict__ src, uint64_t base,
                              int mode, int arg, ShardMap sh) {
@@ -177,7 +179,8 @@ __global__ void k_qmat_write(QViewW m, int R_src, const uint8_t* __restrict__ sr
   uint8_t b[210];
   const int bs = block_bytes(m.type);
   if (src) {
-    const uint8_t* p = src + ((size_t)s * m.G + g) * bs;
+    const size_t blk = sh.pack ? ((size_t)(s >> 3) * m.G + g) * 8 + (s & 7) : (size_t)s * m.G + g;
+    const uint8_t* p = src + blk * bs;
     for (int i = 0; i < bs; i++) b[i] = p[i];
   } else if (m.type == Q4K) {
     gen_q4k_block(base, (uint64_t)(s + sh.row_off) * sh.G_src + (uint64_t)(g + sh.g_off), b);

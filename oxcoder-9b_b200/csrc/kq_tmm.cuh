@@ -52,13 +52,18 @@ __device__ __forceinline__ void xp_store(__half* xp, int Npad, int tok, int col,
   xp[o + (size_t)64 * Npad] = lo;
 }
 
-// fp32 [M][C] -> packed activations (tokens M..Npad-1 zero).
-__global__ void __launch_bounds__(256) k_xpack(const float* __restrict__ x, int M, int Npad, int C, __half* xp) {
-  const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
-  if (i >= (long long)Npad * C) return;
-  const int t = (int)(i / C), col = (int)(i % C);
-  xp_store(xp, Npad, t, col, t < M ? x[(size_t)t * C + col] : 0.f);
+// Per-token range scaling of the packed activations. hi = fp16(x) overflows for |x| > 65504, and
+// hi + lo then turns into inf - inf in the MMA. A producer that cannot bound its values (the
+// SwiGLU output, a caller's fp32 rows, a norm output with large gamma) packs token t's row scaled
+// by 2^-e_t, the smallest e_t >= 0 that brings the row's largest magnitude below 2^15, and
+// records 2^e_t; the GEMM epilogue multiplies token t's results by it. Powers of two are exact,
+// so a row that needs no scaling (e_t = 0) packs bit for bit as before. NaN and inf keep e_t = 0
+// and propagate.
+__device__ __forceinline__ int xp_scale_exp(float amax) {
+  if (!(amax >= 32768.f) || amax > 3.0e38f) return 0;
+  return (int)((__float_as_uint(amax) >> 23) & 255u) - 127 - 14;   // floor(log2 amax) - 14
 }
+__device__ __forceinline__ float xp_pow2(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
 
 // ------------------------------------------------------------------------------ tcgen05 wrappers
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
@@ -189,7 +194,7 @@ struct TmmParams {
   int M, Npad;         // tokens, MMA N (multiple of 16)
   int xs;              // activation ring stages (1..TM_XS_MAX), see tmm_smem
   const __half* xp;    // packed activations (xp_off layout)
-  __half* xp_out;      // SWIGLU: packed input of the next GEMM (same Npad)
+  const float* xscale; // per token: the power of two its packed row was divided by (null: none)
   BatchParams B;
   int out_ld;          // row length of the fp32 outputs
   const float* cos_t;
@@ -268,6 +273,52 @@ __device__ __forceinline__ void tm_split(float a, float b, uint32_t& hi, uint32_
   hi = h2u(h);
   lo = h2u(__floats2half2_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y)));
 }
+// fp32 rows x [M][ld] (C columns) -> packed activations, one CTA per token, each row scaled as
+// xp_scale_exp says; scale[t] = 2^e_t. Tokens M..Npad-1 are left as they are (their GEMM columns
+// are never stored).
+constexpr int XP_THREADS = 256;
+struct XPackParams {
+  const float* x;      // [M][ld] rows, C columns (C and ld multiples of 8)
+  int ld, C, Npad;
+  __half* xp;          // packed activations
+  float* scale;        // [M]
+};
+__global__ void __launch_bounds__(XP_THREADS) k_xpack_tok(const __grid_constant__ XPackParams P) {
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float red[XP_THREADS / 32];
+  pdl_wait();
+  pdl_trigger();
+  const float4* row = reinterpret_cast<const float4*>(P.x + (size_t)t * P.ld);
+  const int nch = P.C / 8, Npad = P.Npad;
+  __half* xp = P.xp;
+  float mx = 0.f;
+  for (int c = tid; c < nch; c += XP_THREADS) {
+    const float4 a = row[2 * c], b = row[2 * c + 1];
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < XP_THREADS / 32; ++w) mx = fmaxf(mx, red[w]);
+  const int e = xp_scale_exp(mx);
+  const float inv = xp_pow2(-e);
+  for (int c = tid; c < nch; c += XP_THREADS) {
+    const float4 a = row[2 * c], b = row[2 * c + 1];
+    uint4 hi, lo;
+    tm_split(__fmul_rn(a.x, inv), __fmul_rn(a.y, inv), hi.x, lo.x);
+    tm_split(__fmul_rn(a.z, inv), __fmul_rn(a.w, inv), hi.y, lo.y);
+    tm_split(__fmul_rn(b.x, inv), __fmul_rn(b.y, inv), hi.z, lo.z);
+    tm_split(__fmul_rn(b.z, inv), __fmul_rn(b.w, inv), hi.w, lo.w);
+    const size_t o = xp_off(Npad, t, 8 * c);
+    *reinterpret_cast<uint4*>(xp + o) = hi;
+    *reinterpret_cast<uint4*>(xp + o + (size_t)64 * Npad) = lo;
+  }
+  if (tid == 0) P.scale[t] = xp_pow2(e);
+}
+
 // 32 Q4_K weights of one row, columns j = 0..31 of a sub-block: the nibble at `sh` (0 or 4) of the
 // 32 bytes W0, W1; w = ds*q - dm, as 16 hi and 16 lo words (column pairs 2m, 2m + 1).
 __device__ __forceinline__ void tm_q4_row32(const uint4& W0, const uint4& W1, int sh, float ds, float dm,
@@ -304,6 +355,11 @@ __device__ __forceinline__ void tm_q6_row32(const uint4& L0, const uint4& L1, co
 
 // Epilogue of one (row, token) value. lrow: row within the segment; vo: the value of row lrow ^ 1.
 __device__ __forceinline__ void tm_epilogue(const TmmParams& P, const TmmSeg& S, int lrow, int tk, float v, float vo) {
+  if (P.xscale) {   // undo the token's range scaling (a power of two: exact)
+    const float sc = P.xscale[tk];
+    v = __fmul_rn(v, sc);
+    vo = __fmul_rn(vo, sc);
+  }
   switch (S.epi) {
     case EPI_F32:
       S.out_f[(size_t)tk * P.out_ld + lrow] = v;
@@ -313,8 +369,8 @@ __device__ __forceinline__ void tm_epilogue(const TmmParams& P, const TmmSeg& S,
       const int sq = P.B.seq ? P.B.seq[tk] : 0;
       S.out_h[((size_t)(sq * P.nkv + kv) * P.ctx + P.B.slot[tk]) * P.hd + d] = __float2half_rn(v);
     } break;
-    case EPI_SWIGLU:   // rows (2i, 2i + 1) = (gate i, up i)
-      if ((lrow & 1) == 0) xp_store(P.xp_out, P.Npad, tk, lrow >> 1, __fmul_rn(silu_f(v), vo));
+    case EPI_SWIGLU:   // rows (2i, 2i + 1) = (gate i, up i); fp32 [M][out_ld], packed by k_xpack_tok
+      if ((lrow & 1) == 0) S.out_f[(size_t)tk * P.out_ld + (lrow >> 1)] = __fmul_rn(silu_f(v), vo);
       break;
     case EPI_ROPE_Q:
     case EPI_ROPE_K:   // rows (2i, 2i + 1) of a head = NeoX pair (i, i + hd/2)

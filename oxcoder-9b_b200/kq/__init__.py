@@ -3,7 +3,7 @@
 The host runtime is C++/CUDA; this module is a thin ctypes shim with the same engine interface
 as the reference's Q4 engines (scripts/kindi_q4/kindi/cpu4.py:94-236 and gpu4.py:50-110):
 
-    e = Engine(config)          # make_engine(pack, ctx) -> gpu4.Engine
+    e = make_engine(pack, ctx)  # engine.make_engine -> gpu4.Engine (or Engine(config) synthetic)
     e.reset(); e.feed(tok, pos); e.feed_batch(toks, pos)
     e.step(tok, pos) -> greedy id; e.generate(ids, n) -> list; e.ylog -> logits
 
@@ -58,6 +58,8 @@ SIGNATURES = {
     "kq_config_default": (None, [C.POINTER(Config)]),
     "kq_model_create": (C.c_void_p, [C.POINTER(Config), C.c_int]),
     "kq_model_free": (None, [C.c_void_p]),
+    "kq_pack_read_config": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(Config)]),
+    "kq_model_load_pack": (C.c_void_p, [C.c_char_p, C.c_int, C.c_int]),
     "kq_tp_unique_id": (C.c_int, [C.c_char_p]),
     "kq_batch_caches": (C.c_int, [C.c_void_p, C.c_int]),
     "kq_batch_feed": (C.c_int, [C.c_void_p, C.c_int, PI32, C.c_int, C.c_int]),
@@ -227,12 +229,22 @@ class Engine(object):
     this process's shard of a tensor-parallel model over `world` GPUs (one process per GPU, the
     same 128-byte NCCL id from tp_unique_id() on every rank); it returns when all ranks joined."""
 
-    def __init__(self, config=None, device=0, seed=0, tp=None, **overrides):
-        self.config = config if config is not None else Config.default(**overrides)
+    def __init__(self, config=None, device=0, seed=0, tp=None, pack=None, **overrides):
+        if pack is not None:
+            if config is not None or tp is not None:
+                raise ValueError("a pack engine takes its configuration from the pack")
+            self.config = read_pack_config(pack, overrides.pop("ctx", 4096))
+            if overrides:
+                raise ValueError("unexpected arguments for a pack engine: %s" % sorted(overrides))
+            seed = None
+        else:
+            self.config = config if config is not None else Config.default(**overrides)
         self.ctx = self.config.ctx
         self.vocab = self.config.vocab
         self.tp = tp
-        if tp is not None:
+        if pack is not None:
+            h = lib().kq_model_load_pack(os.fsencode(pack), self.ctx, device)
+        elif tp is not None:
             rank, world, uid = tp
             if len(uid) != 128:
                 raise ValueError("the NCCL id is 128 bytes")
@@ -439,8 +451,27 @@ class Engine(object):
         return out
 
 
-def make_engine(config=None, ctx=None, device=0, seed=0, **overrides):
-    """engine.make_engine for the Q4 path: one GPU engine (no spec/approximate head flags)."""
+def read_pack_config(pack, ctx=4096):
+    """Validate a Kindi Q4 pack directory without touching the GPU (kq_pack_read_config) and
+    return its Config at context ctx. Raises ValueError with the reference's messages
+    ("Unsupported pack", "Pack size mismatch: ...", "Invalid packed tensor span: ...", ...)."""
+    c = Config()
+    check(lib().kq_pack_read_config(os.fsencode(pack), int(ctx), C.byref(c)))
+    return c
+
+
+def make_engine(pack=None, ctx=4096, clusters=None, log=print, device=0, seed=0, **overrides):
+    """engine.make_engine (engine.py:369-381) for the Q4 path on one GPU. `pack`: a Kindi Q4 pack
+    directory (validated, then loaded); a Config, or None, builds the synthetic model of that
+    configuration (the default: config-2) from `seed`. The approximate head (`clusters`) is not
+    part of the Q4 path, as in the reference."""
+    if clusters is not None:
+        raise ValueError("Q4 approximate-head paths are not validated")
+    if isinstance(pack, (str, bytes, os.PathLike)):
+        if overrides:
+            raise ValueError("a pack engine takes its configuration from the pack")
+        log("kq: loading Q4 pack %s (ctx %d, device %d)" % (os.fspath(pack), ctx, device))
+        return Engine(pack=pack, ctx=ctx, device=device)
     if ctx is not None:
         overrides["ctx"] = ctx
-    return Engine(config, device=device, seed=seed, **overrides)
+    return Engine(pack, device=device, seed=seed, **overrides)

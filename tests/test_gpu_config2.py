@@ -69,8 +69,9 @@ def test_config2_greedy_identity_256_steps(kq, oracle, record_property):
     k_min = int(np.argmin(margins))
     record_property("min_top2_margin", margins[k_min])
     record_property("max_logit_rel_l2", max(errs))
-    print("config-2 greedy: %d steps, smallest oracle top-2 margin %.4g (step %d), largest logits rel-L2 %.3g"
-          % (len(got), margins[k_min], k_min, max(errs)))
+    print("config-2 greedy: %d steps, smallest oracle top-2 margin %.4g (step %d), logits rel-L2 first %.3g "
+          "median %.3g largest %.3g (step %d)" % (len(got), margins[k_min], k_min, errs[0], float(np.median(errs)),
+                                                  max(errs), int(np.argmax(errs))))
     assert got == ref, ("first divergence at step %d; oracle top-2 margin there %.4g" % (len(got) - 1, margins[-1]))
     assert len(got) == steps
     assert max(errs) < RTOL, max(errs)
