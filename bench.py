@@ -382,9 +382,69 @@ def cfg1_bench(e, hbm_gbs, peak_tflops, n=96):
     return out
 
 
+def tp_split(args):
+    """Where the time of the tensor-parallel passes goes, per rank: the config-4 prefill (8192
+    tokens) and, for world > 1, three steps of the config-4 batched decode, with the model built
+    under KQ_PHASE_TIMES=1 (an event between launch groups: GEMM, attention, all-reduce, other).
+    The events remove programmatic launch overlap, so the totals run a little above the timed
+    lines of the full run; the split is what this mode is for. One JSON line per rank."""
+    os.environ["KQ_PHASE_TIMES"] = "1"
+    import numpy as np
+    import kq
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    uid = None
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    out = {"mode": "tp-split", "rank": rank, "world": world}
+
+    def engine(ctx):
+        if dist is None:
+            return kq.Engine(kq.Config.default(ctx=ctx), device=local, seed=0)
+        obj = [kq.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        return kq.Engine(kq.Config.default(ctx=ctx), device=local, seed=0, tp=(rank, world, obj[0]))
+
+    e = engine(TP_PROMPT + 256)
+    ids = np.random.default_rng(1).integers(0, e.vocab, TP_PROMPT).astype(np.int32)
+    e.feed_batch(ids[:512], 0)
+    e.phase_times()
+    t0 = time.perf_counter()
+    e.feed_batch(ids, 0)
+    out["prefill_ms"] = 1e3 * (time.perf_counter() - t0)
+    out["prefill_split_ms"] = e.phase_times()
+    e.close()
+    if dist is not None:
+        e = engine(TP_DEC_CTX)
+        e.batch_caches(TP_DEC_SEQ)
+        seqs = list(range(TP_DEC_SEQ))
+        cur = [int(v) for v in (np.arange(TP_DEC_SEQ) * 7919) % e.vocab]
+        pos0 = TP_DEC_CTX - 8
+        cur = e.batch_step(seqs, cur, [pos0] * TP_DEC_SEQ)
+        e.phase_times()
+        t0 = time.perf_counter()
+        for i in range(3):
+            cur = e.batch_step(seqs, cur, [pos0 + 1 + i] * TP_DEC_SEQ)
+        out["decode_ms_per_step"] = 1e3 * (time.perf_counter() - t0) / 3
+        out["decode_split_ms_per_step"] = {k: v / 3 for k, v in e.phase_times().items()}
+        e.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def run_profile_mode(args):
     """decode-only: fill the config-2 model (optionally fewer layers), W + K device-resident
     decode steps at ctx 4K. gemv-only: the config-0 Q4_K GEMV over 16 rotating copies."""
+    if args.mode == "tp-split":
+        return tp_split(args)
     import kq
     if args.mode == "spec":
         e = kq.Engine(kq.Config.default(ctx=CTX, n_layers=args.layers), seed=0)
@@ -446,7 +506,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=32, help="decode-only: layers of the model (small ncu captures)")
-    ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only", "spec", "prefill", "gemm", "batch-decode"],
+    ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only", "spec", "prefill", "gemm", "batch-decode", "tp-split"],
                     help="decode-only / gemv-only: the small commands the ncu captures in profiles/ run")
     args = ap.parse_args()
     if args.mode != "full":

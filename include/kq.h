@@ -125,6 +125,12 @@ int kq_time_decode(kq_model* m, int tok, int pos, int n, float* ms_out);
  * persistent form), or < 0 on error. A measurement hook with no reference counterpart: the
  * reference's CuPy engine launches its kernels one by one from Python (gpu4.py:50-110). */
 int kq_step_kernels(kq_model* m);
+/* Time split of the batched passes (prefill, verify, batched decode) since the last call, in ms:
+ * [0] tensor-core GEMMs and their activation packing, [1] attention, [2] NCCL all-reduces,
+ * [3] norms, head argmax and the rest; then resets. Only for a model created with
+ * KQ_PHASE_TIMES=1 in the environment (an event separates every launch group, so the passes run
+ * without programmatic launch overlap). A measurement hook with no reference counterpart. */
+int kq_phase_times(kq_model* m, float* ms4);
 
 /* ------------------------------------------------------------------ speculative verification
  * Draft-then-verify over a draft TREE (the reference verifies linear chains only: spec.py:790-793

@@ -21,8 +21,10 @@
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <unistd.h>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <thread>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -489,6 +491,19 @@ struct kq_model {
   int tp_rank = 0, tp_world = 1;
   int nh_l = 0, nkv_l = 0, ffn_l = 0, vocab_l = 0;
   ncclComm_t comm = nullptr;
+  bool comm_dead = false;           // the communicator was aborted after a peer stopped answering
+  // pinned staging of a batched pass's per-token metadata (tokens, slots, rotary positions,
+  // sequences, masks): a ring whose slot is reused once the copies that read it have run, so the
+  // uploads stay asynchronous (a pageable upload may wait for the stream, and a stream stuck in a
+  // collective would then hold the host beyond the tensor-parallel deadline)
+  struct MetaSlot {
+    int tok[128], slot[128], rpos[128], seq[128];
+    unsigned long long mask[256];
+  };
+  static constexpr int META_RING = 4;
+  MetaSlot* meta = nullptr;
+  cudaEvent_t meta_ev[META_RING] = {};
+  int meta_i = 0, meta_cur = 0;
   int n_seq = 0;                    // sequences of the batched-decode caches (kq_batch_caches)
   int *bseq = nullptr, *bposv = nullptr;   // [MM_MAXM] per-token sequence / position of a batched step
   float* dpart = nullptr;           // batched decode attention partials
@@ -519,6 +534,13 @@ struct kq_model {
   int* aticket = nullptr;
   cudaGraphExec_t g_step = nullptr, g_feed = nullptr;
   int step_kernels = 0;             // kernel nodes of the decode-step graph
+  // optional time split of the batched passes (KQ_PHASE_TIMES=1): an event before each launch
+  // group, its category, and the accumulated ms per category (GEMM, attention, all-reduce, other)
+  bool prof = false;
+  std::vector<cudaEvent_t> pev;
+  std::vector<int> pcat;
+  size_t pn = 0;
+  double pms[4] = {0, 0, 0, 0};
   // persistent decode kernel (k_decode): phase table, arrival counters, launch shape
   bool persist = true;
   PhaseDesc* d_phases = nullptr;
@@ -550,11 +572,39 @@ struct kq_model {
   std::vector<void*> allocs;
 };
 
+static_assert(MM_MAXM == 128, "the metadata staging slots hold MM_MAXM tokens");
+
 static int model_check(kq_model* m) {
   if (!m) return set_err(KQ_ERR_ARG, "null model");
   CU(cudaSetDevice(m->device));
   return KQ_OK;
 }
+
+// Time split of the batched passes (KQ_PHASE_TIMES=1 only): prof_mark records an event before a
+// launch group of category cat; prof_flush (after the stream synchronised) adds each interval
+// between consecutive events to the category of its first event. The events separate the
+// kernels, so programmatic launch overlap is lost while the split is on.
+enum { PC_GEMM = 0, PC_ATTN = 1, PC_COMM = 2, PC_OTHER = 3, PC_END = 4 };
+static void prof_mark(kq_model* m, int cat) {
+  if (!m->prof) return;
+  if (m->pn == m->pev.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) { m->prof = false; return; }
+    m->pev.push_back(e);
+    m->pcat.push_back(0);
+  }
+  cudaEventRecord(m->pev[m->pn], m->stream);
+  m->pcat[m->pn++] = cat;
+}
+static void prof_flush(kq_model* m) {
+  if (!m->prof) return;
+  for (size_t i = 1; i < m->pn; ++i) {
+    float ms = 0.f;
+    if (m->pcat[i - 1] < PC_END && cudaEventElapsedTime(&ms, m->pev[i - 1], m->pev[i]) == cudaSuccess) m->pms[m->pcat[i - 1]] += ms;
+  }
+  m->pn = 0;
+}
+
 
 extern "C" {
 
@@ -577,11 +627,130 @@ void kq_config_default(kq_config* c) {
 
 }  // extern "C"
 
+// ------------------------------------------------------------------------------ bounded NCCL waits
+// Every host wait on the peers of a tensor-parallel model ends by a deadline: KQ_TP_TIMEOUT_MS
+// (default 60000) from the start of the wait. At the deadline the communicator is aborted
+// (ncclCommAbort also ends this rank's collective kernels, so its stream drains), the model is
+// marked dead for tensor-parallel work and the call returns KQ_ERR_TIMEOUT.
+static double host_ms() {
+  return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+static double tp_timeout_ms() {
+  const char* v = std::getenv("KQ_TP_TIMEOUT_MS");
+  const double t = v ? std::atof(v) : 60000.0;
+  return t > 0 ? t : 60000.0;
+}
+static void tp_abort(kq_model* m) {
+  if (m->comm) nccl().CommAbort(m->comm);
+  m->comm = nullptr;
+  m->comm_dead = true;
+}
+static void tp_comm_close(kq_model* m) {
+  if (!m->comm) return;
+  ncclResult_t st = nccl().CommFinalize(m->comm);
+  const double end = host_ms() + 10000.0;
+  while (st == ncclInProgress && host_ms() < end) {
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+    if (nccl().CommGetAsyncError(m->comm, &st) != ncclSuccess) break;
+  }
+  if (st == ncclSuccess) nccl().CommDestroy(m->comm);
+  else nccl().CommAbort(m->comm);
+  m->comm = nullptr;
+}
+// Completes a non-blocking NCCL call that returned r.
+static int nccl_wait(kq_model* m, ncclResult_t r, const char* what) {
+  const double end = host_ms() + tp_timeout_ms();
+  while (r == ncclInProgress) {
+    if (host_ms() > end) {
+      tp_abort(m);
+      return set_err(KQ_ERR_TIMEOUT, std::string(what) + ": a tensor-parallel peer did not answer in time; the communicator was aborted");
+    }
+    std::this_thread::yield();
+    if (nccl().CommGetAsyncError(m->comm, &r) != ncclSuccess) break;
+  }
+  if (r != ncclSuccess) {
+    const std::string msg = std::string(what) + ": " + nccl().GetErrorString(r);
+    tp_abort(m);
+    return set_err(KQ_ERR_BACKEND, msg);
+  }
+  return KQ_OK;
+}
+// The end of a pass: the model's stream drained, for a tensor-parallel model with the peers'
+// health polled and the wait bounded.
+static int tp_sync(kq_model* m) {
+  if (m->tp_world == 1 || !m->comm) {
+    CU(cudaStreamSynchronize(m->stream));
+    return KQ_OK;
+  }
+  const double start = host_ms(), end = start + tp_timeout_ms();
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(m->stream);
+    if (q == cudaSuccess) return KQ_OK;
+    if (q != cudaErrorNotReady) return set_err(KQ_ERR_BACKEND, std::string("tensor-parallel pass: ") + cudaGetErrorString(q));
+    ncclResult_t st = ncclSuccess;
+    nccl().CommGetAsyncError(m->comm, &st);
+    if (st != ncclSuccess && st != ncclInProgress) {
+      const std::string msg = std::string("NCCL: ") + nccl().GetErrorString(st);
+      tp_abort(m);
+      cudaStreamSynchronize(m->stream);
+      return set_err(KQ_ERR_BACKEND, msg);
+    }
+    const double now = host_ms();
+    if (now > end) {
+      tp_abort(m);
+      cudaStreamSynchronize(m->stream);   // the aborted collectives return; the stream drains
+      char buf[160];
+      std::snprintf(buf, sizeof buf, "a tensor-parallel peer did not answer within %.0f ms; the communicator was aborted",
+                    tp_timeout_ms());
+      return set_err(KQ_ERR_TIMEOUT, buf);
+    }
+    if (now - start > 2.0) std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+static int tp_alive(const kq_model* m) {
+  if (m->comm_dead) return set_err(KQ_ERR_BACKEND, "the tensor-parallel communicator was aborted after a peer stopped answering");
+  return KQ_OK;
+}
+// An event of the model's stream has completed; bounded like tp_sync for a tensor-parallel model.
+static int tp_wait_event(kq_model* m, cudaEvent_t ev) {
+  if (m->tp_world == 1 || !m->comm) {
+    CU(cudaEventSynchronize(ev));
+    return KQ_OK;
+  }
+  const double end = host_ms() + tp_timeout_ms();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(ev);
+    if (q == cudaSuccess) return KQ_OK;
+    if (q != cudaErrorNotReady) return set_err(KQ_ERR_BACKEND, std::string("tensor-parallel pass: ") + cudaGetErrorString(q));
+    if (host_ms() > end) return tp_sync(m);   // aborts the communicator and reports the timeout
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+// The next metadata slot, once the uploads that last read it have run.
+static int meta_acquire(kq_model* m, kq_model::MetaSlot** out) {
+  if (!m->meta) {
+    CU(cudaMallocHost(&m->meta, sizeof(kq_model::MetaSlot) * kq_model::META_RING));
+    for (cudaEvent_t& e : m->meta_ev) CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  const int i = m->meta_i++ % kq_model::META_RING;
+  int rc = tp_wait_event(m, m->meta_ev[i]);
+  if (rc) return rc;
+  m->meta_cur = i;
+  *out = &m->meta[i];
+  return KQ_OK;
+}
+// After the uploads from the current slot are enqueued.
+static int meta_release(kq_model* m) {
+  CU(cudaEventRecord(m->meta_ev[m->meta_cur], m->stream));
+  return KQ_OK;
+}
+
 static void model_release(kq_model* m) {
   if (!m) return;
   cudaSetDevice(m->device);
+  if (m->stream && m->comm) tp_sync(m);   // bounded: a silent peer gets the communicator aborted
   if (m->stream) cudaStreamSynchronize(m->stream);
-  if (m->comm && nccl().ok) nccl().CommDestroy(m->comm);
+  if (m->comm && nccl().ok) tp_comm_close(m);
   if (m->g_step) cudaGraphExecDestroy(m->g_step);
   if (m->g_feed) cudaGraphExecDestroy(m->g_feed);
   for (auto& l : m->L) {
@@ -594,6 +763,10 @@ static void model_release(kq_model* m) {
   for (void* p : m->allocs) cudaFree(p);
   if (m->st_host) cudaFreeHost(m->st_host);
   if (m->vstates) cudaFreeHost(m->vstates);
+  for (cudaEvent_t e : m->pev) cudaEventDestroy(e);
+  for (cudaEvent_t e : m->meta_ev)
+    if (e) cudaEventDestroy(e);
+  if (m->meta) cudaFreeHost(m->meta);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
 }
@@ -699,6 +872,7 @@ static kq_model* model_create(const kq_config* cfg, int device, int rank, int wo
     m->dpart1 = dalloc<float>(m, (size_t)c.n_kv_heads * DA_MAX_SPLIT * (c.n_heads / c.n_kv_heads) * (c.head_dim + 4), ok);
     m->persist = std::getenv("KQ_PERSIST") && std::atoi(std::getenv("KQ_PERSIST")) == 1;   // opt-in for now
     m->verify_seq = std::getenv("KQ_VERIFY_SEQ") && std::atoi(std::getenv("KQ_VERIFY_SEQ")) == 1;
+    m->prof = std::getenv("KQ_PHASE_TIMES") && std::atoi(std::getenv("KQ_PHASE_TIMES")) == 1;
     m->attn_nsplit = std::min(ATT_SPLITS_MAX, std::max(1, m->nsm / c.n_kv_heads));
     m->apart = dalloc<float>(m, (size_t)c.n_kv_heads * m->attn_nsplit * (c.n_heads / c.n_kv_heads) * c.head_dim, ok);
     m->apart_ml = dalloc<float>(m, (size_t)c.n_kv_heads * m->attn_nsplit * (c.n_heads / c.n_kv_heads) * 2, ok);
@@ -759,11 +933,19 @@ extern "C" kq_model* kq_model_create_tp(const kq_config* cfg, int device, int ra
   if (!nccl().ok) { set_err(KQ_ERR_BACKEND, "NCCL could not be loaded"); model_release(m); return nullptr; }
   ncclUniqueId id;
   std::memcpy(&id, id128, 128);
-  const ncclResult_t r = nccl().CommInitRank(&m->comm, world, id, rank);
-  if (r != ncclSuccess) {
-    set_err(KQ_ERR_BACKEND, std::string("ncclCommInitRank: ") + nccl().GetErrorString(r));
+  ncclConfig_t cfgc = NCCL_CONFIG_INITIALIZER;
+  cfgc.blocking = 0;   // every wait on the peers is then a host poll with a deadline
+  const ncclResult_t r = nccl().CommInitRankConfig(&m->comm, world, id, rank, &cfgc);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    set_err(KQ_ERR_BACKEND, std::string("ncclCommInitRankConfig: ") + nccl().GetErrorString(r));
     m->comm = nullptr;
     model_release(m);
+    return nullptr;
+  }
+  if (nccl_wait(m, r, "ncclCommInitRankConfig") != KQ_OK) {
+    const std::string keep = g_err;
+    model_release(m);
+    set_err(KQ_ERR_TIMEOUT, keep);
     return nullptr;
   }
   return m;
@@ -1454,7 +1636,9 @@ extern "C" int kq_feed_batch(kq_model* m, const int32_t* toks, int n, int pos) {
   for (int c0 = 0; c0 < n; c0 += MM_MAXM)
     if ((rc = verify_pass(m, toks + c0, 0, std::min(MM_MAXM, n - c0), pos + c0, chain.depth, chain.anc, false)))
       return rc;
-  CU(cudaStreamSynchronize(m->stream));
+  prof_mark(m, PC_END);
+  if ((rc = tp_sync(m))) return rc;
+  prof_flush(m);
   return check_dev_err(m);
 }
 
@@ -1515,6 +1699,18 @@ extern "C" int kq_decode_loop(kq_model* m, int tok, int pos, int n, int32_t* out
   CU(cudaMemcpyAsync(out, m->out_ids, (size_t)n * sizeof(int32_t), cudaMemcpyDeviceToHost, m->stream));
   CU(cudaStreamSynchronize(m->stream));
   return check_dev_err(m);
+}
+
+extern "C" int kq_phase_times(kq_model* m, float* ms4) {
+  int rc = model_check(m);
+  if (rc) return rc;
+  if (!ms4) return set_err(KQ_ERR_ARG, "null output");
+  if (!m->prof) return set_err(KQ_ERR_ARG, "the time split is off (set KQ_PHASE_TIMES=1 before creating the model)");
+  for (int i = 0; i < 4; ++i) {
+    ms4[i] = (float)m->pms[i];
+    m->pms[i] = 0.0;
+  }
+  return KQ_OK;
 }
 
 extern "C" int kq_step_kernels(kq_model* m) {
@@ -1654,9 +1850,10 @@ static cudaError_t tmm_launch(const TmmParams& P, cudaStream_t s, bool pdl) {
 // model's stream). World 1: nothing.
 static int tp_allreduce(kq_model* m, float* buf, size_t n) {
   if (m->tp_world == 1) return KQ_OK;
-  const ncclResult_t r = nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum, m->comm, m->stream);
-  if (r != ncclSuccess) return set_err(KQ_ERR_BACKEND, std::string("ncclAllReduce: ") + nccl().GetErrorString(r));
-  return KQ_OK;
+  prof_mark(m, PC_COMM);
+  int rc = tp_alive(m);
+  if (rc) return rc;
+  return nccl_wait(m, nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum, m->comm, m->stream), "ncclAllReduce");
 }
 
 static int batch_buffers(kq_model* m) {
@@ -1710,6 +1907,7 @@ static bool batch_supported(const kq_model* m) {
 // xscale: the per-token scales of the packed input xp (k_bnorm / k_xpack_tok), or null.
 static int launch_tmm(kq_model* m, const SegSpec* ss, int nseg, const __half* xp, const float* xscale, int out_ld,
                       const BatchParams& B) {
+  prof_mark(m, PC_GEMM);
   TmmParams P;
   tmm_fill(ss, nseg, B.M, m->device, P);
   P.xp = xp;
@@ -1731,6 +1929,7 @@ static int launch_tmm(kq_model* m, const SegSpec* ss, int nseg, const __half* xp
 }
 
 static int launch_bnorm(kq_model* m, int M, bool embed, const float* gamma, bool add) {
+  prof_mark(m, PC_OTHER);
   BNormParams P;
   std::memset(&P, 0, sizeof(P));
   P.M = M; P.D = m->c.dim; P.tok = m->btok;
@@ -1750,6 +1949,7 @@ static int launch_mlp(kq_model* m, LayerW& w, float* y, const BatchParams& B) {
   SegSpec sg[1] = {{w.gu, EPI_SWIGLU, m->bmf, nullptr}};
   int rc = launch_tmm(m, sg, 1, m->bxd, m->bxs_n, m->ffn_l, B);
   if (rc) return rc;
+  prof_mark(m, PC_GEMM);
   const XPackParams X = {m->bmf, m->ffn_l, m->ffn_l, Npad, m->bxf, m->bxs_f};
   CU(launch_pdl(k_xpack_tok, dim3((unsigned)M), dim3(XP_THREADS), 0, m->stream, X));
   SegSpec sd[1] = {{w.down, EPI_F32, y, nullptr}};
@@ -1757,6 +1957,7 @@ static int launch_mlp(kq_model* m, LayerW& w, float* y, const BatchParams& B) {
 }
 
 static int launch_battn(kq_model* m, const __half* kc, const __half* vc, int npos, const BatchParams& B) {
+  prof_mark(m, PC_ATTN);
   const kq_config& c = m->c;
   const int G = c.n_heads / c.n_kv_heads, M = B.M;
   const int rowgroups = (M * G + BA_ROWS - 1) / BA_ROWS, nblocks = (npos + BA_KB - 1) / BA_KB;
@@ -1788,25 +1989,26 @@ static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int p
                        const unsigned long long (*anc)[2], bool head, int seq) {
   const kq_config& c = m->c;
   const int M = b1 - b0;
-  std::vector<int> tk(M), sl(M), rp(M);
-  std::vector<unsigned long long> mk(2 * M);
+  kq_model::MetaSlot* ms = nullptr;
+  int rc = meta_acquire(m, &ms);
+  if (rc) return rc;
   for (int i = 0; i < M; ++i) {
-    tk[i] = tokens[b0 + i];
-    sl[i] = pos + b0 + i;
-    rp[i] = pos + depth[b0 + i];
-    mk[2 * i] = anc[b0 + i][0];
-    mk[2 * i + 1] = anc[b0 + i][1];
+    ms->tok[i] = tokens[b0 + i];
+    ms->slot[i] = pos + b0 + i;
+    ms->rpos[i] = pos + depth[b0 + i];
+    ms->mask[2 * i] = anc[b0 + i][0];
+    ms->mask[2 * i + 1] = anc[b0 + i][1];
   }
   cudaStream_t s = m->stream;
-  CU(cudaMemcpyAsync(m->btok, tk.data(), M * sizeof(int), cudaMemcpyHostToDevice, s));
-  CU(cudaMemcpyAsync(m->bslot, sl.data(), M * sizeof(int), cudaMemcpyHostToDevice, s));
-  CU(cudaMemcpyAsync(m->brpos, rp.data(), M * sizeof(int), cudaMemcpyHostToDevice, s));
-  CU(cudaMemcpyAsync(m->bmask, mk.data(), 2 * M * sizeof(unsigned long long), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->btok, ms->tok, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->bslot, ms->slot, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->brpos, ms->rpos, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->bmask, ms->mask, 2 * M * sizeof(unsigned long long), cudaMemcpyHostToDevice, s));
+  if ((rc = meta_release(m))) return rc;
   BatchParams B;
   B.M = M; B.slot = m->bslot; B.rpos = m->brpos; B.mask = m->bmask; B.tree_base = pos; B.seq = nullptr;
   const size_t sstride = (size_t)m->nkv_l * c.ctx * c.head_dim;   // one sequence of the batched-decode caches
   const int QD = m->nh_l * c.head_dim;
-  int rc;
   for (int l = 0; l < c.n_layers; ++l) {
     LayerW& w = m->L[l];
     if ((rc = launch_bnorm(m, M, l == 0, w.attn_norm, l > 0))) return rc;
@@ -1835,6 +2037,7 @@ static int head_argmax(kq_model* m, int M, const BatchParams& B, int* out_ids, s
   const size_t V = (size_t)m->vocab_l;   // this rank's vocabulary slice
   SegSpec sh[1] = {{m->out, EPI_F32, m->vlogits + row0 * V, nullptr}};
   if ((rc = launch_tmm(m, sh, 1, m->bxd, m->bxs_n, (int)V, B))) return rc;
+  prof_mark(m, PC_OTHER);
   if (m->tp_world == 1) {
     k_argmax_rows<<<M, 256, 0, s>>>(m->vlogits + row0 * V, (int)V, out_ids);
     CU(cudaGetLastError());
@@ -1847,9 +2050,10 @@ static int head_argmax(kq_model* m, int M, const BatchParams& B, int* out_ids, s
   int* si = m->tp_idx + (size_t)W * MM_MAXM;
   k_argmax_rows_vi<<<M, 256, 0, s>>>(m->vlogits + row0 * V, (int)V, m->tp_rank * (int)V, sv, si);
   CU(cudaGetLastError());
-  if (nccl().AllGather(sv, m->tp_val, (size_t)MM_MAXM, ncclFloat32, m->comm, s) != ncclSuccess ||
-      nccl().AllGather(si, m->tp_idx, (size_t)MM_MAXM, ncclInt32, m->comm, s) != ncclSuccess)
-    return set_err(KQ_ERR_BACKEND, "NCCL all-gather of the head's argmax failed");
+  if ((rc = tp_alive(m)) ||
+      (rc = nccl_wait(m, nccl().AllGather(sv, m->tp_val, (size_t)MM_MAXM, ncclFloat32, m->comm, s), "ncclAllGather")) ||
+      (rc = nccl_wait(m, nccl().AllGather(si, m->tp_idx, (size_t)MM_MAXM, ncclInt32, m->comm, s), "ncclAllGather")))
+    return rc;
   k_pick_rows<<<(M + 127) / 128, 128, 0, s>>>(m->tp_val, m->tp_idx, W, MM_MAXM, M, out_ids);
   CU(cudaGetLastError());
   return KQ_OK;
@@ -1894,9 +2098,12 @@ extern "C" int kq_verify(kq_model* m, const int32_t* tokens, const int32_t* pare
     }
     CU(cudaMemcpyAsync(m->vlogits + i * V, m->logits, V * sizeof(float), cudaMemcpyDeviceToDevice, m->stream));
   }
+  prof_mark(m, PC_END);
+  if ((rc = tp_sync(m))) return rc;   // the results are read once the stream drained (bounded for TP)
+  prof_flush(m);
   if (best) CU(cudaMemcpyAsync(best, m->out_ids, (size_t)n * sizeof(int32_t), cudaMemcpyDeviceToHost, m->stream));
   if (logits) CU(cudaMemcpyAsync(logits, m->vlogits, (size_t)n * V * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
-  CU(cudaStreamSynchronize(m->stream));
+  if (best || logits) CU(cudaStreamSynchronize(m->stream));
   m->vn = n;
   return check_dev_err(m);
 }
@@ -2012,7 +2219,7 @@ extern "C" int kq_batch_feed(kq_model* m, int seq, const int32_t* toks, int n, i
   for (int c0 = 0; c0 < n; c0 += MM_MAXM)
     if ((rc = verify_pass(m, toks + c0, 0, std::min(MM_MAXM, n - c0), pos + c0, chain.depth, chain.anc, false, seq)))
       return rc;
-  CU(cudaStreamSynchronize(m->stream));
+  if ((rc = tp_sync(m))) return rc;
   return check_dev_err(m);
 }
 
@@ -2037,10 +2244,16 @@ extern "C" int kq_batch_step(kq_model* m, const int32_t* seqs, const int32_t* to
   if ((rc = verify_buffers(m)) || (rc = batch_buffers(m))) return rc;
   cudaStream_t s = m->stream;
   const int M = n;
-  CU(cudaMemcpyAsync(m->btok, toks, M * sizeof(int), cudaMemcpyHostToDevice, s));
-  CU(cudaMemcpyAsync(m->bslot, pos, M * sizeof(int), cudaMemcpyHostToDevice, s));
-  CU(cudaMemcpyAsync(m->brpos, pos, M * sizeof(int), cudaMemcpyHostToDevice, s));
-  CU(cudaMemcpyAsync(m->bseq, seqs, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  kq_model::MetaSlot* ms = nullptr;
+  if ((rc = meta_acquire(m, &ms))) return rc;
+  std::memcpy(ms->tok, toks, M * sizeof(int));
+  std::memcpy(ms->slot, pos, M * sizeof(int));
+  std::memcpy(ms->seq, seqs, M * sizeof(int));
+  CU(cudaMemcpyAsync(m->btok, ms->tok, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->bslot, ms->slot, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->brpos, ms->slot, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->bseq, ms->seq, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  if ((rc = meta_release(m))) return rc;
   BatchParams B;
   std::memset(&B, 0, sizeof(B));
   B.M = M; B.slot = m->bslot; B.rpos = m->brpos; B.seq = m->bseq;
@@ -2059,6 +2272,7 @@ extern "C" int kq_batch_step(kq_model* m, const int32_t* seqs, const int32_t* to
     if ((rc = launch_tmm(m, qkv, 3, m->bxd, m->bxs_n, QD, B))) return rc;
     D.kc = w.bkc;
     D.vc = w.bvc;
+    prof_mark(m, PC_ATTN);
     cudaError_t e = G == 1 ? launch_dattn_t<1>(D, M, m->nkv_l, s) : G == 2 ? launch_dattn_t<2>(D, M, m->nkv_l, s)
                   : G == 4 ? launch_dattn_t<4>(D, M, m->nkv_l, s) : launch_dattn_t<8>(D, M, m->nkv_l, s);
     CU(e);
@@ -2070,8 +2284,10 @@ extern "C" int kq_batch_step(kq_model* m, const int32_t* seqs, const int32_t* to
     if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;
   }
   if ((rc = head_argmax(m, M, B, m->out_ids))) return rc;
-  CU(cudaMemcpyAsync(out, m->out_ids, M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-  CU(cudaStreamSynchronize(s));
+  prof_mark(m, PC_END);
+  if ((rc = tp_sync(m))) return rc;
+  prof_flush(m);
+  CU(cudaMemcpy(out, m->out_ids, M * sizeof(int32_t), cudaMemcpyDeviceToHost));
   return check_dev_err(m);
 }
 

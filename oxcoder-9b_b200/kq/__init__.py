@@ -80,6 +80,7 @@ SIGNATURES = {
     "kq_decode_loop": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, PI32]),
     "kq_time_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, PF]),
     "kq_step_kernels": (C.c_int, [C.c_void_p]),
+    "kq_phase_times": (C.c_int, [C.c_void_p, PF]),
     "kq_ffn_block": (C.c_int, [C.c_void_p, C.c_int, PF, C.c_int, PF]),
     "kq_time_ffn_block": (C.c_int, [C.c_void_p, C.c_int, C.c_int, PF]),
     "kq_qmat_create": (C.c_void_p, [C.c_int, C.c_int, C.c_int, C.c_int]),
@@ -422,6 +423,13 @@ class Engine(object):
         ms = C.c_float()
         check(lib().kq_time_ffn_block(self.h, int(M), int(n), C.byref(ms)))
         return ms.value
+
+    def phase_times(self):
+        """ms per category of the batched passes since the last call (model created with
+        KQ_PHASE_TIMES=1): {"gemm", "attention", "allreduce", "other"}."""
+        out = np.zeros(4, np.float32)
+        check(lib().kq_phase_times(self.h, _ptr(out)))
+        return dict(zip(("gemm", "attention", "allreduce", "other"), [float(v) for v in out]))
 
     def step_kernels(self):
         """Kernels one decode step launches (kernel nodes of the step graph)."""

@@ -96,3 +96,74 @@ def test_tp_prefill_and_steps_match_whole_model(kq, world):
                 got = res[r][1][l][w].view(np.float16).astype(np.float32).reshape(end, nkv_l, hd)
                 ref = kv[l][w].view(np.float16).astype(np.float32).reshape(end, CFG["NKV"], hd)[:, r * nkv_l:(r + 1) * nkv_l]
                 assert rel_l2(got, ref) < 1e-3, (r, l, w)
+
+
+def _loss_rank(rank, uid, q_out, q_in):
+    """Rank 1 stops taking part after the prefill (it keeps its process and memory until rank 0
+    is done); rank 0's next step must end with a timeout, not hang."""
+    try:
+        sys.path.insert(0, PKG)
+        import time
+        import kq
+        e = kq.Engine(_cfg(kq, CFG), device=rank, seed=0, tp=(rank, 2, uid))
+        e.feed_batch(list(range(1, 40)), 0)            # collectives of both ranks complete
+        if rank == 1:
+            q_out.put((1, "left"))
+            q_in.get(timeout=240)                      # rank 0 finished; no collective of ours in flight
+            e.close()
+            return
+        assert q_in.get(timeout=120) == "rank 1 left"
+        t0 = time.time()
+        try:
+            e.step(5, 39)                              # its all-reduce has no partner
+            res = "no error"
+        except Exception as ex:
+            res = repr(ex)
+        dt = time.time() - t0
+        try:
+            e.step(5, 39)
+            again = "no error"
+        except Exception as ex:
+            again = repr(ex)
+        e.close()
+        q_out.put((0, (res, dt, again)))
+    except Exception as ex:
+        q_out.put((rank, "error: " + repr(ex)))
+
+
+def test_tp_silent_peer_times_out(kq):
+    """Failure detection on the NCCL path (the reference bounds its cross-GPU wait and reports
+    it: kindi.cu:1007-1014, tp.py:788-792): a rank whose peer stops answering gets
+    KQ_ERR_TIMEOUT after KQ_TP_TIMEOUT_MS, its communicator aborted, instead of blocking in
+    NCCL. NVLS stays off (NCCL_NVLS_ENABLE=0) and the silent rank leaves between steps."""
+    if kq.lib().kq_device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = {"NCCL_NVLS_ENABLE": "0", "KQ_TP_TIMEOUT_MS": "3000"}
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
+    try:
+        uid = kq.tp_unique_id()
+        ctx = mp.get_context("spawn")
+        q_out, q0, q1 = ctx.Queue(), ctx.Queue(), ctx.Queue()
+        p0 = ctx.Process(target=_loss_rank, args=(0, uid, q_out, q0))
+        p1 = ctx.Process(target=_loss_rank, args=(1, uid, q_out, q1))
+        p0.start()
+        p1.start()
+        first = q_out.get(timeout=300)
+        assert first == (1, "left"), first
+        q0.put("rank 1 left")
+        r0 = q_out.get(timeout=300)
+        q1.put("done")
+        p0.join(timeout=60)
+        p1.join(timeout=60)
+    finally:
+        for k, v in old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    assert r0[0] == 0 and not isinstance(r0[1], str), r0
+    res, dt, again = r0[1]
+    assert "did not answer" in res, res
+    assert 2.5 < dt < 60, dt
+    assert "aborted" in again, again
