@@ -484,10 +484,16 @@ def run_profile_mode(args):
         print(json.dumps({"mode": "gemm", "rows": 24576, "cols": 4096, "tokens": 45, "checksum": float(np.abs(Y).sum())}))
         return 0
     if args.mode == "gemv-only":
-        mats = [kq.QMat(12, 12288, 4096).fill_synthetic(0, 1000 + i) for i in range(16)]
+        # the config-0 Q4_K GEMV (or `--rows` rows of it) over enough weight copies to exceed L2
+        rows = args.rows
+        nbytes = rows * 16 * 144
+        copies = max(2, min(16, -(-453 * 10 ** 6 // nbytes)))
+        mats = [kq.QMat(12, rows, 4096).fill_synthetic(0, 1000 + i) for i in range(copies)]
         kq.time_matvec(mats, args.warmup)
         ms = kq.time_matvec(mats, args.steps)
-        print(json.dumps({"mode": "gemv-only", "ms_per_launch": ms, "gbs": CFG0_BYTES / (ms * 1e-3) / 1e9}))
+        algo = nbytes + 4 * 4096 + 4 * rows
+        print(json.dumps({"mode": "gemv-only", "rows": rows, "copies": copies, "ms_per_launch": ms,
+                          "gbs": algo / (ms * 1e-3) / 1e9}))
         return 0
     e = kq.Engine(kq.Config.default(ctx=CTX, n_layers=args.layers), seed=0)
     pos0 = CTX - (args.steps + args.warmup) - 1
@@ -506,6 +512,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=32, help="decode-only: layers of the model (small ncu captures)")
+    ap.add_argument("--rows", type=int, default=12288, help="gemv-only: rows of the Q4_K x 4096 matrix (12288 = config-0)")
     ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only", "spec", "prefill", "gemm", "batch-decode", "tp-split"],
                     help="decode-only / gemv-only: the small commands the ncu captures in profiles/ run")
     args = ap.parse_args()
@@ -626,7 +633,7 @@ def run_ours(args, rank, world, local):
                     "api": "kq_step via ctypes, host-timed"},
             "gpu_launches": step_kernels * K,
             "gpu_launches_per_step": step_kernels,
-            "roofline": {"bound": "hbm", "kernel": "k_gemv (config-0 Q4_K 12288x4096, 16 rotating copies)",
+            "roofline": {"bound": "hbm", "kernel": "k_gemv_mma (config-0 Q4_K 12288x4096, 16 rotating copies)",
                          "achieved": gemv_gbs, "peak": hbm, "unit": "GB/s", "frac": gemv_gbs / hbm,
                          "traffic": CFG0_TRAFFIC, "traffic_source": "ncu capture of the same kernel and shape, not measured by this run",
                          "peak_source": "measured" if pk else "fallback",

@@ -9,6 +9,7 @@
 #include "kq_common.cuh"
 #include "kq_qformat.cuh"
 #include "kq_gemv.cuh"
+#include "kq_gemv_mma.cuh"
 #include "kq_attn.cuh"
 #include "kq_decode.cuh"
 #include "kq_accept.cuh"
@@ -62,6 +63,12 @@ static GemvFn gemv_fn(int tm, int rpg) {
   return tab[tm - 1][rpg == 1 ? 0 : rpg == 2 ? 1 : 2];
 }
 
+// The tensor-core Q4_K GEMV for nw consumer warps, nb 16-row blocks per stage, C columns.
+static GmFn gm_fn(int nw, int nb, int C) {
+  if (nw == 16) return nb == 2 ? gm_fn_for<16, 2>(C) : gm_fn_for<16, 1>(C);
+  return nb == 2 ? gm_fn_for<8, 2>(C) : gm_fn_for<8, 1>(C);
+}
+
 // ------------------------------------------------------------------------------ per-device context
 struct DevCtx {
   bool init = false;
@@ -94,6 +101,10 @@ static int dev_init(int device) {
   for (int tm = 1; tm <= 3; ++tm)
     for (int ri = 0; ri < 3; ++ri)
       CU(cudaFuncSetAttribute(gemv_fn(tm, 1 << ri), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.smem_optin));
+  for (int nw : {8, 16})
+    for (int nb : {1, 2})
+      for (int c : {256, 12288})
+        CU(cudaFuncSetAttribute(gm_fn(nw, nb, c), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.smem_optin));
   {
     cudaFuncAttributes fa;
     CU(cudaFuncGetAttributes(&fa, k_tmm));
@@ -227,6 +238,7 @@ static int qmat_upload_mapped(kq_qmat* a, const void* host, size_t bytes, int R_
 struct GemvPlan {
   int TR, LPR, NRG, RPG, TM, stage_bytes, nslots, threads, grid;
   size_t smem;
+  bool mma;      // k_gemv_mma (all segments Q4_K) instead of k_gemv
 };
 
 static const size_t KQ_SMEM_BUDGET = 220 * 1024;
@@ -286,7 +298,42 @@ static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, boo
     }
   }
   if (!found) return set_err(KQ_ERR_ARG, "no valid GEMV launch shape for this column count");
+  pl.mma = false;
   return KQ_OK;
+}
+
+// Launch shape of the tensor-core Q4_K GEMV (k_gemv_mma): stages of 16 rows, as many ring slots
+// as shared memory holds (at least 2). False when the segments are not all Q4_K, the shape does
+// not fit, or KQ_GEMV_MMA=0 (a comparison switch) asks for k_gemv.
+static bool plan_gemv_mma(int C, const int* types, int nseg, const int* seg_rows, int nsm, size_t optin, GemvPlan& pl) {
+  const char* env = std::getenv("KQ_GEMV_MMA");
+  if (env && std::atoi(env) == 0) return false;
+  for (int i = 0; i < nseg; ++i)
+    if (types[i] != KQ_Q4_K) return false;
+  const int G = C / 256;
+  // 16 consumer warps, stages of two 16-row blocks (measured on config-0: 16 warps x 32 rows
+  // 9.12 us, 8 x 32 9.19, 8 x 16 11.45, 16 x 16 11.73, k_gemv 11.07; a 226 MB launch: 43.0 /
+  // 43.4 / 55.7 / 59.3 / 56.4 us; the decode step 2.16 / 2.20 / 2.34 / 2.36 / 2.45 ms).
+  // Tuning overrides: KQ_GM_WARPS (8 or 16), KQ_GM_BLOCKS (1 or 2).
+  const int nw = std::getenv("KQ_GM_WARPS") && std::atoi(std::getenv("KQ_GM_WARPS")) == 8 ? 8 : 16;
+  const int nb = std::getenv("KQ_GM_BLOCKS") && std::atoi(std::getenv("KQ_GM_BLOCKS")) == 1 ? 1 : 2;
+  const int TR = 16 * nb;
+  if (G * 256 != C || C > 8 * GM_MAXI * 32 * nw) return false;
+  const size_t budget = std::min(KQ_SMEM_BUDGET, optin);
+  const int stage_bytes = (int)align_up((size_t)TR * 144 * G, 128);
+  const size_t fixed = gm_smem_layout(0, stage_bytes, C).total + 64;
+  if (fixed + 2 * ((size_t)stage_bytes + 16) > budget) return false;
+  int nstages = 0;
+  for (int i = 0; i < nseg; ++i) nstages += (seg_rows[i] + TR - 1) / TR;
+  const int slots = std::min(8, (int)((budget - fixed) / (stage_bytes + 16)));
+  pl.TR = TR; pl.LPR = 4 * G; pl.NRG = nw; pl.RPG = nb; pl.TM = TM_Q4K;   // NRG, RPG: warps, row blocks
+  pl.stage_bytes = stage_bytes;
+  pl.nslots = slots;
+  pl.smem = gm_smem_layout(slots, stage_bytes, C).total;
+  pl.threads = (nw + 1) * 32;
+  pl.grid = std::max(1, std::min(nsm, nstages));
+  pl.mma = true;
+  return true;
 }
 
 struct SegSpec {
@@ -306,8 +353,10 @@ static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParam
     types[i] = ss[i].m->type;
     rows[i] = ss[i].m->R;
   }
-  int rc = plan_gemv(C, types, nseg, rows, pairs, nsm, g_dev[ss[0].m->device].smem_optin, pl);
-  if (rc) return rc;
+  int rc = KQ_OK;
+  if (!plan_gemv_mma(C, types, nseg, rows, nsm, g_dev[ss[0].m->device].smem_optin, pl) &&
+      (rc = plan_gemv(C, types, nseg, rows, pairs, nsm, g_dev[ss[0].m->device].smem_optin, pl)))
+    return rc;
   std::memset(&p, 0, sizeof(p));
   p.nseg = nseg;
   int st = 0;
@@ -324,7 +373,9 @@ static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParam
   p.C = C; p.G = C / 256; p.TR = pl.TR; p.LPR = pl.LPR; p.NRG = pl.NRG; p.nlanes = 1; p.tps = 1;
   p.stage_bytes = pl.stage_bytes; p.nslots = pl.nslots;
   // tuning override for sweeps: KQ_GEMV_PREFETCH stages go out before the prologue is done
-  p.prefetch = std::getenv("KQ_GEMV_PREFETCH") ? std::max(0, std::atoi(std::getenv("KQ_GEMV_PREFETCH"))) : KQ_PREFETCH_STAGES;
+  // (the tensor-core GEMV's stages are smaller: its whole ring goes out before the prologue ends)
+  p.prefetch = std::getenv("KQ_GEMV_PREFETCH") ? std::max(0, std::atoi(std::getenv("KQ_GEMV_PREFETCH")))
+                                               : pl.mma ? pl.nslots : KQ_PREFETCH_STAGES;
   return KQ_OK;
 }
 
@@ -386,6 +437,7 @@ static cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& pl, cudaStre
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
+  if (pl.mma) return cudaLaunchKernelEx(&cfg, gm_fn(pl.NRG, pl.RPG, p.C), p);
   return cudaLaunchKernelEx(&cfg, gemv_fn(pl.TM, pl.RPG), p);
 }
 
@@ -1337,7 +1389,7 @@ static int build_step(kq_model* m, bool head, bool persist, std::vector<StepOp>&
   if (!persist)
     for (StepOp& op : ops)
       if (op.kind == PH_GEMV)
-        op.tmv = tmv_plan(op.g, m->nsm, g_dev[m->device].tmv_smem, m->tv_part, m->tv_ticket, op.t, op.tgrid);
+        op.tmv = !op.pl.mma && tmv_plan(op.g, m->nsm, g_dev[m->device].tmv_smem, m->tv_part, m->tv_ticket, op.t, op.tgrid);
   return KQ_OK;
 }
 
@@ -2392,7 +2444,7 @@ static int qmat_gemv_params(kq_qmat* a, const float* x_dev, float* y_dev, Matvec
         cudaMemset(a->tv_ticket, 0, (size_t)TV_MAX_TILES * 4) != cudaSuccess)
       return set_err(KQ_ERR_MEMORY, "matvec scratch");
   }
-  L.tmv = tmv_plan(L.p, D.nsm, D.tmv_smem, a->tv_part, a->tv_ticket, L.t, L.grid);
+  L.tmv = !L.pl.mma && tmv_plan(L.p, D.nsm, D.tmv_smem, a->tv_part, a->tv_ticket, L.t, L.grid);
   return KQ_OK;
 }
 static cudaError_t matvec_launch(const MatvecLaunch& L, cudaStream_t s, bool pdl) {

@@ -593,6 +593,46 @@ __device__ __forceinline__ int gemv_group_count(const GemvParams& P, int n0, int
   return e;
 }
 
+// Epilogue of one finished row: global row `grow` of segment sg, its value, the value of row
+// grow ^ 1 (pair epilogues: SwiGLU, rotary) and whether grow is the even row of its pair.
+__device__ __forceinline__ void gemv_row_epilogue(const GemvParams& P, GemvThread& T, const Seg& sg, int grow, float fin,
+                                                  float fin_odd, bool even) {
+  const int epi = sg.epi;
+  const int pos = T.pos;
+  if (!T.kv_ok && (epi == EPI_ROPE_K || epi == EPI_V || epi == EPI_ROPE_Q)) atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
+  switch (epi) {
+    case EPI_F32: sg.out_f[grow] = fin; break;
+    case EPI_ARGMAX:
+      sg.out_f[grow] = fin;
+      if (fin > T.bv || (fin == T.bv && grow < T.bi)) { T.bv = fin; T.bi = grow; }
+      break;
+    case EPI_V: {
+      const int kv = grow / P.hd, e = grow % P.hd;
+      if (T.kv_ok) sg.out_h[((size_t)kv * P.ctx + pos) * P.hd + e] = __float2half_rn(fin);
+    } break;
+    case EPI_SWIGLU:
+      if (even) sg.out_f[grow >> 1] = __fmul_rn(silu_f(fin), fin_odd);
+      break;
+    case EPI_ROPE_Q:
+    case EPI_ROPE_K:
+      if (even) {
+        const int hh = grow / P.hd, i2 = (grow % P.hd) >> 1, half = P.hd >> 1;
+        const float c = T.rope_c[i2], sn = T.rope_s[i2];
+        const float o0 = __fsub_rn(__fmul_rn(fin, c), __fmul_rn(fin_odd, sn));
+        const float o1v = __fadd_rn(__fmul_rn(fin, sn), __fmul_rn(fin_odd, c));
+        if (epi == EPI_ROPE_Q) {
+          sg.out_f[hh * P.hd + i2] = o0;
+          sg.out_f[hh * P.hd + i2 + half] = o1v;
+        } else if (T.kv_ok) {
+          __half* dst = sg.out_h + ((size_t)hh * P.ctx + pos) * P.hd;
+          dst[i2] = __float2half_rn(o0);
+          dst[i2 + half] = __float2half_rn(o1v);
+        }
+      }
+      break;
+  }
+}
+
 // One stage (TR rows of segment segi starting at global stage s) from shared memory `buf`:
 // load this thread's slice, release the slot (one arrive per warp on `empty_bar`; the warp whose
 // arrival frees it calls on_free()), compute, reduce across the row group (reduction buffer
@@ -623,12 +663,13 @@ __device__ __forceinline__ void gemv_stage(const GemvParams& P, GemvThread& T, i
     const uint8_t* tb = buf + (size_t)(r >> 3) * TB;
     const int r8 = r & 7;
     const uint8_t* p0 = tb + (size_t)r8 * 128 * G;
-    const uint4 A = lds128(p0 + u * 16);
-    const uint4 B = lds128(p0 + (size_t)64 * G + u * 16);
+    const size_t sw = is_q4 ? (size_t)r8 << 4 : 0;   // the Q4_K chunk swizzle (kq_qformat.cuh)
+    const uint4 A = lds128(p0 + (((size_t)u * 16) ^ sw));
+    const uint4 B = lds128(p0 + (((size_t)64 * G + u * 16) ^ sw));
     a[rr][0] = A.x; a[rr][1] = A.y; a[rr][2] = A.z; a[rr][3] = A.w;
     b[rr][0] = B.x; b[rr][1] = B.y; b[rr][2] = B.z; b[rr][3] = B.w;
     if (is_q4) {
-      const uint4 M = lds128(tb + o1 + ((size_t)r8 * G + g) * 16);
+      const uint4 M = lds128(tb + o1 + (size_t)r8 * 16 * G + q4_p1_swz(G, r8, (size_t)g * 16));
       q4k_scale_words(M, h, m2[rr], m3[rr]);
       m1[rr] = M.x;
       q[rr][0] = q[rr][1] = q[rr][2] = q[rr][3] = 0;
@@ -685,47 +726,47 @@ __device__ __forceinline__ void gemv_stage(const GemvParams& P, GemvThread& T, i
   float fin_odd = 0.f;
   if (pair_epi) fin_odd = __shfl_down_sync(0xffffffffu, fin, 1);
   const int rloc = rg * RPG + u;
-  if (u < RPG && rloc < rows) {
-    const int grow = row0 + rloc;
-    const int pos = T.pos;
-    if (!T.kv_ok && (epi == EPI_ROPE_K || epi == EPI_V || epi == EPI_ROPE_Q)) atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
-    switch (epi) {
-      case EPI_F32: sg.out_f[grow] = fin; break;
-      case EPI_ARGMAX:
-        sg.out_f[grow] = fin;
-        if (fin > T.bv || (fin == T.bv && grow < T.bi)) { T.bv = fin; T.bi = grow; }
-        break;
-      case EPI_V: {
-        const int kv = grow / P.hd, e = grow % P.hd;
-        if (T.kv_ok) sg.out_h[((size_t)kv * P.ctx + pos) * P.hd + e] = __float2half_rn(fin);
-      } break;
-      case EPI_SWIGLU:
-        if ((u & 1) == 0) sg.out_f[grow >> 1] = __fmul_rn(silu_f(fin), fin_odd);
-        break;
-      case EPI_ROPE_Q:
-      case EPI_ROPE_K:
-        if ((u & 1) == 0) {
-          const int hh = grow / P.hd, i2 = (grow % P.hd) >> 1, half = P.hd >> 1;
-          const float c = T.rope_c[i2], sn = T.rope_s[i2];
-          const float o0 = __fsub_rn(__fmul_rn(fin, c), __fmul_rn(fin_odd, sn));
-          const float o1v = __fadd_rn(__fmul_rn(fin, sn), __fmul_rn(fin_odd, c));
-          if (epi == EPI_ROPE_Q) {
-            sg.out_f[hh * P.hd + i2] = o0;
-            sg.out_f[hh * P.hd + i2 + half] = o1v;
-          } else if (T.kv_ok) {
-            __half* dst = sg.out_h + ((size_t)hh * P.ctx + pos) * P.hd;
-            dst[i2] = __float2half_rn(o0);
-            dst[i2 + half] = __float2half_rn(o1v);
-          }
-        }
-        break;
-    }
-  }
+  if (u < RPG && rloc < rows) gemv_row_epilogue(P, T, sg, row0 + rloc, fin, fin_odd, (u & 1) == 0);
 }
 
 // ARGMAX epilogue across CTAs: each CTA's best (value, index) to P.part_val / P.part_idx, and
 // the last CTA (ticket) merges them in CTA order (lowest index on ties), advances the step state
 // and re-arms the ticket. Called by the consumer threads of every CTA.
+// The CTA's best (value, index) over the n entries of bestv / besti to P.part_val / P.part_idx;
+// the last CTA (ticket) merges all CTAs' pairs in CTA order (lowest index on ties), advances the
+// step state and re-arms the ticket. Thread 0 of the CTA only.
+__device__ __forceinline__ void gemv_argmax_merge(const GemvParams& P, const float* bestv, const int* besti, int n) {
+  float v0 = -FLT_MAX; int i0 = 0x7fffffff;
+  for (int r = 0; r < n; ++r)
+    if (bestv[r] > v0 || (bestv[r] == v0 && besti[r] < i0)) { v0 = bestv[r]; i0 = besti[r]; }
+  P.part_val[blockIdx.x] = v0;
+  P.part_idx[blockIdx.x] = i0;
+  __threadfence();
+  const int t = atomicAdd(P.ticket, 1);
+  if (t == (int)gridDim.x - 1) {
+    __threadfence();
+    float v1 = -FLT_MAX; int i1 = 0x7fffffff;
+    for (int c = 0; c < (int)gridDim.x; ++c) {
+      const float pv = *(volatile float*)&P.part_val[c];
+      const int pi = *(volatile int*)&P.part_idx[c];
+      if (pv > v1 || (pv == v1 && pi < i1)) { v1 = pv; i1 = pi; }
+    }
+    if (i1 == 0x7fffffff) i1 = 0;
+    // advance the device-resident step state: the next step embeds this token at pos + 1
+    DecodeState* st = P.st;
+    st->next_tok = i1;
+    if (P.out_ids && st->steps < P.out_cap) P.out_ids[st->steps] = i1;
+    st->steps += 1;
+    st->tok = i1;
+    st->pos += 1;
+    st->rpos = st->pos;          // the next step is a plain decode step
+    st->tree_base = st->pos + 1;
+    *P.ticket = 0;
+  }
+}
+
+// ARGMAX epilogue across CTAs: each CTA's best (value, index) to P.part_val / P.part_idx, and
+// the last CTA (ticket) merges them. Called by the consumer threads of every CTA.
 template <int RPG>
 __device__ __forceinline__ void gemv_argmax_tail(const GemvParams& P, uint8_t* smem, const GemvSmem& L, const GemvThread& T,
                                                  int nthr_c) {
@@ -738,34 +779,41 @@ __device__ __forceinline__ void gemv_argmax_tail(const GemvParams& P, uint8_t* s
     besti[r] = T.bi;
   }
   named_bar(KQ_BAR_ARGMAX, nthr_c);
-  if (tid == 0) {
-    float v0 = -FLT_MAX; int i0 = 0x7fffffff;
-    for (int r = 0; r < NRG * RPG; ++r)
-      if (bestv[r] > v0 || (bestv[r] == v0 && besti[r] < i0)) { v0 = bestv[r]; i0 = besti[r]; }
-    P.part_val[blockIdx.x] = v0;
-    P.part_idx[blockIdx.x] = i0;
-    __threadfence();
-    const int t = atomicAdd(P.ticket, 1);
-    if (t == (int)gridDim.x - 1) {
-      __threadfence();
-      float v1 = -FLT_MAX; int i1 = 0x7fffffff;
-      for (int c = 0; c < (int)gridDim.x; ++c) {
-        const float pv = *(volatile float*)&P.part_val[c];
-        const int pi = *(volatile int*)&P.part_idx[c];
-        if (pv > v1 || (pv == v1 && pi < i1)) { v1 = pv; i1 = pi; }
-      }
-      if (i1 == 0x7fffffff) i1 = 0;
-      // advance the device-resident step state: the next step embeds this token at pos + 1
-      DecodeState* st = P.st;
-      st->next_tok = i1;
-      if (P.out_ids && st->steps < P.out_cap) P.out_ids[st->steps] = i1;
-      st->steps += 1;
-      st->tok = i1;
-      st->pos += 1;
-      st->rpos = st->pos;          // the next step is a plain decode step
-      st->tree_base = st->pos + 1;
-      *P.ticket = 0;
+  if (tid == 0) gemv_argmax_merge(P, bestv, besti, NRG * RPG);
+}
+
+// The producer warp of a GEMV kernel (lane 0 works): this CTA's nmine stages from s_begin into the
+// ring of nslots stage buffers at `stages`, full[slot] completing on the copy; the first
+// P.prefetch stages are issued at once, the rest after the consumers' prologue (pro_bar) and as
+// slots are released (empty). On a failed wait it drains its copies in flight (bounded).
+__device__ __forceinline__ void gemv_producer(const GemvParams& P, uint8_t* stages, uint64_t* full, uint64_t* empty,
+                                              uint64_t* pro_bar, int s_begin, int nmine, int* s_fail, int* s_issued,
+                                              const int* s_done) {
+  if ((threadIdx.x & 31) != 0) return;
+  const uint64_t pol = l2_evict_first_policy();
+  int segi = 0;
+  for (int i = 0; i < nmine; ++i) {
+    const int slot = i % P.nslots;
+    const uint32_t round = (uint32_t)(i / P.nslots);
+    if (i == P.prefetch) {
+      if (!mbar_wait(pro_bar, 0, P.err, KQ_DEV_ERR_WAIT_FULL)) { *s_fail = 1; break; }
     }
+    if (i >= P.nslots) {
+      if (!mbar_wait(&empty[slot], (round - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY)) { *s_fail = 1; break; }
+    }
+    if (*(volatile int*)s_fail) break;
+    const uint8_t* src;
+    const uint32_t bytes = gemv_stage_src(P, s_begin + i, segi, &src);
+    uint8_t* buf = stages + (size_t)slot * P.stage_bytes;
+    mbar_arrive_expect_tx(&full[slot], bytes);
+    bulk_g2s(buf, src, bytes, &full[slot], pol);
+    *(volatile int*)s_issued = i + 1;
+  }
+  KQ_TRACE_AT(P.trace_id, 5);
+  if (*(volatile int*)s_fail) {
+    const int issued = *(volatile int*)s_issued;
+    for (int j = *(volatile const int*)s_done; j < issued; ++j)
+      if (!mbar_wait(&full[j % P.nslots], (uint32_t)(j / P.nslots) & 1, P.err, KQ_DEV_ERR_DRAIN)) break;
   }
 }
 
@@ -800,35 +848,7 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
 
   if (tid >= nthr_c) {
     // ---------------------------------------------------------------- producer warp
-    if (tid == nthr_c) {
-      const uint64_t pol = l2_evict_first_policy();
-      int segi = 0;
-      for (int i = 0; i < nmine; ++i) {
-        const int slot = i % P.nslots;
-        const uint32_t round = (uint32_t)(i / P.nslots);
-        // P.prefetch stages go out at once; the rest waits for the consumers' prologue.
-        if (i == P.prefetch) {
-          if (!mbar_wait(&pro_bar, 0, P.err, KQ_DEV_ERR_WAIT_FULL)) { s_fail = 1; break; }
-        }
-        if (i >= P.nslots) {
-          if (!mbar_wait(&empty[slot], (round - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY)) { s_fail = 1; break; }
-        }
-        if (*(volatile int*)&s_fail) break;
-        const uint8_t* src;
-        const uint32_t bytes = gemv_stage_src(P, s_begin + i, segi, &src);
-        uint8_t* buf = smem + L.stages + (size_t)slot * P.stage_bytes;
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        bulk_g2s(buf, src, bytes, &full[slot], pol);
-        *(volatile int*)&s_issued = i + 1;
-      }
-      KQ_TRACE_AT(P.trace_id, 5);
-      // failure path only: wait (bounded) for the copies still in flight before the CTA can exit
-      if (*(volatile int*)&s_fail) {
-        const int issued = *(volatile int*)&s_issued;
-        for (int j = *(volatile int*)&s_done; j < issued; ++j)
-          if (!mbar_wait(&full[j % P.nslots], (uint32_t)(j / P.nslots) & 1, P.err, KQ_DEV_ERR_DRAIN)) break;
-      }
-    }
+    if (tid < nthr_c + 32) gemv_producer(P, smem + L.stages, full, empty, &pro_bar, s_begin, nmine, &s_fail, &s_issued, &s_done);
     pdl_wait();
     return;
   }

@@ -42,10 +42,25 @@ __host__ __device__ inline size_t tile_plane_off(int type, int G, int plane) {
   for (int p = 0; p < plane; ++p) o += 8 * plane_row_bytes(type, p, G);
   return o;
 }
-// byte `off` of plane p of row `row`, relative to a tile-aligned base holding row 0 of a tile
+// Q4_K tiles are laid out so that the 8 rows of a tile can be read in parallel without shared-
+// memory bank conflicts (the tensor-core GEMV reads the same columns of 8 or 16 rows at once),
+// while one row stays conflict-free too (k_gemv reads consecutive chunks of one row): in plane 0
+// (the nibbles) the 16-byte chunk q of row r8 is stored at chunk q ^ r8 of its 128-byte group,
+// and in plane 1 (the 16-byte block headers) header g of row r8 at g ^ r8 when G is a multiple
+// of 8 (rows then start on 128-byte boundaries). Every access is of whole 16-byte chunks or less.
+__host__ __device__ inline size_t q4_p0_swz(int row, size_t off) { return off ^ ((size_t)(row & 7) << 4); }
+__host__ __device__ inline size_t q4_p1_swz(int G, int row, size_t off) {
+  return (G & 7) ? off : off ^ ((size_t)(row & 7) << 4);
+}
+
+// byte `off` of plane p of row `row` (offsets as in the unswizzled [8 rows][bytes] order of the
+// plane), relative to a tile-aligned base holding row 0 of a tile
 __host__ __device__ inline size_t row_plane_off(int type, int G, int row, int plane, size_t off) {
-  return (size_t)(row >> 3) * tile_bytes(type, G) + tile_plane_off(type, G, plane) +
-         (size_t)(row & 7) * plane_row_bytes(type, plane, G) + off;
+  const size_t t = (size_t)(row >> 3) * tile_bytes(type, G) + tile_plane_off(type, G, plane) +
+                   (size_t)(row & 7) * plane_row_bytes(type, plane, G);
+  if (type == Q4K && plane == 0) return t + q4_p0_swz(row, off);
+  if (type == Q4K && plane == 1) return t + q4_p1_swz(G, row, off);
+  return t + off;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -138,12 +153,11 @@ struct QViewW {   // writable view
 __device__ inline void scatter_block(const QViewW& m, int d, int g, const uint8_t* b) {
   const int G = m.G, t = m.type;
   if (t == Q4K) {
-    uint8_t* meta = m.base + row_plane_off(t, G, d, 1, (size_t)g * 16);
+    uint8_t* meta = m.base + row_plane_off(t, G, d, 1, (size_t)g * 16);   // 16 contiguous bytes
     for (int i = 0; i < 16; i++) meta[i] = b[i];
-    uint8_t* row = m.base + row_plane_off(t, G, d, 0, 0);
     for (int o = 0; o < 128; o++) {
       const int h = o >> 6, c = (o >> 5) & 1, jh = (o >> 4) & 1, jp = o & 15;
-      row[(size_t)c * 64 * G + (size_t)g * 64 + (2 * h + jh) * 16 + jp] = b[16 + o];
+      m.base[row_plane_off(t, G, d, 0, (size_t)c * 64 * G + (size_t)g * 64 + (2 * h + jh) * 16 + jp)] = b[16 + o];
     }
   } else {
     uint8_t* row = m.base + row_plane_off(t, G, d, 0, 0);
