@@ -484,16 +484,18 @@ def run_profile_mode(args):
         print(json.dumps({"mode": "gemm", "rows": 24576, "cols": 4096, "tokens": 45, "checksum": float(np.abs(Y).sum())}))
         return 0
     if args.mode == "gemv-only":
-        # the config-0 Q4_K GEMV (or `--rows` rows of it) over enough weight copies to exceed L2
-        rows = args.rows
-        nbytes = rows * 16 * 144
+        # the config-0 Q4_K GEMV (or `--rows` x `--cols` of `--qtype`) over enough weight copies
+        # to exceed L2
+        rows, cols = args.rows, args.cols
+        qt = 12 if args.qtype == "q4k" else 14
+        nbytes = rows * (cols // 256) * (144 if qt == 12 else 210)
         copies = max(2, min(16, -(-453 * 10 ** 6 // nbytes)))
-        mats = [kq.QMat(12, rows, 4096).fill_synthetic(0, 1000 + i) for i in range(copies)]
+        mats = [kq.QMat(qt, rows, cols).fill_synthetic(0, 1000 + i) for i in range(copies)]
         kq.time_matvec(mats, args.warmup)
         ms = kq.time_matvec(mats, args.steps)
-        algo = nbytes + 4 * 4096 + 4 * rows
-        print(json.dumps({"mode": "gemv-only", "rows": rows, "copies": copies, "ms_per_launch": ms,
-                          "gbs": algo / (ms * 1e-3) / 1e9}))
+        algo = nbytes + 4 * cols + 4 * rows
+        print(json.dumps({"mode": "gemv-only", "qtype": args.qtype, "rows": rows, "cols": cols, "copies": copies,
+                          "ms_per_launch": ms, "gbs": algo / (ms * 1e-3) / 1e9}))
         return 0
     e = kq.Engine(kq.Config.default(ctx=CTX, n_layers=args.layers), seed=0)
     pos0 = CTX - (args.steps + args.warmup) - 1
@@ -512,7 +514,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=32, help="decode-only: layers of the model (small ncu captures)")
-    ap.add_argument("--rows", type=int, default=12288, help="gemv-only: rows of the Q4_K x 4096 matrix (12288 = config-0)")
+    ap.add_argument("--rows", type=int, default=12288, help="gemv-only: rows of the matrix (12288 = config-0)")
+    ap.add_argument("--cols", type=int, default=4096, help="gemv-only: columns of the matrix")
+    ap.add_argument("--qtype", default="q4k", choices=["q4k", "q6k"], help="gemv-only: quantisation of the matrix")
     ap.add_argument("--mode", default="full", choices=["full", "decode-only", "gemv-only", "spec", "prefill", "gemm", "batch-decode", "tp-split"],
                     help="decode-only / gemv-only: the small commands the ncu captures in profiles/ run")
     args = ap.parse_args()

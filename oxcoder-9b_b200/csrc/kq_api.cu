@@ -64,9 +64,13 @@ static GemvFn gemv_fn(int tm, int rpg) {
 }
 
 // The tensor-core Q4_K GEMV for nw consumer warps, nb 16-row blocks per stage, C columns.
-static GmFn gm_fn(int nw, int nb, int C) {
-  if (nw == 16) return nb == 2 ? gm_fn_for<16, 2>(C) : gm_fn_for<16, 1>(C);
-  return nb == 2 ? gm_fn_for<8, 2>(C) : gm_fn_for<8, 1>(C);
+static GmFn gm_fn(int nw, int nb, int C, int ty) {
+  if (ty == 1) {
+    if (nw == 16) return nb == 2 ? gm_fn_for<16, 2, 1>(C) : gm_fn_for<16, 1, 1>(C);
+    return nb == 2 ? gm_fn_for<12, 2, 1>(C) : gm_fn_for<12, 1, 1>(C);
+  }
+  if (nw == 16) return nb == 2 ? gm_fn_for<16, 2, 2>(C) : gm_fn_for<16, 1, 2>(C);
+  return nb == 2 ? gm_fn_for<12, 2, 2>(C) : gm_fn_for<12, 1, 2>(C);
 }
 
 // ------------------------------------------------------------------------------ per-device context
@@ -101,10 +105,11 @@ static int dev_init(int device) {
   for (int tm = 1; tm <= 3; ++tm)
     for (int ri = 0; ri < 3; ++ri)
       CU(cudaFuncSetAttribute(gemv_fn(tm, 1 << ri), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.smem_optin));
-  for (int nw : {8, 16})
+  for (int nw : {12, 16})
     for (int nb : {1, 2})
       for (int c : {256, 12288})
-        CU(cudaFuncSetAttribute(gm_fn(nw, nb, c), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.smem_optin));
+        for (int ty : {1, 2})
+          CU(cudaFuncSetAttribute(gm_fn(nw, nb, c, ty), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.smem_optin));
   {
     cudaFuncAttributes fa;
     CU(cudaFuncGetAttributes(&fa, k_tmm));
@@ -237,8 +242,9 @@ static int qmat_upload_mapped(kq_qmat* a, const void* host, size_t bytes, int R_
 // ------------------------------------------------------------------------------ GEMV planning
 struct GemvPlan {
   int TR, LPR, NRG, RPG, TM, stage_bytes, nslots, threads, grid;
+  int tr4, tr6;  // k_gemv_mma: rows per stage of the Q4_K and of the Q6_K segments
   size_t smem;
-  bool mma;      // k_gemv_mma (all segments Q4_K) instead of k_gemv
+  bool mma;      // k_gemv_mma instead of k_gemv
 };
 
 static const size_t KQ_SMEM_BUDGET = 220 * 1024;
@@ -302,34 +308,64 @@ static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, boo
   return KQ_OK;
 }
 
-// Launch shape of the tensor-core Q4_K GEMV (k_gemv_mma): stages of 16 rows, as many ring slots
-// as shared memory holds (at least 2). False when the segments are not all Q4_K, the shape does
-// not fit, or KQ_GEMV_MMA=0 (a comparison switch) asks for k_gemv.
+// Launch shape of the tensor-core GEMV (k_gemv_mma): Q4_K stages of 16 NB rows, Q6_K stages of
+// nt6 8-row tiles, ring slots of the larger stage, as many as shared memory holds (at least 2).
+// False when a segment is of another type, the shape does not fit, or KQ_GEMV_MMA=0 (a
+// comparison switch) asks for k_gemv.
 static bool plan_gemv_mma(int C, const int* types, int nseg, const int* seg_rows, int nsm, size_t optin, GemvPlan& pl) {
   const char* env = std::getenv("KQ_GEMV_MMA");
   if (env && std::atoi(env) == 0) return false;
-  for (int i = 0; i < nseg; ++i)
-    if (types[i] != KQ_Q4_K) return false;
+  bool has4 = false, has6 = false;
+  for (int i = 0; i < nseg; ++i) {
+    if (types[i] != KQ_Q4_K && types[i] != KQ_Q6_K) return false;
+    has4 |= types[i] == KQ_Q4_K;
+    has6 |= types[i] == KQ_Q6_K;
+  }
+  // Q6_K: the tensor-core consumer wins inside a mixed launch (the decode step's q/k/v GEMV: its
+  // compact code and one launch shape for both types) but issues more instructions per weight
+  // than k_gemv's dp4a form, so a launch of Q6_K segments only stays on k_gemv (measured, Q6_K
+  // 151936 x 4096: 100 us k_gemv, 147 us here; 4096 x 12288: 15.0 / 16.7 us). Comparison
+  // switch KQ_GEMV_MMA6: 0 = never for Q6_K, 1 = always.
+  const char* e6 = std::getenv("KQ_GEMV_MMA6");
+  const int mma6 = e6 ? std::atoi(e6) : -1;
+  if (has6 && (mma6 == 0 || (mma6 < 0 && !has4))) return false;
   const int G = C / 256;
-  // 16 consumer warps, stages of two 16-row blocks (measured on config-0: 16 warps x 32 rows
+  // 16 consumer warps, Q4_K stages of two 16-row blocks (measured on config-0: 16 warps x 32 rows
   // 9.12 us, 8 x 32 9.19, 8 x 16 11.45, 16 x 16 11.73, k_gemv 11.07; a 226 MB launch: 43.0 /
   // 43.4 / 55.7 / 59.3 / 56.4 us; the decode step 2.16 / 2.20 / 2.34 / 2.36 / 2.45 ms).
-  // Tuning overrides: KQ_GM_WARPS (8 or 16), KQ_GM_BLOCKS (1 or 2).
-  const int nw = std::getenv("KQ_GM_WARPS") && std::atoi(std::getenv("KQ_GM_WARPS")) == 8 ? 8 : 16;
+  // Tuning overrides: KQ_GM_WARPS (12 or 16), KQ_GM_BLOCKS (1 or 2), KQ_GM6_TILES (1, 2 or 4).
+  const int nw = std::getenv("KQ_GM_WARPS") && std::atoi(std::getenv("KQ_GM_WARPS")) == 12 ? 12 : 16;
   const int nb = std::getenv("KQ_GM_BLOCKS") && std::atoi(std::getenv("KQ_GM_BLOCKS")) == 1 ? 1 : 2;
-  const int TR = 16 * nb;
+  const int want6 = std::getenv("KQ_GM6_TILES") ? std::atoi(std::getenv("KQ_GM6_TILES")) : 0;
   if (G * 256 != C || C > 8 * GM_MAXI * 32 * nw) return false;
   const size_t budget = std::min(KQ_SMEM_BUDGET, optin);
-  const int stage_bytes = (int)align_up((size_t)TR * 144 * G, 128);
-  const size_t fixed = gm_smem_layout(0, stage_bytes, C).total + 64;
-  if (fixed + 2 * ((size_t)stage_bytes + 16) > budget) return false;
+  const size_t fixed = gm_smem_layout(0, 0, C).total + 64;
+  const int tr4 = 16 * nb;
+  const size_t b4 = has4 ? align_up((size_t)tr4 * 144 * G, 128) : 0;
+  // Q6_K: the largest stage (up to 4 tiles) that still leaves two ring slots
+  int nt6 = 0;
+  size_t stage = 0;
+  for (int nt : {4, 2, 1}) {
+    if (!has6) { stage = b4; break; }
+    if (want6 && nt != want6) continue;
+    const size_t st = std::max(b4, align_up((size_t)nt * 8 * 210 * G, 128));
+    if (fixed + 2 * (st + 16) <= budget) { nt6 = nt; stage = st; break; }
+  }
+  if (has6 && !nt6) return false;
+  if (fixed + 2 * (stage + 16) > budget) return false;
+  const int tr6 = 8 * nt6;
   int nstages = 0;
-  for (int i = 0; i < nseg; ++i) nstages += (seg_rows[i] + TR - 1) / TR;
-  const int slots = std::min(8, (int)((budget - fixed) / (stage_bytes + 16)));
-  pl.TR = TR; pl.LPR = 4 * G; pl.NRG = nw; pl.RPG = nb; pl.TM = TM_Q4K;   // NRG, RPG: warps, row blocks
-  pl.stage_bytes = stage_bytes;
+  for (int i = 0; i < nseg; ++i) {
+    const int tr = types[i] == KQ_Q4_K ? tr4 : tr6;
+    nstages += (seg_rows[i] + tr - 1) / tr;
+  }
+  const int slots = std::min(8, (int)((budget - fixed) / (stage + 16)));
+  pl.TR = std::max(has4 ? tr4 : 0, has6 ? tr6 : 0);
+  pl.tr4 = tr4; pl.tr6 = tr6;
+  pl.LPR = 4 * G; pl.NRG = nw; pl.RPG = nb; pl.TM = has6 ? 2 : 1;   // NRG, RPG, TM: warps, row blocks, types
+  pl.stage_bytes = (int)stage;
   pl.nslots = slots;
-  pl.smem = gm_smem_layout(slots, stage_bytes, C).total;
+  pl.smem = gm_smem_layout(slots, (int)stage, C).total;
   pl.threads = (nw + 1) * 32;
   pl.grid = std::max(1, std::min(nsm, nstages));
   pl.mma = true;
@@ -363,7 +399,9 @@ static int fill_gemv(const SegSpec* ss, int nseg, bool pairs, int nsm, GemvParam
   for (int i = 0; i < nseg; ++i) {
     p.seg[i].w = ss[i].m->view();
     p.seg[i].stage0 = st;
-    p.seg[i].nstage = (ss[i].m->R + pl.TR - 1) / pl.TR;
+    const int tr = !pl.mma ? pl.TR : ss[i].m->type == KQ_Q4_K ? pl.tr4 : pl.tr6;
+    p.seg[i].nstage = (ss[i].m->R + tr - 1) / tr;
+    p.seg[i].tr = tr;
     p.seg[i].epi = ss[i].epi;
     p.seg[i].out_f = ss[i].out_f;
     p.seg[i].out_h = ss[i].out_h;
@@ -406,6 +444,7 @@ static int fill_gemv_dec(const SegSpec* ss, int nseg, GemvParams& p, int& stage_
     p.seg[i].w = ss[i].m->view();
     p.seg[i].stage0 = st;
     p.seg[i].nstage = (ss[i].m->R + TR - 1) / TR;
+    p.seg[i].tr = TR;
     p.seg[i].epi = ss[i].epi;
     p.seg[i].out_f = ss[i].out_f;
     p.seg[i].out_h = ss[i].out_h;
@@ -437,7 +476,7 @@ static cudaError_t launch_gemv(const GemvParams& p, const GemvPlan& pl, cudaStre
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (pl.mma) return cudaLaunchKernelEx(&cfg, gm_fn(pl.NRG, pl.RPG, p.C), p);
+  if (pl.mma) return cudaLaunchKernelEx(&cfg, gm_fn(pl.NRG, pl.RPG, p.C, pl.TM), p);
   return cudaLaunchKernelEx(&cfg, gemv_fn(pl.TM, pl.RPG), p);
 }
 

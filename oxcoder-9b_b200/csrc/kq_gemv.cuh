@@ -66,6 +66,7 @@ __device__ __forceinline__ bool slot_attended(int t, int tree_base, unsigned lon
 struct Seg {
   QView w;
   int stage0, nstage;   // global stage range of this segment
+  int tr;               // rows per stage (whole 8-row tiles; the last stage may be shorter)
   int epi;
   float* out_f;         // F32 / ROPE_Q / SWIGLU / ARGMAX (logits)
   __half* out_h;        // ROPE_K / V: this layer's cache [n_kv][ctx][hd]
@@ -211,7 +212,7 @@ __device__ __forceinline__ void q4k_scale_words(const uint4 meta, int h, uint32_
 __device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
 
 __device__ __forceinline__ long long seg_stage_bytes(const GemvParams& P, int i) {
-  return (long long)P.TR * block_bytes(P.seg[i].w.type) * P.seg[i].w.G;
+  return (long long)P.seg[i].tr * block_bytes(P.seg[i].w.type) * P.seg[i].w.G;
 }
 
 // CTA stage range balanced by bytes (segments differ in bytes per stage).
@@ -572,8 +573,9 @@ __device__ __forceinline__ void gemv_load_xs(const GemvParams& P, uint8_t* smem,
 __device__ __forceinline__ uint32_t gemv_stage_src(const GemvParams& P, int s, int& segi, const uint8_t** src) {
   while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
   const QView& w = P.seg[segi].w;
-  const int row0 = (s - P.seg[segi].stage0) * P.TR;
-  const int rows = min(P.TR, w.R - row0);          // a multiple of 8 (whole tiles)
+  const int tr = P.seg[segi].tr;
+  const int row0 = (s - P.seg[segi].stage0) * tr;
+  const int rows = min(tr, w.R - row0);            // a multiple of 8 (whole tiles)
   *src = w.base + (size_t)(row0 >> 3) * tile_bytes(w.type, w.G);
   return (uint32_t)((size_t)(rows >> 3) * tile_bytes(w.type, w.G));
 }
@@ -646,8 +648,8 @@ __device__ __forceinline__ void gemv_stage(const GemvParams& P, GemvThread& T, i
   const int tid = threadIdx.x, rg = T.rg, u = T.u, h = T.h, g = T.g, G = P.G, NRG = P.NRG, LPR = P.LPR;
   const Seg& sg = P.seg[segi];
   const bool is_q4 = TM == TM_Q4K || (TM == TM_MIXED && sg.w.type == Q4K);
-  const int row0 = (s - sg.stage0) * P.TR;
-  const int rows = min(P.TR, sg.w.R - row0);
+  const int row0 = (s - sg.stage0) * sg.tr;
+  const int rows = min(sg.tr, sg.w.R - row0);
   const int type = is_q4 ? Q4K : Q6K;
   const size_t TB = tile_bytes(type, G);
   const size_t o1 = (size_t)8 * 128 * G;                                  // plane 1 in a tile
@@ -663,7 +665,7 @@ __device__ __forceinline__ void gemv_stage(const GemvParams& P, GemvThread& T, i
     const uint8_t* tb = buf + (size_t)(r >> 3) * TB;
     const int r8 = r & 7;
     const uint8_t* p0 = tb + (size_t)r8 * 128 * G;
-    const size_t sw = is_q4 ? (size_t)r8 << 4 : 0;   // the Q4_K chunk swizzle (kq_qformat.cuh)
+    const size_t sw = (size_t)r8 << 4;   // the plane-0 chunk swizzle (kq_qformat.cuh)
     const uint4 A = lds128(p0 + (((size_t)u * 16) ^ sw));
     const uint4 B = lds128(p0 + (((size_t)64 * G + u * 16) ^ sw));
     a[rr][0] = A.x; a[rr][1] = A.y; a[rr][2] = A.z; a[rr][3] = A.w;
@@ -674,9 +676,9 @@ __device__ __forceinline__ void gemv_stage(const GemvParams& P, GemvThread& T, i
       m1[rr] = M.x;
       q[rr][0] = q[rr][1] = q[rr][2] = q[rr][3] = 0;
     } else {
-      const uint4 H = lds128(tb + o1 + (size_t)r8 * 64 * G + u * 16);
+      const uint4 H = lds128(tb + o1 + (size_t)r8 * 64 * G + q6_qh_swz(G, r8, (size_t)u * 16));
       q[rr][0] = H.x; q[rr][1] = H.y; q[rr][2] = H.z; q[rr][3] = H.w;
-      m1[rr] = lds32(tb + o2 + (size_t)r8 * 16 * G + u * 4);
+      m1[rr] = lds32(tb + o2 + (size_t)r8 * 16 * G + q4_p1_swz(G, r8, (size_t)u * 4));
       const size_t doff = ((size_t)r8 * G + g) * 2;
       const uint32_t dw = lds32(tb + o3 + (doff & ~(size_t)3));
       m2[rr] = (doff & 2) ? (dw >> 16) : (dw & 0xFFFFu);

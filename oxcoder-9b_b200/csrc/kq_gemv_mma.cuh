@@ -34,16 +34,19 @@ constexpr int GM_MAX_TR = 32;
 constexpr int GM_MAXI = 6;                        // prologue items (8 columns) per thread at most
 
 struct GmSmem {
-  size_t stages, xb, xsf, sbs, bars, red, redd, best, rope, total;
+  size_t stages, xb, xsf, xo, sbs, bars, red, redd, best, rope, total;
 };
 // xb: the activation digits as B fragments, per pair p of sub-blocks (2p, 2p+1) of a super-block
 // and per plane L: 4 x 16 bytes, lane t's {b0, b1} of sub-block 2p then of 2p + 1.
+// xo: the Q6_K offset terms, per sub-block 8 int32 for the 8 MMA columns (plane L, half jh) at
+// 3 jh + L: -32 (-512 for the high-nibble sub-blocks) x the digit sum of the 16 columns.
 __host__ __device__ inline GmSmem gm_smem_layout(int nslots, int stage_bytes, int C) {
   GmSmem s;
   size_t o = 0;
   s.stages = o; o += (size_t)nslots * stage_bytes;
   s.xb = o = gs_align(o, 16); o += (size_t)(C / 64) * 192;    // [pair][plane][t][16 bytes]
   s.xsf = o = gs_align(o, 16); o += (size_t)(C / 32) * 4;     // digit sums per sub-block
+  s.xo = o = gs_align(o, 16); o += (size_t)(C / 32) * 32;     // [sub-block][column]
   s.sbs = o = gs_align(o, 16); o += (size_t)(C / 256) * 8;    // per super-block: s3, poison
   s.bars = o = gs_align(o, 8); o += (size_t)2 * nslots * 8;
   s.red = o = gs_align(o, 16); o += (size_t)2 * GM_MAX_WARPS * GM_MAX_TR * 4;
@@ -81,7 +84,8 @@ __device__ __forceinline__ void gm_load_gamma(const GemvParams& P, float (&gm)[M
 // one k_gemv's prologue performs (exact power-of-two steps), with the exponent taken over the
 // element's 256-column super-block (the 32 items of one warp).
 template <int NW, int MAXI>
-__device__ __forceinline__ void gm_prologue(const GemvParams& P, uint8_t* smem, const GmSmem& L, const float (&gm)[MAXI][8]) {
+__device__ __forceinline__ void gm_prologue(const GemvParams& P, uint8_t* smem, const GmSmem& L, const float (&gm)[MAXI][8],
+                                            bool has6) {
   constexpr int NC = NW * 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nitems = P.C / 8;
@@ -209,13 +213,22 @@ __device__ __forceinline__ void gm_prologue(const GemvParams& P, uint8_t* smem, 
       *reinterpret_cast<uint32_t*>(xq + p * 64) = w[0];
       *reinterpret_cast<uint32_t*>(xq + p * 64 + 16) = w[1];
     }
-    // digit sums of the sub-block: its 4 items sit in 4 consecutive lanes
-#pragma unroll
-    for (int off = 1; off < 4; off <<= 1) {
-      S0 += __shfl_xor_sync(0xffffffffu, S0, off);
-      S1 += __shfl_xor_sync(0xffffffffu, S1, off);
-      S2 += __shfl_xor_sync(0xffffffffu, S2, off);
+    // digit sums of the 16-column halves (2 consecutive lanes), then of the sub-block (4 lanes)
+    S0 += __shfl_xor_sync(0xffffffffu, S0, 1);
+    S1 += __shfl_xor_sync(0xffffffffu, S1, 1);
+    S2 += __shfl_xor_sync(0xffffffffu, S2, 1);
+    if (has6 && (lane & 1) == 0) {
+      // the Q6_K "-32" in the units of the sub-block's sums (16 for the high nibbles)
+      const int f = (sbi & 3) >= 2 ? -512 : -32, jh = (j0 >> 4) * 3;
+      int* xo = reinterpret_cast<int*>(smem + L.xo) + (size_t)sbi * 8;
+      xo[jh] = f * S0;
+      xo[jh + 1] = f * S1;
+      xo[jh + 2] = f * S2;
+      if (jh) { xo[6] = 0; xo[7] = 0; }
     }
+    S0 += __shfl_xor_sync(0xffffffffu, S0, 2);
+    S1 += __shfl_xor_sync(0xffffffffu, S1, 2);
+    S2 += __shfl_xor_sync(0xffffffffu, S2, 2);
     if ((lane & 3) == 0) xsf[sbi] = (float)(S0 * 16384 + S1 * 128 + S2);
     if (lane == 0) {
       sbs[2 * (col0 >> 8)] = pow2f(e - 14);
@@ -267,7 +280,7 @@ __device__ __forceinline__ void gm_stage(const GemvParams& P, GemvThread& T, int
       const int c = p & 1, h = p >> 1, k = 2 * p;   // sub-blocks k (low nibbles), k + 1 (high)
       const size_t off = (size_t)c * 64 * G + (size_t)sb * 64 + h * 32 + jh * 16;
       uint32_t r[4];
-      gm_ldsm_x4(lrow + q4_p0_swz(mr, off), r);
+      gm_ldsm_x4(lrow + p0_swz(mr, off), r);
       uint4 bx = make_uint4(0u, 0u, 0u, 0u);
       if (g8 < 3) bx = lds128(xb + ((size_t)(sb * 4 + p) * 3 + g8) * 64 + t * 16);
       const uint32_t al[4] = {r[0] & 0x0F0F0F0Fu, r[1] & 0x0F0F0F0Fu, r[2] & 0x0F0F0F0Fu, r[3] & 0x0F0F0F0Fu};
@@ -314,7 +327,7 @@ __device__ __forceinline__ void gm_stage(const GemvParams& P, GemvThread& T, int
   }
   __syncwarp();
   if (lane == 0) mbar_arrive(empty_bar);   // this warp's reads of the stage are done
-  float* red = reinterpret_cast<float*>(smem + L.red) + par * NW * TR;
+  float* red = reinterpret_cast<float*>(smem + L.red) + par * NW * GM_MAX_TR;
   if (t < 2) red[(16 * blk + g8 + 8 * t) * NWG + wg] = acc;
   named_bar(1, NW * 32);
   if (warp == 0) {
@@ -326,11 +339,119 @@ __device__ __forceinline__ void gm_stage(const GemvParams& P, GemvThread& T, int
   }
 }
 
-// NW consumer warps, NB 16-row blocks per stage; MAXI prologue items per thread
-// (C <= 8 * MAXI * 32 * NW columns).
-template <int NW, int NB, int MAXI>
+// Byte k of w, sign-extended (prmt's sign-replicating selector: byte k, then three copies of its
+// sign).
+__device__ __forceinline__ int gm_sbyte(uint32_t w, int k) {
+  const uint32_t sel = (uint32_t)k | ((uint32_t)(8 | k) * 0x1110u);
+  uint32_t r;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
+  return (int)r;
+}
+__device__ __forceinline__ void gm6_mma(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c0, int c1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%12};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(0));
+}
+
+// One stage of a Q6_K segment: sg.tr / 8 tiles of 8 rows (nt); warp w takes tile w % nt and the
+// super-blocks [wg G / NWG, (wg + 1) G / NWG), wg = w / nt, NWG = NW / nt.
+// Per 32-column sub-block (h, k6) ONE mma.m16n8k32 does the 8 rows: A rows 0-7 are the rows'
+// 4-bit parts (ql, low or high nibbles in place), A rows 8-15 the same rows' 2-bit parts (qh,
+// bits 2 k6 in place), both read by ldmatrix from the swizzled tile; the B columns are the
+// activation digit planes split by 16-column half (column 3 jh + L: plane L, zero outside half
+// jh), because a Q6_K scale covers 16 columns; C carries the "-32" (the xo table). The lane
+// holding D rows g8 / g8 + 8 thus has the 4-bit and the 2-bit sums of row g8 for two columns
+// and combines them exactly (the 2-bit part shifted to weight 16); the scale of each (row, half)
+// is applied in int32 and the planes are summed per super-block, then combined in fp32 with d
+// and the activation scale, as k_gemv does.
+template <int NW>
+__device__ __forceinline__ void gm6_stage(const GemvParams& P, GemvThread& T, int s, int segi, const uint8_t* buf,
+                                          uint64_t* empty_bar, int par, uint8_t* smem, const GmSmem& L) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t = lane & 3;
+  const Seg& sg = P.seg[segi];
+  const int G = P.G, tr = sg.tr, nt = tr >> 3, NWG = NW / nt;
+  const int row0 = (s - sg.stage0) * tr;
+  const int rows = min(tr, sg.w.R - row0);           // a multiple of 8
+  const int tile = warp % nt, wg = warp / nt;
+  // a short stage reads its last tile again (rows unused)
+  const uint8_t* tb = buf + (size_t)min(tile, (rows >> 3) - 1) * tile_bytes(Q6K, G);
+  const size_t o1 = (size_t)8 * 128 * G, o2 = o1 + (size_t)8 * 64 * G, o3 = o2 + (size_t)8 * 16 * G;
+  // ldmatrix: matrix mi = lane / 8 is 16-byte chunk mi of the 64 bytes of (h, jh) = (mi / 2, mi % 2)
+  const int mi = lane >> 3, mr = lane & 7;
+  const uint8_t* lrow = tb + (size_t)mr * 128 * G;        // ql of tile row mr
+  const uint8_t* qrow = tb + o1 + (size_t)mr * 64 * G;    // qh of tile row mr
+  // B column g8 of this lane: plane g8 % 3 of half g8 / 3 (columns 6, 7 read real data, unused)
+  const int bjh = g8 >= 3 ? 1 : 0, bpl = min(g8 - 3 * bjh, 2);
+  const uint8_t* xa = smem + L.xb + bpl * 64 + t * 16 + bjh * 4;
+  const int* xo = reinterpret_cast<const int*>(smem + L.xo) + 2 * t;
+  const float* sbs = reinterpret_cast<const float*>(smem + L.sbs);
+  // D columns 2t, 2t + 1 of this lane: halves ja, jb
+  const bool ja = 2 * t >= 3, jb = 2 * t + 1 >= 3;
+  const uint8_t* scrow = tb + o2 + (size_t)g8 * 16 * G;   // scales of row g8
+  const uint8_t* drow = tb + o3 + (size_t)g8 * 2 * G;     // d of row g8
+  const int sb0 = wg * G / NWG, sb1 = (wg + 1) * G / NWG;
+  float acc = 0.f;   // lanes t = 0: row g8 of the tile
+  for (int sb = sb0; sb < sb1; ++sb) {
+    uint32_t q[4], r0[4], r1[4];
+    gm_ldsm_x4(qrow + q6_qh_swz(G, mr, (size_t)sb * 64 + 16 * mi), q);
+    gm_ldsm_x4(lrow + p0_swz(mr, (size_t)sb * 64 + 16 * mi), r0);                    // c = 0
+    gm_ldsm_x4(lrow + p0_swz(mr, (size_t)64 * G + (size_t)sb * 64 + 16 * mi), r1);   // c = 1
+    const uint4 S = lds128(scrow + q4_p1_swz(G, g8, (size_t)sb * 16));   // [u = 2h + jh][k6]
+    const uint32_t wa0 = ja ? S.y : S.x, wa1 = ja ? S.w : S.z, wb0 = jb ? S.y : S.x, wb1 = jb ? S.w : S.z;
+    int PL0 = 0, PL1 = 0, PH0 = 0, PH1 = 0;   // 4-bit-unit sums (PH: high nibbles, weight 16)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int k6 = 0; k6 < 4; ++k6) {
+        const uint32_t* r = (k6 & 1) ? r1 : r0;
+        const uint32_t m = (k6 >> 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu, mq = 0x03030303u << (2 * k6);
+        const uint32_t a[4] = {r[2 * h] & m, q[2 * h] & mq, r[2 * h + 1] & m, q[2 * h + 1] & mq};
+        const int sbi = sb * 8 + 4 * h + k6;
+        const uint32_t av = lds32(xa + (size_t)(sbi >> 1) * 192 + (sbi & 1) * 8);
+        const int2 cx = *reinterpret_cast<const int2*>(xo + (size_t)sbi * 8);
+        int d[4];
+        gm6_mma(d, a, bjh ? 0u : av, bjh ? av : 0u, cx.x, cx.y);
+        const int sh = (k6 & 1) ? 2 : 4;                  // qh bits 2 k6 to weight 16 (x16 more: high)
+        const int E0 = d[0] + (d[2] << sh), E1 = d[1] + (d[3] << sh);
+        const int sa = gm_sbyte(h ? wa1 : wa0, k6), sc = gm_sbyte(h ? wb1 : wb0, k6);
+        if (k6 >> 1) { PH0 += sa * E0; PH1 += sc * E1; }
+        else { PL0 += sa * E0; PL1 += sc * E1; }
+      }
+    }
+    // the high-nibble sums are exact multiples of 16
+    const int Pa0 = PL0 + (PH0 >> 4), Pa1 = PL1 + (PH1 >> 4);   // columns 2t, 2t + 1
+    // planes of row g8: column L (half 0) + column 3 + L (half 1), gathered in lane t = 0
+    const int c2 = __shfl_down_sync(0xffffffffu, Pa0, 1), c3 = __shfl_down_sync(0xffffffffu, Pa1, 1);
+    const int c4 = __shfl_down_sync(0xffffffffu, Pa0, 2), c5 = __shfl_down_sync(0xffffffffu, Pa1, 2);
+    if (t == 0) {
+      const int P3[3] = {Pa0 + c3, Pa1 + c4, c2 + c5};
+      const float Pf = planes_combine(P3);
+      const float d = h2f_bits(*reinterpret_cast<const uint16_t*>(drow + (size_t)sb * 2));
+      const float2 sc = *reinterpret_cast<const float2*>(sbs + 2 * sb);   // s3, poison
+      acc = __fadd_rn(acc, __fadd_rn(__fmul_rn(sc.x, __fmul_rn(d, Pf)), sc.y));
+    }
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty_bar);   // this warp's reads of the stage are done
+  float* red = reinterpret_cast<float*>(smem + L.red) + par * NW * GM_MAX_TR;
+  if (t == 0) red[(tile * 8 + g8) * NWG + wg] = acc;
+  named_bar(1, NW * 32);
+  if (warp == 0) {
+    float fin = 0.f;
+    if (lane < rows)
+      for (int w = 0; w < NWG; ++w) fin = __fadd_rn(fin, red[lane * NWG + w]);
+    const float fin_odd = __shfl_down_sync(0xffffffffu, fin, 1);
+    if (lane < rows) gemv_row_epilogue(P, T, sg, row0 + lane, fin, fin_odd, (lane & 1) == 0);
+  }
+}
+
+// NW consumer warps, NB 16-row blocks per Q4_K stage; MAXI prologue items per thread
+// (C <= 8 * MAXI * 32 * NW columns); TY 1: every segment is Q4_K, 2: some are Q6_K (the Q4_K-only
+// instances carry no Q6_K code). With NW = 16 the 17 warps leave 96 registers a thread (one SM
+// sub-partition holds 5 of them), with NW = 12 128.
+template <int NW, int NB, int MAXI, int TY>
 __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv_mma(const __grid_constant__ GemvParams P) {
-  constexpr int NC = NW * 32, TR = 16 * NB;
+  constexpr int NC = NW * 32;
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x;
   const GmSmem L = gm_smem_layout(P.nslots, P.stage_bytes, P.C);
@@ -375,7 +496,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv_mma(const __grid_cons
     rc[KQ_MAX_HALF_HD + tid] = __ldcg(P.sin_t + (size_t)rp * (P.hd >> 1) + tid);
   }
   pdl_wait();
-  gm_prologue<NW, MAXI>(P, smem, L, gm);
+  gm_prologue<NW, MAXI>(P, smem, L, gm, TY == 2);
   if (tid == 0) mbar_arrive(&pro_bar);
   int segi = 0;
   for (int i = 0; i < nmine; ++i) {
@@ -384,26 +505,29 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv_mma(const __grid_cons
     if (!mbar_wait(&full[slot], round & 1, P.err, KQ_DEV_ERR_WAIT_FULL)) { s_fail = 1; break; }
     const int s = s_begin + i;
     while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
-    gm_stage<NW, NB>(P, T, s, segi, smem + L.stages + (size_t)slot * P.stage_bytes, &empty[slot], i & 1, smem, L);
+    const uint8_t* buf = smem + L.stages + (size_t)slot * P.stage_bytes;
+    if (TY == 1 || P.seg[segi].w.type == Q4K) gm_stage<NW, NB>(P, T, s, segi, buf, &empty[slot], i & 1, smem, L);
+    else gm6_stage<NW>(P, T, s, segi, buf, &empty[slot], i & 1, smem, L);
     if (tid == 0) *(volatile int*)&s_done = i + 1;
   }
   if (P.seg[0].epi == EPI_ARGMAX) {
     float* bestv = reinterpret_cast<float*>(smem + L.best);
     int* besti = reinterpret_cast<int*>(bestv + GM_MAX_TR);
-    if (tid < TR) {
+    if (tid < GM_MAX_TR) {   // the epilogue lanes of warp 0 (rows of a stage: at most GM_MAX_TR)
       bestv[tid] = T.bv;
       besti[tid] = T.bi;
     }
     named_bar(KQ_BAR_ARGMAX, NC);
-    if (tid == 0) gemv_argmax_merge(P, bestv, besti, TR);
+    if (tid == 0) gemv_argmax_merge(P, bestv, besti, GM_MAX_TR);
   }
 }
 
-// The kernel instances the host picks from: (warps, row blocks) and the prologue width.
+// The kernel instances the host picks from: (warps, row blocks, segment types) and the prologue
+// width.
 typedef void (*GmFn)(GemvParams);
-template <int NW, int NB>
+template <int NW, int NB, int TY>
 __host__ inline GmFn gm_fn_for(int C) {
-  return C <= 2 * 8 * 32 * NW ? k_gemv_mma<NW, NB, 2> : k_gemv_mma<NW, NB, (12288 + 8 * 32 * NW - 1) / (8 * 32 * NW)>;
+  return C <= 2 * 8 * 32 * NW ? k_gemv_mma<NW, NB, 2, TY> : k_gemv_mma<NW, NB, (12288 + 8 * 32 * NW - 1) / (8 * 32 * NW), TY>;
 }
 
 }  // namespace kq

@@ -42,15 +42,21 @@ __host__ __device__ inline size_t tile_plane_off(int type, int G, int plane) {
   for (int p = 0; p < plane; ++p) o += 8 * plane_row_bytes(type, p, G);
   return o;
 }
-// Q4_K tiles are laid out so that the 8 rows of a tile can be read in parallel without shared-
-// memory bank conflicts (the tensor-core GEMV reads the same columns of 8 or 16 rows at once),
-// while one row stays conflict-free too (k_gemv reads consecutive chunks of one row): in plane 0
-// (the nibbles) the 16-byte chunk q of row r8 is stored at chunk q ^ r8 of its 128-byte group,
-// and in plane 1 (the 16-byte block headers) header g of row r8 at g ^ r8 when G is a multiple
-// of 8 (rows then start on 128-byte boundaries). Every access is of whole 16-byte chunks or less.
-__host__ __device__ inline size_t q4_p0_swz(int row, size_t off) { return off ^ ((size_t)(row & 7) << 4); }
+// Tiles are laid out so that the 8 rows of a tile can be read in parallel without shared-memory
+// bank conflicts (the tensor-core GEMV reads the same columns of 8 or 16 rows at once), while one
+// row stays conflict-free too (k_gemv reads consecutive chunks of one row). Every access is of
+// whole 16-byte chunks or less, and a chunk moves only inside its 128-byte group (XOR with the
+// row's index in its tile):
+//   plane 0, both types (the nibbles, 128 G bytes a row): chunk q of row r8 at q ^ r8;
+//   plane 1, Q4_K (16-byte block headers) and plane 2, Q6_K (16 int8 scales a block): chunk g of
+//            row r8 at g ^ r8 when G is a multiple of 8 (rows then start on 128-byte boundaries);
+//   plane 1, Q6_K (qh, 64 bytes a block): chunk q at q ^ r8 when G is even.
+__host__ __device__ inline size_t p0_swz(int row, size_t off) { return off ^ ((size_t)(row & 7) << 4); }
 __host__ __device__ inline size_t q4_p1_swz(int G, int row, size_t off) {
   return (G & 7) ? off : off ^ ((size_t)(row & 7) << 4);
+}
+__host__ __device__ inline size_t q6_qh_swz(int G, int row, size_t off) {
+  return (G & 1) ? off : off ^ ((size_t)(row & 7) << 4);
 }
 
 // byte `off` of plane p of row `row` (offsets as in the unswizzled [8 rows][bytes] order of the
@@ -58,8 +64,10 @@ __host__ __device__ inline size_t q4_p1_swz(int G, int row, size_t off) {
 __host__ __device__ inline size_t row_plane_off(int type, int G, int row, int plane, size_t off) {
   const size_t t = (size_t)(row >> 3) * tile_bytes(type, G) + tile_plane_off(type, G, plane) +
                    (size_t)(row & 7) * plane_row_bytes(type, plane, G);
-  if (type == Q4K && plane == 0) return t + q4_p0_swz(row, off);
+  if (plane == 0) return t + p0_swz(row, off);
   if (type == Q4K && plane == 1) return t + q4_p1_swz(G, row, off);
+  if (type == Q6K && plane == 1) return t + q6_qh_swz(G, row, off);
+  if (type == Q6K && plane == 2) return t + q4_p1_swz(G, row, off);
   return t + off;
 }
 
@@ -160,14 +168,12 @@ __device__ inline void scatter_block(const QViewW& m, int d, int g, const uint8_
       m.base[row_plane_off(t, G, d, 0, (size_t)c * 64 * G + (size_t)g * 64 + (2 * h + jh) * 16 + jp)] = b[16 + o];
     }
   } else {
-    uint8_t* row = m.base + row_plane_off(t, G, d, 0, 0);
     for (int o = 0; o < 128; o++) {
       const int h = o >> 6, c = (o >> 5) & 1, jh = (o >> 4) & 1, jp = o & 15;
-      row[(size_t)c * 64 * G + (size_t)g * 64 + (2 * h + jh) * 16 + jp] = b[o];
+      m.base[row_plane_off(t, G, d, 0, (size_t)c * 64 * G + (size_t)g * 64 + (2 * h + jh) * 16 + jp)] = b[o];
     }
-    uint8_t* qh = m.base + row_plane_off(t, G, d, 1, (size_t)g * 64);
-    for (int o = 0; o < 64; o++) qh[o] = b[128 + o];
-    uint8_t* sc = m.base + row_plane_off(t, G, d, 2, (size_t)g * 16);
+    for (int o = 0; o < 64; o++) m.base[row_plane_off(t, G, d, 1, (size_t)g * 64 + o)] = b[128 + o];
+    uint8_t* sc = m.base + row_plane_off(t, G, d, 2, (size_t)g * 16);   // 16 contiguous bytes
     for (int h = 0; h < 2; h++)
       for (int jh = 0; jh < 2; jh++)
         for (int k = 0; k < 4; k++) sc[(2 * h + jh) * 4 + k] = b[192 + 8 * h + 2 * k + jh];

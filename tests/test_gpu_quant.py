@@ -76,6 +76,59 @@ def test_matvec_edge_activations(kq, oracle):
     assert np.isnan(m.matvec(x)).all()
 
 
+Q6_SHAPES = [(14, 4096, 12288), (14, 1024, 4096), (14, 16, 512), (14, 64, 2048), (14, 8, 4096), (14, 24, 256),
+             (14, 40, 1024), (14, 8, 12288)]
+
+
+@pytest.mark.parametrize("path", ["0", "1"])
+@pytest.mark.parametrize("ty,R,Cc", Q6_SHAPES)
+def test_matvec_parity_q6k_both_paths(kq, oracle, monkeypatch, ty, R, Cc, path):
+    """Q6_K through the dp4a GEMV (KQ_GEMV_MMA6=0) and through the tensor-core one (=1; by
+    default it serves Q6_K only inside mixed launches)."""
+    monkeypatch.setenv("KQ_GEMV_MMA6", path)
+    W = oracle.gen_matrix(R, Cc, ty, 0, 300 + R)
+    x = oracle.gen_normal(Cc, 0.0, 1.0, 1, 7 + R)
+    m = kq.QMat(ty, R, Cc).upload(W)
+    assert rel_l2(m.matvec(x), oracle.matvec(W, R, Cc, ty, x)) < TIGHT_L2
+
+
+@pytest.mark.parametrize("path", ["0", "1"])
+@pytest.mark.parametrize("qbyte,sign", [(0x00, 1.0), (0xFF, -1.0), (0xFF, 1.0)])
+def test_matvec_q6k_extreme_magnitudes(kq, oracle, monkeypatch, qbyte, sign, path):
+    """Q6_K blocks at the ends of every range: all weights q - 32 = -32 (or +31), every scale
+    -128, activations all +-127 (the largest first digit): the int32 sums of the tensor-core and
+    the dp4a paths must not overflow."""
+    monkeypatch.setenv("KQ_GEMV_MMA6", path)
+    R, Cc = 64, 4096
+    blk = np.zeros(210, np.uint8)
+    blk[:192] = qbyte                      # ql, qh
+    blk[192:208] = 0x80                    # int8 scales -128
+    blk[208:210] = np.frombuffer(np.float16(1e-3).tobytes(), np.uint8)
+    W = np.tile(blk, R * (Cc // 256))
+    m = kq.QMat(14, R, Cc).upload(W)
+    x = np.full(Cc, 127.0 * sign, np.float32)
+    ref = oracle.matvec(W, R, Cc, 14, x)
+    assert np.isfinite(ref).all()
+    assert rel_l2(m.matvec(x), ref) < RTOL_L2   # identical addends: the oracle's fp32 sums drift
+
+
+@pytest.mark.parametrize("path", ["0", "1"])
+@pytest.mark.parametrize("ty", [12, 14])
+def test_matvec_edge_activations_both_types(kq, oracle, monkeypatch, ty, path):
+    """Zero, tiny, huge-range and non-finite activations on a launch of each type and path."""
+    monkeypatch.setenv("KQ_GEMV_MMA6", path)
+    R, Cc = 64, 4096
+    W = oracle.gen_matrix(R, Cc, ty, 0, 6)
+    m = kq.QMat(ty, R, Cc).upload(W)
+    assert np.array_equal(m.matvec(np.zeros(Cc, np.float32)), oracle.matvec(W, R, Cc, ty, np.zeros(Cc, np.float32)))
+    x = oracle.gen_normal(Cc, 0.0, 1.0, 1, 10)
+    x[:256] *= 1e-30
+    x[256:1024] *= 1e20
+    assert rel_l2(m.matvec(x), oracle.matvec(W, R, Cc, ty, x)) < TIGHT_L2
+    x[3000] = np.inf
+    assert not np.isfinite(m.matvec(x)).any()
+
+
 def test_matvec_nan_weights_propagate(kq, golden):
     raw = golden["edge_raw_12"]
     m = kq.QMat(12, 8, 256).upload(raw.reshape(-1))
