@@ -628,7 +628,7 @@ def run_ours(args, rank, world, local):
         line = {
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "q4_k/q6_k x int8 digit planes (dp4a, int32) + f32", "data": "synthetic (seeded generator, random-init Q4_K/Q6_K weights of the config-2 architecture)",
+            "dtype": "q4_k/q6_k x int8 digit planes (int8 mma.sync and dp4a, int32) + f32", "data": "synthetic (seeded generator, random-init Q4_K/Q6_K weights of the config-2 architecture)",
             "config": {"workload": "config-2 batch-1 greedy decode at ctx 4K (KV pre-filled to %d, %d timed steps)" % (pos0 + W, K),
                        "model": "dense GQA 32L d4096 32q/8kv hd128 ffn12288 vocab151936, Q4_K + Q6_K",
                        "global_batch": world, "seq_len": CTX, "parallelism": "replicas" if world > 1 else "single",

@@ -328,7 +328,7 @@ static bool plan_gemv_mma(int C, const int* types, int nseg, const int* seg_rows
   // switch KQ_GEMV_MMA6: 0 = never for Q6_K, 1 = always.
   const char* e6 = std::getenv("KQ_GEMV_MMA6");
   const int mma6 = e6 ? std::atoi(e6) : -1;
-  if (has6 && (mma6 == 0 || (mma6 < 0 && !has4))) return false;
+  if (has6 && mma6 == 0) return false;
   const int G = C / 256;
   // 16 consumer warps, Q4_K stages of two 16-row blocks (measured on config-0: 16 warps x 32 rows
   // 9.12 us, 8 x 32 9.19, 8 x 16 11.45, 16 x 16 11.73, k_gemv 11.07; a 226 MB launch: 43.0 /
@@ -359,6 +359,11 @@ static bool plan_gemv_mma(int C, const int* types, int nseg, const int* seg_rows
     const int tr = types[i] == KQ_Q4_K ? tr4 : tr6;
     nstages += (seg_rows[i] + tr - 1) / tr;
   }
+  // a Q6_K-only launch with many stages per CTA is streaming-bound: k_gemv's cheaper consumer
+  // wins there; a short one (the decode step's down projection, ~3.5 stages per CTA) is bound by
+  // the prologue, which is shorter here
+  const int max_per_cta = std::getenv("KQ_MMA6_MAX_PER_CTA") ? std::atoi(std::getenv("KQ_MMA6_MAX_PER_CTA")) : 8;
+  if (has6 && !has4 && mma6 < 0 && nstages > max_per_cta * nsm) return false;
   const int slots = std::min(8, (int)((budget - fixed) / (stage + 16)));
   pl.TR = std::max(has4 ? tr4 : 0, has6 ? tr6 : 0);
   pl.tr4 = tr4; pl.tr6 = tr6;

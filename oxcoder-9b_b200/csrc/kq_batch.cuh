@@ -512,24 +512,19 @@ __global__ void __launch_bounds__(DA_WARPS * 32) k_dattn(const __grid_constant__
 // GEMV's tail. The step state (pos, tree) was written by the previous step's output head.
 constexpr int DM_KB = 32;                                            // keys per block
 constexpr size_t DM_SMEM = (size_t)2 * 2 * DM_KB * BA_LD * 2;          // K and V, two stages
+// One warp's flash pass (token t, KV head kv, keys [0, n) attended): the 32-key blocks starting at
+// p0, p0 + bs, p0 + 2 bs, ... below p1 through its two shared-memory stages ksm / vsm; returns the
+// unnormalised output rows and the running max / sum of rows grp (A) and grp + 8 (B). With a
+// decode step state (P.st) the first two blocks are requested before the dependency wait when
+// none of their keys is the new slot pos; the wait is always taken in that case.
 template <int G>
-__global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnParams P) {
-  constexpr int HD = 128, PLD = HD + 4;
-  extern __shared__ __align__(16) uint8_t dm_sm[];
-  __half* ksm = reinterpret_cast<__half*>(dm_sm);   // [2][DM_KB][BA_LD]
-  __half* vsm = ksm + 2 * DM_KB * BA_LD;
-  const int t = blockIdx.x, kv = blockIdx.y, sp = blockIdx.z, lane = threadIdx.x, grp = lane >> 2, t4 = lane & 3;
-  pdl_trigger();   // the merge may launch now; it reads the partials after its own dependency wait
-  if (!P.st) pdl_wait();
-  int n = (P.st ? P.st->pos : P.pos[t]) + 1;
-  if (n > P.ctx || n < 1) {
-    if (lane == 0 && sp == 0 && kv == 0 && P.err) atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
-    n = n < 1 ? 1 : P.ctx;
-  }
+__device__ __forceinline__ void dm_warp_pass(const DAttnParams& P, int t, int kv, int n, int p0, int bs, int p1,
+                                             __half* ksm, __half* vsm, float (&o)[16][4], float& mA, float& mB,
+                                             float& lA, float& lB) {
+  constexpr int HD = 128;
+  const int lane = threadIdx.x & 31, grp = lane >> 2, t4 = lane & 3;
   const int tbase = P.st ? P.st->tree_base : n;
   const unsigned long long tm0 = P.st ? P.st->mask[0] : 0ull, tm1 = P.st ? P.st->mask[1] : 0ull;
-  const int per = (n + P.nsplit - 1) / P.nsplit;
-  const int p0 = min(n, sp * per), p1 = min(n, p0 + per);
   const size_t cbase = ((size_t)(P.seq ? P.seq[t] : 0) * P.n_kv + kv) * P.ctx * HD;
   const __half* kg = P.kc + cbase;
   const __half* vg = P.vc + cbase;
@@ -540,7 +535,7 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
     for (int i = lane; i < DM_KB * 16; i += 32) {   // 16 chunks of 16 B per key row
       const int r = i >> 4, c = i & 15, tk = b0 + r;
       const bool ok = tk < p1;
-      const size_t off = (size_t)(ok ? tk : p0) * HD + c * 8;
+      const size_t off = (size_t)(ok ? tk : b0) * HD + c * 8;
       cp_async16_plain(kd + r * BA_LD + c * 8, kg + off, ok ? 16u : 0u);
       cp_async16_plain(vd + r * BA_LD + c * 8, vg + off, ok ? 16u : 0u);
     }
@@ -550,10 +545,10 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
   bool pre0 = false, pre1 = false;
   if (P.st) {
     pre0 = p0 < p1 && min(p0 + DM_KB, p1) <= n - 1;
-    pre1 = p0 + DM_KB < p1 && min(p0 + 2 * DM_KB, p1) <= n - 1;
+    pre1 = p0 + bs < p1 && min(p0 + bs + DM_KB, p1) <= n - 1;
     if (pre0) load_block(p0, 0);
     cp_async_commit();
-    if (pre1) load_block(p0 + DM_KB, 1);
+    if (pre1) load_block(p0 + bs, 1);
     cp_async_commit();
     pdl_wait();
   }
@@ -578,14 +573,13 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
     tm_split(x2.x, x2.y, qh[ks][2], ql[ks][2]);
     tm_split(x3.x, x3.y, qh[ks][3], ql[ks][3]);
   }
-  float o[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+  mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
   const int mi = lane >> 3;
   int st = 0;
-  for (int b0 = p0; b0 < p1; b0 += DM_KB, st ^= 1) {
-    if (b0 + DM_KB < p1 && !(b0 == p0 && pre1)) load_block(b0 + DM_KB, st ^ 1);
+  for (int b0 = p0; b0 < p1; b0 += bs, st ^= 1) {
+    if (b0 + bs < p1 && !(b0 == p0 && pre1)) load_block(b0 + bs, st ^ 1);
     cp_async_commit();
     cp_async_wait1();
     __syncwarp();
@@ -663,7 +657,29 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
     }
     __syncwarp();   // the stage is refilled by the next iteration's prefetch
   }
+}
+
+template <int G>
+__global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnParams P) {
+  constexpr int HD = 128, PLD = HD + 4;
+  extern __shared__ __align__(16) uint8_t dm_sm[];
+  __half* ksm = reinterpret_cast<__half*>(dm_sm);   // [2][DM_KB][BA_LD]
+  __half* vsm = ksm + 2 * DM_KB * BA_LD;
+  const int t = blockIdx.x, kv = blockIdx.y, sp = blockIdx.z, lane = threadIdx.x, grp = lane >> 2, t4 = lane & 3;
+  pdl_trigger();   // the merge may launch now; it reads the partials after its own dependency wait
+  if (!P.st) pdl_wait();
+  int n = (P.st ? P.st->pos : P.pos[t]) + 1;
+  if (n > P.ctx || n < 1) {
+    if (lane == 0 && sp == 0 && kv == 0 && P.err) atomicOr(P.err, KQ_DEV_ERR_BAD_POS);
+    n = n < 1 ? 1 : P.ctx;
+  }
+  const int per = (n + P.nsplit - 1) / P.nsplit;
+  const int p0 = min(n, sp * per), p1 = min(n, p0 + per);
+  float o[16][4];
+  float mA, mB, lA, lB;
+  dm_warp_pass<G>(P, t, kv, n, p0, DM_KB, p1, ksm, vsm, o, mA, mB, lA, lB);
   // partial of rows 0..G-1 (row grp in elements 0-1, row grp + 8 in elements 2-3)
+  const bool va = grp < G, vb = grp + 8 < G;
   float* part = P.part + (((size_t)t * P.n_kv + kv) * P.nsplit + sp) * G * PLD;
   if (va) {
     float* pr = part + (size_t)grp * PLD;

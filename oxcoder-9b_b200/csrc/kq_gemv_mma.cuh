@@ -124,6 +124,7 @@ __device__ __forceinline__ void gm_prologue(const GemvParams& P, uint8_t* smem, 
       }
     }
   }
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 6);
   if (P.xmode != XS_PLAIN) {
     // residual write-back and the norm (q4_rms q4.cu:39-46 / rmsfold kcpu4.c:123-139)
     double acc = 0.0;
@@ -144,7 +145,9 @@ __device__ __forceinline__ void gm_prologue(const GemvParams& P, uint8_t* smem, 
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
     if (lane == 0) redd[warp] = acc;
+    if (tid == 0) KQ_TRACE_AT(P.trace_id, 7);
     named_bar(KQ_BAR_PROLOGUE, NC);
+    if (tid == 0) KQ_TRACE_AT(P.trace_id, 8);
     double tot = 0.0;
     for (int w = 0; w < NW; ++w) tot += redd[w];
     const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / (double)P.C), P.eps)));
@@ -157,6 +160,7 @@ __device__ __forceinline__ void gm_prologue(const GemvParams& P, uint8_t* smem, 
       }
     }
   }
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 9);
   // ---- exact digit split, one exponent per super-block (a warp's 32 items)
   const float RND = 12582912.0f;   // 1.5 * 2^23: adding it rounds to an integer (RNE), |y| <= 128
 #pragma unroll
@@ -230,6 +234,7 @@ __device__ __forceinline__ void gm_prologue(const GemvParams& P, uint8_t* smem, 
     S1 += __shfl_xor_sync(0xffffffffu, S1, 2);
     S2 += __shfl_xor_sync(0xffffffffu, S2, 2);
     if ((lane & 3) == 0) xsf[sbi] = (float)(S0 * 16384 + S1 * 128 + S2);
+    if (tid == 0) KQ_TRACE_AT(P.trace_id, 10);
     if (lane == 0) {
       sbs[2 * (col0 >> 8)] = pow2f(e - 14);
       sbs[2 * (col0 >> 8) + 1] = bad ? __int_as_float(0x7fc00000) : 0.f;
@@ -472,6 +477,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv_mma(const __grid_cons
   }
   __syncthreads();
   pdl_trigger();
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 0);
   if (tid >= NC) {
     gemv_producer(P, smem + L.stages, full, empty, &pro_bar, s_begin, nmine, &s_fail, &s_issued, &s_done);
     pdl_wait();
@@ -496,13 +502,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv_mma(const __grid_cons
     rc[KQ_MAX_HALF_HD + tid] = __ldcg(P.sin_t + (size_t)rp * (P.hd >> 1) + tid);
   }
   pdl_wait();
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 1);
   gm_prologue<NW, MAXI>(P, smem, L, gm, TY == 2);
   if (tid == 0) mbar_arrive(&pro_bar);
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 2);
   int segi = 0;
   for (int i = 0; i < nmine; ++i) {
     const int slot = i % P.nslots;
     const uint32_t round = (uint32_t)(i / P.nslots);
     if (!mbar_wait(&full[slot], round & 1, P.err, KQ_DEV_ERR_WAIT_FULL)) { s_fail = 1; break; }
+    if (tid == 0 && i == 0) KQ_TRACE_AT(P.trace_id, 3);
     const int s = s_begin + i;
     while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
     const uint8_t* buf = smem + L.stages + (size_t)slot * P.stage_bytes;
@@ -510,6 +519,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv_mma(const __grid_cons
     else gm6_stage<NW>(P, T, s, segi, buf, &empty[slot], i & 1, smem, L);
     if (tid == 0) *(volatile int*)&s_done = i + 1;
   }
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 4);
   if (P.seg[0].epi == EPI_ARGMAX) {
     float* bestv = reinterpret_cast<float*>(smem + L.best);
     int* besti = reinterpret_cast<int*>(bestv + GM_MAX_TR);

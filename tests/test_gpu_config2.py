@@ -97,6 +97,29 @@ def test_decode_attention_at_context_4096(kq, oracle, npos):
         o.close()
 
 
+@pytest.mark.parametrize("splits", ["1", "7", "18", "64"])
+@pytest.mark.parametrize("npos", [31, 4095])
+def test_decode_attention_splits(kq, oracle, monkeypatch, splits, npos):
+    """The decode step's tensor-core attention over key-split counts from 1 to 64, at a short
+    context (most splits empty) and at the benchmark's, three consecutive steps."""
+    monkeypatch.setenv("KQ_DSPLIT", splits)
+    t = dict(NL=1, vocab=4096, ctx=4100)
+    e = kq.Engine(kq.Config.default(n_layers=1, vocab=4096, ctx=4100), seed=0)
+    o = oracle.Model(seed=0, **t)
+    try:
+        e.fill_kv(npos, 3)
+        o.fill_kv(npos, 3)
+        for k in range(3):
+            a = e.step(11 + k, npos + k)
+            b = o.step(11 + k, npos + k)
+            assert rel_l2(e.hidden(), o.hidden()) < RTOL
+            assert rel_l2(e.ylog, o.logits()) < RTOL
+            assert a == b
+    finally:
+        e.close()
+        o.close()
+
+
 @pytest.mark.parametrize("temperature", [0.7, 0.0])
 def test_accept_bit_exact_at_full_vocabulary(kq, oracle, temperature):
     """Config-3's acceptance over a vocabulary of 151936 ids: tree [4, 2, 2, 1] (45 nodes),
