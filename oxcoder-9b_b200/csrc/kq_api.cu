@@ -248,6 +248,7 @@ struct GemvPlan {
 };
 
 static const size_t KQ_SMEM_BUDGET = 220 * 1024;
+static const int KQ_MAX_STEP_GEMVS = 4 * 256 + 8;   // GEMV launches of one step at most (4 a layer + head)
 
 // Launch shape of a (fused) GEMV over segments sharing the column count C.
 static int plan_gemv(int C, const int* types, int nseg, const int* seg_rows, bool pairs, int nsm, size_t optin,
@@ -623,6 +624,7 @@ struct kq_model {
   int attn_mode = 0;                 // 0: split form, 1: cluster form, 2: tensor-core split form
   int dsplit = 0;                    // key splits of the tensor-core decode attention
   float* dpart1 = nullptr;          // decode-step partials of the tensor-core split form
+  int* gdyn = nullptr;               // stage-claim counter pairs of the step's GEMV launches (zeroed)
   float* tv_part = nullptr;         // split-K scratch of the tensor-core GEMV (decode graph)
   int* tv_ticket = nullptr;
   int attn_nsplit = 1;
@@ -966,6 +968,8 @@ static kq_model* model_create(const kq_config* cfg, int device, int rank, int wo
     m->dsplit = std::getenv("KQ_DSPLIT") ? std::atoi(std::getenv("KQ_DSPLIT")) : DA_MAX_SPLIT;   // tuning override
     if (m->dsplit < 1 || m->dsplit > DA_MAX_SPLIT) m->dsplit = DA_MAX_SPLIT;
     m->dpart1 = dalloc<float>(m, (size_t)c.n_kv_heads * DA_MAX_SPLIT * (c.n_heads / c.n_kv_heads) * (c.head_dim + 4), ok);
+    if (!(std::getenv("KQ_GEMV_DYN") && std::atoi(std::getenv("KQ_GEMV_DYN")) == 0))
+      m->gdyn = dalloc<int>(m, (size_t)2 * KQ_MAX_STEP_GEMVS, ok);
     m->persist = std::getenv("KQ_PERSIST") && std::atoi(std::getenv("KQ_PERSIST")) == 1;   // opt-in for now
     m->verify_seq = std::getenv("KQ_VERIFY_SEQ") && std::atoi(std::getenv("KQ_VERIFY_SEQ")) == 1;
     m->prof = std::getenv("KQ_PHASE_TIMES") && std::atoi(std::getenv("KQ_PHASE_TIMES")) == 1;
@@ -1328,6 +1332,7 @@ static bool tmv_plan(const GemvParams& g, int nsm, size_t smem_max, float* part,
 static int build_step(kq_model* m, bool head, bool persist, std::vector<StepOp>& ops) {
   const kq_config& c = m->c;
   int trace = 0;   // launch index within the step (phase trace of KQ_TRACE builds)
+  int ngemv = 0;   // GEMV launches so far: each has its own stage-claim counters
   ops.clear();
   int cur = 0;
   auto gemv = [&](const SegSpec* ss, int nseg, bool pairs, StepOp& op) -> int {
@@ -1350,6 +1355,12 @@ static int build_step(kq_model* m, bool head, bool persist, std::vector<StepOp>&
     pp.err = m->err;
     pp.eps = c.eps;
     pp.trace_id = trace++;
+    // run-time stage claims for launches of at least 3 stages per CTA (gate/up, down, head; the
+    // short q/k/v and o launches keep fixed ranges, which balance better at 1-2 stages a CTA).
+    // The launches of one step run in stream order, and the same launch of the next step only
+    // after this one finished, so a counter pair per launch suffices. Switch: KQ_GEMV_DYN=0
+    if (!persist && m->gdyn && ngemv < KQ_MAX_STEP_GEMVS && pp.nstages >= 3 * op.pl.grid) pp.dyn = m->gdyn + 2 * ngemv;
+    ++ngemv;
     return KQ_OK;
   };
   for (int l = 0; l < c.n_layers; ++l) {

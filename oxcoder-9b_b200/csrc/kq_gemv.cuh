@@ -44,6 +44,7 @@ constexpr int KQ_MAX_HALF_HD = 128;        // rotary half width held in shared m
 // Measured on the config-0 GEMV / config-2 decode step: 1 stage 12.1 us / 2.62 ms, 2 stages
 // 12.05 us / 2.57 ms, the whole ring (3 slots) 13.0 us / 2.58 ms.
 constexpr int KQ_PREFETCH_STAGES = 2;
+constexpr int KQ_MAX_SLOTS = 8;             // ring slots of a GEMV kernel at most (the planners' cap)
 
 struct DecodeState {   // device-resident per-step state
   int tok;        // token processed by this step
@@ -103,6 +104,8 @@ struct GemvParams {
   int* err;
   int trace_id;          // launch index for the optional phase trace (KQ_TRACE builds)
   int prefetch;          // k_gemv: stages the producer issues before the consumers' prologue is done
+  int* dyn;              // {next stage, CTAs done claiming}, zero between launches: every CTA's
+                         // producer claims its stages at run time, one ahead (null: fixed ranges)
 };
 
 // Shared-memory carve-up, identical on host (sizing) and device.
@@ -784,17 +787,27 @@ __device__ __forceinline__ void gemv_argmax_tail(const GemvParams& P, uint8_t* s
   if (tid == 0) gemv_argmax_merge(P, bestv, besti, NRG * RPG);
 }
 
-// The producer warp of a GEMV kernel (lane 0 works): this CTA's nmine stages from s_begin into the
-// ring of nslots stage buffers at `stages`, full[slot] completing on the copy; the first
-// P.prefetch stages are issued at once, the rest after the consumers' prologue (pro_bar) and as
-// slots are released (empty). On a failed wait it drains its copies in flight (bounded).
+// The producer warp of a GEMV kernel (lane 0 works): this CTA's stages into the ring of nslots
+// stage buffers at `stages`, full[slot] completing on the copy and s_stage[slot] naming the stage;
+// the first P.prefetch stages are issued at once, the rest after the consumers' prologue (pro_bar)
+// and as slots are released (empty). Fixed ranges: the nmine stages from s_begin. Claimed stages
+// (P.dyn): stages come from a launch-wide counter, each claimed when the previous one is issued
+// (the last 2 x grid stages only when a slot is free, so that no CTA holds a stage it cannot
+// start yet), so a CTA that starts late (its SM still ran the previous kernel) takes fewer; the claim past
+// the last stage becomes an end mark (s_stage = -1, full completed without a copy), and the last
+// CTA to finish claiming re-arms the counters for the next launch. Stages claimed by one CTA
+// increase, and each row is still computed by one CTA, so results do not depend on the claims.
+// On a failed wait it drains its copies in flight (bounded).
 __device__ __forceinline__ void gemv_producer(const GemvParams& P, uint8_t* stages, uint64_t* full, uint64_t* empty,
                                               uint64_t* pro_bar, int s_begin, int nmine, int* s_fail, int* s_issued,
-                                              const int* s_done) {
+                                              const int* s_done, int* s_stage) {
   if ((threadIdx.x & 31) != 0) return;
   const uint64_t pol = l2_evict_first_policy();
   int segi = 0;
-  for (int i = 0; i < nmine; ++i) {
+  // claims ahead stop for the last two stages per CTA: those are claimed when a slot is free
+  const int tail0 = P.nstages - 2 * (int)gridDim.x;
+  int s_next = P.dyn ? atomicAdd(P.dyn, 1) : s_begin;   // < 0: none claimed ahead
+  for (int i = 0; P.dyn || i < nmine; ++i) {
     const int slot = i % P.nslots;
     const uint32_t round = (uint32_t)(i / P.nslots);
     if (i == P.prefetch) {
@@ -804,12 +817,27 @@ __device__ __forceinline__ void gemv_producer(const GemvParams& P, uint8_t* stag
       if (!mbar_wait(&empty[slot], (round - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY)) { *s_fail = 1; break; }
     }
     if (*(volatile int*)s_fail) break;
+    const int s = s_next >= 0 ? s_next : atomicAdd(P.dyn, 1);
+    if (s >= P.nstages) {   // claimed past the end: the end mark
+      *(volatile int*)&s_stage[slot] = -1;
+      mbar_arrive(&full[slot]);
+      break;
+    }
+    s_next = !P.dyn ? s + 1 : s < tail0 ? atomicAdd(P.dyn, 1) : -1;
+    *(volatile int*)&s_stage[slot] = s;
     const uint8_t* src;
-    const uint32_t bytes = gemv_stage_src(P, s_begin + i, segi, &src);
+    const uint32_t bytes = gemv_stage_src(P, s, segi, &src);
     uint8_t* buf = stages + (size_t)slot * P.stage_bytes;
     mbar_arrive_expect_tx(&full[slot], bytes);
     bulk_g2s(buf, src, bytes, &full[slot], pol);
     *(volatile int*)s_issued = i + 1;
+  }
+  if (P.dyn) {
+    __threadfence();   // this CTA's last claim is performed before it counts as done
+    if (atomicAdd(P.dyn + 1, 1) == (int)gridDim.x - 1) {
+      P.dyn[0] = 0;
+      P.dyn[1] = 0;
+    }
   }
   KQ_TRACE_AT(P.trace_id, 5);
   if (*(volatile int*)s_fail) {
@@ -830,6 +858,7 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + P.nslots;
   __shared__ int s_fail, s_issued, s_done;
+  __shared__ int s_stage[KQ_MAX_SLOTS];      // the stage in each ring slot
   __shared__ __align__(8) uint64_t pro_bar;   // completes when the consumers' prologue is done
 
   int s_begin, s_end;
@@ -850,7 +879,7 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
 
   if (tid >= nthr_c) {
     // ---------------------------------------------------------------- producer warp
-    if (tid < nthr_c + 32) gemv_producer(P, smem + L.stages, full, empty, &pro_bar, s_begin, nmine, &s_fail, &s_issued, &s_done);
+    if (tid < nthr_c + 32) gemv_producer(P, smem + L.stages, full, empty, &pro_bar, s_begin, nmine, &s_fail, &s_issued, &s_done, s_stage);
     pdl_wait();
     return;
   }
@@ -873,12 +902,13 @@ __global__ void __launch_bounds__(KQ_GEMV_MAX_THREADS, 1) k_gemv(const __grid_co
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 2);
   gemv_load_xs(P, smem, L, T);
   int segi = 0;
-  for (int i = 0; i < nmine; ++i) {
+  for (int i = 0; P.dyn || i < nmine; ++i) {
     const int slot = i % P.nslots;
     const uint32_t round = (uint32_t)(i / P.nslots);
     if (!mbar_wait(&full[slot], round & 1, P.err, KQ_DEV_ERR_WAIT_FULL)) { s_fail = 1; break; }
     if (tid == 0 && i == 0) KQ_TRACE_AT(P.trace_id, 3);
-    const int s = s_begin + i;
+    const int s = *(volatile int*)&s_stage[slot];
+    if (s < 0) break;   // the producer's end mark
     while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
     gemv_stage<TM, RPG>(P, T, s, segi, smem + L.stages + (size_t)slot * P.stage_bytes, &empty[slot], i & 1);
     if (tid == 0) *(volatile int*)&s_done = i + 1;

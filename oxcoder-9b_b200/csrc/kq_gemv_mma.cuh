@@ -463,6 +463,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv_mma(const __grid_cons
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + P.nslots;
   __shared__ int s_fail, s_issued, s_done;
+  __shared__ int s_stage[KQ_MAX_SLOTS];   // the stage in each ring slot
   __shared__ __align__(8) uint64_t pro_bar;
   int s_begin, s_end;
   cta_stage_range(P, s_begin, s_end);
@@ -479,7 +480,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv_mma(const __grid_cons
   pdl_trigger();
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 0);
   if (tid >= NC) {
-    gemv_producer(P, smem + L.stages, full, empty, &pro_bar, s_begin, nmine, &s_fail, &s_issued, &s_done);
+    gemv_producer(P, smem + L.stages, full, empty, &pro_bar, s_begin, nmine, &s_fail, &s_issued, &s_done, s_stage);
     pdl_wait();
     return;
   }
@@ -507,12 +508,13 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv_mma(const __grid_cons
   if (tid == 0) mbar_arrive(&pro_bar);
   if (tid == 0) KQ_TRACE_AT(P.trace_id, 2);
   int segi = 0;
-  for (int i = 0; i < nmine; ++i) {
+  for (int i = 0; P.dyn || i < nmine; ++i) {
     const int slot = i % P.nslots;
     const uint32_t round = (uint32_t)(i / P.nslots);
     if (!mbar_wait(&full[slot], round & 1, P.err, KQ_DEV_ERR_WAIT_FULL)) { s_fail = 1; break; }
     if (tid == 0 && i == 0) KQ_TRACE_AT(P.trace_id, 3);
-    const int s = s_begin + i;
+    const int s = *(volatile int*)&s_stage[slot];
+    if (s < 0) break;   // the producer's end mark
     while (s >= P.seg[segi].stage0 + P.seg[segi].nstage) ++segi;
     const uint8_t* buf = smem + L.stages + (size_t)slot * P.stage_bytes;
     if (TY == 1 || P.seg[segi].w.type == Q4K) gm_stage<NW, NB>(P, T, s, segi, buf, &empty[slot], i & 1, smem, L);
