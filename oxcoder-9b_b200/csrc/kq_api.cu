@@ -1493,7 +1493,7 @@ static int enqueue_step(kq_model* m, bool head, cudaStream_t s) {
       std::memset(&D, 0, sizeof(D));
       D.q = op.a.a.q; D.kc = op.a.a.kc; D.vc = op.a.a.vc; D.st = op.a.a.st; D.err = op.a.a.err;
       D.n_kv = op.a.a.n_kv; D.ctx = op.a.a.ctx; D.scale = op.a.a.scale;
-      D.nsplit = m->dsplit; D.part = m->dpart1; D.out_f = op.a.a.out;
+      D.nsplit = m->dsplit; D.part = m->dpart1; D.out_f = op.a.a.out; D.trace_id = op.a.a.trace_id;
       CU(G == 1 ? launch_dattn_t<1>(D, 1, D.n_kv, s) : G == 2 ? launch_dattn_t<2>(D, 1, D.n_kv, s)
          : G == 4 ? launch_dattn_t<4>(D, 1, D.n_kv, s) : launch_dattn_t<8>(D, 1, D.n_kv, s));
     } else {

@@ -429,6 +429,7 @@ struct DAttnParams {
   const DecodeState* st;     // decode step (M = 1): position, tree base and ancestor mask from the
                              // device-resident step state instead of pos / seq
   int* err;
+  int trace_id;              // launch index for the optional phase trace (KQ_TRACE builds)
 };
 template <int G>
 __global__ void __launch_bounds__(DA_WARPS * 32) k_dattn(const __grid_constant__ DAttnParams P) {
@@ -551,6 +552,7 @@ __device__ __forceinline__ void dm_warp_pass(const DAttnParams& P, int t, int kv
     if (pre1) load_block(p0 + bs, 1);
     cp_async_commit();
     pdl_wait();
+    if (lane == 0) KQ_TRACE_AT(P.trace_id, 1);
   }
   if (p0 < p1 && !pre0) load_block(p0, 0);
   cp_async_commit();
@@ -667,6 +669,7 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
   __half* vsm = ksm + 2 * DM_KB * BA_LD;
   const int t = blockIdx.x, kv = blockIdx.y, sp = blockIdx.z, lane = threadIdx.x, grp = lane >> 2, t4 = lane & 3;
   pdl_trigger();   // the merge may launch now; it reads the partials after its own dependency wait
+  if (lane == 0) KQ_TRACE_AT(P.trace_id, 0);
   if (!P.st) pdl_wait();
   int n = (P.st ? P.st->pos : P.pos[t]) + 1;
   if (n > P.ctx || n < 1) {
@@ -693,6 +696,7 @@ __global__ void __launch_bounds__(32) k_dattn_mma(const __grid_constant__ DAttnP
     for (int i = 0; i < 16; ++i) __stcg(reinterpret_cast<float2*>(pr + 8 * i + 2 * t4), make_float2(o[i][2], o[i][3]));
     if (t4 == 0) { __stcg(pr + HD, mB); __stcg(pr + HD + 1, lB); }
   }
+  if (lane == 0) KQ_TRACE_AT(P.trace_id, 4);
 }
 
 // grid (token, KV head, query head), DM_MERGE_THREADS threads: the split weights exp(m_s - M) and
@@ -713,7 +717,9 @@ __global__ void __launch_bounds__(DM_MERGE_THREADS) k_dattn_merge(const __grid_c
   // the next kernel (the o GEMV) may become resident now and request its weights while the
   // partials finish; it reads this kernel's output only after its own dependency wait
   pdl_trigger();
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 6);
   pdl_wait();
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 7);
   const int ns = P.nsplit;
   const float* pb = P.part + ((size_t)t * P.n_kv + kv) * ns * G * PLD + (size_t)g * PLD;
   const int q = tid / HD, d = tid % HD, per = (ns + NQ - 1) / NQ, s0 = q * per, s1 = min(ns, s0 + per);
@@ -763,6 +769,7 @@ __global__ void __launch_bounds__(DM_MERGE_THREADS) k_dattn_merge(const __grid_c
     if (P.out_f) P.out_f[(size_t)t * P.n_kv * G * HD + col] = v;
     else xp_store(P.out_xp, P.Npad, t, col, v);
   }
+  if (tid == 0) KQ_TRACE_AT(P.trace_id, 8);
 }
 
 // Tensor-parallel head: per-token (best value, global id) of this rank's vocabulary slice, whose

@@ -118,7 +118,7 @@ constexpr int KQ_TRACE_LAUNCHES = 256, KQ_TRACE_CTAS = 1024, KQ_TRACE_POINTS = 1
 __device__ unsigned long long g_kq_trace[KQ_TRACE_LAUNCHES][KQ_TRACE_CTAS][KQ_TRACE_POINTS];
 __device__ __forceinline__ void kq_trace(int launch, int point) {
   if (launch < 0 || launch >= KQ_TRACE_LAUNCHES) return;
-  const int cta = blockIdx.x + blockIdx.y * gridDim.x;
+  const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
   if (cta >= KQ_TRACE_CTAS) return;
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
