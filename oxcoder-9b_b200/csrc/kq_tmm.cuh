@@ -204,6 +204,7 @@ struct TmmParams {
   float* part;         // split-K partials [nsplit][Npad][ntiles * TM_ROWS]
   int* ticket;         // [ntiles], zero between launches
   int* err;
+  int trace_id;        // launch index for the optional phase trace (KQ_TRACE builds)
 };
 
 // Dynamic shared memory: 1024-byte alignment slack, raw ring, `xs` activation stages of
@@ -443,6 +444,7 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
   tc_fence_after();
   const uint32_t tmem = s_tmem;
   pdl_trigger();
+  if (threadIdx.x == 0) KQ_TRACE_AT(P.trace_id, 0);
 
   if (warp == 8) {
     // ---------------- raw loader: weights do not depend on the previous kernel (no PDL wait)
@@ -482,12 +484,15 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
         }
       }
       cp_async_arrive(&raw_full[slot]);
+      if (lane == 0 && k == 0) KQ_TRACE_AT(P.trace_id, 1);
+      if (lane == 0 && k == nsb - 1) KQ_TRACE_AT(P.trace_id, 11);
     }
     cp_async_wait_all();
   } else if (warp == 10) {
     // ---------------- activation loader
     if (lane == 0) {
       pdl_wait();
+      KQ_TRACE_AT(P.trace_id, 8);
       const uint64_t pol = l2_evict_last_policy();
       int i = 0;
       for (; i < nsub; ++i) {
@@ -522,7 +527,10 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
         }
         tc_commit(&sfree[slot]);
         tc_commit(&x_free[xsl]);
+        if (i == 0) KQ_TRACE_AT(P.trace_id, 3);
+        if (i == nsub / 2) KQ_TRACE_AT(P.trace_id, 10);
       }
+      KQ_TRACE_AT(P.trace_id, 5);
       tc_commit(&acc_full);   // also after a failure: arrives once the issued MMAs are done
     }
     __syncwarp();
@@ -602,6 +610,9 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[as]);
+        if (warp == 0 && lane == 0 && i == 0) KQ_TRACE_AT(P.trace_id, 2);
+        if (warp == 0 && lane == 0 && i == nsub / 2) KQ_TRACE_AT(P.trace_id, 9);
+        if (warp == 0 && lane == 0 && i == nsub - 1) KQ_TRACE_AT(P.trace_id, 4);
       }
       __syncwarp();
       if (lane == 0 && ok) mbar_arrive(&raw_empty[slot]);
@@ -609,6 +620,7 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
     // ---------------- epilogue (warps 0-7): TMEM lane quarter warp & 3, token half warp >> 2
     if (ok) ok = tm_wait(&acc_full, 0, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f);
     const bool good = named_bar_and(1, TM_DQ_WARPS * 32, ok && !*abort_f);
+    if (threadIdx.x == 0) KQ_TRACE_AT(P.trace_id, 6);
     if (good) {
       pdl_wait();
       tc_fence_after();
@@ -633,13 +645,28 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
         named_bar(1, TM_DQ_WARPS * 32);
         if (s_last) {
           __threadfence();
-          for (int cc = 0; cc < nc; ++cc) {
-            const int tk = c0 + cc;
-            if (tk >= P.M) break;   // uniform over the warp
-            float v = 0.f;
-            for (int s2 = 0; s2 < P.nsplit; ++s2) v = __fadd_rn(v, __ldcg(P.part + ((size_t)s2 * Npad + tk) * Rtot + grow));
-            const float vo = __shfl_xor_sync(0xffffffffu, v, 1);
-            if (row_ok) tm_epilogue(P, S, lrow, tk, v, vo);
+          // 8 tokens at a time: every split's partial requested before any is summed (one L2
+          // round trip per group, not one per token and split); sums in split order
+          for (int cb = 0; cb < nc; cb += 8) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = 0.f;
+            for (int s2 = 0; s2 < P.nsplit; ++s2) {
+              float u[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int tk = c0 + cb + e;
+                u[e] = cb + e < nc && tk < P.M ? __ldcg(P.part + ((size_t)s2 * Npad + tk) * Rtot + grow) : 0.f;
+              }
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], u[e]);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int tk = c0 + cb + e;
+              const float vo = __shfl_xor_sync(0xffffffffu, v[e], 1);
+              if (cb + e < nc && tk < P.M && row_ok) tm_epilogue(P, S, lrow, tk, v[e], vo);
+            }
           }
           if (threadIdx.x == 0) P.ticket[tile] = 0;
         }
@@ -660,6 +687,7 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) KQ_TRACE_AT(P.trace_id, 7);
   if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, TM_TMEM_COLS);
