@@ -449,26 +449,32 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
   if (warp == 8) {
     // ---------------- raw loader: weights do not depend on the previous kernel (no PDL wait)
     const uint64_t pol = l2_evict_first_policy();
+    // The nibble / ql and qh copies: lane = (row r8 of every 8-row tile, 16-byte chunk pc of a
+    // 64-byte run). Every row this lane copies sits at position r8 of its tile (row0 is a
+    // multiple of 128), so the row-dependent part of the address (row_plane_off) is a per-lane
+    // base plus a multiple of the tile size, and per super-block only the swizzled column offset
+    // changes.
+    const int r8 = lane >> 2, pc = lane & 3;
+    const size_t TB = tile_bytes(w.type, G);
+    const uint8_t* pbase = w.base + (size_t)(row0 >> 3) * TB + (size_t)r8 * 128 * G;                    // p0, row r8
+    const uint8_t* qbase = w.base + (size_t)(row0 >> 3) * TB + (size_t)8 * 128 * G + (size_t)r8 * 64 * G;   // Q6_K qh
     for (int k = 0; k < nsb; ++k) {
       const int slot = k % TM_RS;
       if (k >= TM_RS && !tm_wait(&raw_empty[slot], (uint32_t)((k / TM_RS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
         break;
       const int g = g0 + k;
       uint8_t* dst = raw_ring + slot * TM_RAW_BYTES;
-      // nibbles / ql (and Q6_K qh): 8 rows per instruction, 4 lanes per 64-byte run
+      const size_t o0 = p0_swz(r8, (size_t)g * 64 + pc * 16), o1 = p0_swz(r8, (size_t)64 * G + (size_t)g * 64 + pc * 16);
+      const size_t oq = q6_qh_swz(G, r8, (size_t)g * 64 + pc * 16);
+      // 8 rows per instruction, 4 lanes per 64-byte run
 #pragma unroll 4
       for (int rb = 0; rb < TM_ROWS / 8; ++rb) {
-        const int r = 8 * rb + (lane >> 2), pc = lane & 3, row = row0 + r;
+        const int r = 8 * rb + r8, row = row0 + r;
         const bool ok = row < w.R;
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint8_t* src = ok ? w.base + row_plane_off(w.type, G, row, 0, (size_t)c * 64 * G + (size_t)g * 64 + pc * 16) : w.base;
-          cp_async16(dst + r * rstride + c * 64 + pc * 16, src, ok ? 16u : 0u, pol);
-        }
-        if (!q4) {
-          const uint8_t* src = ok ? w.base + row_plane_off(Q6K, G, row, 1, (size_t)g * 64 + pc * 16) : w.base;
-          cp_async16(dst + r * rstride + 128 + pc * 16, src, ok ? 16u : 0u, pol);
-        }
+        const uint8_t* tp = pbase + (size_t)rb * TB;
+        cp_async16(dst + r * rstride + pc * 16, ok ? tp + o0 : w.base, ok ? 16u : 0u, pol);
+        cp_async16(dst + r * rstride + 64 + pc * 16, ok ? tp + o1 : w.base, ok ? 16u : 0u, pol);
+        if (!q4) cp_async16(dst + r * rstride + 128 + pc * 16, ok ? qbase + (size_t)rb * TB + oq : w.base, ok ? 16u : 0u, pol);
       }
       // Q4_K header / Q6_K scales (16 B per row); Q6_K d: the aligned 4-byte word that holds it
 #pragma unroll
