@@ -1,26 +1,29 @@
-// kq_gemv_mma.cuh -- single-token Q4_K GEMV with the multiply-adds on the tensor cores.
+// kq_gemv_mma.cuh -- single-token Q4_K / Q6_K GEMV with the multiply-adds on the tensor cores.
 //
-// The same job as k_gemv (kq_gemv.cuh) for matrices whose segments are all Q4_K: the decode
-// step's o and gate/up GEMVs and config-0's matrix. k_gemv spends about three thread instructions
-// per weight on dp4a digit-plane arithmetic and is issue-bound near 4.5 TB/s; here one
-// mma.sync.m16n8k32 (u8 weights x s8 activation digits, s32 accumulation) does the work of 384
-// dp4a lanes, so the consumers can keep up with HBM.
+// The same job as k_gemv (kq_gemv.cuh): the decode step's q/k/v (Q4_K q, k and Q6_K v in one
+// launch), o, gate/up and down GEMVs and config-0's matrix; the planner keeps long Q6_K-only
+// launches (the output head) on k_gemv, whose dp4a consumer streams Q6_K faster once the
+// prologue is amortised. k_gemv spends about three thread instructions per weight on dp4a
+// digit-plane arithmetic; here one mma.sync.m16n8k32 (u8 weights x s8 activation digits, s32
+// accumulation) does the work of 384 dp4a lanes.
 //
 //  * Weight stream: as in k_gemv (producer warp, 1-D bulk copies of whole 8-row tiles into an
-//    mbarrier ring), with stages of one 16-row MMA block.
+//    mbarrier ring, stages fixed per CTA or claimed at run time), with Q4_K stages of 16 NB rows
+//    and Q6_K stages of 8-32 rows (the segment's `tr`).
 //  * Activations: the prologue (residual + fp64 RMS norm, embedding row or plain vector, exactly
 //    as k_gemv's) splits x exactly into three int8 digit planes with one power-of-two scale per
-//    256-column super-block, x = s3 (16384 x1 + 128 x2 + x3), stored per 32-column sub-block as
-//    the B operand bytes [sub-block][plane][32], plus the digit sums of every sub-block (the
-//    dmin term) and per super-block s3 and a NaN poison.
-//  * Consumers: warp w takes super-blocks [w G / 8, (w + 1) G / 8) of the stage's 16 rows. Per
-//    pair of sub-blocks one ldmatrix.x4 brings the 16 rows x 32 bytes of nibbles (conflict-free
-//    thanks to the swizzled tile layout, kq_qformat.cuh) in A-fragment order; the low and the
-//    high nibbles are two MMAs against the sub-blocks' digit columns (planes 0-2 of N = 8). The
-//    int32 results are multiplied by the 6-bit block scales and summed per super-block in
-//    int32 (exact), then combined in fp32 with d, dmin and the activation scale, in a fixed
-//    order; the 8 warps' row partials are summed in warp order. The int32 sums are the exact dot
-//    products the dp4a form computes, so results agree with k_gemv to fp32 rounding.
+//    256-column super-block, x = s3 (16384 x1 + 128 x2 + x3), stored per pair of 32-column
+//    sub-blocks as MMA fragment bytes, plus the digit sums of every sub-block (the Q4_K dmin
+//    term), the Q6_K "-32" table per 16-column half, and per super-block s3 and a NaN poison.
+//  * Q4_K consumers: per pair of sub-blocks one ldmatrix.x4 brings 16 rows x 32 bytes of
+//    nibbles (conflict-free thanks to the swizzled tile layout, kq_qformat.cuh) in A-fragment
+//    order; the low and the high nibbles are two MMAs against the digit columns (planes 0-2 of
+//    N = 8). Q6_K consumers (gm6_stage): one MMA per sub-block for the 8 rows of a tile, the
+//    4-bit and 2-bit parts as the A rows. The int32 results are multiplied by the block scales
+//    and summed per super-block in int32 (exact), then combined in fp32 with d (dmin) and the
+//    activation scale, in a fixed order; the warps' row partials are summed in warp order. The
+//    int32 sums are the exact dot products the dp4a form computes, so results agree with k_gemv
+//    to fp32 rounding.
 //  * Epilogues: those of k_gemv (gemv_row_epilogue), the argmax merge included.
 #pragma once
 #include "kq_gemv.cuh"
