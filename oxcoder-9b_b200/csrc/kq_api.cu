@@ -658,6 +658,7 @@ struct kq_model {
   float *bh = nullptr, *by = nullptr, *bq = nullptr, *bpart = nullptr;
   __half *bxd = nullptr, *bxa = nullptr, *bxf = nullptr;   // packed GEMM inputs: C = dim, NH*HD, ffn
   float *bxs_n = nullptr, *bxs_f = nullptr;   // per-token range scales of bxd (norm) and bxf (SwiGLU)
+  float *bxd_sum = nullptr, *bxf_sum = nullptr;   // their sub-block sums (xp_sub_sum; C % 256 == 0)
   float* bmf = nullptr;                       // [MM_MAXM][ffn_l] SwiGLU output before packing
   int *btok = nullptr, *bslot = nullptr, *brpos = nullptr, *bticket = nullptr;
   unsigned long long* bmask = nullptr;
@@ -1908,6 +1909,12 @@ static int tmm_split(int ntiles, int G, int nsm) {
   }
   return best;
 }
+// Comparison switch: KQ_TMM_EXACT=0 keeps every row tile on the split-weight form (the exact form
+// needs the sub-block sums of the packed input and Npad <= 64; it covers Q4_K row tiles).
+static bool tmm_exact_ok() {
+  const char* e = std::getenv("KQ_TMM_EXACT");
+  return !(e && std::atoi(e) == 0);
+}
 static int tmm_tiles(const SegSpec* ss, int nseg) {
   int t = 0;
   for (int i = 0; i < nseg; ++i) t += (ss[i].m->R + TM_ROWS - 1) / TM_ROWS;
@@ -1976,6 +1983,8 @@ static int batch_buffers(kq_model* m) {
   m->bxf = dalloc<__half>(m, xp_halves(MM_MAXM, m->ffn_l), ok);
   m->bxs_n = dalloc<float>(m, MM, ok);
   m->bxs_f = dalloc<float>(m, MM, ok);
+  if (c.dim % 256 == 0) m->bxd_sum = dalloc<float>(m, MM * (c.dim / 32), ok);
+  if (m->ffn_l % 256 == 0) m->bxf_sum = dalloc<float>(m, MM * (m->ffn_l / 32), ok);
   m->bmf = dalloc<float>(m, MM * m->ffn_l, ok);
   m->btok = dalloc<int>(m, MM, ok);
   m->bslot = dalloc<int>(m, MM, ok);
@@ -2011,14 +2020,16 @@ static bool batch_supported(const kq_model* m) {
   return m->ffn_l % 64 == 0 && (m->nh_l * m->c.head_dim) % 64 == 0;
 }
 
-// xscale: the per-token scales of the packed input xp (k_bnorm / k_xpack_tok), or null.
-static int launch_tmm(kq_model* m, const SegSpec* ss, int nseg, const __half* xp, const float* xscale, int out_ld,
-                      const BatchParams& B) {
+// xscale: the per-token scales of the packed input xp (k_bnorm / k_xpack_tok), or null; xsum: its
+// sub-block sums (they enable the exact form for Q4_K row tiles), or null.
+static int launch_tmm(kq_model* m, const SegSpec* ss, int nseg, const __half* xp, const float* xscale,
+                      const float* xsum, int out_ld, const BatchParams& B) {
   prof_mark(m, PC_GEMM);
   TmmParams P;
   tmm_fill(ss, nseg, B.M, m->device, P);
   P.xp = xp;
   P.xscale = xscale;
+  P.xsum = tmm_exact_ok() ? xsum : nullptr;
   P.B = B;
   P.out_ld = out_ld;
   P.cos_t = m->cos_t;
@@ -2042,7 +2053,7 @@ static int launch_bnorm(kq_model* m, int M, bool embed, const float* gamma, bool
   P.M = M; P.D = m->c.dim; P.tok = m->btok;
   if (embed) P.emb = m->emb->view();
   P.h = m->bh; P.y = add ? m->by : nullptr; P.gamma = gamma; P.eps = m->c.eps;
-  P.xp = m->bxd; P.xscale = m->bxs_n; P.Npad = (M + 15) & ~15;
+  P.xp = m->bxd; P.xscale = m->bxs_n; P.xsum = m->bxd_sum; P.Npad = (M + 15) & ~15;
   P.vocab = m->c.vocab; P.err = m->err;
   CU(launch_pdl(k_bnorm, dim3((unsigned)M), dim3(BN_THREADS), 0, m->stream, P));
   return KQ_OK;
@@ -2054,13 +2065,13 @@ static int launch_bnorm(kq_model* m, int M, bool embed, const float* gamma, bool
 static int launch_mlp(kq_model* m, LayerW& w, float* y, const BatchParams& B) {
   const int M = B.M, Npad = (M + 15) & ~15;
   SegSpec sg[1] = {{w.gu, EPI_SWIGLU, m->bmf, nullptr}};
-  int rc = launch_tmm(m, sg, 1, m->bxd, m->bxs_n, m->ffn_l, B);
+  int rc = launch_tmm(m, sg, 1, m->bxd, m->bxs_n, m->bxd_sum, m->ffn_l, B);
   if (rc) return rc;
   prof_mark(m, PC_GEMM);
-  const XPackParams X = {m->bmf, m->ffn_l, m->ffn_l, Npad, m->bxf, m->bxs_f};
+  const XPackParams X = {m->bmf, m->ffn_l, m->ffn_l, Npad, m->bxf, m->bxs_f, m->bxf_sum};
   CU(launch_pdl(k_xpack_tok, dim3((unsigned)M), dim3(XP_THREADS), 0, m->stream, X));
   SegSpec sd[1] = {{w.down, EPI_F32, y, nullptr}};
-  return launch_tmm(m, sd, 1, m->bxf, m->bxs_f, m->c.dim, B);
+  return launch_tmm(m, sd, 1, m->bxf, m->bxs_f, m->bxf_sum, m->c.dim, B);
 }
 
 static int launch_battn(kq_model* m, const __half* kc, const __half* vc, int npos, const BatchParams& B) {
@@ -2122,10 +2133,10 @@ static int verify_pass(kq_model* m, const int32_t* tokens, int b0, int b1, int p
     __half* kc = seq < 0 ? w.kc : w.bkc + (size_t)seq * sstride;
     __half* vc = seq < 0 ? w.vc : w.bvc + (size_t)seq * sstride;
     SegSpec qkv[3] = {{w.q, EPI_ROPE_Q, m->bq, nullptr}, {w.k, EPI_ROPE_K, nullptr, kc}, {w.v, EPI_V, nullptr, vc}};
-    if ((rc = launch_tmm(m, qkv, 3, m->bxd, m->bxs_n, QD, B))) return rc;
+    if ((rc = launch_tmm(m, qkv, 3, m->bxd, m->bxs_n, m->bxd_sum, QD, B))) return rc;
     if ((rc = launch_battn(m, kc, vc, pos + b1, B))) return rc;
     SegSpec so[1] = {{w.o, EPI_F32, m->by, nullptr}};
-    if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, c.dim, B))) return rc;   // attention output: |x| <= max|V|
+    if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, nullptr, c.dim, B))) return rc;   // attention output: |x| <= max|V|
     if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;   // row-split o: sum the partials
     if ((rc = launch_bnorm(m, M, false, w.ffn_norm, true))) return rc;
     if ((rc = launch_mlp(m, w, m->by, B))) return rc;
@@ -2143,7 +2154,7 @@ static int head_argmax(kq_model* m, int M, const BatchParams& B, int* out_ids, s
   if ((rc = launch_bnorm(m, M, false, m->out_norm, true))) return rc;
   const size_t V = (size_t)m->vocab_l;   // this rank's vocabulary slice
   SegSpec sh[1] = {{m->out, EPI_F32, m->vlogits + row0 * V, nullptr}};
-  if ((rc = launch_tmm(m, sh, 1, m->bxd, m->bxs_n, (int)V, B))) return rc;
+  if ((rc = launch_tmm(m, sh, 1, m->bxd, m->bxs_n, m->bxd_sum, (int)V, B))) return rc;
   prof_mark(m, PC_OTHER);
   if (m->tp_world == 1) {
     k_argmax_rows<<<M, 256, 0, s>>>(m->vlogits + row0 * V, (int)V, out_ids);
@@ -2376,7 +2387,7 @@ extern "C" int kq_batch_step(kq_model* m, const int32_t* seqs, const int32_t* to
     LayerW& w = m->L[l];
     if ((rc = launch_bnorm(m, M, l == 0, w.attn_norm, l > 0))) return rc;
     SegSpec qkv[3] = {{w.q, EPI_ROPE_Q, m->bq, nullptr}, {w.k, EPI_ROPE_K, nullptr, w.bkc}, {w.v, EPI_V, nullptr, w.bvc}};
-    if ((rc = launch_tmm(m, qkv, 3, m->bxd, m->bxs_n, QD, B))) return rc;
+    if ((rc = launch_tmm(m, qkv, 3, m->bxd, m->bxs_n, m->bxd_sum, QD, B))) return rc;
     D.kc = w.bkc;
     D.vc = w.bvc;
     prof_mark(m, PC_ATTN);
@@ -2384,7 +2395,7 @@ extern "C" int kq_batch_step(kq_model* m, const int32_t* seqs, const int32_t* to
                   : G == 4 ? launch_dattn_t<4>(D, M, m->nkv_l, s) : launch_dattn_t<8>(D, M, m->nkv_l, s);
     CU(e);
     SegSpec so[1] = {{w.o, EPI_F32, m->by, nullptr}};
-    if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, c.dim, B))) return rc;   // attention output: |x| <= max|V|
+    if ((rc = launch_tmm(m, so, 1, m->bxa, nullptr, nullptr, c.dim, B))) return rc;   // attention output: |x| <= max|V|
     if ((rc = tp_allreduce(m, m->by, (size_t)M * c.dim))) return rc;
     if ((rc = launch_bnorm(m, M, false, w.ffn_norm, true))) return rc;
     if ((rc = launch_mlp(m, w, m->by, B))) return rc;
@@ -2555,11 +2566,13 @@ extern "C" int kq_qmat_matmul(kq_qmat* a, const float* x, int M, float* y) {
   TmmParams P;
   tmm_fill(ss, 1, M, a->device, P);
   const size_t pf = tmm_part_floats(P.ntiles, P.nsplit, P.Npad);
-  float *xd = nullptr, *yd = nullptr, *part = nullptr, *xs = nullptr;
+  float *xd = nullptr, *yd = nullptr, *part = nullptr, *xs = nullptr, *xsum = nullptr;
   __half* xp = nullptr;
   int* ticket = nullptr;
+  const bool sums = a->C % 256 == 0 && tmm_exact_ok();
   bool ok = cudaMalloc(&xd, (size_t)M * a->C * 4) == cudaSuccess;
   ok = ok && cudaMalloc(&xs, (size_t)M * 4) == cudaSuccess;
+  ok = ok && (!sums || cudaMalloc(&xsum, (size_t)P.Npad * (a->C / 32) * 4) == cudaSuccess);
   ok = ok && cudaMalloc(&yd, (size_t)M * a->R * 4) == cudaSuccess;
   ok = ok && cudaMalloc(&xp, xp_halves(P.Npad, a->C) * 2) == cudaSuccess;
   ok = ok && cudaMalloc(&part, std::max<size_t>(pf, 1) * 4) == cudaSuccess;
@@ -2570,10 +2583,11 @@ extern "C" int kq_qmat_matmul(kq_qmat* a, const float* x, int M, float* y) {
               cudaMemcpy(xd, x, (size_t)M * a->C * 4, cudaMemcpyHostToDevice) != cudaSuccess))
     rc = set_err(KQ_ERR_BACKEND, "matmul upload");
   if (!rc) {
-    const XPackParams X = {xd, a->C, a->C, P.Npad, xp, xs};
+    const XPackParams X = {xd, a->C, a->C, P.Npad, xp, xs, xsum};
     k_xpack_tok<<<(unsigned)M, XP_THREADS>>>(X);
     P.xp = xp;
     P.xscale = xs;
+    P.xsum = xsum;
     P.seg[0].out_f = yd;
     P.out_ld = a->R;
     P.part = part;
@@ -2588,6 +2602,7 @@ extern "C" int kq_qmat_matmul(kq_qmat* a, const float* x, int M, float* y) {
   cudaFree(yd);
   cudaFree(xp);
   cudaFree(xs);
+  cudaFree(xsum);
   cudaFree(part);
   cudaFree(ticket);
   if (!rc) rc = dev_err_check(a->device);
@@ -2661,7 +2676,7 @@ static int ffn_block_enqueue(kq_model* m, int layer, float* x_dev, int M, float*
   BNormParams P;
   std::memset(&P, 0, sizeof(P));
   P.M = M; P.D = c.dim; P.h = x_dev; P.gamma = w.ffn_norm; P.eps = c.eps;
-  P.xp = m->bxd; P.xscale = m->bxs_n; P.Npad = (M + 15) & ~15; P.vocab = c.vocab; P.err = m->err;
+  P.xp = m->bxd; P.xscale = m->bxs_n; P.xsum = m->bxd_sum; P.Npad = (M + 15) & ~15; P.vocab = c.vocab; P.err = m->err;
   CU(launch_pdl(k_bnorm, dim3((unsigned)M), dim3(BN_THREADS), 0, s, P, pdl));
   BatchParams B;
   B.M = M; B.slot = m->bslot; B.rpos = m->brpos; B.mask = m->bmask; B.tree_base = 0; B.seq = nullptr;

@@ -33,6 +33,7 @@ struct BNormParams {
   float eps;
   __half* xp;              // packed input of the next GEMM (C = D)
   float* xscale;           // [M] the power of two each packed row was divided by (xp_scale_exp)
+  float* xsum;             // sub-block sums of the packed rows (xp_sub_sum; D % 256 == 0), or null
   int Npad;
   int vocab;
   int* err;
@@ -122,6 +123,7 @@ __global__ void __launch_bounds__(BN_THREADS) k_bnorm(const __grid_constant__ BN
     const size_t o = xp_off(P.Npad, t, 8 * c);   // 8 consecutive halves
     *reinterpret_cast<uint4*>(P.xp + o) = hi;
     *reinterpret_cast<uint4*>(P.xp + o + (size_t)64 * P.Npad) = lo;
+    if (P.xsum) xp_sub_sum(P.xsum, P.Npad, t, c, x);   // whole warps: nch is a multiple of 32
   }
 }
 

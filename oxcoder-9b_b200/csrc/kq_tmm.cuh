@@ -51,17 +51,32 @@ __device__ __forceinline__ void xp_store(__half* xp, int Npad, int tok, int col,
   xp[o] = hi;
   xp[o + (size_t)64 * Npad] = lo;
 }
+// Sub-block sums of the packed rows, for the exact form of the GEMM: xsum[g][t][b] = the fp32 sum
+// of token t's packed values over columns 256 g + 32 b .. + 31. The caller holds the 8 packed
+// values of chunk c (columns 8c .. 8c + 7) of token t; the four chunks of a sub-block sit in four
+// adjacent lanes, and every lane of the warp takes part.
+__device__ __forceinline__ void xp_sub_sum(float* xsum, int Npad, int t, int c, const float (&x)[8]) {
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(x[0], x[1]), __fadd_rn(x[2], x[3])),
+                      __fadd_rn(__fadd_rn(x[4], x[5]), __fadd_rn(x[6], x[7])));
+  s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
+  s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 2));
+  if ((c & 3) == 0) {
+    const int sb = c >> 2;
+    xsum[((size_t)(sb >> 3) * Npad + t) * 8 + (sb & 7)] = s;
+  }
+}
 
-// Per-token range scaling of the packed activations. hi = fp16(x) overflows for |x| > 65504, and
-// hi + lo then turns into inf - inf in the MMA. A producer that cannot bound its values (the
-// SwiGLU output, a caller's fp32 rows, a norm output with large gamma) packs token t's row scaled
-// by 2^-e_t, the smallest e_t >= 0 that brings the row's largest magnitude below 2^15, and
-// records 2^e_t; the GEMM epilogue multiplies token t's results by it. Powers of two are exact,
-// so a row that needs no scaling (e_t = 0) packs bit for bit as before. NaN and inf keep e_t = 0
-// and propagate.
+// Per-token range scaling of the packed activations. hi = fp16(x) overflows for |x| > 65504 (hi +
+// lo then turns into inf - inf in the MMA), and below 2^-14 hi and lo lose bits to fp16's
+// subnormal range. A producer (the SwiGLU output, a caller's fp32 rows, a norm output) packs token
+// t's row scaled by 2^-e_t, e_t = floor(log2 of the row's largest magnitude, or a bound of it) - 14,
+// so that magnitude lands in [2^14, 2^15), and records 2^e_t; the GEMM epilogue multiplies token
+// t's results by it. Powers of two are exact. e_t is kept >= -100 (2^100 and 2^-100 are normal
+// floats); a zero row, NaN and inf keep e_t = 0 (non-finite values propagate).
 __device__ __forceinline__ int xp_scale_exp(float amax) {
-  if (!(amax >= 32768.f) || amax > 3.0e38f) return 0;
-  return (int)((__float_as_uint(amax) >> 23) & 255u) - 127 - 14;   // floor(log2 amax) - 14
+  if (!(amax > 0.f) || amax > 3.0e38f) return 0;
+  const int e = (int)((__float_as_uint(amax) >> 23) & 255u) - 127 - 14;   // floor(log2 amax) - 14
+  return e < -100 ? -100 : e;
 }
 __device__ __forceinline__ float xp_pow2(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
 
@@ -178,6 +193,21 @@ constexpr uint32_t TM_TMEM_COLS = 512, TM_ASTAGE_COLS = 128;
 __host__ __device__ constexpr uint32_t tmm_acol(int Npad) { return Npad <= 64 ? 128u : 256u; }
 __host__ __device__ constexpr int tmm_as(int Npad) { return Npad <= 64 ? 3 : 2; }
 static_assert(128 + 3 * TM_ASTAGE_COLS <= TM_TMEM_COLS && 256 + 2 * TM_ASTAGE_COLS <= TM_TMEM_COLS, "tensor memory plan");
+// Exact-integer form (Q4_K row tiles, Npad <= 64, activations packed with their sub-block sums).
+// A holds q * sc, an integer <= 945 and so exact in fp16: one MMA per K step (N = 2 Npad against
+// the hi and the lo token rows) and a quarter of the dequantisation work. The super-block scale d
+// and the minimum term are applied outside the tensor core: each super-block accumulates into one
+// of two buffers of tensor memory (columns [0, 128) and [128, 256): A * hi(x) in the first Npad
+// columns, A * lo(x) in the next), which the dequantising warps read back, scale by d and add to
+// registers while the next super-block accumulates in the other buffer; the minimum term
+// dmin * mn * (sum of x over the sub-block) is an fp32 product with the sub-block sums that the
+// packer wrote. Then 2 A stages of one super-block (128 columns of q * sc fp16 pairs) from column
+// 256. Every hand-off (A stage, activation stage, accumulator buffer) is per super-block: the
+// waits and commits of the single MMA-issuing thread, not the MMAs, set the pace of this kernel.
+constexpr int TM_XAS = 2, TM_SR = 4;               // A stages (super-blocks); sub-block-sum stages
+constexpr uint32_t TM_XD_COLS = 128, TM_XA0 = 256, TM_XASTAGE_COLS = 128;
+constexpr int TM_AS_MAX = TM_XAS > TM_AS ? TM_XAS : TM_AS;
+static_assert(TM_XA0 + TM_XAS * TM_XASTAGE_COLS <= TM_TMEM_COLS && 2 * TM_XD_COLS <= TM_XA0, "tensor memory plan (exact form)");
 static_assert(TM_RAW_BYTES % 1024 == 0, "rings must keep 1024-byte alignment");
 
 struct TmmSeg {
@@ -195,6 +225,7 @@ struct TmmParams {
   int xs;              // activation ring stages (1..TM_XS_MAX), see tmm_smem
   const __half* xp;    // packed activations (xp_off layout)
   const float* xscale; // per token: the power of two its packed row was divided by (null: none)
+  const float* xsum;   // sub-block sums of the packed rows [G][Npad][8] (xp_sub_sum), or null
   BatchParams B;
   int out_ld;          // row length of the fp32 outputs
   const float* cos_t;
@@ -208,14 +239,18 @@ struct TmmParams {
 };
 
 // Dynamic shared memory: 1024-byte alignment slack, raw ring, `xs` activation stages of
-// 512 * Npad bytes (two 64-column groups; 1024-byte aligned: SWIZZLE_128B atoms), Q6_K d words.
+// 512 * Npad bytes (two 64-column groups; 1024-byte aligned: SWIZZLE_128B atoms), Q6_K d words,
+// TM_SR stages of one super-block's sub-block sums (32 * Npad bytes; exact form).
 __host__ __device__ inline size_t tmm_smem_fixed() {
   return 1024 + (size_t)TM_RS * TM_RAW_BYTES + (size_t)TM_RS * TM_ROWS * 4;
 }
-__host__ __device__ inline size_t tmm_smem(int Npad, int xs) { return tmm_smem_fixed() + (size_t)xs * 512 * Npad; }
+__host__ __device__ inline size_t tmm_smem(int Npad, int xs) {
+  return tmm_smem_fixed() + (size_t)xs * 512 * Npad + (size_t)TM_SR * 32 * Npad;
+}
 // The deepest activation ring that fits `budget` bytes of dynamic shared memory.
 __host__ __device__ inline int tmm_xs(int Npad, size_t budget) {
-  const size_t room = budget > tmm_smem_fixed() ? budget - tmm_smem_fixed() : 0;
+  const size_t fixed = tmm_smem_fixed() + (size_t)TM_SR * 32 * Npad;
+  const size_t room = budget > fixed ? budget - fixed : 0;
   const int xs = (int)(room / ((size_t)512 * Npad));
   return xs < 1 ? 0 : xs > TM_XS_MAX ? TM_XS_MAX : xs;
 }
@@ -283,6 +318,7 @@ struct XPackParams {
   int ld, C, Npad;
   __half* xp;          // packed activations
   float* scale;        // [M]
+  float* xsum;         // sub-block sums (xp_sub_sum; C a multiple of 256), or null
 };
 __global__ void __launch_bounds__(XP_THREADS) k_xpack_tok(const __grid_constant__ XPackParams P) {
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -306,16 +342,19 @@ __global__ void __launch_bounds__(XP_THREADS) k_xpack_tok(const __grid_constant_
   for (int w = 1; w < XP_THREADS / 32; ++w) mx = fmaxf(mx, red[w]);
   const int e = xp_scale_exp(mx);
   const float inv = xp_pow2(-e);
-  for (int c = tid; c < nch; c += XP_THREADS) {
+  for (int c = tid; c < nch; c += XP_THREADS) {   // with sums: nch is a multiple of 32 (whole warps)
     const float4 a = row[2 * c], b = row[2 * c + 1];
+    const float x[8] = {__fmul_rn(a.x, inv), __fmul_rn(a.y, inv), __fmul_rn(a.z, inv), __fmul_rn(a.w, inv),
+                        __fmul_rn(b.x, inv), __fmul_rn(b.y, inv), __fmul_rn(b.z, inv), __fmul_rn(b.w, inv)};
     uint4 hi, lo;
-    tm_split(__fmul_rn(a.x, inv), __fmul_rn(a.y, inv), hi.x, lo.x);
-    tm_split(__fmul_rn(a.z, inv), __fmul_rn(a.w, inv), hi.y, lo.y);
-    tm_split(__fmul_rn(b.x, inv), __fmul_rn(b.y, inv), hi.z, lo.z);
-    tm_split(__fmul_rn(b.z, inv), __fmul_rn(b.w, inv), hi.w, lo.w);
+    tm_split(x[0], x[1], hi.x, lo.x);
+    tm_split(x[2], x[3], hi.y, lo.y);
+    tm_split(x[4], x[5], hi.z, lo.z);
+    tm_split(x[6], x[7], hi.w, lo.w);
     const size_t o = xp_off(Npad, t, 8 * c);
     *reinterpret_cast<uint4*>(xp + o) = hi;
     *reinterpret_cast<uint4*>(xp + o + (size_t)64 * Npad) = lo;
+    if (P.xsum) xp_sub_sum(P.xsum, Npad, t, c, x);
   }
   if (tid == 0) P.scale[t] = xp_pow2(e);
 }
@@ -351,6 +390,46 @@ __device__ __forceinline__ void tm_q6_row32(const uint4& L0, const uint4& L1, co
     for (int e = 0; e < 4; ++e) w[e] = __fmul_rn(ds, __fsub_rn(tm_magic(x, e), 8388640.f));
     tm_split(w[0], w[1], h[2 * i], l[2 * i]);
     tm_split(w[2], w[3], h[2 * i + 1], l[2 * i + 1]);
+  }
+}
+// 32 Q4_K weights of one row in the exact form: q * sc as fp16 (q the nibble at `sh` of the 32
+// bytes W0, W1; sc <= 63, so q * sc <= 945 is an integer fp16 holds exactly). The byte pair
+// (q, 0x64) is the fp16 1024 + q; one fused multiply-add per two weights gives
+// (1024 + q) * sc - 1024 sc with a single rounding of an exact integer result.
+__device__ __forceinline__ void tm_q4_exact32(const uint4& W0, const uint4& W1, int sh, uint32_t sc, uint32_t (&a)[16]) {
+  const __half2 s2 = __floats2half2_rn((float)sc, (float)sc);
+  const __half2 c2 = __floats2half2_rn(-1024.f * (float)sc, -1024.f * (float)sc);
+  const uint32_t wd[8] = {W0.x, W0.y, W0.z, W0.w, W1.x, W1.y, W1.z, W1.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t x = (wd[i] >> sh) & 0x0F0F0F0Fu;
+    uint32_t p0 = __byte_perm(x, 0x64u, 0x4140), p1 = __byte_perm(x, 0x64u, 0x4342);
+    a[2 * i] = h2u(__hfma2(*reinterpret_cast<__half2*>(&p0), s2, c2));
+    a[2 * i + 1] = h2u(__hfma2(*reinterpret_cast<__half2*>(&p1), s2, c2));
+  }
+}
+// 8 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tc_st8(uint32_t taddr, const float (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+               "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+               : "memory");
+}
+// Two loads of 8 fp32 columns (at a and at b), one wait.
+__device__ __forceinline__ void tc_ld8x2(uint32_t a, uint32_t b, float (&v)[8], float (&u)[8]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%16];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%17];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(a), "r"(b)
+      : "memory");
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    v[e] = __uint_as_float(r[e]);
+    u[e] = __uint_as_float(r[8 + e]);
   }
 }
 
@@ -405,9 +484,10 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
   uint8_t* raw_ring = sm;
   uint8_t* x_ring = raw_ring + TM_RS * TM_RAW_BYTES;   // 1024-aligned (SWIZZLE_128B atoms)
   uint32_t* d_ring = reinterpret_cast<uint32_t*>(x_ring + (size_t)XS * xbytes);
-  __shared__ __align__(8) uint64_t raw_full[TM_RS], raw_empty[TM_RS], a_full[TM_AS], sfree[TM_AS];
+  float* s_ring = reinterpret_cast<float*>(d_ring + TM_RS * TM_ROWS);   // [TM_SR][Npad][8]
+  __shared__ __align__(8) uint64_t raw_full[TM_RS], raw_empty[TM_RS], a_full[TM_AS_MAX], sfree[TM_AS_MAX];
   __shared__ __align__(8) uint64_t x_full[TM_XS_MAX], x_free[TM_XS_MAX];
-  __shared__ __align__(8) uint64_t acc_full;
+  __shared__ __align__(8) uint64_t acc_full, d_full[2], d_free[2], s_full[TM_SR], s_free[TM_SR];
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_last;
   volatile int* abort_f = &s_abort;
@@ -423,14 +503,19 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
   const int g0 = (int)((long long)sp * G / P.nsplit), g1 = (int)((long long)(sp + 1) * G / P.nsplit);
   const int nsb = g1 - g0, nsub = 2 * nsb;
   const bool q4 = w.type == Q4K;
+  // the exact form (this CTA's row tile): activation stages of a whole super-block, at least 2
+  const bool ex = q4 && P.xsum != nullptr && Npad <= 64 && XS >= 4;
+  const int XS2 = XS >> 1;
   const int rstride = q4 ? TM_RAW_Q4 : TM_RAW_Q6;
-  const int AS = tmm_as(Npad);
+  const int AS = ex ? TM_XAS : tmm_as(Npad);
   const uint32_t acol = tmm_acol(Npad);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < TM_RS; ++i) { mbar_init(&raw_full[i], 32); mbar_init(&raw_empty[i], TM_DQ_WARPS); }
     for (int i = 0; i < AS; ++i) { mbar_init(&a_full[i], TM_DQ_WARPS); mbar_init(&sfree[i], 1); }
     for (int i = 0; i < XS; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_free[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&d_full[i], 1); mbar_init(&d_free[i], TM_DQ_WARPS); }
+    for (int i = 0; i < TM_SR; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], TM_DQ_WARPS); }
     mbar_init(&acc_full, 1);
     s_abort = 0;
     fence_mbar_init();
@@ -501,7 +586,31 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
       KQ_TRACE_AT(P.trace_id, 8);
       const uint64_t pol = l2_evict_last_policy();
       int i = 0;
-      for (; i < nsub; ++i) {
+      if (ex) {
+        // exact form: per super-block its sub-block sums, then its 4 activation groups in one copy
+        int k = 0;
+        for (; k < nsb; ++k) {
+          const int ss = k % TM_SR, slot = k % XS2;
+          if (k >= TM_SR && !tm_wait(&s_free[ss], (uint32_t)((k / TM_SR) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
+            break;
+          mbar_arrive_expect_tx(&s_full[ss], 32u * (uint32_t)Npad);
+          bulk_g2s(s_ring + (size_t)ss * 8 * Npad, P.xsum + (size_t)(g0 + k) * 8 * Npad, 32u * (uint32_t)Npad, &s_full[ss], pol);
+          if (k >= XS2 && !tm_wait(&x_free[slot], (uint32_t)((k / XS2) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f)) {
+            ++k;
+            break;
+          }
+          mbar_arrive_expect_tx(&x_full[slot], 2 * xbytes);
+          bulk_g2s(x_ring + (size_t)slot * 2 * xbytes, P.xp + (size_t)(4 * (g0 + k)) * xp_group_halves(Npad), 2 * xbytes,
+                   &x_full[slot], pol);
+        }
+        // drain: the last copy into each buffer has completed before the CTA exits
+        for (int j = k - XS2 < 0 ? 0 : k - XS2; j < k; ++j)
+          tm_wait(&x_full[j % XS2], (uint32_t)(j / XS2) & 1, P.err, KQ_DEV_ERR_DRAIN, abort_f);
+        for (int j = k - TM_SR < 0 ? 0 : k - TM_SR; j < k; ++j)
+          tm_wait(&s_full[j % TM_SR], (uint32_t)(j / TM_SR) & 1, P.err, KQ_DEV_ERR_DRAIN, abort_f);
+        i = nsub;
+      }
+      for (; i < nsub && !ex; ++i) {
         const int slot = i % XS;
         if (i >= XS && !tm_wait(&x_free[slot], (uint32_t)((i / XS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f))
           break;
@@ -509,12 +618,39 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
         bulk_g2s(x_ring + slot * xbytes, P.xp + (size_t)(4 * g0 + 2 * i) * xp_group_halves(Npad), xbytes, &x_full[slot], pol);
       }
       // drain: the last copy into each buffer has completed before the CTA exits
-      for (int j = i - XS < 0 ? 0 : i - XS; j < i; ++j)
-        tm_wait(&x_full[j % XS], (uint32_t)(j / XS) & 1, P.err, KQ_DEV_ERR_DRAIN, abort_f);
+      if (!ex)
+        for (int j = i - XS < 0 ? 0 : i - XS; j < i; ++j)
+          tm_wait(&x_full[j % XS], (uint32_t)(j / XS) & 1, P.err, KQ_DEV_ERR_DRAIN, abort_f);
     }
   } else if (warp == 9) {
     // ---------------- MMA issue (one thread): A from tensor memory, activations from shared memory
-    if (lane == 0) {
+    if (lane == 0 && ex) {
+      // exact form: per super-block k one A stage (k & 1), one activation stage, and the
+      // accumulator buffer k & 1, which the dequantising warps have read back (d_free) before it
+      // is overwritten (accumulate = 0 at its first K step); 16 MMAs, three commits
+      const uint32_t idesc = tc_idesc_f16(TM_ROWS, 2 * Npad);
+      const uint64_t dX = sw128_desc(smem_u32(x_ring));
+      const uint64_t gstep = (256u * (uint32_t)Npad) >> 4;
+      for (int k = 0; k < nsb; ++k) {
+        const int as = k & 1, xsl = k % XS2;
+        if (!tm_wait(&a_full[as], (uint32_t)(k >> 1) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
+        if (!tm_wait(&x_full[xsl], (uint32_t)(k / XS2) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)) break;
+        if (k >= 2 && !tm_wait(&d_free[as], (uint32_t)((k >> 1) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f)) break;
+        tc_fence_after();
+        const uint32_t ta = tmem + TM_XA0 + (uint32_t)as * TM_XASTAGE_COLS, td = tmem + (uint32_t)as * TM_XD_COLS;
+        const uint64_t x0 = dX + (uint64_t)(((uint32_t)xsl * 2 * xbytes) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk)   // 16 K elements = 8 columns of A; 64-column group kk / 4, + 32 bytes per K step
+          tc_mma_f16_ts(td, ta + 8 * kk, x0 + (kk >> 2) * gstep + 2 * (kk & 3), idesc, kk ? 1u : 0u);
+        tc_commit(&sfree[as]);
+        tc_commit(&x_free[xsl]);
+        tc_commit(&d_full[as]);
+        if (k == 0) KQ_TRACE_AT(P.trace_id, 3);
+        if (k == nsb / 2) KQ_TRACE_AT(P.trace_id, 10);
+      }
+      KQ_TRACE_AT(P.trace_id, 5);
+      tc_commit(&acc_full);
+    } else if (lane == 0) {
       const uint32_t idesc1 = tc_idesc_f16(TM_ROWS, 2 * Npad), idesc2 = tc_idesc_f16(TM_ROWS, Npad);
       const uint64_t dX = sw128_desc(smem_u32(x_ring));
       for (int i = 0; i < nsub; ++i) {
@@ -546,82 +682,224 @@ __global__ void __launch_bounds__(TM_THREADS, 1) k_tmm(const __grid_constant__ T
     const int qd = warp & 3, hf = warp >> 2, r = 32 * qd + lane;
     const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
     bool ok = true;
-    for (int k = 0; k < nsb && ok; ++k) {
-      const int slot = k % TM_RS;
-      ok = __all_sync(0xffffffffu, tm_wait(&raw_full[slot], (uint32_t)(k / TM_RS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f));
-      if (!ok) break;
-      const uint8_t* rw = raw_ring + slot * TM_RAW_BYTES + r * rstride;
-      // scales of this row for sub-stage h (columns 128h + 64hf + 32m + j):
-      // Q4_K sub-block 4h + 2hf + m: (d*sc, dmin*mn); Q6_K sub-block k = 2hf + m: d*scale for j < 16, j >= 16
-      float ds[2][2][2], dm[2][2];
-      if (q4) {
+    if (ex) {
+      // ---------------- exact form. Per super-block k: the minimum term, the A stage (q * sc for
+      // both halves of this warp's columns), then the read-back of super-block k - 1's buffer
+      // scaled by its d into acc (this thread's row r, token half hf).
+      // The minimum term -sum_b (dmin * mn_b) * xsum[t][b] is computed transposed: warp w takes the
+      // tokens [w tpw, (w + 1) tpw) for the four rows lane + 32 j, so each sum loaded from shared
+      // memory serves four rows (a quarter of the broadcast traffic of one row per thread); the
+      // partial results stay in registers (mterm) and reach their owners once, at the end.
+      const int nc = Npad >> 1, c0 = hf * nc, tpw = Npad >> 3, tw0 = warp * tpw;
+      float acc[32], mterm[4][8];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mterm[j][e] = 0.f;
+      auto read_back = [&](int kb, float dk) -> bool {
+        const int db = kb & 1;
+        if (!__all_sync(0xffffffffu, tm_wait(&d_full[db], (uint32_t)(kb >> 1) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f)))
+          return false;
+        tc_fence_after();
+        const uint32_t td = trow + (uint32_t)db * TM_XD_COLS;
+#pragma unroll
+        for (int cc = 0; cc < 32; cc += 8) {
+          if (cc < nc) {
+            float v[8], u[8];
+            tc_ld8x2(td + (uint32_t)(c0 + cc), td + (uint32_t)(Npad + c0 + cc), v, u);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[cc + e] = __fmaf_rn(dk, __fadd_rn(v[e], u[e]), acc[cc + e]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&d_free[db]);
+        return true;
+      };
+      float dprev = 0.f;
+      for (int k = 0; k < nsb && ok; ++k) {
+        const int slot = k % TM_RS, ss = k % TM_SR, as = k & 1;
+        ok = __all_sync(0xffffffffu, tm_wait(&raw_full[slot], (uint32_t)(k / TM_RS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f));
+        if (!ok) break;
+        const uint8_t* rs = raw_ring + slot * TM_RAW_BYTES;
+        ok = __all_sync(0xffffffffu, tm_wait(&s_full[ss], (uint32_t)(k / TM_SR) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f));
+        if (!ok) break;
+        {
+          float dm[4][8];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 Hj = lds128(rs + (lane + 32 * j) * rstride + 128);
+            const float dmin = h2f_bits(Hj.x >> 16);
+            const uint32_t mlo = Hj.z & 0x3F3F3F3Fu, mhi = ((Hj.w >> 4) & 0x0F0F0F0Fu) | ((Hj.z >> 2) & 0x30303030u);
+#pragma unroll
+            for (int b = 0; b < 8; ++b) dm[j][b] = __fmul_rn(dmin, (float)(((b < 4 ? mlo : mhi) >> (8 * (b & 3))) & 0xFFu));
+          }
+          const float4* xs4 = reinterpret_cast<const float4*>(s_ring + (size_t)ss * 8 * Npad + (size_t)tw0 * 8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (e < tpw) {
+              const float4 xa = xs4[2 * e], xb = xs4[2 * e + 1];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float u = __fmul_rn(dm[j][0], xa.x), w2 = __fmul_rn(dm[j][4], xb.x);
+                u = __fmaf_rn(dm[j][1], xa.y, u); w2 = __fmaf_rn(dm[j][5], xb.y, w2);
+                u = __fmaf_rn(dm[j][2], xa.z, u); w2 = __fmaf_rn(dm[j][6], xb.z, w2);
+                u = __fmaf_rn(dm[j][3], xa.w, u); w2 = __fmaf_rn(dm[j][7], xb.w, w2);
+                mterm[j][e] = __fadd_rn(mterm[j][e], __fadd_rn(u, w2));
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[ss]);
+        // the A stage: this row's scales; both 128-column halves of the super-block
+        const uint8_t* rw = rs + r * rstride;
         const uint4 H = lds128(rw + 128);
-        const float d = h2f_bits(H.x & 0xFFFFu), dmin = h2f_bits(H.x >> 16);
-        const uint32_t sc_lo = H.y & 0x3F3F3F3Fu, mn_lo = H.z & 0x3F3F3F3Fu;
+        const float d = h2f_bits(H.x & 0xFFFFu);
+        const uint32_t sc_lo = H.y & 0x3F3F3F3Fu;
         const uint32_t sc_hi = (H.w & 0x0F0F0F0Fu) | ((H.y >> 2) & 0x30303030u);
-        const uint32_t mn_hi = ((H.w >> 4) & 0x0F0F0F0Fu) | ((H.z >> 2) & 0x30303030u);
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            const int sh = 8 * (2 * hf + m);   // sub-block 4h + 2hf + m: byte 2hf + m of word h
-            ds[h][m][0] = ds[h][m][1] = __fmul_rn(d, (float)(((h ? sc_hi : sc_lo) >> sh) & 0xFFu));
-            dm[h][m] = __fmul_rn(dmin, (float)(((h ? mn_hi : mn_lo) >> sh) & 0xFFu));
-          }
-      } else {
-        const uint4 Sc = lds128(rw + 192);   // [u = 2h + jh][k]
-        const uint32_t dw = d_ring[slot * TM_ROWS + r];
-        const float d = h2f_bits(((r & 7) * G + g0 + k) & 1 ? dw >> 16 : dw & 0xFFFFu);
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            const int sh = 8 * (2 * hf + m);
-            ds[h][m][0] = __fmul_rn(d, (float)(int8_t)(((h ? Sc.z : Sc.x) >> sh) & 0xFFu));
-            ds[h][m][1] = __fmul_rn(d, (float)(int8_t)(((h ? Sc.w : Sc.y) >> sh) & 0xFFu));
-            dm[h][m] = 0.f;
-          }
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int i = 2 * k + h, as = i % AS;
-        if (i >= AS) {
-          ok = __all_sync(0xffffffffu, tm_wait(&sfree[as], (uint32_t)((i / AS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f));
+        if (k >= TM_XAS) {
+          ok = __all_sync(0xffffffffu, tm_wait(&sfree[as], (uint32_t)((k >> 1) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f));
           if (!ok) break;
           tc_fence_after();   // the MMAs that read this stage have completed
         }
-        uint32_t hv[2][16], lv[2][16];
-        if (q4) {
-          // the 32 bytes of (h, c = hf): low nibbles = sub-block 4h + 2hf, high = 4h + 2hf + 1
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          // this warp's 64 columns of half h: sub-blocks 4h + 2hf (low nibbles), 4h + 2hf + 1 (high)
           const uint8_t* b = rw + hf * 64 + h * 32;
           const uint4 W0 = lds128(b), W1 = lds128(b + 16);
-          tm_q4_row32(W0, W1, 0, ds[h][0][0], dm[h][0], hv[0], lv[0]);
-          tm_q4_row32(W0, W1, 4, ds[h][1][0], dm[h][1], hv[1], lv[1]);
-        } else {
-          // sub-block k = 2hf + m of half h: ql chunk c = m, nibble hf, qh shift 2k
-          const uint8_t* hq = rw + 128 + h * 32;
-          const uint4 H0 = lds128(hq), H1 = lds128(hq + 16);
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            const uint8_t* lq = rw + m * 64 + h * 32;
-            tm_q6_row32(lds128(lq), lds128(lq + 16), H0, H1, 4 * hf, 2 * (2 * hf + m), ds[h][m][0], ds[h][m][1], hv[m], lv[m]);
-          }
+          const uint32_t scw = (h ? sc_hi : sc_lo) >> (16 * hf);
+          uint32_t av[2][16];
+          tm_q4_exact32(W0, W1, 0, scw & 0xFFu, av[0]);
+          tm_q4_exact32(W0, W1, 4, (scw >> 8) & 0xFFu, av[1]);
+          const uint32_t ta = trow + TM_XA0 + (uint32_t)as * TM_XASTAGE_COLS + 64u * (uint32_t)h + 32u * (uint32_t)hf;
+          tc_st16(ta, av[0]);
+          tc_st16(ta + 16, av[1]);
         }
-        const uint32_t ta = trow + acol + (uint32_t)as * TM_ASTAGE_COLS + 32u * (uint32_t)hf;
-        tc_st16(ta, hv[0]);
-        tc_st16(ta + 16, hv[1]);
-        tc_st16(ta + 64, lv[0]);
-        tc_st16(ta + 80, lv[1]);
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[as]);
-        if (warp == 0 && lane == 0 && i == 0) KQ_TRACE_AT(P.trace_id, 2);
-        if (warp == 0 && lane == 0 && i == nsub / 2) KQ_TRACE_AT(P.trace_id, 9);
-        if (warp == 0 && lane == 0 && i == nsub - 1) KQ_TRACE_AT(P.trace_id, 4);
+        if (lane == 0) {
+          mbar_arrive(&a_full[as]);
+          mbar_arrive(&raw_empty[slot]);
+        }
+        if (warp == 0 && lane == 0 && k == 0) KQ_TRACE_AT(P.trace_id, 2);
+        if (warp == 0 && lane == 0 && k == nsb / 2) KQ_TRACE_AT(P.trace_id, 9);
+        if (warp == 0 && lane == 0 && k == nsb - 1) KQ_TRACE_AT(P.trace_id, 4);
+        if (k >= 1) ok = read_back(k - 1, dprev);
+        dprev = d;
       }
-      __syncwarp();
-      if (lane == 0 && ok) mbar_arrive(&raw_empty[slot]);
+      if (ok) ok = read_back(nsb - 1, dprev);
+      // the minimum terms to their owners through shared memory (the raw ring, read by nobody now:
+      // every dequantising warp has passed its last super-block, every raw copy has landed)
+      const bool all_ok = named_bar_and(2, TM_DQ_WARPS * 32, ok && !*abort_f);
+      ok = all_ok;
+      if (ok) {
+        float* mbuf = reinterpret_cast<float*>(raw_ring);   // [128][Npad + 1]
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (e < tpw) mbuf[(lane + 32 * j) * (Npad + 1) + tw0 + e] = mterm[j][e];
+        named_bar(2, TM_DQ_WARPS * 32);
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (e < nc) acc[e] = __fsub_rn(acc[e], mbuf[r * (Npad + 1) + c0 + e]);
+        // the results into buffer 0 (read back already): value in column c, 0 in column Npad + c,
+        // the form the shared epilogue reads
+        const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int cc = 0; cc < 32; cc += 8) {
+          if (cc < nc) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = acc[cc + e];
+            tc_st8(trow + (uint32_t)(c0 + cc), v);
+            tc_st8(trow + (uint32_t)(Npad + c0 + cc), z);
+          }
+        }
+        tc_wait_st();
+      }
+    } else {
+      for (int k = 0; k < nsb && ok; ++k) {
+        const int slot = k % TM_RS;
+        ok = __all_sync(0xffffffffu, tm_wait(&raw_full[slot], (uint32_t)(k / TM_RS) & 1, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f));
+        if (!ok) break;
+        const uint8_t* rw = raw_ring + slot * TM_RAW_BYTES + r * rstride;
+        // scales of this row for sub-stage h (columns 128h + 64hf + 32m + j):
+        // Q4_K sub-block 4h + 2hf + m: (d*sc, dmin*mn); Q6_K sub-block k = 2hf + m: d*scale for j < 16, j >= 16
+        float ds[2][2][2], dm[2][2];
+        if (q4) {
+          const uint4 H = lds128(rw + 128);
+          const float d = h2f_bits(H.x & 0xFFFFu), dmin = h2f_bits(H.x >> 16);
+          const uint32_t sc_lo = H.y & 0x3F3F3F3Fu, mn_lo = H.z & 0x3F3F3F3Fu;
+          const uint32_t sc_hi = (H.w & 0x0F0F0F0Fu) | ((H.y >> 2) & 0x30303030u);
+          const uint32_t mn_hi = ((H.w >> 4) & 0x0F0F0F0Fu) | ((H.z >> 2) & 0x30303030u);
+  #pragma unroll
+          for (int h = 0; h < 2; ++h)
+  #pragma unroll
+            for (int m = 0; m < 2; ++m) {
+              const int sh = 8 * (2 * hf + m);   // sub-block 4h + 2hf + m: byte 2hf + m of word h
+              ds[h][m][0] = ds[h][m][1] = __fmul_rn(d, (float)(((h ? sc_hi : sc_lo) >> sh) & 0xFFu));
+              dm[h][m] = __fmul_rn(dmin, (float)(((h ? mn_hi : mn_lo) >> sh) & 0xFFu));
+            }
+        } else {
+          const uint4 Sc = lds128(rw + 192);   // [u = 2h + jh][k]
+          const uint32_t dw = d_ring[slot * TM_ROWS + r];
+          const float d = h2f_bits(((r & 7) * G + g0 + k) & 1 ? dw >> 16 : dw & 0xFFFFu);
+  #pragma unroll
+          for (int h = 0; h < 2; ++h)
+  #pragma unroll
+            for (int m = 0; m < 2; ++m) {
+              const int sh = 8 * (2 * hf + m);
+              ds[h][m][0] = __fmul_rn(d, (float)(int8_t)(((h ? Sc.z : Sc.x) >> sh) & 0xFFu));
+              ds[h][m][1] = __fmul_rn(d, (float)(int8_t)(((h ? Sc.w : Sc.y) >> sh) & 0xFFu));
+              dm[h][m] = 0.f;
+            }
+        }
+  #pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int i = 2 * k + h, as = i % AS;
+          if (i >= AS) {
+            ok = __all_sync(0xffffffffu, tm_wait(&sfree[as], (uint32_t)((i / AS) - 1) & 1, P.err, KQ_DEV_ERR_WAIT_EMPTY, abort_f));
+            if (!ok) break;
+            tc_fence_after();   // the MMAs that read this stage have completed
+          }
+          uint32_t hv[2][16], lv[2][16];
+          if (q4) {
+            // the 32 bytes of (h, c = hf): low nibbles = sub-block 4h + 2hf, high = 4h + 2hf + 1
+            const uint8_t* b = rw + hf * 64 + h * 32;
+            const uint4 W0 = lds128(b), W1 = lds128(b + 16);
+            tm_q4_row32(W0, W1, 0, ds[h][0][0], dm[h][0], hv[0], lv[0]);
+            tm_q4_row32(W0, W1, 4, ds[h][1][0], dm[h][1], hv[1], lv[1]);
+          } else {
+            // sub-block k = 2hf + m of half h: ql chunk c = m, nibble hf, qh shift 2k
+            const uint8_t* hq = rw + 128 + h * 32;
+            const uint4 H0 = lds128(hq), H1 = lds128(hq + 16);
+  #pragma unroll
+            for (int m = 0; m < 2; ++m) {
+              const uint8_t* lq = rw + m * 64 + h * 32;
+              tm_q6_row32(lds128(lq), lds128(lq + 16), H0, H1, 4 * hf, 2 * (2 * hf + m), ds[h][m][0], ds[h][m][1], hv[m], lv[m]);
+            }
+          }
+          const uint32_t ta = trow + acol + (uint32_t)as * TM_ASTAGE_COLS + 32u * (uint32_t)hf;
+          tc_st16(ta, hv[0]);
+          tc_st16(ta + 16, hv[1]);
+          tc_st16(ta + 64, lv[0]);
+          tc_st16(ta + 80, lv[1]);
+          tc_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[as]);
+          if (warp == 0 && lane == 0 && i == 0) KQ_TRACE_AT(P.trace_id, 2);
+          if (warp == 0 && lane == 0 && i == nsub / 2) KQ_TRACE_AT(P.trace_id, 9);
+          if (warp == 0 && lane == 0 && i == nsub - 1) KQ_TRACE_AT(P.trace_id, 4);
+        }
+        __syncwarp();
+        if (lane == 0 && ok) mbar_arrive(&raw_empty[slot]);
+      }
     }
     // ---------------- epilogue (warps 0-7): TMEM lane quarter warp & 3, token half warp >> 2
     if (ok) ok = tm_wait(&acc_full, 0, P.err, KQ_DEV_ERR_WAIT_FULL, abort_f);

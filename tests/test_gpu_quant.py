@@ -179,6 +179,59 @@ def test_matmul_parity(kq, oracle, ty, R, Cc, M):
         assert e < TIGHT_L2, (i, e)
 
 
+# The same products through the split-weight form only (KQ_TMM_EXACT=0): Q4_K row tiles otherwise
+# take the exact form (q * sc in the MMA, d and the minimum term applied outside it).
+@pytest.mark.parametrize("M", [4, 16, 45])
+@pytest.mark.parametrize("ty,R,Cc", [(12, 256, 4096), (12, 200, 1024), (12, 12288, 4096), (14, 1024, 4096)])
+def test_matmul_parity_split_form(kq, oracle, monkeypatch, ty, R, Cc, M):
+    monkeypatch.setenv("KQ_TMM_EXACT", "0")
+    W = oracle.gen_matrix(R, Cc, ty, 0, 300 + R)
+    X = np.stack([oracle.gen_normal(Cc, 0.0, 1.0, 1, 1000 * M + i) for i in range(M)])
+    Y = kq.QMat(ty, R, Cc).upload(W).matmul(X)
+    for i in range(M):
+        assert rel_l2(Y[i], oracle.matvec(W, R, Cc, ty, X[i])) < TIGHT_L2, i
+
+
+@pytest.mark.parametrize("form", ["0", "1"])
+@pytest.mark.parametrize("qbyte,sign", [(0x00, 1.0), (0xFF, -1.0), (0xFF, 1.0), (0x0F, 1.0)])
+def test_matmul_q4k_extreme_magnitudes(kq, oracle, monkeypatch, qbyte, sign, form):
+    """Q4_K blocks at the ends of every range: every scale and minimum 63, nibbles 0 or 15 (or 15
+    and 0), large d and dmin, activations all +-127 over 8 tokens: q * sc = 945 is the largest A
+    value of the exact form; both forms against the oracle."""
+    monkeypatch.setenv("KQ_TMM_EXACT", form)
+    R, Cc, M = 256, 4096, 8
+    blk = np.zeros(144, np.uint8)
+    blk[0:2] = np.frombuffer(np.float16(30.0).tobytes(), np.uint8)      # d
+    blk[2:4] = np.frombuffer(np.float16(7.5).tobytes(), np.uint8)       # dmin
+    blk[4:16] = 0xFF                                                    # scales, minimums: 63
+    blk[16:144] = qbyte
+    W = np.tile(blk, R * (Cc // 256))
+    X = np.stack([np.full(Cc, 127.0 * sign * (1 + (i % 3)), np.float32) for i in range(M)])
+    Y = kq.QMat(12, R, Cc).upload(W).matmul(X)
+    for i in range(M):
+        ref = oracle.matvec(W, R, Cc, 12, X[i])
+        assert np.isfinite(ref).all()
+        assert rel_l2(Y[i], ref) < RTOL_L2, i   # identical addends: the oracle's fp32 sums drift
+
+
+def test_matmul_edge_activations_exact_form(kq, oracle):
+    """Zero rows, tiny and huge-range rows, a row with an infinity, in one Q4_K batch: the range
+    scaling and the sub-block sums see the same packed values."""
+    R, Cc = 384, 4096
+    W = oracle.gen_matrix(R, Cc, 12, 0, 21)
+    X = np.stack([oracle.gen_normal(Cc, 0.0, 1.0, 1, 400 + i) for i in range(5)])
+    X[0] = 0.0
+    X[1, :256] *= 1e-30
+    X[1, 256:1024] *= 1e20
+    X[2] *= 1e-6
+    X[3, 3000] = np.inf
+    Y = kq.QMat(12, R, Cc).upload(W).matmul(X)
+    assert np.array_equal(Y[0], oracle.matvec(W, R, Cc, 12, X[0]))
+    for i in (1, 2, 4):
+        assert rel_l2(Y[i], oracle.matvec(W, R, Cc, 12, X[i])) < TIGHT_L2, i
+    assert not np.isfinite(Y[3]).all()
+
+
 def test_matmul_rows_independent_of_batch(kq, oracle):
     """Each token's row depends only on its own activations: the same x gives the same products
     whatever the other tokens of the batch are (the MMA N dimension only carries tokens)."""
