@@ -8,7 +8,8 @@
 // the argmax (lowest id on ties). It generalises the reference's one-hot-draft chain acceptance
 // (scripts/kindi_q4/kindi/spec.py:769-787) to draft distributions and trees.
 //
-// Exactness: one CTA of 1024 threads. e^t is kq_exp (Cody-Waite reduction, Taylor degree 7, the
+// Exactness (k_accept: one CTA of 1024 threads; k_accept_grid below: the same arithmetic over a
+// cooperative grid). e^t is kq_exp (Cody-Waite reduction, Taylor degree 7, the
 // same fp32 operations as the oracle); vocabulary sums are blocked exactly as in the oracle:
 // blocks of 1024 consecutive ids, each block summed as a balanced pairwise tree (over the 32 ids
 // of a row, then over the 32 rows; acc_blocked_sum says how one warp forms it), the block sums
@@ -20,6 +21,7 @@
 #pragma once
 #include "kq_common.cuh"
 #include <cfloat>
+#include <cstddef>
 
 namespace kq {
 
@@ -58,6 +60,7 @@ struct AcceptParams {
   int* path;             // out: [n + 1] accepted nodes (path[0] = 0)
   int* out;              // out: [n + 1] emitted tokens
   int* count;            // out: [2] emitted tokens, path length
+  int* err;              // device error word (the multi-CTA form's grid-barrier waits)
 };
 
 struct AccShared {
@@ -309,6 +312,290 @@ __global__ void __launch_bounds__(ACC_THREADS, 1) k_accept(const AcceptParams A)
   if (tid == 0) {
     A.count[0] = no;
     A.count[1] = np;
+  }
+}
+
+// ------------------------------------------------------------------------------ multi-CTA form
+// The same rule with the same arithmetic over a cooperative grid: CTA c owns the 1024-id blocks c
+// and c + gridDim.x (gridDim.x = ceil(blocks / 2)), one id per thread per block, and keeps its p
+// and q values in registers. Everything elementwise stays in the CTA; a vocabulary-wide result
+// (the argmax, a blocked sum, an acceptance decision, the inverse-CDF pick) goes through global
+// memory and a software grid barrier, after which every CTA forms it the same way: the block sums
+// are each formed by one warp exactly as acc_blocked_sum forms them and added in block order by
+// one thread of every CTA; the argmax keeps the lowest id among equal values; the inverse CDF
+// takes, of the blocks whose in-order prefix plus sum exceeds the target, the first whose
+// one-thread scan finds the id. So every result is bit-identical to k_accept's. The exchange
+// arrays alternate between two halves by barrier parity: a CTA that runs ahead writes the half
+// that no other CTA can still be reading. Barrier waits are bounded (KQ_DEV_ERR_GRID).
+constexpr uint32_t ACC_GRID_WAIT_LIMIT = 1u << 22;   // acquire polls (~seconds) before giving up
+struct AccGridScratch {
+  unsigned bar;          // barrier arrivals (cleared by the host before each launch)
+  unsigned pick;         // inverse-CDF pick: the smallest found id (host: 0xFFFFFFFF)
+  int hi;                // fallback: the largest id with p > 0 (host: -1)
+  int decision[2];       // acceptance decision of the current child, by barrier parity
+  float bs[2][ACC_MAX_BLOCKS];
+  float val[2][ACC_MAX_BLOCKS];
+  int idx[2][ACC_MAX_BLOCKS];
+};
+static_assert(offsetof(AccGridScratch, hi) == offsetof(AccGridScratch, pick) + sizeof(unsigned),
+              "pick and hi are cleared by one host memset");
+struct AccGridShared {
+  float blk[2][ACC_BLK];   // this CTA's blocks of the last blocked sum
+  float sbs[ACC_MAX_BLOCKS];   // the grid's block sums / per-CTA maxima, staged by all threads at
+  float sval[ACC_MAX_BLOCKS];  // once (one L2 round trip) before one thread combines them in order
+  int sidx[ACC_MAX_BLOCKS];
+  float wval[32];
+  int widx[32];
+  float S, bv;
+  int bi, fail;
+};
+__device__ __forceinline__ unsigned acc_ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Grid barrier number gen (1, 2, ...); false when this CTA's wait gave up (or another CTA's did).
+__device__ bool acc_grid_sync(AccGridScratch* G, unsigned gen, int* err, AccGridShared& sh) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(&G->bar, 1u);
+    const unsigned target = gen * gridDim.x;
+    for (uint32_t it = 0; acc_ld_acquire(&G->bar) < target; ++it) {
+      if (it > ACC_GRID_WAIT_LIMIT || ((it & 1023) == 1023 && (*(volatile int*)err & KQ_DEV_ERR_GRID))) {
+        atomicOr(err, KQ_DEV_ERR_GRID);
+        sh.fail = 1;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return !sh.fail;
+}
+
+__global__ void __launch_bounds__(ACC_THREADS, 1) k_accept_grid(const AcceptParams A, AccGridScratch* G) {
+  __shared__ AccGridShared sh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, V = A.V, n = A.n;
+  const int nb = (V + ACC_BLK - 1) / ACC_BLK, NC = gridDim.x, cta = blockIdx.x;
+  const int nown = cta + NC < nb ? 2 : 1;   // this CTA's blocks: cta, cta + NC
+  if (tid == 0) sh.fail = 0;
+  __syncthreads();
+  unsigned gen = 0;
+  int idk[2];
+#pragma unroll
+  for (int kb = 0; kb < 2; ++kb) idk[kb] = kb < nown ? (cta + kb * NC) * ACC_BLK + tid : V;   // V: no id
+
+  // the argmax of a row over the vocabulary (lowest id among equal values), to every thread
+  auto argmax = [&](const float* row, float& best, int& bidx) -> bool {
+    float v = -INFINITY;
+    int vi = 0x7fffffff;
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+      if (idk[kb] < V) {
+        const float x = row[idk[kb]];
+        if (x > v || (x == v && idk[kb] < vi)) { v = x; vi = idk[kb]; }
+      }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, vi, off);
+      if (ov > v || (ov == v && oi < vi)) { v = ov; vi = oi; }
+    }
+    if (lane == 0) { sh.wval[warp] = v; sh.widx[warp] = vi; }
+    __syncthreads();
+    const int par = (gen + 1) & 1;
+    if (tid == 0) {
+      float bv = sh.wval[0];
+      int bi = sh.widx[0];
+      for (int w = 1; w < 32; ++w)
+        if (sh.wval[w] > bv || (sh.wval[w] == bv && sh.widx[w] < bi)) { bv = sh.wval[w]; bi = sh.widx[w]; }
+      G->val[par][cta] = bv;
+      G->idx[par][cta] = bi;
+    }
+    if (!acc_grid_sync(G, ++gen, A.err, sh)) return false;
+    for (int c = tid; c < NC; c += ACC_THREADS) {
+      sh.sval[c] = __ldcg(&G->val[par][c]);
+      sh.sidx[c] = __ldcg(&G->idx[par][c]);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float bv = sh.sval[0];
+      int bi = sh.sidx[0];
+      for (int c = 1; c < NC; ++c) {
+        const float cv = sh.sval[c];
+        const int ci = sh.sidx[c];
+        if (cv > bv || (cv == bv && ci < bi)) { bv = cv; bi = ci; }
+      }
+      sh.bv = bv;
+      sh.bi = bi;
+    }
+    __syncthreads();
+    best = sh.bv;
+    bidx = sh.bi == 0x7fffffff ? 0 : sh.bi;
+    __syncthreads();
+    return true;
+  };
+  // the in-order total of the block sums of w (acc_blocked_sum's form); sh.blk keeps this CTA's
+  // blocks and sh.sbs all block sums until the next call
+  auto blocksum = [&](const float (&w)[2], float& S) -> bool {
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+      if (kb < nown) sh.blk[kb][tid] = idk[kb] < V ? w[kb] : 0.0f;
+    __syncthreads();
+    const int par = (gen + 1) & 1;
+    if (warp < nown) {
+      float x[32];
+#pragma unroll
+      for (int r = 0; r < 32; ++r) x[r] = sh.blk[warp][r * 32 + lane];
+#pragma unroll
+      for (int k = 0; k < 5; ++k) {
+        const int m = 16 >> k;
+        const bool keep_hi = (lane >> k) & 1;
+#pragma unroll
+        for (int i = 0; i < m; ++i) {
+          const float send = keep_hi ? x[i] : x[i + m];
+          const float kept = keep_hi ? x[i + m] : x[i];
+          x[i] = __fadd_rn(kept, __shfl_xor_sync(0xffffffffu, send, 1 << k));
+        }
+      }
+      float t = x[0];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, off));
+      if (lane == 0) G->bs[par][cta + warp * NC] = t;
+    }
+    if (!acc_grid_sync(G, ++gen, A.err, sh)) return false;
+    for (int b = tid; b < nb; b += ACC_THREADS) sh.sbs[b] = __ldcg(&G->bs[par][b]);
+    __syncthreads();
+    if (tid == 0) {
+      float tot = 0.0f;
+      for (int b = 0; b < nb; ++b) tot = __fadd_rn(tot, sh.sbs[b]);
+      sh.S = tot;
+    }
+    __syncthreads();
+    S = sh.S;
+    __syncthreads();
+    return true;
+  };
+  // p = softmax(row * tau) on this CTA's ids
+  auto softmax = [&](const float* row, float tau, float (&p)[2]) -> bool {
+    float mx;
+    int mi;
+    if (!argmax(row, mx, mi)) return false;
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb) p[kb] = idk[kb] < V ? kq_exp(__fmul_rn(__fsub_rn(row[idk[kb]], mx), tau)) : 0.0f;
+    float S;
+    if (!blocksum(p, S)) return false;
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+      if (idk[kb] < V) p[kb] = __fdiv_rn(p[kb], S);
+    return true;
+  };
+
+  float pv[2] = {0.0f, 0.0f}, qv[2] = {0.0f, 0.0f};
+  const bool writer = cta == 0 && tid == 0;
+  int v = 0, np = 0, no = 0;
+  if (writer) A.path[np] = 0;
+  ++np;
+  bool ok = true;
+  for (int guard = 0; guard <= n && ok; ++guard) {
+    const float* zv = A.z + (size_t)v * V;
+    int acc = -1;
+    if (A.tau == 0.0f) {
+      float bv;
+      int best;
+      if (!(ok = argmax(zv, bv, best))) break;
+      for (int c = v + 1; c < n && acc < 0; ++c)
+        if (A.parents[c] == v && A.tokens[c] == best) acc = c;
+      if (acc < 0) {
+        if (writer) A.out[no] = best;
+        ++no;
+        break;
+      }
+    } else {
+      if (!(ok = softmax(zv, A.tau, pv))) break;
+      bool first = true;
+      for (int c = v + 1; c < n && acc < 0; ++c) {
+        if (A.parents[c] != v) continue;
+        if (first) {
+          if (!(ok = softmax(A.g + (size_t)v * V, 1.0f, qv))) break;
+          first = false;
+        }
+        // the owner of id d decides, the grid reads its decision
+        const int d = A.tokens[c], bd = d / ACC_BLK, par = (gen + 1) & 1;
+        if (bd % NC == cta && tid == d % ACC_BLK) {
+          const int kb = bd / NC;
+          G->decision[par] = __fmul_rn(A.u_acc[c], qv[kb]) < pv[kb] ? 1 : 0;
+        }
+        if (!(ok = acc_grid_sync(G, ++gen, A.err, sh))) break;
+        if (__ldcg(&G->decision[par])) { acc = c; break; }
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+          if (idk[kb] < V) {
+            const float r = __fsub_rn(pv[kb], qv[kb]);
+            pv[kb] = r > 0.0f ? r : 0.0f;
+          }
+        float R;
+        if (!(ok = blocksum(pv, R))) break;
+        if (R > 0.0f) {
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb)
+            if (idk[kb] < V) pv[kb] = __fdiv_rn(pv[kb], R);
+        } else if (!(ok = softmax(zv, A.tau, pv))) {   // empty residual (p == q): back to p_v
+          break;
+        }
+      }
+      if (!ok) break;
+      if (acc < 0) {
+        // inverse CDF of p at u_fin[v]: the first block (in order) whose prefix + sum exceeds the
+        // target and whose scan from the prefix finds the id; none: the largest id with p > 0
+        float W;
+        if (!(ok = blocksum(pv, W))) break;
+        const float target = __fmul_rn(A.u_fin[v], W);
+        if (tid == 0) {
+          for (int kb = 0; kb < nown; ++kb) {
+            const int b = cta + kb * NC;
+            float prefix = 0.0f;
+            for (int b2 = 0; b2 < b; ++b2) prefix = __fadd_rn(prefix, sh.sbs[b2]);
+            if (__fadd_rn(prefix, sh.sbs[b]) > target) {
+              float run = prefix;
+              for (int i = b * ACC_BLK; i < V && i < (b + 1) * ACC_BLK; ++i) {
+                run = __fadd_rn(run, sh.blk[kb][i - b * ACC_BLK]);
+                if (run > target) { atomicMin(&G->pick, (unsigned)i); break; }
+              }
+            }
+          }
+        }
+        if (!(ok = acc_grid_sync(G, ++gen, A.err, sh))) break;
+        const unsigned pk = __ldcg(&G->pick);
+        int pick = (int)pk;
+        if (pk == 0xFFFFFFFFu) {
+          int hi = -1;
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb)
+            if (idk[kb] < V && pv[kb] > 0.0f) hi = max(hi, idk[kb]);
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, off));
+          if (lane == 0 && hi >= 0) atomicMax(&G->hi, hi);
+          if (!(ok = acc_grid_sync(G, ++gen, A.err, sh))) break;
+          const int h = __ldcg(&G->hi);
+          pick = h < 0 ? 0 : h;
+        }
+        if (writer) A.out[no] = pick;
+        ++no;
+        break;
+      }
+    }
+    if (writer) {
+      A.out[no] = A.tokens[acc];
+      A.path[np] = acc;
+    }
+    ++no;
+    ++np;
+    v = acc;
+  }
+  if (writer) {
+    A.count[0] = ok ? no : 0;
+    A.count[1] = ok ? np : 0;
   }
 }
 

@@ -652,6 +652,7 @@ struct kq_model {
   DecodeState* vstates = nullptr;   // pinned, one per node
   float *ap = nullptr, *aq = nullptr, *ag = nullptr;   // acceptance scratch, draft logits
   int *atok = nullptr, *apar = nullptr, *apath = nullptr, *aout = nullptr, *acnt = nullptr;
+  AccGridScratch* agrid = nullptr;   // the multi-CTA acceptance's exchange area
   float *auacc = nullptr, *aufin = nullptr;
   __half** caches = nullptr;        // [2 * n_layers] K/V cache pointers (compaction)
   // batched verification pass (up to MM_MAXM tokens at once)
@@ -1885,6 +1886,7 @@ static int verify_buffers(kq_model* m) {
   m->apath = dalloc<int>(m, KQ_MAX_TREE + 1, ok);
   m->aout = dalloc<int>(m, KQ_MAX_TREE + 1, ok);
   m->acnt = dalloc<int>(m, 2, ok);
+  m->agrid = dalloc<AccGridScratch>(m, 1, ok);
   m->auacc = dalloc<float>(m, KQ_MAX_TREE, ok);
   m->aufin = dalloc<float>(m, KQ_MAX_TREE, ok);
   m->caches = dalloc<__half*>(m, 2 * (size_t)m->c.n_layers, ok);
@@ -2258,7 +2260,23 @@ static int accept_impl(kq_model* m, const int32_t* tokens, const int32_t* parent
   }
   A.z = m->vlogits; A.g = m->ag; A.tokens = m->atok; A.parents = m->apar; A.u_acc = m->auacc; A.u_fin = m->aufin;
   A.n = n; A.V = (int)V; A.p = m->ap; A.q = m->aq; A.path = m->apath; A.out = m->aout; A.count = m->acnt;
-  k_accept<<<1, ACC_THREADS, 0, s>>>(A);
+  A.err = m->err;
+  // the multi-CTA form (a cooperative grid of ceil(blocks / 2) CTAs) unless KQ_ACCEPT_GRID=0 asks
+  // for the one-CTA kernel (comparison) or the grid cannot be co-resident
+  const int nbk = (int)((V + ACC_BLK - 1) / ACC_BLK), nc = (nbk + 1) / 2;
+  const char* eg = std::getenv("KQ_ACCEPT_GRID");
+  int coop = 0, per_sm = 0;
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device);
+  if (coop) CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_accept_grid, ACC_THREADS, 0));
+  if (!(eg && std::atoi(eg) == 0) && coop && nc <= per_sm * m->nsm) {
+    CU(cudaMemsetAsync(&m->agrid->bar, 0, sizeof(unsigned), s));
+    CU(cudaMemsetAsync(&m->agrid->pick, 0xFF, sizeof(unsigned) + sizeof(int), s));   // pick, hi
+    AccGridScratch* G = m->agrid;
+    void* args[] = {(void*)&A, (void*)&G};
+    CU(cudaLaunchCooperativeKernel((const void*)k_accept_grid, dim3((unsigned)nc), dim3(ACC_THREADS), args, 0, s));
+  } else {
+    k_accept<<<1, ACC_THREADS, 0, s>>>(A);
+  }
   CU(cudaGetLastError());
   int cnt[2] = {0, 0};
   CU(cudaMemcpyAsync(cnt, m->acnt, sizeof(cnt), cudaMemcpyDeviceToHost, s));

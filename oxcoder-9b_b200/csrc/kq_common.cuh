@@ -17,6 +17,7 @@ enum : int {
   KQ_DEV_ERR_DRAIN = 4,         // copies still in flight at exit after a failure
   KQ_DEV_ERR_BAD_TOKEN = 8,     // a token id outside [0, vocab) reached a kernel
   KQ_DEV_ERR_BAD_POS = 16,      // a position outside [0, ctx) reached a kernel
+  KQ_DEV_ERR_GRID = 32,         // a software grid-barrier wait gave up
 };
 
 // Polls of mbarrier.try_wait before giving up. Each poll may suspend the thread for a

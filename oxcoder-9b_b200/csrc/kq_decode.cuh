@@ -42,7 +42,6 @@ static_assert(DEC_CONSUMERS * DEC_REGS_CONSUMER + 128 * DEC_REGS_PRODUCER <= DEC
 constexpr int DEC_CWARPS = DEC_CONSUMERS / 32;
 constexpr int DEC_BAR_ATTN = 12, DEC_BAR_PHASE = 13;        // named barriers (ids 1..8: GEMV rows)
 constexpr uint32_t DEC_GRID_WAIT_LIMIT = 1u << 24;          // polls (~seconds) before giving up
-constexpr int KQ_DEV_ERR_GRID = 32;                         // a grid-barrier wait gave up
 constexpr int DEC_NB = 16;                                  // stages in flight (mbarrier pairs)
 constexpr int DEC_NDESC = 4;                                // phase descriptors cached in shared memory
 

@@ -98,9 +98,11 @@ def test_chain_verify_reproduces_greedy_steps(kq, monkeypatch, seq):
             assert best[i] == chain[i + 1]
 
 
+@pytest.mark.parametrize("form", ["1", "0"])   # KQ_ACCEPT_GRID: the cooperative multi-CTA kernel, the one-CTA kernel
 @pytest.mark.parametrize("temperature", [0.0, 0.7, 1.3])
 @pytest.mark.parametrize("branching,seed", [([4, 2, 2, 1], 1), ([2, 2, 2], 2), ([1] * 8, 3), ([], 4)])
-def test_accept_bit_exact_with_oracle(kq, oracle, temperature, branching, seed):
+def test_accept_bit_exact_with_oracle(kq, oracle, monkeypatch, temperature, branching, seed, form):
+    monkeypatch.setenv("KQ_ACCEPT_GRID", form)
     e = kq.Engine(kq_cfg(kq, TINY), seed=0)
     rng = np.random.default_rng(100 + seed)
     npos = 60
