@@ -2281,7 +2281,12 @@ static int accept_impl(kq_model* m, const int32_t* tokens, const int32_t* parent
   int cnt[2] = {0, 0};
   CU(cudaMemcpyAsync(cnt, m->acnt, sizeof(cnt), cudaMemcpyDeviceToHost, s));
   CU(cudaStreamSynchronize(s));
-  if (cnt[0] < 1 || cnt[0] > n + 1 || cnt[1] < 1 || cnt[1] > n) return set_err(KQ_ERR_BACKEND, "acceptance kernel failed");
+  if (cnt[0] < 1 || cnt[0] > n + 1 || cnt[1] < 1 || cnt[1] > n) {
+    // a grid-barrier wait of the multi-CTA form that gave up is reported (and the error word
+    // cleared) here rather than by the next call
+    const int rc2 = check_dev_err(m);
+    return rc2 ? rc2 : set_err(KQ_ERR_BACKEND, "acceptance kernel failed");
+  }
   CU(cudaMemcpy(out, m->aout, cnt[0] * sizeof(int32_t), cudaMemcpyDeviceToHost));
   CU(cudaMemcpy(path, m->apath, cnt[1] * sizeof(int32_t), cudaMemcpyDeviceToHost));
   if (path_len) *path_len = cnt[1];
