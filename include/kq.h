@@ -233,6 +233,29 @@ size_t kq_qmat_bytes(const kq_qmat* a);
 #define KQ_NOALLOC_MAX_ROWS 262144
 int kq_qmat_argmax_noalloc(kq_qmat* a, const float* x_dev, int32_t* idx_dev, void* stream);
 
+/* ------------------------------------------------------------------ prompt-lookup drafter
+ * Replaces NgramDraft (scripts/kindi_q4/kindi/spec.py:801-841): the tokens that followed the
+ * latest earlier occurrence of the longest matching suffix of the history, suffix lengths
+ * nmax .. nmin; -1 marks an unknown token (a suffix holding one is skipped, a continuation holding
+ * one gives no proposal). Host-side only (no GPU). A proposal of k tokens is a draft chain for
+ * kq_verify: tokens [last, d0, .., d(k-1)], parents [-1, 0, .., k-1].
+ *  kq_ngram_create    nmax >= nmin >= 1, nmax <= 64 (NgramDraft(nmax=4, nmin=1) by default there);
+ *                     null (kq_error) on bad sizes
+ *  kq_ngram_reset     NgramDraft.reset(hist): the history is replaced by hist[0..n)
+ *  kq_ngram_push      NgramDraft.push(t)
+ *  kq_ngram_truncate  NgramDraft.truncate(L): drop positions >= L (L >= 0)
+ *  kq_ngram_propose   NgramDraft.propose(k): writes up to k tokens to out and returns how many
+ *                     (k >= 0), or a negative KQ_ERR_* code
+ *  kq_ngram_length    tokens in the history */
+typedef struct kq_ngram kq_ngram;
+kq_ngram* kq_ngram_create(int nmax, int nmin);
+void kq_ngram_free(kq_ngram* d);
+int kq_ngram_reset(kq_ngram* d, const int32_t* hist, int n);
+int kq_ngram_push(kq_ngram* d, int32_t tok);
+int kq_ngram_truncate(kq_ngram* d, int L);
+int kq_ngram_propose(kq_ngram* d, int k, int32_t* out);
+int kq_ngram_length(const kq_ngram* d);
+
 #ifdef __cplusplus
 }
 #endif

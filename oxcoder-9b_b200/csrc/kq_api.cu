@@ -14,6 +14,7 @@
 #include "kq_decode.cuh"
 #include "kq_accept.cuh"
 #include "kq_batch.cuh"
+#include "kq_ngram.h"
 #include "kq_tmv.cuh"
 #include "kq_nccl.h"
 #include "kq_pack.h"
@@ -2836,3 +2837,50 @@ extern "C" int kq_qmat_argmax_noalloc(kq_qmat* a, const float* x_dev, int32_t* i
   CU(launch_gemv(p, pl, (cudaStream_t)stream, false));
   return KQ_OK;
 }
+
+// ------------------------------------------------------------------------------ prompt-lookup drafter
+struct kq_ngram {
+  kq::NgramIndex ix;
+  kq_ngram(int nmax, int nmin) : ix(nmax, nmin) {}
+};
+extern "C" kq_ngram* kq_ngram_create(int nmax, int nmin) {
+  if (nmin < 1 || nmax < nmin || nmax > 64) {
+    set_err(KQ_ERR_ARG, "n-gram sizes must satisfy 1 <= nmin <= nmax <= 64");
+    return nullptr;
+  }
+  try {
+    return new kq_ngram(nmax, nmin);
+  } catch (...) {
+    set_err(KQ_ERR_MEMORY, "n-gram drafter");
+    return nullptr;
+  }
+}
+extern "C" void kq_ngram_free(kq_ngram* d) { delete d; }
+extern "C" int kq_ngram_reset(kq_ngram* d, const int32_t* hist, int n) {
+  if (!d || n < 0 || (n > 0 && !hist)) return set_err(KQ_ERR_ARG, "bad n-gram history");
+  try {
+    d->ix.reset(hist, n);
+  } catch (...) {
+    return set_err(KQ_ERR_MEMORY, "n-gram drafter");
+  }
+  return KQ_OK;
+}
+extern "C" int kq_ngram_push(kq_ngram* d, int32_t tok) {
+  if (!d) return set_err(KQ_ERR_ARG, "null n-gram drafter");
+  try {
+    d->ix.push(tok);
+  } catch (...) {
+    return set_err(KQ_ERR_MEMORY, "n-gram drafter");
+  }
+  return KQ_OK;
+}
+extern "C" int kq_ngram_truncate(kq_ngram* d, int L) {
+  if (!d || L < 0) return set_err(KQ_ERR_ARG, "bad n-gram truncation");
+  d->ix.truncate(L);
+  return KQ_OK;
+}
+extern "C" int kq_ngram_propose(kq_ngram* d, int k, int32_t* out) {
+  if (!d || k < 0 || (k > 0 && !out)) return set_err(KQ_ERR_ARG, "bad n-gram proposal arguments");
+  return d->ix.propose(k, out);
+}
+extern "C" int kq_ngram_length(const kq_ngram* d) { return d ? d->ix.length() : 0; }

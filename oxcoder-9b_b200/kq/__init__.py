@@ -100,6 +100,13 @@ SIGNATURES = {
     "kq_draft_logits": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_int)]),
     "kq_draft_upload": (C.c_int, [C.c_void_p, PF, C.c_int]),
     "kq_commit": (C.c_int, [C.c_void_p, PI32, C.c_int, C.c_int]),
+    "kq_ngram_create": (C.c_void_p, [C.c_int, C.c_int]),
+    "kq_ngram_free": (None, [C.c_void_p]),
+    "kq_ngram_reset": (C.c_int, [C.c_void_p, PI32, C.c_int]),
+    "kq_ngram_push": (C.c_int, [C.c_void_p, C.c_int32]),
+    "kq_ngram_truncate": (C.c_int, [C.c_void_p, C.c_int]),
+    "kq_ngram_propose": (C.c_int, [C.c_void_p, C.c_int, PI32]),
+    "kq_ngram_length": (C.c_int, [C.c_void_p]),
 }
 
 _lib = None
@@ -457,6 +464,51 @@ class Engine(object):
         out = np.empty(self.config.dim, np.float32)
         check(lib().kq_hidden(self.h, _ptr(out)))
         return out
+
+
+# ----------------------------------------------------------------------------- drafter
+class NgramDraft(object):
+    """The library's prompt-lookup drafter (kq_ngram_*) behind the interface of the reference's
+    NgramDraft (scripts/kindi_q4/kindi/spec.py:801-841): reset(hist), truncate(L), push(t) and
+    propose(k) -> up to k token ids that followed the latest earlier occurrence of the longest
+    matching suffix (lengths nmax .. nmin). Host-side; no GPU. Negative L or k raise ValueError
+    (the reference would apply Python's slice rules to them)."""
+
+    def __init__(self, nmax=4, nmin=1):
+        self.nmax, self.nmin = nmax, nmin
+        self._d = lib().kq_ngram_create(int(nmax), int(nmin))
+        if not self._d:
+            raise ValueError(last_error())
+
+    def close(self):
+        if getattr(self, "_d", None):
+            lib().kq_ngram_free(self._d)
+            self._d = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self, hist):
+        h = np.ascontiguousarray(np.asarray(hist, dtype=np.int64).astype(np.int32))
+        check(lib().kq_ngram_reset(self._d, _ptr(h, PI32), int(h.size)))
+
+    def truncate(self, L):
+        check(lib().kq_ngram_truncate(self._d, int(L)))
+
+    def push(self, t):
+        check(lib().kq_ngram_push(self._d, int(t)))
+
+    def propose(self, k):
+        k = int(k)
+        out = np.empty(max(k, 1), np.int32)
+        n = check(lib().kq_ngram_propose(self._d, k, _ptr(out, PI32)))
+        return [int(v) for v in out[:n]]
+
+    def __len__(self):
+        return lib().kq_ngram_length(self._d)
 
 
 def read_pack_config(pack, ctx=4096):
