@@ -316,3 +316,34 @@ def ref_dequant(Wpack, R, Cc, ty, row):
     y = np.empty(Cc, np.float32)
     L.kc_dequant(C.byref(m), row, ptr(y))
     return y
+
+
+_ref_ffn = None
+
+
+def ref_ffn_lib():
+    """oracle/_ref/libkcpu4_ffn.so (ref_ffn.c over the reference's own kcpu4.c), or None."""
+    global _ref_ffn
+    if _ref_ffn is None:
+        path = os.path.join(HERE, "_ref", "libkcpu4_ffn.so")
+        if not os.path.exists(path):
+            return None
+        L = C.CDLL(path)
+        L.ref_ffn_block.restype = C.c_int
+        L.ref_ffn_block.argtypes = [PU8, PU8, PU8, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, PF, PF, PF]
+        _ref_ffn = L
+    return _ref_ffn
+
+
+def ref_ffn_block(Wg, Wu, Wd, types, D, NFF, norm, x):
+    """The reference's MLP block (kcpu4.c:287-295 ffn) on GGUF row-major weights (converted to the
+    Kindi pack layout it reads), one token x [D] -> y [D]."""
+    tg, tu, td = types
+    pg, pu, pd = (to_pack_layout(Wg, NFF, D, tg), to_pack_layout(Wu, NFF, D, tu), to_pack_layout(Wd, D, NFF, td))
+    norm = np.ascontiguousarray(norm, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty(D, np.float32)
+    rc = ref_ffn_lib().ref_ffn_block(ptr(pg, PU8), ptr(pu, PU8), ptr(pd, PU8), tg, tu, td, D, NFF, ptr(norm), ptr(x), ptr(y))
+    if rc:
+        raise MemoryError("ref_ffn_block scratch")
+    return y
