@@ -318,21 +318,23 @@ def ref_dequant(Wpack, R, Cc, ty, row):
     return y
 
 
-_ref_ffn = None
+_ref_blocks = None
 
 
-def ref_ffn_lib():
-    """oracle/_ref/libkcpu4_ffn.so (ref_ffn.c over the reference's own kcpu4.c), or None."""
-    global _ref_ffn
-    if _ref_ffn is None:
-        path = os.path.join(HERE, "_ref", "libkcpu4_ffn.so")
+def ref_blocks_lib():
+    """oracle/_ref/libkcpu4_blocks.so (ref_blocks.c over the reference's own kcpu4.c), or None."""
+    global _ref_blocks
+    if _ref_blocks is None:
+        path = os.path.join(HERE, "_ref", "libkcpu4_blocks.so")
         if not os.path.exists(path):
             return None
         L = C.CDLL(path)
         L.ref_ffn_block.restype = C.c_int
         L.ref_ffn_block.argtypes = [PU8, PU8, PU8, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, PF, PF, PF]
-        _ref_ffn = L
-    return _ref_ffn
+        L.ref_head_step.restype = C.c_int
+        L.ref_head_step.argtypes = [PU8, C.c_int, PU8, C.c_int, C.c_int, C.c_int, PF, C.c_int, PF]
+        _ref_blocks = L
+    return _ref_blocks
 
 
 def ref_ffn_block(Wg, Wu, Wd, types, D, NFF, norm, x):
@@ -343,7 +345,20 @@ def ref_ffn_block(Wg, Wu, Wd, types, D, NFF, norm, x):
     norm = np.ascontiguousarray(norm, np.float32)
     x = np.ascontiguousarray(x, np.float32)
     y = np.empty(D, np.float32)
-    rc = ref_ffn_lib().ref_ffn_block(ptr(pg, PU8), ptr(pu, PU8), ptr(pd, PU8), tg, tu, td, D, NFF, ptr(norm), ptr(x), ptr(y))
+    rc = ref_blocks_lib().ref_ffn_block(ptr(pg, PU8), ptr(pu, PU8), ptr(pd, PU8), tg, tu, td, D, NFF, ptr(norm), ptr(x), ptr(y))
     if rc:
         raise MemoryError("ref_ffn_block scratch")
     return y
+
+
+def ref_head_step(Wemb, t_emb, Whead, t_head, D, V, out_norm, tok):
+    """The reference's kc_step on a model of no layers (embedding row, final norm, head GEMV,
+    argmax): (best token, logits [V]); weights GGUF row-major, converted to the pack layout."""
+    pe, ph = to_pack_layout(Wemb, V, D, t_emb), to_pack_layout(Whead, V, D, t_head)
+    out_norm = np.ascontiguousarray(out_norm, np.float32)
+    logits = np.empty(V, np.float32)
+    best = ref_blocks_lib().ref_head_step(ptr(pe, PU8), t_emb, ptr(ph, PU8), t_head, D, V, ptr(out_norm), int(tok),
+                                          ptr(logits))
+    if best < 0:
+        raise RuntimeError("ref_head_step failed (%d)" % best)
+    return best, logits

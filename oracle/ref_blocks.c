@@ -1,13 +1,17 @@
-/* ref_ffn.c -- TEST INFRASTRUCTURE ONLY (never part of the product): a thin entry point into the
- * reference's own MLP block, so that tests can check the oracle's or_ffn_block against it.
+/* ref_blocks.c -- TEST INFRASTRUCTURE ONLY (never part of the product): thin entry points into
+ * the reference's own CPU engine, so that tests can check the oracle's blocks against it.
  *
  * The reference CPU engine keeps its block functions static: ffn (kcpu4.c:287-295) with rmsfold
  * (:123-139), fold (:89-93, an identity copy for these weights), gemv (:100-118) and q4_dot
  * (q4kernels.h:37-83). This file is compiled together with the unmodified reference source,
  * which it includes by the path given at build time (-DKCPU4_SOURCE, see oracle/Makefile), into
- * oracle/_ref/libkcpu4_ffn.so; nothing of the reference is copied here. ref_ffn_block fills the
- * reference's own Model / Layer structures with the caller's weights (Kindi pack layout) and
- * runs its ffn once: y = down(silu(gate(xn)) * up(xn)), xn = rmsnorm(x + 0) * norm.
+ * oracle/_ref/libkcpu4_blocks.so; nothing of the reference is copied here.
+ *  - ref_ffn_block fills the reference's own Model / Layer structures with the caller's weights
+ *    (Kindi pack layout) and runs its ffn once: y = down(silu(gate(xn)) * up(xn)),
+ *    xn = rmsnorm(x + 0) * norm.
+ *  - ref_head_step runs the reference's kc_step (:303-335) on a model of no layers: the embedding
+ *    row of tok (q4_row), the final rmsfold with out_norm, the head GEMV and its argmax (strictly
+ *    greater: the lowest index among equal logits).
  */
 #include KCPU4_SOURCE
 #include <stdlib.h>
@@ -55,4 +59,29 @@ int ref_ffn_block(const uint8_t* wg, const uint8_t* wu, const uint8_t* wd, int t
   memcpy(y, m.y, sizeof(float) * (size_t)D);
   free(buf);
   return 0;
+}
+
+/* The argmax token (and the logits [V]) of kc_step(tok, pos 0, head) on a model of no layers. */
+int ref_head_step(const uint8_t* emb, int t_emb, const uint8_t* head, int t_head, int D, int V,
+                  const float* out_norm, int tok, float* logits) {
+  Model m;
+  memset(&m, 0, sizeof m);
+  float* buf = (float*)calloc(4 * (size_t)D + (size_t)V, sizeof(float));
+  if (!buf) return -1;
+  m.D = D;
+  m.NL = 0;
+  m.vocab = V;
+  m.L = NULL;
+  m.emb = ref_mat(emb, V, D, t_emb);
+  m.head = ref_mat(head, V, D, t_head);
+  m.out_norm = out_norm;
+  m.h = buf;
+  m.y = m.h + D;
+  m.xn = m.y + D;
+  m.xp = m.xn + D;
+  m.logits = m.xp + D;
+  const int best = kc_step(&m, tok, 0, 1);
+  memcpy(logits, m.logits, sizeof(float) * (size_t)V);
+  free(buf);
+  return best;
 }
