@@ -23,7 +23,12 @@
  * Parity pins: or_decode_block and or_matvec are checked bit-for-bit against the reference's
  * own kc_dequant / kc_matvec (compiled from the reference sources into oracle/_ref) and against
  * the golden vectors in tests/golden, which were produced by the reference's numpy decoder
- * (q4pack.py:52-76) and kc_matvec.
+ * (q4pack.py:52-76) and kc_matvec. or_ffn_block is checked bit-for-bit against the reference's
+ * ffn, and the embedding row, final norm, head and argmax of a step against the reference's
+ * kc_step on a model of no layers (oracle/ref_blocks.c over the unmodified kcpu4.c). or_accept
+ * is checked in distribution against the reference's spec_accept (spec.py:769-787). The dense
+ * attention and the layer composition are pinned to this restatement only (parity unpinned
+ * there: the reference's attention is the hybrid model's gated form).
  *
  * Build flags follow cpu4.py:65-66 (-O3 -ffp-contract=off -fno-math-errno -fopenmp).
  */
